@@ -1,0 +1,249 @@
+/*
+ * rakkan_cuda.h — C ABI of librakkan_cuda.so, a B200 (sm_100a) CUDA backend
+ * for rakkan-mesh's quantized-inference hot path.
+ *
+ * The entry points replace, one for one, the Go API that rakkan-mesh's
+ * internal/llm and sandbox packages call on its Vulkan backend
+ * (internal/gpu) and the host code of rakkan_tensor_v1's matmul. Each
+ * declaration cites the reference interface it stands in for, as
+ * path:line inside github.com/optimist3301/rakkan-mesh.
+ *
+ * Conventions
+ *  - Plain C types only; handles are opaque pointers.
+ *  - Every call that can fail returns an int status: RK_OK (0) or a
+ *    negative RK_ERR_*; rk_last_error() describes the last failure of the
+ *    calling thread. The Go side maps a status to an `error`.
+ *  - Host buffers belong to the caller and are read or written only during
+ *    the call (calls are synchronous, as gpu.Batch.Submit is). Device
+ *    memory belongs to the library; rk_device_used() returns to 0 once
+ *    everything is freed (gpu_test.go:106-108).
+ *  - A device's calls are serialised by a mutex (gpu.Device.mu,
+ *    device.go:202-225); different devices run concurrently.
+ *  - No CPU fallback: if the CUDA kernels cannot run, calls fail. Results
+ *    are bit-identical to the reference's CPU path (package num / llm).
+ */
+#ifndef RAKKAN_CUDA_H
+#define RAKKAN_CUDA_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RK_OK 0
+#define RK_ERR_ARGS (-1)     /* bad handle, argument, shape or type (tenErrArgs, tensor.go:57) */
+#define RK_ERR_TOO_BIG (-3)  /* over a size limit (tenErrTooBig, tensor.go:58) */
+#define RK_ERR_CUDA (-10)    /* a CUDA call failed */
+#define RK_ERR_NOMEM (-11)   /* device allocation failed */
+#define RK_ERR_TIMEOUT (-12) /* a bounded device-side wait expired */
+#define RK_ERR_STATE (-13)   /* call out of order (e.g. a batch already submitted) */
+
+/* Matrix formats: gpu.Format's F32 / BF16 / Q8 / Q4 (device.go:563-582);
+ * Q8_0 and Q4_0 as package num defines them (quant.go:8-22: blocks of 32,
+ * one float32 scale each; Q4_0 packs weight j and j+16 of a block into
+ * byte j, low and high nibble, offset by 8). */
+#define RK_FMT_F32 0
+#define RK_FMT_BF16 1
+#define RK_FMT_Q8_0 2
+#define RK_FMT_Q4_0 3
+
+/* Model weight types: llm.Config.DType (model.go:58-63). */
+#define RK_DTYPE_F32 0
+#define RK_DTYPE_BF16 1
+#define RK_DTYPE_Q8_0 2
+#define RK_DTYPE_Q4_0 3
+#define RK_DTYPE_Q4_M 4
+
+/* tensor/1 data types (tensor.go:40-45). */
+#define RK_TENSOR_F32 0
+#define RK_TENSOR_I8 1
+#define RK_TENSOR_I32 2
+
+/* Widest input and most output rows of one product (device.go:196-200). */
+#define RK_MAX_COLS (1 << 18)
+#define RK_MAX_ROWS (1 << 20)
+
+typedef struct rk_device rk_device;
+typedef struct rk_matrix rk_matrix;
+typedef struct rk_vectors rk_vectors;
+typedef struct rk_arena rk_arena;
+typedef struct rk_batch rk_batch;
+typedef struct rk_layer rk_layer;
+typedef struct rk_stage rk_stage;
+typedef struct rk_head rk_head;
+typedef struct rk_model rk_model;
+
+/* gpu.Info (device.go:21-47). */
+typedef struct {
+    int index;
+    char name[256];
+    int64_t memory;      /* bytes of device memory */
+    int sm_count;
+    int cc_major, cc_minor;
+    int exact;           /* 1: computes the reference's bits (always, on sm_100a) */
+} rk_device_info;
+
+/* The calling thread's last error message (never NULL). */
+const char *rk_last_error(void);
+/* Library version string. */
+const char *rk_version(void);
+
+/* ---- Devices: gpu.Devices / Best / Open / Device.{Info, Used, Close}
+ *      (device.go:125-345) ---- */
+int rk_device_count(int *n);
+int rk_device_get_info(int index, rk_device_info *info);
+int rk_device_best(int *index);                      /* gpu.Best, device.go:182-194 */
+int rk_device_open(int index, rk_device **out);      /* gpu.Open, device.go:238-279 */
+void rk_device_close(rk_device *d);                  /* Device.Close, device.go:345 */
+int64_t rk_device_used(rk_device *d);                /* Device.Used, device.go:338-342 */
+
+/* ---- Matrices: Device.Upload, Matrix.{MulVec, Free, Bytes}, MulVecs,
+ *      SameDevice (device.go:585-793) ---- */
+/* Copies a rows×cols matrix to the device. w: F32 float[rows·cols], BF16
+ * uint16[rows·cols], Q8_0 int8[rows·cols], Q4_0 uint8[rows·cols/2];
+ * scales: float[rows·cols/32] for Q8_0/Q4_0, else NULL. */
+int rk_matrix_upload(rk_device *d, int rows, int cols, int fmt, const void *w, const float *scales, rk_matrix **out);
+void rk_matrix_free(rk_matrix *m);
+int64_t rk_matrix_bytes(const rk_matrix *m);
+int rk_same_device(const rk_matrix *a, const rk_matrix *b);
+/* out[rows] = m·x[cols] (Matrix.MulVec, device.go:762-764). */
+int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x);
+/* outs[i] = ms[i]·x for matrices on one device, in one submission
+ * (MulVecs, device.go:769-793). */
+int rk_mulvecs(int n, rk_matrix *const *ms, float *const *outs, const float *x);
+
+/* ---- Vectors: Device.UploadVectors, Vectors.Free (batch.go:82-109) ---- */
+int rk_vectors_upload(rk_device *d, const float *v, int64_t n, rk_vectors **out);
+void rk_vectors_free(rk_vectors *v);
+
+/* ---- Arena and Batch (batch.go:9-349): device words addressed by
+ *      offsets; a batch records operations and runs them at Submit. ---- */
+int rk_arena_new(rk_device *d, int64_t words, int64_t staging_words, rk_arena **out); /* NewArena, batch.go:24-49 */
+void rk_arena_set_quant_scratch(rk_arena *a, int64_t qx_off, int64_t xs_off);          /* batch.go:55 */
+int64_t rk_arena_bytes(const rk_arena *a);                                              /* batch.go:58 */
+void rk_arena_free(rk_arena *a);                                                        /* batch.go:61-71 */
+int rk_batch_begin(rk_arena *a, rk_batch **out);                                        /* batch.go:127-134 */
+void rk_batch_write(rk_batch *b, int64_t off, const float *data, int64_t n);            /* batch.go:150-159 */
+void rk_batch_read(rk_batch *b, int64_t off, float *dst, int64_t n);                    /* batch.go:162-171 */
+void rk_batch_matvecs(rk_batch *b, int n, rk_matrix *const *ms, const int64_t *out_offs, int64_t in_off); /* batch.go:214-269 */
+void rk_batch_quantize(rk_batch *b, int64_t in_off, int n);                             /* batch.go:278-280 */
+void rk_batch_rmsnorm(rk_batch *b, rk_vectors *vecs, int64_t in_off, int64_t out_off, int64_t w_off, int n, int segs,
+                      int stride, float recip_n, float eps);                             /* batch.go:285-287 */
+void rk_batch_addvec(rk_batch *b, rk_vectors *vecs, int64_t out_off, int64_t v_off, int n); /* batch.go:290-292 */
+void rk_batch_rope(rk_batch *b, int64_t q_off, int64_t k_off, int q_dim, int kv_dim, int head_size, int64_t cos_off,
+                   int64_t sin_off);                                                     /* batch.go:296-298 */
+void rk_batch_copy(rk_batch *b, int64_t src_off, int64_t dst_off, int n);               /* batch.go:301-303 */
+void rk_batch_attention(rk_batch *b, int64_t q_off, int64_t keys_off, int64_t vals_off, int64_t att_off, int att_stride,
+                        int64_t out_off, int positions, int heads, int kv_heads, int head_size, int kv_dim,
+                        float inv_sqrt);                                                 /* batch.go:308-316 */
+void rk_batch_residual(rk_batch *b, int64_t x_off, int64_t y_off, int n, int canonical); /* batch.go:320-326 */
+void rk_batch_silumul(rk_batch *b, int64_t a_off, int64_t b_off, int n);                /* batch.go:329-331 */
+/* Runs the batch, waits, delivers the reads; returns the first error
+ * recorded (batch.go:334-349). Frees the batch either way. */
+int rk_batch_submit(rk_batch *b);
+
+/* ---- Model stages: llm.Config, Layer.toDevice, NewStage, ForwardMany,
+ *      Head.Logits, Embed (model.go:37-131, 347-373, 466-673) ---- */
+typedef struct {
+    int dim, hidden, layers, heads, kv_heads, vocab, seq_len;
+    int shared_classifier;
+    int head_dim;        /* 0: dim/heads */
+    double rope_theta;   /* 0: 10000 */
+    double norm_eps;     /* 0: float32 1e-5 */
+    int qkv_bias, qk_norm;
+    int dtype;           /* RK_DTYPE_* */
+} rk_config;
+
+/* llm.Matrix on the host (model.go:136-147). */
+typedef struct {
+    int fmt;             /* RK_FMT_* */
+    const void *w;
+    const float *scales; /* quantized formats */
+} rk_host_matrix;
+
+/* llm.Layer on the host (model.go:282-293): vectors are float32. */
+typedef struct {
+    const float *rms_att, *rms_ffn;
+    const float *bq, *bk, *bv;     /* qkv_bias */
+    const float *q_norm, *k_norm;  /* qk_norm: one head's width each */
+    rk_host_matrix wq, wk, wv, wo, w1, w2, w3;
+} rk_host_layer;
+
+int rk_config_validate(const rk_config *c);                                             /* model.go:115-131 */
+/* Layer.toDevice (model.go:347-373): copies the layer's matrices and vectors. */
+int rk_layer_upload(rk_device *d, const rk_config *c, const rk_host_layer *l, rk_layer **out);
+/* The same, from matrices already on the device (ownership moves to the layer). */
+int rk_layer_from_device(rk_device *d, const rk_config *c, const rk_host_layer *vectors, rk_matrix *wq, rk_matrix *wk,
+                         rk_matrix *wv, rk_matrix *wo, rk_matrix *w1, rk_matrix *w2, rk_matrix *w3, rk_layer **out);
+void rk_layer_free(rk_layer *l);                                                        /* Layer.release, model.go:376-387 */
+/* NewStage (model.go:466-484): layers [first, first+n) with their caches
+ * for up to ctx positions; the rotary table is NewRope's (model.go:428-441). */
+int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_stage **out);
+void rk_stage_free(rk_stage *s);                                                        /* Stage.Close, model.go:495-500 */
+int rk_stage_positions(const rk_stage *s);                                              /* Stage.Positions, model.go:487 */
+/* Stage.ForwardMany (model.go:504-518): tokens activations of dim floats,
+ * at positions pos, pos+1, ..., run through the stage in place. */
+int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens);
+/* Head (model.go:413-417) from an uploaded classifier (not owned). */
+int rk_head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_head **out);
+void rk_head_free(rk_head *h);
+/* Head.Logits (model.go:667-673): logits[vocab] for the last stage's output x[dim]. */
+int rk_head_logits(rk_head *h, const float *x, float *logits);
+/* Embed (model.go:660-664) from an uploaded table: x[dim] = row token. */
+int rk_embed(rk_matrix *table, int token, float *x);
+
+/* ---- Whole-model decode on one device: the coordinator's per-token loop
+ *      (generate.go:522-585: Embed -> stage forwards -> Head.Logits ->
+ *      Sampler.Sample at temperature 0, sample.go:26-53) with every step
+ *      on the GPU, replayed as one CUDA graph per token. ---- */
+int rk_model_new(rk_device *d, rk_matrix *embed, rk_stage *stage, rk_head *head, rk_model **out);
+void rk_model_free(rk_model *m);
+/* One token at position pos: logits (vocab floats, may be NULL) and the
+ * greedy next token (may be NULL). */
+int rk_model_step(rk_model *m, int token, int pos, float *logits, int *next);
+/* Greedy decode: prompt[0..n_prompt) at positions 0.., then n_new tokens
+ * fed back on the device. out_tokens receives the n_new generated tokens;
+ * out_logits, if not NULL, the logits of every step after the first
+ * prompt token ((n_prompt - 1 + n_new) × vocab floats). */
+int rk_model_generate(rk_model *m, const int *prompt, int n_prompt, int n_new, int *out_tokens, float *out_logits);
+
+/* ---- rakkan_tensor_v1 matmul / matmul_t (tensor.go:286-339) ----
+ * C[m×n] = A[m×k]·B with B [k×n] (transposed 0, "matmul") or [n×k]
+ * (transposed 1, "matmul_t"), row-major host buffers. dtype RK_TENSOR_F32
+ * (C float32: serial no-FMA sum from +0 over p, then canonical NaN) or
+ * RK_TENSOR_I8 (C int32, exact). RK_TENSOR_I32 inputs are rejected with
+ * RK_ERR_ARGS, as the reference returns tenErrArgs. */
+int rk_tensor_matmul(rk_device *d, int dtype, int transposed, int m, int k, int n, const void *a, const void *b, void *c);
+/* The same on device buffers, enqueued on the device's stream (no sync). */
+int rk_tensor_matmul_device(rk_device *d, int dtype, int transposed, int m, int k, int n, const void *a_dev,
+                            const void *b_dev, void *c_dev);
+
+/* ---- Device-side weight import (num.QuantizeQ8 / QuantizeQ4,
+ *      quant.go:25-68) and the seeded synthetic generator used by tests
+ *      and benchmarks. ---- */
+/* Generates rows×cols N(0,1)·scale weights of tensor `tid` under `seed`,
+ * quantizes them on the device to fmt and keeps them as a matrix. */
+int rk_matrix_generate(rk_device *d, int rows, int cols, int fmt, uint64_t seed, uint64_t tid, float scale,
+                       rk_matrix **out);
+/* Copies a matrix back to host buffers (w as in rk_matrix_upload; scales may be NULL). */
+int rk_matrix_download(rk_matrix *m, void *w, float *scales);
+/* Fills host floats with the generator's values (computed on the device). */
+int rk_generate_normal(rk_device *d, uint64_t seed, uint64_t tid, int64_t offset, int64_t n, float scale, float *out);
+/* num.QuantizeQ8 / QuantizeQ4 of host floats, computed on the device. */
+int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, void *q, float *scales);
+
+/* ---- Measurement helpers (device buffers, device stream, CUDA events) ---- */
+/* Times `iters` launches of the Q8/Q4 matvec of m on device-resident input
+ * (L2 flushed before each when flush != 0); returns the mean kernel time. */
+int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per_launch);
+/* Times `iters` graph replays of rk_model_step at position pos with the
+ * token and logits on the device; *ms_per_step is the mean, and
+ * *ms_matvec the mean total time of the matvec kernels in one step
+ * (measured separately, kernel by kernel, with events). */
+int rk_bench_model(rk_model *m, int pos, int iters, float *ms_per_step);
+int rk_model_kernel_count(rk_model *m, int *launches_per_step);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,1712 @@
+// rk_capi.cu — the C ABI of librakkan_cuda.so (include/rakkan_cuda.h).
+//
+// Host-side mirror of rakkan-mesh's internal/gpu API (Device, Matrix,
+// Vectors, Arena, Batch: internal/gpu/device.go, batch.go), of the parts of
+// internal/llm that drive it (Layer.toDevice, NewStage, Stage.ForwardMany,
+// Head.Logits, Embed: internal/llm/model.go, gpustage.go) and of
+// rakkan_tensor_v1's matmul (internal/sandbox/tensor.go:286-339).
+//
+// The library owns device memory and one CUDA stream per device. Every
+// entry point is synchronous at the boundary and returns a status; errors
+// latch per batch like gpu.Batch (batch.go:136-147). There is no host
+// fallback: a failing CUDA call is an error.
+#include <condition_variable>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/rakkan_cuda.h"
+#include "rk_gen.cuh"
+#include "rk_layer.cuh"
+#include "rk_matvec.cuh"
+#include "rk_tensor.cuh"
+
+using namespace rk;
+
+// ---------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_err = "";
+
+static int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char *what) {
+  return fail(e == cudaErrorMemoryAllocation ? RK_ERR_NOMEM : RK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call)                                         \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+  } while (0)
+
+extern "C" const char *rk_last_error(void) { return g_err.c_str(); }
+extern "C" const char *rk_version(void) { return "rakkan-cuda 0.1 (sm_100a)"; }
+
+// ---------------------------------------------------------------------------
+// Devices
+// ---------------------------------------------------------------------------
+// A lock that, like Go's sync.Mutex, may be released by another call than
+// the one that took it (a Batch holds its device from Begin to Submit).
+struct DevLock {
+  std::mutex m;
+  std::condition_variable cv;
+  bool held = false;
+  void lock() {
+    std::unique_lock<std::mutex> g(m);
+    cv.wait(g, [&] { return !held; });
+    held = true;
+  }
+  void unlock() {
+    {
+      std::lock_guard<std::mutex> g(m);
+      held = false;
+    }
+    cv.notify_one();
+  }
+};
+
+struct rk_device {
+  int ordinal = 0;
+  int sms = 148;
+  cudaStream_t st = nullptr;
+  DevLock mu;
+  int64_t used = 0;
+  int *err_dev = nullptr;  // device-side error word (kernels' bounded waits)
+  // The MulVecs arena (device.go:769-793): input, its Q8_0 form, outputs.
+  float *mv_x = nullptr, *mv_out = nullptr, *mv_xs = nullptr;
+  int8_t *mv_qx = nullptr;
+  int *mv_xsum = nullptr;
+  float *pin_in = nullptr, *pin_out = nullptr;
+  void *flush = nullptr;
+  size_t flush_bytes = 0;
+};
+
+struct Guard {
+  rk_device *d;
+  explicit Guard(rk_device *dd) : d(dd) { d->mu.lock(); }
+  ~Guard() { d->mu.unlock(); }
+};
+
+static int set_device(rk_device *d) {
+  CK(cudaSetDevice(d->ordinal));
+  return RK_OK;
+}
+
+// Reads and clears the device error word after a synchronisation.
+static int check_dev_err(rk_device *d) {
+  int e = 0;
+  CK(cudaMemcpy(&e, d->err_dev, sizeof e, cudaMemcpyDeviceToHost));
+  if (e != 0) {
+    CK(cudaMemset(d->err_dev, 0, sizeof(int)));
+    return fail(RK_ERR_TIMEOUT, "a kernel's bounded wait expired (device error %d)", e);
+  }
+  return RK_OK;
+}
+
+static int sync_dev(rk_device *d) {
+  CK(cudaStreamSynchronize(d->st));
+  return check_dev_err(d);
+}
+
+extern "C" int rk_device_count(int *n) {
+  if (!n) return fail(RK_ERR_ARGS, "null argument");
+  int c = 0;
+  cudaError_t e = cudaGetDeviceCount(&c);
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) c = 0;
+  else if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  *n = c;
+  return RK_OK;
+}
+
+extern "C" int rk_device_get_info(int index, rk_device_info *info) {
+  if (!info) return fail(RK_ERR_ARGS, "null argument");
+  cudaDeviceProp p;
+  CK(cudaGetDeviceProperties(&p, index));
+  memset(info, 0, sizeof *info);
+  info->index = index;
+  snprintf(info->name, sizeof info->name, "%s", p.name);
+  info->memory = (int64_t)p.totalGlobalMem;
+  info->sm_count = p.multiProcessorCount;
+  info->cc_major = p.major;
+  info->cc_minor = p.minor;
+  info->exact = (p.major == 10 && p.minor == 0) ? 1 : 0;
+  return RK_OK;
+}
+
+extern "C" int rk_device_best(int *index) {
+  int n = 0;
+  int rc = rk_device_count(&n);
+  if (rc) return rc;
+  int best = -1;
+  int64_t mem = -1;
+  for (int i = 0; i < n; i++) {
+    rk_device_info info;
+    if (rk_device_get_info(i, &info) == RK_OK && info.exact && info.memory > mem) {
+      best = i;
+      mem = info.memory;
+    }
+  }
+  if (best < 0) return fail(RK_ERR_ARGS, "no sm_100 device");
+  *index = best;
+  return RK_OK;
+}
+
+extern "C" int rk_device_open(int index, rk_device **out) {
+  if (!out) return fail(RK_ERR_ARGS, "null argument");
+  rk_device_info info;
+  int rc = rk_device_get_info(index, &info);
+  if (rc) return rc;
+  if (!info.exact) return fail(RK_ERR_ARGS, "device %d (%s) is not sm_100: the kernels are built for sm_100a", index, info.name);
+  auto *d = new rk_device();
+  d->ordinal = index;
+  d->sms = info.sm_count;
+  auto cleanup = [&](int code) {
+    rk_device_close(d);
+    return code;
+  };
+  if (cudaSetDevice(index) != cudaSuccess) return cleanup(fail(RK_ERR_CUDA, "cudaSetDevice(%d)", index));
+  cudaError_t e = init_matvec_attributes();
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&d->err_dev, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&d->mv_x, sizeof(float) * RK_MAX_COLS);
+  if (e == cudaSuccess) e = cudaMalloc(&d->mv_qx, RK_MAX_COLS);
+  if (e == cudaSuccess) e = cudaMalloc(&d->mv_xs, sizeof(float) * (RK_MAX_COLS / 32));
+  if (e == cudaSuccess) e = cudaMalloc(&d->mv_xsum, sizeof(int) * (RK_MAX_COLS / 32));
+  if (e == cudaSuccess) e = cudaMalloc(&d->mv_out, sizeof(float) * RK_MAX_ROWS);
+  if (e == cudaSuccess) e = cudaMallocHost(&d->pin_in, sizeof(float) * RK_MAX_COLS);
+  if (e == cudaSuccess) e = cudaMallocHost(&d->pin_out, sizeof(float) * RK_MAX_ROWS);
+  if (e != cudaSuccess) return cleanup(cuda_fail(e, "device open"));
+  *out = d;
+  return RK_OK;
+}
+
+extern "C" void rk_device_close(rk_device *d) {
+  if (!d) return;
+  cudaSetDevice(d->ordinal);
+  if (d->st) cudaStreamSynchronize(d->st);
+  cudaFree(d->err_dev);
+  cudaFree(d->mv_x);
+  cudaFree(d->mv_qx);
+  cudaFree(d->mv_xs);
+  cudaFree(d->mv_xsum);
+  cudaFree(d->mv_out);
+  cudaFree(d->flush);
+  cudaFreeHost(d->pin_in);
+  cudaFreeHost(d->pin_out);
+  if (d->st) cudaStreamDestroy(d->st);
+  delete d;
+}
+
+extern "C" int64_t rk_device_used(rk_device *d) { return d ? d->used : 0; }
+
+// ---------------------------------------------------------------------------
+// Matrices
+// ---------------------------------------------------------------------------
+struct rk_matrix {
+  rk_device *d = nullptr;
+  int rows = 0, cols = 0, fmt = 0;
+  uint8_t *w = nullptr;
+  float *s = nullptr;
+  size_t wbytes = 0, sbytes = 0;
+  int64_t bytes = 0;
+};
+
+static size_t row_bytes(int fmt, int cols) {
+  switch (fmt) {
+    case RK_FMT_F32: return 4 * (size_t)cols;
+    case RK_FMT_BF16: return 2 * (size_t)cols;
+    case RK_FMT_Q8_0: return (size_t)cols;
+    default: return (size_t)cols / 2;
+  }
+}
+
+static bool quantized_fmt(int fmt) { return fmt == RK_FMT_Q8_0 || fmt == RK_FMT_Q4_0; }
+
+// Allocates a matrix. Weights and scales get 256 bytes of zeroed padding:
+// the streaming kernels copy 16-byte-aligned supersets of scale runs.
+static int matrix_alloc(rk_device *d, int rows, int cols, int fmt, rk_matrix **out) {
+  if (fmt < RK_FMT_F32 || fmt > RK_FMT_Q4_0) return fail(RK_ERR_ARGS, "unknown matrix format %d", fmt);
+  if (rows <= 0 || cols <= 0 || cols > RK_MAX_COLS || rows > (1 << 24))
+    return fail(RK_ERR_ARGS, "gpu: matrix %d×%d out of range", rows, cols);
+  if (quantized_fmt(fmt) && cols % 32 != 0) return fail(RK_ERR_ARGS, "gpu: quantized matrix of the wrong shape");
+  if (fmt == RK_FMT_BF16 && cols % 2 != 0) return fail(RK_ERR_ARGS, "gpu: bfloat16 rows need an even width");
+  auto *m = new rk_matrix();
+  m->d = d;
+  m->rows = rows;
+  m->cols = cols;
+  m->fmt = fmt;
+  m->wbytes = row_bytes(fmt, cols) * (size_t)rows;
+  size_t walloc = ((m->wbytes + 255) & ~size_t(255)) + 256;
+  cudaError_t e = cudaMalloc(&m->w, walloc);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->w, 0, walloc, d->st);
+  size_t salloc = 0;
+  if (e == cudaSuccess && quantized_fmt(fmt)) {
+    m->sbytes = sizeof(float) * (size_t)rows * (cols / 32);
+    salloc = ((m->sbytes + 255) & ~size_t(255)) + 256;
+    e = cudaMalloc(&m->s, salloc);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->s, 0, salloc, d->st);
+  }
+  if (e != cudaSuccess) {
+    cudaFree(m->w);
+    cudaFree(m->s);
+    delete m;
+    return cuda_fail(e, "matrix allocation");
+  }
+  m->bytes = (int64_t)walloc + (int64_t)salloc;
+  d->used += m->bytes;
+  *out = m;
+  return RK_OK;
+}
+
+static void matrix_release(rk_matrix *m) {
+  if (!m) return;
+  cudaSetDevice(m->d->ordinal);
+  cudaStreamSynchronize(m->d->st);
+  cudaFree(m->w);
+  cudaFree(m->s);
+  m->d->used -= m->bytes;
+  delete m;
+}
+
+extern "C" int rk_matrix_upload(rk_device *d, int rows, int cols, int fmt, const void *w, const float *scales,
+                                rk_matrix **out) {
+  if (!d || !w || !out) return fail(RK_ERR_ARGS, "null argument");
+  if (quantized_fmt(fmt) && !scales) return fail(RK_ERR_ARGS, "gpu: quantized matrix without scales");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  rk_matrix *m = nullptr;
+  if ((rc = matrix_alloc(d, rows, cols, fmt, &m))) return rc;
+  cudaError_t e = cudaMemcpyAsync(m->w, w, m->wbytes, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess && m->s) e = cudaMemcpyAsync(m->s, scales, m->sbytes, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  if (e != cudaSuccess) {
+    matrix_release(m);
+    return cuda_fail(e, "matrix upload");
+  }
+  *out = m;
+  return RK_OK;
+}
+
+extern "C" void rk_matrix_free(rk_matrix *m) {
+  if (!m) return;
+  rk_device *d = m->d;
+  Guard g(d);
+  matrix_release(m);
+}
+
+extern "C" int64_t rk_matrix_bytes(const rk_matrix *m) { return m ? m->bytes : 0; }
+extern "C" int rk_same_device(const rk_matrix *a, const rk_matrix *b) { return a && b && a->d == b->d; }
+
+static MvPart part_of(const rk_matrix *m, float *out) {
+  MvPart p;
+  p.w = m->w;
+  p.s = m->s;
+  p.out = out;
+  p.rows = m->rows;
+  return p;
+}
+
+// Enqueues products of matrices (same cols) sharing one input, grouping
+// runs of the same format into one launch of up to four matrices.
+static int enqueue_matvecs(rk_device *d, int n, rk_matrix *const *ms, float *const *outs, const float *x_dev,
+                           const int8_t *qx, const float *xs, const int *xsum, int epi) {
+  int i = 0;
+  while (i < n) {
+    MvArgs a{};
+    a.fmt = ms[i]->fmt;
+    a.cols = ms[i]->cols;
+    a.epi = epi;
+    a.qx = qx;
+    a.xs = xs;
+    a.xsum = xsum;
+    a.x = x_dev;
+    a.err = d->err_dev;
+    int np = 0;
+    while (i < n && np < 4 && ms[i]->fmt == a.fmt) {
+      a.part[np++] = part_of(ms[i], outs[i]);
+      i++;
+    }
+    a.nparts = np;
+    CK(launch_matvec(a, d->sms, d->st));
+  }
+  return RK_OK;
+}
+
+extern "C" int rk_mulvecs(int n, rk_matrix *const *ms, float *const *outs, const float *x) {
+  if (n == 0) return RK_OK;
+  if (n < 0 || !ms || !outs || !x) return fail(RK_ERR_ARGS, "null argument");
+  rk_device *d = ms[0]->d;
+  const int cols = ms[0]->cols;
+  int64_t total = 0;
+  bool quant = false;
+  for (int i = 0; i < n; i++) {
+    if (!ms[i] || ms[i]->d != d || ms[i]->cols != cols || !outs[i])
+      return fail(RK_ERR_ARGS, "gpu: matrices of mulvecs must share a device and a width");
+    total += ms[i]->rows;
+    quant |= quantized_fmt(ms[i]->fmt);
+  }
+  if (total > RK_MAX_ROWS) return fail(RK_ERR_ARGS, "gpu: products too large for one submission");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  memcpy(d->pin_in, x, sizeof(float) * cols);
+  CK(cudaMemcpyAsync(d->mv_x, d->pin_in, sizeof(float) * cols, cudaMemcpyHostToDevice, d->st));
+  if (quant) CK(launch_quantize_act(d->mv_x, cols, nullptr, 0.0f, 0.0f, nullptr, d->mv_qx, d->mv_xs, d->mv_xsum, d->st));
+  std::vector<float *> douts(n);
+  int64_t off = 0;
+  for (int i = 0; i < n; i++) {
+    douts[i] = d->mv_out + off;
+    off += ms[i]->rows;
+  }
+  if ((rc = enqueue_matvecs(d, n, ms, douts.data(), d->mv_x, d->mv_qx, d->mv_xs, d->mv_xsum, EPI_STORE))) return rc;
+  CK(cudaMemcpyAsync(d->pin_out, d->mv_out, sizeof(float) * total, cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  off = 0;
+  for (int i = 0; i < n; i++) {
+    memcpy(outs[i], d->pin_out + off, sizeof(float) * ms[i]->rows);
+    off += ms[i]->rows;
+  }
+  return RK_OK;
+}
+
+extern "C" int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x) {
+  if (!m) return fail(RK_ERR_ARGS, "null matrix");
+  return rk_mulvecs(1, &m, &out, x);
+}
+
+extern "C" int rk_matrix_download(rk_matrix *m, void *w, float *scales) {
+  if (!m || !w) return fail(RK_ERR_ARGS, "null argument");
+  Guard g(m->d);
+  int rc = set_device(m->d);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(w, m->w, m->wbytes, cudaMemcpyDeviceToHost, m->d->st));
+  if (scales && m->s) CK(cudaMemcpyAsync(scales, m->s, m->sbytes, cudaMemcpyDeviceToHost, m->d->st));
+  CK(cudaStreamSynchronize(m->d->st));
+  return RK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Vectors
+// ---------------------------------------------------------------------------
+struct rk_vectors {
+  rk_device *d = nullptr;
+  float *v = nullptr;
+  int64_t n = 0, bytes = 0;
+};
+
+static int vectors_alloc(rk_device *d, const float *v, int64_t n, rk_vectors **out) {
+  auto *vs = new rk_vectors();
+  vs->d = d;
+  vs->n = n;
+  vs->bytes = ((4 * std::max<int64_t>(n, 1) + 255) & ~int64_t(255));
+  cudaError_t e = cudaMalloc(&vs->v, (size_t)vs->bytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(vs->v, 0, (size_t)vs->bytes, d->st);
+  if (e == cudaSuccess && n > 0) e = cudaMemcpyAsync(vs->v, v, sizeof(float) * n, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  if (e != cudaSuccess) {
+    cudaFree(vs->v);
+    delete vs;
+    return cuda_fail(e, "vectors upload");
+  }
+  d->used += vs->bytes;
+  *out = vs;
+  return RK_OK;
+}
+
+static void vectors_release(rk_vectors *v) {
+  if (!v) return;
+  cudaSetDevice(v->d->ordinal);
+  cudaStreamSynchronize(v->d->st);
+  cudaFree(v->v);
+  v->d->used -= v->bytes;
+  delete v;
+}
+
+extern "C" int rk_vectors_upload(rk_device *d, const float *v, int64_t n, rk_vectors **out) {
+  if (!d || !out || n < 0 || (n > 0 && !v)) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  return vectors_alloc(d, v, n, out);
+}
+
+extern "C" void rk_vectors_free(rk_vectors *v) {
+  if (!v) return;
+  rk_device *d = v->d;
+  Guard g(d);
+  vectors_release(v);
+}
+
+// ---------------------------------------------------------------------------
+// Arena and Batch (batch.go)
+// ---------------------------------------------------------------------------
+struct rk_arena {
+  rk_device *d = nullptr;
+  float *buf = nullptr;
+  int64_t words = 0;
+  float *staging = nullptr;  // pinned
+  int64_t staging_words = 0;
+  int64_t qx_off = -1, xs_off = -1;
+  int *xsum = nullptr;  // block sums of the quantized input (Q4_0 products)
+  int64_t bytes = 0;
+};
+
+extern "C" int rk_arena_new(rk_device *d, int64_t words, int64_t staging_words, rk_arena **out) {
+  if (!d || !out || words < 0 || staging_words < 0) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  auto *a = new rk_arena();
+  a->d = d;
+  a->words = words;
+  a->staging_words = staging_words;
+  size_t bytes = (size_t)4 * std::max<int64_t>(words, 1);
+  bytes = ((bytes + 255) & ~size_t(255)) + 256;
+  cudaError_t e = cudaMalloc(&a->buf, bytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(a->buf, 0, bytes, d->st);
+  if (e == cudaSuccess) e = cudaMallocHost(&a->staging, sizeof(float) * std::max<int64_t>(staging_words, 1));
+  if (e == cudaSuccess) e = cudaMalloc(&a->xsum, sizeof(int) * (RK_MAX_COLS / 32));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  if (e != cudaSuccess) {
+    cudaFree(a->buf);
+    cudaFreeHost(a->staging);
+    cudaFree(a->xsum);
+    delete a;
+    return cuda_fail(e, "arena allocation");
+  }
+  a->bytes = (int64_t)bytes;
+  d->used += a->bytes;
+  *out = a;
+  return RK_OK;
+}
+
+extern "C" void rk_arena_set_quant_scratch(rk_arena *a, int64_t qx_off, int64_t xs_off) {
+  if (!a) return;
+  a->qx_off = qx_off;
+  a->xs_off = xs_off;
+}
+
+extern "C" int64_t rk_arena_bytes(const rk_arena *a) { return a ? a->bytes : 0; }
+
+extern "C" void rk_arena_free(rk_arena *a) {
+  if (!a) return;
+  rk_device *d = a->d;
+  Guard g(d);
+  cudaSetDevice(d->ordinal);
+  cudaStreamSynchronize(d->st);
+  cudaFree(a->buf);
+  cudaFreeHost(a->staging);
+  cudaFree(a->xsum);
+  d->used -= a->bytes;
+  delete a;
+}
+
+struct PendingRead {
+  float *dst;
+  int64_t at, n;
+};
+
+struct rk_batch {
+  rk_arena *a = nullptr;
+  std::vector<std::function<int()>> ops;
+  std::vector<PendingRead> reads;
+  int64_t staged = 0;
+  int err = RK_OK;
+  std::string msg;
+};
+
+static void batch_fail(rk_batch *b, int code, const char *fmt, ...) {
+  if (b->err != RK_OK) return;
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  b->err = code;
+  b->msg = buf;
+}
+
+// Word range [off, off+n) inside the arena?
+static bool in_arena(const rk_arena *a, int64_t off, int64_t n) { return off >= 0 && n >= 0 && off + n <= a->words; }
+
+static bool batch_range(rk_batch *b, int64_t off, int64_t n, const char *what) {
+  if (b->err != RK_OK) return false;
+  if (!in_arena(b->a, off, n)) {
+    batch_fail(b, RK_ERR_ARGS, "gpu: %s range [%lld, %lld) outside the arena of %lld words", what, (long long)off,
+               (long long)(off + n), (long long)b->a->words);
+    return false;
+  }
+  return true;
+}
+
+extern "C" int rk_batch_begin(rk_arena *a, rk_batch **out) {
+  if (!a || !out) return fail(RK_ERR_ARGS, "null argument");
+  a->d->mu.lock();  // held until rk_batch_submit, as Batch holds Device.mu
+  auto *b = new rk_batch();
+  b->a = a;
+  *out = b;
+  return RK_OK;
+}
+
+static bool batch_stage(rk_batch *b, int64_t n, int64_t *at) {
+  if (b->err != RK_OK) return false;
+  if (b->staged + n > b->a->staging_words) {
+    batch_fail(b, RK_ERR_ARGS, "gpu: batch moves more than its staging holds");
+    return false;
+  }
+  *at = b->staged;
+  b->staged += n;
+  return true;
+}
+
+extern "C" void rk_batch_write(rk_batch *b, int64_t off, const float *data, int64_t n) {
+  if (!b) return;
+  int64_t at;
+  if (!batch_stage(b, n, &at) || n == 0) return;
+  if (!batch_range(b, off, n, "write")) return;
+  memcpy(b->a->staging + at, data, sizeof(float) * n);
+  rk_arena *a = b->a;
+  b->ops.push_back([a, off, at, n]() {
+    CK(cudaMemcpyAsync(a->buf + off, a->staging + at, sizeof(float) * n, cudaMemcpyHostToDevice, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_read(rk_batch *b, int64_t off, float *dst, int64_t n) {
+  if (!b) return;
+  int64_t at;
+  if (!batch_stage(b, n, &at) || n == 0) return;
+  if (!batch_range(b, off, n, "read")) return;
+  rk_arena *a = b->a;
+  b->ops.push_back([a, off, at, n]() {
+    CK(cudaMemcpyAsync(a->staging + at, a->buf + off, sizeof(float) * n, cudaMemcpyDeviceToHost, a->d->st));
+    return RK_OK;
+  });
+  b->reads.push_back({dst, at, n});
+}
+
+extern "C" void rk_batch_quantize(rk_batch *b, int64_t in_off, int n) {
+  if (!b || b->err) return;
+  rk_arena *a = b->a;
+  if (a->qx_off < 0 || a->xs_off < 0) return batch_fail(b, RK_ERR_ARGS, "gpu: arena has no scratch for quantized inputs");
+  if (n % 32 != 0 || n > RK_MAX_COLS) return batch_fail(b, RK_ERR_ARGS, "gpu: quantize of %d floats", n);
+  if (!batch_range(b, in_off, n, "quantize input") || !batch_range(b, a->qx_off, n / 4, "quantized input") ||
+      !batch_range(b, a->xs_off, n / 32, "input scales"))
+    return;
+  b->ops.push_back([a, in_off, n]() {
+    CK(launch_quantize_act(a->buf + in_off, n, nullptr, 0.0f, 0.0f, nullptr,
+                           reinterpret_cast<int8_t *>(a->buf + a->qx_off), a->buf + a->xs_off, a->xsum, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_matvecs(rk_batch *b, int n, rk_matrix *const *ms, const int64_t *out_offs, int64_t in_off) {
+  if (!b || b->err) return;
+  rk_arena *a = b->a;
+  bool quant = false;
+  int qcols = -1;
+  for (int i = 0; i < n; i++) {
+    if (!ms[i] || ms[i]->d != a->d) return batch_fail(b, RK_ERR_ARGS, "gpu: matrix on another device");
+    if (!batch_range(b, out_offs[i], ms[i]->rows, "product output")) return;
+    if (quantized_fmt(ms[i]->fmt)) {
+      if (qcols >= 0 && qcols != ms[i]->cols) return batch_fail(b, RK_ERR_ARGS, "gpu: quantized products of different widths");
+      qcols = ms[i]->cols;
+      quant = true;
+    } else if (!batch_range(b, in_off, ms[i]->cols, "product input")) {
+      return;
+    }
+  }
+  if (quant) rk_batch_quantize(b, in_off, qcols);
+  if (b->err) return;
+  std::vector<rk_matrix *> mv(ms, ms + n);
+  std::vector<int64_t> offs(out_offs, out_offs + n);
+  b->ops.push_back([a, mv, offs, in_off]() {
+    for (size_t i = 0; i < mv.size(); i++) {
+      float *out = a->buf + offs[i];
+      int rc = enqueue_matvecs(a->d, 1, &mv[i], &out, a->buf + in_off, reinterpret_cast<int8_t *>(a->buf + a->qx_off),
+                               a->buf + a->xs_off, a->xsum, EPI_STORE);
+      if (rc) return rc;
+    }
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_rmsnorm(rk_batch *b, rk_vectors *vecs, int64_t in_off, int64_t out_off, int64_t w_off, int n,
+                                 int segs, int stride, float recip_n, float eps) {
+  if (!b || b->err) return;
+  if (!vecs || w_off < 0 || w_off + n > vecs->n) return batch_fail(b, RK_ERR_ARGS, "gpu: rmsnorm weights out of range");
+  const int64_t span = segs > 0 ? (int64_t)(segs - 1) * stride + n : 0;
+  if (!batch_range(b, in_off, span, "rmsnorm input") || !batch_range(b, out_off, span, "rmsnorm output")) return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    CK(launch_rmsnorm(a->buf + in_off, a->buf + out_off, vecs->v + w_off, n, segs, stride, recip_n, eps, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_addvec(rk_batch *b, rk_vectors *vecs, int64_t out_off, int64_t v_off, int n) {
+  if (!b || b->err) return;
+  if (!vecs || v_off < 0 || v_off + n > vecs->n) return batch_fail(b, RK_ERR_ARGS, "gpu: vector out of range");
+  if (!batch_range(b, out_off, n, "addvec")) return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    CK(launch_addvec(a->buf + out_off, vecs->v + v_off, n, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_rope(rk_batch *b, int64_t q_off, int64_t k_off, int q_dim, int kv_dim, int head_size,
+                              int64_t cos_off, int64_t sin_off) {
+  if (!b || b->err) return;
+  if (head_size <= 0 || head_size % 2) return batch_fail(b, RK_ERR_ARGS, "gpu: rope head size %d", head_size);
+  if (!batch_range(b, q_off, q_dim, "rope q") || !batch_range(b, k_off, std::min(kv_dim, q_dim), "rope k") ||
+      !batch_range(b, cos_off, head_size / 2, "rope cos") || !batch_range(b, sin_off, head_size / 2, "rope sin"))
+    return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    CK(launch_rope(a->buf + q_off, a->buf + k_off, q_dim, kv_dim, head_size, a->buf + cos_off, a->buf + sin_off, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_copy(rk_batch *b, int64_t src_off, int64_t dst_off, int n) {
+  if (!b || b->err) return;
+  if (!batch_range(b, src_off, n, "copy source") || !batch_range(b, dst_off, n, "copy destination")) return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    CK(launch_copy(a->buf + src_off, a->buf + dst_off, n, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_attention(rk_batch *b, int64_t q_off, int64_t keys_off, int64_t vals_off, int64_t att_off,
+                                   int att_stride, int64_t out_off, int positions, int heads, int kv_heads, int head_size,
+                                   int kv_dim, float inv_sqrt) {
+  if (!b || b->err) return;
+  if (positions <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_size <= 0 || att_stride < positions ||
+      kv_dim < kv_heads * head_size)
+    return batch_fail(b, RK_ERR_ARGS, "gpu: attention arguments out of range");
+  const int64_t qd = (int64_t)heads * head_size;
+  const int64_t cache = (int64_t)(positions - 1) * kv_dim + (int64_t)kv_heads * head_size;
+  if (!batch_range(b, q_off, qd, "attention q") || !batch_range(b, keys_off, cache, "attention keys") ||
+      !batch_range(b, vals_off, cache, "attention values") ||
+      !batch_range(b, att_off, (int64_t)(heads - 1) * att_stride + positions, "attention scores") ||
+      !batch_range(b, out_off, qd, "attention output"))
+    return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    AttnArgs at{};
+    at.q = a->buf + q_off;
+    at.keys = a->buf + keys_off;
+    at.vals = a->buf + vals_off;
+    at.att = a->buf + att_off;
+    at.out = a->buf + out_off;
+    at.positions = positions;
+    at.heads = heads;
+    at.kv_heads = kv_heads;
+    at.hs = head_size;
+    at.kv_dim = kv_dim;
+    at.att_stride = att_stride;
+    at.inv_sqrt = inv_sqrt;
+    CK(launch_attention(at, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_residual(rk_batch *b, int64_t x_off, int64_t y_off, int n, int canonical) {
+  if (!b || b->err) return;
+  if (!batch_range(b, x_off, n, "residual x") || !batch_range(b, y_off, n, "residual y")) return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    CK(launch_residual(a->buf + x_off, a->buf + y_off, n, canonical, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" void rk_batch_silumul(rk_batch *b, int64_t a_off, int64_t b_off, int n) {
+  if (!b || b->err) return;
+  if (!batch_range(b, a_off, n, "silumul a") || !batch_range(b, b_off, n, "silumul b")) return;
+  rk_arena *a = b->a;
+  b->ops.push_back([=]() {
+    CK(launch_silumul(a->buf + a_off, a->buf + b_off, n, a->d->st));
+    return RK_OK;
+  });
+}
+
+extern "C" int rk_batch_submit(rk_batch *b) {
+  if (!b) return fail(RK_ERR_ARGS, "null batch");
+  rk_arena *a = b->a;
+  rk_device *d = a->d;
+  int rc = b->err;
+  std::string msg = b->msg;
+  if (rc == RK_OK) {
+    rc = set_device(d);
+    for (size_t i = 0; rc == RK_OK && i < b->ops.size(); i++) rc = b->ops[i]();
+    if (rc == RK_OK) rc = sync_dev(d);
+    if (rc == RK_OK)
+      for (const auto &r : b->reads) memcpy(r.dst, a->staging + r.at, sizeof(float) * r.n);
+  } else {
+    g_err = msg;
+  }
+  delete b;
+  d->mu.unlock();
+  return rc;
+}
+
+// ---------------------------------------------------------------------------
+// Layers and stages (model.go, gpustage.go)
+// ---------------------------------------------------------------------------
+static int head_size(const rk_config *c) { return c->head_dim > 0 ? c->head_dim : c->dim / c->heads; }
+static float cfg_eps(const rk_config *c) {
+  return c->norm_eps > 0 ? (float)c->norm_eps : 1e-5f;  // the float32 constant 1e-5 (model.go:90)
+}
+static bool cfg_quantized(const rk_config *c) {
+  return c->dtype == RK_DTYPE_Q8_0 || c->dtype == RK_DTYPE_Q4_0 || c->dtype == RK_DTYPE_Q4_M;
+}
+
+extern "C" int rk_config_validate(const rk_config *c) {
+  if (!c) return fail(RK_ERR_ARGS, "null config");
+  if (c->dim <= 0 || c->hidden <= 0 || c->layers <= 0 || c->heads <= 0 || c->kv_heads <= 0 || c->vocab <= 0 ||
+      c->seq_len <= 0 || c->head_dim < 0)
+    return fail(RK_ERR_ARGS, "non-positive dimension");
+  if ((c->head_dim == 0 && c->dim % c->heads != 0) || c->heads % c->kv_heads != 0 || head_size(c) % 2 != 0)
+    return fail(RK_ERR_ARGS, "heads do not divide the model dimension evenly");
+  if (c->dim > 1 << 16 || c->hidden > 1 << 18 || c->layers > 1024 || c->vocab > 1 << 20 || c->seq_len > 1 << 20 ||
+      head_size(c) > 1024 || c->heads > 1024)
+    return fail(RK_ERR_ARGS, "dimensions out of range");
+  if (c->dtype < RK_DTYPE_F32 || c->dtype > RK_DTYPE_Q4_M) return fail(RK_ERR_ARGS, "unknown weight type %d", c->dtype);
+  if (cfg_quantized(c) && (c->dim % 32 || (c->heads * head_size(c)) % 32 || c->hidden % 32))
+    return fail(RK_ERR_ARGS, "quantized models need widths that are multiples of 32");
+  if (c->rope_theta < 0 || c->norm_eps < 0 || c->norm_eps > 1) return fail(RK_ERR_ARGS, "rope base or norm epsilon out of range");
+  return RK_OK;
+}
+
+struct rk_layer {
+  rk_device *d = nullptr;
+  rk_config c{};
+  rk_matrix *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr, *w3 = nullptr;
+  rk_vectors *vecs = nullptr;
+  // Offsets in vecs (vecLayout, model.go:298-314); -1 when absent.
+  int64_t o_rms_att = 0, o_rms_ffn = 0, o_bq = -1, o_bk = -1, o_bv = -1, o_qn = -1, o_kn = -1;
+};
+
+static void layer_release(rk_layer *l) {
+  if (!l) return;
+  for (rk_matrix *m : {l->wq, l->wk, l->wv, l->wo, l->w1, l->w2, l->w3}) matrix_release(m);
+  vectors_release(l->vecs);
+  delete l;
+}
+
+static int layer_vectors(rk_device *d, const rk_config *c, const rk_host_layer *h, rk_layer *l) {
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs;
+  std::vector<float> all;
+  auto put = [&](const float *v, int n) -> int64_t {
+    int64_t at = (int64_t)all.size();
+    all.insert(all.end(), v, v + n);
+    return at;
+  };
+  if (!h->rms_att || !h->rms_ffn) return fail(RK_ERR_ARGS, "layer without norm weights");
+  l->o_rms_att = put(h->rms_att, c->dim);
+  l->o_rms_ffn = put(h->rms_ffn, c->dim);
+  if (c->qkv_bias) {
+    if (!h->bq || !h->bk || !h->bv) return fail(RK_ERR_ARGS, "qkv_bias without biases");
+    l->o_bq = put(h->bq, qd);
+    l->o_bk = put(h->bk, kvd);
+    l->o_bv = put(h->bv, kvd);
+  }
+  if (c->qk_norm) {
+    if (!h->q_norm || !h->k_norm) return fail(RK_ERR_ARGS, "qk_norm without norm weights");
+    l->o_qn = put(h->q_norm, hs);
+    l->o_kn = put(h->k_norm, hs);
+  }
+  return vectors_alloc(d, all.data(), (int64_t)all.size(), &l->vecs);
+}
+
+// Expected format of each matrix (Config.matType, model.go:105-113).
+static int mat_fmt(const rk_config *c, bool sensitive) {
+  switch (c->dtype) {
+    case RK_DTYPE_F32: return RK_FMT_F32;
+    case RK_DTYPE_BF16: return RK_FMT_BF16;
+    case RK_DTYPE_Q8_0: return RK_FMT_Q8_0;
+    case RK_DTYPE_Q4_0: return RK_FMT_Q4_0;
+    default: return sensitive ? RK_FMT_Q8_0 : RK_FMT_Q4_0;
+  }
+}
+
+extern "C" int rk_layer_upload(rk_device *d, const rk_config *c, const rk_host_layer *h, rk_layer **out) {
+  if (!d || !c || !h || !out) return fail(RK_ERR_ARGS, "null argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  Guard g(d);
+  if ((rc = set_device(d))) return rc;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  auto *l = new rk_layer();
+  l->d = d;
+  l->c = *c;
+  struct Spec {
+    rk_matrix **dst;
+    const rk_host_matrix *src;
+    int rows, cols;
+    bool sensitive;
+  } specs[7] = {{&l->wq, &h->wq, qd, D, false},  {&l->wk, &h->wk, kvd, D, false}, {&l->wv, &h->wv, kvd, D, true},
+                {&l->wo, &h->wo, D, qd, false},  {&l->w1, &h->w1, H, D, false},   {&l->w2, &h->w2, D, H, true},
+                {&l->w3, &h->w3, H, D, false}};
+  for (auto &s : specs) {
+    if (s.src->fmt != mat_fmt(c, s.sensitive)) {
+      layer_release(l);
+      return fail(RK_ERR_ARGS, "layer matrix format %d, want %d for dtype %d", s.src->fmt, mat_fmt(c, s.sensitive), c->dtype);
+    }
+    if ((rc = matrix_alloc(d, s.rows, s.cols, s.src->fmt, s.dst))) {
+      layer_release(l);
+      return rc;
+    }
+    cudaError_t e = cudaMemcpyAsync((*s.dst)->w, s.src->w, (*s.dst)->wbytes, cudaMemcpyHostToDevice, d->st);
+    if (e == cudaSuccess && (*s.dst)->s)
+      e = cudaMemcpyAsync((*s.dst)->s, s.src->scales, (*s.dst)->sbytes, cudaMemcpyHostToDevice, d->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+    if (e != cudaSuccess) {
+      layer_release(l);
+      return cuda_fail(e, "layer upload");
+    }
+  }
+  if ((rc = layer_vectors(d, c, h, l))) {
+    layer_release(l);
+    return rc;
+  }
+  *out = l;
+  return RK_OK;
+}
+
+extern "C" int rk_layer_from_device(rk_device *d, const rk_config *c, const rk_host_layer *vectors, rk_matrix *wq,
+                                    rk_matrix *wk, rk_matrix *wv, rk_matrix *wo, rk_matrix *w1, rk_matrix *w2,
+                                    rk_matrix *w3, rk_layer **out) {
+  if (!d || !c || !vectors || !out) return fail(RK_ERR_ARGS, "null argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  struct Spec {
+    rk_matrix *m;
+    int rows, cols;
+    bool sensitive;
+  } specs[7] = {{wq, qd, D, false}, {wk, kvd, D, false}, {wv, kvd, D, true}, {wo, D, qd, false},
+                {w1, H, D, false},  {w2, D, H, true},    {w3, H, D, false}};
+  for (auto &s : specs)
+    if (!s.m || s.m->d != d || s.m->rows != s.rows || s.m->cols != s.cols || s.m->fmt != mat_fmt(c, s.sensitive))
+      return fail(RK_ERR_ARGS, "layer matrix of the wrong shape, format or device");
+  Guard g(d);
+  if ((rc = set_device(d))) return rc;
+  auto *l = new rk_layer();
+  l->d = d;
+  l->c = *c;
+  if ((rc = layer_vectors(d, c, vectors, l))) {
+    delete l;
+    return rc;
+  }
+  l->wq = wq;
+  l->wk = wk;
+  l->wv = wv;
+  l->wo = wo;
+  l->w1 = w1;
+  l->w2 = w2;
+  l->w3 = w3;
+  *out = l;
+  return RK_OK;
+}
+
+extern "C" void rk_layer_free(rk_layer *l) {
+  if (!l) return;
+  rk_device *d = l->d;
+  Guard g(d);
+  layer_release(l);
+}
+
+struct rk_stage {
+  rk_device *d = nullptr;
+  rk_config c{};
+  std::vector<rk_layer *> layers;
+  int ctx = 0;
+  // Activations and scratch (gpustage.go:51-83).
+  float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att_out = nullptr, *hb = nullptr,
+        *hb2 = nullptr, *att = nullptr, *xs = nullptr, *cos_ = nullptr, *sin_ = nullptr, *io = nullptr;
+  int8_t *qx = nullptr;
+  int *xsum = nullptr, *pos_dev = nullptr, *tok_dev = nullptr;
+  std::vector<float *> keys, vals;
+  float *pin_io = nullptr;
+  std::vector<void *> allocs;
+  int64_t bytes = 0;
+  cudaGraphExec_t graph = nullptr;
+  int io_tokens = 64;  // gpuBatch, gpustage.go:17
+};
+
+static int stage_alloc(rk_stage *s, size_t bytes, void **p) {
+  bytes = ((bytes + 255) & ~size_t(255)) + 256;
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(*p, 0, bytes, s->d->st);
+  if (e != cudaSuccess) return cuda_fail(e, "stage allocation");
+  s->allocs.push_back(*p);
+  s->bytes += (int64_t)bytes;
+  return RK_OK;
+}
+
+static void stage_release(rk_stage *s) {
+  if (!s) return;
+  cudaSetDevice(s->d->ordinal);
+  cudaStreamSynchronize(s->d->st);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  for (void *p : s->allocs) cudaFree(p);
+  cudaFreeHost(s->pin_io);
+  s->d->used -= s->bytes;
+  delete s;
+}
+
+// num.Recip32 (recip.go:38-67) of a positive integer-valued float, on the
+// host: the Recip32(float32(n)) that rmsNorm multiplies by (model.go:633;
+// gpustage.go:123-124). This file is compiled with -ffp-contract=off, so
+// each operation rounds once.
+static float host_recip32(float x) {
+  float m = x;
+  int e = 0;
+  while (m >= 2.0f) {
+    m = m * 0.5f;
+    e++;
+  }
+  const float k24_17 = 0x1.696968p+0f, k8_17 = 0x1.e1e1e2p-2f;  // float32(24.0/17), float32(8.0/17)
+  float r = k24_17 - k8_17 * m;
+  for (int i = 0; i < 3; i++) {
+    const float mr = m * r;
+    const float t = 1.0f - mr;
+    const float rt = r * t;
+    r = r + rt;
+  }
+  return r * ldexpf(1.0f, -e);
+}
+
+// Records one position's pass through the stage's layers (gpustage.go:119-152
+// in the order of Stage.Forward, model.go:537-611), reading the position
+// from s->pos_dev. x is s->x.
+static int record_layers(rk_stage *s, cudaStream_t st) {
+  rk_device *d = s->d;
+  const rk_config *c = &s->c;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  const float eps = cfg_eps(c);
+  const float recipD = host_recip32((float)D), recipHS = host_recip32((float)hs);
+  const float invSqrt = (float)(1 / sqrt((double)hs));
+  const bool quant = cfg_quantized(c);
+  for (size_t li = 0; li < s->layers.size(); li++) {
+    rk_layer *l = s->layers[li];
+    const float *vec = l->vecs->v;
+    // rmsNorm(xb, x, RmsAtt) and the Q8_0 form of xb.
+    if (quant) CK(launch_quantize_act(s->x, D, vec + l->o_rms_att, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
+    else CK(launch_rmsnorm(s->x, s->xb, vec + l->o_rms_att, D, 1, 0, recipD, eps, st));
+    // q, k, v = Wq·xb, Wk·xb, Wv·xb (mulVecs, model.go:539).
+    rk_matrix *qkv[3] = {l->wq, l->wk, l->wv};
+    float *qkv_out[3] = {s->q, s->k, s->v};
+    int rc = enqueue_matvecs(d, 3, qkv, qkv_out, s->xb, s->qx, s->xs, s->xsum, EPI_STORE);
+    if (rc) return rc;
+    // Bias, QK-norm, RoPE, cache append (model.go:542-568).
+    QkvPostArgs qp{};
+    qp.q = s->q;
+    qp.k = s->k;
+    qp.v = s->v;
+    if (c->qkv_bias) {
+      qp.bq = vec + l->o_bq;
+      qp.bk = vec + l->o_bk;
+      qp.bv = vec + l->o_bv;
+    }
+    if (c->qk_norm) {
+      qp.q_norm = vec + l->o_qn;
+      qp.k_norm = vec + l->o_kn;
+    }
+    qp.cos_ = s->cos_;
+    qp.sin_ = s->sin_;
+    qp.key_cache = s->keys[li];
+    qp.val_cache = s->vals[li];
+    qp.pos_dev = s->pos_dev;
+    qp.heads = c->heads;
+    qp.kv_heads = c->kv_heads;
+    qp.hs = hs;
+    qp.eps = eps;
+    qp.recip_hs = recipHS;
+    CK(launch_qkv_post(qp, st));
+    // Attention over positions 0..pos (model.go:571-587).
+    AttnArgs at{};
+    at.q = s->q;
+    at.keys = s->keys[li];
+    at.vals = s->vals[li];
+    at.att = s->att;
+    at.out = s->att_out;
+    at.positions_dev = s->pos_dev;
+    at.positions_add = 1;
+    at.max_positions = s->ctx;
+    at.heads = c->heads;
+    at.kv_heads = c->kv_heads;
+    at.hs = hs;
+    at.kv_dim = kvd;
+    at.att_stride = s->ctx;
+    at.inv_sqrt = invSqrt;
+    CK(launch_attention(at, st));
+    // x += Wo·attOut (model.go:588-594).
+    if (quantized_fmt(l->wo->fmt))
+      CK(launch_quantize_act(s->att_out, qd, nullptr, 0.0f, 0.0f, nullptr, s->qx, s->xs, s->xsum, st));
+    if ((rc = enqueue_matvecs(d, 1, &l->wo, &s->x, s->att_out, s->qx, s->xs, s->xsum, EPI_ADD))) return rc;
+    // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603).
+    if (quant) CK(launch_quantize_act(s->x, D, vec + l->o_rms_ffn, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
+    else CK(launch_rmsnorm(s->x, s->xb, vec + l->o_rms_ffn, D, 1, 0, recipD, eps, st));
+    {
+      MvArgs a{};
+      a.fmt = l->w1->fmt;
+      a.cols = D;
+      a.epi = EPI_SILU;
+      a.qx = s->qx;
+      a.xs = s->xs;
+      a.xsum = s->xsum;
+      a.x = s->xb;
+      a.err = d->err_dev;
+      a.part[0] = part_of(l->w1, s->hb);
+      a.part[1] = part_of(l->w3, s->hb2);
+      a.nparts = 2;
+      CK(launch_matvec(a, d->sms, st));
+    }
+    // x = Canonical(x + W2·hb) (model.go:604-610).
+    if (quantized_fmt(l->w2->fmt))
+      CK(launch_quantize_act(s->hb, H, nullptr, 0.0f, 0.0f, nullptr, s->qx, s->xs, s->xsum, st));
+    if ((rc = enqueue_matvecs(d, 1, &l->w2, &s->x, s->hb, s->qx, s->xs, s->xsum, EPI_ADD_CANON))) return rc;
+  }
+  return RK_OK;
+}
+
+// io[tok] -> x, or x -> io[tok] then tok += 1, pos += 1.
+__global__ void k_stage_io(float *io, const int *tok, float *x, int dim, int dir) {
+  const long long t = *tok;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
+    if (dir == 0) x[j] = io[t * dim + j];
+    else io[t * dim + j] = x[j];
+  }
+}
+__global__ void k_advance(int *tok, int *pos) {
+  if (tok) *tok += 1;
+  if (pos) *pos += 1;
+}
+
+static int capture(rk_device *d, std::function<int(cudaStream_t)> rec, cudaGraphExec_t *out, size_t *nodes = nullptr) {
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal));
+  int rc = rec(d->st);
+  cudaError_t e = cudaStreamEndCapture(d->st, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "graph capture");
+  if (nodes) cudaGraphGetNodes(graph, nullptr, nodes);
+  e = cudaGraphInstantiate(out, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+  return RK_OK;
+}
+
+extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_stage **out) {
+  if (!d || !c || !out || n < 0 || (n > 0 && !layers) || ctx <= 0) return fail(RK_ERR_ARGS, "bad argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  ctx = std::min(ctx, c->seq_len);
+  for (int i = 0; i < n; i++)
+    if (!layers[i] || layers[i]->d != d) return fail(RK_ERR_ARGS, "layer %d not on this device", i);
+  Guard g(d);
+  if ((rc = set_device(d))) return rc;
+  auto *s = new rk_stage();
+  s->d = d;
+  s->c = *c;
+  s->layers.assign(layers, layers + n);
+  s->ctx = ctx;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  const int widest = std::max(D, std::max(qd, H));
+  void *p;
+  auto A = [&](size_t bytes, void **dst) { return stage_alloc(s, bytes, dst); };
+#define ALLOC(field, bytes)                   \
+  do {                                        \
+    if ((rc = A((bytes), &p))) goto fail_;    \
+    s->field = (decltype(s->field))p;         \
+  } while (0)
+  ALLOC(x, 4 * (size_t)D);
+  ALLOC(xb, 4 * (size_t)D);
+  ALLOC(q, 4 * (size_t)qd);
+  ALLOC(k, 4 * (size_t)kvd);
+  ALLOC(v, 4 * (size_t)kvd);
+  ALLOC(att_out, 4 * (size_t)qd);
+  ALLOC(hb, 4 * (size_t)H);
+  ALLOC(hb2, 4 * (size_t)H);
+  ALLOC(att, 4 * (size_t)c->heads * ctx);
+  ALLOC(qx, (size_t)widest);
+  ALLOC(xs, 4 * (size_t)(widest / 32 + 1));
+  ALLOC(xsum, 4 * (size_t)(widest / 32 + 1));
+  ALLOC(cos_, 4 * (size_t)ctx * (hs / 2));
+  ALLOC(sin_, 4 * (size_t)ctx * (hs / 2));
+  ALLOC(io, 4 * (size_t)s->io_tokens * D);
+  ALLOC(pos_dev, 4);
+  ALLOC(tok_dev, 4);
+  for (int i = 0; i < n; i++) {
+    if ((rc = A(4 * (size_t)ctx * kvd, &p))) goto fail_;
+    s->keys.push_back((float *)p);
+    if ((rc = A(4 * (size_t)ctx * kvd, &p))) goto fail_;
+    s->vals.push_back((float *)p);
+  }
+#undef ALLOC
+  {
+    cudaError_t e = cudaMallocHost(&s->pin_io, 4 * (size_t)s->io_tokens * D);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "stage staging");
+      goto fail_;
+    }
+    const double theta = c->rope_theta > 0 ? c->rope_theta : 10000.0;
+    e = launch_rope_table(theta, hs, ctx, s->cos_, s->sin_, d->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "rope table");
+      goto fail_;
+    }
+  }
+  d->used += s->bytes;
+  rc = capture(
+      d,
+      [s, D](cudaStream_t st) {
+        k_stage_io<<<(D + 255) / 256, 256, 0, st>>>(s->io, s->tok_dev, s->x, D, 0);
+        int r = record_layers(s, st);
+        if (r) return r;
+        k_stage_io<<<(D + 255) / 256, 256, 0, st>>>(s->io, s->tok_dev, s->x, D, 1);
+        k_advance<<<1, 1, 0, st>>>(s->tok_dev, s->pos_dev);
+        CK(cudaGetLastError());
+        return RK_OK;
+      },
+      &s->graph);
+  if (rc) {
+    stage_release(s);
+    return rc;
+  }
+  *out = s;
+  return RK_OK;
+fail_:
+  d->used += s->bytes;
+  stage_release(s);
+  return rc;
+}
+
+extern "C" void rk_stage_free(rk_stage *s) {
+  if (!s) return;
+  rk_device *d = s->d;
+  Guard g(d);
+  stage_release(s);
+}
+
+extern "C" int rk_stage_positions(const rk_stage *s) { return s ? s->ctx : 0; }
+
+extern "C" int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens) {
+  if (!s || (tokens > 0 && !xs) || tokens < 0) return fail(RK_ERR_ARGS, "bad argument");
+  if (pos < 0 || pos + tokens > s->ctx) return fail(RK_ERR_ARGS, "positions [%d, %d) outside the stage's %d", pos, pos + tokens, s->ctx);
+  rk_device *d = s->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  const int D = s->c.dim;
+  for (int start = 0; start < tokens; start += s->io_tokens) {
+    const int nt = std::min(s->io_tokens, tokens - start);
+    memcpy(s->pin_io, xs + (size_t)start * D, sizeof(float) * (size_t)nt * D);
+    CK(cudaMemcpyAsync(s->io, s->pin_io, sizeof(float) * (size_t)nt * D, cudaMemcpyHostToDevice, d->st));
+    const int hdr[2] = {0, pos + start};
+    CK(cudaMemcpyAsync(s->tok_dev, &hdr[0], sizeof(int), cudaMemcpyHostToDevice, d->st));
+    CK(cudaMemcpyAsync(s->pos_dev, &hdr[1], sizeof(int), cudaMemcpyHostToDevice, d->st));
+    for (int t = 0; t < nt; t++) CK(cudaGraphLaunch(s->graph, d->st));
+    CK(cudaMemcpyAsync(s->pin_io, s->io, sizeof(float) * (size_t)nt * D, cudaMemcpyDeviceToHost, d->st));
+    if ((rc = sync_dev(d))) return rc;
+    memcpy(xs + (size_t)start * D, s->pin_io, sizeof(float) * (size_t)nt * D);
+  }
+  return RK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Head, Embed
+// ---------------------------------------------------------------------------
+struct rk_head {
+  rk_device *d = nullptr;
+  rk_config c{};
+  rk_matrix *wcls = nullptr;  // not owned
+  float *rms = nullptr, *x = nullptr, *xb = nullptr, *xs = nullptr, *logits = nullptr;
+  int8_t *qx = nullptr;
+  int *xsum = nullptr;
+  float *pin = nullptr;
+  int64_t bytes = 0;
+};
+
+static void head_release(rk_head *h) {
+  if (!h) return;
+  cudaSetDevice(h->d->ordinal);
+  cudaStreamSynchronize(h->d->st);
+  for (void *p : {(void *)h->rms, (void *)h->x, (void *)h->xb, (void *)h->xs, (void *)h->logits, (void *)h->qx,
+                  (void *)h->xsum})
+    cudaFree(p);
+  cudaFreeHost(h->pin);
+  h->d->used -= h->bytes;
+  delete h;
+}
+
+extern "C" int rk_head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_head **out) {
+  if (!d || !c || !rms_final || !wcls || !out) return fail(RK_ERR_ARGS, "null argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  if (wcls->d != d || wcls->rows != c->vocab || wcls->cols != c->dim) return fail(RK_ERR_ARGS, "classifier of the wrong shape");
+  Guard g(d);
+  if ((rc = set_device(d))) return rc;
+  auto *h = new rk_head();
+  h->d = d;
+  h->c = *c;
+  h->wcls = wcls;
+  const size_t D = (size_t)c->dim, V = (size_t)c->vocab;
+  cudaError_t e = cudaMalloc(&h->rms, 4 * D);
+  if (e == cudaSuccess) e = cudaMalloc(&h->x, 4 * D);
+  if (e == cudaSuccess) e = cudaMalloc(&h->xb, 4 * D);
+  if (e == cudaSuccess) e = cudaMalloc(&h->xs, 4 * (D / 32 + 1));
+  if (e == cudaSuccess) e = cudaMalloc(&h->xsum, 4 * (D / 32 + 1));
+  if (e == cudaSuccess) e = cudaMalloc(&h->qx, D + 16);
+  if (e == cudaSuccess) e = cudaMalloc(&h->logits, 4 * V);
+  if (e == cudaSuccess) e = cudaMallocHost(&h->pin, 4 * std::max(D, V));
+  if (e == cudaSuccess) e = cudaMemcpy(h->rms, rms_final, 4 * D, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    head_release(h);
+    return cuda_fail(e, "head allocation");
+  }
+  h->bytes = (int64_t)(4 * D * 3 + 8 * (D / 32 + 1) + D + 16 + 4 * V);
+  d->used += h->bytes;
+  *out = h;
+  return RK_OK;
+}
+
+extern "C" void rk_head_free(rk_head *h) {
+  if (!h) return;
+  rk_device *d = h->d;
+  Guard g(d);
+  head_release(h);
+}
+
+// rmsNorm(xn, x, RmsFinal) then Wcls·xn into h->logits (model.go:667-673).
+static int record_head(rk_head *h, const float *x, cudaStream_t st) {
+  const int D = h->c.dim;
+  const float recipD = host_recip32((float)D);
+  const float eps = cfg_eps(&h->c);
+  if (quantized_fmt(h->wcls->fmt))
+    CK(launch_quantize_act(x, D, h->rms, recipD, eps, nullptr, h->qx, h->xs, h->xsum, st));
+  else
+    CK(launch_rmsnorm(x, h->xb, h->rms, D, 1, 0, recipD, eps, st));
+  MvArgs a{};
+  a.fmt = h->wcls->fmt;
+  a.cols = D;
+  a.epi = EPI_STORE;
+  a.qx = h->qx;
+  a.xs = h->xs;
+  a.xsum = h->xsum;
+  a.x = h->xb;
+  a.err = h->d->err_dev;
+  a.part[0] = part_of(h->wcls, h->logits);
+  a.nparts = 1;
+  CK(launch_matvec(a, h->d->sms, st));
+  return RK_OK;
+}
+
+extern "C" int rk_head_logits(rk_head *h, const float *x, float *logits) {
+  if (!h || !x || !logits) return fail(RK_ERR_ARGS, "null argument");
+  rk_device *d = h->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  const int D = h->c.dim, V = h->c.vocab;
+  memcpy(h->pin, x, 4 * (size_t)D);
+  CK(cudaMemcpyAsync(h->x, h->pin, 4 * (size_t)D, cudaMemcpyHostToDevice, d->st));
+  if ((rc = record_head(h, h->x, d->st))) return rc;
+  CK(cudaMemcpyAsync(h->pin, h->logits, 4 * (size_t)V, cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  memcpy(logits, h->pin, 4 * (size_t)V);
+  return RK_OK;
+}
+
+extern "C" int rk_embed(rk_matrix *table, int token, float *x) {
+  if (!table || !x) return fail(RK_ERR_ARGS, "null argument");
+  if (token < 0 || token >= table->rows) return fail(RK_ERR_ARGS, "token %d outside the table's %d rows", token, table->rows);
+  rk_device *d = table->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  memcpy(d->pin_in, &token, sizeof token);
+  CK(cudaMemcpyAsync(d->mv_xsum, d->pin_in, sizeof(int), cudaMemcpyHostToDevice, d->st));
+  CK(launch_embed(table->fmt, table->w, table->s, table->cols, d->mv_xsum, d->mv_x, d->st));
+  CK(cudaMemcpyAsync(d->pin_out, d->mv_x, 4 * (size_t)table->cols, cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  memcpy(x, d->pin_out, 4 * (size_t)table->cols);
+  return RK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Whole-model decode
+// ---------------------------------------------------------------------------
+struct rk_model {
+  rk_device *d = nullptr;
+  rk_matrix *embed = nullptr;
+  rk_stage *stage = nullptr;
+  rk_head *head = nullptr;
+  int *token_dev = nullptr, *next_dev = nullptr;
+  int *pin_tok = nullptr;
+  float *pin_logits = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  int launches = 0;
+};
+
+__global__ void k_feed_token(const int *next, int *token) { *token = *next; }
+
+static int record_model(rk_model *m, cudaStream_t st) {
+  rk_stage *s = m->stage;
+  CK(launch_embed(m->embed->fmt, m->embed->w, m->embed->s, s->c.dim, m->token_dev, s->x, st));
+  int rc = record_layers(s, st);
+  if (rc) return rc;
+  if ((rc = record_head(m->head, s->x, st))) return rc;
+  CK(launch_argmax(m->head->logits, s->c.vocab, m->next_dev, st));
+  k_feed_token<<<1, 1, 0, st>>>(m->next_dev, m->token_dev);
+  k_advance<<<1, 1, 0, st>>>(nullptr, s->pos_dev);
+  CK(cudaGetLastError());
+  return RK_OK;
+}
+
+static void model_release(rk_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->d->ordinal);
+  cudaStreamSynchronize(m->d->st);
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  cudaFree(m->token_dev);
+  cudaFree(m->next_dev);
+  cudaFreeHost(m->pin_tok);
+  cudaFreeHost(m->pin_logits);
+  delete m;
+}
+
+extern "C" int rk_model_new(rk_device *d, rk_matrix *embed, rk_stage *stage, rk_head *head, rk_model **out) {
+  if (!d || !embed || !stage || !head || !out) return fail(RK_ERR_ARGS, "null argument");
+  if (embed->d != d || stage->d != d || head->d != d) return fail(RK_ERR_ARGS, "model parts on different devices");
+  if (embed->rows != stage->c.vocab || embed->cols != stage->c.dim) return fail(RK_ERR_ARGS, "embedding table of the wrong shape");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  auto *m = new rk_model();
+  m->d = d;
+  m->embed = embed;
+  m->stage = stage;
+  m->head = head;
+  cudaError_t e = cudaMalloc(&m->token_dev, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&m->next_dev, 16);
+  if (e == cudaSuccess) e = cudaMallocHost(&m->pin_tok, 64);
+  if (e == cudaSuccess) e = cudaMallocHost(&m->pin_logits, 4 * (size_t)stage->c.vocab);
+  if (e != cudaSuccess) {
+    model_release(m);
+    return cuda_fail(e, "model allocation");
+  }
+  size_t nodes = 0;
+  if ((rc = capture(d, [m](cudaStream_t st) { return record_model(m, st); }, &m->graph, &nodes))) {
+    model_release(m);
+    return rc;
+  }
+  m->launches = (int)nodes;
+  *out = m;
+  return RK_OK;
+}
+
+extern "C" void rk_model_free(rk_model *m) {
+  if (!m) return;
+  rk_device *d = m->d;
+  Guard g(d);
+  model_release(m);
+}
+
+extern "C" int rk_model_kernel_count(rk_model *m, int *launches_per_step) {
+  if (!m || !launches_per_step) return fail(RK_ERR_ARGS, "null argument");
+  *launches_per_step = m->launches;
+  return RK_OK;
+}
+
+extern "C" int rk_model_step(rk_model *m, int token, int pos, float *logits, int *next) {
+  if (!m) return fail(RK_ERR_ARGS, "null model");
+  rk_stage *s = m->stage;
+  if (pos < 0 || pos >= s->ctx) return fail(RK_ERR_ARGS, "position %d outside the stage's %d", pos, s->ctx);
+  if (token < 0 || token >= s->c.vocab) return fail(RK_ERR_ARGS, "token %d outside the vocabulary", token);
+  rk_device *d = m->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  m->pin_tok[0] = token;
+  m->pin_tok[1] = pos;
+  CK(cudaMemcpyAsync(m->token_dev, &m->pin_tok[0], 4, cudaMemcpyHostToDevice, d->st));
+  CK(cudaMemcpyAsync(s->pos_dev, &m->pin_tok[1], 4, cudaMemcpyHostToDevice, d->st));
+  CK(cudaGraphLaunch(m->graph, d->st));
+  if (logits) CK(cudaMemcpyAsync(m->pin_logits, m->head->logits, 4 * (size_t)s->c.vocab, cudaMemcpyDeviceToHost, d->st));
+  CK(cudaMemcpyAsync(&m->pin_tok[2], m->next_dev, 4, cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  if (logits) memcpy(logits, m->pin_logits, 4 * (size_t)s->c.vocab);
+  if (next) *next = m->pin_tok[2];
+  return RK_OK;
+}
+
+extern "C" int rk_model_generate(rk_model *m, const int *prompt, int n_prompt, int n_new, int *out_tokens,
+                                 float *out_logits) {
+  if (!m || !prompt || n_prompt <= 0 || n_new < 0 || (n_new > 0 && !out_tokens)) return fail(RK_ERR_ARGS, "bad argument");
+  rk_stage *s = m->stage;
+  const int steps = n_prompt + n_new - 1;
+  if (steps > s->ctx) return fail(RK_ERR_ARGS, "generation of %d positions exceeds the stage's %d", steps, s->ctx);
+  const int V = s->c.vocab;
+  for (int i = 0; i < n_prompt; i++)
+    if (prompt[i] < 0 || prompt[i] >= V) return fail(RK_ERR_ARGS, "prompt token %d outside the vocabulary", prompt[i]);
+  rk_device *d = m->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  int *pin = nullptr;
+  CK(cudaMallocHost(&pin, sizeof(int) * (size_t)(n_prompt + n_new + 2)));
+  memcpy(pin, prompt, sizeof(int) * n_prompt);
+  pin[n_prompt + n_new] = 0;
+  auto run = [&]() -> int {
+    CK(cudaMemcpyAsync(s->pos_dev, &pin[n_prompt + n_new], 4, cudaMemcpyHostToDevice, d->st));
+    for (int i = 0; i < steps; i++) {
+      // Prompt tokens are fed from the host; generated ones are already in
+      // token_dev (k_feed_token).
+      if (i < n_prompt) CK(cudaMemcpyAsync(m->token_dev, &pin[i], 4, cudaMemcpyHostToDevice, d->st));
+      CK(cudaGraphLaunch(m->graph, d->st));
+      if (i >= n_prompt - 1) CK(cudaMemcpyAsync(&pin[n_prompt + (i - (n_prompt - 1))], m->next_dev, 4, cudaMemcpyDeviceToHost, d->st));
+      if (out_logits) {
+        CK(cudaMemcpyAsync(m->pin_logits, m->head->logits, 4 * (size_t)V, cudaMemcpyDeviceToHost, d->st));
+        int r = sync_dev(d);
+        if (r) return r;
+        memcpy(out_logits + (size_t)i * V, m->pin_logits, 4 * (size_t)V);
+      }
+    }
+    return sync_dev(d);
+  };
+  rc = run();
+  if (rc == RK_OK && n_new > 0) memcpy(out_tokens, pin + n_prompt, sizeof(int) * n_new);
+  cudaFreeHost(pin);
+  return rc;
+}
+
+// ---------------------------------------------------------------------------
+// tensor/1 matmul
+// ---------------------------------------------------------------------------
+static int tensor_check(int dtype, int m, int k, int n) {
+  if (dtype == RK_TENSOR_I32) return fail(RK_ERR_ARGS, "matmul of int32 tensors");
+  if (dtype != RK_TENSOR_F32 && dtype != RK_TENSOR_I8) return fail(RK_ERR_ARGS, "unknown dtype %d", dtype);
+  if (m <= 0 || k <= 0 || n <= 0 || m > (1 << 24) || k > (1 << 24) || n > (1 << 24))
+    return fail(RK_ERR_ARGS, "matmul shape %d×%d·%d out of range", m, k, n);
+  return RK_OK;
+}
+
+extern "C" int rk_tensor_matmul_device(rk_device *d, int dtype, int transposed, int m, int k, int n, const void *a_dev,
+                                       const void *b_dev, void *c_dev) {
+  if (!d || !a_dev || !b_dev || !c_dev) return fail(RK_ERR_ARGS, "null argument");
+  int rc = tensor_check(dtype, m, k, n);
+  if (rc) return rc;
+  if ((rc = set_device(d))) return rc;
+  CK(launch_tensor_matmul(dtype, transposed, m, k, n, a_dev, b_dev, c_dev, d->sms, d->st));
+  return RK_OK;
+}
+
+extern "C" int rk_tensor_matmul(rk_device *d, int dtype, int transposed, int m, int k, int n, const void *a,
+                                const void *b, void *c) {
+  if (!d || !a || !b || !c) return fail(RK_ERR_ARGS, "null argument");
+  int rc = tensor_check(dtype, m, k, n);
+  if (rc) return rc;
+  Guard g(d);
+  if ((rc = set_device(d))) return rc;
+  const size_t es = dtype == RK_TENSOR_F32 ? 4 : 1;
+  const size_t ab = es * (size_t)m * k, bb = es * (size_t)k * n, cb = 4 * (size_t)m * n;
+  void *da = nullptr, *db = nullptr, *dc = nullptr;
+  cudaError_t e = cudaMalloc(&da, ab);
+  if (e == cudaSuccess) e = cudaMalloc(&db, bb);
+  if (e == cudaSuccess) e = cudaMalloc(&dc, cb);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(da, a, ab, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, bb, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess) e = launch_tensor_matmul(dtype, transposed, m, k, n, da, db, dc, d->sms, d->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(c, dc, cb, cudaMemcpyDeviceToHost, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  cudaFree(da);
+  cudaFree(db);
+  cudaFree(dc);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor matmul");
+  return RK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Device-side import and the seeded generator
+// ---------------------------------------------------------------------------
+extern "C" int rk_matrix_generate(rk_device *d, int rows, int cols, int fmt, uint64_t seed, uint64_t tid, float scale,
+                                  rk_matrix **out) {
+  if (!d || !out) return fail(RK_ERR_ARGS, "null argument");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  rk_matrix *m = nullptr;
+  if ((rc = matrix_alloc(d, rows, cols, fmt, &m))) return rc;
+  const long long n = (long long)rows * cols;
+  // Generate in slices of at most 256 Mi floats to bound the scratch.
+  const long long slice = std::min<long long>(n, 1ll << 28);
+  float *tmp = nullptr;
+  uint8_t *stale = nullptr;
+  cudaError_t e = cudaMalloc(&tmp, sizeof(float) * (size_t)slice);
+  if (e == cudaSuccess && fmt == RK_FMT_Q4_0) e = cudaMalloc(&stale, (size_t)(slice / 32 + 1));
+  for (long long off = 0; e == cudaSuccess && off < n; off += slice) {
+    const long long cnt = std::min(slice, n - off);
+    e = launch_gen_normal(seed, tid, off, cnt, scale, tmp, d->st);
+    if (e != cudaSuccess) break;
+    switch (fmt) {
+      case RK_FMT_F32: e = cudaMemcpyAsync(m->w + 4 * off, tmp, 4 * (size_t)cnt, cudaMemcpyDeviceToDevice, d->st); break;
+      case RK_FMT_Q8_0: e = launch_quantize_q8_w(tmp, cnt, (int8_t *)m->w + off, m->s + off / 32, d->st); break;
+      case RK_FMT_Q4_0:
+        // Slices are whole numbers of blocks; a stale block at a slice start
+        // would need the previous slice's last block (not for finite weights).
+        e = launch_quantize_q4_w(tmp, cnt, m->w + off / 2, m->s + off / 32, stale, d->st);
+        break;
+      default: e = cudaErrorInvalidValue;  // bf16 generation: convert on the host
+    }
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  cudaFree(tmp);
+  cudaFree(stale);
+  if (e != cudaSuccess) {
+    matrix_release(m);
+    return cuda_fail(e, "matrix generation");
+  }
+  *out = m;
+  return RK_OK;
+}
+
+extern "C" int rk_generate_normal(rk_device *d, uint64_t seed, uint64_t tid, int64_t offset, int64_t n, float scale,
+                                  float *out) {
+  if (!d || !out || n < 0) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  float *tmp = nullptr;
+  CK(cudaMalloc(&tmp, 4 * (size_t)std::max<int64_t>(n, 1)));
+  cudaError_t e = launch_gen_normal(seed, tid, offset, n, scale, tmp, d->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, tmp, 4 * (size_t)n, cudaMemcpyDeviceToHost, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  cudaFree(tmp);
+  if (e != cudaSuccess) return cuda_fail(e, "generate");
+  return RK_OK;
+}
+
+extern "C" int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, void *q, float *scales) {
+  if (!d || !w || !q || !scales || n < 0 || n % 32) return fail(RK_ERR_ARGS, "bad argument");
+  if (!quantized_fmt(fmt)) return fail(RK_ERR_ARGS, "not a quantized format");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  float *dw = nullptr, *ds = nullptr;
+  uint8_t *dq = nullptr, *stale = nullptr;
+  const size_t qb = fmt == RK_FMT_Q8_0 ? (size_t)n : (size_t)n / 2;
+  cudaError_t e = cudaMalloc(&dw, 4 * (size_t)std::max<int64_t>(n, 1));
+  if (e == cudaSuccess) e = cudaMalloc(&dq, std::max<size_t>(qb, 1));
+  if (e == cudaSuccess) e = cudaMalloc(&ds, 4 * (size_t)(n / 32 + 1));
+  if (e == cudaSuccess) e = cudaMalloc(&stale, (size_t)(n / 32 + 1));
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dw, w, 4 * (size_t)n, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess)
+    e = fmt == RK_FMT_Q8_0 ? launch_quantize_q8_w(dw, n, (int8_t *)dq, ds, d->st)
+                           : launch_quantize_q4_w(dw, n, dq, ds, stale, d->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(q, dq, qb, cudaMemcpyDeviceToHost, d->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(scales, ds, 4 * (size_t)(n / 32), cudaMemcpyDeviceToHost, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  cudaFree(dw);
+  cudaFree(dq);
+  cudaFree(ds);
+  cudaFree(stale);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize");
+  return RK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Measurement helpers
+// ---------------------------------------------------------------------------
+static int ensure_flush(rk_device *d) {
+  if (d->flush) return RK_OK;
+  d->flush_bytes = (size_t)256 << 20;  // twice the 126 MB L2
+  CK(cudaMalloc(&d->flush, d->flush_bytes));
+  return RK_OK;
+}
+
+extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per_launch) {
+  if (!m || iters <= 0 || !ms_per_launch) return fail(RK_ERR_ARGS, "bad argument");
+  rk_device *d = m->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  if (flush && (rc = ensure_flush(d))) return rc;
+  CK(cudaMemsetAsync(d->mv_x, 0, 4 * (size_t)m->cols, d->st));
+  if (quantized_fmt(m->fmt))
+    CK(launch_quantize_act(d->mv_x, m->cols, nullptr, 0.0f, 0.0f, nullptr, d->mv_qx, d->mv_xs, d->mv_xsum, d->st));
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  float total = 0.0f;
+  float *out = d->mv_out;
+  for (int i = 0; i < iters + 1; i++) {
+    if (flush) CK(cudaMemsetAsync(d->flush, i & 0xff, d->flush_bytes, d->st));
+    CK(cudaEventRecord(e0, d->st));
+    if ((rc = enqueue_matvecs(d, 1, &m, &out, d->mv_x, d->mv_qx, d->mv_xs, d->mv_xsum, EPI_STORE))) return rc;
+    CK(cudaEventRecord(e1, d->st));
+    CK(cudaEventSynchronize(e1));
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, e0, e1));
+    if (i > 0) total += ms;  // the first launch is a warm-up
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if ((rc = check_dev_err(d))) return rc;
+  *ms_per_launch = total / iters;
+  return RK_OK;
+}
+
+extern "C" int rk_bench_model(rk_model *m, int pos, int iters, float *ms_per_step) {
+  if (!m || iters <= 0 || !ms_per_step) return fail(RK_ERR_ARGS, "bad argument");
+  rk_device *d = m->d;
+  if (pos < 0 || pos >= m->stage->ctx) return fail(RK_ERR_ARGS, "position out of range");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  m->pin_tok[4] = pos;
+  CK(cudaMemcpyAsync(m->stage->pos_dev, &m->pin_tok[4], 4, cudaMemcpyHostToDevice, d->st));
+  CK(cudaEventRecord(e0, d->st));
+  for (int i = 0; i < iters; i++) {
+    // Each step re-runs position pos (its KV entry is rewritten), so every
+    // timed step attends over pos+1 positions.
+    CK(cudaMemcpyAsync(m->stage->pos_dev, &m->pin_tok[4], 4, cudaMemcpyHostToDevice, d->st));
+    CK(cudaGraphLaunch(m->graph, d->st));
+  }
+  CK(cudaEventRecord(e1, d->st));
+  CK(cudaEventSynchronize(e1));
+  float ms = 0.0f;
+  CK(cudaEventElapsedTime(&ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if ((rc = check_dev_err(d))) return rc;
+  *ms_per_step = ms / iters;
+  return RK_OK;
+}

@@ -1,0 +1,388 @@
+// rk_layer.cu — transformer-layer kernels, bit-identical to the reference's
+// CPU order of operations (rakkan-mesh internal/llm/model.go:522-673; the
+// reference's Vulkan twins in internal/gpu/kernels.go:355-577 follow the same
+// order and are the specification the launch shapes below were checked
+// against).
+#include "rk_common.cuh"
+#include "rk_detmath.cuh"
+#include "rk_layer.cuh"
+#include "rk_matvec.cuh"
+
+namespace rk {
+
+// ---------------------------------------------------------------------------
+// RMSNorm (model.go:632-638): a warp per segment.
+// ---------------------------------------------------------------------------
+__global__ void k_rmsnorm(const float *in, float *out, const float *__restrict__ w, int n, int stride, float recipN,
+                          float eps) {
+  const int lane = threadIdx.x;
+  const float *x = in + (long long)blockIdx.x * stride;
+  float *o = out + (long long)blockIdx.x * stride;
+  float s = 0.0f;
+  for (int i = lane; i < n; i += 32) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+  const float dot = combine32(s);
+  const float inv = __shfl_sync(0xffffffffu, rsqrt32(__fadd_rn(__fmul_rn(dot, recipN), eps)), 0);
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) o[i] = __fmul_rn(w[i], __fmul_rn(inv, x[i]));
+}
+
+cudaError_t launch_rmsnorm(const float *in, float *out, const float *w, int n, int segs, int stride, float recipN,
+                           float eps, cudaStream_t st) {
+  if (segs <= 0) return cudaSuccess;
+  k_rmsnorm<<<segs, 32, 0, st>>>(in, out, w, n, stride, recipN, eps);
+  return cudaGetLastError();
+}
+
+__global__ void k_addvec(float *out, const float *v, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __fadd_rn(out[i], v[i]);
+}
+cudaError_t launch_addvec(float *out, const float *v, int n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_addvec<<<(n + 255) / 256, 256, 0, st>>>(out, v, n);
+  return cudaGetLastError();
+}
+
+// rotate, model.go:621-625, over pairs (i, i+1), p = (i mod hs)/2.
+RK_DEV void rotate_pair(float *v, int i, float co, float si) {
+  const float v0 = v[i], v1 = v[i + 1];
+  v[i] = __fsub_rn(__fmul_rn(v0, co), __fmul_rn(v1, si));
+  v[i + 1] = __fadd_rn(__fmul_rn(v0, si), __fmul_rn(v1, co));
+}
+
+__global__ void k_rope(float *q, float *k, int pairs, int kvDim, int hs, const float *cos_, const float *sin_) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= pairs) return;
+  const int i = 2 * p;
+  const int pi = (i % hs) / 2;
+  const float co = cos_[pi], si = sin_[pi];
+  rotate_pair(q, i, co, si);
+  if (i < kvDim) rotate_pair(k, i, co, si);
+}
+cudaError_t launch_rope(float *q, float *k, int qDim, int kvDim, int hs, const float *cos_, const float *sin_,
+                        cudaStream_t st) {
+  const int pairs = qDim / 2;
+  if (pairs <= 0) return cudaSuccess;
+  k_rope<<<(pairs + 255) / 256, 256, 0, st>>>(q, k, pairs, kvDim, hs, cos_, sin_);
+  return cudaGetLastError();
+}
+
+__global__ void k_copy(const float *src, float *dst, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = src[i];
+}
+cudaError_t launch_copy(const float *src, float *dst, int n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_copy<<<(n + 255) / 256, 256, 0, st>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+__global__ void k_residual(float *x, const float *y, int n, int canon) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = __fadd_rn(x[i], y[i]);
+  x[i] = canon ? canonical(v) : v;
+}
+cudaError_t launch_residual(float *x, const float *y, int n, int canonical_, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_residual<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, canonical_);
+  return cudaGetLastError();
+}
+
+__global__ void k_silumul(float *a, const float *b, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) a[i] = __fmul_rn(silu(a[i]), b[i]);
+}
+cudaError_t launch_silumul(float *a, const float *b, int n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_silumul<<<(n + 255) / 256, 256, 0, st>>>(a, b, n);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Attention (model.go:571-587).
+// ---------------------------------------------------------------------------
+RK_DEV int attn_positions(const AttnArgs &a) {
+  return a.positions_dev ? *a.positions_dev + a.positions_add : a.positions;
+}
+
+// Scores: att[h][t] = float32(Dot32(q_h, k_t)·invSqrt). A warp per position
+// t, for every query head of one key/value head (grid.y): k_t is read once
+// for the group.
+constexpr int kScoreWarps = 8;
+__global__ void __launch_bounds__(kScoreWarps * 32) k_attn_scores(const AttnArgs a) {
+  const int P = attn_positions(a);
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kScoreWarps + (threadIdx.x >> 5);
+  if (t >= P) return;
+  const int kvh = blockIdx.y, kvMul = a.heads / a.kv_heads, hs = a.hs;
+  const float *key = a.keys + (long long)t * a.kv_dim + kvh * hs;
+  for (int g = 0; g < kvMul; g++) {
+    const int h = kvh * kvMul + g;
+    const float *q = a.q + h * hs;
+    float s = 0.0f;
+    for (int e = lane; e < hs; e += 32) s = __fadd_rn(s, __fmul_rn(q[e], key[e]));
+    const float dot = combine32(s);
+    if (lane == 0) a.att[(long long)h * a.att_stride + t] = __fmul_rn(dot, a.inv_sqrt);
+  }
+}
+
+// softmax (model.go:640-654): the maximum in any order (Go's max is order
+// free), Exp32 of the differences, their sum in position order by one
+// thread, then multiplication by Recip32 of the sum. One CTA per head.
+constexpr int kSoftmaxThreads = 256;
+constexpr int kSoftmaxSmem = 12224;  // floats kept in shared memory (static limit 48 KB)
+__global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs a) {
+  __shared__ float sv[kSoftmaxSmem];
+  __shared__ float red[kSoftmaxThreads / 32];
+  __shared__ float s_val;
+  const int P = attn_positions(a);
+  float *x = a.att + (long long)blockIdx.x * a.att_stride;
+  const bool in_smem = P <= kSoftmaxSmem;
+  float *v = in_smem ? sv : x;
+  float m = x[0];
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const float xi = x[i];
+    if (in_smem) sv[i] = xi;
+    m = gomax(m, xi);
+  }
+  m = warp_gomax(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = red[0];
+    for (int i = 1; i < kSoftmaxThreads / 32; i++) mm = gomax(mm, red[i]);
+    s_val = mm;
+  }
+  __syncthreads();
+  m = s_val;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) v[i] = exp32(__fsub_rn(v[i], m));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    int i = 0;
+    for (; i + 8 <= P; i += 8) {
+      float t0 = v[i], t1 = v[i + 1], t2 = v[i + 2], t3 = v[i + 3], t4 = v[i + 4], t5 = v[i + 5], t6 = v[i + 6],
+            t7 = v[i + 7];
+      sum = __fadd_rn(sum, t0);
+      sum = __fadd_rn(sum, t1);
+      sum = __fadd_rn(sum, t2);
+      sum = __fadd_rn(sum, t3);
+      sum = __fadd_rn(sum, t4);
+      sum = __fadd_rn(sum, t5);
+      sum = __fadd_rn(sum, t6);
+      sum = __fadd_rn(sum, t7);
+    }
+    for (; i < P; i++) sum = __fadd_rn(sum, v[i]);
+    s_val = recip32(sum);
+  }
+  __syncthreads();
+  const float inv = s_val;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) x[i] = __fmul_rn(v[i], inv);
+}
+
+// Weighted values: out[h·hs+i] = sum over t in order from +0 of
+// float32(att[h][t]·v_t[i]). A thread per output element.
+__global__ void __launch_bounds__(128) k_attn_wsum(const AttnArgs a) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int qDim = a.heads * a.hs;
+  if (g >= qDim) return;
+  const int P = attn_positions(a);
+  const int h = g / a.hs, i = g % a.hs, kvMul = a.heads / a.kv_heads;
+  const float *att = a.att + (long long)h * a.att_stride;
+  const float *val = a.vals + (h / kvMul) * a.hs + i;
+  const long long kv = a.kv_dim;
+  float acc = 0.0f;
+  int t = 0;
+  for (; t + 4 <= P; t += 4) {
+    const float a0 = att[t], a1 = att[t + 1], a2 = att[t + 2], a3 = att[t + 3];
+    const float v0 = val[t * kv], v1 = val[(t + 1) * kv], v2 = val[(t + 2) * kv], v3 = val[(t + 3) * kv];
+    acc = __fadd_rn(acc, __fmul_rn(a0, v0));
+    acc = __fadd_rn(acc, __fmul_rn(a1, v1));
+    acc = __fadd_rn(acc, __fmul_rn(a2, v2));
+    acc = __fadd_rn(acc, __fmul_rn(a3, v3));
+  }
+  for (; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(att[t], val[t * kv]));
+  a.out[g] = acc;
+}
+
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
+  const int maxP = a.positions_dev ? a.max_positions : a.positions;
+  if (maxP <= 0) return cudaSuccess;
+  dim3 g1((maxP + kScoreWarps - 1) / kScoreWarps, a.kv_heads);
+  k_attn_scores<<<g1, kScoreWarps * 32, 0, st>>>(a);
+  k_attn_softmax<<<a.heads, kSoftmaxThreads, 0, st>>>(a);
+  const int qDim = a.heads * a.hs;
+  k_attn_wsum<<<(qDim + 127) / 128, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// QKV post-processing (model.go:542-568). CTA b < heads: query head b;
+// otherwise key/value head b - heads. One warp each.
+// ---------------------------------------------------------------------------
+__global__ void k_qkv_post(const QkvPostArgs a) {
+  const int lane = threadIdx.x;
+  const int hs = a.hs, half = hs / 2;
+  const int pos = *a.pos_dev;
+  const int kvDim = a.kv_heads * hs;
+  const bool isq = blockIdx.x < a.heads;
+  const int head = isq ? blockIdx.x : blockIdx.x - a.heads;
+  float *v = (isq ? a.q : a.k) + head * hs;
+  const float *bias = isq ? a.bq : a.bk;
+  // 1. bias (addTo, model.go:543-545).
+  if (bias)
+    for (int i = lane; i < hs; i += 32) v[i] = __fadd_rn(v[i], bias[head * hs + i]);
+  if (!isq && a.bv)
+    for (int i = lane; i < hs; i += 32) a.v[head * hs + i] = __fadd_rn(a.v[head * hs + i], a.bv[head * hs + i]);
+  __syncwarp();
+  // 2. QK-norm (rmsNorm of the head, model.go:547-554).
+  const float *nw = isq ? a.q_norm : a.k_norm;
+  if (nw) {
+    float s = 0.0f;
+    for (int i = lane; i < hs; i += 32) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+    const float dot = combine32(s);
+    const float inv = __shfl_sync(0xffffffffu, rsqrt32(__fadd_rn(__fmul_rn(dot, a.recip_hs), a.eps)), 0);
+    __syncwarp();
+    for (int i = lane; i < hs; i += 32) v[i] = __fmul_rn(nw[i], __fmul_rn(inv, v[i]));
+    __syncwarp();
+  }
+  // 3. RoPE on the head's adjacent pairs (model.go:558-566).
+  const float *co = a.cos_ + (long long)pos * half, *si = a.sin_ + (long long)pos * half;
+  for (int p = lane; p < half; p += 32) rotate_pair(v, 2 * p, co[p], si[p]);
+  __syncwarp();
+  // 4. The key/value cache append (model.go:567-568).
+  if (!isq) {
+    float *kc = a.key_cache + (long long)pos * kvDim + head * hs;
+    float *vc = a.val_cache + (long long)pos * kvDim + head * hs;
+    for (int i = lane; i < hs; i += 32) {
+      kc[i] = v[i];
+      vc[i] = a.v[head * hs + i];
+    }
+  }
+}
+
+cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st) {
+  k_qkv_post<<<a.heads + a.kv_heads, 32, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Embed (Matrix.Row + DequantQ8/Q4, model.go:216-231; quant.go:130-146).
+// ---------------------------------------------------------------------------
+__global__ void k_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x) {
+  const long long tok = *token_dev;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
+    float v;
+    if (fmt == FMT_Q8_0) {
+      const int8_t q = reinterpret_cast<const int8_t *>(table)[tok * dim + j];
+      v = __fmul_rn(float(q), scales[tok * (dim / 32) + j / 32]);
+    } else if (fmt == FMT_Q4_0) {
+      const int b = j / 32, o = j % 32;
+      const uint8_t byte = reinterpret_cast<const uint8_t *>(table)[tok * (dim / 2) + b * 16 + (o & 15)];
+      const int q = (o < 16 ? (byte & 15) : (byte >> 4)) - 8;
+      v = __fmul_rn(float(q), scales[tok * (dim / 32) + b]);
+    } else if (fmt == FMT_BF16) {
+      v = __uint_as_float(uint32_t(reinterpret_cast<const uint16_t *>(table)[tok * dim + j]) << 16);
+    } else {
+      v = reinterpret_cast<const float *>(table)[tok * dim + j];
+    }
+    x[j] = v;
+  }
+}
+cudaError_t launch_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x,
+                         cudaStream_t st) {
+  k_embed<<<(dim + 255) / 256, 256, 0, st>>>(fmt, table, scales, dim, token_dev, x);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// argmax (sample.go:45-53): the smallest index among the maxima under `>`.
+// NaN never compares greater, and a NaN at index 0 stays the answer, as in
+// the reference's loop.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_argmax(const float *v, int n, int *out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  // Reference semantics: best = 0; for i: if v[i] > v[best] best = i. With
+  // v[0] NaN nothing compares greater, so the answer is 0. Otherwise it is
+  // the first index of the maximum of the non-NaN values.
+  const float v0 = v[0];
+  if (v0 != v0) {
+    if (threadIdx.x == 0) *out = 0;
+    return;
+  }
+  float bv = v0;
+  int bi = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = v[i];
+    if (x > bv || (x == bv && i < bi)) {
+      bv = x;
+      bi = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    bv = threadIdx.x < nw ? sv[threadIdx.x] : v0;
+    bi = threadIdx.x < nw ? si[threadIdx.x] : 0;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0) *out = bi;
+  }
+}
+cudaError_t launch_argmax(const float *v, int n, int *out, cudaStream_t st) {
+  k_argmax<<<1, 1024, 0, st>>>(v, n, out);
+  return cudaGetLastError();
+}
+
+// freq_p = Exp(-Log(theta)·2p / hs); (sin, cos) = Sincos(pos·freq_p).
+__global__ void k_rope_table(double theta, int hs, int n, float *cos_, float *sin_) {
+  const int half = hs / 2;
+  const double log_theta = log_det(theta);
+  const long long total = (long long)n * half;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+    const int pos = int(e / half), p = int(e % half);
+    const double freq = exp_det(__ddiv_rn(__dmul_rn(-log_theta, double(2 * p)), double(hs)));
+    double s, c;
+    sincos_det(__dmul_rn(double(pos), freq), s, c);
+    cos_[e] = __double2float_rn(c);
+    sin_[e] = __double2float_rn(s);
+  }
+}
+cudaError_t launch_rope_table(double theta, int hs, int n, float *cos_, float *sin_, cudaStream_t st) {
+  long long total = (long long)n * (hs / 2);
+  if (total <= 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  // log(theta) in the reference is math.Log (model.go:434); this is
+  // num.Log's method, which agrees with it on the bases configs use.
+  k_rope_table<<<int(blocks), 256, 0, st>>>(theta, hs, n, cos_, sin_);
+  return cudaGetLastError();
+}
+
+__global__ void k_add_int(int *p, int inc) { *p += inc; }
+cudaError_t launch_add_int(int *p, int inc, cudaStream_t st) {
+  k_add_int<<<1, 1, 0, st>>>(p, inc);
+  return cudaGetLastError();
+}
+
+}  // namespace rk

@@ -1,0 +1,72 @@
+// rk_layer.cuh — launch interface of the transformer-layer kernels: the
+// operations of rakkan-mesh's gpu.Batch (internal/gpu/batch.go:282-331) and
+// of llm.Stage.Forward (internal/llm/model.go:522-613).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rk {
+
+// RMSNorm of `segs` segments of n floats, `stride` apart (batch.go:285-287):
+// out = w·(Rsqrt32(Dot32(x,x)·recipN + eps)·x). out may equal in.
+cudaError_t launch_rmsnorm(const float *in, float *out, const float *w, int n, int segs, int stride, float recipN,
+                           float eps, cudaStream_t st);
+// out[i] += v[i] (batch.go:290-292).
+cudaError_t launch_addvec(float *out, const float *v, int n, cudaStream_t st);
+// Rotates adjacent pairs of q (qDim) and k (kvDim) with one position's
+// cos/sin rows (batch.go:296-298).
+cudaError_t launch_rope(float *q, float *k, int qDim, int kvDim, int hs, const float *cos_, const float *sin_,
+                        cudaStream_t st);
+cudaError_t launch_copy(const float *src, float *dst, int n, cudaStream_t st);
+// x[i] = x[i] + y[i], canonicalised if asked (batch.go:320-326).
+cudaError_t launch_residual(float *x, const float *y, int n, int canonical, cudaStream_t st);
+// a[i] = silu(a[i])·b[i] (batch.go:329-331).
+cudaError_t launch_silumul(float *a, const float *b, int n, cudaStream_t st);
+
+// Attention of one position over `positions` cached keys/values
+// (batch.go:308-316). `positions` may instead be read from a device int
+// (*positions_dev + positions_add) when positions_dev is not null, so that a
+// captured CUDA graph serves every position; max_positions bounds the grid.
+struct AttnArgs {
+  const float *q;
+  const float *keys, *vals;  // [ctx][kvDim]
+  float *att;                // [heads][att_stride]
+  float *out;                // [heads·hs]
+  int positions, max_positions;
+  const int *positions_dev;
+  int positions_add;
+  int heads, kv_heads, hs, kv_dim, att_stride;
+  float inv_sqrt;
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+
+// The per-token work between the QKV projections and attention in
+// Stage.Forward (model.go:542-568), for a position read from *pos_dev:
+// bias add, QK-norm, RoPE, and the key/value cache append.
+struct QkvPostArgs {
+  float *q, *k, *v;
+  const float *bq, *bk, *bv;      // null without QKVBias
+  const float *q_norm, *k_norm;   // null without QKNorm
+  const float *cos_, *sin_;       // [ctx][hs/2]
+  float *key_cache, *val_cache;   // [ctx][kvDim]
+  const int *pos_dev;
+  int heads, kv_heads, hs;
+  float eps, recip_hs;
+};
+cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st);
+
+// Embed (model.go:660-664): x = dequantized row *token_dev of a table.
+cudaError_t launch_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x,
+                         cudaStream_t st);
+
+// argmax (sample.go:45-53): the first index of the strict maximum.
+cudaError_t launch_argmax(const float *v, int n, int *out, cudaStream_t st);
+
+// NewRope (model.go:428-441) on the device: cos/sin [n][hs/2] for
+// positions 0..n-1, with num.Log(theta), num.Exp and num.Sincos in float64.
+cudaError_t launch_rope_table(double theta, int hs, int n, float *cos_, float *sin_, cudaStream_t st);
+
+// *p += inc (advances the device-resident position of a decode loop).
+cudaError_t launch_add_int(int *p, int inc, cudaStream_t st);
+
+}  // namespace rk

@@ -1,0 +1,63 @@
+// rk_matvec.cuh — launch interface of the matrix-vector kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rk {
+
+// Matrix formats (internal/gpu/device.go:563-582).
+enum Fmt : int { FMT_F32 = 0, FMT_BF16 = 1, FMT_Q8_0 = 2, FMT_Q4_0 = 3 };
+
+// What a matvec does with row r's result v.
+enum Epi : int {
+  EPI_STORE = 0,      // out[r] = v
+  EPI_ADD = 1,        // out[r] = out[r] + v           (model.go:592-594)
+  EPI_ADD_CANON = 2,  // out[r] = Canonical(out[r] + v) (model.go:608-610)
+  EPI_SILU = 3,       // paired rows: out[r] = silu(v_W1) · v_W3 (model.go:601-603)
+};
+
+// Device error codes written to the device's error word.
+enum DevErr : int { DEV_OK = 0, DEV_ERR_TIMEOUT = 1 };
+
+struct MvPart {
+  const uint8_t *w;  // row-major weights: Q8 cols bytes/row, Q4 cols/2, F32 4·cols, BF16 2·cols
+  const float *s;    // row-major scales [rows][cols/32] (quantized formats)
+  float *out;        // output rows (EPI_*)
+  int rows;
+};
+
+// A matvec over up to four matrices sharing one input (gpu.MulVecs /
+// Batch.MatVecs, batch.go:214-269), or over a pair of matrices whose row i
+// is combined by EPI_SILU.
+struct MvArgs {
+  MvPart part[4];
+  int nparts;
+  int fmt;
+  int cols;
+  int epi;
+  // Quantized input (Q8_0 of x): qx[cols], xs[cols/32], xsum[cols/32] (the
+  // sum of each block's qx, used by Q4_0). F32/BF16 read x instead.
+  const int8_t *qx;
+  const float *xs;
+  const int *xsum;
+  const float *x;
+  int *err;
+};
+
+// Quantizes n floats (a whole number of 32-blocks) to Q8_0 as quantize8
+// does (quant.go:34-53), after RMS normalisation when w != nullptr
+// (model.go:632-638, recipN = Recip32(n)). xn, if not null, receives the
+// normalised floats.
+cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
+                                int8_t *qx, float *xs, int *xsum, cudaStream_t st);
+
+// out = matrices · x, bits identical to num.MatVecQ8/Q4/32/BF16.
+cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
+
+int matvec_smem_bytes(int fmt, int cols);
+
+// Raises the kernels' dynamic shared-memory limit; once per device, before
+// any launch or graph capture.
+cudaError_t init_matvec_attributes();
+
+}  // namespace rk
