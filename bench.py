@@ -1,0 +1,295 @@
+#!/usr/bin/env python
+"""Benchmark: batch-1 Q8_0 greedy decode of a Llama-3-8B-shaped model.
+
+The workload is BASELINE.json's headline metric, "Q8 decode tok/s (8B shape,
+bs1)": dim 4096, 32 layers, 32 heads / 8 KV heads, hidden 14336, vocab
+128256, Q8_0 weights (group 32, the reference's only block size), random
+N(0, 0.02) from a fixed seed, a 4096-token key/value context (synthetic
+values) and one decode step per "step": embed -> 32 layers -> RMSNorm ->
+classifier -> argmax, replayed as one CUDA graph.
+
+value:  whole-job decode tokens/s with everything resident in HBM, timed on
+        the device with CUDA events over K steps (max over ranks).
+e2e:    the same through the public C ABI (rk_model_step): each step copies
+        its token from pinned host memory and reads the logits back.
+roofline: the Q8_0 matvec kernels inside the step, each launch timed with
+        CUDA events: algorithmic bytes (weights + scales) / time, against the
+        measured HBM copy bandwidth.
+cpu_baseline: the CPU oracle (a C restatement of the reference's Go CPU
+        path) on a bounded sample of the same step, on this host's cores.
+
+--impl reference runs only that CPU implementation (no GPU).
+With --gpus N (under torchrun) every GPU decodes its own sequence: N
+independent replicas (weak scaling); there is no data-path collective.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rakkan-mesh_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "Q8 decode tok/s (8B shape, bs1)"
+SEED = 20261201
+CTX = 4096
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--dtype", default="q8_0")
+    p.add_argument("--ctx", type=int, default=CTX)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--kernel", default=None, choices=["matvec"],
+                   help="time one kernel alone instead of the decode step (profiling aid)")
+    p.add_argument("--shape", default="28672x4096", help="rows x cols for --kernel matvec")
+    return p.parse_args()
+
+
+def run_kernel(args):
+    """One Q8_0/Q4_0 matvec of --shape, L2 flushed before each launch."""
+    import rkcuda as rk
+    rows, cols = map(int, args.shape.split("x"))
+    fmt = {"q8_0": rk.FMT_Q8_0, "q4_0": rk.FMT_Q4_0}[args.dtype]
+    dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
+    m = rk.Matrix.generate(dev, rows, cols, fmt, SEED, 1, 0.02)
+    m.bench(max(1, args.warmup), flush=True)
+    ms = m.bench(args.steps, flush=True)
+    n = rows * cols
+    nbytes = n + n // 32 * 4 if fmt == rk.FMT_Q8_0 else n // 2 + n // 32 * 4
+    peak, kind = measured_peak()
+    print(json.dumps({"kernel": f"k_matvec_q<{args.dtype}>", "shape": args.shape, "ms": ms,
+                      "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
+                      "frac": nbytes / (ms * 1e-3) / 1e9 / peak}), flush=True)
+    m.free()
+    dev.close()
+
+
+def workload(args):
+    return {"workload": f"{args.model}-shaped {args.dtype} greedy decode, batch 1, {args.ctx}-token KV context",
+            "shape": "dim 4096, 32 layers, 32/8 heads, hidden 14336, vocab 128256" if args.model == "llama3-8b"
+            else args.model,
+            "weights": "random N(0,0.02), seeded, quantized by the reference's quantize8 (group 32)",
+            "batch": 1, "context": args.ctx,
+            "l2": "inputs larger than L2 (8.4 GB of weights + 1.07 GB of KV cache read per step)"}
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            self.p.wait()
+
+    def summary(self):
+        self.f.seek(0)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per Q8_0 matvec launch from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "matvec_q8_llama3-8b.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_sample(args, steps=1, sample_layers=2, threads=None):
+    """Times the CPU oracle on a bounded sample of one decode step: the
+    forward through `sample_layers` of the 32 layers at position ctx (over a
+    synthetic ctx-token cache), plus the classifier; returns the extrapolated
+    whole-step rate and the description."""
+    import rk_oracle as ro
+    import synth
+    threads = threads or ro.THREADS
+    full = synth.config(args.model, args.dtype)
+    c = synth.config(args.model, args.dtype, layers=sample_layers, seq_len=args.ctx + 1)
+    om = ro.OracleModel(c, SEED, ctx=args.ctx + 1, threads=threads)
+    try:
+        om.fill_cache(args.ctx, SEED)
+        x = om.embed_token(1)
+        t_layers, t_head = [], []
+        for _ in range(max(1, steps)):
+            t0 = time.perf_counter()
+            y = om.forward(x, args.ctx)
+            t1 = time.perf_counter()
+            om.logits(y)
+            t2 = time.perf_counter()
+            t_layers.append(t1 - t0)
+            t_head.append(t2 - t1)
+        per_token = statistics.median(t_layers) * full.layers / sample_layers + statistics.median(t_head)
+    finally:
+        om.free()
+    sample = (f"{sample_layers} of {full.layers} layers at position {args.ctx} plus the classifier, scaled to "
+              f"the whole step; {max(1, steps)} step(s), median")
+    return 1.0 / per_token, threads, sample
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    value, cores, sample = cpu_sample(args, steps=max(1, args.steps // 10))
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8xint8->int32, f32 combine", "data": "synthetic",
+            "impl": "reference", "config": workload(args),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    if args.kernel:
+        return run_kernel(args)
+
+    import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    import rkcuda as rk
+    import synth
+
+    dev = rk.Device(local)
+    c = synth.config(args.model, args.dtype, seq_len=args.ctx + 64)
+    dm = synth.DeviceModel(dev, c, SEED, ctx=args.ctx + 64)
+    dm.stage.fill_cache(args.ctx, SEED)
+    pos, tok = args.ctx, 1
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(local)
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Warm-up, then K device-timed steps (graph replays at position ctx).
+    dm.model.bench(pos, max(3, args.warmup))
+    barrier()
+    with Clocks(local) as clk:
+        ms = dm.model.bench(pos, args.steps)
+        barrier()
+    clocks = clk.summary()
+    ms = max_over_ranks(ms)
+
+    # End to end through the public API: token in from pinned host memory,
+    # logits and the next token back, every step.
+    for _ in range(max(3, args.warmup)):
+        dm.model.step(tok, pos)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dm.model.step(tok, pos)
+    barrier()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / args.steps)
+
+    # Roofline of the dominant kernel: every Q8_0 matvec launch of a step
+    # timed with CUDA events on its stream.
+    prof = dm.model.profile(pos, 3)
+    achieved = prof.matvec_bytes / (prof.matvec_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    launches = dm.model.kernel_count()
+
+    baseline = None
+    if rank == 0 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_sample(args)
+        baseline = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+
+    traffic = traffic_per_launch()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8xint8->int32, f32 combine", "data": "synthetic",
+            "config": workload(args),
+            "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4 * c.vocab + 4},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "traffic": traffic, "kernel": "k_matvec_q<Q8_0>",
+                         "bytes_per_step": prof.matvec_bytes, "matvec_ms_per_step": prof.matvec_ms,
+                         "matvec_launches_per_step": prof.matvec_launches,
+                         "eager_step_ms": prof.step_ms},
+            "cpu_baseline": baseline,
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    dm.free()
+    dev.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

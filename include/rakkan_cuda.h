@@ -233,15 +233,29 @@ int rk_generate_normal(rk_device *d, uint64_t seed, uint64_t tid, int64_t offset
 int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, void *q, float *scales);
 
 /* ---- Measurement helpers (device buffers, device stream, CUDA events) ---- */
-/* Times `iters` launches of the Q8/Q4 matvec of m on device-resident input
- * (L2 flushed before each when flush != 0); returns the mean kernel time. */
+/* Times `iters` launches of the matvec of m on device-resident input (L2
+ * flushed before each when flush != 0); returns the mean kernel time. */
 int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per_launch);
-/* Times `iters` graph replays of rk_model_step at position pos with the
- * token and logits on the device; *ms_per_step is the mean, and
- * *ms_matvec the mean total time of the matvec kernels in one step
- * (measured separately, kernel by kernel, with events). */
+/* Times `iters` graph replays of one decode step at position pos (the
+ * position is re-set before each, so every step attends over pos+1
+ * positions); *ms_per_step is the mean, by CUDA events on the device's stream. */
 int rk_bench_model(rk_model *m, int pos, int iters, float *ms_per_step);
+/* Kernel launches in one step's CUDA graph. */
 int rk_model_kernel_count(rk_model *m, int *launches_per_step);
+typedef struct {
+    float step_ms;        /* mean time of one eagerly launched step */
+    float matvec_ms;      /* mean total time of its matvec launches (events around each) */
+    double matvec_bytes;  /* algorithmic bytes those launches read (weights + scales) */
+    int matvec_launches;  /* matvec launches per step */
+    int launches;         /* kernel launches per step */
+} rk_profile;
+/* Runs `iters` steps at position pos launched one kernel at a time (not
+ * as a graph), timing every matvec launch with CUDA events. */
+int rk_model_profile(rk_model *m, int pos, int iters, rk_profile *out);
+/* Fills the stage's key/value caches for positions [0, positions) with the
+ * seeded generator's N(0,1) values (tensor ids 0xA0000 + 2·layer for keys,
+ * + 1 for values): a synthetic context of that length. */
+int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed);
 
 #ifdef __cplusplus
 }

@@ -307,10 +307,23 @@ static float combine32(const float s[32]) {
     return ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
 }
 
-/* num.Dot32, matvec.go:32-43: element i is added to sum i mod 32 in order. */
-float rko_dot32(const float *a, const float *b, int n) {
+/* The hot loops are cloned for AVX2 (no FMA: -ffp-contract=off, and the
+ * clone does not enable it). Vectorizing them keeps each float32 chain in
+ * its order: the 32 lanes of Dot32 and the elements of a weighted sum are
+ * independent chains, and block sums are exact integers. */
+#define RKO_HOT __attribute__((target_clones("avx2", "default")))
+
+/* num.Dot32, matvec.go:32-43: element i is added to sum i mod 32 in order
+ * (whole chunks of 32 as dot32Generic, matvec.go:69-76, then the tail). */
+RKO_HOT float rko_dot32(const float *a, const float *b, int n) {
     float s[32] = {0};
-    for (int i = 0; i < n; i++) {
+    int i = 0;
+    for (; i + 32 <= n; i += 32)
+        for (int j = 0; j < 32; j++) {
+            float p = a[i + j] * b[i + j];
+            s[j] += p;
+        }
+    for (; i < n; i++) {
         float p = a[i] * b[i];
         s[i & 31] += p;
     }
@@ -327,9 +340,15 @@ uint16_t rko_to_bf16(float f) {
 }
 
 /* num.DotBF16, matvec.go:47-58. */
-float rko_dotbf16(const uint16_t *w, const float *x, int n) {
+RKO_HOT float rko_dotbf16(const uint16_t *w, const float *x, int n) {
     float s[32] = {0};
-    for (int i = 0; i < n; i++) {
+    int i = 0;
+    for (; i + 32 <= n; i += 32)
+        for (int j = 0; j < 32; j++) {
+            float p = rko_bf16(w[i + j]) * x[i + j];
+            s[j] += p;
+        }
+    for (; i < n; i++) {
         float p = rko_bf16(w[i]) * x[i];
         s[i & 31] += p;
     }
@@ -452,7 +471,7 @@ void rko_dequant_q4(float *dst, int64_t n, const uint8_t *q, const float *scales
 
 /* quant.go:198-207 (the AVX2 code in dot_amd64.s computes the same exact
  * integers). */
-void rko_block_sums_q8(const int8_t *w, const int8_t *x, int nb, int32_t *sums) {
+RKO_HOT void rko_block_sums_q8(const int8_t *w, const int8_t *x, int nb, int32_t *sums) {
     for (int b = 0; b < nb; b++) {
         int32_t s = 0;
         for (int j = 0; j < 32; j++) s += (int32_t)w[32 * b + j] * (int32_t)x[32 * b + j];
@@ -461,7 +480,7 @@ void rko_block_sums_q8(const int8_t *w, const int8_t *x, int nb, int32_t *sums) 
 }
 
 /* quant.go:209-218. */
-void rko_block_sums_q4(const uint8_t *w, const int8_t *x, int nb, int32_t *sums) {
+RKO_HOT void rko_block_sums_q4(const uint8_t *w, const int8_t *x, int nb, int32_t *sums) {
     for (int b = 0; b < nb; b++) {
         int32_t s = 0;
         for (int j = 0; j < 16; j++) {
@@ -576,29 +595,42 @@ typedef struct {
     void *c;
 } mm_job;
 
-static void mm_rows(const mm_job *j) {
+/* Row i of C: acc[j] for all j, p outer, so every output keeps its own
+ * serial chain over p = 0..k-1 (tensor.go:316-337) while the loop over j
+ * vectorizes. b_kn is B as [k][n] (B itself for matmul, its transpose for
+ * matmul_t). */
+RKO_HOT static void mm_rows(const mm_job *j) {
     int k = j->k, n = j->n;
-    int64_t stride = j->transposed ? 1 : n, step = j->transposed ? k : 1;
-    for (int i = j->lo; i < j->hi; i++) {
-        for (int jj = 0; jj < n; jj++) {
-            int64_t bj = (int64_t)jj * step;
-            if (j->dtype == RKO_DT_F32) {
-                const float *ar = (const float *)j->a + (int64_t)i * k;
-                const float *bf = (const float *)j->b;
-                float acc = 0;
-                for (int p = 0; p < k; p++) {
-                    float prod = ar[p] * bf[(int64_t)p * stride + bj];
-                    acc += prod;
+    if (j->dtype == RKO_DT_F32) {
+        const float *b = (const float *)j->b;
+        float *acc = (float *)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+        for (int i = j->lo; i < j->hi; i++) {
+            const float *ar = (const float *)j->a + (int64_t)i * k;
+            for (int jj = 0; jj < n; jj++) acc[jj] = 0;
+            for (int p = 0; p < k; p++) {
+                const float av = ar[p], *br = b + (int64_t)p * n;
+                for (int jj = 0; jj < n; jj++) {
+                    float prod = av * br[jj];
+                    acc[jj] += prod;
                 }
-                ((float *)j->c)[(int64_t)i * n + jj] = rko_canonical(acc);
-            } else {
-                const int8_t *ar = (const int8_t *)j->a + (int64_t)i * k;
-                const int8_t *bi = (const int8_t *)j->b;
-                uint32_t acc = 0; /* Go's int32 addition wraps */
-                for (int p = 0; p < k; p++) acc += (uint32_t)((int32_t)ar[p] * (int32_t)bi[(int64_t)p * stride + bj]);
-                ((int32_t *)j->c)[(int64_t)i * n + jj] = (int32_t)acc;
             }
+            for (int jj = 0; jj < n; jj++) ((float *)j->c)[(int64_t)i * n + jj] = rko_canonical(acc[jj]);
         }
+        free(acc);
+    } else {
+        const int8_t *b = (const int8_t *)j->b;
+        uint32_t *acc = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)(n > 0 ? n : 1)); /* Go's int32 wraps */
+        for (int i = j->lo; i < j->hi; i++) {
+            const int8_t *ar = (const int8_t *)j->a + (int64_t)i * k;
+            for (int jj = 0; jj < n; jj++) acc[jj] = 0;
+            for (int p = 0; p < k; p++) {
+                const int32_t av = ar[p];
+                const int8_t *br = b + (int64_t)p * n;
+                for (int jj = 0; jj < n; jj++) acc[jj] += (uint32_t)(av * (int32_t)br[jj]);
+            }
+            for (int jj = 0; jj < n; jj++) ((int32_t *)j->c)[(int64_t)i * n + jj] = (int32_t)acc[jj];
+        }
+        free(acc);
     }
 }
 
@@ -610,6 +642,15 @@ static void *mm_thread(void *arg) {
 int rko_tensor_matmul(int dtype, int transposed, int m, int k, int n, const void *a, const void *b, void *c, int threads) {
     if (dtype != RKO_DT_F32 && dtype != RKO_DT_I8) return -1;
     if (m < 0 || k < 0 || n < 0) return -1;
+    const size_t es = dtype == RKO_DT_F32 ? 4 : 1;
+    void *bt = NULL;
+    if (transposed) { /* B [n][k] -> [k][n] */
+        bt = malloc(es * (size_t)k * n + 1);
+        for (int jj = 0; jj < n; jj++)
+            for (int p = 0; p < k; p++)
+                memcpy((char *)bt + es * ((size_t)p * n + jj), (const char *)b + es * ((size_t)jj * k + p), es);
+        b = bt;
+    }
     if (threads < 1) threads = 1;
     if (threads > m) threads = m > 0 ? m : 1;
     mm_job *jobs = (mm_job *)calloc((size_t)threads, sizeof(mm_job));
@@ -627,6 +668,7 @@ int rko_tensor_matmul(int dtype, int transposed, int m, int k, int n, const void
         for (int t = 0; t < started; t++) pthread_join(tids[t], NULL);
     free(jobs);
     free(tids);
+    free(bt);
     return 0;
 }
 
@@ -792,7 +834,7 @@ static void rotate(float *v, int i, float co, float si) {
 }
 
 /* Stage.Forward, model.go:522-613. */
-int rko_stage_forward(rko_stage *s, float *x, int pos) {
+RKO_HOT int rko_stage_forward(rko_stage *s, float *x, int pos) {
     const rko_config *c = &s->c;
     if (pos < 0 || pos >= s->ctx) return -1;
     int hs = rko_head_size(c), qDim = c->heads * hs, kvDim = c->kv_heads * hs;
@@ -976,5 +1018,16 @@ void rko_transcendental_stream(uint8_t *out) {
         rko_sincos((f4 - 0.5) * 2e5, &s, &c);
         put64(&o, d2u(s));
         put64(&o, d2u(c));
+    }
+}
+
+/* Fills the stage's key/value caches for positions [0, positions) with the
+ * seeded generator's N(0,1) values, tensor ids 0xA0000 + 2·layer (keys) and
+ * + 1 (values), as rk_stage_fill_cache does on the GPU. */
+void rko_stage_fill_cache(rko_stage *s, int positions, uint64_t seed) {
+    const int kvd = s->c.kv_heads * rko_head_size(&s->c);
+    for (int l = 0; l < s->nlayers; l++) {
+        rko_gen_normal(seed, 0xA0000ull + 2 * (uint64_t)l, 0, (int64_t)positions * kvd, 1.0f, s->keys[l]);
+        rko_gen_normal(seed, 0xA0001ull + 2 * (uint64_t)l, 0, (int64_t)positions * kvd, 1.0f, s->vals[l]);
     }
 }

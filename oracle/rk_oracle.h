@@ -107,6 +107,7 @@ typedef struct rko_stage rko_stage;
 rko_stage *rko_stage_new(const rko_config *c, const rko_layer *layers, int nlayers, int ctx, int threads); /* model.go:466-484 */
 void rko_stage_free(rko_stage *s);
 int rko_stage_forward(rko_stage *s, float *x, int pos);   /* model.go:522-613 */
+void rko_stage_fill_cache(rko_stage *s, int positions, uint64_t seed); /* synthetic context */
 void rko_embed(const rko_config *c, const rko_mat *table, int token, float *x); /* model.go:660-664 */
 void rko_head_logits(const rko_config *c, const float *rms_final, const rko_mat *wcls,
                      const float *x, float *logits, int threads);               /* model.go:667-673 */

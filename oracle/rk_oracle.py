@@ -67,7 +67,7 @@ def lib():
             "rko_head_size": (i, [vp]), "rko_eps": (f, [vp]), "rko_rmsnorm": (None, [vp, vp, vp, i, f]),
             "rko_softmax": (None, [vp, i]), "rko_silu": (f, [f]), "rko_rope_table": (None, [vp, i, vp, vp]),
             "rko_argmax": (i, [vp, i]), "rko_stage_new": (vp, [vp, vp, i, i, i]), "rko_stage_free": (None, [vp]),
-            "rko_stage_forward": (i, [vp, vp, i]), "rko_embed": (None, [vp, vp, i, vp]),
+            "rko_stage_forward": (i, [vp, vp, i]), "rko_stage_fill_cache": (None, [vp, i, u64]), "rko_embed": (None, [vp, vp, i, vp]),
             "rko_head_logits": (None, [vp, vp, vp, vp, vp, i]), "rko_splitmix64": (u64, [u64]),
             "rko_gen_normal": (None, [u64, u64, i64, i64, f, vp]), "rko_transcendental_stream": (None, [vp]),
         }
@@ -222,6 +222,9 @@ class OracleModel:
         if fmt == BF16:
             return synth.to_bf16(w), None
         return quantize(fmt, w)
+
+    def fill_cache(self, positions, seed):
+        lib().rko_stage_fill_cache(self.stage, positions, seed)
 
     def embed_token(self, tok):
         x = np.empty(self.c.dim, np.float32)

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/rakkan_cuda.h"
+#include "rk_common.cuh"
 #include "rk_gen.cuh"
 #include "rk_layer.cuh"
 #include "rk_matvec.cuh"
@@ -312,6 +313,43 @@ extern "C" void rk_matrix_free(rk_matrix *m) {
 extern "C" int64_t rk_matrix_bytes(const rk_matrix *m) { return m ? m->bytes : 0; }
 extern "C" int rk_same_device(const rk_matrix *a, const rk_matrix *b) { return a && b && a->d == b->d; }
 
+// Per-launch timing of the matvec kernels during rk_model_profile: events
+// around each launch on the launching stream, and the launch's algorithmic
+// bytes (weights + scales: matBytes, model.go:269-279).
+struct ProfLaunch {
+  cudaEvent_t e0, e1;
+  double bytes;
+};
+static thread_local std::vector<ProfLaunch> *g_prof = nullptr;
+
+static double algorithmic_bytes(const MvArgs &a) {
+  double b = 0;
+  const int nsub = a.epi == EPI_SILU ? 2 : a.nparts;
+  for (int p = 0; p < nsub; p++) {
+    const double n = (double)a.part[p].rows * a.cols;
+    switch (a.fmt) {
+      case FMT_F32: b += 4 * n; break;
+      case FMT_BF16: b += 2 * n; break;
+      case FMT_Q8_0: b += n + n / 32 * 4; break;
+      default: b += n / 2 + n / 32 * 4;
+    }
+  }
+  return b;
+}
+
+static cudaError_t launch_mv(rk_device *d, const MvArgs &a, cudaStream_t st) {
+  if (!g_prof) return launch_matvec(a, d->sms, st);
+  ProfLaunch pl{};
+  pl.bytes = algorithmic_bytes(a);
+  cudaError_t e = cudaEventCreate(&pl.e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&pl.e1);
+  if (e == cudaSuccess) e = cudaEventRecord(pl.e0, st);
+  if (e == cudaSuccess) e = launch_matvec(a, d->sms, st);
+  if (e == cudaSuccess) e = cudaEventRecord(pl.e1, st);
+  g_prof->push_back(pl);
+  return e;
+}
+
 static MvPart part_of(const rk_matrix *m, float *out) {
   MvPart p;
   p.w = m->w;
@@ -324,7 +362,8 @@ static MvPart part_of(const rk_matrix *m, float *out) {
 // Enqueues products of matrices (same cols) sharing one input, grouping
 // runs of the same format into one launch of up to four matrices.
 static int enqueue_matvecs(rk_device *d, int n, rk_matrix *const *ms, float *const *outs, const float *x_dev,
-                           const int8_t *qx, const float *xs, const int *xsum, int epi) {
+                           const int8_t *qx, const float *xs, const int *xsum, int epi, cudaStream_t st = nullptr) {
+  if (!st) st = d->st;
   int i = 0;
   while (i < n) {
     MvArgs a{};
@@ -342,7 +381,7 @@ static int enqueue_matvecs(rk_device *d, int n, rk_matrix *const *ms, float *con
       i++;
     }
     a.nparts = np;
-    CK(launch_matvec(a, d->sms, d->st));
+    CK(launch_mv(d, a, st));
   }
   return RK_OK;
 }
@@ -985,7 +1024,11 @@ static float host_recip32(float x) {
     m = m * 0.5f;
     e++;
   }
-  const float k24_17 = 0x1.696968p+0f, k8_17 = 0x1.e1e1e2p-2f;  // float32(24.0/17), float32(8.0/17)
+  // float32(24.0/17) and float32(8.0/17), from the bit patterns the device
+  // code uses (rk_common.cuh).
+  float k24_17, k8_17;
+  memcpy(&k24_17, &K_24_17, sizeof k24_17);
+  memcpy(&k8_17, &K_8_17, sizeof k8_17);
   float r = k24_17 - k8_17 * m;
   for (int i = 0; i < 3; i++) {
     const float mr = m * r;
@@ -1016,7 +1059,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     // q, k, v = Wq·xb, Wk·xb, Wv·xb (mulVecs, model.go:539).
     rk_matrix *qkv[3] = {l->wq, l->wk, l->wv};
     float *qkv_out[3] = {s->q, s->k, s->v};
-    int rc = enqueue_matvecs(d, 3, qkv, qkv_out, s->xb, s->qx, s->xs, s->xsum, EPI_STORE);
+    int rc = enqueue_matvecs(d, 3, qkv, qkv_out, s->xb, s->qx, s->xs, s->xsum, EPI_STORE, st);
     if (rc) return rc;
     // Bias, QK-norm, RoPE, cache append (model.go:542-568).
     QkvPostArgs qp{};
@@ -1063,7 +1106,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     // x += Wo·attOut (model.go:588-594).
     if (quantized_fmt(l->wo->fmt))
       CK(launch_quantize_act(s->att_out, qd, nullptr, 0.0f, 0.0f, nullptr, s->qx, s->xs, s->xsum, st));
-    if ((rc = enqueue_matvecs(d, 1, &l->wo, &s->x, s->att_out, s->qx, s->xs, s->xsum, EPI_ADD))) return rc;
+    if ((rc = enqueue_matvecs(d, 1, &l->wo, &s->x, s->att_out, s->qx, s->xs, s->xsum, EPI_ADD, st))) return rc;
     // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603).
     if (quant) CK(launch_quantize_act(s->x, D, vec + l->o_rms_ffn, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
     else CK(launch_rmsnorm(s->x, s->xb, vec + l->o_rms_ffn, D, 1, 0, recipD, eps, st));
@@ -1080,12 +1123,12 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
       a.part[0] = part_of(l->w1, s->hb);
       a.part[1] = part_of(l->w3, s->hb2);
       a.nparts = 2;
-      CK(launch_matvec(a, d->sms, st));
+      CK(launch_mv(d, a, st));
     }
     // x = Canonical(x + W2·hb) (model.go:604-610).
     if (quantized_fmt(l->w2->fmt))
       CK(launch_quantize_act(s->hb, H, nullptr, 0.0f, 0.0f, nullptr, s->qx, s->xs, s->xsum, st));
-    if ((rc = enqueue_matvecs(d, 1, &l->w2, &s->x, s->hb, s->qx, s->xs, s->xsum, EPI_ADD_CANON))) return rc;
+    if ((rc = enqueue_matvecs(d, 1, &l->w2, &s->x, s->hb, s->qx, s->xs, s->xsum, EPI_ADD_CANON, st))) return rc;
   }
   return RK_OK;
 }
@@ -1322,7 +1365,7 @@ static int record_head(rk_head *h, const float *x, cudaStream_t st) {
   a.err = h->d->err_dev;
   a.part[0] = part_of(h->wcls, h->logits);
   a.nparts = 1;
-  CK(launch_matvec(a, h->d->sms, st));
+  CK(launch_mv(h->d, a, st));
   return RK_OK;
 }
 
@@ -1709,4 +1752,64 @@ extern "C" int rk_bench_model(rk_model *m, int pos, int iters, float *ms_per_ste
   if ((rc = check_dev_err(d))) return rc;
   *ms_per_step = ms / iters;
   return RK_OK;
+}
+
+extern "C" int rk_model_profile(rk_model *m, int pos, int iters, rk_profile *out) {
+  if (!m || iters <= 0 || !out) return fail(RK_ERR_ARGS, "bad argument");
+  rk_device *d = m->d;
+  if (pos < 0 || pos >= m->stage->ctx) return fail(RK_ERR_ARGS, "position out of range");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  std::vector<ProfLaunch> launches;
+  cudaEvent_t s0, s1;
+  CK(cudaEventCreate(&s0));
+  CK(cudaEventCreate(&s1));
+  m->pin_tok[4] = pos;
+  g_prof = &launches;
+  CK(cudaEventRecord(s0, d->st));
+  for (int i = 0; i < iters && rc == RK_OK; i++) {
+    cudaError_t e = cudaMemcpyAsync(m->stage->pos_dev, &m->pin_tok[4], 4, cudaMemcpyHostToDevice, d->st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "profile");
+    if (rc == RK_OK) rc = record_model(m, d->st);
+  }
+  g_prof = nullptr;
+  CK(cudaEventRecord(s1, d->st));
+  CK(cudaEventSynchronize(s1));
+  if (rc == RK_OK) rc = check_dev_err(d);
+  float total = 0.0f, mv = 0.0f;
+  double bytes = 0;
+  cudaEventElapsedTime(&total, s0, s1);
+  for (auto &l : launches) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, l.e0, l.e1);
+    mv += ms;
+    bytes += l.bytes;
+    cudaEventDestroy(l.e0);
+    cudaEventDestroy(l.e1);
+  }
+  cudaEventDestroy(s0);
+  cudaEventDestroy(s1);
+  if (rc) return rc;
+  out->step_ms = total / iters;
+  out->matvec_ms = mv / iters;
+  out->matvec_bytes = bytes / iters;
+  out->matvec_launches = (int)(launches.size() / iters);
+  out->launches = m->launches;
+  return RK_OK;
+}
+
+extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
+  if (!s || positions < 0 || positions > s->ctx) return fail(RK_ERR_ARGS, "bad argument");
+  rk_device *d = s->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  const int kvd = s->c.kv_heads * head_size(&s->c);
+  const long long n = (long long)positions * kvd;
+  for (size_t l = 0; l < s->layers.size(); l++) {
+    CK(launch_gen_normal(seed, 0xA0000ull + 2 * l, 0, n, 1.0f, s->keys[l], d->st));
+    CK(launch_gen_normal(seed, 0xA0001ull + 2 * l, 0, n, 1.0f, s->vals[l], d->st));
+  }
+  return sync_dev(d);
 }

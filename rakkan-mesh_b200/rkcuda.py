@@ -31,7 +31,7 @@ EXPORTS = [
     "rk_stage_positions", "rk_stage_forward", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed",
     "rk_model_new", "rk_model_free", "rk_model_step", "rk_model_generate", "rk_tensor_matmul",
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
-    "rk_bench_matvec", "rk_bench_model", "rk_model_kernel_count",
+    "rk_bench_matvec", "rk_bench_model", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
 ]
 
 
@@ -52,6 +52,11 @@ class Config(C.Structure):
                 ("kv_heads", C.c_int), ("vocab", C.c_int), ("seq_len", C.c_int), ("shared_classifier", C.c_int),
                 ("head_dim", C.c_int), ("rope_theta", C.c_double), ("norm_eps", C.c_double), ("qkv_bias", C.c_int),
                 ("qk_norm", C.c_int), ("dtype", C.c_int)]
+
+
+class Profile(C.Structure):
+    _fields_ = [("step_ms", C.c_float), ("matvec_ms", C.c_float), ("matvec_bytes", C.c_double),
+                ("matvec_launches", C.c_int), ("launches", C.c_int)]
 
 
 class HostMatrix(C.Structure):
@@ -107,7 +112,8 @@ def lib():
             "rk_matrix_generate": (i, [vp, i, i, i, u64, u64, f, vp]), "rk_matrix_download": (i, [vp, vp, vp]),
             "rk_generate_normal": (i, [vp, u64, u64, i64, i64, f, vp]), "rk_quantize": (i, [vp, i, vp, i64, vp, vp]),
             "rk_bench_matvec": (i, [vp, i, i, vp]), "rk_bench_model": (i, [vp, i, i, vp]),
-            "rk_model_kernel_count": (i, [vp, vp]),
+            "rk_model_kernel_count": (i, [vp, vp]), "rk_model_profile": (i, [vp, i, i, vp]),
+            "rk_stage_fill_cache": (i, [vp, i, u64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -341,6 +347,9 @@ class Stage:
     def positions(self):
         return lib().rk_stage_positions(self.h)
 
+    def fill_cache(self, positions, seed):
+        _check(lib().rk_stage_fill_cache(self.h, positions, seed))
+
     def forward(self, xs, pos):
         xs = np.ascontiguousarray(xs, dtype=np.float32).copy()
         tokens = xs.size // self.dim
@@ -404,6 +413,11 @@ class Model:
         ms = C.c_float()
         _check(lib().rk_bench_model(self.h, pos, iters, C.byref(ms)))
         return ms.value
+
+    def profile(self, pos, iters):
+        p = Profile()
+        _check(lib().rk_model_profile(self.h, pos, iters, C.byref(p)))
+        return p
 
     def kernel_count(self):
         n = C.c_int()

@@ -113,16 +113,25 @@ class DeviceModel:
     """A whole synthetic model on one device: embed, stage of all layers,
     head and the greedy decode loop (rk_model)."""
 
-    def __init__(self, dev, c, seed, ctx=None):
+    def __init__(self, dev, c, seed, ctx=None, keep_host=False):
+        """keep_host: also download every matrix (host_weights, keyed like
+        the oracle's OracleModel(weights=...)) before the layers own them."""
         self.c, self.dev, self.seed = c, dev, seed
         self.ctx = ctx or c.seq_len
         self.layers = []
+        self.host_weights = {} if keep_host else None
         for l in range(c.layers):
             mats = [generate_matrix(dev, *mat_shape(c, k), mat_fmt(c, k), seed, tid(l, k)) for k in MATS]
+            if keep_host:
+                for k, m in zip(MATS, mats):
+                    self.host_weights[(l, k)] = m.download()
             self.layers.append(rk.Layer(dev, c, mats=mats, vectors=host_layer_vectors(c)))
         ef = embed_fmt(c)
         self.embed = generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_EMBED)
         self.wcls = self.embed if c.shared_classifier else generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_CLS)
+        if keep_host:
+            self.host_weights["embed"] = self.embed.download()
+            self.host_weights["cls"] = self.wcls.download()
         self.stage = rk.Stage(dev, c, self.layers, self.ctx)
         self.head = rk.Head(dev, c, np.ones(c.dim, np.float32), self.wcls)
         self.model = rk.Model(dev, self.embed, self.stage, self.head, c.vocab)
