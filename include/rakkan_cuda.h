@@ -112,6 +112,25 @@ int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x);
  * (MulVecs, device.go:769-793). */
 int rk_mulvecs(int n, rk_matrix *const *ms, float *const *outs, const float *x);
 
+/* out_dev[rows] = m·x_dev[cols] for a Q8_0 or Q4_0 matrix, with x_dev and
+ * out_dev device buffers the caller owns, enqueued on `stream` (a
+ * cudaStream_t; NULL: the device's own stream) and waited for. No
+ * counterpart in the reference: it exists for callers that cannot let the
+ * library allocate device memory during the call — a node that reserves its
+ * whole GPU memory up front for weights, caches and buffers, a worker
+ * whose device memory is metered, or code that keeps cudaMalloc's implicit
+ * synchronisation off the per-token path. The call allocates nothing: the
+ * quantized copy of the input lives in a fixed array inside the library
+ * (40 KiB held on every GPU that loads it, until the process exits), so
+ * cols is limited to RK_NOALLOC_MAX_COLS; wider inputs return
+ * RK_ERR_TOO_BIG. The first call on each device looks the array's address
+ * up (cudaGetSymbolAddress); make that first call before any stream
+ * capture. Every call reuses the same array and overwrites all of it that it
+ * reads, so nothing needs clearing between calls, but two calls that
+ * overlap on the GPU (on different streams) race on it. */
+#define RK_NOALLOC_MAX_COLS 32768
+int rk_matrix_mulvec_noalloc(rk_matrix *m, const float *x_dev, float *out_dev, void *stream);
+
 /* ---- Vectors: Device.UploadVectors, Vectors.Free (batch.go:82-109) ---- */
 int rk_vectors_upload(rk_device *d, const float *v, int64_t n, rk_vectors **out);
 void rk_vectors_free(rk_vectors *v);

@@ -1813,3 +1813,25 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
   }
   return sync_dev(d);
 }
+
+// ---------------------------------------------------------------------------
+// Accessors for rk_noalloc.cu (C++ linkage, not part of the C ABI).
+// ---------------------------------------------------------------------------
+namespace rk {
+int internal_fail(int code, const char *msg) { return fail(code, "%s", msg); }
+
+int internal_matrix_view(const rk_matrix *m, int *device, int *rows, int *cols, int *fmt, const void **w,
+                         const float **scales, void **stream, int **err_word, int *sms) {
+  if (!m) return fail(RK_ERR_ARGS, "null matrix");
+  *device = m->d->ordinal;
+  *rows = m->rows;
+  *cols = m->cols;
+  *fmt = m->fmt;
+  *w = m->w;
+  *scales = m->s;
+  *stream = m->d->st;
+  *err_word = m->d->err_dev;
+  *sms = m->d->sms;
+  return RK_OK;
+}
+}  // namespace rk

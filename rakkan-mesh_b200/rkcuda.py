@@ -18,12 +18,13 @@ FMT_F32, FMT_BF16, FMT_Q8_0, FMT_Q4_0 = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16, DTYPE_Q8_0, DTYPE_Q4_0, DTYPE_Q4_M = 0, 1, 2, 3, 4
 TENSOR_F32, TENSOR_I8, TENSOR_I32 = 0, 1, 2
 MAX_COLS, MAX_ROWS = 1 << 18, 1 << 20
+NOALLOC_MAX_COLS = 32768
 
 # Every symbol include/rakkan_cuda.h declares.
 EXPORTS = [
     "rk_last_error", "rk_version", "rk_device_count", "rk_device_get_info", "rk_device_best", "rk_device_open",
     "rk_device_close", "rk_device_used", "rk_matrix_upload", "rk_matrix_free", "rk_matrix_bytes", "rk_same_device",
-    "rk_matrix_mulvec", "rk_mulvecs", "rk_vectors_upload", "rk_vectors_free", "rk_arena_new",
+    "rk_matrix_mulvec", "rk_mulvecs", "rk_matrix_mulvec_noalloc", "rk_vectors_upload", "rk_vectors_free", "rk_arena_new",
     "rk_arena_set_quant_scratch", "rk_arena_bytes", "rk_arena_free", "rk_batch_begin", "rk_batch_write",
     "rk_batch_read", "rk_batch_matvecs", "rk_batch_quantize", "rk_batch_rmsnorm", "rk_batch_addvec", "rk_batch_rope",
     "rk_batch_copy", "rk_batch_attention", "rk_batch_residual", "rk_batch_silumul", "rk_batch_submit",
@@ -87,6 +88,7 @@ def lib():
             "rk_matrix_upload": (i, [vp, i, i, i, vp, vp, vp]), "rk_matrix_free": (None, [vp]),
             "rk_matrix_bytes": (i64, [vp]), "rk_same_device": (i, [vp, vp]),
             "rk_matrix_mulvec": (i, [vp, vp, vp]), "rk_mulvecs": (i, [i, vp, vp, vp]),
+            "rk_matrix_mulvec_noalloc": (i, [vp, vp, vp, vp]),
             "rk_vectors_upload": (i, [vp, vp, i64, vp]), "rk_vectors_free": (None, [vp]),
             "rk_arena_new": (i, [vp, i64, i64, vp]), "rk_arena_set_quant_scratch": (None, [vp, i64, i64]),
             "rk_arena_bytes": (i64, [vp]), "rk_arena_free": (None, [vp]), "rk_batch_begin": (i, [vp, vp]),
