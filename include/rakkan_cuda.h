@@ -210,6 +210,9 @@ void rk_head_free(rk_head *h);
 int rk_head_logits(rk_head *h, const float *x, float *logits);
 /* Embed (model.go:660-664) from an uploaded table: x[dim] = row token. */
 int rk_embed(rk_matrix *table, int token, float *x);
+/* Sampler.Sample at temperature 0 (sample.go:26-53): the index of the first
+ * strict maximum of n host logits (0 when logits[0] is NaN), on the device. */
+int rk_sample_argmax(rk_device *d, const float *logits, int n, int *index);
 
 /* ---- Whole-model decode on one device: the coordinator's per-token loop
  *      (generate.go:522-585: Embed -> stage forwards -> Head.Logits ->

@@ -180,9 +180,10 @@ extern "C" int rk_device_open(int index, rk_device **out) {
   };
   if (cudaSetDevice(index) != cudaSuccess) return cleanup(fail(RK_ERR_CUDA, "cudaSetDevice(%d)", index));
   cudaError_t e = init_matvec_attributes();
+  if (e == cudaSuccess) e = init_layer_attributes();
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaMalloc(&d->err_dev, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&d->err_dev, 2 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, 2 * sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&d->mv_x, sizeof(float) * RK_MAX_COLS);
   if (e == cudaSuccess) e = cudaMalloc(&d->mv_qx, RK_MAX_COLS);
   if (e == cudaSuccess) e = cudaMalloc(&d->mv_xs, sizeof(float) * (RK_MAX_COLS / 32));
@@ -359,10 +360,19 @@ static MvPart part_of(const rk_matrix *m, float *out) {
   return p;
 }
 
+// How a quantized product gets its Q8_0 input: given in qx/xs/xsum, or
+// quantized by every CTA from x_dev (after rmsNorm with norm_w).
+struct Pro {
+  int pro = PRO_GIVEN;
+  const float *norm_w = nullptr;
+  float recipN = 0.0f, eps = 0.0f;
+};
+
 // Enqueues products of matrices (same cols) sharing one input, grouping
 // runs of the same format into one launch of up to four matrices.
 static int enqueue_matvecs(rk_device *d, int n, rk_matrix *const *ms, float *const *outs, const float *x_dev,
-                           const int8_t *qx, const float *xs, const int *xsum, int epi, cudaStream_t st = nullptr) {
+                           const int8_t *qx, const float *xs, const int *xsum, int epi, cudaStream_t st = nullptr,
+                           Pro pro = Pro()) {
   if (!st) st = d->st;
   int i = 0;
   while (i < n) {
@@ -375,6 +385,12 @@ static int enqueue_matvecs(rk_device *d, int n, rk_matrix *const *ms, float *con
     a.xsum = xsum;
     a.x = x_dev;
     a.err = d->err_dev;
+    if (quantized_fmt(a.fmt)) {
+      a.pro = pro.pro;
+      a.norm_w = pro.norm_w;
+      a.recipN = pro.recipN;
+      a.eps = pro.eps;
+    }
     int np = 0;
     while (i < n && np < 4 && ms[i]->fmt == a.fmt) {
       a.part[np++] = part_of(ms[i], outs[i]);
@@ -979,6 +995,7 @@ struct rk_stage {
   rk_config c{};
   std::vector<rk_layer *> layers;
   int ctx = 0;
+  int att_stride = 0;  // ctx rounded up to 4 floats (16-byte rows of scores)
   // Activations and scratch (gpustage.go:51-83).
   float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att_out = nullptr, *hb = nullptr,
         *hb2 = nullptr, *att = nullptr, *xs = nullptr, *cos_ = nullptr, *sin_ = nullptr, *io = nullptr;
@@ -1049,17 +1066,39 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   const float eps = cfg_eps(c);
   const float recipD = host_recip32((float)D), recipHS = host_recip32((float)hs);
   const float invSqrt = (float)(1 / sqrt((double)hs));
-  const bool quant = cfg_quantized(c);
+  // ms·(rmsNorm(x, norm_w) or x). A quantized product's CTAs quantize their
+  // input themselves when it fits their shared memory; otherwise one
+  // quantize launch fills the stage's scratch first. Float matrices get the
+  // normalised input in xb.
+  auto products = [&](int n, rk_matrix *const *ms, float *const *outs, const float *x, const float *norm_w, int cols,
+                      int epi) -> int {
+    const float recip = host_recip32((float)cols);
+    if (quantized_fmt(ms[0]->fmt)) {
+      if (matvec_fused_ok(ms[0]->fmt, cols)) {
+        Pro p;
+        p.pro = norm_w ? PRO_NORM_QUANT : PRO_QUANT;
+        p.norm_w = norm_w;
+        p.recipN = recip;
+        p.eps = eps;
+        return enqueue_matvecs(d, n, ms, outs, x, nullptr, nullptr, nullptr, epi, st, p);
+      }
+      CK(launch_quantize_act(x, cols, norm_w, recip, eps, nullptr, s->qx, s->xs, s->xsum, st));
+      return enqueue_matvecs(d, n, ms, outs, x, s->qx, s->xs, s->xsum, epi, st);
+    }
+    const float *in = x;
+    if (norm_w) {
+      CK(launch_rmsnorm(x, s->xb, norm_w, cols, 1, 0, recip, eps, st));
+      in = s->xb;
+    }
+    return enqueue_matvecs(d, n, ms, outs, in, nullptr, nullptr, nullptr, epi, st);
+  };
   for (size_t li = 0; li < s->layers.size(); li++) {
     rk_layer *l = s->layers[li];
     const float *vec = l->vecs->v;
-    // rmsNorm(xb, x, RmsAtt) and the Q8_0 form of xb.
-    if (quant) CK(launch_quantize_act(s->x, D, vec + l->o_rms_att, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
-    else CK(launch_rmsnorm(s->x, s->xb, vec + l->o_rms_att, D, 1, 0, recipD, eps, st));
-    // q, k, v = Wq·xb, Wk·xb, Wv·xb (mulVecs, model.go:539).
+    // q, k, v = Wq·xb, Wk·xb, Wv·xb with xb = rmsNorm(x, RmsAtt) (model.go:538-539).
     rk_matrix *qkv[3] = {l->wq, l->wk, l->wv};
     float *qkv_out[3] = {s->q, s->k, s->v};
-    int rc = enqueue_matvecs(d, 3, qkv, qkv_out, s->xb, s->qx, s->xs, s->xsum, EPI_STORE, st);
+    int rc = products(3, qkv, qkv_out, s->x, vec + l->o_rms_att, D, EPI_STORE);
     if (rc) return rc;
     // Bias, QK-norm, RoPE, cache append (model.go:542-568).
     QkvPostArgs qp{};
@@ -1100,41 +1139,50 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.kv_heads = c->kv_heads;
     at.hs = hs;
     at.kv_dim = kvd;
-    at.att_stride = s->ctx;
+    at.att_stride = s->att_stride;
     at.inv_sqrt = invSqrt;
     CK(launch_attention(at, st));
     // x += Wo·attOut (model.go:588-594).
-    if (quantized_fmt(l->wo->fmt))
-      CK(launch_quantize_act(s->att_out, qd, nullptr, 0.0f, 0.0f, nullptr, s->qx, s->xs, s->xsum, st));
-    if ((rc = enqueue_matvecs(d, 1, &l->wo, &s->x, s->att_out, s->qx, s->xs, s->xsum, EPI_ADD, st))) return rc;
-    // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603).
-    if (quant) CK(launch_quantize_act(s->x, D, vec + l->o_rms_ffn, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
-    else CK(launch_rmsnorm(s->x, s->xb, vec + l->o_rms_ffn, D, 1, 0, recipD, eps, st));
+    if ((rc = products(1, &l->wo, &s->x, s->att_out, nullptr, qd, EPI_ADD))) return rc;
+    // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603):
+    // row i of W1 and of W3 in one warp, SiLU·mul as the epilogue.
     {
       MvArgs a{};
       a.fmt = l->w1->fmt;
       a.cols = D;
       a.epi = EPI_SILU;
-      a.qx = s->qx;
-      a.xs = s->xs;
-      a.xsum = s->xsum;
-      a.x = s->xb;
       a.err = d->err_dev;
       a.part[0] = part_of(l->w1, s->hb);
       a.part[1] = part_of(l->w3, s->hb2);
       a.nparts = 2;
+      const float *norm_w = vec + l->o_rms_ffn;
+      if (quantized_fmt(a.fmt) && matvec_fused_ok(a.fmt, D)) {
+        a.pro = PRO_NORM_QUANT;
+        a.x = s->x;
+        a.norm_w = norm_w;
+        a.recipN = recipD;
+        a.eps = eps;
+      } else if (quantized_fmt(a.fmt)) {
+        CK(launch_quantize_act(s->x, D, norm_w, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
+        a.qx = s->qx;
+        a.xs = s->xs;
+        a.xsum = s->xsum;
+      } else {
+        CK(launch_rmsnorm(s->x, s->xb, norm_w, D, 1, 0, recipD, eps, st));
+        a.x = s->xb;
+      }
       CK(launch_mv(d, a, st));
     }
     // x = Canonical(x + W2·hb) (model.go:604-610).
-    if (quantized_fmt(l->w2->fmt))
-      CK(launch_quantize_act(s->hb, H, nullptr, 0.0f, 0.0f, nullptr, s->qx, s->xs, s->xsum, st));
-    if ((rc = enqueue_matvecs(d, 1, &l->w2, &s->x, s->hb, s->qx, s->xs, s->xsum, EPI_ADD_CANON, st))) return rc;
+    if ((rc = products(1, &l->w2, &s->x, s->hb, nullptr, H, EPI_ADD_CANON))) return rc;
   }
   return RK_OK;
 }
 
 // io[tok] -> x, or x -> io[tok] then tok += 1, pos += 1.
 __global__ void k_stage_io(float *io, const int *tok, float *x, int dim, int dir) {
+  griddep_trigger();
+  griddep_wait();
   const long long t = *tok;
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
     if (dir == 0) x[j] = io[t * dim + j];
@@ -1142,6 +1190,8 @@ __global__ void k_stage_io(float *io, const int *tok, float *x, int dim, int dir
   }
 }
 __global__ void k_advance(int *tok, int *pos) {
+  griddep_trigger();
+  griddep_wait();
   if (tok) *tok += 1;
   if (pos) *pos += 1;
 }
@@ -1149,7 +1199,11 @@ __global__ void k_advance(int *tok, int *pos) {
 static int capture(rk_device *d, std::function<int(cudaStream_t)> rec, cudaGraphExec_t *out, size_t *nodes = nullptr) {
   cudaGraph_t graph = nullptr;
   CK(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal));
+  // Kernels of a captured step use programmatic dependent launch: each may
+  // start (and stream its weights) while its predecessor finishes.
+  g_pdl = true;
   int rc = rec(d->st);
+  g_pdl = false;
   cudaError_t e = cudaStreamEndCapture(d->st, &graph);
   if (rc) {
     if (graph) cudaGraphDestroy(graph);
@@ -1194,7 +1248,8 @@ extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *l
   ALLOC(att_out, 4 * (size_t)qd);
   ALLOC(hb, 4 * (size_t)H);
   ALLOC(hb2, 4 * (size_t)H);
-  ALLOC(att, 4 * (size_t)c->heads * ctx);
+  s->att_stride = (ctx + 3) & ~3;
+  ALLOC(att, 4 * (size_t)c->heads * s->att_stride);
   ALLOC(qx, (size_t)widest);
   ALLOC(xs, 4 * (size_t)(widest / 32 + 1));
   ALLOC(xsum, 4 * (size_t)(widest / 32 + 1));
@@ -1228,11 +1283,11 @@ extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *l
   rc = capture(
       d,
       [s, D](cudaStream_t st) {
-        k_stage_io<<<(D + 255) / 256, 256, 0, st>>>(s->io, s->tok_dev, s->x, D, 0);
+        CK(launch_k(k_stage_io, (D + 255) / 256, 256, 0, st, s->io, (const int *)s->tok_dev, s->x, D, 0));
         int r = record_layers(s, st);
         if (r) return r;
-        k_stage_io<<<(D + 255) / 256, 256, 0, st>>>(s->io, s->tok_dev, s->x, D, 1);
-        k_advance<<<1, 1, 0, st>>>(s->tok_dev, s->pos_dev);
+        CK(launch_k(k_stage_io, (D + 255) / 256, 256, 0, st, s->io, (const int *)s->tok_dev, s->x, D, 1));
+        CK(launch_k(k_advance, 1, 1, 0, st, s->tok_dev, s->pos_dev));
         CK(cudaGetLastError());
         return RK_OK;
       },
@@ -1350,19 +1405,27 @@ static int record_head(rk_head *h, const float *x, cudaStream_t st) {
   const int D = h->c.dim;
   const float recipD = host_recip32((float)D);
   const float eps = cfg_eps(&h->c);
-  if (quantized_fmt(h->wcls->fmt))
-    CK(launch_quantize_act(x, D, h->rms, recipD, eps, nullptr, h->qx, h->xs, h->xsum, st));
-  else
-    CK(launch_rmsnorm(x, h->xb, h->rms, D, 1, 0, recipD, eps, st));
   MvArgs a{};
   a.fmt = h->wcls->fmt;
   a.cols = D;
   a.epi = EPI_STORE;
-  a.qx = h->qx;
-  a.xs = h->xs;
-  a.xsum = h->xsum;
-  a.x = h->xb;
   a.err = h->d->err_dev;
+  if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D)) {
+    // Every CTA computes rmsNorm + quantize8 of x itself.
+    a.pro = PRO_NORM_QUANT;
+    a.x = x;
+    a.norm_w = h->rms;
+    a.recipN = recipD;
+    a.eps = eps;
+  } else if (quantized_fmt(h->wcls->fmt)) {
+    CK(launch_quantize_act(x, D, h->rms, recipD, eps, nullptr, h->qx, h->xs, h->xsum, st));
+    a.qx = h->qx;
+    a.xs = h->xs;
+    a.xsum = h->xsum;
+  } else {
+    CK(launch_rmsnorm(x, h->xb, h->rms, D, 1, 0, recipD, eps, st));
+    a.x = h->xb;
+  }
   a.part[0] = part_of(h->wcls, h->logits);
   a.nparts = 1;
   CK(launch_mv(h->d, a, st));
@@ -1410,13 +1473,18 @@ struct rk_model {
   rk_stage *stage = nullptr;
   rk_head *head = nullptr;
   int *token_dev = nullptr, *next_dev = nullptr;
+  unsigned long long *key_dev = nullptr;  // argmax key (0 between steps)
   int *pin_tok = nullptr;
   float *pin_logits = nullptr;
   cudaGraphExec_t graph = nullptr;
   int launches = 0;
 };
 
-__global__ void k_feed_token(const int *next, int *token) { *token = *next; }
+__global__ void k_feed_token(const int *next, int *token) {
+  griddep_trigger();
+  griddep_wait();
+  *token = *next;
+}
 
 static int record_model(rk_model *m, cudaStream_t st) {
   rk_stage *s = m->stage;
@@ -1424,9 +1492,8 @@ static int record_model(rk_model *m, cudaStream_t st) {
   int rc = record_layers(s, st);
   if (rc) return rc;
   if ((rc = record_head(m->head, s->x, st))) return rc;
-  CK(launch_argmax(m->head->logits, s->c.vocab, m->next_dev, st));
-  k_feed_token<<<1, 1, 0, st>>>(m->next_dev, m->token_dev);
-  k_advance<<<1, 1, 0, st>>>(nullptr, s->pos_dev);
+  CK(launch_argmax_multi(m->head->logits, s->c.vocab, m->key_dev, m->next_dev, m->token_dev, st));
+  CK(launch_k(k_advance, 1, 1, 0, st, (int *)nullptr, s->pos_dev));
   CK(cudaGetLastError());
   return RK_OK;
 }
@@ -1438,6 +1505,7 @@ static void model_release(rk_model *m) {
   if (m->graph) cudaGraphExecDestroy(m->graph);
   cudaFree(m->token_dev);
   cudaFree(m->next_dev);
+  cudaFree(m->key_dev);
   cudaFreeHost(m->pin_tok);
   cudaFreeHost(m->pin_logits);
   delete m;
@@ -1456,6 +1524,8 @@ extern "C" int rk_model_new(rk_device *d, rk_matrix *embed, rk_stage *stage, rk_
   m->stage = stage;
   m->head = head;
   cudaError_t e = cudaMalloc(&m->token_dev, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&m->key_dev, 16);
+  if (e == cudaSuccess) e = cudaMemset(m->key_dev, 0, 16);
   if (e == cudaSuccess) e = cudaMalloc(&m->next_dev, 16);
   if (e == cudaSuccess) e = cudaMallocHost(&m->pin_tok, 64);
   if (e == cudaSuccess) e = cudaMallocHost(&m->pin_logits, 4 * (size_t)stage->c.vocab);
@@ -1685,10 +1755,23 @@ extern "C" int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, voi
 // ---------------------------------------------------------------------------
 // Measurement helpers
 // ---------------------------------------------------------------------------
+// Reads a buffer twice L2's size, so the timed kernel starts with L2 full of
+// clean lines that are not its own (a write-based flush would leave dirty
+// lines whose write-back would land inside the timed kernel).
+__global__ void k_flush_read(const int4 *p, long long n, int *sink) {
+  int acc = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int4 v = p[i];
+    acc ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (acc == 0x7fffffff) *sink = acc;  // never true for the zeroed buffer; keeps the loads
+}
+
 static int ensure_flush(rk_device *d) {
   if (d->flush) return RK_OK;
   d->flush_bytes = (size_t)256 << 20;  // twice the 126 MB L2
   CK(cudaMalloc(&d->flush, d->flush_bytes));
+  CK(cudaMemset(d->flush, 0, d->flush_bytes));
   return RK_OK;
 }
 
@@ -1708,7 +1791,7 @@ extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per
   float total = 0.0f;
   float *out = d->mv_out;
   for (int i = 0; i < iters + 1; i++) {
-    if (flush) CK(cudaMemsetAsync(d->flush, i & 0xff, d->flush_bytes, d->st));
+    if (flush) k_flush_read<<<d->sms * 4, 512, 0, d->st>>>((const int4 *)d->flush, (long long)(d->flush_bytes / 16), d->err_dev + 1);
     CK(cudaEventRecord(e0, d->st));
     if ((rc = enqueue_matvecs(d, 1, &m, &out, d->mv_x, d->mv_qx, d->mv_xs, d->mv_xsum, EPI_STORE))) return rc;
     CK(cudaEventRecord(e1, d->st));
@@ -1835,3 +1918,20 @@ int internal_matrix_view(const rk_matrix *m, int *device, int *rows, int *cols, 
   return RK_OK;
 }
 }  // namespace rk
+
+extern "C" int rk_sample_argmax(rk_device *d, const float *logits, int n, int *index) {
+  if (!d || !logits || !index || n <= 0 || n > RK_MAX_ROWS) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  memcpy(d->pin_out, logits, sizeof(float) * (size_t)n);
+  CK(cudaMemcpyAsync(d->mv_out, d->pin_out, sizeof(float) * (size_t)n, cudaMemcpyHostToDevice, d->st));
+  // The key and the index use the device scratch of MulVecs (mv_xsum).
+  unsigned long long *key = reinterpret_cast<unsigned long long *>(d->mv_xsum);
+  CK(cudaMemsetAsync(key, 0, sizeof *key, d->st));
+  CK(launch_argmax_multi(d->mv_out, n, key, d->mv_xsum + 2, nullptr, d->st));
+  CK(cudaMemcpyAsync(d->pin_in, d->mv_xsum + 2, sizeof(int), cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  memcpy(index, d->pin_in, sizeof(int));
+  return RK_OK;
+}

@@ -11,6 +11,8 @@
 // not CUDA's expf / rsqrtf / division.
 #pragma once
 #include <cstdint>
+#include <utility>
+
 #include <cuda_runtime.h>
 
 #define RK_DEV __device__ __forceinline__
@@ -174,10 +176,41 @@ RK_DEV float warp_gomax(float v) {
   return v;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor is still
+// running; it calls griddep_wait() before it reads anything the predecessor
+// writes and before its own first global write, and may do read-only work
+// (streaming weights) before that. griddep_trigger() lets the successor
+// launch. Both are no-ops for a kernel launched without the attribute.
+RK_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+RK_DEV void griddep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 RK_DEV uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Whether launches on this host thread use programmatic dependent launch
+// (set while a decode step is being recorded into a CUDA graph).
+inline thread_local bool g_pdl = false;
+
+// Launches kernel k with the programmatic stream-serialization attribute
+// when g_pdl is set, else as an ordinary launch.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
 }  // namespace rk

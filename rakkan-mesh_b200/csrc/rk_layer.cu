@@ -15,6 +15,8 @@ namespace rk {
 // ---------------------------------------------------------------------------
 __global__ void k_rmsnorm(const float *in, float *out, const float *__restrict__ w, int n, int stride, float recipN,
                           float eps) {
+  griddep_trigger();
+  griddep_wait();
   const int lane = threadIdx.x;
   const float *x = in + (long long)blockIdx.x * stride;
   float *o = out + (long long)blockIdx.x * stride;
@@ -29,17 +31,19 @@ __global__ void k_rmsnorm(const float *in, float *out, const float *__restrict__
 cudaError_t launch_rmsnorm(const float *in, float *out, const float *w, int n, int segs, int stride, float recipN,
                            float eps, cudaStream_t st) {
   if (segs <= 0) return cudaSuccess;
-  k_rmsnorm<<<segs, 32, 0, st>>>(in, out, w, n, stride, recipN, eps);
+  launch_k(k_rmsnorm, segs, 32, 0, st, in, out, w, n, stride, recipN, eps);
   return cudaGetLastError();
 }
 
 __global__ void k_addvec(float *out, const float *v, int n) {
+  griddep_trigger();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = __fadd_rn(out[i], v[i]);
 }
 cudaError_t launch_addvec(float *out, const float *v, int n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_addvec<<<(n + 255) / 256, 256, 0, st>>>(out, v, n);
+  launch_k(k_addvec, (n + 255) / 256, 256, 0, st, out, v, n);
   return cudaGetLastError();
 }
 
@@ -51,6 +55,8 @@ RK_DEV void rotate_pair(float *v, int i, float co, float si) {
 }
 
 __global__ void k_rope(float *q, float *k, int pairs, int kvDim, int hs, const float *cos_, const float *sin_) {
+  griddep_trigger();
+  griddep_wait();
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= pairs) return;
   const int i = 2 * p;
@@ -63,21 +69,25 @@ cudaError_t launch_rope(float *q, float *k, int qDim, int kvDim, int hs, const f
                         cudaStream_t st) {
   const int pairs = qDim / 2;
   if (pairs <= 0) return cudaSuccess;
-  k_rope<<<(pairs + 255) / 256, 256, 0, st>>>(q, k, pairs, kvDim, hs, cos_, sin_);
+  launch_k(k_rope, (pairs + 255) / 256, 256, 0, st, q, k, pairs, kvDim, hs, cos_, sin_);
   return cudaGetLastError();
 }
 
 __global__ void k_copy(const float *src, float *dst, int n) {
+  griddep_trigger();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) dst[i] = src[i];
 }
 cudaError_t launch_copy(const float *src, float *dst, int n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_copy<<<(n + 255) / 256, 256, 0, st>>>(src, dst, n);
+  launch_k(k_copy, (n + 255) / 256, 256, 0, st, src, dst, n);
   return cudaGetLastError();
 }
 
 __global__ void k_residual(float *x, const float *y, int n, int canon) {
+  griddep_trigger();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = __fadd_rn(x[i], y[i]);
@@ -85,17 +95,19 @@ __global__ void k_residual(float *x, const float *y, int n, int canon) {
 }
 cudaError_t launch_residual(float *x, const float *y, int n, int canonical_, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_residual<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, canonical_);
+  launch_k(k_residual, (n + 255) / 256, 256, 0, st, x, y, n, canonical_);
   return cudaGetLastError();
 }
 
 __global__ void k_silumul(float *a, const float *b, int n) {
+  griddep_trigger();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) a[i] = __fmul_rn(silu(a[i]), b[i]);
 }
 cudaError_t launch_silumul(float *a, const float *b, int n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_silumul<<<(n + 255) / 256, 256, 0, st>>>(a, b, n);
+  launch_k(k_silumul, (n + 255) / 256, 256, 0, st, a, b, n);
   return cudaGetLastError();
 }
 
@@ -111,6 +123,8 @@ RK_DEV int attn_positions(const AttnArgs &a) {
 // for the group.
 constexpr int kScoreWarps = 8;
 __global__ void __launch_bounds__(kScoreWarps * 32) k_attn_scores(const AttnArgs a) {
+  griddep_trigger();
+  griddep_wait();
   const int P = attn_positions(a);
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * kScoreWarps + (threadIdx.x >> 5);
@@ -127,13 +141,57 @@ __global__ void __launch_bounds__(kScoreWarps * 32) k_attn_scores(const AttnArgs
   }
 }
 
+// Scores, a lane per position: CTA (32-position tile, kv head) stages the
+// tile's keys in shared memory (rows padded to HS+1 floats, so lanes reading
+// different rows hit different banks); warp g computes, for query head g of
+// the group, lane p's whole Dot32(q, k_p) in registers: element e is added
+// to partial sum e mod 32 in increasing e, then the fixed tree
+// (matvec.go:60-66). No shuffles.
+constexpr int kTileT = 32;
+template <int HS>
+__global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int gpb) {
+  griddep_trigger();
+  griddep_wait();
+  __shared__ float sk[kTileT * (HS + 1)];
+  __shared__ float sq[8 * HS];
+  const int P = attn_positions(a);
+  const int t0 = blockIdx.x * kTileT;
+  if (t0 >= P) return;
+  const int kvh = blockIdx.y, kvMul = a.heads / a.kv_heads;
+  const int g0 = blockIdx.z * gpb, ng = min(gpb, kvMul - g0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nt = min(kTileT, P - t0);
+  for (int e = threadIdx.x; e < kTileT * HS; e += blockDim.x) {
+    const int p = e / HS, i = e % HS;
+    sk[p * (HS + 1) + i] = p < nt ? a.keys[(long long)(t0 + p) * a.kv_dim + kvh * HS + i] : 0.0f;
+  }
+  for (int e = threadIdx.x; e < ng * HS; e += blockDim.x) sq[e] = a.q[(kvh * kvMul + g0) * HS + e];
+  __syncthreads();
+  if (warp >= ng) return;
+  const float *q = sq + warp * HS;
+  const float *k = sk + lane * (HS + 1);
+  float s[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) s[j] = 0.0f;
+#pragma unroll
+  for (int e = 0; e < HS; e++) s[e & 31] = __fadd_rn(s[e & 31], __fmul_rn(q[e], k[e]));
+  float e8[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) e8[j] = __fadd_rn(__fadd_rn(s[j], s[j + 8]), __fadd_rn(s[j + 16], s[j + 24]));
+  const float dot = __fadd_rn(__fadd_rn(__fadd_rn(e8[0], e8[1]), __fadd_rn(e8[2], e8[3])),
+                              __fadd_rn(__fadd_rn(e8[4], e8[5]), __fadd_rn(e8[6], e8[7])));
+  if (lane < nt) a.att[(long long)(kvh * kvMul + g0 + warp) * a.att_stride + t0 + lane] = __fmul_rn(dot, a.inv_sqrt);
+}
+
 // softmax (model.go:640-654): the maximum in any order (Go's max is order
 // free), Exp32 of the differences, their sum in position order by one
 // thread, then multiplication by Recip32 of the sum. One CTA per head.
 constexpr int kSoftmaxThreads = 256;
 constexpr int kSoftmaxSmem = 12224;  // floats kept in shared memory (static limit 48 KB)
 __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs a) {
-  __shared__ float sv[kSoftmaxSmem];
+  griddep_trigger();
+  griddep_wait();
+  __shared__ __align__(16) float sv[kSoftmaxSmem];
   __shared__ float red[kSoftmaxThreads / 32];
   __shared__ float s_val;
   const int P = attn_positions(a);
@@ -159,19 +217,23 @@ __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs
   for (int i = threadIdx.x; i < P; i += blockDim.x) v[i] = exp32(__fsub_rn(v[i], m));
   __syncthreads();
   if (threadIdx.x == 0) {
+    // One chain in position order; the loads run two float4s ahead of it.
     float sum = 0.0f;
     int i = 0;
-    for (; i + 8 <= P; i += 8) {
-      float t0 = v[i], t1 = v[i + 1], t2 = v[i + 2], t3 = v[i + 3], t4 = v[i + 4], t5 = v[i + 5], t6 = v[i + 6],
-            t7 = v[i + 7];
-      sum = __fadd_rn(sum, t0);
-      sum = __fadd_rn(sum, t1);
-      sum = __fadd_rn(sum, t2);
-      sum = __fadd_rn(sum, t3);
-      sum = __fadd_rn(sum, t4);
-      sum = __fadd_rn(sum, t5);
-      sum = __fadd_rn(sum, t6);
-      sum = __fadd_rn(sum, t7);
+    if (in_smem) {
+      const float4 *v4 = reinterpret_cast<const float4 *>(sv);
+      const int n4 = P >> 2;
+      float4 c0 = n4 > 0 ? v4[0] : make_float4(0, 0, 0, 0), c1 = n4 > 1 ? v4[1] : make_float4(0, 0, 0, 0);
+      for (int j = 0; j < n4; j++) {
+        const float4 nx = j + 2 < n4 ? v4[j + 2] : make_float4(0, 0, 0, 0);
+        sum = __fadd_rn(sum, c0.x);
+        sum = __fadd_rn(sum, c0.y);
+        sum = __fadd_rn(sum, c0.z);
+        sum = __fadd_rn(sum, c0.w);
+        c0 = c1;
+        c1 = nx;
+      }
+      i = n4 << 2;
     }
     for (; i < P; i++) sum = __fadd_rn(sum, v[i]);
     s_val = recip32(sum);
@@ -184,6 +246,8 @@ __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs
 // Weighted values: out[h·hs+i] = sum over t in order from +0 of
 // float32(att[h][t]·v_t[i]). A thread per output element.
 __global__ void __launch_bounds__(128) k_attn_wsum(const AttnArgs a) {
+  griddep_trigger();
+  griddep_wait();
   const int g = blockIdx.x * blockDim.x + threadIdx.x;
   const int qDim = a.heads * a.hs;
   if (g >= qDim) return;
@@ -206,15 +270,119 @@ __global__ void __launch_bounds__(128) k_attn_wsum(const AttnArgs a) {
   a.out[g] = acc;
 }
 
+// Weighted values, staged: CTA (kv head, 32-element slice of the head, group
+// of query heads) owns GPB heads × 32 elements, one serial chain per thread.
+// The chains are bound by FADD latency (one position per few cycles), so
+// the V row-slices (128 B per position, shared by the group's heads) and
+// the heads' attention weights stream through a kWsStages-deep cp.async
+// pipeline in shared memory and each thread's chain reads only shared
+// memory. Positions go in order from 0 and every product is rounded, as
+// model.go:580-586 sums them.
+constexpr int kWsT = 128;     // positions per chunk
+constexpr int kWsStages = 8;  // chunks in flight
+constexpr int kWsMaxGroup = 8;
+
+RK_DEV void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+RK_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+RK_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kWsMaxGroup * 32) k_attn_wsum_staged(const AttnArgs a, int gpb) {
+  griddep_trigger();
+  griddep_wait();
+  extern __shared__ __align__(16) float ws_smem[];
+  float *sV = ws_smem;                            // [stages][kWsT][32]
+  float *sA = ws_smem + kWsStages * kWsT * 32;    // [stages][gpb][kWsT]
+  const int P = attn_positions(a);
+  const int kvh = blockIdx.x, slice = blockIdx.y;
+  const int kvMul = a.heads / a.kv_heads;
+  const int g0 = blockIdx.z * gpb;
+  const int ng = min(gpb, kvMul - g0);
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int nthreads = blockDim.x;
+  const float *vbase = a.vals + kvh * a.hs + slice * 32;
+  const long long kv = a.kv_dim;
+  const int nchunks = (P + kWsT - 1) / kWsT;
+
+  auto load = [&](int c) {
+    if (c < nchunks) {
+      const int t0 = c * kWsT, stage = c % kWsStages;
+      float *dv = sV + stage * kWsT * 32;
+      for (int e = threadIdx.x; e < kWsT * 8; e += nthreads) {
+        const int tt = e >> 3, piece = e & 7;
+        const int t = min(t0 + tt, P - 1);  // rows past P are loaded but never used
+        cp_async16(dv + tt * 32 + piece * 4, vbase + t * kv + piece * 4);
+      }
+      float *da = sA + stage * kWsMaxGroup * kWsT;
+      for (int e = threadIdx.x; e < ng * (kWsT / 4); e += nthreads) {
+        const int gg = e / (kWsT / 4), piece = e % (kWsT / 4);
+        const int h = kvh * kvMul + g0 + gg;
+        const int t = min(t0 + piece * 4, ((P - 1) / 4) * 4);
+        cp_async16(da + gg * kWsT + piece * 4, a.att + (long long)h * a.att_stride + t);
+      }
+    }
+    cp_async_commit();
+  };
+
+  for (int c = 0; c < kWsStages - 1; c++) load(c);
+  float acc = 0.0f;
+  for (int c = 0; c < nchunks; c++) {
+    load(c + kWsStages - 1);
+    cp_async_wait<kWsStages - 1>();
+    __syncthreads();
+    const int stage = c % kWsStages;
+    const float *v = sV + stage * kWsT * 32 + lane;
+    const float *w = sA + stage * kWsMaxGroup * kWsT + g * kWsT;
+    const int n = min(kWsT, P - c * kWsT);
+    if (g < ng) {
+      int tt = 0;
+#pragma unroll 8
+      for (; tt < n; tt++) acc = __fadd_rn(acc, __fmul_rn(w[tt], v[tt * 32]));
+    }
+    __syncthreads();
+  }
+  if (g < ng) a.out[(kvh * kvMul + g0 + g) * a.hs + slice * 32 + lane] = acc;
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   const int maxP = a.positions_dev ? a.max_positions : a.positions;
   if (maxP <= 0) return cudaSuccess;
-  dim3 g1((maxP + kScoreWarps - 1) / kScoreWarps, a.kv_heads);
-  k_attn_scores<<<g1, kScoreWarps * 32, 0, st>>>(a);
-  k_attn_softmax<<<a.heads, kSoftmaxThreads, 0, st>>>(a);
+  const int kvMul = a.heads / a.kv_heads;
+  if (a.hs == 64 || a.hs == 128) {
+    const int gpb = kvMul < 8 ? kvMul : 8;
+    dim3 g1((maxP + kTileT - 1) / kTileT, a.kv_heads, (kvMul + gpb - 1) / gpb);
+    if (a.hs == 64) launch_k(k_attn_scores_tile<64>, g1, gpb * 32 < 64 ? 64 : gpb * 32, 0, st, a, gpb);
+    else launch_k(k_attn_scores_tile<128>, g1, gpb * 32 < 64 ? 64 : gpb * 32, 0, st, a, gpb);
+  } else {
+    dim3 g1((maxP + kScoreWarps - 1) / kScoreWarps, a.kv_heads);
+    launch_k(k_attn_scores, g1, kScoreWarps * 32, 0, st, a);
+  }
+  launch_k(k_attn_softmax, a.heads, kSoftmaxThreads, 0, st, a);
   const int qDim = a.heads * a.hs;
-  k_attn_wsum<<<(qDim + 127) / 128, 128, 0, st>>>(a);
+  // The staged kernel copies 16-byte pieces: it needs whole 32-float slices
+  // and 16-byte-aligned rows of values and scores.
+  const bool staged = a.hs % 32 == 0 && a.kv_dim % 4 == 0 && a.att_stride % 4 == 0 &&
+                      reinterpret_cast<uintptr_t>(a.vals) % 16 == 0 && reinterpret_cast<uintptr_t>(a.att) % 16 == 0;
+  if (staged) {
+    const int gpb = kvMul < kWsMaxGroup ? kvMul : kWsMaxGroup;
+    dim3 g3(a.kv_heads, a.hs / 32, (kvMul + gpb - 1) / gpb);
+    const size_t smem = sizeof(float) * (kWsStages * kWsT * 32 + kWsStages * kWsMaxGroup * kWsT);
+    launch_k(k_attn_wsum_staged, g3, gpb * 32, smem, st, a, gpb);
+  } else {
+    launch_k(k_attn_wsum, (qDim + 127) / 128, 128, 0, st, a);
+  }
   return cudaGetLastError();
+}
+
+cudaError_t init_layer_attributes() {
+  const int smem = sizeof(float) * (kWsStages * kWsT * 32 + kWsStages * kWsMaxGroup * kWsT);
+  return cudaFuncSetAttribute(k_attn_wsum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -222,6 +390,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
 // otherwise key/value head b - heads. One warp each.
 // ---------------------------------------------------------------------------
 __global__ void k_qkv_post(const QkvPostArgs a) {
+  griddep_trigger();
+  griddep_wait();
   const int lane = threadIdx.x;
   const int hs = a.hs, half = hs / 2;
   const int pos = *a.pos_dev;
@@ -263,7 +433,7 @@ __global__ void k_qkv_post(const QkvPostArgs a) {
 }
 
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st) {
-  k_qkv_post<<<a.heads + a.kv_heads, 32, 0, st>>>(a);
+  launch_k(k_qkv_post, a.heads + a.kv_heads, 32, 0, st, a);
   return cudaGetLastError();
 }
 
@@ -271,6 +441,8 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st) {
 // Embed (Matrix.Row + DequantQ8/Q4, model.go:216-231; quant.go:130-146).
 // ---------------------------------------------------------------------------
 __global__ void k_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x) {
+  griddep_trigger();
+  griddep_wait();
   const long long tok = *token_dev;
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
     float v;
@@ -292,7 +464,7 @@ __global__ void k_embed(int fmt, const void *table, const float *scales, int dim
 }
 cudaError_t launch_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x,
                          cudaStream_t st) {
-  k_embed<<<(dim + 255) / 256, 256, 0, st>>>(fmt, table, scales, dim, token_dev, x);
+  launch_k(k_embed, (dim + 255) / 256, 256, 0, st, fmt, table, scales, dim, token_dev, x);
   return cudaGetLastError();
 }
 
@@ -302,6 +474,8 @@ cudaError_t launch_embed(int fmt, const void *table, const float *scales, int di
 // the reference's loop.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_argmax(const float *v, int n, int *out) {
+  griddep_trigger();
+  griddep_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   // Reference semantics: best = 0; for i: if v[i] > v[best] best = i. With
@@ -349,13 +523,70 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *v, int n, int *out
     if (threadIdx.x == 0) *out = bi;
   }
 }
+// argmax over many CTAs: each non-NaN value v_i becomes the key
+// (order(v_i) << 32) | ~i, where order() maps floats to unsigned integers in
+// increasing order after folding -0 into +0 (the reference compares with
+// `>`, under which they are equal); the largest key is the largest value at
+// the smallest index, i.e. the first strict maximum. k_argmax_finish turns
+// the key into the index, answers 0 when v[0] is NaN (nothing is `>` NaN, so
+// the reference's loop never leaves index 0), and clears the key.
+RK_DEV unsigned long long argmax_key(float v, int i) {
+  uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(i));
+}
+
+__global__ void __launch_bounds__(256) k_argmax_part(const float *v, int n, unsigned long long *key) {
+  griddep_trigger();
+  griddep_wait();
+  __shared__ unsigned long long red[8];
+  unsigned long long best = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float x = v[i];
+    if (x == x) {
+      const unsigned long long k = argmax_key(x, i);
+      best = k > best ? k : best;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = red[w] > best ? red[w] : best;
+    if (best) atomicMax(key, best);
+  }
+}
+
+__global__ void k_argmax_finish(const float *v, unsigned long long *key, int *out, int *also) {
+  griddep_trigger();
+  griddep_wait();
+  const float v0 = v[0];
+  const unsigned long long k = *key;
+  const int idx = (v0 != v0 || k == 0) ? 0 : static_cast<int>(~static_cast<uint32_t>(k & 0xffffffffu));
+  *out = idx;
+  if (also) *also = idx;
+  *key = 0;
+}
+
+cudaError_t launch_argmax_multi(const float *v, int n, unsigned long long *key, int *out, int *also, cudaStream_t st) {
+  const int blocks = n / 2048 + 1 < 296 ? n / 2048 + 1 : 296;
+  launch_k(k_argmax_part, blocks, 256, 0, st, v, n, key);
+  launch_k(k_argmax_finish, 1, 1, 0, st, v, key, out, also);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_argmax(const float *v, int n, int *out, cudaStream_t st) {
-  k_argmax<<<1, 1024, 0, st>>>(v, n, out);
+  launch_k(k_argmax, 1, 1024, 0, st, v, n, out);
   return cudaGetLastError();
 }
 
 // freq_p = Exp(-Log(theta)·2p / hs); (sin, cos) = Sincos(pos·freq_p).
 __global__ void k_rope_table(double theta, int hs, int n, float *cos_, float *sin_) {
+  griddep_trigger();
+  griddep_wait();
   const int half = hs / 2;
   const double log_theta = log_det(theta);
   const long long total = (long long)n * half;
@@ -375,13 +606,15 @@ cudaError_t launch_rope_table(double theta, int hs, int n, float *cos_, float *s
   if (blocks > 148 * 16) blocks = 148 * 16;
   // log(theta) in the reference is math.Log (model.go:434); this is
   // num.Log's method, which agrees with it on the bases configs use.
-  k_rope_table<<<int(blocks), 256, 0, st>>>(theta, hs, n, cos_, sin_);
+  launch_k(k_rope_table, int(blocks), 256, 0, st, theta, hs, n, cos_, sin_);
   return cudaGetLastError();
 }
 
-__global__ void k_add_int(int *p, int inc) { *p += inc; }
+__global__ void k_add_int(int *p, int inc) {
+  griddep_trigger();
+  griddep_wait(); *p += inc; }
 cudaError_t launch_add_int(int *p, int inc, cudaStream_t st) {
-  k_add_int<<<1, 1, 0, st>>>(p, inc);
+  launch_k(k_add_int, 1, 1, 0, st, p, inc);
   return cudaGetLastError();
 }
 

@@ -39,6 +39,8 @@ struct AttnArgs {
   float inv_sqrt;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+// Raises the attention kernels' shared-memory limit; once per device.
+cudaError_t init_layer_attributes();
 
 // The per-token work between the QKV projections and attention in
 // Stage.Forward (model.go:542-568), for a position read from *pos_dev:
@@ -61,6 +63,10 @@ cudaError_t launch_embed(int fmt, const void *table, const float *scales, int di
 
 // argmax (sample.go:45-53): the first index of the strict maximum.
 cudaError_t launch_argmax(const float *v, int n, int *out, cudaStream_t st);
+// The same over many CTAs through a 64-bit key in device memory that must
+// be 0 on entry (it is 0 again on exit); the index goes to *out and, when
+// `also` is not null, to *also.
+cudaError_t launch_argmax_multi(const float *v, int n, unsigned long long *key, int *out, int *also, cudaStream_t st);
 
 // NewRope (model.go:428-441) on the device: cos/sin [n][hs/2] for
 // positions 0..n-1, with num.Log(theta), num.Exp and num.Sincos in float64.

@@ -26,53 +26,110 @@ namespace rk {
 // Activation quantization (quantize8, quant.go:34-53), optionally after
 // rmsNorm (model.go:632-638). One CTA; warp w quantizes blocks w, w+W, ...
 // ---------------------------------------------------------------------------
+// Floats of x staged at a time in shared memory for the norm's Dot32.
+constexpr int kStageFloats = 8192;
+
+// quantize8 of x[n] (after rmsNorm when NORM) by one CTA that owns the
+// whole input: x goes to `stage` (stage_floats floats, a multiple of 32) chunk by
+// chunk, and thread t quantizes block t of the chunk on its own (amax,
+// scale, values and sum over the block's 32 values, read in a rotated order
+// so that the threads of a warp use different banks: amax and the sum are
+// order free). With NORM and n <= stage_floats, x is staged once for both
+// the norm's Dot32 and the quantization.
 template <bool NORM>
-__global__ void __launch_bounds__(1024) k_quantize_act(const float *__restrict__ x, int n,
-                                                       const float *__restrict__ w, float recipN, float eps,
-                                                       float *__restrict__ xn, int8_t *__restrict__ qx,
-                                                       float *__restrict__ xs, int *__restrict__ xsum) {
-  __shared__ float s_inv;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+RK_DEV void quantize_staged(const float *__restrict__ x, int n, const float *__restrict__ w, float recipN, float eps,
+                            int8_t *qx, float *xs, int *xsum, float *s_inv, float *stage, int stage_floats) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  auto load = [&](int c0, int m) {
+    if (aligned)
+      for (int i = threadIdx.x; i < m / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(stage)[i] = reinterpret_cast<const float4 *>(x + c0)[i];
+    else
+      for (int i = threadIdx.x; i < m; i += blockDim.x) stage[i] = x[c0 + i];
+  };
   float inv = 0.0f;
+  const bool single = n <= stage_floats;
   if (NORM) {
+    // Dot32(x, x): lane j sums elements j, j+32, ... in order (matvec.go:32-43).
+    float s = 0.0f;
+    for (int c0 = 0; c0 < n; c0 += stage_floats) {
+      const int m = min(stage_floats, n - c0);
+      __syncthreads();
+      load(c0, m);
+      __syncthreads();
+      if (warp == 0) {
+#pragma unroll 8
+        for (int i = lane; i < m; i += 32) s = __fadd_rn(s, __fmul_rn(stage[i], stage[i]));
+      }
+    }
     if (warp == 0) {
-      // Dot32(x, x): lane j sums elements j, j+32, ... in order (matvec.go:32-43).
-      float s = 0.0f;
-      for (int i = lane; i < n; i += 32) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
-      float dot = combine32(s);
-      if (lane == 0) s_inv = rsqrt32(__fadd_rn(__fmul_rn(dot, recipN), eps));
+      const float dot = combine32(s);
+      if (lane == 0) *s_inv = rsqrt32(__fadd_rn(__fmul_rn(dot, recipN), eps));
     }
     __syncthreads();
-    inv = s_inv;
+    inv = *s_inv;
   }
-  const int nb = n >> 5;
-  for (int b = warp; b < nb; b += nwarps) {
-    const int i = b * 32 + lane;
-    float v = x[i];
-    if (NORM) v = __fmul_rn(w[i], __fmul_rn(inv, v));
-    if (xn) xn[i] = v;
-    // amax starts at +0 and takes Go's max with each |v| (NaN propagates).
-    float amax = warp_gomax(fabsf(v));
-    float d = __fmul_rn(amax, u2f(K_1_127));
-    int q = 0;
-    if (!(d == 0.0f || d != d)) q = quant_q8(__fmul_rn(v, recip32(d)));
-    qx[i] = (int8_t)q;
-    int qs = q;
+  for (int c0 = 0; c0 < n; c0 += stage_floats) {
+    const int m = min(stage_floats, n - c0);
+    if (!(NORM && single)) {
+      __syncthreads();
+      load(c0, m);
+      __syncthreads();
+    }
+    for (int t = threadIdx.x; t < m / 32; t += blockDim.x) {
+      const int b = c0 / 32 + t;
+      const float *src = stage + t * 32;
+      float v[32];
+      float amax = 0.0f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-    if (lane == 0) {
+      for (int j = 0; j < 32; j++) {
+        const int jj = (j + t) & 31;
+        float vv = src[jj];
+        if (NORM) vv = __fmul_rn(w[b * 32 + jj], __fmul_rn(inv, vv));
+        v[j] = vv;
+        amax = gomax(amax, fabsf(vv));
+      }
+      const float d = __fmul_rn(amax, u2f(K_1_127));
+      int8_t *q = qx + b * 32;
+      int sum = 0;
+      if (d == 0.0f || d != d) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) q[(j + t) & 31] = 0;
+      } else {
+        const float id = recip32(d);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int qq = quant_q8(__fmul_rn(v[j], id));
+          q[(j + t) & 31] = (int8_t)qq;
+          sum += qq;
+        }
+      }
       xs[b] = d;
-      if (xsum) xsum[b] = qs;
+      if (xsum) xsum[b] = sum;
     }
   }
 }
 
+constexpr int kQuantStage = 8192;  // floats of shared memory for the standalone quantizer
+
+template <bool NORM>
+__global__ void __launch_bounds__(512) k_quantize_act(const float *__restrict__ x, int n,
+                                                       const float *__restrict__ w, float recipN, float eps,
+                                                       float *__restrict__ xn, int8_t *__restrict__ qx,
+                                                       float *__restrict__ xs, int *__restrict__ xsum) {
+  __shared__ float s_inv;
+  __shared__ __align__(16) float stage[kQuantStage];
+  griddep_trigger();
+  griddep_wait();
+  quantize_staged<NORM>(x, n, w, recipN, eps, qx, xs, xsum, &s_inv, stage, kQuantStage);
+}
+
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st) {
-  int threads = n >= 32 * 32 ? 1024 : ((n / 32) > 0 ? (n / 32) * 32 : 32);
-  if (w) k_quantize_act<true><<<1, threads, 0, st>>>(x, n, w, recipN, eps, xn, qx, xs, xsum);
-  else k_quantize_act<false><<<1, threads, 0, st>>>(x, n, w, recipN, eps, xn, qx, xs, xsum);
-  return cudaGetLastError();
+  int threads = n >= 16 * 32 ? 512 : ((n / 32) > 0 ? (n / 32) * 32 : 32);
+  if (w) return launch_k(k_quantize_act<true>, 1, threads, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
+  return launch_k(k_quantize_act<false>, 1, threads, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
 }
 
 // ---------------------------------------------------------------------------
@@ -127,8 +184,6 @@ RK_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar
 // ---------------------------------------------------------------------------
 // Quantized matvec with a per-warp TMA ring.
 // ---------------------------------------------------------------------------
-constexpr int kWarps = 8;
-constexpr int kSlots = 4;
 constexpr int kSegBytes = 4096;  // weight bytes per segment
 
 template <int FMT>
@@ -149,45 +204,68 @@ __host__ __device__ constexpr int slot_bytes() {
   return kSegBytes + QTraits<FMT>::kSegBlocks * 4 + 32;
 }
 
+// Position in a warp's stream of segments: unit (row, or row pair for
+// EPI_SILU), which of the pair, segment of the row, and the matrix / row
+// it maps to. Advanced by one segment at a time, without divisions.
+struct Cursor {
+  long long u;
+  int sub, sg, part, row;
+};
+
 struct SegInfo {
   const uint8_t *wsrc;
   const uint8_t *ssrc;  // 16-byte aligned start of the scale copy
   uint32_t wbytes, sbytes;
   int soff;             // float index of the segment's first scale in the copy
   int blk0, nblk;
-  int part, row, sub;
-  bool first, last;     // first/last segment of its row
 };
 
+RK_DEV void cursor_init(Cursor &c, const MvArgs &a, int nsub, long long u0) {
+  c.u = u0;
+  c.sub = 0;
+  c.sg = 0;
+  c.part = 0;
+  long long row = u0;
+  if (nsub == 1)
+    while (c.part < a.nparts - 1 && row >= a.part[c.part].rows) {
+      row -= a.part[c.part].rows;
+      c.part++;
+    }
+  c.row = int(row);
+}
+
+RK_DEV void cursor_next(Cursor &c, const MvArgs &a, int nsub, int nseg) {
+  if (++c.sg < nseg) return;
+  c.sg = 0;
+  if (nsub == 2) {
+    if (++c.sub < 2) {
+      c.part = 1;
+      return;
+    }
+    c.sub = 0;
+    c.part = 0;
+    c.u++;
+    c.row++;
+    return;
+  }
+  c.u++;
+  if (++c.row == a.part[c.part].rows) {
+    c.part++;
+    c.row = 0;
+  }
+}
+
 template <int FMT>
-RK_DEV SegInfo seg_info(const MvArgs &a, int nb, int nseg, int nsub, long long u0, long long k) {
+RK_DEV SegInfo seg_info(const MvArgs &a, int nb, const Cursor &c) {
   using T = QTraits<FMT>;
   SegInfo s;
-  const long long per_unit = (long long)nsub * nseg;
-  const long long unit = u0 + k / per_unit;
-  const int rem = int(k % per_unit);
-  s.sub = rem / nseg;
-  const int sg = rem % nseg;
-  int part = 0;
-  long long row = unit;
-  if (nsub == 2) {
-    part = s.sub;
-  } else {
-    while (part < a.nparts - 1 && row >= a.part[part].rows) {
-      row -= a.part[part].rows;
-      part++;
-    }
-  }
-  s.part = part;
-  s.row = int(row);
-  s.blk0 = sg * T::kSegBlocks;
+  s.blk0 = c.sg * T::kSegBlocks;
   s.nblk = min(T::kSegBlocks, nb - s.blk0);
-  s.first = sg == 0;
-  s.last = sg == nseg - 1;
-  const MvPart &p = a.part[part];
-  s.wsrc = p.w + (row * nb + s.blk0) * (long long)T::kBlkBytes;
+  const MvPart &p = a.part[c.part];
+  const long long b0 = (long long)c.row * nb + s.blk0;
+  s.wsrc = p.w + b0 * T::kBlkBytes;
   s.wbytes = uint32_t(s.nblk * T::kBlkBytes);
-  const uintptr_t sa = reinterpret_cast<uintptr_t>(p.s + row * nb + s.blk0);
+  const uintptr_t sa = reinterpret_cast<uintptr_t>(p.s + b0);
   const uintptr_t s0 = sa & ~uintptr_t(15);
   const uintptr_t s1 = (sa + uintptr_t(s.nblk) * 4 + 15) & ~uintptr_t(15);
   s.ssrc = reinterpret_cast<const uint8_t *>(s0);
@@ -231,8 +309,17 @@ RK_DEV int block_sum(const uint8_t *wblk, const int8_t *xblk, int xsum) {
   }
 }
 
+// term = float32(sum_b)·float32(ws_b·xs_b) for block bb of the segment.
 template <int FMT>
-__global__ void __launch_bounds__(kWarps * 32, 1) k_matvec_q(const MvArgs a, int qx_in_smem) {
+RK_DEV float block_term(const uint8_t *W, const float *S, int bb, int gb, const int8_t *sqx, const float *sxs,
+                        const int *sxsum) {
+  using T = QTraits<FMT>;
+  const int sum = block_sum<FMT>(W + bb * T::kBlkBytes, sqx + gb * 32, FMT == FMT_Q4_0 ? sxsum[gb] : 0);
+  return __fmul_rn(__int2float_rn(sum), __fmul_rn(S[bb], sxs[gb]));
+}
+
+template <int FMT, int WARPS, int SLOTS>
+__global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int qx_in_smem) {
   using T = QTraits<FMT>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -245,9 +332,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_matvec_q(const MvArgs a, int
     for (int p = 0; p < a.nparts; p++) units += a.part[p].rows;
 
   // Shared memory: mbarriers, the input (qx, xs, xsum) when it fits, then
-  // one ring of kSlots slots per warp.
+  // one ring of SLOTS slots per warp.
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-  uint8_t *p = smem + kWarps * kSlots * 8;
+  uint8_t *p = smem + WARPS * SLOTS * 8;
   const int8_t *sqx = a.qx;
   const float *sxs = a.xs;
   const int *sxsum = a.xsum;
@@ -262,39 +349,60 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_matvec_q(const MvArgs a, int
     sxs = xs;
     sxsum = xsum;
   }
-  uint8_t *ring = p + warp * kSlots * slot_bytes<FMT>();
+  // The norm's staging area (kStageFloats floats) sits just below the rings.
+  uint8_t *ring_base = p + (a.pro != PRO_GIVEN ? kStageFloats * 4 : 0);
+  uint8_t *ring = ring_base + warp * SLOTS * slot_bytes<FMT>();
 
-  const int gw = blockIdx.x * kWarps + warp, G = gridDim.x * kWarps;
+  const int gw = blockIdx.x * WARPS + warp, G = gridDim.x * WARPS;
   const long long u0 = units * gw / G, u1 = units * (gw + 1) / G;
   const long long total = (u1 - u0) * nsub * nseg;
-  const uint32_t bar0 = smem_addr(bars + warp * kSlots);
+  const uint32_t bar0 = smem_addr(bars + warp * SLOTS);
 
   uint64_t pol = 0;
+  Cursor pc;  // the producer's cursor (lane 0), SLOTS segments ahead
+  long long issued = 0;
+  int pslot = 0;
   if (lane == 0) {
-    for (int s = 0; s < kSlots; s++) mbar_init(bar0 + 8 * s, 1);
+    for (int s = 0; s < SLOTS; s++) mbar_init(bar0 + 8 * s, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     pol = evict_first_policy();
+    cursor_init(pc, a, nsub, u0);
   }
   __syncwarp();
 
-  auto issue = [&](long long k) {
-    if (k >= total) return;
-    const SegInfo s = seg_info<FMT>(a, nb, nseg, nsub, u0, k);
-    const int slot = int(k % kSlots);
-    uint8_t *dst = ring + slot * slot_bytes<FMT>();
-    const uint32_t bar = bar0 + 8 * slot;
+  auto issue = [&]() {
+    if (issued >= total) return;
+    const SegInfo s = seg_info<FMT>(a, nb, pc);
+    uint8_t *dst = ring + pslot * slot_bytes<FMT>();
+    const uint32_t bar = bar0 + 8 * pslot;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_expect_tx(bar, s.wbytes + s.sbytes);
     bulk_g2s(smem_addr(dst), s.wsrc, s.wbytes, bar, pol);
     bulk_g2s(smem_addr(dst + kSegBytes), s.ssrc, s.sbytes, bar, pol);
+    cursor_next(pc, a, nsub, nseg);
+    issued++;
+    pslot = pslot + 1 == SLOTS ? 0 : pslot + 1;
   };
 
-  // Start the weight stream before staging the input: the copies run while
-  // the CTA loads qx/xs.
+  // Start the weight stream (read-only: it may run before the predecessor
+  // kernel has finished), then wait for the predecessor and stage the
+  // input: the copies run meanwhile.
+  griddep_trigger();
   if (lane == 0)
-    for (int k = 0; k < kSlots; k++) issue(k);
+    for (int k = 0; k < SLOTS; k++) issue();
+  griddep_wait();
 
-  if (qx_in_smem) {
+  if (a.pro != PRO_GIVEN) {
+    __shared__ float s_inv;
+    int8_t *q = const_cast<int8_t *>(sqx);
+    float *stage = reinterpret_cast<float *>(p);
+    if (a.pro == PRO_NORM_QUANT)
+      quantize_staged<true>(a.x, cols, a.norm_w, a.recipN, a.eps, q, const_cast<float *>(sxs),
+                            const_cast<int *>(sxsum), &s_inv, stage, kStageFloats);
+    else
+      quantize_staged<false>(a.x, cols, nullptr, 0.0f, 0.0f, q, const_cast<float *>(sxs), const_cast<int *>(sxsum),
+                             &s_inv, stage, kStageFloats);
+  } else if (qx_in_smem) {
     int8_t *q = const_cast<int8_t *>(sqx);
     for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
       reinterpret_cast<int4 *>(q)[i] = reinterpret_cast<const int4 *>(a.qx)[i];
@@ -305,53 +413,70 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_matvec_q(const MvArgs a, int
   }
   __syncthreads();
 
+  Cursor cc;  // the consumer's cursor
+  cursor_init(cc, a, nsub, u0);
+  int slot = 0;
+  uint32_t parity = 0;
   float acc = 0.0f, r0 = 0.0f;
   for (long long k = 0; k < total; k++) {
-    const int slot = int(k % kSlots);
-    const uint32_t parity = uint32_t((k / kSlots) & 1);
     if (!mbar_wait_bounded(bar0 + 8 * slot, parity)) {
       if (lane == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
       // Give the copies already issued a bounded chance to land, then stop.
-      for (long long j = k + 1; j < min(total, k + kSlots); j++)
-        mbar_wait_bounded(bar0 + 8 * int(j % kSlots), uint32_t((j / kSlots) & 1));
+      int js = slot;
+      uint32_t jp = parity;
+      for (long long j = k + 1; j < min(total, k + SLOTS); j++) {
+        js = js + 1 == SLOTS ? 0 : js + 1;
+        if (js == 0) jp ^= 1;
+        mbar_wait_bounded(bar0 + 8 * js, jp);
+      }
       return;
     }
-    const SegInfo s = seg_info<FMT>(a, nb, nseg, nsub, u0, k);
+    const SegInfo s = seg_info<FMT>(a, nb, cc);
     const uint8_t *W = ring + slot * slot_bytes<FMT>();
     const float *S = reinterpret_cast<const float *>(W + kSegBytes) + s.soff;
-    if (s.first) acc = 0.0f;
-    for (int c = 0; c * 32 < s.nblk; c++) {
+    if (cc.sg == 0) acc = 0.0f;
+    // Full 32-block chunks: lane t takes block t; lanes 0..7 then add the
+    // terms of blocks t, t+8, t+16, t+24 in order (lanes 8..31 compute
+    // values nobody reads).
+    const int nfull = s.nblk >> 5;
+#pragma unroll 2
+    for (int c = 0; c < nfull; c++) {
       const int bb = c * 32 + lane;
+      const float term = block_term<FMT>(W, S, bb, s.blk0 + bb, sqx, sxs, sxsum);
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * j));
+    }
+    if (s.nblk & 31) {
+      // A partial chunk: blocks past the row are skipped, not added as zeros.
+      const int bb = nfull * 32 + lane;
       float term = 0.0f;
-      if (bb < s.nblk) {
-        const int gb = s.blk0 + bb;
-        const int sum = block_sum<FMT>(W + bb * T::kBlkBytes, sqx + gb * 32, FMT == FMT_Q4_0 ? sxsum[gb] : 0);
-        const float d = __fmul_rn(S[bb], sxs[gb]);
-        term = __fmul_rn(__int2float_rn(sum), d);
-      }
+      if (bb < s.nblk) term = block_term<FMT>(W, S, bb, s.blk0 + bb, sqx, sxs, sxsum);
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const float t = __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * j);
-        if (lane < 8 && c * 32 + lane + 8 * j < s.nblk) acc = __fadd_rn(acc, t);
+        if (nfull * 32 + (lane & 7) + 8 * j < s.nblk) acc = __fadd_rn(acc, t);
       }
     }
-    if (s.last) {
+    if (cc.sg == nseg - 1) {
       const float r = combine8(acc);
       if (lane == 0) {
-        float *out = a.part[s.part].out;
+        float *out = a.part[cc.part].out;
         switch (a.epi) {
-          case EPI_STORE: out[s.row] = r; break;
-          case EPI_ADD: out[s.row] = __fadd_rn(out[s.row], r); break;
-          case EPI_ADD_CANON: out[s.row] = canonical(__fadd_rn(out[s.row], r)); break;
+          case EPI_STORE: out[cc.row] = r; break;
+          case EPI_ADD: out[cc.row] = __fadd_rn(out[cc.row], r); break;
+          case EPI_ADD_CANON: out[cc.row] = canonical(__fadd_rn(out[cc.row], r)); break;
           case EPI_SILU:
-            if (s.sub == 0) r0 = r;
-            else a.part[0].out[s.row] = __fmul_rn(silu(r0), r);
+            if (cc.sub == 0) r0 = r;
+            else a.part[0].out[cc.row] = __fmul_rn(silu(r0), r);
             break;
         }
       }
     }
     __syncwarp();
-    if (lane == 0) issue(k + kSlots);
+    if (lane == 0) issue();
+    cursor_next(cc, a, nsub, nseg);
+    slot = slot + 1 == SLOTS ? 0 : slot + 1;
+    if (slot == 0) parity ^= 1;
   }
 }
 
@@ -362,6 +487,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_matvec_q(const MvArgs a, int
 // ---------------------------------------------------------------------------
 template <int FMT>
 __global__ void __launch_bounds__(256) k_matvec_f(const MvArgs a) {
+  griddep_trigger();
+  griddep_wait();
   const int lane = threadIdx.x & 31;
   const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const long long G = (long long)gridDim.x * (blockDim.x >> 5);
@@ -412,33 +539,53 @@ static int input_smem_bytes(int cols) {
   return ((cols + 15) & ~15) + 2 * ((nb * 4 + 15) & ~15);
 }
 
-// Columns up to which the quantized input is staged in shared memory.
-constexpr int kSmemColsMax = 32768;
+// Ring geometry: 16 warps per CTA, 2 slots of 4 KiB per warp (64 KiB of
+// weights in flight per SM), one CTA per SM. Measured on B200 against 8×4
+// and 12×3 rings and against direct 128-bit loads: best on every shape.
+constexpr int kWarps = 16, kSlots = 2;
+
+template <int FMT>
+static int smem_for(int cols, bool fused) {
+  return kWarps * kSlots * 8 + (cols <= kSmemColsMax ? input_smem_bytes(cols) : 0) + (fused ? kStageFloats * 4 : 0) +
+         kWarps * kSlots * slot_bytes<FMT>();
+}
 
 int matvec_smem_bytes(int fmt, int cols) {
-  const int ring = kWarps * kSlots * (fmt == FMT_Q8_0 ? slot_bytes<FMT_Q8_0>() : slot_bytes<FMT_Q4_0>());
-  return kWarps * kSlots * 8 + (cols <= kSmemColsMax ? input_smem_bytes(cols) : 0) + ring;
+  return fmt == FMT_Q8_0 ? smem_for<FMT_Q8_0>(cols, false) : smem_for<FMT_Q4_0>(cols, false);
+}
+
+// Dynamic shared memory a matvec CTA may use: the B200 opt-in limit per CTA
+// (227 KiB) less 1 KiB for the kernel's static shared memory.
+constexpr int kSmemLimit = 232448 - 1024;
+
+bool matvec_fused_ok(int fmt, int cols) {
+  if (cols > kSmemColsMax) return false;
+  if (fmt == FMT_Q8_0) return smem_for<FMT_Q8_0>(cols, true) <= kSmemLimit;
+  if (fmt == FMT_Q4_0) return smem_for<FMT_Q4_0>(cols, true) <= kSmemLimit;
+  return false;
 }
 
 cudaError_t init_matvec_attributes() {
-  const int maxq8 = matvec_smem_bytes(FMT_Q8_0, kSmemColsMax), maxq4 = matvec_smem_bytes(FMT_Q4_0, kSmemColsMax);
-  cudaError_t e = cudaFuncSetAttribute(k_matvec_q<FMT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxq8);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_matvec_q<FMT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxq4);
+  cudaError_t e = cudaFuncSetAttribute(k_matvec_q<FMT_Q8_0, kWarps, kSlots>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemLimit);
   return e;
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
-  if (a.fmt == FMT_Q8_0 || a.fmt == FMT_Q4_0) {
-    const int smem = matvec_smem_bytes(a.fmt, a.cols);
-    const int in_smem = a.cols <= kSmemColsMax ? 1 : 0;
-    if (a.fmt == FMT_Q8_0) k_matvec_q<FMT_Q8_0><<<num_sms, kWarps * 32, smem, st>>>(a, in_smem);
-    else k_matvec_q<FMT_Q4_0><<<num_sms, kWarps * 32, smem, st>>>(a, in_smem);
-  } else if (a.fmt == FMT_F32) {
-    k_matvec_f<FMT_F32><<<num_sms * 4, 256, 0, st>>>(a);
-  } else {
-    k_matvec_f<FMT_BF16><<<num_sms * 4, 256, 0, st>>>(a);
-  }
-  return cudaGetLastError();
+  const bool quant = a.fmt == FMT_Q8_0 || a.fmt == FMT_Q4_0;
+  if (quant && a.pro != PRO_GIVEN && !matvec_fused_ok(a.fmt, a.cols)) return cudaErrorInvalidValue;
+  const bool fused = a.pro != PRO_GIVEN;
+  if (a.fmt == FMT_Q8_0)
+    return launch_k(k_matvec_q<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q8_0>(a.cols, fused), st, a,
+                    a.cols <= kSmemColsMax ? 1 : 0);
+  if (a.fmt == FMT_Q4_0)
+    return launch_k(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q4_0>(a.cols, fused), st, a,
+                    a.cols <= kSmemColsMax ? 1 : 0);
+  if (a.fmt == FMT_F32) return launch_k(k_matvec_f<FMT_F32>, num_sms * 4, 256, 0, st, a);
+  return launch_k(k_matvec_f<FMT_BF16>, num_sms * 4, 256, 0, st, a);
 }
 
 }  // namespace rk

@@ -42,7 +42,18 @@ struct MvArgs {
   const int *xsum;
   const float *x;
   int *err;
+  // PRO_QUANT / PRO_NORM_QUANT: each CTA quantizes x (after rmsNorm with
+  // norm_w, recipN, eps) into its shared memory itself, and qx/xs/xsum are
+  // not used (quantized formats, cols <= 32768).
+  int pro;
+  const float *norm_w;
+  float recipN, eps;
 };
+
+enum Prologue : int { PRO_GIVEN = 0, PRO_QUANT = 1, PRO_NORM_QUANT = 2 };
+
+// Widest input whose Q8_0 form a matvec CTA stages in shared memory.
+constexpr int kSmemColsMax = 32768;
 
 // Quantizes n floats (a whole number of 32-blocks) to Q8_0 as quantize8
 // does (quant.go:34-53), after RMS normalisation when w != nullptr
@@ -55,6 +66,11 @@ cudaError_t launch_quantize_act(const float *x, int n, const float *w, float rec
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
 
 int matvec_smem_bytes(int fmt, int cols);
+
+// Whether a matvec of this format and width can quantize its input in its
+// own prologue (PRO_QUANT / PRO_NORM_QUANT): the input and its staging must
+// fit shared memory beside the weight rings.
+bool matvec_fused_ok(int fmt, int cols);
 
 // Raises the kernels' dynamic shared-memory limit; once per device, before
 // any launch or graph capture.

@@ -29,7 +29,7 @@ EXPORTS = [
     "rk_batch_read", "rk_batch_matvecs", "rk_batch_quantize", "rk_batch_rmsnorm", "rk_batch_addvec", "rk_batch_rope",
     "rk_batch_copy", "rk_batch_attention", "rk_batch_residual", "rk_batch_silumul", "rk_batch_submit",
     "rk_config_validate", "rk_layer_upload", "rk_layer_from_device", "rk_layer_free", "rk_stage_new", "rk_stage_free",
-    "rk_stage_positions", "rk_stage_forward", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed",
+    "rk_stage_positions", "rk_stage_forward", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
     "rk_model_new", "rk_model_free", "rk_model_step", "rk_model_generate", "rk_tensor_matmul",
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
     "rk_bench_matvec", "rk_bench_model", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
@@ -107,6 +107,7 @@ def lib():
             "rk_stage_free": (None, [vp]), "rk_stage_positions": (i, [vp]), "rk_stage_forward": (i, [vp, vp, i, i]),
             "rk_head_new": (i, [vp, vp, vp, vp, vp]), "rk_head_free": (None, [vp]),
             "rk_head_logits": (i, [vp, vp, vp]), "rk_embed": (i, [vp, i, vp]),
+            "rk_sample_argmax": (i, [vp, vp, i, vp]),
             "rk_model_new": (i, [vp, vp, vp, vp, vp]), "rk_model_free": (None, [vp]),
             "rk_model_step": (i, [vp, i, i, vp, vp]), "rk_model_generate": (i, [vp, vp, i, i, vp, vp]),
             "rk_tensor_matmul": (i, [vp, i, i, i, i, i, vp, vp, vp]),
@@ -381,6 +382,14 @@ class Head:
         if self.h:
             lib().rk_head_free(self.h)
             self.h = C.c_void_p()
+
+
+def sample_argmax(dev, logits):
+    """Sampler.Sample at temperature 0 (sample.go:26-53), on the device."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    idx = C.c_int()
+    _check(lib().rk_sample_argmax(dev.h, _ptr(logits), logits.size, C.byref(idx)))
+    return idx.value
 
 
 def embed(table, token):
