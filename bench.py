@@ -50,9 +50,12 @@ def parse():
     p.add_argument("--dtype", default="q8_0")
     p.add_argument("--ctx", type=int, default=CTX)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", default=None, choices=["matvec"],
+    p.add_argument("--kernel", default=None, choices=["matvec", "tensor"],
                    help="time one kernel alone instead of the decode step (profiling aid)")
     p.add_argument("--shape", default="28672x4096", help="rows x cols for --kernel matvec")
+    p.add_argument("--prologue", default="fused", choices=["fused", "given"],
+                   help="--kernel matvec: quantize the input inside the kernel (as the decode step does) "
+                        "or read a quantized copy")
     return p.parse_args()
 
 
@@ -63,15 +66,41 @@ def run_kernel(args):
     fmt = {"q8_0": rk.FMT_Q8_0, "q4_0": rk.FMT_Q4_0}[args.dtype]
     dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
     m = rk.Matrix.generate(dev, rows, cols, fmt, SEED, 1, 0.02)
-    m.bench(max(1, args.warmup), flush=True)
-    ms = m.bench(args.steps, flush=True)
+    fused = args.prologue == "fused"
+    m.bench(max(1, args.warmup), flush=True, fused=fused)
+    ms = m.bench(args.steps, flush=True, fused=fused)
     n = rows * cols
     nbytes = n + n // 32 * 4 if fmt == rk.FMT_Q8_0 else n // 2 + n // 32 * 4
     peak, kind = measured_peak()
-    print(json.dumps({"kernel": f"k_matvec_q<{args.dtype}>", "shape": args.shape, "ms": ms,
+    print(json.dumps({"kernel": f"k_matvec_q<{args.dtype}>", "shape": args.shape, "prologue": args.prologue, "ms": ms,
                       "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
                       "frac": nbytes / (ms * 1e-3) / 1e9 / peak}), flush=True)
     m.free()
+    dev.close()
+
+
+def run_tensor(args):
+    """rakkan_tensor_v1 matmul_t of config 2 (M in {1, 16, 128, 512}, N = K =
+    4096), int8 and f32, device-resident inputs, L2 flushed before each."""
+    import rkcuda as rk
+    dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    for dtype, name in ((rk.TENSOR_I8, "i8"), (rk.TENSOR_F32, "f32")):
+        for transposed in (True, False):
+            for m in (1, 16, 128, 512):
+                n = k = 4096
+                rk.bench_tensor(dev, dtype, transposed, m, k, n, max(1, args.warmup))
+                ms = rk.bench_tensor(dev, dtype, transposed, m, k, n, args.steps)
+                es = 1 if dtype == rk.TENSOR_I8 else 4
+                nbytes = es * (m * k + k * n) + 4 * m * n
+                print(json.dumps({"kernel": f"tensor_{name}", "op": "matmul_t" if transposed else "matmul",
+                                  "m": m, "k": k, "n": n, "ms": ms, "tops": 2 * m * n * k / (ms * 1e-3) / 1e12,
+                                  "gbs": nbytes / (ms * 1e-3) / 1e9, "hbm_peak_gbs": peaks.get("hbm_gbs")}),
+                      flush=True)
     dev.close()
 
 
@@ -203,6 +232,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.kernel == "tensor":
+        return run_tensor(args)
     if args.kernel:
         return run_kernel(args)
 

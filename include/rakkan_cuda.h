@@ -255,9 +255,20 @@ int rk_generate_normal(rk_device *d, uint64_t seed, uint64_t tid, int64_t offset
 int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, void *q, float *scales);
 
 /* ---- Measurement helpers (device buffers, device stream, CUDA events) ---- */
-/* Times `iters` launches of the matvec of m on device-resident input (L2
- * flushed before each when flush != 0); returns the mean kernel time. */
-int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per_launch);
+/* Times `iters` launches of the matvec of m on device-resident input and
+ * returns the mean kernel time. Flags: RK_BENCH_FLUSH flushes L2 before each
+ * launch; RK_BENCH_FUSED has the kernel quantize its float input itself, as
+ * the decode step's matvecs do (quantized formats), instead of reading a
+ * quantized copy made beforehand. */
+#define RK_BENCH_FLUSH 1
+#define RK_BENCH_FUSED 2
+int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per_launch);
+/* Times `iters` tensor matmuls (rk_tensor_matmul_device) of the given dtype,
+ * layout and shape on device buffers this call allocates and fills with
+ * hashed values (int8 in [-127, 127], floats in [-1, 1)); returns the mean
+ * time per product. Flags: RK_BENCH_FLUSH flushes L2 before each product. */
+int rk_bench_tensor(rk_device *d, int dtype, int transposed, int m, int k, int n, int iters, int flags,
+                    float *ms_per_product);
 /* Times `iters` graph replays of one decode step at position pos (the
  * position is re-set before each, so every step attends over pos+1
  * positions); *ms_per_step is the mean, by CUDA events on the device's stream. */

@@ -181,6 +181,7 @@ extern "C" int rk_device_open(int index, rk_device **out) {
   if (cudaSetDevice(index) != cudaSuccess) return cleanup(fail(RK_ERR_CUDA, "cudaSetDevice(%d)", index));
   cudaError_t e = init_matvec_attributes();
   if (e == cudaSuccess) e = init_layer_attributes();
+  if (e == cudaSuccess) e = init_tensor_attributes();
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&d->err_dev, 2 * sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, 2 * sizeof(int));
@@ -1635,7 +1636,7 @@ extern "C" int rk_tensor_matmul_device(rk_device *d, int dtype, int transposed, 
   int rc = tensor_check(dtype, m, k, n);
   if (rc) return rc;
   if ((rc = set_device(d))) return rc;
-  CK(launch_tensor_matmul(dtype, transposed, m, k, n, a_dev, b_dev, c_dev, d->sms, d->st));
+  CK(launch_tensor_matmul(dtype, transposed, m, k, n, a_dev, b_dev, c_dev, d->sms, d->err_dev, d->st));
   return RK_OK;
 }
 
@@ -1654,14 +1655,14 @@ extern "C" int rk_tensor_matmul(rk_device *d, int dtype, int transposed, int m, 
   if (e == cudaSuccess) e = cudaMalloc(&dc, cb);
   if (e == cudaSuccess) e = cudaMemcpyAsync(da, a, ab, cudaMemcpyHostToDevice, d->st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, bb, cudaMemcpyHostToDevice, d->st);
-  if (e == cudaSuccess) e = launch_tensor_matmul(dtype, transposed, m, k, n, da, db, dc, d->sms, d->st);
+  if (e == cudaSuccess) e = launch_tensor_matmul(dtype, transposed, m, k, n, da, db, dc, d->sms, d->err_dev, d->st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(c, dc, cb, cudaMemcpyDeviceToHost, d->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
   cudaFree(da);
   cudaFree(db);
   cudaFree(dc);
   if (e != cudaSuccess) return cuda_fail(e, "tensor matmul");
-  return RK_OK;
+  return check_dev_err(d);
 }
 
 // ---------------------------------------------------------------------------
@@ -1775,9 +1776,12 @@ static int ensure_flush(rk_device *d) {
   return RK_OK;
 }
 
-extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per_launch) {
+extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per_launch) {
   if (!m || iters <= 0 || !ms_per_launch) return fail(RK_ERR_ARGS, "bad argument");
   rk_device *d = m->d;
+  const int flush = flags & RK_BENCH_FLUSH;
+  Pro pro;
+  if ((flags & RK_BENCH_FUSED) && quantized_fmt(m->fmt) && matvec_fused_ok(m->fmt, m->cols)) pro.pro = PRO_QUANT;
   Guard g(d);
   int rc = set_device(d);
   if (rc) return rc;
@@ -1793,7 +1797,8 @@ extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per
   for (int i = 0; i < iters + 1; i++) {
     if (flush) k_flush_read<<<d->sms * 4, 512, 0, d->st>>>((const int4 *)d->flush, (long long)(d->flush_bytes / 16), d->err_dev + 1);
     CK(cudaEventRecord(e0, d->st));
-    if ((rc = enqueue_matvecs(d, 1, &m, &out, d->mv_x, d->mv_qx, d->mv_xs, d->mv_xsum, EPI_STORE))) return rc;
+    if ((rc = enqueue_matvecs(d, 1, &m, &out, d->mv_x, d->mv_qx, d->mv_xs, d->mv_xsum, EPI_STORE, d->st, pro)))
+      return rc;
     CK(cudaEventRecord(e1, d->st));
     CK(cudaEventSynchronize(e1));
     float ms = 0.0f;
@@ -1804,6 +1809,49 @@ extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flush, float *ms_per
   cudaEventDestroy(e1);
   if ((rc = check_dev_err(d))) return rc;
   *ms_per_launch = total / iters;
+  return RK_OK;
+}
+
+extern "C" int rk_bench_tensor(rk_device *d, int dtype, int transposed, int m, int k, int n, int iters, int flags,
+                               float *ms_per_product) {
+  if (!d || iters <= 0 || !ms_per_product) return fail(RK_ERR_ARGS, "bad argument");
+  int rc = tensor_check(dtype, m, k, n);
+  if (rc) return rc;
+  Guard g(d);
+  if ((rc = set_device(d))) return rc;
+  const int flush = flags & RK_BENCH_FLUSH;
+  if (flush && (rc = ensure_flush(d))) return rc;
+  const size_t es = dtype == RK_TENSOR_F32 ? 4 : 1;
+  void *da = nullptr, *db = nullptr, *dc = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float total = 0.0f;
+  cudaError_t e = cudaMalloc(&da, es * (size_t)m * k);
+  if (e == cudaSuccess) e = cudaMalloc(&db, es * (size_t)k * n);
+  if (e == cudaSuccess) e = cudaMalloc(&dc, 4 * (size_t)m * n);
+  if (e == cudaSuccess) e = launch_fill_hash(dtype, da, (long long)m * k, 1u, d->st);
+  if (e == cudaSuccess) e = launch_fill_hash(dtype, db, (long long)k * n, 2u, d->st);
+  if (e == cudaSuccess) e = cudaEventCreate(&e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&e1);
+  for (int i = 0; i < iters + 1 && e == cudaSuccess; i++) {
+    if (flush)
+      k_flush_read<<<d->sms * 4, 512, 0, d->st>>>((const int4 *)d->flush, (long long)(d->flush_bytes / 16),
+                                                  d->err_dev + 1);
+    e = cudaEventRecord(e0, d->st);
+    if (e == cudaSuccess) e = launch_tensor_matmul(dtype, transposed, m, k, n, da, db, dc, d->sms, d->err_dev, d->st);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, d->st);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (i > 0) total += ms;  // the first product is a warm-up
+  }
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaFree(da);
+  cudaFree(db);
+  cudaFree(dc);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor bench");
+  if ((rc = check_dev_err(d))) return rc;
+  *ms_per_product = total / iters;
   return RK_OK;
 }
 

@@ -12,7 +12,20 @@ enum TensorDType : int { DT_F32 = 0, DT_I8 = 1, DT_I32 = 2 };
 // (transposed = 1), all row-major on the device. f32: every output is a
 // serial chain over p = 0..k-1 of float32(a·b) from +0, then Canonical.
 // i8: exact int32 sums (two's complement wrap, as Go's int32).
+// int8 products run on the tensor cores when tensor_i8_tc_ok() holds;
+// `err` is the device error word a timed-out pipeline wait writes.
 cudaError_t launch_tensor_matmul(int dtype, int transposed, int m, int k, int n, const void *a, const void *b, void *c,
-                                 int num_sms, cudaStream_t st);
+                                 int num_sms, int *err, cudaStream_t st);
+
+// Whether an int8 product of this shape and these operand addresses can use
+// the tensor-core kernel (16-byte aligned operands and rows, k < 2^17).
+bool tensor_i8_tc_ok(int transposed, int m, int k, int n, const void *a, const void *b);
+
+// Fills n elements of an int8 (dtype DT_I8) or float matrix with hashed
+// values of (seed, index): int8 in [-127, 127], floats in [-1, 1).
+cudaError_t launch_fill_hash(int dtype, void *p, long long n, uint32_t seed, cudaStream_t st);
+
+// Raises the tensor-core kernels' shared-memory limit; once per device.
+cudaError_t init_tensor_attributes();
 
 }  // namespace rk

@@ -17,6 +17,7 @@ RK_ERR_CUDA, RK_ERR_NOMEM, RK_ERR_TIMEOUT, RK_ERR_STATE = -10, -11, -12, -13
 FMT_F32, FMT_BF16, FMT_Q8_0, FMT_Q4_0 = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16, DTYPE_Q8_0, DTYPE_Q4_0, DTYPE_Q4_M = 0, 1, 2, 3, 4
 TENSOR_F32, TENSOR_I8, TENSOR_I32 = 0, 1, 2
+RK_BENCH_FLUSH, RK_BENCH_FUSED = 1, 2
 MAX_COLS, MAX_ROWS = 1 << 18, 1 << 20
 NOALLOC_MAX_COLS = 32768
 
@@ -32,7 +33,7 @@ EXPORTS = [
     "rk_stage_positions", "rk_stage_forward", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
     "rk_model_new", "rk_model_free", "rk_model_step", "rk_model_generate", "rk_tensor_matmul",
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
-    "rk_bench_matvec", "rk_bench_model", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
+    "rk_bench_matvec", "rk_bench_tensor", "rk_bench_model", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
 ]
 
 
@@ -115,6 +116,7 @@ def lib():
             "rk_matrix_generate": (i, [vp, i, i, i, u64, u64, f, vp]), "rk_matrix_download": (i, [vp, vp, vp]),
             "rk_generate_normal": (i, [vp, u64, u64, i64, i64, f, vp]), "rk_quantize": (i, [vp, i, vp, i64, vp, vp]),
             "rk_bench_matvec": (i, [vp, i, i, vp]), "rk_bench_model": (i, [vp, i, i, vp]),
+            "rk_bench_tensor": (i, [vp, i, i, i, i, i, i, i, vp]),
             "rk_model_kernel_count": (i, [vp, vp]), "rk_model_profile": (i, [vp, i, i, vp]),
             "rk_stage_fill_cache": (i, [vp, i, u64]),
         }
@@ -211,9 +213,12 @@ class Matrix:
         _check(lib().rk_matrix_mulvec(self.h, _ptr(out), _ptr(x)))
         return out
 
-    def bench(self, iters=20, flush=True):
+    def bench(self, iters=20, flush=True, fused=False):
+        """Mean kernel time (ms) of one matvec; `fused` quantizes the input
+        inside the kernel as the decode step does."""
         ms = C.c_float()
-        _check(lib().rk_bench_matvec(self.h, iters, 1 if flush else 0, C.byref(ms)))
+        flags = (RK_BENCH_FLUSH if flush else 0) | (RK_BENCH_FUSED if fused else 0)
+        _check(lib().rk_bench_matvec(self.h, iters, flags, C.byref(ms)))
         return ms.value
 
     def free(self):
@@ -461,6 +466,14 @@ def tensor_matmul(dev, a, b, transposed):
     c = np.empty((m, n), dtype=out_t)
     _check(lib().rk_tensor_matmul(dev.h, dt, 1 if transposed else 0, m, k, n, _ptr(a), _ptr(b), _ptr(c)))
     return c
+
+
+def bench_tensor(dev, dtype, transposed, m, k, n, iters=20, flush=True):
+    """Mean device time (ms) of one tensor matmul on device-resident inputs."""
+    ms = C.c_float()
+    _check(lib().rk_bench_tensor(dev.h, dtype, 1 if transposed else 0, m, k, n, iters,
+                                 RK_BENCH_FLUSH if flush else 0, C.byref(ms)))
+    return ms.value
 
 
 def generate_normal(dev, seed, tid, offset, n, scale):

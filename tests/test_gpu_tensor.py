@@ -47,6 +47,32 @@ def test_f32_and_i8_match_oracle(dev, shape, transposed):
     assert (rk.tensor_matmul(dev, ai, bi, transposed) == ro.tensor_matmul(ai, bi, transposed)).all()
 
 
+# int8 shapes for the tensor-core kernel (16-byte aligned rows): every A-row
+# tile width (16/32/64/128/256), partial tiles on both sides, K not a
+# multiple of the 128-byte stage, and split-K accumulation.
+TC_SHAPES = [(1, 64, 128), (3, 64, 16), (17, 208, 130), (40, 1024, 300), (100, 96, 144), (129, 512, 1000),
+             (300, 160, 272), (513, 384, 384), (16, 8192, 256)]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("transposed", [False, True], ids=["matmul", "matmul_t"])
+def test_i8_tensor_core_shapes(dev, shape, transposed):
+    m, k, n = shape
+    rng = np.random.default_rng(m * 131 + k * 17 + n)
+    ai = rng.integers(-128, 128, (m, k), dtype=np.int64).astype(np.int8)
+    bi = rng.integers(-128, 128, (n, k) if transposed else (k, n), dtype=np.int64).astype(np.int8)
+    assert (rk.tensor_matmul(dev, ai, bi, transposed) == ro.tensor_matmul(ai, bi, transposed)).all()
+
+
+def test_i8_extremes(dev):
+    """-128·-128 summed over K = 4096 (2^26) and mixed signs: exact int32."""
+    a = np.full((5, 4096), -128, np.int8)
+    b = np.full((4096, 48), -128, np.int8)
+    b[:, 1::2] = 127
+    got = rk.tensor_matmul(dev, a, b, False)
+    assert (got == a.astype(np.int64) @ b.astype(np.int64)).all()
+
+
 def test_transposed_agrees(dev):
     rng = np.random.default_rng(1)
     a = rng.standard_normal((7, 33)).astype(np.float32)
