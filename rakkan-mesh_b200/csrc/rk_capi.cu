@@ -779,6 +779,7 @@ extern "C" void rk_batch_attention(rk_batch *b, int64_t q_off, int64_t keys_off,
     at.kv_dim = kv_dim;
     at.att_stride = att_stride;
     at.inv_sqrt = inv_sqrt;
+    at.err = a->d->err_dev;
     CK(launch_attention(at, a->d->st));
     return RK_OK;
   });
@@ -1075,6 +1076,10 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
                       int epi) -> int {
     const float recip = host_recip32((float)cols);
     if (quantized_fmt(ms[0]->fmt)) {
+      if (mv_mode() != 0) {
+        CK(launch_quantize_wide(x, cols, norm_w, recip, eps, nullptr, s->qx, s->xs, s->xsum, st));
+        return enqueue_matvecs(d, n, ms, outs, x, s->qx, s->xs, s->xsum, epi, st);
+      }
       if (matvec_fused_ok(ms[0]->fmt, cols)) {
         Pro p;
         p.pro = norm_w ? PRO_NORM_QUANT : PRO_QUANT;
@@ -1142,6 +1147,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.kv_dim = kvd;
     at.att_stride = s->att_stride;
     at.inv_sqrt = invSqrt;
+    at.err = s->d->err_dev;
     CK(launch_attention(at, st));
     // x += Wo·attOut (model.go:588-594).
     if ((rc = products(1, &l->wo, &s->x, s->att_out, nullptr, qd, EPI_ADD))) return rc;
@@ -1411,7 +1417,12 @@ static int record_head(rk_head *h, const float *x, cudaStream_t st) {
   a.cols = D;
   a.epi = EPI_STORE;
   a.err = h->d->err_dev;
-  if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D)) {
+  if (quantized_fmt(h->wcls->fmt) && mv_mode() != 0) {
+    CK(launch_quantize_wide(x, D, h->rms, recipD, eps, nullptr, h->qx, h->xs, h->xsum, st));
+    a.qx = h->qx;
+    a.xs = h->xs;
+    a.xsum = h->xsum;
+  } else if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D)) {
     // Every CTA computes rmsNorm + quantize8 of x itself.
     a.pro = PRO_NORM_QUANT;
     a.x = x;

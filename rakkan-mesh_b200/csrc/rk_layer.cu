@@ -7,6 +7,8 @@
 #include "rk_detmath.cuh"
 #include "rk_layer.cuh"
 #include "rk_matvec.cuh"
+#include "rk_tma.h"
+#include "rk_umma.cuh"
 
 namespace rk {
 
@@ -161,9 +163,28 @@ __global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int 
   const int g0 = blockIdx.z * gpb, ng = min(gpb, kvMul - g0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nt = min(kTileT, P - t0);
-  for (int e = threadIdx.x; e < kTileT * HS; e += blockDim.x) {
-    const int p = e / HS, i = e % HS;
-    sk[p * (HS + 1) + i] = p < nt ? a.keys[(long long)(t0 + p) * a.kv_dim + kvh * HS + i] : 0.0f;
+  // The key tile in 16-byte pieces, eight loads in flight per thread (the
+  // rows are contiguous 4·HS-byte runs of the cache).
+  constexpr int kPieces = kTileT * HS / 4;
+  for (int base = threadIdx.x; base < kPieces; base += blockDim.x * 8) {
+    float4 r[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int idx = base + u * blockDim.x;
+      const int p = idx / (HS / 4), i4 = idx % (HS / 4);
+      r[u] = idx < kPieces && p < nt
+                 ? *reinterpret_cast<const float4 *>(a.keys + (long long)(t0 + p) * a.kv_dim + kvh * HS + 4 * i4)
+                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int idx = base + u * blockDim.x;
+      if (idx < kPieces) {
+        const int p = idx / (HS / 4), i4 = idx % (HS / 4);
+        float *d = sk + p * (HS + 1) + 4 * i4;
+        d[0] = r[u].x, d[1] = r[u].y, d[2] = r[u].z, d[3] = r[u].w;
+      }
+    }
   }
   for (int e = threadIdx.x; e < ng * HS; e += blockDim.x) sq[e] = a.q[(kvh * kvMul + g0) * HS + e];
   __syncthreads();
@@ -350,11 +371,191 @@ __global__ void __launch_bounds__(kWsMaxGroup * 32) k_attn_wsum_staged(const Att
   if (g < ng) a.out[(kvh * kvMul + g0 + g) * a.hs + slice * 32 + lane] = acc;
 }
 
+// Softmax and weighted values in one kernel. Both are serial chains over
+// the positions (the softmax sum per head, then the value sum per output
+// element), so the kernel is bound by the FADD latency of two chains of P
+// steps (about 4 cycles a step on B200); everything else is arranged to
+// stay off them.
+//
+// CTA (kv head, slice of kFsSlice value elements) serves all GPB query
+// heads of the kv head. At the start it copies the heads' scores into
+// shared memory (one bulk copy per head) and its whole value slice (P rows
+// of 32 bytes) with cp.async from every thread: a strided slice streams at
+// only tens of GB/s per SM, so it is loaded while the softmax runs, not
+// during the value chain. The WPH warps of each head then
+//   1. take the maximum of the scores (order free, as Go's max is),
+//   2. replace them by Exp32(x - max),
+//   3. sum them in position order in one thread (softmax, model.go:640-654),
+//   4. multiply them by Recip32(sum): the attention weights,
+// and thread (head h, element d) finally sums weight·value in position
+// order (model.go:580-586), reading only shared memory, its operands
+// loaded a group of 8 positions ahead. The kFsSlice-wide slices of one kv
+// head all compute the same softmax; the scores stay in L2, so the
+// repetition costs only exps.
+constexpr int kFsSlice = 8;  // value elements per CTA
+constexpr int kFsSmemLimit = 227 * 1024 - 1024;
+constexpr int kFsMaxThreads = 640;
+
+RK_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+
+// Warps per head for the softmax phases.
+static int fs_wph(int gpb) {
+  const int w = (kFsMaxThreads / 32) / gpb;
+  return w > 4 ? 4 : (w < 1 ? 1 : w);
+}
+
+__global__ void __launch_bounds__(kFsMaxThreads)
+    k_attn_softmax_wsum(const AttnArgs a, int gpb, int wph, int ppad) {
+  griddep_trigger();
+  extern __shared__ __align__(128) float fs_smem[];
+  float *sE = fs_smem;                             // [gpb][ppad] scores, then weights
+  float *sV = fs_smem + (size_t)gpb * ppad;        // [P][kFsSlice] values
+  const int maxP = a.positions_dev ? a.max_positions : a.positions;
+  uint64_t *sbar = reinterpret_cast<uint64_t *>(sV + (size_t)((maxP + 3) & ~3) * kFsSlice);
+  float *red = reinterpret_cast<float *>(sbar + 1);  // [gpb][wph] maxima, then [gpb] 1/sum
+  const int kvh = blockIdx.x, slice = blockIdx.y;
+  const int hbase = kvh * gpb;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nthr = blockDim.x;
+  const uint32_t bar = umma::smem_u32(sbar);
+  if (threadIdx.x == 0) {
+    umma::mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  griddep_wait();
+  const int P = attn_positions(a);
+  const int P4 = P & ~3;
+  if (threadIdx.x == 0) {
+    umma::mbar_expect_tx(bar, (uint32_t)gpb * P4 * 4u);
+    if (P4 > 0)
+      for (int g = 0; g < gpb; g++)
+        umma::bulk_g2s(umma::smem_u32(sE + (size_t)g * ppad), a.att + (long long)(hbase + g) * a.att_stride,
+                       P4 * 4u, bar);
+  }
+  {
+    // The value slice: row t's kFsSlice floats in 16-byte pieces.
+    constexpr int kPieces = kFsSlice / 4;
+    const float *vb = a.vals + kvh * a.hs + slice * kFsSlice;
+    for (int i = threadIdx.x; i < P * kPieces; i += nthr) {
+      const int t = i / kPieces, pc = i % kPieces;
+      cp_async16(sV + t * kFsSlice + pc * 4, vb + (long long)t * a.kv_dim + pc * 4);
+    }
+    cp_async_commit();
+  }
+
+  const int g = warp / wph, sub = warp % wph;
+  const bool active = g < gpb;
+  float *e = sE + (size_t)(active ? g : 0) * ppad;
+  const float *x = a.att + (long long)(hbase + (active ? g : 0)) * a.att_stride;
+  if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
+  // 1. maximum.
+  float m = x[0];
+  if (active) {
+    for (int q = sub * 32 + lane; q < P4 / 4; q += wph * 32) {
+      const float4 v = ld4(e + 4 * q);
+      m = gomax(gomax(m, gomax(v.x, v.y)), gomax(v.z, v.w));
+    }
+    if (sub == 0 && P4 + lane < P) {
+      const float t = x[P4 + lane];
+      e[P4 + lane] = t;
+      m = gomax(m, t);
+    }
+  }
+  m = warp_gomax(m);
+  if (lane == 0 && active) red[g * wph + sub] = m;
+  __syncthreads();
+  // 2. exponentials.
+  if (active) {
+    m = red[g * wph];
+    for (int j = 1; j < wph; j++) m = gomax(m, red[g * wph + j]);
+#pragma unroll 4
+    for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = exp32(__fsub_rn(e[i], m));
+  }
+  __syncthreads();
+  // 3. their sum in position order.
+  if (active && sub == 0 && lane == 0) {
+    float sum = 0.0f;
+    int i = 0;
+    const int P32 = P & ~31;
+    if (P32 > 0) {
+      float4 cur[8], nxt[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) cur[j] = ld4(e + 4 * j);
+      for (; i < P32; i += 32) {
+        const int nb = i + 32 < P32 ? i + 32 : i;
+#pragma unroll
+        for (int j = 0; j < 8; j++) nxt[j] = ld4(e + nb + 4 * j);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          sum = __fadd_rn(sum, cur[j].x);
+          sum = __fadd_rn(sum, cur[j].y);
+          sum = __fadd_rn(sum, cur[j].z);
+          sum = __fadd_rn(sum, cur[j].w);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) cur[j] = nxt[j];
+      }
+    }
+    for (; i < P; i++) sum = __fadd_rn(sum, e[i]);
+    red[gpb * wph + g] = recip32(sum);
+  }
+  __syncthreads();
+  // 4. attention weights.
+  if (active) {
+    const float inv = red[gpb * wph + g];
+    for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = __fmul_rn(e[i], inv);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  // 5. weighted values: thread (head h, element d).
+  if (threadIdx.x >= gpb * kFsSlice) return;
+  const int h = threadIdx.x / kFsSlice, d = threadIdx.x % kFsSlice;
+  const float *w = sE + (size_t)h * ppad;
+  const float *v = sV + d;
+  float acc = 0.0f;
+  const int P8 = P & ~7;
+  float wc[8], vc[8], wn[8], vn[8];
+  auto ld8 = [&](int t, float(&wd)[8], float(&vd)[8]) {
+    const float4 a0 = ld4(w + t), a1 = ld4(w + t + 4);
+    wd[0] = a0.x, wd[1] = a0.y, wd[2] = a0.z, wd[3] = a0.w, wd[4] = a1.x, wd[5] = a1.y, wd[6] = a1.z, wd[7] = a1.w;
+#pragma unroll
+    for (int k = 0; k < 8; k++) vd[k] = v[(t + k) * kFsSlice];
+  };
+  if (P8 > 0) {
+    ld8(0, wc, vc);
+    for (int t = 0; t < P8; t += 8) {
+      ld8(t + 8 < P8 ? t + 8 : t, wn, vn);
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, __fmul_rn(wc[k], vc[k]));
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        wc[k] = wn[k];
+        vc[k] = vn[k];
+      }
+    }
+  }
+  for (int t = P8; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t * kFsSlice]));
+  a.out[(hbase + h) * a.hs + slice * kFsSlice + d] = acc;
+}
+
+// Shared memory of k_attn_softmax_wsum for gpb heads of up to maxP
+// positions, or 0 when it does not fit. The score rows are padded to 8 mod
+// 32 floats, so that the heads' rows start in different banks.
+static int fs_smem_bytes(int gpb, int wph, int maxP, int *ppad) {
+  const int pp = ((maxP + 31) & ~31) + 8;
+  const long long bytes = 4LL * gpb * pp + 4LL * ((maxP + 3) & ~3) * kFsSlice + 8 + 4LL * gpb * (wph + 1);
+  if (bytes > kFsSmemLimit) return 0;
+  *ppad = pp;
+  return (int)bytes;
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
   const int maxP = a.positions_dev ? a.max_positions : a.positions;
   if (maxP <= 0) return cudaSuccess;
   const int kvMul = a.heads / a.kv_heads;
-  if (a.hs == 64 || a.hs == 128) {
+  const bool keys16 = reinterpret_cast<uintptr_t>(a.keys) % 16 == 0 && a.kv_dim % 4 == 0;
+  if ((a.hs == 64 || a.hs == 128) && keys16) {
     const int gpb = kvMul < 8 ? kvMul : 8;
     dim3 g1((maxP + kTileT - 1) / kTileT, a.kv_heads, (kvMul + gpb - 1) / gpb);
     if (a.hs == 64) launch_k(k_attn_scores_tile<64>, g1, gpb * 32 < 64 ? 64 : gpb * 32, 0, st, a, gpb);
@@ -363,8 +564,24 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     dim3 g1((maxP + kScoreWarps - 1) / kScoreWarps, a.kv_heads);
     launch_k(k_attn_scores, g1, kScoreWarps * 32, 0, st, a);
   }
-  launch_k(k_attn_softmax, a.heads, kSoftmaxThreads, 0, st, a);
   const int qDim = a.heads * a.hs;
+  {
+    // One kernel for softmax and weighted values when the scores and a value
+    // slice of every position fit shared memory and the operands suit
+    // 16-byte copies.
+    const int gpb = kvMul;
+    const int wph = fs_wph(gpb);
+    int ppad = 0;
+    const int smem = gpb <= 8 ? fs_smem_bytes(gpb, wph, maxP, &ppad) : 0;
+    const bool fused = smem > 0 && a.hs % kFsSlice == 0 && a.kv_dim % 4 == 0 && a.att_stride % 4 == 0 && a.err &&
+                       reinterpret_cast<uintptr_t>(a.vals) % 16 == 0 && reinterpret_cast<uintptr_t>(a.att) % 16 == 0;
+    if (fused) {
+      dim3 g(a.kv_heads, a.hs / kFsSlice);
+      launch_k(k_attn_softmax_wsum, g, gpb * wph * 32, smem, st, a, gpb, wph, ppad);
+      return cudaGetLastError();
+    }
+  }
+  launch_k(k_attn_softmax, a.heads, kSoftmaxThreads, 0, st, a);
   // The staged kernel copies 16-byte pieces: it needs whole 32-float slices
   // and 16-byte-aligned rows of values and scores.
   const bool staged = a.hs % 32 == 0 && a.kv_dim % 4 == 0 && a.att_stride % 4 == 0 &&
@@ -382,7 +599,10 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
 
 cudaError_t init_layer_attributes() {
   const int smem = sizeof(float) * (kWsStages * kWsT * 32 + kWsStages * kWsMaxGroup * kWsT);
-  return cudaFuncSetAttribute(k_attn_wsum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(k_attn_wsum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attn_softmax_wsum, cudaFuncAttributeMaxDynamicSharedMemorySize, kFsSmemLimit);
+  return e;
 }
 
 // ---------------------------------------------------------------------------

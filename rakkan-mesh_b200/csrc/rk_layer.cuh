@@ -37,6 +37,7 @@ struct AttnArgs {
   int positions_add;
   int heads, kv_heads, hs, kv_dim, att_stride;
   float inv_sqrt;
+  int *err;  // device error word for a pipeline wait that timed out
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 // Raises the attention kernels' shared-memory limit; once per device.

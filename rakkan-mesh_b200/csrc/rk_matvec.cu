@@ -17,6 +17,8 @@
 // is exactly qrow's lane order, and at the end of the row combine8 gives
 // the reference's bits. The integer part is order-free, so only those 8
 // serial f32 chains per row are ordered.
+#include <cstdlib>
+
 #include "rk_common.cuh"
 #include "rk_matvec.cuh"
 
@@ -125,6 +127,62 @@ __global__ void __launch_bounds__(512) k_quantize_act(const float *__restrict__ 
   quantize_staged<NORM>(x, n, w, recipN, eps, qx, xs, xsum, &s_inv, stage, kQuantStage);
 }
 
+// The same over many CTAs, a warp per 32-block: lane j holds element j,
+// amax and the block's integer sum are warp reductions (both order free),
+// so a block costs a few dozen instructions and the whole vector one wave.
+// With NORM every CTA first forms Dot32(x, x) in warp 0 (the norm's serial
+// lanes cannot be split) and broadcasts Rsqrt32 through shared memory.
+constexpr int kQwWarps = 8;
+
+template <bool NORM>
+__global__ void __launch_bounds__(kQwWarps * 32) k_quantize_wide(const float *__restrict__ x, int n,
+                                                                  const float *__restrict__ w, float recipN, float eps,
+                                                                  float *__restrict__ xn, int8_t *__restrict__ qx,
+                                                                  float *__restrict__ xs, int *__restrict__ xsum) {
+  __shared__ float s_inv;
+  griddep_trigger();
+  griddep_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float inv = 0.0f;
+  if (NORM) {
+    if (warp == 0) {
+      float s = 0.0f;
+#pragma unroll 8
+      for (int i = lane; i < n; i += 32) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+      const float dot = combine32(s);
+      if (lane == 0) s_inv = rsqrt32(__fadd_rn(__fmul_rn(dot, recipN), eps));
+    }
+    __syncthreads();
+    inv = s_inv;
+  }
+  const int b = blockIdx.x * kQwWarps + warp;
+  if (b >= n / 32) return;
+  float v = x[b * 32 + lane];
+  if (NORM) {
+    v = __fmul_rn(w[b * 32 + lane], __fmul_rn(inv, v));
+    if (xn) xn[b * 32 + lane] = v;
+  }
+  const float amax = gomax(0.0f, warp_gomax(fabsf(v)));
+  const float d = __fmul_rn(amax, u2f(K_1_127));
+  int q = 0;
+  if (!(d == 0.0f || d != d)) q = quant_q8(__fmul_rn(v, recip32(d)));
+  qx[b * 32 + lane] = (int8_t)q;
+  const int sum = __reduce_add_sync(0xffffffffu, q);
+  if (lane == 0) {
+    xs[b] = d;
+    if (xsum) xsum[b] = sum;
+  }
+}
+
+cudaError_t launch_quantize_wide(const float *x, int n, const float *w, float recipN, float eps, float *xn,
+                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st) {
+  const int nb = n / 32;
+  if (nb <= 0) return cudaSuccess;
+  const int grid = (nb + kQwWarps - 1) / kQwWarps;
+  if (w) return launch_k(k_quantize_wide<true>, grid, kQwWarps * 32, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
+  return launch_k(k_quantize_wide<false>, grid, kQwWarps * 32, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
+}
+
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st) {
   int threads = n >= 16 * 32 ? 512 : ((n / 32) > 0 ? (n / 32) * 32 : 32);
@@ -173,6 +231,11 @@ RK_DEV uint64_t evict_first_policy() {
   return pol;
 }
 
+// Brings bytes of global memory into L2 without occupying the SM.
+RK_DEV void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 RK_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
@@ -185,6 +248,7 @@ RK_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar
 // Quantized matvec with a per-warp TMA ring.
 // ---------------------------------------------------------------------------
 constexpr int kSegBytes = 4096;  // weight bytes per segment
+constexpr int kPrefetchSegs = 4;  // segments per warp prefetched into L2 before the predecessor ends
 
 template <int FMT>
 struct QTraits;
@@ -384,13 +448,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     pslot = pslot + 1 == SLOTS ? 0 : pslot + 1;
   };
 
-  // Start the weight stream (read-only: it may run before the predecessor
-  // kernel has finished), then wait for the predecessor and stage the
-  // input: the copies run meanwhile.
+  // Before the predecessor kernel has finished, only the weights (which no
+  // kernel writes) may be touched: pull the warp's first segments into L2.
+  // They are not copied to shared memory yet, because the input's loads
+  // below would then queue behind a full ring of weight traffic; from L2 the
+  // ring fills quickly once the input is on its way.
   griddep_trigger();
+  if (lane == 0) {
+    Cursor pf = pc;
+    for (long long k = 0; k < min(total, (long long)kPrefetchSegs); k++) {
+      const SegInfo s = seg_info<FMT>(a, nb, pf);
+      bulk_prefetch_l2(s.wsrc, s.wbytes);
+      bulk_prefetch_l2(s.ssrc, s.sbytes);
+      cursor_next(pf, a, nsub, nseg);
+    }
+  }
+  griddep_wait();
   if (lane == 0)
     for (int k = 0; k < SLOTS; k++) issue();
-  griddep_wait();
 
   if (a.pro != PRO_GIVEN) {
     __shared__ float s_inv;
@@ -574,16 +649,25 @@ cudaError_t init_matvec_attributes() {
   return e;
 }
 
+int mv_mode() {
+  static const int m = [] {
+    const char *e = getenv("RK_MV_MODE");
+    return e ? atoi(e) : 0;
+  }();
+  return m;
+}
+
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
   const bool quant = a.fmt == FMT_Q8_0 || a.fmt == FMT_Q4_0;
   if (quant && a.pro != PRO_GIVEN && !matvec_fused_ok(a.fmt, a.cols)) return cudaErrorInvalidValue;
   const bool fused = a.pro != PRO_GIVEN;
+  const int in_smem = a.cols <= kSmemColsMax && (fused || mv_mode() != 2) ? 1 : 0;
   if (a.fmt == FMT_Q8_0)
     return launch_k(k_matvec_q<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q8_0>(a.cols, fused), st, a,
-                    a.cols <= kSmemColsMax ? 1 : 0);
+                    in_smem);
   if (a.fmt == FMT_Q4_0)
     return launch_k(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q4_0>(a.cols, fused), st, a,
-                    a.cols <= kSmemColsMax ? 1 : 0);
+                    in_smem);
   if (a.fmt == FMT_F32) return launch_k(k_matvec_f<FMT_F32>, num_sms * 4, 256, 0, st, a);
   return launch_k(k_matvec_f<FMT_BF16>, num_sms * 4, 256, 0, st, a);
 }

@@ -62,10 +62,20 @@ constexpr int kSmemColsMax = 32768;
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st);
 
+// The same quantization spread over ceil(n/256) CTAs, a warp per 32-block
+// (each CTA recomputes the norm's Dot32 when w != nullptr).
+cudaError_t launch_quantize_wide(const float *x, int n, const float *w, float recipN, float eps, float *xn,
+                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st);
+
 // out = matrices · x, bits identical to num.MatVecQ8/Q4/32/BF16.
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
 
 int matvec_smem_bytes(int fmt, int cols);
+
+// Experiment selector (RK_MV_MODE): 0 = quantize in the matvec prologue,
+// 1 = separate multi-CTA quantizer, input staged in shared memory,
+// 2 = separate quantizer, input read from global memory.
+int mv_mode();
 
 // Whether a matvec of this format and width can quantize its input in its
 // own prologue (PRO_QUANT / PRO_NORM_QUANT): the input and its staging must

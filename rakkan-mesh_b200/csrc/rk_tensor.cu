@@ -19,6 +19,7 @@
 #include "rk_common.cuh"
 #include "rk_matvec.cuh"
 #include "rk_tensor.cuh"
+#include "rk_tma.h"
 #include "rk_umma.cuh"
 
 namespace rk {
@@ -294,19 +295,26 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   return fn;
 }
 
+bool tmap_available() { return tmap_encoder() != nullptr; }
+
+bool tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *ptr, uint64_t inner, uint64_t outer,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  auto fn = tmap_encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dtype, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // A row-major int8 matrix [outer][inner] seen in (box_inner × box_outer)
 // tiles with the 128-byte swizzle; out-of-range elements read as zero.
 static bool tmap_i8(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
                     uint32_t box_outer) {
-  auto fn = tmap_encoder();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, ptr, inner, outer, inner, box_inner, box_outer, true);
 }
 
 template <int NT, bool BMN>
@@ -348,7 +356,7 @@ bool tensor_i8_tc_ok(int transposed, int m, int k, int n, const void *a, const v
   const auto aligned = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
   if (!aligned(a) || !aligned(b) || k % 16 != 0 || (!transposed && n % 16 != 0)) return false;
   // |sum| <= k·128·128 stays below 2^31 for k < 2^17, so no partial sum wraps.
-  return k < (1 << 17) && tmap_encoder() != nullptr;
+  return k < (1 << 17) && tmap_available();
 }
 
 __global__ void k_fill_hash(int dtype, void *p, long long n, uint32_t seed) {

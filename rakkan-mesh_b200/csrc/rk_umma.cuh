@@ -1,6 +1,6 @@
-// rk_umma.cuh — sm_100a building blocks for tensor-core tiles: mbarriers,
-// 2-D TMA tile loads (no multicast), shared-memory matrix descriptors, and
-// the tcgen05 MMA / TMEM instructions, as inline PTX.
+// rk_umma.cuh — sm_100a building blocks as inline PTX: mbarriers, 1-D bulk
+// and 2-D TMA tile loads (no multicast), shared-memory matrix descriptors,
+// and the tcgen05 MMA / TMEM instructions.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -18,6 +18,18 @@ RK_DEV void mbar_init(uint32_t bar, uint32_t count) {
 
 RK_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+RK_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple
+// of 16), counted in bytes on `bar`; no multicast.
+RK_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 
 RK_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
