@@ -133,6 +133,10 @@ RK_DEV float exp32(float x) {
   p = __fadd_rn(__fmul_rn(p, r), 1.0f);
   p = __fadd_rn(__fmul_rn(p, r), 1.0f);
   int ni = int(n);
+  // p·2^n rounded once to float32. When 2^n is a normal float the float
+  // product is that single rounding already; otherwise (n > 127 or n < -126)
+  // form the exact product in float64 and round it once.
+  if (ni >= -126 && ni <= 127) return __fmul_rn(p, u2f(uint32_t(ni + 127) << 23));
   double scale = __longlong_as_double((long long)(ni + 1023) << 52);
   return __double2float_rn(__dmul_rn(double(p), scale));
 }

@@ -378,23 +378,26 @@ __global__ void __launch_bounds__(kWsMaxGroup * 32) k_attn_wsum_staged(const Att
 // stay off them.
 //
 // CTA (kv head, slice of kFsSlice value elements) serves all GPB query
-// heads of the kv head. At the start it copies the heads' scores into
-// shared memory (one bulk copy per head) and its whole value slice (P rows
-// of 32 bytes) with cp.async from every thread: a strided slice streams at
-// only tens of GB/s per SM, so it is loaded while the softmax runs, not
-// during the value chain. The WPH warps of each head then
-//   1. take the maximum of the scores (order free, as Go's max is),
-//   2. replace them by Exp32(x - max),
-//   3. sum them in position order in one thread (softmax, model.go:640-654),
-//   4. multiply them by Recip32(sum): the attention weights,
+// heads of the kv head; warp w works for head w mod GPB, so the heads'
+// serial threads sit on different SM sub-partitions. At the start one
+// thread copies the heads' scores into shared memory (one bulk copy per
+// head). Then, per head,
+//   1. the maximum of the scores (order free, as Go's max is),
+//   2. Exp32(x - max) in place,
+//   3. their sum in position order by one thread (softmax,
+//      model.go:640-654), while the warps of no head copy the value slice
+//      (P rows of kFsSlice floats) into shared memory transposed, element-
+//      major, so that the value chains read four positions per load,
+//   4. multiplication by Recip32(sum): the attention weights,
 // and thread (head h, element d) finally sums weight·value in position
 // order (model.go:580-586), reading only shared memory, its operands
-// loaded a group of 8 positions ahead. The kFsSlice-wide slices of one kv
-// head all compute the same softmax; the scores stay in L2, so the
-// repetition costs only exps.
+// loaded 16 positions ahead. The kFsSlice-wide slices of one kv head all
+// compute the same softmax; the scores stay in L2, so the repetition costs
+// only exps.
 constexpr int kFsSlice = 8;  // value elements per CTA
 constexpr int kFsSmemLimit = 227 * 1024 - 1024;
 constexpr int kFsMaxThreads = 640;
+constexpr int kFsRowsPerThread = 4;  // value rows in flight per loading thread
 
 RK_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
@@ -404,19 +407,24 @@ static int fs_wph(int gpb) {
   return w > 4 ? 4 : (w < 1 ? 1 : w);
 }
 
+// Row pitches: score rows 8 mod 32 floats apart and value rows 4 mod 32, so
+// that the lanes' 16-byte loads of one step fall in distinct banks.
+RK_HD int fs_ppad(int maxP) { return ((maxP + 31) & ~31) + 8; }
+RK_HD int fs_vpad(int maxP) { return ((maxP + 31) & ~31) + 4; }
+
 __global__ void __launch_bounds__(kFsMaxThreads)
-    k_attn_softmax_wsum(const AttnArgs a, int gpb, int wph, int ppad) {
+    k_attn_softmax_wsum(const AttnArgs a, int gpb, int wph) {
   griddep_trigger();
   extern __shared__ __align__(128) float fs_smem[];
-  float *sE = fs_smem;                             // [gpb][ppad] scores, then weights
-  float *sV = fs_smem + (size_t)gpb * ppad;        // [P][kFsSlice] values
   const int maxP = a.positions_dev ? a.max_positions : a.positions;
-  uint64_t *sbar = reinterpret_cast<uint64_t *>(sV + (size_t)((maxP + 3) & ~3) * kFsSlice);
+  const int ppad = fs_ppad(maxP), vpad = fs_vpad(maxP);
+  float *sE = fs_smem;                        // [gpb][ppad] scores, then weights
+  float *sV = fs_smem + (size_t)gpb * ppad;   // [kFsSlice][vpad] values, element-major
+  uint64_t *sbar = reinterpret_cast<uint64_t *>(sV + (size_t)kFsSlice * vpad);
   float *red = reinterpret_cast<float *>(sbar + 1);  // [gpb][wph] maxima, then [gpb] 1/sum
   const int kvh = blockIdx.x, slice = blockIdx.y;
   const int hbase = kvh * gpb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nthr = blockDim.x;
   const uint32_t bar = umma::smem_u32(sbar);
   if (threadIdx.x == 0) {
     umma::mbar_init(bar, 1);
@@ -433,121 +441,135 @@ __global__ void __launch_bounds__(kFsMaxThreads)
         umma::bulk_g2s(umma::smem_u32(sE + (size_t)g * ppad), a.att + (long long)(hbase + g) * a.att_stride,
                        P4 * 4u, bar);
   }
-  {
-    // The value slice: row t's kFsSlice floats in 16-byte pieces.
-    constexpr int kPieces = kFsSlice / 4;
-    const float *vb = a.vals + kvh * a.hs + slice * kFsSlice;
-    for (int i = threadIdx.x; i < P * kPieces; i += nthr) {
-      const int t = i / kPieces, pc = i % kPieces;
-      cp_async16(sV + t * kFsSlice + pc * 4, vb + (long long)t * a.kv_dim + pc * 4);
-    }
-    cp_async_commit();
-  }
 
-  const int g = warp / wph, sub = warp % wph;
-  const bool active = g < gpb;
-  float *e = sE + (size_t)(active ? g : 0) * ppad;
-  const float *x = a.att + (long long)(hbase + (active ? g : 0)) * a.att_stride;
+  const int g = warp % gpb, sub = warp / gpb;
+  float *e = sE + (size_t)g * ppad;
+  const float *x = a.att + (long long)(hbase + g) * a.att_stride;
+  const float tail = P4 + lane < P ? x[P4 + lane] : 0.0f;
   if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
   // 1. maximum.
-  float m = x[0];
-  if (active) {
-    for (int q = sub * 32 + lane; q < P4 / 4; q += wph * 32) {
-      const float4 v = ld4(e + 4 * q);
-      m = gomax(gomax(m, gomax(v.x, v.y)), gomax(v.z, v.w));
-    }
-    if (sub == 0 && P4 + lane < P) {
-      const float t = x[P4 + lane];
-      e[P4 + lane] = t;
-      m = gomax(m, t);
-    }
+  float m = P4 > 0 ? e[0] : x[0];
+  for (int q = sub * 32 + lane; q < P4 / 4; q += wph * 32) {
+    const float4 v = ld4(e + 4 * q);
+    m = gomax(gomax(m, gomax(v.x, v.y)), gomax(v.z, v.w));
+  }
+  if (sub == 0 && P4 + lane < P) {
+    e[P4 + lane] = tail;
+    m = gomax(m, tail);
   }
   m = warp_gomax(m);
-  if (lane == 0 && active) red[g * wph + sub] = m;
+  if (lane == 0) red[g * wph + sub] = m;
   __syncthreads();
   // 2. exponentials.
-  if (active) {
-    m = red[g * wph];
-    for (int j = 1; j < wph; j++) m = gomax(m, red[g * wph + j]);
+  m = red[g * wph];
+  for (int j = 1; j < wph; j++) m = gomax(m, red[g * wph + j]);
 #pragma unroll 4
-    for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = exp32(__fsub_rn(e[i], m));
-  }
+  for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = exp32(__fsub_rn(e[i], m));
   __syncthreads();
-  // 3. their sum in position order.
-  if (active && sub == 0 && lane == 0) {
-    float sum = 0.0f;
-    int i = 0;
-    const int P32 = P & ~31;
-    if (P32 > 0) {
-      float4 cur[8], nxt[8];
+  if (warp < gpb) {
+    // 3. their sum in position order.
+    if (lane == 0) {
+      float sum = 0.0f;
+      int i = 0;
+      const int P32 = P & ~31;
+      if (P32 > 0) {
+        float4 cur[8], nxt[8];
 #pragma unroll
-      for (int j = 0; j < 8; j++) cur[j] = ld4(e + 4 * j);
-      for (; i < P32; i += 32) {
-        const int nb = i + 32 < P32 ? i + 32 : i;
+        for (int j = 0; j < 8; j++) cur[j] = ld4(e + 4 * j);
+        for (; i < P32; i += 32) {
+          const int nb = i + 32 < P32 ? i + 32 : i;
 #pragma unroll
-        for (int j = 0; j < 8; j++) nxt[j] = ld4(e + nb + 4 * j);
+          for (int j = 0; j < 8; j++) nxt[j] = ld4(e + nb + 4 * j);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          sum = __fadd_rn(sum, cur[j].x);
-          sum = __fadd_rn(sum, cur[j].y);
-          sum = __fadd_rn(sum, cur[j].z);
-          sum = __fadd_rn(sum, cur[j].w);
+          for (int j = 0; j < 8; j++) {
+            sum = __fadd_rn(sum, cur[j].x);
+            sum = __fadd_rn(sum, cur[j].y);
+            sum = __fadd_rn(sum, cur[j].z);
+            sum = __fadd_rn(sum, cur[j].w);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; j++) cur[j] = nxt[j];
         }
+      }
+      for (; i < P; i++) sum = __fadd_rn(sum, e[i]);
+      red[gpb * wph + g] = recip32(sum);
+    }
+  } else {
+    // Meanwhile: the value slice, row t's kFsSlice floats to sV[d][t].
+    const int tid = threadIdx.x - gpb * 32, nld = blockDim.x - gpb * 32;
+    const float *vb = a.vals + kvh * a.hs + slice * kFsSlice;
+    for (int t0 = 0; t0 < P; t0 += nld * kFsRowsPerThread) {
+      float4 r[kFsRowsPerThread][2];
 #pragma unroll
-        for (int j = 0; j < 8; j++) cur[j] = nxt[j];
+      for (int u = 0; u < kFsRowsPerThread; u++) {
+        const int t = t0 + u * nld + tid;
+        if (t < P) {
+          r[u][0] = ld4(vb + (long long)t * a.kv_dim);
+          r[u][1] = ld4(vb + (long long)t * a.kv_dim + 4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kFsRowsPerThread; u++) {
+        const int t = t0 + u * nld + tid;
+        if (t < P) {
+          sV[0 * vpad + t] = r[u][0].x, sV[1 * vpad + t] = r[u][0].y, sV[2 * vpad + t] = r[u][0].z;
+          sV[3 * vpad + t] = r[u][0].w, sV[4 * vpad + t] = r[u][1].x, sV[5 * vpad + t] = r[u][1].y;
+          sV[6 * vpad + t] = r[u][1].z, sV[7 * vpad + t] = r[u][1].w;
+        }
       }
     }
-    for (; i < P; i++) sum = __fadd_rn(sum, e[i]);
-    red[gpb * wph + g] = recip32(sum);
   }
   __syncthreads();
   // 4. attention weights.
-  if (active) {
+  {
     const float inv = red[gpb * wph + g];
     for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = __fmul_rn(e[i], inv);
   }
-  cp_async_wait<0>();
   __syncthreads();
   // 5. weighted values: thread (head h, element d).
   if (threadIdx.x >= gpb * kFsSlice) return;
   const int h = threadIdx.x / kFsSlice, d = threadIdx.x % kFsSlice;
   const float *w = sE + (size_t)h * ppad;
-  const float *v = sV + d;
+  const float *v = sV + (size_t)d * vpad;
   float acc = 0.0f;
-  const int P8 = P & ~7;
-  float wc[8], vc[8], wn[8], vn[8];
-  auto ld8 = [&](int t, float(&wd)[8], float(&vd)[8]) {
-    const float4 a0 = ld4(w + t), a1 = ld4(w + t + 4);
-    wd[0] = a0.x, wd[1] = a0.y, wd[2] = a0.z, wd[3] = a0.w, wd[4] = a1.x, wd[5] = a1.y, wd[6] = a1.z, wd[7] = a1.w;
+  const int P16 = P & ~15;
+  if (P16 > 0) {
+    float4 wc[4], vc[4], wn[4], vn[4];
 #pragma unroll
-    for (int k = 0; k < 8; k++) vd[k] = v[(t + k) * kFsSlice];
-  };
-  if (P8 > 0) {
-    ld8(0, wc, vc);
-    for (int t = 0; t < P8; t += 8) {
-      ld8(t + 8 < P8 ? t + 8 : t, wn, vn);
+    for (int j = 0; j < 4; j++) {
+      wc[j] = ld4(w + 4 * j);
+      vc[j] = ld4(v + 4 * j);
+    }
+    for (int t = 0; t < P16; t += 16) {
+      const int tn = t + 16 < P16 ? t + 16 : t;
 #pragma unroll
-      for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, __fmul_rn(wc[k], vc[k]));
+      for (int j = 0; j < 4; j++) {
+        wn[j] = ld4(w + tn + 4 * j);
+        vn[j] = ld4(v + tn + 4 * j);
+      }
 #pragma unroll
-      for (int k = 0; k < 8; k++) {
-        wc[k] = wn[k];
-        vc[k] = vn[k];
+      for (int j = 0; j < 4; j++) {
+        acc = __fadd_rn(acc, __fmul_rn(wc[j].x, vc[j].x));
+        acc = __fadd_rn(acc, __fmul_rn(wc[j].y, vc[j].y));
+        acc = __fadd_rn(acc, __fmul_rn(wc[j].z, vc[j].z));
+        acc = __fadd_rn(acc, __fmul_rn(wc[j].w, vc[j].w));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        wc[j] = wn[j];
+        vc[j] = vn[j];
       }
     }
   }
-  for (int t = P8; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t * kFsSlice]));
+  for (int t = P16; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t]));
   a.out[(hbase + h) * a.hs + slice * kFsSlice + d] = acc;
 }
 
 // Shared memory of k_attn_softmax_wsum for gpb heads of up to maxP
-// positions, or 0 when it does not fit. The score rows are padded to 8 mod
-// 32 floats, so that the heads' rows start in different banks.
-static int fs_smem_bytes(int gpb, int wph, int maxP, int *ppad) {
-  const int pp = ((maxP + 31) & ~31) + 8;
-  const long long bytes = 4LL * gpb * pp + 4LL * ((maxP + 3) & ~3) * kFsSlice + 8 + 4LL * gpb * (wph + 1);
-  if (bytes > kFsSmemLimit) return 0;
-  *ppad = pp;
-  return (int)bytes;
+// positions, or 0 when it does not fit.
+static int fs_smem_bytes(int gpb, int wph, int maxP) {
+  const long long bytes = 4LL * gpb * fs_ppad(maxP) + 4LL * kFsSlice * fs_vpad(maxP) + 8 + 4LL * gpb * (wph + 1);
+  return bytes > kFsSmemLimit ? 0 : (int)bytes;
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
@@ -569,15 +591,16 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     // One kernel for softmax and weighted values when the scores and a value
     // slice of every position fit shared memory and the operands suit
     // 16-byte copies.
+    // The value rows are loaded by the warps beyond the first gpb, so the
+    // kernel needs gpb < total warps (wph >= 2).
     const int gpb = kvMul;
     const int wph = fs_wph(gpb);
-    int ppad = 0;
-    const int smem = gpb <= 8 ? fs_smem_bytes(gpb, wph, maxP, &ppad) : 0;
+    const int smem = gpb <= 8 && wph >= 2 ? fs_smem_bytes(gpb, wph, maxP) : 0;
     const bool fused = smem > 0 && a.hs % kFsSlice == 0 && a.kv_dim % 4 == 0 && a.att_stride % 4 == 0 && a.err &&
                        reinterpret_cast<uintptr_t>(a.vals) % 16 == 0 && reinterpret_cast<uintptr_t>(a.att) % 16 == 0;
     if (fused) {
       dim3 g(a.kv_heads, a.hs / kFsSlice);
-      launch_k(k_attn_softmax_wsum, g, gpb * wph * 32, smem, st, a, gpb, wph, ppad);
+      launch_k(k_attn_softmax_wsum, g, gpb * wph * 32, smem, st, a, gpb, wph);
       return cudaGetLastError();
     }
   }
