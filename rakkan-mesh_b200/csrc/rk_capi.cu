@@ -998,6 +998,11 @@ struct rk_stage {
   std::vector<rk_layer *> layers;
   int ctx = 0;
   int att_stride = 0;  // ctx rounded up to 4 floats (16-byte rows of scores)
+  // Value caches are stored transposed (element i's positions contiguous,
+  // v_pitch floats apart) when the attention runs as one fused kernel,
+  // which then fetches a CTA's value slice with a few bulk copies; 0 keeps
+  // the reference's [ctx][kvDim] rows.
+  int v_pitch = 0;
   // Activations and scratch (gpustage.go:51-83).
   float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att_out = nullptr, *hb = nullptr,
         *hb2 = nullptr, *att = nullptr, *xs = nullptr, *cos_ = nullptr, *sin_ = nullptr, *io = nullptr;
@@ -1124,6 +1129,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     qp.sin_ = s->sin_;
     qp.key_cache = s->keys[li];
     qp.val_cache = s->vals[li];
+    qp.v_pitch = s->v_pitch;
     qp.pos_dev = s->pos_dev;
     qp.heads = c->heads;
     qp.kv_heads = c->kv_heads;
@@ -1136,6 +1142,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.q = s->q;
     at.keys = s->keys[li];
     at.vals = s->vals[li];
+    at.v_pitch = s->v_pitch;
     at.att = s->att;
     at.out = s->att_out;
     at.positions_dev = s->pos_dev;
@@ -1256,6 +1263,7 @@ extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *l
   ALLOC(hb, 4 * (size_t)H);
   ALLOC(hb2, 4 * (size_t)H);
   s->att_stride = (ctx + 3) & ~3;
+  s->v_pitch = attention_fused_ok(c->heads, c->kv_heads, hs, ctx) ? s->att_stride : 0;
   ALLOC(att, 4 * (size_t)c->heads * s->att_stride);
   ALLOC(qx, (size_t)widest);
   ALLOC(xs, 4 * (size_t)(widest / 32 + 1));
@@ -1268,7 +1276,7 @@ extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *l
   for (int i = 0; i < n; i++) {
     if ((rc = A(4 * (size_t)ctx * kvd, &p))) goto fail_;
     s->keys.push_back((float *)p);
-    if ((rc = A(4 * (size_t)ctx * kvd, &p))) goto fail_;
+    if ((rc = A(4 * (size_t)(s->v_pitch > 0 ? s->v_pitch : ctx) * kvd, &p))) goto fail_;
     s->vals.push_back((float *)p);
   }
 #undef ALLOC
@@ -1951,7 +1959,10 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
   const long long n = (long long)positions * kvd;
   for (size_t l = 0; l < s->layers.size(); l++) {
     CK(launch_gen_normal(seed, 0xA0000ull + 2 * l, 0, n, 1.0f, s->keys[l], d->st));
-    CK(launch_gen_normal(seed, 0xA0001ull + 2 * l, 0, n, 1.0f, s->vals[l], d->st));
+    if (s->v_pitch > 0)
+      CK(launch_gen_normal_t(seed, 0xA0001ull + 2 * l, positions, kvd, s->v_pitch, 1.0f, s->vals[l], d->st));
+    else
+      CK(launch_gen_normal(seed, 0xA0001ull + 2 * l, 0, n, 1.0f, s->vals[l], d->st));
   }
   return sync_dev(d);
 }

@@ -174,6 +174,15 @@ RK_DEV float combine8(float s) {
   return s;
 }
 
+// Go's max over a set, branch free: floats map to unsigned keys whose order
+// is the float order with -0 below +0, so the largest key is max(...) of the
+// non-NaN values (+0 over -0, as Go); any NaN makes the result NaN.
+RK_DEV uint32_t fkey(float v) {
+  const uint32_t b = f2u(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+RK_DEV float fkey_value(uint32_t k) { return u2f((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k); }
+
 RK_DEV float warp_gomax(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = gomax(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -13,20 +13,44 @@
 namespace rk {
 
 
+// Element i of the tensor whose stream key is `key`.
+RK_DEV float gen_value(uint64_t key, long long i, float scale) {
+  const uint64_t p = uint64_t(i >> 1);
+  const uint64_t a = splitmix64(key + 2 * p), b = splitmix64(key + 2 * p + 1);
+  const double u1 = __dmul_rn(double((a >> 11) + 1), 0x1p-53);
+  const double u2 = __dmul_rn(double(b >> 11), 0x1p-53);
+  const double r = __dsqrt_rn(__dmul_rn(-2.0, log_det(u1)));
+  double s, c;
+  sincos_det(__dmul_rn(0x1.921fb54442d18p+2, u2), s, c);
+  const double z = (i & 1) ? s : c;
+  return __double2float_rn(__dmul_rn(double(scale), __dmul_rn(r, z)));
+}
+
 __global__ void k_gen_normal(uint64_t seed, uint64_t tid, long long offset, long long n, float scale, float *out) {
   const uint64_t key = splitmix64(splitmix64(seed) ^ tid);
+  for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x)
+    out[j] = gen_value(key, offset + j, scale);
+}
+
+// Element (t, i) of a rows × cols tensor (index t·cols + i) to out[i·pitch + t].
+__global__ void k_gen_normal_t(uint64_t seed, uint64_t tid, int rows, int cols, long long pitch, float scale,
+                               float *out) {
+  const uint64_t key = splitmix64(splitmix64(seed) ^ tid);
+  const long long n = (long long)rows * cols;
   for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x) {
-    const long long i = offset + j;
-    const uint64_t p = uint64_t(i >> 1);
-    const uint64_t a = splitmix64(key + 2 * p), b = splitmix64(key + 2 * p + 1);
-    const double u1 = __dmul_rn(double((a >> 11) + 1), 0x1p-53);
-    const double u2 = __dmul_rn(double(b >> 11), 0x1p-53);
-    const double r = __dsqrt_rn(__dmul_rn(-2.0, log_det(u1)));
-    double s, c;
-    sincos_det(__dmul_rn(0x1.921fb54442d18p+2, u2), s, c);
-    const double z = (i & 1) ? s : c;
-    out[j] = __double2float_rn(__dmul_rn(double(scale), __dmul_rn(r, z)));
+    const long long t = j % rows, i = j / rows;  // consecutive threads write consecutive t
+    out[i * pitch + t] = gen_value(key, t * cols + i, scale);
   }
+}
+
+cudaError_t launch_gen_normal_t(uint64_t seed, uint64_t tid, int rows, int cols, long long pitch, float scale,
+                                float *out, cudaStream_t st) {
+  const long long n = (long long)rows * cols;
+  if (n <= 0) return cudaSuccess;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  k_gen_normal_t<<<int(blocks), 256, 0, st>>>(seed, tid, rows, cols, pitch, scale, out);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gen_normal(uint64_t seed, uint64_t tid, long long offset, long long n, float scale, float *out,

@@ -308,6 +308,10 @@ RK_DEV void cp_async16(void *smem, const void *gmem) {
                "l"(gmem)
                : "memory");
 }
+RK_DEV void cp_async4(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
 RK_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 RK_DEV void cp_async_wait() {
@@ -381,13 +385,14 @@ __global__ void __launch_bounds__(kWsMaxGroup * 32) k_attn_wsum_staged(const Att
 // heads of the kv head; warp w works for head w mod GPB, so the heads'
 // serial threads sit on different SM sub-partitions. At the start one
 // thread copies the heads' scores into shared memory (one bulk copy per
-// head). Then, per head,
+// head) and every thread starts asynchronous 4-byte copies of the value
+// slice (P rows of kFsSlice floats) into shared memory transposed,
+// element-major, so that the value chains read four positions per load;
+// they land while the softmax runs. Then, per head,
 //   1. the maximum of the scores (order free, as Go's max is),
 //   2. Exp32(x - max) in place,
 //   3. their sum in position order by one thread (softmax,
-//      model.go:640-654), while the warps of no head copy the value slice
-//      (P rows of kFsSlice floats) into shared memory transposed, element-
-//      major, so that the value chains read four positions per load,
+//      model.go:640-654),
 //   4. multiplication by Recip32(sum): the attention weights,
 // and thread (head h, element d) finally sums weight·value in position
 // order (model.go:580-586), reading only shared memory, its operands
@@ -397,7 +402,6 @@ __global__ void __launch_bounds__(kWsMaxGroup * 32) k_attn_wsum_staged(const Att
 constexpr int kFsSlice = 8;  // value elements per CTA
 constexpr int kFsSmemLimit = 227 * 1024 - 1024;
 constexpr int kFsMaxThreads = 640;
-constexpr int kFsRowsPerThread = 4;  // value rows in flight per loading thread
 
 RK_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
@@ -409,7 +413,7 @@ static int fs_wph(int gpb) {
 
 // Row pitches: score rows 8 mod 32 floats apart and value rows 4 mod 32, so
 // that the lanes' 16-byte loads of one step fall in distinct banks.
-RK_HD int fs_ppad(int maxP) { return ((maxP + 31) & ~31) + 8; }
+RK_HD int fs_ppad(int maxP) { return ((maxP + 31) & ~31) + 40; }
 RK_HD int fs_vpad(int maxP) { return ((maxP + 31) & ~31) + 4; }
 
 __global__ void __launch_bounds__(kFsMaxThreads)
@@ -420,14 +424,16 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   const int ppad = fs_ppad(maxP), vpad = fs_vpad(maxP);
   float *sE = fs_smem;                        // [gpb][ppad] scores, then weights
   float *sV = fs_smem + (size_t)gpb * ppad;   // [kFsSlice][vpad] values, element-major
-  uint64_t *sbar = reinterpret_cast<uint64_t *>(sV + (size_t)kFsSlice * vpad);
-  float *red = reinterpret_cast<float *>(sbar + 1);  // [gpb][wph] maxima, then [gpb] 1/sum
+  uint64_t *sbar = reinterpret_cast<uint64_t *>(sV + (size_t)kFsSlice * vpad);  // scores, values
+  float *red = reinterpret_cast<float *>(sbar + 2);  // [gpb][wph] maxima, then [gpb] 1/sum
   const int kvh = blockIdx.x, slice = blockIdx.y;
   const int hbase = kvh * gpb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t bar = umma::smem_u32(sbar);
+  const uint32_t vbar = bar + 8;
   if (threadIdx.x == 0) {
     umma::mbar_init(bar, 1);
+    umma::mbar_init(vbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -442,29 +448,77 @@ __global__ void __launch_bounds__(kFsMaxThreads)
                        P4 * 4u, bar);
   }
 
+  if (a.v_pitch > 0) {
+    // Transposed cache: the slice's kFsSlice elements are contiguous runs
+    // of positions, one bulk copy each (rounded up to whole float4s, which
+    // the cache's pitch leaves room for).
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = (uint32_t)((P + 3) & ~3) * 4u;
+      umma::mbar_expect_tx(vbar, bytes * kFsSlice);
+      for (int dd = 0; dd < kFsSlice; dd++)
+        umma::bulk_g2s(umma::smem_u32(sV + (size_t)dd * vpad),
+                       a.vals + (long long)(kvh * a.hs + slice * kFsSlice + dd) * a.v_pitch, bytes, vbar);
+    }
+  } else {
+    // Row cache: copied asynchronously and transposed, element d of row t
+    // to sV[d][t], 4 bytes per copy (a warp writes 32 consecutive positions
+    // of one element; a thread's 8 copies of a row share one 32-byte
+    // sector). They land while the softmax runs.
+    const float *vb = a.vals + kvh * a.hs + slice * kFsSlice;
+    for (int t = threadIdx.x; t < P; t += blockDim.x) {
+      const float *src = vb + (long long)t * a.kv_dim;
+#pragma unroll
+      for (int dd = 0; dd < kFsSlice; dd++) cp_async4(sV + (size_t)dd * vpad + t, src + dd);
+    }
+    cp_async_commit();
+  }
   const int g = warp % gpb, sub = warp / gpb;
   float *e = sE + (size_t)g * ppad;
   const float *x = a.att + (long long)(hbase + g) * a.att_stride;
   const float tail = P4 + lane < P ? x[P4 + lane] : 0.0f;
   if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
-  // 1. maximum.
-  float m = P4 > 0 ? e[0] : x[0];
+  // 1. maximum, as the largest order key plus a NaN flag.
+  uint32_t key = fkey(P4 > 0 ? e[0] : x[0]);
+  bool nan = false;
   for (int q = sub * 32 + lane; q < P4 / 4; q += wph * 32) {
     const float4 v = ld4(e + 4 * q);
-    m = gomax(gomax(m, gomax(v.x, v.y)), gomax(v.z, v.w));
+    key = max(key, max(max(fkey(v.x), fkey(v.y)), max(fkey(v.z), fkey(v.w))));
+    nan |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
   }
   if (sub == 0 && P4 + lane < P) {
     e[P4 + lane] = tail;
-    m = gomax(m, tail);
+    key = max(key, fkey(tail));
+    nan |= tail != tail;
   }
-  m = warp_gomax(m);
-  if (lane == 0) red[g * wph + sub] = m;
+  key = __reduce_max_sync(0xffffffffu, key);
+  nan = __any_sync(0xffffffffu, nan);
+  if (lane == 0) reinterpret_cast<uint32_t *>(red)[g * wph + sub] = nan ? 0xffffffffu : key;
   __syncthreads();
-  // 2. exponentials.
-  m = red[g * wph];
-  for (int j = 1; j < wph; j++) m = gomax(m, red[g * wph + j]);
-#pragma unroll 4
-  for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = exp32(__fsub_rn(e[i], m));
+  // 2. exponentials, four independent ones per thread at a time.
+  float m;
+  {
+    uint32_t k = 0;
+    bool anynan = false;
+    for (int j = 0; j < wph; j++) {
+      const uint32_t r = reinterpret_cast<const uint32_t *>(red)[g * wph + j];
+      anynan |= r == 0xffffffffu;
+      k = max(k, r);
+    }
+    m = anynan ? u2f(kCanonNaN) : fkey_value(k);
+  }
+  {
+    const int stride = wph * 32;
+    for (int i0 = sub * 32 + lane; i0 < P; i0 += 4 * stride) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) v[u] = i0 + u * stride < P ? e[i0 + u * stride] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 4; u++) v[u] = exp32(__fsub_rn(v[u], m));
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (i0 + u * stride < P) e[i0 + u * stride] = v[u];
+    }
+  }
   __syncthreads();
   if (warp < gpb) {
     // 3. their sum in position order.
@@ -473,50 +527,25 @@ __global__ void __launch_bounds__(kFsMaxThreads)
       int i = 0;
       const int P32 = P & ~31;
       if (P32 > 0) {
-        float4 cur[8], nxt[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) cur[j] = ld4(e + 4 * j);
+        // Eight float4 registers in rotation: each is added, then refilled
+        // from 32 positions further on, so every load runs about 32 adds
+        // ahead of its use (the row has room past P: ppad >= P32 + 40).
+        float4 r0 = ld4(e), r1 = ld4(e + 4), r2 = ld4(e + 8), r3 = ld4(e + 12);
+        float4 r4 = ld4(e + 16), r5 = ld4(e + 20), r6 = ld4(e + 24), r7 = ld4(e + 28);
+#define RK_FS_STEP(R, K)                 \
+  sum = __fadd_rn(sum, R.x);             \
+  sum = __fadd_rn(sum, R.y);             \
+  sum = __fadd_rn(sum, R.z);             \
+  sum = __fadd_rn(sum, R.w);             \
+  R = ld4(e + i + 32 + 4 * K);
         for (; i < P32; i += 32) {
-          const int nb = i + 32 < P32 ? i + 32 : i;
-#pragma unroll
-          for (int j = 0; j < 8; j++) nxt[j] = ld4(e + nb + 4 * j);
-#pragma unroll
-          for (int j = 0; j < 8; j++) {
-            sum = __fadd_rn(sum, cur[j].x);
-            sum = __fadd_rn(sum, cur[j].y);
-            sum = __fadd_rn(sum, cur[j].z);
-            sum = __fadd_rn(sum, cur[j].w);
-          }
-#pragma unroll
-          for (int j = 0; j < 8; j++) cur[j] = nxt[j];
+          RK_FS_STEP(r0, 0) RK_FS_STEP(r1, 1) RK_FS_STEP(r2, 2) RK_FS_STEP(r3, 3)
+          RK_FS_STEP(r4, 4) RK_FS_STEP(r5, 5) RK_FS_STEP(r6, 6) RK_FS_STEP(r7, 7)
         }
+#undef RK_FS_STEP
       }
       for (; i < P; i++) sum = __fadd_rn(sum, e[i]);
       red[gpb * wph + g] = recip32(sum);
-    }
-  } else {
-    // Meanwhile: the value slice, row t's kFsSlice floats to sV[d][t].
-    const int tid = threadIdx.x - gpb * 32, nld = blockDim.x - gpb * 32;
-    const float *vb = a.vals + kvh * a.hs + slice * kFsSlice;
-    for (int t0 = 0; t0 < P; t0 += nld * kFsRowsPerThread) {
-      float4 r[kFsRowsPerThread][2];
-#pragma unroll
-      for (int u = 0; u < kFsRowsPerThread; u++) {
-        const int t = t0 + u * nld + tid;
-        if (t < P) {
-          r[u][0] = ld4(vb + (long long)t * a.kv_dim);
-          r[u][1] = ld4(vb + (long long)t * a.kv_dim + 4);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kFsRowsPerThread; u++) {
-        const int t = t0 + u * nld + tid;
-        if (t < P) {
-          sV[0 * vpad + t] = r[u][0].x, sV[1 * vpad + t] = r[u][0].y, sV[2 * vpad + t] = r[u][0].z;
-          sV[3 * vpad + t] = r[u][0].w, sV[4 * vpad + t] = r[u][1].x, sV[5 * vpad + t] = r[u][1].y;
-          sV[6 * vpad + t] = r[u][1].z, sV[7 * vpad + t] = r[u][1].w;
-        }
-      }
     }
   }
   __syncthreads();
@@ -524,6 +553,11 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   {
     const float inv = red[gpb * wph + g];
     for (int i = sub * 32 + lane; i < P; i += wph * 32) e[i] = __fmul_rn(e[i], inv);
+  }
+  if (a.v_pitch > 0) {
+    if (!umma::mbar_wait(vbar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
+  } else {
+    cp_async_wait<0>();
   }
   __syncthreads();
   // 5. weighted values: thread (head h, element d).
@@ -568,8 +602,13 @@ __global__ void __launch_bounds__(kFsMaxThreads)
 // Shared memory of k_attn_softmax_wsum for gpb heads of up to maxP
 // positions, or 0 when it does not fit.
 static int fs_smem_bytes(int gpb, int wph, int maxP) {
-  const long long bytes = 4LL * gpb * fs_ppad(maxP) + 4LL * kFsSlice * fs_vpad(maxP) + 8 + 4LL * gpb * (wph + 1);
+  const long long bytes = 4LL * gpb * fs_ppad(maxP) + 4LL * kFsSlice * fs_vpad(maxP) + 16 + 4LL * gpb * (wph + 1);
   return bytes > kFsSmemLimit ? 0 : (int)bytes;
+}
+
+bool attention_fused_ok(int heads, int kv_heads, int hs, int max_positions) {
+  const int gpb = heads / kv_heads;
+  return gpb <= 8 && hs % kFsSlice == 0 && fs_smem_bytes(gpb, fs_wph(gpb), max_positions) > 0;
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
@@ -591,13 +630,13 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     // One kernel for softmax and weighted values when the scores and a value
     // slice of every position fit shared memory and the operands suit
     // 16-byte copies.
-    // The value rows are loaded by the warps beyond the first gpb, so the
-    // kernel needs gpb < total warps (wph >= 2).
     const int gpb = kvMul;
     const int wph = fs_wph(gpb);
-    const int smem = gpb <= 8 && wph >= 2 ? fs_smem_bytes(gpb, wph, maxP) : 0;
+    const int smem = gpb <= 8 ? fs_smem_bytes(gpb, wph, maxP) : 0;
     const bool fused = smem > 0 && a.hs % kFsSlice == 0 && a.kv_dim % 4 == 0 && a.att_stride % 4 == 0 && a.err &&
-                       reinterpret_cast<uintptr_t>(a.vals) % 16 == 0 && reinterpret_cast<uintptr_t>(a.att) % 16 == 0;
+                       a.v_pitch % 4 == 0 && reinterpret_cast<uintptr_t>(a.vals) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(a.att) % 16 == 0;
+    if (!fused && a.v_pitch > 0) return cudaErrorInvalidValue;  // only the fused kernel reads transposed values
     if (fused) {
       dim3 g(a.kv_heads, a.hs / kFsSlice);
       launch_k(k_attn_softmax_wsum, g, gpb * wph * 32, smem, st, a, gpb, wph);
@@ -667,10 +706,10 @@ __global__ void k_qkv_post(const QkvPostArgs a) {
   // 4. The key/value cache append (model.go:567-568).
   if (!isq) {
     float *kc = a.key_cache + (long long)pos * kvDim + head * hs;
-    float *vc = a.val_cache + (long long)pos * kvDim + head * hs;
     for (int i = lane; i < hs; i += 32) {
       kc[i] = v[i];
-      vc[i] = a.v[head * hs + i];
+      if (a.v_pitch > 0) a.val_cache[(long long)(head * hs + i) * a.v_pitch + pos] = a.v[head * hs + i];
+      else a.val_cache[(long long)pos * kvDim + head * hs + i] = a.v[head * hs + i];
     }
   }
 }

@@ -29,7 +29,12 @@ cudaError_t launch_silumul(float *a, const float *b, int n, cudaStream_t st);
 // captured CUDA graph serves every position; max_positions bounds the grid.
 struct AttnArgs {
   const float *q;
-  const float *keys, *vals;  // [ctx][kvDim]
+  const float *keys;  // [ctx][kvDim]
+  // Values: [ctx][kvDim] when v_pitch == 0; otherwise stored transposed,
+  // element i of position t at vals[i·v_pitch + t] (the stage's layout:
+  // each value element's positions are contiguous).
+  const float *vals;
+  int v_pitch;
   float *att;                // [heads][att_stride]
   float *out;                // [heads·hs]
   int positions, max_positions;
@@ -40,6 +45,10 @@ struct AttnArgs {
   int *err;  // device error word for a pipeline wait that timed out
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+// Whether launch_attention serves heads/kv_heads/hs over up to max_positions
+// positions with its single softmax + value kernel, the only one that reads
+// transposed values (AttnArgs.v_pitch > 0).
+bool attention_fused_ok(int heads, int kv_heads, int hs, int max_positions);
 // Raises the attention kernels' shared-memory limit; once per device.
 cudaError_t init_layer_attributes();
 
@@ -51,7 +60,8 @@ struct QkvPostArgs {
   const float *bq, *bk, *bv;      // null without QKVBias
   const float *q_norm, *k_norm;   // null without QKNorm
   const float *cos_, *sin_;       // [ctx][hs/2]
-  float *key_cache, *val_cache;   // [ctx][kvDim]
+  float *key_cache, *val_cache;   // [ctx][kvDim]; values transposed when v_pitch > 0 (as AttnArgs)
+  int v_pitch;
   const int *pos_dev;
   int heads, kv_heads, hs;
   float eps, recip_hs;
