@@ -50,6 +50,12 @@ def parse():
     p.add_argument("--dtype", default="q8_0")
     p.add_argument("--ctx", type=int, default=CTX)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layers", type=int, default=0,
+                   help="profiling aid: build the model with this many layers instead of the config's")
+    p.add_argument("--tensor-shape", default=None,
+                   help="--kernel tensor: one MxKxN shape instead of config 2's sweep")
+    p.add_argument("--tensor-dtype", default="both", choices=["both", "i8", "f32"])
+    p.add_argument("--tensor-op", default="both", choices=["both", "matmul", "matmul_t"])
     p.add_argument("--kernel", default=None, choices=["matvec", "tensor"],
                    help="time one kernel alone instead of the decode step (profiling aid)")
     p.add_argument("--shape", default="28672x4096", help="rows x cols for --kernel matvec")
@@ -89,10 +95,16 @@ def run_tensor(args):
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except (OSError, ValueError):
         pass
+    shapes = [(m, 4096, 4096) for m in (1, 16, 128, 512)]
+    if args.tensor_shape:
+        shapes = [tuple(int(v) for v in args.tensor_shape.split("x"))]
     for dtype, name in ((rk.TENSOR_I8, "i8"), (rk.TENSOR_F32, "f32")):
+        if args.tensor_dtype not in ("both", name):
+            continue
         for transposed in (True, False):
-            for m in (1, 16, 128, 512):
-                n = k = 4096
+            if args.tensor_op not in ("both", "matmul_t" if transposed else "matmul"):
+                continue
+            for m, k, n in shapes:
                 rk.bench_tensor(dev, dtype, transposed, m, k, n, max(1, args.warmup))
                 ms = rk.bench_tensor(dev, dtype, transposed, m, k, n, args.steps)
                 es = 1 if dtype == rk.TENSOR_I8 else 4
@@ -110,7 +122,8 @@ def workload(args):
             else args.model,
             "weights": "random N(0,0.02), seeded, quantized by the reference's quantize8 (group 32)",
             "batch": 1, "context": args.ctx,
-            "l2": "inputs larger than L2 (8.4 GB of weights + 1.07 GB of KV cache read per step)"}
+            "l2": "inputs larger than L2 (8.4 GB of weights + 1.07 GB of KV cache read per step)",
+            **({"layers": f"{args.layers} (profiling run, not the headline)"} if args.layers > 0 else {})}
 
 
 class Clocks:
@@ -169,14 +182,15 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def traffic_per_launch():
-    """DRAM bytes per Q8_0 matvec launch from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "matvec_q8_llama3-8b.txt")
+def traffic_ratio():
+    """DRAM bytes per algorithmic byte of a Q8_0 matvec launch, from the
+    committed ncu summary (one launch of the 28672x4096 W1/W3 shape)."""
+    path = os.path.join(ROOT, "profiles", "matvec_q8_28672x4096.txt")
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith("dram_bytes_per_algorithmic_byte:"):
                 return float(line.split(":")[1])
-    except OSError:
+    except (OSError, ValueError):
         pass
     return None
 
@@ -247,7 +261,8 @@ def main():
     import synth
 
     dev = rk.Device(local)
-    c = synth.config(args.model, args.dtype, seq_len=args.ctx + 64)
+    over = {"layers": args.layers} if args.layers > 0 else {}
+    c = synth.config(args.model, args.dtype, seq_len=args.ctx + 64, **over)
     dm = synth.DeviceModel(dev, c, SEED, ctx=args.ctx + 64)
     dm.stage.fill_cache(args.ctx, SEED)
     pos, tok = args.ctx, 1
@@ -296,7 +311,11 @@ def main():
         v, cores, sample = cpu_sample(args)
         baseline = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
 
-    traffic = traffic_per_launch()
+    # DRAM bytes of the average matvec launch of a step: the captured
+    # launch's traffic per algorithmic byte times the step's average
+    # algorithmic bytes per launch (traffic scales with the rows read).
+    ratio = traffic_ratio()
+    traffic = ratio * prof.matvec_bytes / prof.matvec_launches if ratio and prof.matvec_launches else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,

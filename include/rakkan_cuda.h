@@ -72,6 +72,7 @@ typedef struct rk_layer rk_layer;
 typedef struct rk_stage rk_stage;
 typedef struct rk_head rk_head;
 typedef struct rk_model rk_model;
+typedef struct rk_group rk_group;
 
 /* gpu.Info (device.go:21-47). */
 typedef struct {
@@ -229,6 +230,45 @@ int rk_model_step(rk_model *m, int token, int pos, float *logits, int *next);
  * prompt token ((n_prompt - 1 + n_new) × vocab floats). */
 int rk_model_generate(rk_model *m, const int *prompt, int n_prompt, int n_new, int *out_tokens, float *out_logits);
 
+/* ---- Row sharding over the GPUs of one box (one process per GPU) ----
+ * No counterpart in the reference: it splits a model by layers across
+ * nodes (plan.go:158-207) and runs each stage on one device. Here a stage's
+ * weight rows are split over G GPUs, which is bit-identical because every
+ * output row is still computed from the whole input in the reference's
+ * order (the goroutine split of matvec.go:384-400 relies on the same fact).
+ * Shard r of G holds, per layer, query heads [r·heads/G, …) and kv heads
+ * [r·kvHeads/G, …) of Wq/Wk/Wv (rows of whole heads, so RoPE, the KV cache
+ * and attention stay local), rows [r·dim/G, …) of Wo and W2, rows
+ * [r·hidden/G, …) of W1 and W3, and rows [r·vocab/G, …) of the classifier;
+ * after attention, Wo, W1/W3 and W2 the outputs are reassembled with an
+ * NCCL all-gather over NVLink, captured in the step's CUDA graph. kvHeads,
+ * dim, hidden and vocab must be multiples of G. NCCL (libnccl.so.2) is
+ * loaded at run time by the first group call. */
+#define RK_GROUP_ID_BYTES 128
+/* A fresh group id (on one rank; the caller passes it to every rank). */
+int rk_group_id(unsigned char id[RK_GROUP_ID_BYTES]);
+/* Joins rank `rank` of `nranks` on device d (collective: every rank calls it). */
+int rk_group_new(rk_device *d, int nranks, int rank, const unsigned char id[RK_GROUP_ID_BYTES], rk_group **out);
+void rk_group_free(rk_group *g);
+int rk_group_size(const rk_group *g, int *rank, int *nranks);
+/* In place on the device: rank r's count floats at buf_dev + r·count reach
+ * every rank's buf_dev (collective; synchronous). */
+int rk_group_all_gather(rk_group *g, float *buf_dev, int64_t count);
+/* Shard `shard` of `nshards` of a layer: l's matrices hold that shard's rows
+ * (above); the vectors are whole. */
+int rk_layer_upload_shard(rk_device *d, const rk_config *c, int nshards, int shard, const rk_host_layer *l,
+                          rk_layer **out);
+int rk_layer_from_device_shard(rk_device *d, const rk_config *c, int nshards, int shard, const rk_host_layer *vectors,
+                               rk_matrix *wq, rk_matrix *wk, rk_matrix *wv, rk_matrix *wo, rk_matrix *w1,
+                               rk_matrix *w2, rk_matrix *w3, rk_layer **out);
+/* A stage over shard layers (shard = the group's rank); its forward, and a
+ * model built on it, run collectively on every rank. */
+int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *g,
+                       rk_stage **out);
+/* A head whose classifier holds the rank's vocab/G rows; logits are whole. */
+int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *g,
+                      rk_head **out);
+
 /* ---- rakkan_tensor_v1 matmul / matmul_t (tensor.go:286-339) ----
  * C[m×n] = A[m×k]·B with B [k×n] (transposed 0, "matmul") or [n×k]
  * (transposed 1, "matmul_t"), row-major host buffers. dtype RK_TENSOR_F32
@@ -247,6 +287,9 @@ int rk_tensor_matmul_device(rk_device *d, int dtype, int transposed, int m, int 
  * quantizes them on the device to fmt and keeps them as a matrix. */
 int rk_matrix_generate(rk_device *d, int rows, int cols, int fmt, uint64_t seed, uint64_t tid, float scale,
                        rk_matrix **out);
+/* Rows [row0, row0 + rows) of that rows_total × cols tensor (a row shard). */
+int rk_matrix_generate_rows(rk_device *d, int rows_total, int row0, int rows, int cols, int fmt, uint64_t seed,
+                            uint64_t tid, float scale, rk_matrix **out);
 /* Copies a matrix back to host buffers (w as in rk_matrix_upload; scales may be NULL). */
 int rk_matrix_download(rk_matrix *m, void *w, float *scales);
 /* Fills host floats with the generator's values (computed on the device). */

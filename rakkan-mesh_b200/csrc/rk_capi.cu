@@ -10,6 +10,9 @@
 // entry point is synchronous at the boundary and returns a status; errors
 // latch per batch like gpu.Batch (batch.go:136-147). There is no host
 // fallback: a failing CUDA call is an error.
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
@@ -215,6 +218,113 @@ extern "C" void rk_device_close(rk_device *d) {
 }
 
 extern "C" int64_t rk_device_used(rk_device *d) { return d ? d->used : 0; }
+
+// ---------------------------------------------------------------------------
+// Groups: one NCCL communicator per process (one process per GPU), for the
+// row-sharded stage and head. NCCL is loaded when the first group is made,
+// so the library itself does not depend on it; a process that already has
+// NCCL loaded (e.g. through torch) shares that copy.
+// ---------------------------------------------------------------------------
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char *(*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+static const NcclApi &nccl() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return a;
+    a.get_unique_id = (decltype(a.get_unique_id))dlsym(h, "ncclGetUniqueId");
+    a.comm_init_rank = (decltype(a.comm_init_rank))dlsym(h, "ncclCommInitRank");
+    a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
+    a.all_gather = (decltype(a.all_gather))dlsym(h, "ncclAllGather");
+    a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
+    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather && a.error_string;
+    return a;
+  }();
+  return api;
+}
+
+static int nccl_fail(ncclResult_t r, const char *what) {
+  return fail(RK_ERR_CUDA, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "nccl");
+}
+
+struct rk_group {
+  rk_device *d = nullptr;
+  ncclComm_t comm = nullptr;
+  int rank = 0, n = 1;
+};
+
+extern "C" int rk_group_id(unsigned char id[RK_GROUP_ID_BYTES]) {
+  if (!id) return fail(RK_ERR_ARGS, "null argument");
+  if (!nccl().ok) return fail(RK_ERR_STATE, "NCCL (libnccl.so.2) is not available");
+  static_assert(sizeof(ncclUniqueId) == RK_GROUP_ID_BYTES, "group id size");
+  ncclUniqueId u;
+  ncclResult_t r = nccl().get_unique_id(&u);
+  if (r != ncclSuccess) return nccl_fail(r, "group id");
+  memcpy(id, &u, sizeof u);
+  return RK_OK;
+}
+
+extern "C" int rk_group_new(rk_device *d, int nranks, int rank, const unsigned char id[RK_GROUP_ID_BYTES],
+                            rk_group **out) {
+  if (!d || !id || !out || nranks < 1 || rank < 0 || rank >= nranks) return fail(RK_ERR_ARGS, "bad argument");
+  if (!nccl().ok) return fail(RK_ERR_STATE, "NCCL (libnccl.so.2) is not available");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  auto *gr = new rk_group();
+  gr->d = d;
+  gr->rank = rank;
+  gr->n = nranks;
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof u);
+  ncclResult_t r = nccl().comm_init_rank(&gr->comm, nranks, u, rank);
+  if (r != ncclSuccess) {
+    delete gr;
+    return nccl_fail(r, "group init");
+  }
+  *out = gr;
+  return RK_OK;
+}
+
+extern "C" void rk_group_free(rk_group *g) {
+  if (!g) return;
+  cudaSetDevice(g->d->ordinal);
+  cudaStreamSynchronize(g->d->st);
+  if (g->comm) nccl().comm_destroy(g->comm);
+  delete g;
+}
+
+extern "C" int rk_group_size(const rk_group *g, int *rank, int *nranks) {
+  if (!g) return fail(RK_ERR_ARGS, "null group");
+  if (rank) *rank = g->rank;
+  if (nranks) *nranks = g->n;
+  return RK_OK;
+}
+
+// In place: rank r's count floats at buf + r·count go to every rank's buf.
+static int group_gather(rk_group *g, float *buf, size_t count, cudaStream_t st) {
+  ncclResult_t r = nccl().all_gather(buf + (size_t)g->rank * count, buf, count, ncclFloat32, g->comm, st);
+  if (r != ncclSuccess) return nccl_fail(r, "all-gather");
+  return RK_OK;
+}
+
+extern "C" int rk_group_all_gather(rk_group *g, float *buf_dev, int64_t count) {
+  if (!g || !buf_dev || count < 0) return fail(RK_ERR_ARGS, "bad argument");
+  rk_device *d = g->d;
+  Guard gd(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  if ((rc = group_gather(g, buf_dev, (size_t)count, d->st))) return rc;
+  return sync_dev(d);
+}
 
 // ---------------------------------------------------------------------------
 // Matrices
@@ -856,6 +966,7 @@ extern "C" int rk_config_validate(const rk_config *c) {
 struct rk_layer {
   rk_device *d = nullptr;
   rk_config c{};
+  int nshards = 1, shard = 0;  // row shard `shard` of `nshards` (see layer_dims)
   rk_matrix *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr, *w3 = nullptr;
   rk_vectors *vecs = nullptr;
   // Offsets in vecs (vecLayout, model.go:298-314); -1 when absent.
@@ -905,24 +1016,43 @@ static int mat_fmt(const rk_config *c, bool sensitive) {
   }
 }
 
-extern "C" int rk_layer_upload(rk_device *d, const rk_config *c, const rk_host_layer *h, rk_layer **out) {
-  if (!d || !c || !h || !out) return fail(RK_ERR_ARGS, "null argument");
+// Row sharding over G GPUs (by whole kv heads, so attention stays local):
+// shard r holds query heads [r·heads/G, …) and kv heads [r·kvHeads/G, …) of
+// Wq / Wk / Wv, rows [r·D/G, …) of Wo and W2, and rows [r·H/G, …) of W1
+// and W3; the inputs of every product stay whole. dims[i] = {rows, cols} of
+// wq, wk, wv, wo, w1, w2, w3 in that order.
+static int layer_dims(const rk_config *c, int G, int dims[7][2]) {
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  if (G < 1 || c->kv_heads % G || D % G || H % G)
+    return fail(RK_ERR_ARGS, "cannot shard kv heads %d, dim %d, hidden %d over %d", c->kv_heads, D, H, G);
+  const int r[7][2] = {{qd / G, D}, {kvd / G, D}, {kvd / G, D}, {D / G, qd}, {H / G, D}, {D / G, H}, {H / G, D}};
+  memcpy(dims, r, sizeof r);
+  return RK_OK;
+}
+
+static int layer_upload(rk_device *d, const rk_config *c, int nshards, int shard, const rk_host_layer *h,
+                        rk_layer **out) {
+  if (!d || !c || !h || !out || shard < 0 || shard >= nshards) return fail(RK_ERR_ARGS, "bad argument");
   int rc = rk_config_validate(c);
   if (rc) return rc;
+  int dims[7][2];
+  if ((rc = layer_dims(c, nshards, dims))) return rc;
   Guard g(d);
   if ((rc = set_device(d))) return rc;
-  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
   auto *l = new rk_layer();
   l->d = d;
   l->c = *c;
+  l->nshards = nshards;
+  l->shard = shard;
   struct Spec {
     rk_matrix **dst;
     const rk_host_matrix *src;
     int rows, cols;
     bool sensitive;
-  } specs[7] = {{&l->wq, &h->wq, qd, D, false},  {&l->wk, &h->wk, kvd, D, false}, {&l->wv, &h->wv, kvd, D, true},
-                {&l->wo, &h->wo, D, qd, false},  {&l->w1, &h->w1, H, D, false},   {&l->w2, &h->w2, D, H, true},
-                {&l->w3, &h->w3, H, D, false}};
+  } specs[7] = {{&l->wq, &h->wq, dims[0][0], dims[0][1], false}, {&l->wk, &h->wk, dims[1][0], dims[1][1], false},
+                {&l->wv, &h->wv, dims[2][0], dims[2][1], true},  {&l->wo, &h->wo, dims[3][0], dims[3][1], false},
+                {&l->w1, &h->w1, dims[4][0], dims[4][1], false}, {&l->w2, &h->w2, dims[5][0], dims[5][1], true},
+                {&l->w3, &h->w3, dims[6][0], dims[6][1], false}};
   for (auto &s : specs) {
     if (s.src->fmt != mat_fmt(c, s.sensitive)) {
       layer_release(l);
@@ -949,19 +1079,31 @@ extern "C" int rk_layer_upload(rk_device *d, const rk_config *c, const rk_host_l
   return RK_OK;
 }
 
-extern "C" int rk_layer_from_device(rk_device *d, const rk_config *c, const rk_host_layer *vectors, rk_matrix *wq,
-                                    rk_matrix *wk, rk_matrix *wv, rk_matrix *wo, rk_matrix *w1, rk_matrix *w2,
-                                    rk_matrix *w3, rk_layer **out) {
-  if (!d || !c || !vectors || !out) return fail(RK_ERR_ARGS, "null argument");
+extern "C" int rk_layer_upload(rk_device *d, const rk_config *c, const rk_host_layer *h, rk_layer **out) {
+  return layer_upload(d, c, 1, 0, h, out);
+}
+
+extern "C" int rk_layer_upload_shard(rk_device *d, const rk_config *c, int nshards, int shard, const rk_host_layer *h,
+                                     rk_layer **out) {
+  return layer_upload(d, c, nshards, shard, h, out);
+}
+
+static int layer_from_device(rk_device *d, const rk_config *c, int nshards, int shard, const rk_host_layer *vectors,
+                             rk_matrix *wq, rk_matrix *wk, rk_matrix *wv, rk_matrix *wo, rk_matrix *w1, rk_matrix *w2,
+                             rk_matrix *w3, rk_layer **out) {
+  if (!d || !c || !vectors || !out || shard < 0 || shard >= nshards) return fail(RK_ERR_ARGS, "bad argument");
   int rc = rk_config_validate(c);
   if (rc) return rc;
-  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  int dims[7][2];
+  if ((rc = layer_dims(c, nshards, dims))) return rc;
   struct Spec {
     rk_matrix *m;
     int rows, cols;
     bool sensitive;
-  } specs[7] = {{wq, qd, D, false}, {wk, kvd, D, false}, {wv, kvd, D, true}, {wo, D, qd, false},
-                {w1, H, D, false},  {w2, D, H, true},    {w3, H, D, false}};
+  } specs[7] = {{wq, dims[0][0], dims[0][1], false}, {wk, dims[1][0], dims[1][1], false},
+                {wv, dims[2][0], dims[2][1], true},  {wo, dims[3][0], dims[3][1], false},
+                {w1, dims[4][0], dims[4][1], false}, {w2, dims[5][0], dims[5][1], true},
+                {w3, dims[6][0], dims[6][1], false}};
   for (auto &s : specs)
     if (!s.m || s.m->d != d || s.m->rows != s.rows || s.m->cols != s.cols || s.m->fmt != mat_fmt(c, s.sensitive))
       return fail(RK_ERR_ARGS, "layer matrix of the wrong shape, format or device");
@@ -970,6 +1112,8 @@ extern "C" int rk_layer_from_device(rk_device *d, const rk_config *c, const rk_h
   auto *l = new rk_layer();
   l->d = d;
   l->c = *c;
+  l->nshards = nshards;
+  l->shard = shard;
   if ((rc = layer_vectors(d, c, vectors, l))) {
     delete l;
     return rc;
@@ -983,6 +1127,19 @@ extern "C" int rk_layer_from_device(rk_device *d, const rk_config *c, const rk_h
   l->w3 = w3;
   *out = l;
   return RK_OK;
+}
+
+extern "C" int rk_layer_from_device(rk_device *d, const rk_config *c, const rk_host_layer *vectors, rk_matrix *wq,
+                                    rk_matrix *wk, rk_matrix *wv, rk_matrix *wo, rk_matrix *w1, rk_matrix *w2,
+                                    rk_matrix *w3, rk_layer **out) {
+  return layer_from_device(d, c, 1, 0, vectors, wq, wk, wv, wo, w1, w2, w3, out);
+}
+
+extern "C" int rk_layer_from_device_shard(rk_device *d, const rk_config *c, int nshards, int shard,
+                                          const rk_host_layer *vectors, rk_matrix *wq, rk_matrix *wk, rk_matrix *wv,
+                                          rk_matrix *wo, rk_matrix *w1, rk_matrix *w2, rk_matrix *w3,
+                                          rk_layer **out) {
+  return layer_from_device(d, c, nshards, shard, vectors, wq, wk, wv, wo, w1, w2, w3, out);
 }
 
 extern "C" void rk_layer_free(rk_layer *l) {
@@ -1014,6 +1171,9 @@ struct rk_stage {
   int64_t bytes = 0;
   cudaGraphExec_t graph = nullptr;
   int io_tokens = 64;  // gpuBatch, gpustage.go:17
+  // Row sharding (layer_dims): this process's rank of G; null/1 unsharded.
+  rk_group *grp = nullptr;
+  int G = 1, rank = 0;
 };
 
 static int stage_alloc(rk_stage *s, size_t bytes, void **p) {
@@ -1069,7 +1229,12 @@ static float host_recip32(float x) {
 static int record_layers(rk_stage *s, cudaStream_t st) {
   rk_device *d = s->d;
   const rk_config *c = &s->c;
-  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  const int hs = head_size(c), qd = c->heads * hs, D = c->dim, H = c->hidden;
+  // This rank's part (everything when unsharded): query heads h0.., kv
+  // heads kv0.., rows r0.. of Wo/W2 (of D) and rH0.. of W1/W3 (of H).
+  const int G = s->G, heads_l = c->heads / G, kvh_l = c->kv_heads / G;
+  const int h0 = s->rank * heads_l, kv0 = s->rank * kvh_l, r0 = s->rank * (D / G), rH0 = s->rank * (H / G);
+  auto gather = [&](float *buf, int total) -> int { return G > 1 ? group_gather(s->grp, buf, total / G, st) : RK_OK; };
   const float eps = cfg_eps(c);
   const float recipD = host_recip32((float)D), recipHS = host_recip32((float)hs);
   const float invSqrt = (float)(1 / sqrt((double)hs));
@@ -1117,9 +1282,9 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     qp.k = s->k;
     qp.v = s->v;
     if (c->qkv_bias) {
-      qp.bq = vec + l->o_bq;
-      qp.bk = vec + l->o_bk;
-      qp.bv = vec + l->o_bv;
+      qp.bq = vec + l->o_bq + h0 * hs;
+      qp.bk = vec + l->o_bk + kv0 * hs;
+      qp.bv = vec + l->o_bv + kv0 * hs;
     }
     if (c->qk_norm) {
       qp.q_norm = vec + l->o_qn;
@@ -1131,8 +1296,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     qp.val_cache = s->vals[li];
     qp.v_pitch = s->v_pitch;
     qp.pos_dev = s->pos_dev;
-    qp.heads = c->heads;
-    qp.kv_heads = c->kv_heads;
+    qp.heads = heads_l;
+    qp.kv_heads = kvh_l;
     qp.hs = hs;
     qp.eps = eps;
     qp.recip_hs = recipHS;
@@ -1144,20 +1309,25 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.vals = s->vals[li];
     at.v_pitch = s->v_pitch;
     at.att = s->att;
-    at.out = s->att_out;
+    at.out = s->att_out + h0 * hs;
     at.positions_dev = s->pos_dev;
     at.positions_add = 1;
     at.max_positions = s->ctx;
-    at.heads = c->heads;
-    at.kv_heads = c->kv_heads;
+    at.heads = heads_l;
+    at.kv_heads = kvh_l;
     at.hs = hs;
-    at.kv_dim = kvd;
+    at.kv_dim = kvh_l * hs;
     at.att_stride = s->att_stride;
     at.inv_sqrt = invSqrt;
     at.err = s->d->err_dev;
     CK(launch_attention(at, st));
+    if ((rc = gather(s->att_out, qd))) return rc;
     // x += Wo·attOut (model.go:588-594).
-    if ((rc = products(1, &l->wo, &s->x, s->att_out, nullptr, qd, EPI_ADD))) return rc;
+    {
+      float *xo = s->x + r0;
+      if ((rc = products(1, &l->wo, &xo, s->att_out, nullptr, qd, EPI_ADD))) return rc;
+    }
+    if ((rc = gather(s->x, D))) return rc;
     // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603):
     // row i of W1 and of W3 in one warp, SiLU·mul as the epilogue.
     {
@@ -1166,8 +1336,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
       a.cols = D;
       a.epi = EPI_SILU;
       a.err = d->err_dev;
-      a.part[0] = part_of(l->w1, s->hb);
-      a.part[1] = part_of(l->w3, s->hb2);
+      a.part[0] = part_of(l->w1, s->hb + rH0);
+      a.part[1] = part_of(l->w3, s->hb2 + rH0);
       a.nparts = 2;
       const float *norm_w = vec + l->o_rms_ffn;
       if (quantized_fmt(a.fmt) && matvec_fused_ok(a.fmt, D)) {
@@ -1187,8 +1357,13 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
       }
       CK(launch_mv(d, a, st));
     }
+    if ((rc = gather(s->hb, H))) return rc;
     // x = Canonical(x + W2·hb) (model.go:604-610).
-    if ((rc = products(1, &l->w2, &s->x, s->hb, nullptr, H, EPI_ADD_CANON))) return rc;
+    {
+      float *xo = s->x + r0;
+      if ((rc = products(1, &l->w2, &xo, s->hb, nullptr, H, EPI_ADD_CANON))) return rc;
+    }
+    if ((rc = gather(s->x, D))) return rc;
   }
   return RK_OK;
 }
@@ -1210,34 +1385,46 @@ __global__ void k_advance(int *tok, int *pos) {
   if (pos) *pos += 1;
 }
 
+// Records rec's launches into a graph; *nodes receives the number of this
+// library's kernels in it (collectives are not counted).
 static int capture(rk_device *d, std::function<int(cudaStream_t)> rec, cudaGraphExec_t *out, size_t *nodes = nullptr) {
   cudaGraph_t graph = nullptr;
   CK(cudaStreamBeginCapture(d->st, cudaStreamCaptureModeThreadLocal));
   // Kernels of a captured step use programmatic dependent launch: each may
   // start (and stream its weights) while its predecessor finishes.
   g_pdl = true;
+  const long long k0 = g_kernel_launches;
   int rc = rec(d->st);
   g_pdl = false;
+  if (nodes) *nodes = (size_t)(g_kernel_launches - k0);
   cudaError_t e = cudaStreamEndCapture(d->st, &graph);
   if (rc) {
     if (graph) cudaGraphDestroy(graph);
     return rc;
   }
   if (e != cudaSuccess) return cuda_fail(e, "graph capture");
-  if (nodes) cudaGraphGetNodes(graph, nullptr, nodes);
   e = cudaGraphInstantiate(out, graph, 0);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
   return RK_OK;
 }
 
-extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_stage **out) {
+static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *grp,
+                     rk_stage **out) {
   if (!d || !c || !out || n < 0 || (n > 0 && !layers) || ctx <= 0) return fail(RK_ERR_ARGS, "bad argument");
   int rc = rk_config_validate(c);
   if (rc) return rc;
   ctx = std::min(ctx, c->seq_len);
-  for (int i = 0; i < n; i++)
+  const int G = grp ? grp->n : 1, rank = grp ? grp->rank : 0;
+  if (grp && grp->d != d) return fail(RK_ERR_ARGS, "group on another device");
+  int dims[7][2];
+  if ((rc = layer_dims(c, G, dims))) return rc;
+  for (int i = 0; i < n; i++) {
     if (!layers[i] || layers[i]->d != d) return fail(RK_ERR_ARGS, "layer %d not on this device", i);
+    if (layers[i]->nshards != G || layers[i]->shard != rank)
+      return fail(RK_ERR_ARGS, "layer %d is shard %d of %d, the stage is rank %d of %d", i, layers[i]->shard,
+                  layers[i]->nshards, rank, G);
+  }
   Guard g(d);
   if ((rc = set_device(d))) return rc;
   auto *s = new rk_stage();
@@ -1245,7 +1432,10 @@ extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *l
   s->c = *c;
   s->layers.assign(layers, layers + n);
   s->ctx = ctx;
-  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  s->grp = grp;
+  s->G = G;
+  s->rank = rank;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs / G, D = c->dim, H = c->hidden;
   const int widest = std::max(D, std::max(qd, H));
   void *p;
   auto A = [&](size_t bytes, void **dst) { return stage_alloc(s, bytes, dst); };
@@ -1256,15 +1446,15 @@ extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *l
   } while (0)
   ALLOC(x, 4 * (size_t)D);
   ALLOC(xb, 4 * (size_t)D);
-  ALLOC(q, 4 * (size_t)qd);
+  ALLOC(q, 4 * (size_t)(qd / G));
   ALLOC(k, 4 * (size_t)kvd);
   ALLOC(v, 4 * (size_t)kvd);
   ALLOC(att_out, 4 * (size_t)qd);
   ALLOC(hb, 4 * (size_t)H);
   ALLOC(hb2, 4 * (size_t)H);
   s->att_stride = (ctx + 3) & ~3;
-  s->v_pitch = attention_fused_ok(c->heads, c->kv_heads, hs, ctx) ? s->att_stride : 0;
-  ALLOC(att, 4 * (size_t)c->heads * s->att_stride);
+  s->v_pitch = attention_fused_ok(c->heads / G, c->kv_heads / G, hs, ctx) ? s->att_stride : 0;
+  ALLOC(att, 4 * (size_t)(c->heads / G) * s->att_stride);
   ALLOC(qx, (size_t)widest);
   ALLOC(xs, 4 * (size_t)(widest / 32 + 1));
   ALLOC(xsum, 4 * (size_t)(widest / 32 + 1));
@@ -1319,6 +1509,16 @@ fail_:
   return rc;
 }
 
+extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_stage **out) {
+  return stage_new(d, c, layers, n, ctx, nullptr, out);
+}
+
+extern "C" int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx,
+                                  rk_group *g, rk_stage **out) {
+  if (!g) return fail(RK_ERR_ARGS, "null group");
+  return stage_new(d, c, layers, n, ctx, g, out);
+}
+
 extern "C" void rk_stage_free(rk_stage *s) {
   if (!s) return;
   rk_device *d = s->d;
@@ -1363,6 +1563,7 @@ struct rk_head {
   int *xsum = nullptr;
   float *pin = nullptr;
   int64_t bytes = 0;
+  rk_group *grp = nullptr;  // sharded: wcls holds rows [rank·V/G, …) and the logits are gathered
 };
 
 static void head_release(rk_head *h) {
@@ -1377,17 +1578,23 @@ static void head_release(rk_head *h) {
   delete h;
 }
 
-extern "C" int rk_head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_head **out) {
+static int head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *grp,
+                    rk_head **out) {
   if (!d || !c || !rms_final || !wcls || !out) return fail(RK_ERR_ARGS, "null argument");
   int rc = rk_config_validate(c);
   if (rc) return rc;
-  if (wcls->d != d || wcls->rows != c->vocab || wcls->cols != c->dim) return fail(RK_ERR_ARGS, "classifier of the wrong shape");
+  const int G = grp ? grp->n : 1;
+  if (c->vocab % G) return fail(RK_ERR_ARGS, "cannot shard vocabulary %d over %d", c->vocab, G);
+  if (wcls->d != d || wcls->rows != c->vocab / G || wcls->cols != c->dim)
+    return fail(RK_ERR_ARGS, "classifier of the wrong shape");
+  if (grp && grp->d != d) return fail(RK_ERR_ARGS, "group on another device");
   Guard g(d);
   if ((rc = set_device(d))) return rc;
   auto *h = new rk_head();
   h->d = d;
   h->c = *c;
   h->wcls = wcls;
+  h->grp = grp;
   const size_t D = (size_t)c->dim, V = (size_t)c->vocab;
   cudaError_t e = cudaMalloc(&h->rms, 4 * D);
   if (e == cudaSuccess) e = cudaMalloc(&h->x, 4 * D);
@@ -1406,6 +1613,16 @@ extern "C" int rk_head_new(rk_device *d, const rk_config *c, const float *rms_fi
   d->used += h->bytes;
   *out = h;
   return RK_OK;
+}
+
+extern "C" int rk_head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_head **out) {
+  return head_new(d, c, rms_final, wcls, nullptr, out);
+}
+
+extern "C" int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls,
+                                 rk_group *g, rk_head **out) {
+  if (!g) return fail(RK_ERR_ARGS, "null group");
+  return head_new(d, c, rms_final, wcls, g, out);
 }
 
 extern "C" void rk_head_free(rk_head *h) {
@@ -1446,9 +1663,11 @@ static int record_head(rk_head *h, const float *x, cudaStream_t st) {
     CK(launch_rmsnorm(x, h->xb, h->rms, D, 1, 0, recipD, eps, st));
     a.x = h->xb;
   }
-  a.part[0] = part_of(h->wcls, h->logits);
+  const int G = h->grp ? h->grp->n : 1;
+  a.part[0] = part_of(h->wcls, h->logits + (size_t)(h->grp ? h->grp->rank : 0) * (h->c.vocab / G));
   a.nparts = 1;
   CK(launch_mv(h->d, a, st));
+  if (G > 1) return group_gather(h->grp, h->logits, (size_t)(h->c.vocab / G), st);
   return RK_OK;
 }
 
@@ -1687,8 +1906,23 @@ extern "C" int rk_tensor_matmul(rk_device *d, int dtype, int transposed, int m, 
 // ---------------------------------------------------------------------------
 // Device-side import and the seeded generator
 // ---------------------------------------------------------------------------
+static int matrix_generate(rk_device *d, long long first, int rows, int cols, int fmt, uint64_t seed, uint64_t tid,
+                           float scale, rk_matrix **out);
+
 extern "C" int rk_matrix_generate(rk_device *d, int rows, int cols, int fmt, uint64_t seed, uint64_t tid, float scale,
                                   rk_matrix **out) {
+  return matrix_generate(d, 0, rows, cols, fmt, seed, tid, scale, out);
+}
+
+extern "C" int rk_matrix_generate_rows(rk_device *d, int rows_total, int row0, int rows, int cols, int fmt,
+                                       uint64_t seed, uint64_t tid, float scale, rk_matrix **out) {
+  if (row0 < 0 || rows < 0 || row0 + rows > rows_total) return fail(RK_ERR_ARGS, "rows out of range");
+  return matrix_generate(d, (long long)row0 * cols, rows, cols, fmt, seed, tid, scale, out);
+}
+
+// Elements [first, first + rows·cols) of the tensor's stream as a matrix.
+static int matrix_generate(rk_device *d, long long first, int rows, int cols, int fmt, uint64_t seed, uint64_t tid,
+                           float scale, rk_matrix **out) {
   if (!d || !out) return fail(RK_ERR_ARGS, "null argument");
   Guard g(d);
   int rc = set_device(d);
@@ -1704,7 +1938,7 @@ extern "C" int rk_matrix_generate(rk_device *d, int rows, int cols, int fmt, uin
   if (e == cudaSuccess && fmt == RK_FMT_Q4_0) e = cudaMalloc(&stale, (size_t)(slice / 32 + 1));
   for (long long off = 0; e == cudaSuccess && off < n; off += slice) {
     const long long cnt = std::min(slice, n - off);
-    e = launch_gen_normal(seed, tid, off, cnt, scale, tmp, d->st);
+    e = launch_gen_normal(seed, tid, first + off, cnt, scale, tmp, d->st);
     if (e != cudaSuccess) break;
     switch (fmt) {
       case RK_FMT_F32: e = cudaMemcpyAsync(m->w + 4 * off, tmp, 4 * (size_t)cnt, cudaMemcpyDeviceToDevice, d->st); break;
@@ -1955,14 +2189,16 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
   Guard g(d);
   int rc = set_device(d);
   if (rc) return rc;
-  const int kvd = s->c.kv_heads * head_size(&s->c);
-  const long long n = (long long)positions * kvd;
+  // Position t's cache row is elements [t·kvd, …) of the layer's stream;
+  // this rank holds columns [c0, c0 + kvd_l) (its kv heads).
+  const int kvd = s->c.kv_heads * head_size(&s->c), kvd_l = kvd / s->G, c0 = s->rank * kvd_l;
   for (size_t l = 0; l < s->layers.size(); l++) {
-    CK(launch_gen_normal(seed, 0xA0000ull + 2 * l, 0, n, 1.0f, s->keys[l], d->st));
+    CK(launch_gen_normal_2d(seed, 0xA0000ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, s->keys[l], d->st));
     if (s->v_pitch > 0)
-      CK(launch_gen_normal_t(seed, 0xA0001ull + 2 * l, positions, kvd, s->v_pitch, 1.0f, s->vals[l], d->st));
+      CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, 1, s->v_pitch, 1.0f, s->vals[l],
+                              d->st));
     else
-      CK(launch_gen_normal(seed, 0xA0001ull + 2 * l, 0, n, 1.0f, s->vals[l], d->st));
+      CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, s->vals[l], d->st));
   }
   return sync_dev(d);
 }

@@ -207,6 +207,9 @@ RK_DEV uint64_t globaltimer_ns() {
 // Whether launches on this host thread use programmatic dependent launch
 // (set while a decode step is being recorded into a CUDA graph).
 inline thread_local bool g_pdl = false;
+// Kernels this host thread has launched through launch_k (capture counts a
+// recorded step's own kernels with it).
+inline thread_local long long g_kernel_launches = 0;
 
 // Launches kernel k with the programmatic stream-serialization attribute
 // when g_pdl is set, else as an ordinary launch.
@@ -223,6 +226,7 @@ inline cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_pdl ? 1 : 0;
+  g_kernel_launches++;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 

@@ -32,24 +32,26 @@ __global__ void k_gen_normal(uint64_t seed, uint64_t tid, long long offset, long
     out[j] = gen_value(key, offset + j, scale);
 }
 
-// Element (t, i) of a rows × cols tensor (index t·cols + i) to out[i·pitch + t].
-__global__ void k_gen_normal_t(uint64_t seed, uint64_t tid, int rows, int cols, long long pitch, float scale,
-                               float *out) {
+// Columns [col0, col0 + ncols) of a rows × cols tensor: element (t, col0 + i)
+// (index t·cols + col0 + i) to out[t·pitch_t + i·pitch_i].
+__global__ void k_gen_normal_2d(uint64_t seed, uint64_t tid, int rows, int cols, int col0, int ncols,
+                                long long pitch_t, long long pitch_i, float scale, float *out) {
   const uint64_t key = splitmix64(splitmix64(seed) ^ tid);
-  const long long n = (long long)rows * cols;
+  const long long n = (long long)rows * ncols;
+  const bool by_t = pitch_t == 1;  // consecutive threads write consecutive addresses
   for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x) {
-    const long long t = j % rows, i = j / rows;  // consecutive threads write consecutive t
-    out[i * pitch + t] = gen_value(key, t * cols + i, scale);
+    const long long t = by_t ? j % rows : j / ncols, i = by_t ? j / rows : j % ncols;
+    out[t * pitch_t + i * pitch_i] = gen_value(key, t * cols + col0 + i, scale);
   }
 }
 
-cudaError_t launch_gen_normal_t(uint64_t seed, uint64_t tid, int rows, int cols, long long pitch, float scale,
-                                float *out, cudaStream_t st) {
-  const long long n = (long long)rows * cols;
+cudaError_t launch_gen_normal_2d(uint64_t seed, uint64_t tid, int rows, int cols, int col0, int ncols,
+                                 long long pitch_t, long long pitch_i, float scale, float *out, cudaStream_t st) {
+  const long long n = (long long)rows * ncols;
   if (n <= 0) return cudaSuccess;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 64) blocks = 148 * 64;
-  k_gen_normal_t<<<int(blocks), 256, 0, st>>>(seed, tid, rows, cols, pitch, scale, out);
+  k_gen_normal_2d<<<int(blocks), 256, 0, st>>>(seed, tid, rows, cols, col0, ncols, pitch_t, pitch_i, scale, out);
   return cudaGetLastError();
 }
 

@@ -8,10 +8,12 @@ namespace rk {
 // out[j] = element offset+j of tensor `tid` (see rk_gen.cu).
 cudaError_t launch_gen_normal(uint64_t seed, uint64_t tid, long long offset, long long n, float scale, float *out,
                               cudaStream_t st);
-// The same elements for a rows × cols tensor stored transposed: element
-// (t, i), index t·cols + i, goes to out[i·pitch + t].
-cudaError_t launch_gen_normal_t(uint64_t seed, uint64_t tid, int rows, int cols, long long pitch, float scale,
-                                float *out, cudaStream_t st);
+// Columns [col0, col0 + ncols) of a rows × cols tensor, laid out freely:
+// element (t, col0 + i) (index t·cols + col0 + i) goes to
+// out[t·pitch_t + i·pitch_i] (rows: pitch_t = ncols, pitch_i = 1;
+// transposed: pitch_t = 1, pitch_i = the row pitch).
+cudaError_t launch_gen_normal_2d(uint64_t seed, uint64_t tid, int rows, int cols, int col0, int ncols,
+                                 long long pitch_t, long long pitch_i, float scale, float *out, cudaStream_t st);
 // num.QuantizeQ8 (quant.go:25-30) of n floats.
 cudaError_t launch_quantize_q8_w(const float *w, long long n, int8_t *q, float *scales, cudaStream_t st);
 // num.QuantizeQ4 (quant.go:62-68) of n floats; stale_scratch holds n/32 bytes.
