@@ -19,8 +19,11 @@ cpu_baseline: the CPU oracle (a C restatement of the reference's Go CPU
         path) on a bounded sample of the same step, on this host's cores.
 
 --impl reference runs only that CPU implementation (no GPU).
-With --gpus N (under torchrun) every GPU decodes its own sequence: N
-independent replicas (weak scaling); there is no data-path collective.
+With --gpus N (under torchrun) the default --mode rows shards every layer's
+weight rows over the N GPUs (whole kv heads per GPU) and reassembles each
+product's output with an NCCL all-gather inside the step's CUDA graph: one
+sequence decoded by all N GPUs (strong scaling; value = its tokens/s).
+--mode replicas runs N independent copies instead (weak scaling).
 """
 import argparse
 import json
@@ -50,6 +53,9 @@ def parse():
     p.add_argument("--dtype", default="q8_0")
     p.add_argument("--ctx", type=int, default=CTX)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--mode", default="rows", choices=["rows", "replicas"],
+                   help="N>1: shard every layer's rows over the N GPUs (NCCL all-gather; one sequence), "
+                        "or run N independent replicas")
     p.add_argument("--layers", type=int, default=0,
                    help="profiling aid: build the model with this many layers instead of the config's")
     p.add_argument("--tensor-shape", default=None,
@@ -263,7 +269,15 @@ def main():
     dev = rk.Device(local)
     over = {"layers": args.layers} if args.layers > 0 else {}
     c = synth.config(args.model, args.dtype, seq_len=args.ctx + 64, **over)
-    dm = synth.DeviceModel(dev, c, SEED, ctx=args.ctx + 64)
+    sharded = world > 1 and args.mode == "rows"
+    group = None
+    if sharded:
+        # Row shards of every layer over the N GPUs; the group id travels
+        # over the torch process group.
+        gid = [rk.group_id() if rank == 0 else None]
+        dist.broadcast_object_list(gid, src=0)
+        group = rk.Group(dev, world, rank, gid[0])
+    dm = synth.DeviceModel(dev, c, SEED, ctx=args.ctx + 64, group=group)
     dm.stage.fill_cache(args.ctx, SEED)
     pos, tok = args.ctx, 1
 
@@ -316,13 +330,18 @@ def main():
     # algorithmic bytes per launch (traffic scales with the rows read).
     ratio = traffic_ratio()
     traffic = ratio * prof.matvec_bytes / prof.matvec_launches if ratio and prof.matvec_launches else None
+    # Sequences decoded at once: one sharded over all GPUs, or one per replica.
+    seqs = 1 if sharded else world
     if rank == 0:
+        cfg = workload(args)
+        cfg["parallelism"] = f"rows{world}" if sharded else (f"replicas{world}" if world > 1 else "none")
         line = {
-            "metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "metric": METRIC, "value": seqs * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if sharded else "weak",
             "vs_baseline": None, "dtype": "int8xint8->int32, f32 combine", "data": "synthetic",
-            "config": workload(args),
-            "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8,
+            "config": cfg,
+            "e2e": {"value": seqs * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4 * c.vocab + 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
@@ -336,6 +355,9 @@ def main():
         }
         print(json.dumps(line), flush=True)
     dm.free()
+    if group:
+        barrier()
+        group.free()
     dev.close()
     if dist:
         dist.destroy_process_group()

@@ -206,6 +206,13 @@ class Matrix:
         _check(lib().rk_matrix_generate(dev.h, rows, cols, fmt, seed, tid, scale, C.byref(h)))
         return cls(dev, rows, cols, fmt, handle=h)
 
+    @classmethod
+    def generate_rows(cls, dev, rows_total, row0, rows, cols, fmt, seed, tid, scale):
+        """Rows [row0, row0+rows) of the generated rows_total x cols tensor."""
+        h = C.c_void_p()
+        _check(lib().rk_matrix_generate_rows(dev.h, rows_total, row0, rows, cols, fmt, seed, tid, scale, C.byref(h)))
+        return cls(dev, rows, cols, fmt, handle=h)
+
     def download(self):
         w = np.empty(self.rows * row_bytes(self.fmt, self.cols) // np.dtype(weight_dtype(self.fmt)).itemsize,
                      dtype=weight_dtype(self.fmt))
@@ -329,20 +336,47 @@ class Batch:
         _check(lib().rk_batch_submit(h))
 
 
-class Layer:
-    """llm.Layer on a device (model.go:282-387)."""
+def group_id():
+    """A fresh group id (bytes) for Group on every rank."""
+    buf = (C.c_ubyte * 128)()
+    _check(lib().rk_group_id(buf))
+    return bytes(buf)
 
-    def __init__(self, dev, cfg, host=None, mats=None, vectors=None):
+
+class Group:
+    """Rank `rank` of `nranks` GPUs sharing row-sharded stages (NCCL)."""
+
+    def __init__(self, dev, nranks, rank, gid):
         self.h = C.c_void_p()
+        self.nranks, self.rank = nranks, rank
+        buf = (C.c_ubyte * 128).from_buffer_copy(gid)
+        _check(lib().rk_group_new(dev.h, nranks, rank, buf, C.byref(self.h)))
+
+    def all_gather(self, buf_dev_ptr, count):
+        _check(lib().rk_group_all_gather(self.h, C.c_void_p(buf_dev_ptr), count))
+
+    def free(self):
+        if self.h:
+            lib().rk_group_free(self.h)
+            self.h = C.c_void_p()
+
+
+class Layer:
+    """llm.Layer on a device (model.go:282-387); shard=(n, r) for rank r's
+    rows of n (rk_layer_*_shard)."""
+
+    def __init__(self, dev, cfg, host=None, mats=None, vectors=None, shard=None):
+        self.h = C.c_void_p()
+        n, r = shard if shard else (1, 0)
         if host is not None:
             hl, keep = host
             self._keep = keep
-            _check(lib().rk_layer_upload(dev.h, C.byref(cfg), C.byref(hl), C.byref(self.h)))
+            _check(lib().rk_layer_upload_shard(dev.h, C.byref(cfg), n, r, C.byref(hl), C.byref(self.h)))
         else:
             hl, keep = vectors
             self._keep = keep
-            _check(lib().rk_layer_from_device(dev.h, C.byref(cfg), C.byref(hl), *[m.h for m in mats],
-                                              C.byref(self.h)))
+            _check(lib().rk_layer_from_device_shard(dev.h, C.byref(cfg), n, r, C.byref(hl), *[m.h for m in mats],
+                                                    C.byref(self.h)))
             for m in mats:
                 m.h = C.c_void_p()  # owned by the layer now
 
@@ -355,11 +389,14 @@ class Layer:
 class Stage:
     """llm.Stage on a device (model.go:446-613)."""
 
-    def __init__(self, dev, cfg, layers, ctx):
+    def __init__(self, dev, cfg, layers, ctx, group=None):
         hs = (C.c_void_p * max(1, len(layers)))(*[l.h for l in layers])
         self.h = C.c_void_p()
         self.dim = cfg.dim
-        _check(lib().rk_stage_new(dev.h, C.byref(cfg), hs, len(layers), ctx, C.byref(self.h)))
+        if group is None:
+            _check(lib().rk_stage_new(dev.h, C.byref(cfg), hs, len(layers), ctx, C.byref(self.h)))
+        else:
+            _check(lib().rk_stage_new_group(dev.h, C.byref(cfg), hs, len(layers), ctx, group.h, C.byref(self.h)))
 
     def positions(self):
         return lib().rk_stage_positions(self.h)
@@ -380,11 +417,14 @@ class Stage:
 
 
 class Head:
-    def __init__(self, dev, cfg, rms_final, wcls):
+    def __init__(self, dev, cfg, rms_final, wcls, group=None):
         rms = np.ascontiguousarray(rms_final, dtype=np.float32)
         self.vocab = cfg.vocab
         self.h = C.c_void_p()
-        _check(lib().rk_head_new(dev.h, C.byref(cfg), _ptr(rms), wcls.h, C.byref(self.h)))
+        if group is None:
+            _check(lib().rk_head_new(dev.h, C.byref(cfg), _ptr(rms), wcls.h, C.byref(self.h)))
+        else:
+            _check(lib().rk_head_new_group(dev.h, C.byref(cfg), _ptr(rms), wcls.h, group.h, C.byref(self.h)))
 
     def logits(self, x):
         x = np.ascontiguousarray(x, dtype=np.float32)

@@ -72,6 +72,19 @@ def mat_shape(c, kind):
     return {"wq": (q, d), "wk": (kv, d), "wv": (kv, d), "wo": (d, q), "w1": (h, d), "w2": (d, h), "w3": (h, d)}[kind]
 
 
+def shard_rows(c, nshards, shard):
+    """Rows [row0, row0 + rows) of each layer matrix (and "cls", the
+    classifier) that shard `shard` of `nshards` holds: whole query / kv heads
+    of Wq, Wk, Wv; dim/G rows of Wo and W2; hidden/G rows of W1 and W3;
+    vocab/G classifier rows (the layout rk_layer_*_shard checks)."""
+    G, r, hs = nshards, shard, head_size(c)
+    if c.kv_heads % G or c.dim % G or c.hidden % G or c.vocab % G:
+        raise ValueError(f"cannot shard {c.kv_heads} kv heads / dim {c.dim} / hidden {c.hidden} / vocab {c.vocab} over {G}")
+    q, kv, d, h = c.heads * hs // G, c.kv_heads * hs // G, c.dim // G, c.hidden // G
+    return {"wq": (r * q, q), "wk": (r * kv, kv), "wv": (r * kv, kv), "wo": (r * d, d), "w1": (r * h, h),
+            "w2": (r * d, d), "w3": (r * h, h), "cls": (r * (c.vocab // G), c.vocab // G)}
+
+
 def layer_vectors(c):
     """RmsAtt, RmsFfn = 1; biases = 0; QNorm, KNorm = 1."""
     hs = head_size(c)
@@ -102,10 +115,15 @@ def to_bf16(f):
     return r
 
 
-def generate_matrix(dev, rows, cols, fmt, seed, t):
+def generate_matrix(dev, rows, cols, fmt, seed, t, part=None):
+    """The seeded rows x cols tensor t; part=(row0, n) generates only rows
+    [row0, row0 + n) (a shard)."""
+    row0, n = part if part else (0, rows)
     if fmt == rk.FMT_BF16:
-        w = rk.generate_normal(dev, seed, t, 0, rows * cols, WEIGHT_SCALE)
-        return rk.Matrix(dev, rows, cols, fmt, to_bf16(w))
+        w = rk.generate_normal(dev, seed, t, row0 * cols, n * cols, WEIGHT_SCALE)
+        return rk.Matrix(dev, n, cols, fmt, to_bf16(w))
+    if part:
+        return rk.Matrix.generate_rows(dev, rows, row0, n, cols, fmt, seed, t, WEIGHT_SCALE)
     return rk.Matrix.generate(dev, rows, cols, fmt, seed, t, WEIGHT_SCALE)
 
 
@@ -113,27 +131,36 @@ class DeviceModel:
     """A whole synthetic model on one device: embed, stage of all layers,
     head and the greedy decode loop (rk_model)."""
 
-    def __init__(self, dev, c, seed, ctx=None, keep_host=False):
+    def __init__(self, dev, c, seed, ctx=None, keep_host=False, group=None):
         """keep_host: also download every matrix (host_weights, keyed like
-        the oracle's OracleModel(weights=...)) before the layers own them."""
+        the oracle's OracleModel(weights=...)) before the layers own them.
+        group: an rk.Group; this process then holds its row shard of every
+        layer and of the classifier (shard_rows) and decodes collectively."""
         self.c, self.dev, self.seed = c, dev, seed
         self.ctx = ctx or c.seq_len
         self.layers = []
         self.host_weights = {} if keep_host else None
+        G, r = (group.nranks, group.rank) if group else (1, 0)
+        parts = shard_rows(c, G, r) if group else {}
         for l in range(c.layers):
-            mats = [generate_matrix(dev, *mat_shape(c, k), mat_fmt(c, k), seed, tid(l, k)) for k in MATS]
+            mats = [generate_matrix(dev, *mat_shape(c, k), mat_fmt(c, k), seed, tid(l, k), parts.get(k)) for k in MATS]
             if keep_host:
                 for k, m in zip(MATS, mats):
                     self.host_weights[(l, k)] = m.download()
-            self.layers.append(rk.Layer(dev, c, mats=mats, vectors=host_layer_vectors(c)))
+            self.layers.append(rk.Layer(dev, c, mats=mats, vectors=host_layer_vectors(c),
+                                        shard=(G, r) if group else None))
         ef = embed_fmt(c)
         self.embed = generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_EMBED)
-        self.wcls = self.embed if c.shared_classifier else generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_CLS)
+        if group:
+            t = TID_EMBED if c.shared_classifier else TID_CLS
+            self.wcls = generate_matrix(dev, c.vocab, c.dim, ef, seed, t, parts["cls"])
+        else:
+            self.wcls = self.embed if c.shared_classifier else generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_CLS)
         if keep_host:
             self.host_weights["embed"] = self.embed.download()
             self.host_weights["cls"] = self.wcls.download()
-        self.stage = rk.Stage(dev, c, self.layers, self.ctx)
-        self.head = rk.Head(dev, c, np.ones(c.dim, np.float32), self.wcls)
+        self.stage = rk.Stage(dev, c, self.layers, self.ctx, group=group)
+        self.head = rk.Head(dev, c, np.ones(c.dim, np.float32), self.wcls, group=group)
         self.model = rk.Model(dev, self.embed, self.stage, self.head, c.vocab)
 
     def weight_bytes(self):

@@ -1,0 +1,72 @@
+"""Row-sharded decode on two GPUs (rk_group / rk_*_group) against the CPU
+oracle: the same logits, bit for bit, and the same greedy tokens as the
+reference path. Each rank is a child process on its own GPU; NCCL carries
+the all-gathers. Skipped on a box with one GPU.
+"""
+import numpy as np
+import pytest
+
+import rk_oracle as ro
+import rkcuda as rk
+import synth
+from conftest import same_bits
+
+pytestmark = pytest.mark.gpu
+
+SEED = 20261203
+PROMPT = [3, 141, 59, 265, 35, 897]
+N_NEW = 6
+CTX = 64
+
+
+def _small(dtype, variant):
+    over = dict(layers=2, dim=1024, hidden=2816, heads=8, kv_heads=4, vocab=8192, seq_len=CTX)
+    if variant == "qwen3":
+        over.update(head_dim=128, qk_norm=1, rope_theta=1e6, norm_eps=1e-6, heads=16, kv_heads=4)
+    return synth.config("llama3-8b", dtype, **over)
+
+
+def _rank(rank, world, gid, dtype, variant, out):
+    import os
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        c = _small(dtype, variant)
+        dev = rk.Device(rank)
+        grp = rk.Group(dev, world, rank, gid)
+        dm = synth.DeviceModel(dev, c, SEED, ctx=CTX, group=grp)
+        toks, logits = dm.model.generate(np.array(PROMPT, np.int32), N_NEW, want_logits=True)
+        out.put((rank, toks, logits, dev.used() > 0))
+        dm.free()
+        grp.free()
+        dev.close()
+    except Exception as e:
+        out.put((rank, repr(e), None, None))
+
+
+@pytest.mark.parametrize("variant", ["llama", "qwen3"])
+@pytest.mark.parametrize("dtype", ["q8_0", "q4_0"])
+def test_row_sharded_decode_matches_oracle(dtype, variant):
+    if rk.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    gid = rk.group_id()
+    procs = [ctx.Process(target=_rank, args=(r, 2, gid, dtype, variant, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, toks, logits, _used = out.get(timeout=600)
+        res[r] = (toks, logits)
+    for p in procs:
+        p.join(timeout=120)
+    for r in (0, 1):
+        assert not isinstance(res[r][0], str), res[r][0]
+    om = ro.OracleModel(_small(dtype, variant), SEED, ctx=CTX)
+    want_toks, want_logits = om.generate(PROMPT, N_NEW)
+    om.free()
+    for r in (0, 1):
+        toks, logits = res[r]
+        assert list(toks) == list(want_toks)
+        same_bits(logits, want_logits)
