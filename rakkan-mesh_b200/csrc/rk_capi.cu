@@ -1250,7 +1250,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
         CK(launch_quantize_wide(x, cols, norm_w, recip, eps, nullptr, s->qx, s->xs, s->xsum, st));
         return enqueue_matvecs(d, n, ms, outs, x, s->qx, s->xs, s->xsum, epi, st);
       }
-      if (matvec_fused_ok(ms[0]->fmt, cols)) {
+      if (matvec_fused_ok(ms[0]->fmt, cols, norm_w != nullptr)) {
         Pro p;
         p.pro = norm_w ? PRO_NORM_QUANT : PRO_QUANT;
         p.norm_w = norm_w;
@@ -1340,7 +1340,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
       a.part[1] = part_of(l->w3, s->hb2 + rH0);
       a.nparts = 2;
       const float *norm_w = vec + l->o_rms_ffn;
-      if (quantized_fmt(a.fmt) && matvec_fused_ok(a.fmt, D)) {
+      if (quantized_fmt(a.fmt) && matvec_fused_ok(a.fmt, D, true)) {
         a.pro = PRO_NORM_QUANT;
         a.x = s->x;
         a.norm_w = norm_w;
@@ -1647,7 +1647,7 @@ static int record_head(rk_head *h, const float *x, cudaStream_t st) {
     a.qx = h->qx;
     a.xs = h->xs;
     a.xsum = h->xsum;
-  } else if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D)) {
+  } else if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D, true)) {
     // Every CTA computes rmsNorm + quantize8 of x itself.
     a.pro = PRO_NORM_QUANT;
     a.x = x;
@@ -2034,7 +2034,7 @@ extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per
   rk_device *d = m->d;
   const int flush = flags & RK_BENCH_FLUSH;
   Pro pro;
-  if ((flags & RK_BENCH_FUSED) && quantized_fmt(m->fmt) && matvec_fused_ok(m->fmt, m->cols)) pro.pro = PRO_QUANT;
+  if ((flags & RK_BENCH_FUSED) && quantized_fmt(m->fmt) && matvec_fused_ok(m->fmt, m->cols, false)) pro.pro = PRO_QUANT;
   Guard g(d);
   int rc = set_device(d);
   if (rc) return rc;

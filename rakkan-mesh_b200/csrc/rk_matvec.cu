@@ -28,37 +28,61 @@ namespace rk {
 // Activation quantization (quantize8, quant.go:34-53), optionally after
 // rmsNorm (model.go:632-638). One CTA; warp w quantizes blocks w, w+W, ...
 // ---------------------------------------------------------------------------
-// Floats of x staged at a time in shared memory for the norm's Dot32.
-constexpr int kStageFloats = 8192;
+// quantize8 of x[n] (after rmsNorm when NORM) by one CTA, a thread per
+// 32-block. x (and the norm's weights) go to shared memory first, in one
+// round of asynchronous 16-byte copies per chunk of at most `stage_floats`
+// floats (a multiple of 32): while the matvec's weight stream starts, a
+// global load waits microseconds, so all of them are issued at once. With the norm, warp 0
+// runs Dot32(x, x) in the reference's lane order (matvec.go:32-43) and
+// broadcasts Rsqrt32 through *s_inv; when x spans several chunks it is
+// loaded twice (norm, then quantization). With `preloaded` the caller has
+// already issued stage_load for the first chunk.
+RK_DEV void stage_load(const float *__restrict__ x, const float *__restrict__ w, int c0, int m, float *stage,
+                       float *wstage) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  if (vec) {
+    // Asynchronous 16-byte copies: every load of the chunk is in flight at
+    // once; the caller's barrier is preceded by stage_wait().
+    for (int i = threadIdx.x; i < m / 4; i += blockDim.x) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(stage + 4 * i)),
+                   "l"(x + c0 + 4 * i)
+                   : "memory");
+      if (w)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(wstage + 4 * i)),
+                     "l"(w + c0 + 4 * i)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  } else {
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      stage[i] = x[c0 + i];
+      if (w) wstage[i] = w[c0 + i];
+    }
+  }
+}
 
-// quantize8 of x[n] (after rmsNorm when NORM) by one CTA that owns the
-// whole input: x goes to `stage` (stage_floats floats, a multiple of 32) chunk by
-// chunk, and thread t quantizes block t of the chunk on its own (amax,
-// scale, values and sum over the block's 32 values, read in a rotated order
-// so that the threads of a warp use different banks: amax and the sum are
-// order free). With NORM and n <= stage_floats, x is staged once for both
-// the norm's Dot32 and the quantization.
+// Completes this thread's stage_load copies (before the barrier that
+// publishes the chunk).
+RK_DEV void stage_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 template <bool NORM>
-RK_DEV void quantize_staged(const float *__restrict__ x, int n, const float *__restrict__ w, float recipN, float eps,
-                            int8_t *qx, float *xs, int *xsum, float *s_inv, float *stage, int stage_floats) {
+RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__restrict__ w, float recipN, float eps,
+                           int8_t *qx, float *xs, int *xsum, float *s_inv, float *stage, float *wstage,
+                           int stage_floats, bool preloaded) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-  auto load = [&](int c0, int m) {
-    if (aligned)
-      for (int i = threadIdx.x; i < m / 4; i += blockDim.x)
-        reinterpret_cast<float4 *>(stage)[i] = reinterpret_cast<const float4 *>(x + c0)[i];
-    else
-      for (int i = threadIdx.x; i < m; i += blockDim.x) stage[i] = x[c0 + i];
-  };
-  float inv = 0.0f;
   const bool single = n <= stage_floats;
+  float inv = 0.0f;
   if (NORM) {
-    // Dot32(x, x): lane j sums elements j, j+32, ... in order (matvec.go:32-43).
     float s = 0.0f;
     for (int c0 = 0; c0 < n; c0 += stage_floats) {
       const int m = min(stage_floats, n - c0);
-      __syncthreads();
-      load(c0, m);
+      if (!(preloaded && c0 == 0)) {
+        __syncthreads();
+        stage_load(x, single ? w : nullptr, c0, m, stage, wstage);
+      }
+      stage_wait();
       __syncthreads();
       if (warp == 0) {
 #pragma unroll 8
@@ -75,23 +99,34 @@ RK_DEV void quantize_staged(const float *__restrict__ x, int n, const float *__r
   for (int c0 = 0; c0 < n; c0 += stage_floats) {
     const int m = min(stage_floats, n - c0);
     if (!(NORM && single)) {
-      __syncthreads();
-      load(c0, m);
+      if (!(preloaded && c0 == 0 && !NORM)) {
+        __syncthreads();
+        stage_load(x, NORM ? w : nullptr, c0, m, stage, wstage);
+      }
+      stage_wait();
       __syncthreads();
     }
+    // Thread t quantizes block t of the chunk on its own: its 32 values are
+    // independent, so the thread's work pipelines, and a block costs a few
+    // instructions per value instead of warp-wide reductions. The values are
+    // read in a rotated order so that the threads of a warp hit different
+    // banks (amax and the integer sum are order free).
     for (int t = threadIdx.x; t < m / 32; t += blockDim.x) {
       const int b = c0 / 32 + t;
       const float *src = stage + t * 32;
       float v[32];
-      float amax = 0.0f;
+      uint32_t kmax = 0;
 #pragma unroll
       for (int j = 0; j < 32; j++) {
         const int jj = (j + t) & 31;
         float vv = src[jj];
-        if (NORM) vv = __fmul_rn(w[b * 32 + jj], __fmul_rn(inv, vv));
+        if (NORM) vv = __fmul_rn(wstage[t * 32 + jj], __fmul_rn(inv, vv));
         v[j] = vv;
-        amax = gomax(amax, fabsf(vv));
+        kmax = max(kmax, f2u(fabsf(vv)));
       }
+      // amax as Go's max: an unsigned max of the |v| bit patterns (bit order
+      // is value order for non-negative floats; a NaN lands above +Inf).
+      const float amax = kmax > 0x7f800000u ? u2f(kCanonNaN) : u2f(kmax);
       const float d = __fmul_rn(amax, u2f(K_1_127));
       int8_t *q = qx + b * 32;
       int sum = 0;
@@ -113,18 +148,19 @@ RK_DEV void quantize_staged(const float *__restrict__ x, int n, const float *__r
   }
 }
 
-constexpr int kQuantStage = 8192;  // floats of shared memory for the standalone quantizer
+constexpr int kQuantStage = 4096;  // floats per staged chunk in the standalone quantizer
 
 template <bool NORM>
 __global__ void __launch_bounds__(512) k_quantize_act(const float *__restrict__ x, int n,
                                                        const float *__restrict__ w, float recipN, float eps,
-                                                       float *__restrict__ xn, int8_t *__restrict__ qx,
-                                                       float *__restrict__ xs, int *__restrict__ xsum) {
+                                                       int8_t *__restrict__ qx, float *__restrict__ xs,
+                                                       int *__restrict__ xsum) {
   __shared__ float s_inv;
   __shared__ __align__(16) float stage[kQuantStage];
+  __shared__ __align__(16) float wstage[NORM ? kQuantStage : 4];
   griddep_trigger();
   griddep_wait();
-  quantize_staged<NORM>(x, n, w, recipN, eps, qx, xs, xsum, &s_inv, stage, kQuantStage);
+  quantize_warps<NORM>(x, n, w, recipN, eps, qx, xs, xsum, &s_inv, stage, wstage, kQuantStage, false);
 }
 
 // The same over many CTAs, a warp per 32-block: lane j holds element j,
@@ -186,8 +222,9 @@ cudaError_t launch_quantize_wide(const float *x, int n, const float *w, float re
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st) {
   int threads = n >= 16 * 32 ? 512 : ((n / 32) > 0 ? (n / 32) * 32 : 32);
-  if (w) return launch_k(k_quantize_act<true>, 1, threads, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
-  return launch_k(k_quantize_act<false>, 1, threads, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
+  if (xn) return cudaErrorInvalidValue;  // the one-CTA quantizer does not keep the normalised floats
+  if (w) return launch_k(k_quantize_act<true>, 1, threads, 0, st, x, n, w, recipN, eps, qx, xs, xsum);
+  return launch_k(k_quantize_act<false>, 1, threads, 0, st, x, n, w, recipN, eps, qx, xs, xsum);
 }
 
 // ---------------------------------------------------------------------------
@@ -247,6 +284,16 @@ RK_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar
 // ---------------------------------------------------------------------------
 // Quantized matvec with a per-warp TMA ring.
 // ---------------------------------------------------------------------------
+// Staging of the fused prologue: x whole when it fits (up to 16384 floats;
+// 14336-wide W2 inputs in one load round), else in chunks; the norm's
+// weights beside it.
+__host__ __device__ constexpr int stage_floats(int cols, bool norm) {
+  return cols <= (norm ? 8192 : 16384) ? cols : (norm ? 8192 : 16384);
+}
+__host__ __device__ constexpr int stage_bytes(int cols, bool norm) {
+  return 4 * stage_floats(cols, norm) * (norm ? 2 : 1);
+}
+
 constexpr int kSegBytes = 4096;  // weight bytes per segment
 constexpr int kPrefetchSegs = 4;  // segments per warp prefetched into L2 before the predecessor ends
 
@@ -413,8 +460,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     sxs = xs;
     sxsum = xsum;
   }
-  // The norm's staging area (kStageFloats floats) sits just below the rings.
-  uint8_t *ring_base = p + (a.pro != PRO_GIVEN ? kStageFloats * 4 : 0);
+  // The prologue's staging areas (x, and the norm weights) sit below the rings.
+  uint8_t *ring_base = p + (a.pro != PRO_GIVEN ? stage_bytes(cols, a.pro == PRO_NORM_QUANT) : 0);
   uint8_t *ring = ring_base + warp * SLOTS * slot_bytes<FMT>();
 
   const int gw = blockIdx.x * WARPS + warp, G = gridDim.x * WARPS;
@@ -464,19 +511,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     }
   }
   griddep_wait();
+  // The input's loads go first, ahead of the weight ring's copies.
+  const bool norm = a.pro == PRO_NORM_QUANT;
+  float *stage = reinterpret_cast<float *>(p);
+  const int sf = a.pro != PRO_GIVEN ? stage_floats(cols, norm) : 0;
+  if (a.pro != PRO_GIVEN)
+    stage_load(a.x, norm && cols <= sf ? a.norm_w : nullptr, 0, min(cols, sf), stage, stage + sf);
   if (lane == 0)
     for (int k = 0; k < SLOTS; k++) issue();
 
   if (a.pro != PRO_GIVEN) {
     __shared__ float s_inv;
     int8_t *q = const_cast<int8_t *>(sqx);
-    float *stage = reinterpret_cast<float *>(p);
-    if (a.pro == PRO_NORM_QUANT)
-      quantize_staged<true>(a.x, cols, a.norm_w, a.recipN, a.eps, q, const_cast<float *>(sxs),
-                            const_cast<int *>(sxsum), &s_inv, stage, kStageFloats);
+    if (norm)
+      quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, q, const_cast<float *>(sxs),
+                           const_cast<int *>(sxsum), &s_inv, stage, stage + sf, sf, true);
     else
-      quantize_staged<false>(a.x, cols, nullptr, 0.0f, 0.0f, q, const_cast<float *>(sxs), const_cast<int *>(sxsum),
-                             &s_inv, stage, kStageFloats);
+      quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, q, const_cast<float *>(sxs), const_cast<int *>(sxsum),
+                            &s_inv, stage, nullptr, sf, true);
   } else if (qx_in_smem) {
     int8_t *q = const_cast<int8_t *>(sqx);
     for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
@@ -620,9 +672,9 @@ static int input_smem_bytes(int cols) {
 constexpr int kWarps = 16, kSlots = 2;
 
 template <int FMT>
-static int smem_for(int cols, bool fused) {
-  return kWarps * kSlots * 8 + (cols <= kSmemColsMax ? input_smem_bytes(cols) : 0) + (fused ? kStageFloats * 4 : 0) +
-         kWarps * kSlots * slot_bytes<FMT>();
+static int smem_for(int cols, bool fused, bool norm = true) {
+  return kWarps * kSlots * 8 + (cols <= kSmemColsMax ? input_smem_bytes(cols) : 0) +
+         (fused ? stage_bytes(cols, norm) : 0) + kWarps * kSlots * slot_bytes<FMT>();
 }
 
 int matvec_smem_bytes(int fmt, int cols) {
@@ -633,10 +685,10 @@ int matvec_smem_bytes(int fmt, int cols) {
 // (227 KiB) less 1 KiB for the kernel's static shared memory.
 constexpr int kSmemLimit = 232448 - 1024;
 
-bool matvec_fused_ok(int fmt, int cols) {
+bool matvec_fused_ok(int fmt, int cols, bool norm) {
   if (cols > kSmemColsMax) return false;
-  if (fmt == FMT_Q8_0) return smem_for<FMT_Q8_0>(cols, true) <= kSmemLimit;
-  if (fmt == FMT_Q4_0) return smem_for<FMT_Q4_0>(cols, true) <= kSmemLimit;
+  if (fmt == FMT_Q8_0) return smem_for<FMT_Q8_0>(cols, true, norm) <= kSmemLimit;
+  if (fmt == FMT_Q4_0) return smem_for<FMT_Q4_0>(cols, true, norm) <= kSmemLimit;
   return false;
 }
 
@@ -659,14 +711,14 @@ int mv_mode() {
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
   const bool quant = a.fmt == FMT_Q8_0 || a.fmt == FMT_Q4_0;
-  if (quant && a.pro != PRO_GIVEN && !matvec_fused_ok(a.fmt, a.cols)) return cudaErrorInvalidValue;
-  const bool fused = a.pro != PRO_GIVEN;
+  const bool fused = a.pro != PRO_GIVEN, norm = a.pro == PRO_NORM_QUANT;
+  if (quant && fused && !matvec_fused_ok(a.fmt, a.cols, norm)) return cudaErrorInvalidValue;
   const int in_smem = a.cols <= kSmemColsMax && (fused || mv_mode() != 2) ? 1 : 0;
   if (a.fmt == FMT_Q8_0)
-    return launch_k(k_matvec_q<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q8_0>(a.cols, fused), st, a,
+    return launch_k(k_matvec_q<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q8_0>(a.cols, fused, norm), st, a,
                     in_smem);
   if (a.fmt == FMT_Q4_0)
-    return launch_k(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q4_0>(a.cols, fused), st, a,
+    return launch_k(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q4_0>(a.cols, fused, norm), st, a,
                     in_smem);
   if (a.fmt == FMT_F32) return launch_k(k_matvec_f<FMT_F32>, num_sms * 4, 256, 0, st, a);
   return launch_k(k_matvec_f<FMT_BF16>, num_sms * 4, 256, 0, st, a);

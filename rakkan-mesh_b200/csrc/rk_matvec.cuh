@@ -57,13 +57,14 @@ constexpr int kSmemColsMax = 32768;
 
 // Quantizes n floats (a whole number of 32-blocks) to Q8_0 as quantize8
 // does (quant.go:34-53), after RMS normalisation when w != nullptr
-// (model.go:632-638, recipN = Recip32(n)). xn, if not null, receives the
-// normalised floats.
+// (model.go:632-638, recipN = Recip32(n)), in one CTA. xn must be null
+// (launch_quantize_wide keeps the normalised floats).
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st);
 
 // The same quantization spread over ceil(n/256) CTAs, a warp per 32-block
-// (each CTA recomputes the norm's Dot32 when w != nullptr).
+// (each CTA recomputes the norm's Dot32 when w != nullptr); xn, if not
+// null, receives the normalised floats.
 cudaError_t launch_quantize_wide(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                  int8_t *qx, float *xs, int *xsum, cudaStream_t st);
 
@@ -78,9 +79,9 @@ int matvec_smem_bytes(int fmt, int cols);
 int mv_mode();
 
 // Whether a matvec of this format and width can quantize its input in its
-// own prologue (PRO_QUANT / PRO_NORM_QUANT): the input and its staging must
-// fit shared memory beside the weight rings.
-bool matvec_fused_ok(int fmt, int cols);
+// own prologue (PRO_NORM_QUANT when norm, else PRO_QUANT): the input and its
+// staging must fit shared memory beside the weight rings.
+bool matvec_fused_ok(int fmt, int cols, bool norm);
 
 // Raises the kernels' dynamic shared-memory limit; once per device, before
 // any launch or graph capture.
