@@ -180,7 +180,7 @@ class OracleModel:
     """The synthetic model of synth.py rebuilt on the host, run by the CPU
     restatement (Stage.Forward / Head.Logits / argmax)."""
 
-    def __init__(self, c, seed, ctx=None, weights=None, threads=THREADS):
+    def __init__(self, c, seed, ctx=None, weights=None, threads=THREADS, vec_seed=None):
         self.c = to_config(c)
         self.pc = c
         self.ctx = ctx or c.seq_len
@@ -188,7 +188,7 @@ class OracleModel:
         self.keep = []
         self.layers = (Layer * c.layers)()
         for l in range(c.layers):
-            vec = synth.layer_vectors(c)
+            vec = synth.layer_vectors(c, None if vec_seed is None else vec_seed + l)
             self.keep.append(vec)
             L = self.layers[l]
             for k, a in vec.items():

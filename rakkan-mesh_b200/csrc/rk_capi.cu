@@ -15,6 +15,7 @@
 
 #include <condition_variable>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <functional>
@@ -1301,8 +1302,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     qp.hs = hs;
     qp.eps = eps;
     qp.recip_hs = recipHS;
-    CK(launch_qkv_post(qp, st));
-    // Attention over positions 0..pos (model.go:571-587).
+    // Attention over positions 0..pos (model.go:571-587), after the
+    // post-processing above.
     AttnArgs at{};
     at.q = s->q;
     at.keys = s->keys[li];
@@ -1320,7 +1321,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.att_stride = s->att_stride;
     at.inv_sqrt = invSqrt;
     at.err = s->d->err_dev;
-    CK(launch_attention(at, st));
+    CK(launch_attention_post(qp, at, st));
     if ((rc = gather(s->att_out, qd))) return rc;
     // x += Wo·attOut (model.go:588-594).
     {

@@ -150,12 +150,42 @@ __global__ void __launch_bounds__(kScoreWarps * 32) k_attn_scores(const AttnArgs
 // to partial sum e mod 32 in increasing e, then the fixed tree
 // (matvec.go:60-66). No shuffles.
 constexpr int kTileT = 32;
-template <int HS>
-__global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int gpb) {
+
+// The per-token work between the QKV products and attention
+// (model.go:542-566) on one head vector in shared memory, by one warp: bias
+// add, QK-norm (rmsNorm over the head, Dot32 lane order), RoPE on adjacent
+// pairs with position pos's cos/sin rows.
+RK_DEV void head_post(float *v, int hs, const float *bias, const float *nw, const float *co, const float *si,
+                      float recip_hs, float eps) {
+  const int lane = threadIdx.x & 31;
+  if (bias)
+    for (int i = lane; i < hs; i += 32) v[i] = __fadd_rn(v[i], bias[i]);
+  __syncwarp();
+  if (nw) {
+    float s = 0.0f;
+    for (int i = lane; i < hs; i += 32) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+    const float dot = combine32(s);
+    const float inv = __shfl_sync(0xffffffffu, rsqrt32(__fadd_rn(__fmul_rn(dot, recip_hs), eps)), 0);
+    __syncwarp();
+    for (int i = lane; i < hs; i += 32) v[i] = __fmul_rn(nw[i], __fmul_rn(inv, v[i]));
+    __syncwarp();
+  }
+  for (int p = lane; p < hs / 2; p += 32) rotate_pair(v, 2 * p, co[p], si[p]);
+  __syncwarp();
+}
+
+// POST: the kernel also does k_qkv_post's work for its heads: each CTA
+// post-processes its query heads' raw q in shared memory, and the CTAs whose
+// tile holds the new position (pos = P - 1) post-process the kv head's raw k
+// for that row of the tile; the first group's CTA also appends k and v to
+// the caches (the next kernel reads the value row).
+template <int HS, bool POST>
+__global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int gpb, const QkvPostArgs qp) {
   griddep_trigger();
   griddep_wait();
   __shared__ float sk[kTileT * (HS + 1)];
   __shared__ float sq[8 * HS];
+  __shared__ float snew[POST ? HS : 1];
   const int P = attn_positions(a);
   const int t0 = blockIdx.x * kTileT;
   if (t0 >= P) return;
@@ -187,6 +217,33 @@ __global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int 
     }
   }
   for (int e = threadIdx.x; e < ng * HS; e += blockDim.x) sq[e] = a.q[(kvh * kvMul + g0) * HS + e];
+  if (POST) {
+    const int pos = P - 1;
+    const bool has_new = pos < t0 + nt;
+    if (has_new && warp == ng % (blockDim.x >> 5))
+      for (int i = lane; i < HS; i += 32) snew[i] = qp.k[kvh * HS + i];
+    __syncthreads();
+    const float *co = qp.cos_ + (long long)pos * (HS / 2), *si = qp.sin_ + (long long)pos * (HS / 2);
+    if (warp < ng) {
+      const int h = kvh * kvMul + g0 + warp;
+      head_post(sq + warp * HS, HS, qp.bq ? qp.bq + h * HS : nullptr, qp.q_norm, co, si, qp.recip_hs, qp.eps);
+    }
+    if (has_new && warp == ng % (blockDim.x >> 5)) {
+      head_post(snew, HS, qp.bk ? qp.bk + kvh * HS : nullptr, qp.k_norm, co, si, qp.recip_hs, qp.eps);
+      for (int i = lane; i < HS; i += 32) sk[(pos - t0) * (HS + 1) + i] = snew[i];
+      if (blockIdx.z == 0) {
+        // The cache append (model.go:567-568).
+        const int kvDim = qp.kv_heads * HS;
+        for (int i = lane; i < HS; i += 32) {
+          qp.key_cache[(long long)pos * kvDim + kvh * HS + i] = snew[i];
+          float vv = qp.v[kvh * HS + i];
+          if (qp.bv) vv = __fadd_rn(vv, qp.bv[kvh * HS + i]);
+          if (qp.v_pitch > 0) qp.val_cache[(long long)(kvh * HS + i) * qp.v_pitch + pos] = vv;
+          else qp.val_cache[(long long)pos * kvDim + kvh * HS + i] = vv;
+        }
+      }
+    }
+  }
   __syncthreads();
   if (warp >= ng) return;
   const float *q = sq + warp * HS;
@@ -611,17 +668,32 @@ bool attention_fused_ok(int heads, int kv_heads, int hs, int max_positions) {
   return gpb <= 8 && hs % kFsSlice == 0 && fs_smem_bytes(gpb, fs_wph(gpb), max_positions) > 0;
 }
 
-cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
+static bool scores_tile_ok(const AttnArgs &a) {
+  return (a.hs == 64 || a.hs == 128) && reinterpret_cast<uintptr_t>(a.keys) % 16 == 0 && a.kv_dim % 4 == 0;
+}
+
+static cudaError_t launch_attention_impl(const AttnArgs &a, const QkvPostArgs *qp, cudaStream_t st) {
   const int maxP = a.positions_dev ? a.max_positions : a.positions;
   if (maxP <= 0) return cudaSuccess;
   const int kvMul = a.heads / a.kv_heads;
-  const bool keys16 = reinterpret_cast<uintptr_t>(a.keys) % 16 == 0 && a.kv_dim % 4 == 0;
-  if ((a.hs == 64 || a.hs == 128) && keys16) {
+  if (scores_tile_ok(a)) {
     const int gpb = kvMul < 8 ? kvMul : 8;
     dim3 g1((maxP + kTileT - 1) / kTileT, a.kv_heads, (kvMul + gpb - 1) / gpb);
-    if (a.hs == 64) launch_k(k_attn_scores_tile<64>, g1, gpb * 32 < 64 ? 64 : gpb * 32, 0, st, a, gpb);
-    else launch_k(k_attn_scores_tile<128>, g1, gpb * 32 < 64 ? 64 : gpb * 32, 0, st, a, gpb);
+    // One warp more than the heads when the kv head's post-processing needs a warp of its own.
+    const int warps = gpb + (qp ? 1 : 0), threads = warps * 32 < 64 ? 64 : warps * 32;
+    const QkvPostArgs none{};
+    if (a.hs == 64) {
+      if (qp) launch_k(k_attn_scores_tile<64, true>, g1, threads, 0, st, a, gpb, *qp);
+      else launch_k(k_attn_scores_tile<64, false>, g1, threads, 0, st, a, gpb, none);
+    } else {
+      if (qp) launch_k(k_attn_scores_tile<128, true>, g1, threads, 0, st, a, gpb, *qp);
+      else launch_k(k_attn_scores_tile<128, false>, g1, threads, 0, st, a, gpb, none);
+    }
   } else {
+    if (qp) {
+      cudaError_t e = launch_qkv_post(*qp, st);
+      if (e != cudaSuccess) return e;
+    }
     dim3 g1((maxP + kScoreWarps - 1) / kScoreWarps, a.kv_heads);
     launch_k(k_attn_scores, g1, kScoreWarps * 32, 0, st, a);
   }
@@ -657,6 +729,12 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     launch_k(k_attn_wsum, (qDim + 127) / 128, 128, 0, st, a);
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) { return launch_attention_impl(a, nullptr, st); }
+
+cudaError_t launch_attention_post(const QkvPostArgs &qp, const AttnArgs &a, cudaStream_t st) {
+  return launch_attention_impl(a, &qp, st);
 }
 
 cudaError_t init_layer_attributes() {

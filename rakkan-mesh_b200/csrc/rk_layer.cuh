@@ -68,6 +68,10 @@ struct QkvPostArgs {
 };
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st);
 
+// launch_qkv_post then launch_attention for the same position, with the
+// post-processing folded into the scores kernel where it tiles the keys.
+cudaError_t launch_attention_post(const QkvPostArgs &qp, const AttnArgs &a, cudaStream_t st);
+
 // Embed (model.go:660-664): x = dequantized row *token_dev of a table.
 cudaError_t launch_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x,
                          cudaStream_t st);

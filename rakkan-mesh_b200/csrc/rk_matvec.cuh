@@ -73,6 +73,7 @@ cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
 
 int matvec_smem_bytes(int fmt, int cols);
 
+
 // Experiment selector (RK_MV_MODE): 0 = quantize in the matvec prologue,
 // 1 = separate multi-CTA quantizer, input staged in shared memory,
 // 2 = separate quantizer, input read from global memory.

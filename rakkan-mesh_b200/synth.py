@@ -85,20 +85,29 @@ def shard_rows(c, nshards, shard):
             "w2": (r * d, d), "w3": (r * h, h), "cls": (r * (c.vocab // G), c.vocab // G)}
 
 
-def layer_vectors(c):
-    """RmsAtt, RmsFfn = 1; biases = 0; QNorm, KNorm = 1."""
+def layer_vectors(c, vec_seed=None):
+    """RmsAtt, RmsFfn = 1; biases = 0; QNorm, KNorm = 1 (the benchmark's
+    choice: BASELINE.json does not give vectors). With vec_seed the tests get
+    seeded non-trivial vectors instead (norm weights 1 + N(0, 0.1), biases
+    N(0, 0.1)), so that every vector's indexing shows in the bits."""
     hs = head_size(c)
-    v = {"rms_att": np.ones(c.dim, np.float32), "rms_ffn": np.ones(c.dim, np.float32)}
+    if vec_seed is None:
+        one = lambda n: np.ones(n, np.float32)
+        zero = lambda n: np.zeros(n, np.float32)
+    else:
+        rng = np.random.default_rng(vec_seed)
+        one = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+        zero = lambda n: (0.1 * rng.standard_normal(n)).astype(np.float32)
+    v = {"rms_att": one(c.dim), "rms_ffn": one(c.dim)}
     if c.qkv_bias:
-        v.update(bq=np.zeros(c.heads * hs, np.float32), bk=np.zeros(c.kv_heads * hs, np.float32),
-                 bv=np.zeros(c.kv_heads * hs, np.float32))
+        v.update(bq=zero(c.heads * hs), bk=zero(c.kv_heads * hs), bv=zero(c.kv_heads * hs))
     if c.qk_norm:
-        v.update(q_norm=np.ones(hs, np.float32), k_norm=np.ones(hs, np.float32))
+        v.update(q_norm=one(hs), k_norm=one(hs))
     return v
 
 
-def host_layer_vectors(c):
-    v = layer_vectors(c)
+def host_layer_vectors(c, vec_seed=None):
+    v = layer_vectors(c, vec_seed)
     hl = rk.HostLayer()
     for k, a in v.items():
         setattr(hl, k, a.ctypes.data)

@@ -28,7 +28,12 @@ VARIANTS = {
     # Widths that are not powers of two: Recip32(float32(n)) of the norms
     # then depends on every bit of the Newton iteration's constants.
     "odd": dict(dim=96, hidden=224, head_dim=24, qk_norm=1),
+    # Head widths of the tiled scores kernel (64, 128), which also does the
+    # bias / QK-norm / RoPE / cache-append work; seeded vectors.
+    "qwen2_hs64": dict(dim=256, heads=4, kv_heads=2, qkv_bias=1, rope_theta=1e6, norm_eps=1e-6),
+    "qwen3_hs128": dict(dim=256, heads=4, kv_heads=2, head_dim=128, qk_norm=1, rope_theta=1e6, norm_eps=1e-6),
 }
+VEC_SEED = {"qwen2_hs64": 101, "qwen3_hs128": 202}
 DTYPES = ["f32", "bf16", "q8_0", "q4_0", "q4_m"]
 
 
@@ -51,10 +56,10 @@ def oracle_weights(om, c):
     return out
 
 
-def upload_layers(dev, c, weights):
+def upload_layers(dev, c, weights, vec_seed=None):
     layers, keep = [], []
     for l in range(c.layers):
-        hl, vec = synth.host_layer_vectors(c)
+        hl, vec = synth.host_layer_vectors(c, None if vec_seed is None else vec_seed + l)
         for k in synth.MATS:
             w, s = weights[(l, k)]
             setattr(hl, k, rk.HostMatrix(synth.mat_fmt(c, k), w.ctypes.data, None if s is None else s.ctypes.data))
@@ -72,9 +77,10 @@ def inputs(c, n, seed):
 @pytest.mark.parametrize("variant", sorted(VARIANTS))
 def test_stage_matches_cpu(dev, variant, dtype):
     c = small_config(dtype, **VARIANTS[variant])
-    om = ro.OracleModel(c, seed=11)
+    vs = VEC_SEED.get(variant)
+    om = ro.OracleModel(c, seed=11, vec_seed=vs)
     weights = oracle_weights(om, c)
-    layers = upload_layers(dev, c, weights)
+    layers = upload_layers(dev, c, weights, vs)
     st = rk.Stage(dev, c, layers, c.seq_len)
     try:
         xs = inputs(c, 76, 5)
