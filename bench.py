@@ -335,6 +335,8 @@ def main():
     if rank == 0:
         cfg = workload(args)
         cfg["parallelism"] = f"rows{world}" if sharded else (f"replicas{world}" if world > 1 else "none")
+        if sharded:
+            cfg["gathers"] = "fused (NVLink stores + flags)" if dm.stage.fused_gathers() else "NCCL all-gather"
         line = {
             "metric": METRIC, "value": seqs * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,

@@ -265,6 +265,11 @@ int rk_layer_from_device_shard(rk_device *d, const rk_config *c, int nshards, in
  * model built on it, run collectively on every rank. */
 int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *g,
                        rk_stage **out);
+/* 1 when the stage's gathers are fused into its kernels (NVLink stores into
+ * the peers' buffers through CUDA IPC, a flag per gather point); 0 when they
+ * are NCCL all-gathers (peers not reachable by P2P, RK_GATHER=nccl, or an
+ * unsharded stage). */
+int rk_stage_fused_gathers(const rk_stage *s);
 /* A head whose classifier holds the rank's vocab/G rows; logits are whole. */
 int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *g,
                       rk_head **out);

@@ -478,6 +478,8 @@ struct Pro {
   int pro = PRO_GIVEN;
   const float *norm_w = nullptr;
   float recipN = 0.0f, eps = 0.0f;
+  GatherPut put{};    // fused gather of the output (row sharding)
+  GatherWait wait{};  // the input is a fused gather's
 };
 
 // Enqueues products of matrices (same cols) sharing one input, grouping
@@ -502,6 +504,8 @@ static int enqueue_matvecs(rk_device *d, int n, rk_matrix *const *ms, float *con
       a.norm_w = pro.norm_w;
       a.recipN = pro.recipN;
       a.eps = pro.eps;
+      a.put = pro.put;
+      a.wait = pro.wait;
     }
     int np = 0;
     while (i < n && np < 4 && ms[i]->fmt == a.fmt) {
@@ -1175,6 +1179,13 @@ struct rk_stage {
   // Row sharding (layer_dims): this process's rank of G; null/1 unsharded.
   rk_group *grp = nullptr;
   int G = 1, rank = 0;
+  // The fused gathers (p2p): x, attOut, hb, the gather points' flags
+  // [layers·4][G], the producers' CTA counters and the step epoch live in
+  // one allocation `xbase`, mapped by every peer through CUDA IPC.
+  int p2p = 0;
+  char *xbase = nullptr;
+  size_t off_flags = 0, off_cnt = 0, off_epoch = 0;
+  char *peer_base[kMaxPeers] = {};  // by rank; this rank's entry is xbase
 };
 
 static int stage_alloc(rk_stage *s, size_t bytes, void **p) {
@@ -1192,6 +1203,8 @@ static void stage_release(rk_stage *s) {
   cudaSetDevice(s->d->ordinal);
   cudaStreamSynchronize(s->d->st);
   if (s->graph) cudaGraphExecDestroy(s->graph);
+  for (int g = 0; g < s->G && g < kMaxPeers; g++)
+    if (s->peer_base[g] && s->peer_base[g] != s->xbase) cudaIpcCloseMemHandle(s->peer_base[g]);
   for (void *p : s->allocs) cudaFree(p);
   cudaFreeHost(s->pin_io);
   s->d->used -= s->bytes;
@@ -1224,6 +1237,14 @@ static float host_recip32(float x) {
   return r * ldexpf(1.0f, -e);
 }
 
+// Advances a sharded stage's step epoch (the value its fused gathers' flags
+// are raised to).
+__global__ void k_epoch(unsigned *epoch) {
+  griddep_trigger();
+  griddep_wait();
+  if (threadIdx.x == 0) *epoch += 1;
+}
+
 // Records one position's pass through the stage's layers (gpustage.go:119-152
 // in the order of Stage.Forward, model.go:537-611), reading the position
 // from s->pos_dev. x is s->x.
@@ -1236,6 +1257,36 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   const int G = s->G, heads_l = c->heads / G, kvh_l = c->kv_heads / G;
   const int h0 = s->rank * heads_l, kv0 = s->rank * kvh_l, r0 = s->rank * (D / G), rH0 = s->rank * (H / G);
   auto gather = [&](float *buf, int total) -> int { return G > 1 ? group_gather(s->grp, buf, total / G, st) : RK_OK; };
+  // Fused gathers (p2p): gather point slot = layer·4 + {0: attOut, 1: x
+  // after Wo, 2: hb, 3: x after W2}. A point is fused when its producer
+  // and consumer kernels both take part (quantized products that quantize
+  // their own input, the single-kernel attention); the last layer's x
+  // stays an NCCL all-gather, so whatever reads the stage's output needs
+  // no flag.
+  unsigned *epoch = s->p2p ? (unsigned *)(s->xbase + s->off_epoch) : nullptr;
+  auto put_for = [&](int slot, const float *out_local) {
+    GatherPut gp{};
+    const size_t off = (const char *)out_local - s->xbase;
+    for (int g = 0; g < G; g++) {
+      if (g != s->rank) gp.peer_out[gp.nout++] = (float *)(s->peer_base[g] + off);
+      gp.flag[gp.nflag++] = (unsigned *)(s->peer_base[g] + s->off_flags) + (size_t)slot * G + s->rank;
+    }
+    gp.counter = (unsigned *)(s->xbase + s->off_cnt) + slot;
+    gp.epoch = epoch;
+    return gp;
+  };
+  auto wait_for = [&](int slot) {
+    GatherWait w{};
+    w.n = G;
+    w.flags = (unsigned *)(s->xbase + s->off_flags) + (size_t)slot * G;
+    w.epoch = epoch;
+    return w;
+  };
+  auto fusable = [&](const rk_matrix *producer, const rk_matrix *consumer, int cols, bool norm) {
+    return s->p2p && mv_mode() == 0 && quantized_fmt(producer->fmt) && quantized_fmt(consumer->fmt) &&
+           matvec_fused_ok(consumer->fmt, cols, norm);
+  };
+  if (s->p2p) CK(launch_k(k_epoch, 1, 32, 0, st, epoch));
   const float eps = cfg_eps(c);
   const float recipD = host_recip32((float)D), recipHS = host_recip32((float)hs);
   const float invSqrt = (float)(1 / sqrt((double)hs));
@@ -1244,7 +1295,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   // quantize launch fills the stage's scratch first. Float matrices get the
   // normalised input in xb.
   auto products = [&](int n, rk_matrix *const *ms, float *const *outs, const float *x, const float *norm_w, int cols,
-                      int epi) -> int {
+                      int epi, const GatherPut *put = nullptr, const GatherWait *wait = nullptr) -> int {
     const float recip = host_recip32((float)cols);
     if (quantized_fmt(ms[0]->fmt)) {
       if (mv_mode() != 0) {
@@ -1257,6 +1308,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
         p.norm_w = norm_w;
         p.recipN = recip;
         p.eps = eps;
+        if (put) p.put = *put;
+        if (wait) p.wait = *wait;
         return enqueue_matvecs(d, n, ms, outs, x, nullptr, nullptr, nullptr, epi, st, p);
       }
       CK(launch_quantize_act(x, cols, norm_w, recip, eps, nullptr, s->qx, s->xs, s->xsum, st));
@@ -1275,7 +1328,15 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     // q, k, v = Wq·xb, Wk·xb, Wv·xb with xb = rmsNorm(x, RmsAtt) (model.go:538-539).
     rk_matrix *qkv[3] = {l->wq, l->wk, l->wv};
     float *qkv_out[3] = {s->q, s->k, s->v};
-    int rc = products(3, qkv, qkv_out, s->x, vec + l->o_rms_att, D, EPI_STORE);
+    const int sl = 4 * (int)li;
+    rk_layer *next = li + 1 < s->layers.size() ? s->layers[li + 1] : nullptr;
+    const bool f_att = s->p2p && s->v_pitch > 0 && fusable(l->wo, l->wo, qd, false);
+    const bool f_x1 = fusable(l->wo, l->w1, D, true);
+    const bool f_hb = fusable(l->w1, l->w2, H, false);
+    const bool f_x2 = next && fusable(l->w2, next->wq, D, true);
+    const bool f_prev = li > 0 && fusable(s->layers[li - 1]->w2, l->wq, D, true);
+    const GatherWait w_prev = f_prev ? wait_for(sl - 1) : GatherWait{};
+    int rc = products(3, qkv, qkv_out, s->x, vec + l->o_rms_att, D, EPI_STORE, nullptr, &w_prev);
     if (rc) return rc;
     // Bias, QK-norm, RoPE, cache append (model.go:542-568).
     QkvPostArgs qp{};
@@ -1321,14 +1382,17 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.att_stride = s->att_stride;
     at.inv_sqrt = invSqrt;
     at.err = s->d->err_dev;
+    if (f_att) at.put = put_for(sl, at.out);
     CK(launch_attention_post(qp, at, st));
-    if ((rc = gather(s->att_out, qd))) return rc;
+    if (!f_att && (rc = gather(s->att_out, qd))) return rc;
     // x += Wo·attOut (model.go:588-594).
     {
       float *xo = s->x + r0;
-      if ((rc = products(1, &l->wo, &xo, s->att_out, nullptr, qd, EPI_ADD))) return rc;
+      const GatherPut p1 = f_x1 ? put_for(sl + 1, xo) : GatherPut{};
+      const GatherWait w0 = f_att ? wait_for(sl) : GatherWait{};
+      if ((rc = products(1, &l->wo, &xo, s->att_out, nullptr, qd, EPI_ADD, &p1, &w0))) return rc;
     }
-    if ((rc = gather(s->x, D))) return rc;
+    if (!f_x1 && (rc = gather(s->x, D))) return rc;
     // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603):
     // row i of W1 and of W3 in one warp, SiLU·mul as the epilogue.
     {
@@ -1347,6 +1411,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
         a.norm_w = norm_w;
         a.recipN = recipD;
         a.eps = eps;
+        if (f_x1) a.wait = wait_for(sl + 1);
+        if (f_hb) a.put = put_for(sl + 2, s->hb + rH0);
       } else if (quantized_fmt(a.fmt)) {
         CK(launch_quantize_act(s->x, D, norm_w, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
         a.qx = s->qx;
@@ -1358,13 +1424,15 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
       }
       CK(launch_mv(d, a, st));
     }
-    if ((rc = gather(s->hb, H))) return rc;
+    if (!f_hb && (rc = gather(s->hb, H))) return rc;
     // x = Canonical(x + W2·hb) (model.go:604-610).
     {
       float *xo = s->x + r0;
-      if ((rc = products(1, &l->w2, &xo, s->hb, nullptr, H, EPI_ADD_CANON))) return rc;
+      const GatherPut p3 = f_x2 ? put_for(sl + 3, xo) : GatherPut{};
+      const GatherWait w2 = f_hb ? wait_for(sl + 2) : GatherWait{};
+      if ((rc = products(1, &l->w2, &xo, s->hb, nullptr, H, EPI_ADD_CANON, &p3, &w2))) return rc;
     }
-    if ((rc = gather(s->x, D))) return rc;
+    if (!f_x2 && (rc = gather(s->x, D))) return rc;
   }
   return RK_OK;
 }
@@ -1410,6 +1478,84 @@ static int capture(rk_device *d, std::function<int(cudaStream_t)> rec, cudaGraph
   return RK_OK;
 }
 
+// Maps every peer's exchange block (CUDA IPC; the handles and device
+// ordinals travel through the group) when every peer is reachable by P2P,
+// so that the stage's gathers can be fused into its kernels; otherwise (or
+// with RK_GATHER=nccl) they stay NCCL all-gathers. Collective.
+static int stage_p2p_setup(rk_stage *s) {
+  const int G = s->G;
+  s->peer_base[s->rank] = s->xbase;
+  if (G > kMaxPeers) return RK_OK;
+  const char *env = getenv("RK_GATHER");
+  const bool want = !(env && strcmp(env, "nccl") == 0);
+  struct Entry {
+    cudaIpcMemHandle_t h;
+    int ordinal, ok, pad[2];
+  };
+  static_assert(sizeof(Entry) % 4 == 0, "entry");
+  constexpr int kFloats = sizeof(Entry) / 4;
+  Entry mine{};
+  mine.ordinal = s->d->ordinal;
+  mine.ok = want && cudaIpcGetMemHandle(&mine.h, s->xbase) == cudaSuccess;
+  cudaGetLastError();
+  float *buf = nullptr;
+  std::vector<Entry> all(G);
+  CK(cudaMalloc(&buf, sizeof(Entry) * G));
+  cudaError_t e = cudaMemcpy(buf + s->rank * kFloats, &mine, sizeof mine, cudaMemcpyHostToDevice);
+  int rc = e == cudaSuccess ? group_gather(s->grp, buf, kFloats, s->d->st) : cuda_fail(e, "peer exchange");
+  if (!rc) {
+    e = cudaStreamSynchronize(s->d->st);
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), buf, sizeof(Entry) * G, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = cuda_fail(e, "peer exchange");
+  }
+  cudaFree(buf);
+  if (rc) return rc;
+  bool ok = true;
+  for (int g = 0; g < G; g++) {
+    int can = 0;
+    ok = ok && all[g].ok;
+    if (g != s->rank && ok) ok = cudaDeviceCanAccessPeer(&can, s->d->ordinal, all[g].ordinal) == cudaSuccess && can;
+  }
+  // Every rank decides alike: all must have published a handle and see all peers.
+  for (int g = 0; g < G && ok; g++) {
+    if (g == s->rank) continue;
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[g].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = false;
+      break;
+    }
+    s->peer_base[g] = (char *)p;
+  }
+  // Agree: fused gathers only if every rank mapped every peer.
+  {
+    float *fl = nullptr;
+    std::vector<float> oks(G);
+    const float me = ok ? 1.0f : 0.0f;
+    CK(cudaMalloc(&fl, 4 * G));
+    e = cudaMemcpy(fl + s->rank, &me, 4, cudaMemcpyHostToDevice);
+    rc = e == cudaSuccess ? group_gather(s->grp, fl, 1, s->d->st) : cuda_fail(e, "peer agreement");
+    if (!rc) {
+      e = cudaStreamSynchronize(s->d->st);
+      if (e == cudaSuccess) e = cudaMemcpy(oks.data(), fl, 4 * G, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) rc = cuda_fail(e, "peer agreement");
+    }
+    cudaFree(fl);
+    if (rc) return rc;
+    for (int g = 0; g < G; g++) ok = ok && oks[g] == 1.0f;
+  }
+  if (!ok) {
+    for (int g = 0; g < G; g++)
+      if (g != s->rank && s->peer_base[g]) {
+        cudaIpcCloseMemHandle(s->peer_base[g]);
+        s->peer_base[g] = nullptr;
+      }
+    cudaGetLastError();
+  }
+  s->p2p = ok ? 1 : 0;
+  return RK_OK;
+}
+
 static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *grp,
                      rk_stage **out) {
   if (!d || !c || !out || n < 0 || (n > 0 && !layers) || ctx <= 0) return fail(RK_ERR_ARGS, "bad argument");
@@ -1445,13 +1591,28 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     if ((rc = A((bytes), &p))) goto fail_;    \
     s->field = (decltype(s->field))p;         \
   } while (0)
-  ALLOC(x, 4 * (size_t)D);
+  if (G > 1) {
+    // The gathered activations, flags, counters and epoch in one block.
+    const int nslots = 4 * n;
+    auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
+    const size_t ox = 0, oatt = ox + a16(4 * (size_t)D), ohb = oatt + a16(4 * (size_t)qd);
+    s->off_flags = ohb + a16(4 * (size_t)H);
+    s->off_cnt = s->off_flags + a16(4 * (size_t)nslots * G);
+    s->off_epoch = s->off_cnt + a16(4 * (size_t)nslots);
+    if ((rc = A(s->off_epoch + 16, &p))) goto fail_;
+    s->xbase = (char *)p;
+    s->x = (float *)(s->xbase + ox);
+    s->att_out = (float *)(s->xbase + oatt);
+    s->hb = (float *)(s->xbase + ohb);
+  } else {
+    ALLOC(x, 4 * (size_t)D);
+    ALLOC(att_out, 4 * (size_t)qd);
+    ALLOC(hb, 4 * (size_t)H);
+  }
   ALLOC(xb, 4 * (size_t)D);
   ALLOC(q, 4 * (size_t)(qd / G));
   ALLOC(k, 4 * (size_t)kvd);
   ALLOC(v, 4 * (size_t)kvd);
-  ALLOC(att_out, 4 * (size_t)qd);
-  ALLOC(hb, 4 * (size_t)H);
   ALLOC(hb2, 4 * (size_t)H);
   s->att_stride = (ctx + 3) & ~3;
   s->v_pitch = attention_fused_ok(c->heads / G, c->kv_heads / G, hs, ctx) ? s->att_stride : 0;
@@ -1485,6 +1646,7 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
       goto fail_;
     }
   }
+  if (G > 1 && (rc = stage_p2p_setup(s))) goto fail_;
   d->used += s->bytes;
   rc = capture(
       d,
@@ -1513,6 +1675,8 @@ fail_:
 extern "C" int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_stage **out) {
   return stage_new(d, c, layers, n, ctx, nullptr, out);
 }
+
+extern "C" int rk_stage_fused_gathers(const rk_stage *s) { return s && s->G > 1 ? s->p2p : 0; }
 
 extern "C" int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx,
                                   rk_group *g, rk_stage **out) {

@@ -204,6 +204,54 @@ RK_DEV uint64_t globaltimer_ns() {
   return t;
 }
 
+// System-scope acquire load / release store of a 32-bit flag (flags that
+// other GPUs write over NVLink, or that this GPU writes in their memory).
+RK_DEV unsigned ld_acquire_sys(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+RK_DEV void st_release_sys(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits (thread 0 of the CTA spins, then a CTA barrier) until each of n
+// flags holds the step's epoch; false after about a second.
+RK_DEV bool gather_wait(const unsigned *flags, int n, const unsigned *epoch_p) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const unsigned epoch = *epoch_p;
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int g = 0; g < n && ok; g++)
+      while (ld_acquire_sys(flags + g) != epoch)
+        if (globaltimer_ns() - t0 > 1000000000ull) {
+          ok = 0;
+          break;
+        }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// The end of a producer CTA of a fused gather: once every CTA's peer stores
+// are visible system-wide, the last CTA raises this rank's flag in every
+// peer's memory to the step's epoch.
+RK_DEV void gather_done(unsigned *counter, unsigned *const *flag, int nflag, const unsigned *epoch_p) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned done = atomicAdd(counter, 1u);
+    if (done == gridDim.x * gridDim.y * gridDim.z - 1) {
+      *counter = 0;
+      __threadfence_system();
+      const unsigned epoch = *epoch_p;
+      for (int g = 0; g < nflag; g++) st_release_sys(flag[g], epoch);
+    }
+  }
+}
+
 // Whether launches on this host thread use programmatic dependent launch
 // (set while a decode step is being recorded into a CUDA graph).
 inline thread_local bool g_pdl = false;

@@ -618,7 +618,7 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   }
   __syncthreads();
   // 5. weighted values: thread (head h, element d).
-  if (threadIdx.x >= gpb * kFsSlice) return;
+  if (threadIdx.x < gpb * kFsSlice) {
   const int h = threadIdx.x / kFsSlice, d = threadIdx.x % kFsSlice;
   const float *w = sE + (size_t)h * ppad;
   const float *v = sV + (size_t)d * vpad;
@@ -653,7 +653,11 @@ __global__ void __launch_bounds__(kFsMaxThreads)
     }
   }
   for (int t = P16; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t]));
-  a.out[(hbase + h) * a.hs + slice * kFsSlice + d] = acc;
+  const int o = (hbase + h) * a.hs + slice * kFsSlice + d;
+  a.out[o] = acc;
+  for (int g = 0; g < a.put.nout; g++) a.put.peer_out[g][o] = acc;
+  }
+  if (a.put.nflag > 0) gather_done(a.put.counter, a.put.flag, a.put.nflag, a.put.epoch);
 }
 
 // Shared memory of k_attn_softmax_wsum for gpb heads of up to maxP

@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "rk_matvec.cuh"
+
 namespace rk {
 
 // RMSNorm of `segs` segments of n floats, `stride` apart (batch.go:285-287):
@@ -43,6 +45,9 @@ struct AttnArgs {
   int heads, kv_heads, hs, kv_dim, att_stride;
   float inv_sqrt;
   int *err;  // device error word for a pipeline wait that timed out
+  // Row sharding: the output rows also go to the peers (out's offset), and
+  // the gather point's flag is raised when the kernel is done.
+  GatherPut put;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 // Whether launch_attention serves heads/kv_heads/hs over up to max_positions

@@ -511,6 +511,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     }
   }
   griddep_wait();
+  if (a.wait.n > 0 && !gather_wait(a.wait.flags, a.wait.n, a.wait.epoch) && threadIdx.x == 0)
+    atomicExch(a.err, DEV_ERR_TIMEOUT);
   // The input's loads go first, ahead of the weight ring's copies.
   const bool norm = a.pro == PRO_NORM_QUANT;
   float *stage = reinterpret_cast<float *>(p);
@@ -556,7 +558,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
         if (js == 0) jp ^= 1;
         mbar_wait_bounded(bar0 + 8 * js, jp);
       }
-      return;
+      break;  // (not return: a gathering CTA still meets its barrier below)
     }
     const SegInfo s = seg_info<FMT>(a, nb, cc);
     const uint8_t *W = ring + slot * slot_bytes<FMT>();
@@ -588,14 +590,26 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
       const float r = combine8(acc);
       if (lane == 0) {
         float *out = a.part[cc.part].out;
+        float v = r;
+        bool put = true;
         switch (a.epi) {
-          case EPI_STORE: out[cc.row] = r; break;
-          case EPI_ADD: out[cc.row] = __fadd_rn(out[cc.row], r); break;
-          case EPI_ADD_CANON: out[cc.row] = canonical(__fadd_rn(out[cc.row], r)); break;
+          case EPI_STORE: break;
+          case EPI_ADD: v = __fadd_rn(out[cc.row], r); break;
+          case EPI_ADD_CANON: v = canonical(__fadd_rn(out[cc.row], r)); break;
           case EPI_SILU:
-            if (cc.sub == 0) r0 = r;
-            else a.part[0].out[cc.row] = __fmul_rn(silu(r0), r);
+            if (cc.sub == 0) {
+              r0 = r;
+              put = false;
+            } else {
+              v = __fmul_rn(silu(r0), r);
+              out = a.part[0].out;
+            }
             break;
+        }
+        if (put) {
+          out[cc.row] = v;
+          if (cc.part == 0 || a.epi == EPI_SILU)
+            for (int g = 0; g < a.put.nout; g++) a.put.peer_out[g][cc.row] = v;
         }
       }
     }
@@ -605,6 +619,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     slot = slot + 1 == SLOTS ? 0 : slot + 1;
     if (slot == 0) parity ^= 1;
   }
+  if (a.put.nflag > 0) gather_done(a.put.counter, a.put.flag, a.put.nflag, a.put.epoch);
 }
 
 // ---------------------------------------------------------------------------

@@ -19,6 +19,28 @@ enum Epi : int {
 // Device error codes written to the device's error word.
 enum DevErr : int { DEV_OK = 0, DEV_ERR_TIMEOUT = 1 };
 
+// Row sharding's all-gather, fused into the kernels (one process per GPU,
+// peers' buffers mapped through CUDA IPC). A producer kernel stores each
+// output row into every peer's copy of the output as well as its own; when
+// its last CTA is done it raises, in every peer's memory, the flag of this
+// gather point to the step's epoch. A consumer kernel waits, after its
+// dependency wait, for its peers' flags of the gather point it reads. All
+// waits are bounded (about a second, then the device error word is set).
+constexpr int kMaxPeers = 8;
+struct GatherPut {
+  int nout;                         // peers to store into (0: no gather)
+  float *peer_out[kMaxPeers];       // peers' copies of the output (same offset as part[0].out)
+  int nflag;                        // flags to raise: every rank's, this one's included
+  unsigned *flag[kMaxPeers];        // this rank's flag of the gather point, in each rank's memory
+  unsigned *counter;                // local: CTAs done (reset by the last)
+  const unsigned *epoch;            // the step's epoch (local)
+};
+struct GatherWait {
+  int n;                            // 0: nothing to wait for
+  const unsigned *flags;            // local: the peers' flags of the gather point
+  const unsigned *epoch;
+};
+
 struct MvPart {
   const uint8_t *w;  // row-major weights: Q8 cols bytes/row, Q4 cols/2, F32 4·cols, BF16 2·cols
   const float *s;    // row-major scales [rows][cols/32] (quantized formats)
@@ -48,6 +70,8 @@ struct MvArgs {
   int pro;
   const float *norm_w;
   float recipN, eps;
+  GatherPut put;    // part[0]'s output rows also go to the peers
+  GatherWait wait;  // the input comes from a gather
 };
 
 enum Prologue : int { PRO_GIVEN = 0, PRO_QUANT = 1, PRO_NORM_QUANT = 2 };

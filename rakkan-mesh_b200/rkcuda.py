@@ -35,7 +35,7 @@ EXPORTS = [
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
     "rk_bench_matvec", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
     "rk_group_size", "rk_group_all_gather", "rk_layer_upload_shard", "rk_layer_from_device_shard",
-    "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
+    "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
 ]
 
 
@@ -124,7 +124,7 @@ def lib():
             "rk_layer_upload_shard": (i, [vp, vp, i, i, vp, vp]),
             "rk_layer_from_device_shard": (i, [vp, vp, i, i, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
             "rk_stage_new_group": (i, [vp, vp, vp, i, i, vp, vp]),
-            "rk_head_new_group": (i, [vp, vp, vp, vp, vp, vp]),
+            "rk_head_new_group": (i, [vp, vp, vp, vp, vp, vp]), "rk_stage_fused_gathers": (i, [vp]),
             "rk_matrix_generate_rows": (i, [vp, i, i, i, i, i, u64, u64, f, vp]),
             "rk_model_kernel_count": (i, [vp, vp]), "rk_model_profile": (i, [vp, i, i, vp]),
             "rk_stage_fill_cache": (i, [vp, i, u64]),
@@ -400,6 +400,11 @@ class Stage:
 
     def positions(self):
         return lib().rk_stage_positions(self.h)
+
+    def fused_gathers(self):
+        """1 when a sharded stage exchanges activations by NVLink stores and
+        flags inside its kernels, 0 for NCCL all-gathers (or unsharded)."""
+        return lib().rk_stage_fused_gathers(self.h)
 
     def fill_cache(self, positions, seed):
         _check(lib().rk_stage_fill_cache(self.h, positions, seed))

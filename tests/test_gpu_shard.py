@@ -35,7 +35,7 @@ def _rank(rank, world, gid, dtype, variant, out):
         grp = rk.Group(dev, world, rank, gid)
         dm = synth.DeviceModel(dev, c, SEED, ctx=CTX, group=grp)
         toks, logits = dm.model.generate(np.array(PROMPT, np.int32), N_NEW, want_logits=True)
-        out.put((rank, toks, logits, dev.used() > 0))
+        out.put((rank, toks, logits, dm.stage.fused_gathers()))
         dm.free()
         grp.free()
         dev.close()
@@ -55,10 +55,11 @@ def test_row_sharded_decode_matches_oracle(dtype, variant):
     procs = [ctx.Process(target=_rank, args=(r, 2, gid, dtype, variant, out)) for r in range(2)]
     for p in procs:
         p.start()
-    res = {}
+    res, fused = {}, {}
     for _ in procs:
-        r, toks, logits, _used = out.get(timeout=600)
+        r, toks, logits, f = out.get(timeout=600)
         res[r] = (toks, logits)
+        fused[r] = f
     for p in procs:
         p.join(timeout=120)
     for r in (0, 1):
@@ -70,3 +71,7 @@ def test_row_sharded_decode_matches_oracle(dtype, variant):
         toks, logits = res[r]
         assert list(toks) == list(want_toks)
         same_bits(logits, want_logits)
+    # Two GPUs of one box reach each other over NVLink: the gathers are fused
+    # unless the run asks for NCCL.
+    import os
+    assert fused[0] == fused[1] == (0 if os.environ.get("RK_GATHER") == "nccl" else 1)
