@@ -1179,12 +1179,12 @@ struct rk_stage {
   // Row sharding (layer_dims): this process's rank of G; null/1 unsharded.
   rk_group *grp = nullptr;
   int G = 1, rank = 0;
-  // The fused gathers (p2p): x, attOut, hb, the gather points' flags
-  // [layers·4][G], the producers' CTA counters and the step epoch live in
-  // one allocation `xbase`, mapped by every peer through CUDA IPC.
+  // The fused gathers (p2p): x, attOut and hb, their tagged copies (8-byte
+  // words: value and tag) and the step epoch live in one allocation
+  // `xbase`, mapped by every peer through CUDA IPC.
   int p2p = 0;
   char *xbase = nullptr;
-  size_t off_flags = 0, off_cnt = 0, off_epoch = 0;
+  size_t off_xll = 0, off_attll = 0, off_hbll = 0, off_epoch = 0;
   char *peer_base[kMaxPeers] = {};  // by rank; this rank's entry is xbase
 };
 
@@ -1237,8 +1237,8 @@ static float host_recip32(float x) {
   return r * ldexpf(1.0f, -e);
 }
 
-// Advances a sharded stage's step epoch (the value its fused gathers' flags
-// are raised to).
+// Advances a sharded stage's step epoch (the step number in the tags of its
+// fused gathers' words).
 __global__ void k_epoch(unsigned *epoch) {
   griddep_trigger();
   griddep_wait();
@@ -1261,30 +1261,33 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   // after Wo, 2: hb, 3: x after W2}. A point is fused when its producer
   // and consumer kernels both take part (quantized products that quantize
   // their own input, the single-kernel attention); the last layer's x
-  // stays an NCCL all-gather, so whatever reads the stage's output needs
-  // no flag.
+  // stays an NCCL all-gather, so whatever reads the stage's output reads
+  // plain floats.
   unsigned *epoch = s->p2p ? (unsigned *)(s->xbase + s->off_epoch) : nullptr;
-  auto put_for = [&](int slot, const float *out_local) {
+  const int nslots = 4 * (int)s->layers.size();
+  // The tagged copy of a vector (off_ll: its offset in the block) from
+  // element `elem` on, in every rank's memory.
+  auto put_for = [&](int slot, size_t off_ll, size_t elem) {
     GatherPut gp{};
-    const size_t off = (const char *)out_local - s->xbase;
-    for (int g = 0; g < G; g++) {
-      if (g != s->rank) gp.peer_out[gp.nout++] = (float *)(s->peer_base[g] + off);
-      gp.flag[gp.nflag++] = (unsigned *)(s->peer_base[g] + s->off_flags) + (size_t)slot * G + s->rank;
-    }
-    gp.counter = (unsigned *)(s->xbase + s->off_cnt) + slot;
+    for (int g = 0; g < G; g++)
+      gp.ll[gp.nll++] = (unsigned long long *)(s->peer_base[g] + off_ll) + elem;
     gp.epoch = epoch;
+    gp.slot = slot;
+    gp.nslots = nslots;
     return gp;
   };
-  auto wait_for = [&](int slot) {
+  auto wait_for = [&](int slot, size_t off_ll) {
     GatherWait w{};
-    w.n = G;
-    w.flags = (unsigned *)(s->xbase + s->off_flags) + (size_t)slot * G;
+    w.ll = (const unsigned long long *)(s->xbase + off_ll);
     w.epoch = epoch;
+    w.slot = slot;
+    w.nslots = nslots;
     return w;
   };
+  // A consumer reads a gathered input in one chunk of its prologue.
   auto fusable = [&](const rk_matrix *producer, const rk_matrix *consumer, int cols, bool norm) {
-    return s->p2p && mv_mode() == 0 && quantized_fmt(producer->fmt) && quantized_fmt(consumer->fmt) &&
-           matvec_fused_ok(consumer->fmt, cols, norm);
+    return s->p2p && quantized_fmt(producer->fmt) && quantized_fmt(consumer->fmt) &&
+           matvec_fused_ok(consumer->fmt, cols, norm) && cols <= (norm ? 8192 : 16384);
   };
   if (s->p2p) CK(launch_k(k_epoch, 1, 32, 0, st, epoch));
   const float eps = cfg_eps(c);
@@ -1298,10 +1301,6 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
                       int epi, const GatherPut *put = nullptr, const GatherWait *wait = nullptr) -> int {
     const float recip = host_recip32((float)cols);
     if (quantized_fmt(ms[0]->fmt)) {
-      if (mv_mode() != 0) {
-        CK(launch_quantize_wide(x, cols, norm_w, recip, eps, nullptr, s->qx, s->xs, s->xsum, st));
-        return enqueue_matvecs(d, n, ms, outs, x, s->qx, s->xs, s->xsum, epi, st);
-      }
       if (matvec_fused_ok(ms[0]->fmt, cols, norm_w != nullptr)) {
         Pro p;
         p.pro = norm_w ? PRO_NORM_QUANT : PRO_QUANT;
@@ -1332,10 +1331,14 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     rk_layer *next = li + 1 < s->layers.size() ? s->layers[li + 1] : nullptr;
     const bool f_att = s->p2p && s->v_pitch > 0 && fusable(l->wo, l->wo, qd, false);
     const bool f_x1 = fusable(l->wo, l->w1, D, true);
-    const bool f_hb = fusable(l->w1, l->w2, H, false);
+    // The W1·W3 kernel reads x's tagged words and writes hb's; the peers
+    // overwrite x's words (after W2) once they hold every hb row. That is
+    // safe only when each of its CTAs owns a row, i.e. has finished reading
+    // x before any peer can move on; otherwise hb goes through NCCL.
+    const bool f_hb = fusable(l->w1, l->w2, H, false) && l->w1->rows >= d->sms;
     const bool f_x2 = next && fusable(l->w2, next->wq, D, true);
     const bool f_prev = li > 0 && fusable(s->layers[li - 1]->w2, l->wq, D, true);
-    const GatherWait w_prev = f_prev ? wait_for(sl - 1) : GatherWait{};
+    const GatherWait w_prev = f_prev ? wait_for(sl - 1, s->off_xll) : GatherWait{};
     int rc = products(3, qkv, qkv_out, s->x, vec + l->o_rms_att, D, EPI_STORE, nullptr, &w_prev);
     if (rc) return rc;
     // Bias, QK-norm, RoPE, cache append (model.go:542-568).
@@ -1382,14 +1385,14 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     at.att_stride = s->att_stride;
     at.inv_sqrt = invSqrt;
     at.err = s->d->err_dev;
-    if (f_att) at.put = put_for(sl, at.out);
+    if (f_att) at.put = put_for(sl, s->off_attll, (size_t)h0 * hs);
     CK(launch_attention_post(qp, at, st));
     if (!f_att && (rc = gather(s->att_out, qd))) return rc;
     // x += Wo·attOut (model.go:588-594).
     {
       float *xo = s->x + r0;
-      const GatherPut p1 = f_x1 ? put_for(sl + 1, xo) : GatherPut{};
-      const GatherWait w0 = f_att ? wait_for(sl) : GatherWait{};
+      const GatherPut p1 = f_x1 ? put_for(sl + 1, s->off_xll, r0) : GatherPut{};
+      const GatherWait w0 = f_att ? wait_for(sl, s->off_attll) : GatherWait{};
       if ((rc = products(1, &l->wo, &xo, s->att_out, nullptr, qd, EPI_ADD, &p1, &w0))) return rc;
     }
     if (!f_x1 && (rc = gather(s->x, D))) return rc;
@@ -1411,8 +1414,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
         a.norm_w = norm_w;
         a.recipN = recipD;
         a.eps = eps;
-        if (f_x1) a.wait = wait_for(sl + 1);
-        if (f_hb) a.put = put_for(sl + 2, s->hb + rH0);
+        if (f_x1) a.wait = wait_for(sl + 1, s->off_xll);
+        if (f_hb) a.put = put_for(sl + 2, s->off_hbll, rH0);
       } else if (quantized_fmt(a.fmt)) {
         CK(launch_quantize_act(s->x, D, norm_w, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
         a.qx = s->qx;
@@ -1428,8 +1431,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     // x = Canonical(x + W2·hb) (model.go:604-610).
     {
       float *xo = s->x + r0;
-      const GatherPut p3 = f_x2 ? put_for(sl + 3, xo) : GatherPut{};
-      const GatherWait w2 = f_hb ? wait_for(sl + 2) : GatherWait{};
+      const GatherPut p3 = f_x2 ? put_for(sl + 3, s->off_xll, r0) : GatherPut{};
+      const GatherWait w2 = f_hb ? wait_for(sl + 2, s->off_hbll) : GatherWait{};
       if ((rc = products(1, &l->w2, &xo, s->hb, nullptr, H, EPI_ADD_CANON, &p3, &w2))) return rc;
     }
     if (!f_x2 && (rc = gather(s->x, D))) return rc;
@@ -1592,13 +1595,13 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     s->field = (decltype(s->field))p;         \
   } while (0)
   if (G > 1) {
-    // The gathered activations, flags, counters and epoch in one block.
-    const int nslots = 4 * n;
+    // The gathered activations, their tagged copies and the epoch in one block.
     auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
     const size_t ox = 0, oatt = ox + a16(4 * (size_t)D), ohb = oatt + a16(4 * (size_t)qd);
-    s->off_flags = ohb + a16(4 * (size_t)H);
-    s->off_cnt = s->off_flags + a16(4 * (size_t)nslots * G);
-    s->off_epoch = s->off_cnt + a16(4 * (size_t)nslots);
+    s->off_xll = ohb + a16(4 * (size_t)H);
+    s->off_attll = s->off_xll + a16(8 * (size_t)D);
+    s->off_hbll = s->off_attll + a16(8 * (size_t)qd);
+    s->off_epoch = s->off_hbll + a16(8 * (size_t)H);
     if ((rc = A(s->off_epoch + 16, &p))) goto fail_;
     s->xbase = (char *)p;
     s->x = (float *)(s->xbase + ox);
@@ -1807,12 +1810,7 @@ static int record_head(rk_head *h, const float *x, cudaStream_t st) {
   a.cols = D;
   a.epi = EPI_STORE;
   a.err = h->d->err_dev;
-  if (quantized_fmt(h->wcls->fmt) && mv_mode() != 0) {
-    CK(launch_quantize_wide(x, D, h->rms, recipD, eps, nullptr, h->qx, h->xs, h->xsum, st));
-    a.qx = h->qx;
-    a.xs = h->xs;
-    a.xsum = h->xsum;
-  } else if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D, true)) {
+  if (quantized_fmt(h->wcls->fmt) && matvec_fused_ok(h->wcls->fmt, D, true)) {
     // Every CTA computes rmsNorm + quantize8 of x itself.
     a.pro = PRO_NORM_QUANT;
     a.x = x;

@@ -204,52 +204,49 @@ RK_DEV uint64_t globaltimer_ns() {
   return t;
 }
 
-// System-scope acquire load / release store of a 32-bit flag (flags that
-// other GPUs write over NVLink, or that this GPU writes in their memory).
-RK_DEV unsigned ld_acquire_sys(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// A gathered value as one tagged 8-byte word (stored whole, read whole).
+RK_DEV void ll_store(unsigned long long *p, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | f2u(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-RK_DEV void st_release_sys(unsigned *p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Waits (thread 0 of the CTA spins, then a CTA barrier) until each of n
-// flags holds the step's epoch; false after about a second.
-RK_DEV bool gather_wait(const unsigned *flags, int n, const unsigned *epoch_p) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    const unsigned epoch = *epoch_p;
-    int ok = 1;
-    const uint64_t t0 = globaltimer_ns();
-    for (int g = 0; g < n && ok; g++)
-      while (ld_acquire_sys(flags + g) != epoch)
-        if (globaltimer_ns() - t0 > 1000000000ull) {
-          ok = 0;
-          break;
-        }
-    s_ok = ok;
-  }
-  __syncthreads();
-  return s_ok != 0;
+RK_DEV unsigned long long ll_load(const unsigned long long *p) {
+  unsigned long long w;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
 }
 
-// The end of a producer CTA of a fused gather: once every CTA's peer stores
-// are visible system-wide, the last CTA raises this rank's flag in every
-// peer's memory to the step's epoch.
-RK_DEV void gather_done(unsigned *counter, unsigned *const *flag, int nflag, const unsigned *epoch_p) {
+// Copies n gathered floats into shared memory `dst`, each once its word
+// carries `tag` (all threads; then a CTA barrier). false when a word has
+// not arrived after about a second.
+RK_DEV bool ll_gather_load(const unsigned long long *ll, int n, unsigned tag, float *dst) {
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned done = atomicAdd(counter, 1u);
-    if (done == gridDim.x * gridDim.y * gridDim.z - 1) {
-      *counter = 0;
-      __threadfence_system();
-      const unsigned epoch = *epoch_p;
-      for (int g = 0; g < nflag; g++) st_release_sys(flag[g], epoch);
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  // Eight words in flight per thread; a word that has not arrived is
+  // re-read on its own.
+  for (int i0 = threadIdx.x; i0 < n && ok; i0 += 8 * blockDim.x) {
+    unsigned long long w[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * blockDim.x;
+      w[u] = i < n ? ll_load(ll + i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * blockDim.x;
+      if (i >= n) continue;
+      while ((unsigned)(w[u] >> 32) != tag && ok) {
+        if (globaltimer_ns() - t0 > 1000000000ull) ok = false;
+        else w[u] = ll_load(ll + i);
+      }
+      dst[i] = u2f((uint32_t)w[u]);
     }
   }
+  if (!ok) s_bad = 1;
+  __syncthreads();
+  return s_bad == 0;
 }
 
 // Whether launches on this host thread use programmatic dependent launch

@@ -655,9 +655,11 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   for (int t = P16; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t]));
   const int o = (hbase + h) * a.hs + slice * kFsSlice + d;
   a.out[o] = acc;
-  for (int g = 0; g < a.put.nout; g++) a.put.peer_out[g][o] = acc;
+  if (a.put.nll > 0) {
+    const unsigned tag = gather_tag(*a.put.epoch, a.put.slot, a.put.nslots);
+    for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + o, acc, tag);
   }
-  if (a.put.nflag > 0) gather_done(a.put.counter, a.put.flag, a.put.nflag, a.put.epoch);
+  }
 }
 
 // Shared memory of k_attn_softmax_wsum for gpb heads of up to maxP
@@ -666,6 +668,7 @@ static int fs_smem_bytes(int gpb, int wph, int maxP) {
   const long long bytes = 4LL * gpb * fs_ppad(maxP) + 4LL * kFsSlice * fs_vpad(maxP) + 16 + 4LL * gpb * (wph + 1);
   return bytes > kFsSmemLimit ? 0 : (int)bytes;
 }
+
 
 bool attention_fused_ok(int heads, int kv_heads, int hs, int max_positions) {
   const int gpb = heads / kv_heads;

@@ -45,8 +45,8 @@ struct AttnArgs {
   int heads, kv_heads, hs, kv_dim, att_stride;
   float inv_sqrt;
   int *err;  // device error word for a pipeline wait that timed out
-  // Row sharding: the output rows also go to the peers (out's offset), and
-  // the gather point's flag is raised when the kernel is done.
+  // Row sharding: the output values also go to every rank's tagged copy
+  // (at out's offset), one 8-byte value|tag word each.
   GatherPut put;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);

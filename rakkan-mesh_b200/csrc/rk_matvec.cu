@@ -42,12 +42,14 @@ RK_DEV void stage_load(const float *__restrict__ x, const float *__restrict__ w,
   const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
   if (vec) {
     // Asynchronous 16-byte copies: every load of the chunk is in flight at
-    // once; the caller's barrier is preceded by stage_wait().
+    // once; the caller's barrier is preceded by stage_wait(). x may be null
+    // (its values come another way).
     for (int i = threadIdx.x; i < m / 4; i += blockDim.x) {
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                       (uint32_t)__cvta_generic_to_shared(stage + 4 * i)),
-                   "l"(x + c0 + 4 * i)
-                   : "memory");
+      if (x)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(stage + 4 * i)),
+                     "l"(x + c0 + 4 * i)
+                     : "memory");
       if (w)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
                          (uint32_t)__cvta_generic_to_shared(wstage + 4 * i)),
@@ -57,7 +59,7 @@ RK_DEV void stage_load(const float *__restrict__ x, const float *__restrict__ w,
     asm volatile("cp.async.commit_group;" ::: "memory");
   } else {
     for (int i = threadIdx.x; i < m; i += blockDim.x) {
-      stage[i] = x[c0 + i];
+      if (x) stage[i] = x[c0 + i];
       if (w) wstage[i] = w[c0 + i];
     }
   }
@@ -161,62 +163,6 @@ __global__ void __launch_bounds__(512) k_quantize_act(const float *__restrict__ 
   griddep_trigger();
   griddep_wait();
   quantize_warps<NORM>(x, n, w, recipN, eps, qx, xs, xsum, &s_inv, stage, wstage, kQuantStage, false);
-}
-
-// The same over many CTAs, a warp per 32-block: lane j holds element j,
-// amax and the block's integer sum are warp reductions (both order free),
-// so a block costs a few dozen instructions and the whole vector one wave.
-// With NORM every CTA first forms Dot32(x, x) in warp 0 (the norm's serial
-// lanes cannot be split) and broadcasts Rsqrt32 through shared memory.
-constexpr int kQwWarps = 8;
-
-template <bool NORM>
-__global__ void __launch_bounds__(kQwWarps * 32) k_quantize_wide(const float *__restrict__ x, int n,
-                                                                  const float *__restrict__ w, float recipN, float eps,
-                                                                  float *__restrict__ xn, int8_t *__restrict__ qx,
-                                                                  float *__restrict__ xs, int *__restrict__ xsum) {
-  __shared__ float s_inv;
-  griddep_trigger();
-  griddep_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float inv = 0.0f;
-  if (NORM) {
-    if (warp == 0) {
-      float s = 0.0f;
-#pragma unroll 8
-      for (int i = lane; i < n; i += 32) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
-      const float dot = combine32(s);
-      if (lane == 0) s_inv = rsqrt32(__fadd_rn(__fmul_rn(dot, recipN), eps));
-    }
-    __syncthreads();
-    inv = s_inv;
-  }
-  const int b = blockIdx.x * kQwWarps + warp;
-  if (b >= n / 32) return;
-  float v = x[b * 32 + lane];
-  if (NORM) {
-    v = __fmul_rn(w[b * 32 + lane], __fmul_rn(inv, v));
-    if (xn) xn[b * 32 + lane] = v;
-  }
-  const float amax = gomax(0.0f, warp_gomax(fabsf(v)));
-  const float d = __fmul_rn(amax, u2f(K_1_127));
-  int q = 0;
-  if (!(d == 0.0f || d != d)) q = quant_q8(__fmul_rn(v, recip32(d)));
-  qx[b * 32 + lane] = (int8_t)q;
-  const int sum = __reduce_add_sync(0xffffffffu, q);
-  if (lane == 0) {
-    xs[b] = d;
-    if (xsum) xsum[b] = sum;
-  }
-}
-
-cudaError_t launch_quantize_wide(const float *x, int n, const float *w, float recipN, float eps, float *xn,
-                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st) {
-  const int nb = n / 32;
-  if (nb <= 0) return cudaSuccess;
-  const int grid = (nb + kQwWarps - 1) / kQwWarps;
-  if (w) return launch_k(k_quantize_wide<true>, grid, kQwWarps * 32, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
-  return launch_k(k_quantize_wide<false>, grid, kQwWarps * 32, 0, st, x, n, w, recipN, eps, xn, qx, xs, xsum);
 }
 
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
@@ -511,16 +457,23 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     }
   }
   griddep_wait();
-  if (a.wait.n > 0 && !gather_wait(a.wait.flags, a.wait.n, a.wait.epoch) && threadIdx.x == 0)
-    atomicExch(a.err, DEV_ERR_TIMEOUT);
-  // The input's loads go first, ahead of the weight ring's copies.
+  // The input's loads go first, ahead of the weight ring's copies. A
+  // gathered input (row sharding) arrives as tagged words, read once each
+  // carries this step's tag of the gather point.
   const bool norm = a.pro == PRO_NORM_QUANT;
+  const bool gathered = a.wait.ll != nullptr;
   float *stage = reinterpret_cast<float *>(p);
   const int sf = a.pro != PRO_GIVEN ? stage_floats(cols, norm) : 0;
   if (a.pro != PRO_GIVEN)
-    stage_load(a.x, norm && cols <= sf ? a.norm_w : nullptr, 0, min(cols, sf), stage, stage + sf);
+    stage_load(gathered ? nullptr : a.x, norm && cols <= sf ? a.norm_w : nullptr, 0, min(cols, sf), stage,
+               stage + sf);
   if (lane == 0)
     for (int k = 0; k < SLOTS; k++) issue();
+  if (gathered &&
+      !ll_gather_load(a.wait.ll, cols, gather_tag(*a.wait.epoch, a.wait.slot, a.wait.nslots), stage) &&
+      threadIdx.x == 0)
+    atomicExch(a.err, DEV_ERR_TIMEOUT);
+  const unsigned put_tag = a.put.nll > 0 ? gather_tag(*a.put.epoch, a.put.slot, a.put.nslots) : 0u;
 
   if (a.pro != PRO_GIVEN) {
     __shared__ float s_inv;
@@ -609,7 +562,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
         if (put) {
           out[cc.row] = v;
           if (cc.part == 0 || a.epi == EPI_SILU)
-            for (int g = 0; g < a.put.nout; g++) a.put.peer_out[g][cc.row] = v;
+            for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + cc.row, v, put_tag);
         }
       }
     }
@@ -619,7 +572,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     slot = slot + 1 == SLOTS ? 0 : slot + 1;
     if (slot == 0) parity ^= 1;
   }
-  if (a.put.nflag > 0) gather_done(a.put.counter, a.put.flag, a.put.nflag, a.put.epoch);
 }
 
 // ---------------------------------------------------------------------------
@@ -716,19 +668,11 @@ cudaError_t init_matvec_attributes() {
   return e;
 }
 
-int mv_mode() {
-  static const int m = [] {
-    const char *e = getenv("RK_MV_MODE");
-    return e ? atoi(e) : 0;
-  }();
-  return m;
-}
-
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
   const bool quant = a.fmt == FMT_Q8_0 || a.fmt == FMT_Q4_0;
   const bool fused = a.pro != PRO_GIVEN, norm = a.pro == PRO_NORM_QUANT;
   if (quant && fused && !matvec_fused_ok(a.fmt, a.cols, norm)) return cudaErrorInvalidValue;
-  const int in_smem = a.cols <= kSmemColsMax && (fused || mv_mode() != 2) ? 1 : 0;
+  const int in_smem = a.cols <= kSmemColsMax ? 1 : 0;
   if (a.fmt == FMT_Q8_0)
     return launch_k(k_matvec_q<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q8_0>(a.cols, fused, norm), st, a,
                     in_smem);

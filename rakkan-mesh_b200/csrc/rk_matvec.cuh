@@ -20,26 +20,30 @@ enum Epi : int {
 enum DevErr : int { DEV_OK = 0, DEV_ERR_TIMEOUT = 1 };
 
 // Row sharding's all-gather, fused into the kernels (one process per GPU,
-// peers' buffers mapped through CUDA IPC). A producer kernel stores each
-// output row into every peer's copy of the output as well as its own; when
-// its last CTA is done it raises, in every peer's memory, the flag of this
-// gather point to the step's epoch. A consumer kernel waits, after its
-// dependency wait, for its peers' flags of the gather point it reads. All
-// waits are bounded (about a second, then the device error word is set).
+// peers' memory mapped through CUDA IPC), in the manner of a low-latency
+// protocol: every gathered value travels as one 8-byte word holding the
+// float and a tag unique to (step, gather point), stored into every rank's
+// copy of the gathered vector (this rank's included). A consumer reads the
+// words of its input and waits until each carries the expected tag; a
+// word is written by one 8-byte store, so its value and tag arrive
+// together and no fence or flag is needed. Waits are bounded (about a
+// second, then the device error word is set).
 constexpr int kMaxPeers = 8;
 struct GatherPut {
-  int nout;                         // peers to store into (0: no gather)
-  float *peer_out[kMaxPeers];       // peers' copies of the output (same offset as part[0].out)
-  int nflag;                        // flags to raise: every rank's, this one's included
-  unsigned *flag[kMaxPeers];        // this rank's flag of the gather point, in each rank's memory
-  unsigned *counter;                // local: CTAs done (reset by the last)
-  const unsigned *epoch;            // the step's epoch (local)
+  int nll;                                   // ranks to store into (0: no gather)
+  unsigned long long *ll[kMaxPeers];         // each rank's tagged copy, at the output's position
+  const unsigned *epoch;                     // the step's epoch (local)
+  int slot, nslots;                          // tag = epoch · nslots + slot
 };
 struct GatherWait {
-  int n;                            // 0: nothing to wait for
-  const unsigned *flags;            // local: the peers' flags of the gather point
+  const unsigned long long *ll;              // the input's tagged copy (local); null: none
   const unsigned *epoch;
+  int slot, nslots;
 };
+
+__host__ __device__ inline unsigned gather_tag(unsigned epoch, int slot, int nslots) {
+  return epoch * (unsigned)nslots + (unsigned)slot;
+}
 
 struct MvPart {
   const uint8_t *w;  // row-major weights: Q8 cols bytes/row, Q4 cols/2, F32 4·cols, BF16 2·cols
@@ -81,27 +85,15 @@ constexpr int kSmemColsMax = 32768;
 
 // Quantizes n floats (a whole number of 32-blocks) to Q8_0 as quantize8
 // does (quant.go:34-53), after RMS normalisation when w != nullptr
-// (model.go:632-638, recipN = Recip32(n)), in one CTA. xn must be null
-// (launch_quantize_wide keeps the normalised floats).
+// (model.go:632-638, recipN = Recip32(n)), in one CTA. xn must be null.
 cudaError_t launch_quantize_act(const float *x, int n, const float *w, float recipN, float eps, float *xn,
                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st);
-
-// The same quantization spread over ceil(n/256) CTAs, a warp per 32-block
-// (each CTA recomputes the norm's Dot32 when w != nullptr); xn, if not
-// null, receives the normalised floats.
-cudaError_t launch_quantize_wide(const float *x, int n, const float *w, float recipN, float eps, float *xn,
-                                 int8_t *qx, float *xs, int *xsum, cudaStream_t st);
 
 // out = matrices · x, bits identical to num.MatVecQ8/Q4/32/BF16.
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
 
 int matvec_smem_bytes(int fmt, int cols);
 
-
-// Experiment selector (RK_MV_MODE): 0 = quantize in the matvec prologue,
-// 1 = separate multi-CTA quantizer, input staged in shared memory,
-// 2 = separate quantizer, input read from global memory.
-int mv_mode();
 
 // Whether a matvec of this format and width can quantize its input in its
 // own prologue (PRO_NORM_QUANT when norm, else PRO_QUANT): the input and its
