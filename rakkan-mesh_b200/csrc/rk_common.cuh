@@ -256,23 +256,42 @@ inline thread_local bool g_pdl = false;
 // recorded step's own kernels with it).
 inline thread_local long long g_kernel_launches = 0;
 
-// Launches kernel k with the programmatic stream-serialization attribute
-// when g_pdl is set, else as an ordinary launch.
+// Launches kernel k in thread-block clusters of `cluster` CTAs (none when
+// it is 1×1×1), with the programmatic stream-serialization attribute when
+// g_pdl is set.
 template <typename... KArgs, typename... Args>
-inline cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                            Args &&...args) {
+inline cudaError_t launch_kc(void (*k)(KArgs...), dim3 grid, dim3 block, dim3 cluster, size_t smem, cudaStream_t st,
+                             Args &&...args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
+    n++;
+  }
+  if (g_pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = g_pdl ? 1 : 0;
+  cfg.numAttrs = n;
   g_kernel_launches++;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+// launch_kc without clusters.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args &&...args) {
+  return launch_kc(k, grid, block, dim3(1, 1, 1), smem, st, std::forward<Args>(args)...);
 }
 
 }  // namespace rk

@@ -144,12 +144,14 @@ __global__ void __launch_bounds__(kScoreWarps * 32) k_attn_scores(const AttnArgs
 }
 
 // Scores, a lane per position: CTA (32-position tile, kv head) stages the
-// tile's keys in shared memory (rows padded to HS+1 floats, so lanes reading
-// different rows hit different banks); warp g computes, for query head g of
-// the group, lane p's whole Dot32(q, k_p) in registers: element e is added
-// to partial sum e mod 32 in increasing e, then the fixed tree
-// (matvec.go:60-66). No shuffles.
+// tile's keys in shared memory by bulk copies (rows padded to HS+4 floats,
+// so lanes reading different rows hit different banks); warp g computes,
+// for query head g of the group, lane p's whole Dot32(q, k_p) in registers:
+// element e is added to partial sum e mod 32 in increasing e, then the
+// fixed tree (matvec.go:60-66). No shuffles.
 constexpr int kTileT = 32;
+
+RK_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
 // The per-token work between the QKV products and attention
 // (model.go:542-566) on one head vector in shared memory, by one warp: bias
@@ -180,12 +182,23 @@ RK_DEV void head_post(float *v, int hs, const float *bias, const float *nw, cons
 // for that row of the tile; the first group's CTA also appends k and v to
 // the caches (the next kernel reads the value row).
 template <int HS, bool POST>
-__global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int gpb, const QkvPostArgs qp) {
-  griddep_trigger();
-  griddep_wait();
-  __shared__ float sk[kTileT * (HS + 1)];
-  __shared__ float sq[8 * HS];
+__global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int gpb, const QkvPostArgs qp) {
+  // Key rows HS+4 floats apart: lane p's 16-byte loads of row p then cover
+  // all banks in each group of eight lanes.
+  constexpr int KP = HS + 4;
+  __shared__ __align__(16) float sk[kTileT * KP];
+  __shared__ __align__(16) float sq[8 * HS];
   __shared__ float snew[POST ? HS : 1];
+  __shared__ float sco[POST ? HS / 2 : 1], ssi[POST ? HS / 2 : 1];
+  __shared__ __align__(8) uint64_t sbar;
+  griddep_trigger();
+  const uint32_t bar = umma::smem_u32(&sbar);
+  if (threadIdx.x == 0) {
+    umma::mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  griddep_wait();
   const int P = attn_positions(a);
   const int t0 = blockIdx.x * kTileT;
   if (t0 >= P) return;
@@ -193,69 +206,92 @@ __global__ void __launch_bounds__(256) k_attn_scores_tile(const AttnArgs a, int 
   const int g0 = blockIdx.z * gpb, ng = min(gpb, kvMul - g0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nt = min(kTileT, P - t0);
-  // The key tile in 16-byte pieces, eight loads in flight per thread (the
-  // rows are contiguous 4·HS-byte runs of the cache).
-  constexpr int kPieces = kTileT * HS / 4;
-  for (int base = threadIdx.x; base < kPieces; base += blockDim.x * 8) {
-    float4 r[8];
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const int idx = base + u * blockDim.x;
-      const int p = idx / (HS / 4), i4 = idx % (HS / 4);
-      r[u] = idx < kPieces && p < nt
-                 ? *reinterpret_cast<const float4 *>(a.keys + (long long)(t0 + p) * a.kv_dim + kvh * HS + 4 * i4)
-                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const int idx = base + u * blockDim.x;
-      if (idx < kPieces) {
-        const int p = idx / (HS / 4), i4 = idx % (HS / 4);
-        float *d = sk + p * (HS + 1) + 4 * i4;
-        d[0] = r[u].x, d[1] = r[u].y, d[2] = r[u].z, d[3] = r[u].w;
-      }
-    }
+  // The tile's key rows (contiguous 4·HS-byte runs of the cache) and the
+  // group's query rows by bulk copies, one per row, issued by warp 0.
+  if (warp == 0) {
+    if (lane == 0) umma::mbar_expect_tx(bar, (uint32_t)(nt + ng) * HS * 4u);
+    __syncwarp();
+    if (lane < nt)
+      umma::bulk_g2s(umma::smem_u32(sk + lane * KP), a.keys + (long long)(t0 + lane) * a.kv_dim + kvh * HS, HS * 4u,
+                     bar);
+    if (lane == 0) umma::bulk_g2s(umma::smem_u32(sq), a.q + (kvh * kvMul + g0) * HS, (uint32_t)ng * HS * 4u, bar);
   }
-  for (int e = threadIdx.x; e < ng * HS; e += blockDim.x) sq[e] = a.q[(kvh * kvMul + g0) * HS + e];
   if (POST) {
     const int pos = P - 1;
     const bool has_new = pos < t0 + nt;
-    if (has_new && warp == ng % (blockDim.x >> 5))
-      for (int i = lane; i < HS; i += 32) snew[i] = qp.k[kvh * HS + i];
+    // The post warp (the one past the heads) fetches position pos's
+    // cos/sin rows and, in the tile that holds pos, the raw k and v rows
+    // while the keys are in flight.
+    const bool post_warp = warp == ng % (blockDim.x >> 5);
+    float vv[HS / 32];
+    if (post_warp) {
+      for (int i = lane; i < HS / 2; i += 32) {
+        sco[i] = qp.cos_[(long long)pos * (HS / 2) + i];
+        ssi[i] = qp.sin_[(long long)pos * (HS / 2) + i];
+      }
+      if (has_new && blockIdx.z == 0)
+#pragma unroll
+        for (int u = 0; u < HS / 32; u++) {
+          vv[u] = qp.v[kvh * HS + lane + 32 * u];
+          if (qp.bv) vv[u] = __fadd_rn(vv[u], qp.bv[kvh * HS + lane + 32 * u]);
+        }
+      if (has_new)
+        for (int i = lane; i < HS; i += 32) snew[i] = qp.k[kvh * HS + i];
+    }
+    if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0 && a.err) atomicExch(a.err, DEV_ERR_TIMEOUT);
     __syncthreads();
-    const float *co = qp.cos_ + (long long)pos * (HS / 2), *si = qp.sin_ + (long long)pos * (HS / 2);
     if (warp < ng) {
       const int h = kvh * kvMul + g0 + warp;
-      head_post(sq + warp * HS, HS, qp.bq ? qp.bq + h * HS : nullptr, qp.q_norm, co, si, qp.recip_hs, qp.eps);
+      head_post(sq + warp * HS, HS, qp.bq ? qp.bq + h * HS : nullptr, qp.q_norm, sco, ssi, qp.recip_hs, qp.eps);
     }
-    if (has_new && warp == ng % (blockDim.x >> 5)) {
-      head_post(snew, HS, qp.bk ? qp.bk + kvh * HS : nullptr, qp.k_norm, co, si, qp.recip_hs, qp.eps);
-      for (int i = lane; i < HS; i += 32) sk[(pos - t0) * (HS + 1) + i] = snew[i];
+    if (has_new && post_warp) {
+      head_post(snew, HS, qp.bk ? qp.bk + kvh * HS : nullptr, qp.k_norm, sco, ssi, qp.recip_hs, qp.eps);
+      for (int i = lane; i < HS; i += 32) sk[(pos - t0) * KP + i] = snew[i];
       if (blockIdx.z == 0) {
         // The cache append (model.go:567-568).
         const int kvDim = qp.kv_heads * HS;
-        for (int i = lane; i < HS; i += 32) {
+#pragma unroll
+        for (int u = 0; u < HS / 32; u++) {
+          const int i = lane + 32 * u;
           qp.key_cache[(long long)pos * kvDim + kvh * HS + i] = snew[i];
-          float vv = qp.v[kvh * HS + i];
-          if (qp.bv) vv = __fadd_rn(vv, qp.bv[kvh * HS + i]);
-          if (qp.v_pitch > 0) qp.val_cache[(long long)(kvh * HS + i) * qp.v_pitch + pos] = vv;
-          else qp.val_cache[(long long)pos * kvDim + kvh * HS + i] = vv;
+          if (qp.v_pitch > 0) qp.val_cache[(long long)(kvh * HS + i) * qp.v_pitch + pos] = vv[u];
+          else qp.val_cache[(long long)pos * kvDim + kvh * HS + i] = vv[u];
         }
       }
     }
+  } else if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0 && a.err) {
+    atomicExch(a.err, DEV_ERR_TIMEOUT);
   }
   __syncthreads();
   if (warp >= ng) return;
   const float *q = sq + warp * HS;
-  const float *k = sk + lane * (HS + 1);
-  float s[32];
-#pragma unroll
-  for (int j = 0; j < 32; j++) s[j] = 0.0f;
-#pragma unroll
-  for (int e = 0; e < HS; e++) s[e & 31] = __fadd_rn(s[e & 31], __fmul_rn(q[e], k[e]));
+  const float *k = sk + lane * KP;
+  // Partial sum s_r (r = e mod 32) in increasing e; a float4 at e = 4c
+  // feeds s_4c..s_4c+3. Residues 4h..4h+3 (+8u) make e8[4h..4h+3]
+  // = (s_j + s_j+8) + (s_j+16 + s_j+24), half the tree at a time.
   float e8[8];
 #pragma unroll
-  for (int j = 0; j < 8; j++) e8[j] = __fadd_rn(__fadd_rn(s[j], s[j + 8]), __fadd_rn(s[j + 16], s[j + 24]));
+  for (int h = 0; h < 2; h++) {
+    float4 s4[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int m = 0; m < HS / 32; m++) {
+        const int e = 4 * h + 8 * u + 32 * m;
+        const float4 kk = ld4(k + e), qq = ld4(q + e);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(qq.x, kk.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(qq.y, kk.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(qq.z, kk.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(qq.w, kk.w));
+      }
+      s4[u] = acc;
+    }
+    e8[4 * h] = __fadd_rn(__fadd_rn(s4[0].x, s4[1].x), __fadd_rn(s4[2].x, s4[3].x));
+    e8[4 * h + 1] = __fadd_rn(__fadd_rn(s4[0].y, s4[1].y), __fadd_rn(s4[2].y, s4[3].y));
+    e8[4 * h + 2] = __fadd_rn(__fadd_rn(s4[0].z, s4[1].z), __fadd_rn(s4[2].z, s4[3].z));
+    e8[4 * h + 3] = __fadd_rn(__fadd_rn(s4[0].w, s4[1].w), __fadd_rn(s4[2].w, s4[3].w));
+  }
   const float dot = __fadd_rn(__fadd_rn(__fadd_rn(e8[0], e8[1]), __fadd_rn(e8[2], e8[3])),
                               __fadd_rn(__fadd_rn(e8[4], e8[5]), __fadd_rn(e8[6], e8[7])));
   if (lane < nt) a.att[(long long)(kvh * kvMul + g0 + warp) * a.att_stride + t0 + lane] = __fmul_rn(dot, a.inv_sqrt);
@@ -440,27 +476,67 @@ __global__ void __launch_bounds__(kWsMaxGroup * 32) k_attn_wsum_staged(const Att
 //
 // CTA (kv head, slice of kFsSlice value elements) serves all GPB query
 // heads of the kv head; warp w works for head w mod GPB, so the heads'
-// serial threads sit on different SM sub-partitions. At the start one
-// thread copies the heads' scores into shared memory (one bulk copy per
-// head) and every thread starts asynchronous 4-byte copies of the value
-// slice (P rows of kFsSlice floats) into shared memory transposed,
-// element-major, so that the value chains read four positions per load;
-// they land while the softmax runs. Then, per head,
-//   1. the maximum of the scores (order free, as Go's max is),
-//   2. Exp32(x - max) in place,
+// serial threads sit on different SM sub-partitions. The slices of one kv
+// head all need the same softmax, so they run as a thread-block cluster of
+// C CTAs (C = 1 when clusters cannot all be resident) that splits the
+// positions into C chunks: CTA r of the cluster owns chunk r. At the start
+// one thread copies the chunk's scores into shared memory (one bulk copy
+// per head). Then, per head,
+//   1. the maximum of the scores (order free, as Go's max is): each CTA
+//      takes its chunk's and hands it to every member through distributed
+//      shared memory, then each combines the C of them,
+//   2. Exp32(x - max) of the chunk, stored into every member's row, so
+//      after a cluster barrier each CTA holds all P exps; now the value
+//      slice (P positions of kFsSlice floats, stored element-major, so
+//      that the value chains read four positions per load) starts to load,
+//      landing while the sums run,
 //   3. their sum in position order by one thread (softmax,
 //      model.go:640-654),
 //   4. multiplication by Recip32(sum): the attention weights,
 // and thread (head h, element d) finally sums weight·value in position
-// order (model.go:580-586), reading only shared memory, its operands
-// loaded 16 positions ahead. The kFsSlice-wide slices of one kv head all
-// compute the same softmax; the scores stay in L2, so the repetition costs
-// only exps.
+// order (model.go:580-586), reading only shared memory, the products
+// formed one group of 16 positions ahead of the chain.
 constexpr int kFsSlice = 8;  // value elements per CTA
 constexpr int kFsSmemLimit = 227 * 1024 - 1024;
 constexpr int kFsMaxThreads = 640;
 
-RK_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+
+// Thread-block cluster helpers (a launch without clusters is a cluster of
+// one CTA).
+RK_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+RK_DEV uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster; orders the shared-memory
+// stores before it (local and remote) before the loads after it.
+RK_DEV void cluster_sync() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The address of the same shared-memory location in CTA `rank` of the cluster.
+RK_DEV uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+RK_DEV void st_cluster(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+RK_DEV void st_cluster(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+RK_DEV void st_cluster(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+constexpr int kFsMaxCluster = 8;
 
 // Warps per head for the softmax phases.
 static int fs_wph(int gpb) {
@@ -483,6 +559,7 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   float *sV = fs_smem + (size_t)gpb * ppad;   // [kFsSlice][vpad] values, element-major
   uint64_t *sbar = reinterpret_cast<uint64_t *>(sV + (size_t)kFsSlice * vpad);  // scores, values
   float *red = reinterpret_cast<float *>(sbar + 2);  // [gpb][wph] maxima, then [gpb] 1/sum
+  uint32_t *cmax = reinterpret_cast<uint32_t *>(red + gpb * (wph + 1));  // [gpb][kFsMaxCluster] chunk maxima
   const int kvh = blockIdx.x, slice = blockIdx.y;
   const int hbase = kvh * gpb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -497,14 +574,77 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   griddep_wait();
   const int P = attn_positions(a);
   const int P4 = P & ~3;
+  // This CTA's chunk [lo, hi) of the positions: whole float4s [lo, hi4),
+  // then (last chunk only) the fewer than 4 positions from P4 on.
+  const uint32_t crank = cluster_rank(), csize = cluster_size();
+  const int cs = ((P + (int)csize - 1) / (int)csize + 3) & ~3;
+  const int lo = min(P, (int)crank * cs), hi = min(P, lo + cs), hi4 = min(hi, P4);
   if (threadIdx.x == 0) {
-    umma::mbar_expect_tx(bar, (uint32_t)gpb * P4 * 4u);
-    if (P4 > 0)
+    const uint32_t bytes = hi4 > lo ? (uint32_t)(hi4 - lo) * 4u : 0u;
+    umma::mbar_expect_tx(bar, (uint32_t)gpb * bytes);
+    if (bytes)
       for (int g = 0; g < gpb; g++)
-        umma::bulk_g2s(umma::smem_u32(sE + (size_t)g * ppad), a.att + (long long)(hbase + g) * a.att_stride,
-                       P4 * 4u, bar);
+        umma::bulk_g2s(umma::smem_u32(sE + (size_t)g * ppad + lo),
+                       a.att + (long long)(hbase + g) * a.att_stride + lo, bytes, bar);
   }
 
+  const int g = warp % gpb, sub = warp / gpb;
+  float *e = sE + (size_t)g * ppad;
+  const float *x = a.att + (long long)(hbase + g) * a.att_stride;
+  const bool tail_lane = sub == 0 && hi4 + lane < hi;
+  const float tail = tail_lane ? x[hi4 + lane] : 0.0f;
+  if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
+  // 1. the chunk's maximum as the largest order key, 0xffffffff for a NaN
+  // (above every key; key 0 belongs to no non-NaN value, so it is the
+  // empty chunk's).
+  uint32_t key = 0;
+  bool nan = false;
+  for (int q = lo / 4 + sub * 32 + lane; q < hi4 / 4; q += wph * 32) {
+    const float4 v = ld4(e + 4 * q);
+    key = max(key, max(max(fkey(v.x), fkey(v.y)), max(fkey(v.z), fkey(v.w))));
+    nan |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
+  }
+  if (tail_lane) {
+    e[hi4 + lane] = tail;
+    key = max(key, fkey(tail));
+    nan |= tail != tail;
+  }
+  key = __reduce_max_sync(0xffffffffu, key);
+  nan = __any_sync(0xffffffffu, nan);
+  if (lane == 0) reinterpret_cast<uint32_t *>(red)[g * wph + sub] = nan ? 0xffffffffu : key;
+  __syncthreads();
+  if (threadIdx.x < gpb) {
+    uint32_t k = 0;
+    for (int j = 0; j < wph; j++) k = max(k, reinterpret_cast<const uint32_t *>(red)[threadIdx.x * wph + j]);
+    const uint32_t at = umma::smem_u32(cmax + threadIdx.x * kFsMaxCluster + crank);
+    for (uint32_t r = 0; r < csize; r++) st_cluster(cluster_map(at, r), k);
+  }
+  cluster_sync();
+  float m;
+  {
+    uint32_t k = 0;
+    for (uint32_t r = 0; r < csize; r++) k = max(k, cmax[g * kFsMaxCluster + r]);
+    m = k == 0xffffffffu ? u2f(kCanonNaN) : fkey_value(k);
+  }
+  // 2. the chunk's exponentials, into every member's row.
+  {
+    const uint32_t row = umma::smem_u32(e);
+    for (int q = lo / 4 + sub * 32 + lane; q < hi4 / 4; q += wph * 32) {
+      float4 v = ld4(e + 4 * q);
+      v.x = exp32(__fsub_rn(v.x, m));
+      v.y = exp32(__fsub_rn(v.y, m));
+      v.z = exp32(__fsub_rn(v.z, m));
+      v.w = exp32(__fsub_rn(v.w, m));
+      for (uint32_t r = 0; r < csize; r++) st_cluster(cluster_map(row + 16u * q, r), v);
+    }
+    if (tail_lane) {
+      const float v = exp32(__fsub_rn(tail, m));
+      for (uint32_t r = 0; r < csize; r++) st_cluster(cluster_map(row + 4u * (hi4 + lane), r), v);
+    }
+  }
+  cluster_sync();
+  // The value slice, copied while the sum chains run (issued only now: a
+  // cluster barrier's release would wait for a copy in flight).
   if (a.v_pitch > 0) {
     // Transposed cache: the slice's kFsSlice elements are contiguous runs
     // of positions, one bulk copy each (rounded up to whole float4s, which
@@ -529,54 +669,6 @@ __global__ void __launch_bounds__(kFsMaxThreads)
     }
     cp_async_commit();
   }
-  const int g = warp % gpb, sub = warp / gpb;
-  float *e = sE + (size_t)g * ppad;
-  const float *x = a.att + (long long)(hbase + g) * a.att_stride;
-  const float tail = P4 + lane < P ? x[P4 + lane] : 0.0f;
-  if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
-  // 1. maximum, as the largest order key plus a NaN flag.
-  uint32_t key = fkey(P4 > 0 ? e[0] : x[0]);
-  bool nan = false;
-  for (int q = sub * 32 + lane; q < P4 / 4; q += wph * 32) {
-    const float4 v = ld4(e + 4 * q);
-    key = max(key, max(max(fkey(v.x), fkey(v.y)), max(fkey(v.z), fkey(v.w))));
-    nan |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
-  }
-  if (sub == 0 && P4 + lane < P) {
-    e[P4 + lane] = tail;
-    key = max(key, fkey(tail));
-    nan |= tail != tail;
-  }
-  key = __reduce_max_sync(0xffffffffu, key);
-  nan = __any_sync(0xffffffffu, nan);
-  if (lane == 0) reinterpret_cast<uint32_t *>(red)[g * wph + sub] = nan ? 0xffffffffu : key;
-  __syncthreads();
-  // 2. exponentials, four independent ones per thread at a time.
-  float m;
-  {
-    uint32_t k = 0;
-    bool anynan = false;
-    for (int j = 0; j < wph; j++) {
-      const uint32_t r = reinterpret_cast<const uint32_t *>(red)[g * wph + j];
-      anynan |= r == 0xffffffffu;
-      k = max(k, r);
-    }
-    m = anynan ? u2f(kCanonNaN) : fkey_value(k);
-  }
-  {
-    const int stride = wph * 32;
-    for (int i0 = sub * 32 + lane; i0 < P; i0 += 4 * stride) {
-      float v[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++) v[u] = i0 + u * stride < P ? e[i0 + u * stride] : 0.0f;
-#pragma unroll
-      for (int u = 0; u < 4; u++) v[u] = exp32(__fsub_rn(v[u], m));
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        if (i0 + u * stride < P) e[i0 + u * stride] = v[u];
-    }
-  }
-  __syncthreads();
   if (warp < gpb) {
     // 3. their sum in position order.
     if (lane == 0) {
@@ -623,36 +715,41 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   const float *w = sE + (size_t)h * ppad;
   const float *v = sV + (size_t)d * vpad;
   float acc = 0.0f;
-  const int P16 = P & ~15;
-  if (P16 > 0) {
-    float4 wc[4], vc[4], wn[4], vn[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      wc[j] = ld4(w + 4 * j);
-      vc[j] = ld4(v + 4 * j);
-    }
-    for (int t = 0; t < P16; t += 16) {
-      const int tn = t + 16 < P16 ? t + 16 : t;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        wn[j] = ld4(w + tn + 4 * j);
-        vn[j] = ld4(v + tn + 4 * j);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        acc = __fadd_rn(acc, __fmul_rn(wc[j].x, vc[j].x));
-        acc = __fadd_rn(acc, __fmul_rn(wc[j].y, vc[j].y));
-        acc = __fadd_rn(acc, __fmul_rn(wc[j].z, vc[j].z));
-        acc = __fadd_rn(acc, __fmul_rn(wc[j].w, vc[j].w));
-      }
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        wc[j] = wn[j];
-        vc[j] = vn[j];
-      }
+  const int P32 = P & ~31;
+  if (P32 > 0) {
+    // Eight (weight, value) float4 pairs in rotation, as in the sum chain:
+    // quad k's pair is refilled from 32 positions further on once its
+    // products are formed, and the products are formed two quads before
+    // the chain adds them, so only adds sit between adds and a product is
+    // never waited for. The last round's refills re-read its own
+    // positions (the rows end soon after P).
+    float4 w0 = ld4(w), w1 = ld4(w + 4), w2 = ld4(w + 8), w3 = ld4(w + 12);
+    float4 w4 = ld4(w + 16), w5 = ld4(w + 20), w6 = ld4(w + 24), w7 = ld4(w + 28);
+    float4 v0 = ld4(v), v1 = ld4(v + 4), v2 = ld4(v + 8), v3 = ld4(v + 12);
+    float4 v4 = ld4(v + 16), v5 = ld4(v + 20), v6 = ld4(v + 24), v7 = ld4(v + 28);
+#define RK_WS_MUL(W, V) make_float4(__fmul_rn(W.x, V.x), __fmul_rn(W.y, V.y), __fmul_rn(W.z, V.z), __fmul_rn(W.w, V.w))
+    float4 p0 = RK_WS_MUL(w0, v0), p1 = RK_WS_MUL(w1, v1);
+    for (int t = 0; t < P32; t += 32) {
+      const int tn = t + 32 < P32 ? t + 32 : t;
+#define RK_WS_STEP(K, WN, VN)              \
+  {                                        \
+    const float4 p2 = RK_WS_MUL(WN, VN);   \
+    w##K = ld4(w + tn + 4 * K);            \
+    v##K = ld4(v + tn + 4 * K);            \
+    acc = __fadd_rn(acc, p0.x);            \
+    acc = __fadd_rn(acc, p0.y);            \
+    acc = __fadd_rn(acc, p0.z);            \
+    acc = __fadd_rn(acc, p0.w);            \
+    p0 = p1;                               \
+    p1 = p2;                               \
+  }
+      RK_WS_STEP(0, w2, v2) RK_WS_STEP(1, w3, v3) RK_WS_STEP(2, w4, v4) RK_WS_STEP(3, w5, v5)
+      RK_WS_STEP(4, w6, v6) RK_WS_STEP(5, w7, v7) RK_WS_STEP(6, w0, v0) RK_WS_STEP(7, w1, v1)
+#undef RK_WS_MUL
+#undef RK_WS_STEP
     }
   }
-  for (int t = P16; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t]));
+  for (int t = P32; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t]));
   const int o = (hbase + h) * a.hs + slice * kFsSlice + d;
   a.out[o] = acc;
   if (a.put.nll > 0) {
@@ -665,7 +762,8 @@ __global__ void __launch_bounds__(kFsMaxThreads)
 // Shared memory of k_attn_softmax_wsum for gpb heads of up to maxP
 // positions, or 0 when it does not fit.
 static int fs_smem_bytes(int gpb, int wph, int maxP) {
-  const long long bytes = 4LL * gpb * fs_ppad(maxP) + 4LL * kFsSlice * fs_vpad(maxP) + 16 + 4LL * gpb * (wph + 1);
+  const long long bytes = 4LL * gpb * fs_ppad(maxP) + 4LL * kFsSlice * fs_vpad(maxP) + 16 + 4LL * gpb * (wph + 1) +
+                          4LL * gpb * kFsMaxCluster;
   return bytes > kFsSmemLimit ? 0 : (int)bytes;
 }
 
@@ -675,8 +773,24 @@ bool attention_fused_ok(int heads, int kv_heads, int hs, int max_positions) {
   return gpb <= 8 && hs % kFsSlice == 0 && fs_smem_bytes(gpb, fs_wph(gpb), max_positions) > 0;
 }
 
+// How many clusters of 2, 4 and 8 CTAs of k_attn_softmax_wsum (at its
+// largest shared memory, so one CTA per SM) the current device holds at
+// once; filled by init_layer_attributes.
+static int g_fs_active[64][4];
+
+// The cluster size for a k_attn_softmax_wsum grid: the largest that divides
+// the slices and whose clusters are all resident at once, else 1.
+static int fs_cluster(dim3 grid) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  for (int i = 3, c = 8; i >= 1; i--, c /= 2)
+    if (grid.y % c == 0 && (long long)g_fs_active[dev][i] * c >= (long long)grid.x * grid.y) return c;
+  return 1;
+}
+
 static bool scores_tile_ok(const AttnArgs &a) {
-  return (a.hs == 64 || a.hs == 128) && reinterpret_cast<uintptr_t>(a.keys) % 16 == 0 && a.kv_dim % 4 == 0;
+  return (a.hs == 64 || a.hs == 128) && reinterpret_cast<uintptr_t>(a.keys) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && a.kv_dim % 4 == 0;
 }
 
 static cudaError_t launch_attention_impl(const AttnArgs &a, const QkvPostArgs *qp, cudaStream_t st) {
@@ -718,7 +832,8 @@ static cudaError_t launch_attention_impl(const AttnArgs &a, const QkvPostArgs *q
     if (!fused && a.v_pitch > 0) return cudaErrorInvalidValue;  // only the fused kernel reads transposed values
     if (fused) {
       dim3 g(a.kv_heads, a.hs / kFsSlice);
-      launch_k(k_attn_softmax_wsum, g, gpb * wph * 32, smem, st, a, gpb, wph);
+      const int c = fs_cluster(g);
+      launch_kc(k_attn_softmax_wsum, g, gpb * wph * 32, dim3(1, c, 1), smem, st, a, gpb, wph);
       return cudaGetLastError();
     }
   }
@@ -749,6 +864,28 @@ cudaError_t init_layer_attributes() {
   cudaError_t e = cudaFuncSetAttribute(k_attn_wsum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_attn_softmax_wsum, cudaFuncAttributeMaxDynamicSharedMemorySize, kFsSmemLimit);
+  int dev = 0;
+  if (e == cudaSuccess) e = cudaGetDevice(&dev);
+  if (e == cudaSuccess && dev >= 0 && dev < 64)
+    for (int i = 1, c = 2; i <= 3; i++, c *= 2) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, c * 16, 1);
+      cfg.blockDim = dim3(kFsMaxThreads, 1, 1);
+      cfg.dynamicSmemBytes = kFsSmemLimit;
+      cudaLaunchAttribute at;
+      at.id = cudaLaunchAttributeClusterDimension;
+      at.val.clusterDim.x = 1;
+      at.val.clusterDim.y = c;
+      at.val.clusterDim.z = 1;
+      cfg.attrs = &at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, k_attn_softmax_wsum, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      g_fs_active[dev][i] = n;
+    }
   return e;
 }
 

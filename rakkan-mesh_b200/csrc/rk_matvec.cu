@@ -87,8 +87,31 @@ RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__re
       stage_wait();
       __syncthreads();
       if (warp == 0) {
-#pragma unroll 8
-        for (int i = lane; i < m; i += 32) s = __fadd_rn(s, __fmul_rn(stage[i], stage[i]));
+        // Lane j's chain over elements j, j+32, ... (Dot32's order), its
+        // operands in eight rotating registers refilled eight steps ahead
+        // and each square formed a step before it is added.
+        const float *xs_ = stage + lane;
+        const int ns = m >> 5;
+        int k = 0;
+        if (ns >= 8) {
+          float r0 = xs_[0], r1 = xs_[32], r2 = xs_[64], r3 = xs_[96];
+          float r4 = xs_[128], r5 = xs_[160], r6 = xs_[192], r7 = xs_[224];
+          float sq = __fmul_rn(r0, r0);
+          for (; k + 8 <= ns; k += 8) {
+            const float *nx = xs_ + 32 * (k + 16 <= ns ? k + 8 : k);
+#define RK_SS_STEP(J, RN)                         \
+  {                                               \
+    const float sqn = __fmul_rn(RN, RN);          \
+    r##J = nx[32 * J];                            \
+    s = __fadd_rn(s, sq);                         \
+    sq = sqn;                                     \
+  }
+            RK_SS_STEP(0, r1) RK_SS_STEP(1, r2) RK_SS_STEP(2, r3) RK_SS_STEP(3, r4)
+            RK_SS_STEP(4, r5) RK_SS_STEP(5, r6) RK_SS_STEP(6, r7) RK_SS_STEP(7, r0)
+#undef RK_SS_STEP
+          }
+        }
+        for (; k < ns; k++) s = __fadd_rn(s, __fmul_rn(xs_[32 * k], xs_[32 * k]));
       }
     }
     if (warp == 0) {
@@ -108,44 +131,52 @@ RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__re
       stage_wait();
       __syncthreads();
     }
-    // Thread t quantizes block t of the chunk on its own: its 32 values are
-    // independent, so the thread's work pipelines, and a block costs a few
-    // instructions per value instead of warp-wide reductions. The values are
-    // read in a rotated order so that the threads of a warp hit different
-    // banks (amax and the integer sum are order free).
-    for (int t = threadIdx.x; t < m / 32; t += blockDim.x) {
+    // Four threads (a lane quad) quantize block t of the chunk, eight
+    // values each: amax and the integer sum are quad reductions (both order
+    // free). A thread reads its eight values in an order rotated by t, so
+    // the 32 lanes of a warp hit 32 different banks.
+    const int ntask = (m / 32) * 4;
+    for (int task = threadIdx.x; task < ntask; task += blockDim.x) {
+      const int t = task >> 2, sub = task & 3;
+      const unsigned qmask = 0xfu << (lane & ~3);
       const int b = c0 / 32 + t;
-      const float *src = stage + t * 32;
-      float v[32];
+      const float *src = stage + t * 32 + sub * 8;
+      float v[8];
       uint32_t kmax = 0;
 #pragma unroll
-      for (int j = 0; j < 32; j++) {
-        const int jj = (j + t) & 31;
+      for (int j = 0; j < 8; j++) {
+        const int jj = (j + t) & 7;
         float vv = src[jj];
-        if (NORM) vv = __fmul_rn(wstage[t * 32 + jj], __fmul_rn(inv, vv));
+        if (NORM) vv = __fmul_rn(wstage[t * 32 + sub * 8 + jj], __fmul_rn(inv, vv));
         v[j] = vv;
         kmax = max(kmax, f2u(fabsf(vv)));
       }
+      kmax = max(kmax, __shfl_xor_sync(qmask, kmax, 1));
+      kmax = max(kmax, __shfl_xor_sync(qmask, kmax, 2));
       // amax as Go's max: an unsigned max of the |v| bit patterns (bit order
       // is value order for non-negative floats; a NaN lands above +Inf).
       const float amax = kmax > 0x7f800000u ? u2f(kCanonNaN) : u2f(kmax);
       const float d = __fmul_rn(amax, u2f(K_1_127));
-      int8_t *q = qx + b * 32;
+      int8_t *q = qx + b * 32 + sub * 8;
       int sum = 0;
       if (d == 0.0f || d != d) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) q[(j + t) & 31] = 0;
+        for (int j = 0; j < 8; j++) q[(j + t) & 7] = 0;
       } else {
         const float id = recip32(d);
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < 8; j++) {
           const int qq = quant_q8(__fmul_rn(v[j], id));
-          q[(j + t) & 31] = (int8_t)qq;
+          q[(j + t) & 7] = (int8_t)qq;
           sum += qq;
         }
       }
-      xs[b] = d;
-      if (xsum) xsum[b] = sum;
+      sum += __shfl_xor_sync(qmask, sum, 1);
+      sum += __shfl_xor_sync(qmask, sum, 2);
+      if (sub == 0) {
+        xs[b] = d;
+        if (xsum) xsum[b] = sum;
+      }
     }
   }
 }
@@ -456,17 +487,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
       cursor_next(pf, a, nsub, nseg);
     }
   }
-  griddep_wait();
-  // The input's loads go first, ahead of the weight ring's copies. A
-  // gathered input (row sharding) arrives as tagged words, read once each
-  // carries this step's tag of the gather point.
+  // The norm weights are weights too: their copies start now.
   const bool norm = a.pro == PRO_NORM_QUANT;
   const bool gathered = a.wait.ll != nullptr;
   float *stage = reinterpret_cast<float *>(p);
   const int sf = a.pro != PRO_GIVEN ? stage_floats(cols, norm) : 0;
-  if (a.pro != PRO_GIVEN)
-    stage_load(gathered ? nullptr : a.x, norm && cols <= sf ? a.norm_w : nullptr, 0, min(cols, sf), stage,
-               stage + sf);
+  if (norm && cols <= sf) stage_load(nullptr, a.norm_w, 0, cols, stage, stage + sf);
+  griddep_wait();
+  // The input's loads go first, ahead of the weight ring's copies. A
+  // gathered input (row sharding) arrives as tagged words, read once each
+  // carries this step's tag of the gather point.
+  if (a.pro != PRO_GIVEN && !gathered) stage_load(a.x, nullptr, 0, min(cols, sf), stage, stage + sf);
   if (lane == 0)
     for (int k = 0; k < SLOTS; k++) issue();
   if (gathered &&
