@@ -122,7 +122,13 @@ RK_DEV float exp32(float x) {
   if (x != x) return u2f(kCanonNaN);
   if (x > u2f(K_88_72)) return u2f(0x7f800000u);
   if (x < u2f(K_M103_97)) return 0.0f;
-  float n = rintf(__fmul_rn(x, u2f(K_LOG2E)));
+  // n = RoundToEven(x·log2e) by the 1.5·2^23 shifter: here |x·log2e| < 151,
+  // so t lies in [2^23, 2^24) where the float grid is the integers, and the
+  // addition's round-to-nearest-even is the rounding wanted (1.5·2^23 is
+  // even, so ties keep their parity); t's low mantissa bits are n + 2^22.
+  // (n is +0 where rint gives -0; x - (±0)·c is x either way.)
+  const float t = __fadd_rn(__fmul_rn(x, u2f(K_LOG2E)), 12582912.0f);
+  float n = __fsub_rn(t, 12582912.0f);
   float r = __fsub_rn(x, __fmul_rn(n, u2f(K_LN2HI)));
   r = __fsub_rn(r, __fmul_rn(n, u2f(K_LN2LO)));
   float p = u2f(K_1_720);
@@ -132,7 +138,7 @@ RK_DEV float exp32(float x) {
   p = __fadd_rn(__fmul_rn(p, r), 0.5f);
   p = __fadd_rn(__fmul_rn(p, r), 1.0f);
   p = __fadd_rn(__fmul_rn(p, r), 1.0f);
-  int ni = int(n);
+  const int ni = (int)(f2u(t) & 0x7fffffu) - 0x400000;
   // p·2^n rounded once to float32. When 2^n is a normal float the float
   // product is that single rounding already; otherwise (n > 127 or n < -126)
   // form the exact product in float64 and round it once.

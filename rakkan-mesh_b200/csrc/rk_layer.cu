@@ -719,32 +719,30 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   if (P32 > 0) {
     // Eight (weight, value) float4 pairs in rotation, as in the sum chain:
     // quad k's pair is refilled from 32 positions further on once its
-    // products are formed, and the products are formed two quads before
-    // the chain adds them, so only adds sit between adds and a product is
-    // never waited for. The last round's refills re-read its own
-    // positions (the rows end soon after P).
+    // products are formed, and the products are formed one quad before
+    // the chain adds them, so only adds sit between adds. The last round's
+    // refills re-read its own positions (the rows end soon after P).
     float4 w0 = ld4(w), w1 = ld4(w + 4), w2 = ld4(w + 8), w3 = ld4(w + 12);
     float4 w4 = ld4(w + 16), w5 = ld4(w + 20), w6 = ld4(w + 24), w7 = ld4(w + 28);
     float4 v0 = ld4(v), v1 = ld4(v + 4), v2 = ld4(v + 8), v3 = ld4(v + 12);
     float4 v4 = ld4(v + 16), v5 = ld4(v + 20), v6 = ld4(v + 24), v7 = ld4(v + 28);
 #define RK_WS_MUL(W, V) make_float4(__fmul_rn(W.x, V.x), __fmul_rn(W.y, V.y), __fmul_rn(W.z, V.z), __fmul_rn(W.w, V.w))
-    float4 p0 = RK_WS_MUL(w0, v0), p1 = RK_WS_MUL(w1, v1);
+    float4 pc = RK_WS_MUL(w0, v0);
     for (int t = 0; t < P32; t += 32) {
       const int tn = t + 32 < P32 ? t + 32 : t;
 #define RK_WS_STEP(K, WN, VN)              \
   {                                        \
-    const float4 p2 = RK_WS_MUL(WN, VN);   \
+    const float4 pn = RK_WS_MUL(WN, VN);   \
     w##K = ld4(w + tn + 4 * K);            \
     v##K = ld4(v + tn + 4 * K);            \
-    acc = __fadd_rn(acc, p0.x);            \
-    acc = __fadd_rn(acc, p0.y);            \
-    acc = __fadd_rn(acc, p0.z);            \
-    acc = __fadd_rn(acc, p0.w);            \
-    p0 = p1;                               \
-    p1 = p2;                               \
+    acc = __fadd_rn(acc, pc.x);            \
+    acc = __fadd_rn(acc, pc.y);            \
+    acc = __fadd_rn(acc, pc.z);            \
+    acc = __fadd_rn(acc, pc.w);            \
+    pc = pn;                               \
   }
-      RK_WS_STEP(0, w2, v2) RK_WS_STEP(1, w3, v3) RK_WS_STEP(2, w4, v4) RK_WS_STEP(3, w5, v5)
-      RK_WS_STEP(4, w6, v6) RK_WS_STEP(5, w7, v7) RK_WS_STEP(6, w0, v0) RK_WS_STEP(7, w1, v1)
+      RK_WS_STEP(0, w1, v1) RK_WS_STEP(1, w2, v2) RK_WS_STEP(2, w3, v3) RK_WS_STEP(3, w4, v4)
+      RK_WS_STEP(4, w5, v5) RK_WS_STEP(5, w6, v6) RK_WS_STEP(6, w7, v7) RK_WS_STEP(7, w0, v0)
 #undef RK_WS_MUL
 #undef RK_WS_STEP
     }
