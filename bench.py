@@ -260,6 +260,11 @@ def main():
     import torch
     dist = None
     if world > 1:
+        # The ranks' collectives here are two small all-gathers per token
+        # (the rest travel as NVLink stores inside the kernels); NCCL's
+        # NVLink SHARP path would add multicast buffer registration for
+        # nothing, so it stays off unless the caller sets it.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
@@ -336,7 +341,7 @@ def main():
         cfg = workload(args)
         cfg["parallelism"] = f"rows{world}" if sharded else (f"replicas{world}" if world > 1 else "none")
         if sharded:
-            cfg["gathers"] = "fused (NVLink stores + flags)" if dm.stage.fused_gathers() else "NCCL all-gather"
+            cfg["gathers"] = "fused (tagged words stored over NVLink)" if dm.stage.fused_gathers() else "NCCL all-gather"
         line = {
             "metric": METRIC, "value": seqs * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,

@@ -519,6 +519,11 @@ RK_DEV void cluster_sync() {
   __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of a cluster barrier: every CTA of the cluster must have
+// started before any reaches another's shared memory, so the kernel
+// arrives as it starts and waits before its first remote access.
+RK_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+RK_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 // The address of the same shared-memory location in CTA `rank` of the cluster.
 RK_DEV uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
   uint32_t r;
@@ -571,6 +576,8 @@ __global__ void __launch_bounds__(kFsMaxThreads)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  __syncwarp();
+  cluster_arrive_relaxed();
   griddep_wait();
   const int P = attn_positions(a);
   const int P4 = P & ~3;
@@ -613,6 +620,8 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   nan = __any_sync(0xffffffffu, nan);
   if (lane == 0) reinterpret_cast<uint32_t *>(red)[g * wph + sub] = nan ? 0xffffffffu : key;
   __syncthreads();
+  __syncwarp();
+  cluster_wait();  // every member has started: its shared memory may be written
   if (threadIdx.x < gpb) {
     uint32_t k = 0;
     for (int j = 0; j < wph; j++) k = max(k, reinterpret_cast<const uint32_t *>(red)[threadIdx.x * wph + j]);
@@ -776,12 +785,14 @@ bool attention_fused_ok(int heads, int kv_heads, int hs, int max_positions) {
 // once; filled by init_layer_attributes.
 static int g_fs_active[64][4];
 
-// The cluster size for a k_attn_softmax_wsum grid: the largest that divides
-// the slices and whose clusters are all resident at once, else 1.
+// The cluster size for a k_attn_softmax_wsum grid: the largest of 4 and 2
+// that divides the slices and whose clusters are all resident at once, else
+// 1. (Each CTA stores P floats per head into the members' shared memory
+// whatever the size, so 4 is enough to split the exps.)
 static int fs_cluster(dim3 grid) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
-  for (int i = 3, c = 8; i >= 1; i--, c /= 2)
+  for (int i = 2, c = 4; i >= 1; i--, c /= 2)
     if (grid.y % c == 0 && (long long)g_fs_active[dev][i] * c >= (long long)grid.x * grid.y) return c;
   return 1;
 }

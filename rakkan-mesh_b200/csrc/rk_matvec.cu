@@ -21,6 +21,7 @@
 
 #include "rk_common.cuh"
 #include "rk_matvec.cuh"
+#include "rk_umma.cuh"
 
 namespace rk {
 
@@ -243,11 +244,6 @@ RK_DEV uint64_t evict_first_policy() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
-}
-
-// Brings bytes of global memory into L2 without occupying the SM.
-RK_DEV void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 RK_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
@@ -482,8 +478,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
     Cursor pf = pc;
     for (long long k = 0; k < min(total, (long long)kPrefetchSegs); k++) {
       const SegInfo s = seg_info<FMT>(a, nb, pf);
-      bulk_prefetch_l2(s.wsrc, s.wbytes);
-      bulk_prefetch_l2(s.ssrc, s.sbytes);
+      umma::bulk_prefetch_l2(s.wsrc, s.wbytes);
+      umma::bulk_prefetch_l2(s.ssrc, s.sbytes);
       cursor_next(pf, a, nsub, nseg);
     }
   }

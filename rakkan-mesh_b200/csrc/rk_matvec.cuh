@@ -94,7 +94,6 @@ cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
 
 int matvec_smem_bytes(int fmt, int cols);
 
-
 // Whether a matvec of this format and width can quantize its input in its
 // own prologue (PRO_NORM_QUANT when norm, else PRO_QUANT): the input and its
 // staging must fit shared memory beside the weight rings.

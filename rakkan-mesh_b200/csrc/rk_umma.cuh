@@ -55,6 +55,12 @@ RK_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// Brings bytes of global memory into L2 without occupying the SM (16-byte
+// aligned address, size a multiple of 16).
+RK_DEV void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 RK_DEV void prefetch_tmap(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }

@@ -2,13 +2,13 @@
 for bit.
 
 The stage's attention keeps the softmax sum and the value sums as serial
-chains in position order (model.go:571-587, 640-654); at long contexts the
-single softmax + value kernel hands the exps to its chain warp in 128-
-position chunks and the products through a ring of 32-position slots, so
-these cases reach many chunks, ring wraps and a partial last chunk. Both of
-its value-chain forms run: ring (heads per kv head x 8 <= 32 chains) and
-in-thread (more chains). Both sides fill positions 0..P-1 of every layer's
-cache with the same seeded values (rk_stage_fill_cache /
+chains in position order (model.go:571-587, 640-654). At long contexts the
+single softmax + value kernel splits the maximum and the exps over a
+thread-block cluster (each CTA a chunk of the positions, exchanged through
+distributed shared memory) and runs the chains from rotating registers, so
+these cases reach many chunks, uneven last chunks and one or two chain warps
+(heads per kv head x 8 chains). Both sides fill positions 0..P-1 of every
+layer's cache with the same seeded values (rk_stage_fill_cache /
 rko_stage_fill_cache), then decode positions P and P+1.
 """
 import numpy as np
@@ -22,11 +22,11 @@ pytestmark = pytest.mark.gpu
 
 # name: (config overrides, filled positions)
 CASES = {
-    # 4 query heads per kv head, head width 128: 32 chains, the ring.
+    # 4 query heads per kv head, head width 128: 32 chains, one warp.
     "gqa4_hs128": (dict(heads=8, kv_heads=2, head_dim=128), 4093),
-    # One query head per kv head: 8 chains, the ring.
+    # One query head per kv head: 8 chains.
     "mha_hs64": (dict(heads=4, kv_heads=4, head_dim=64), 2050),
-    # 7 query heads per kv head: 56 chains, formed in-thread.
+    # 7 query heads per kv head: 56 chains over two warps.
     "gqa7_hs64": (dict(heads=14, kv_heads=2, head_dim=64), 1531),
     # 8 per kv head: 64 chains over two chain warps.
     "gqa8_hs64": (dict(heads=16, kv_heads=2, head_dim=64), 1200),
