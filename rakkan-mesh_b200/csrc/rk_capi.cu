@@ -116,6 +116,7 @@ static int check_dev_err(rk_device *d) {
   CK(cudaMemcpy(&e, d->err_dev, sizeof e, cudaMemcpyDeviceToHost));
   if (e != 0) {
     CK(cudaMemset(d->err_dev, 0, sizeof(int)));
+    if (e == DEV_ERR_RANGE) return fail(RK_ERR_ARGS, "a kernel refused an out-of-range index (device error %d)", e);
     return fail(RK_ERR_TIMEOUT, "a kernel's bounded wait expired (device error %d)", e);
   }
   return RK_OK;
@@ -1859,7 +1860,7 @@ extern "C" int rk_embed(rk_matrix *table, int token, float *x) {
   if (rc) return rc;
   memcpy(d->pin_in, &token, sizeof token);
   CK(cudaMemcpyAsync(d->mv_xsum, d->pin_in, sizeof(int), cudaMemcpyHostToDevice, d->st));
-  CK(launch_embed(table->fmt, table->w, table->s, table->cols, d->mv_xsum, d->mv_x, d->st));
+  CK(launch_embed(table->fmt, table->w, table->s, table->rows, table->cols, d->mv_xsum, d->mv_x, d->err_dev, d->st));
   CK(cudaMemcpyAsync(d->pin_out, d->mv_x, 4 * (size_t)table->cols, cudaMemcpyDeviceToHost, d->st));
   if ((rc = sync_dev(d))) return rc;
   memcpy(x, d->pin_out, 4 * (size_t)table->cols);
@@ -1890,7 +1891,8 @@ __global__ void k_feed_token(const int *next, int *token) {
 
 static int record_model(rk_model *m, cudaStream_t st) {
   rk_stage *s = m->stage;
-  CK(launch_embed(m->embed->fmt, m->embed->w, m->embed->s, s->c.dim, m->token_dev, s->x, st));
+  CK(launch_embed(m->embed->fmt, m->embed->w, m->embed->s, m->embed->rows, s->c.dim, m->token_dev, s->x,
+                  m->d->err_dev, st));
   int rc = record_layers(s, st);
   if (rc) return rc;
   if ((rc = record_head(m->head, s->x, st))) return rc;
@@ -1925,10 +1927,14 @@ extern "C" int rk_model_new(rk_device *d, rk_matrix *embed, rk_stage *stage, rk_
   m->embed = embed;
   m->stage = stage;
   m->head = head;
+  // The graph embeds *token_dev (argmax writes the next one at the end of a
+  // step), so a replay before any rk_model_step starts from token 0.
   cudaError_t e = cudaMalloc(&m->token_dev, 16);
+  if (e == cudaSuccess) e = cudaMemset(m->token_dev, 0, 16);
   if (e == cudaSuccess) e = cudaMalloc(&m->key_dev, 16);
   if (e == cudaSuccess) e = cudaMemset(m->key_dev, 0, 16);
   if (e == cudaSuccess) e = cudaMalloc(&m->next_dev, 16);
+  if (e == cudaSuccess) e = cudaMemset(m->next_dev, 0, 16);
   if (e == cudaSuccess) e = cudaMallocHost(&m->pin_tok, 64);
   if (e == cudaSuccess) e = cudaMallocHost(&m->pin_logits, 4 * (size_t)stage->c.vocab);
   if (e != cudaSuccess) {

@@ -953,10 +953,16 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // Embed (Matrix.Row + DequantQ8/Q4, model.go:216-231; quant.go:130-146).
 // ---------------------------------------------------------------------------
-__global__ void k_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x) {
+__global__ void k_embed(int fmt, const void *table, const float *scales, int rows, int dim, const int *token_dev,
+                        float *x, int *err) {
   griddep_trigger();
   griddep_wait();
   const long long tok = *token_dev;
+  // A token outside the table is refused (the error word records it), not read.
+  if (tok < 0 || tok >= rows) {
+    if (err && blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, DEV_ERR_RANGE);
+    return;
+  }
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < dim; j += gridDim.x * blockDim.x) {
     float v;
     if (fmt == FMT_Q8_0) {
@@ -975,9 +981,9 @@ __global__ void k_embed(int fmt, const void *table, const float *scales, int dim
     x[j] = v;
   }
 }
-cudaError_t launch_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x,
-                         cudaStream_t st) {
-  launch_k(k_embed, (dim + 255) / 256, 256, 0, st, fmt, table, scales, dim, token_dev, x);
+cudaError_t launch_embed(int fmt, const void *table, const float *scales, int rows, int dim, const int *token_dev,
+                         float *x, int *err, cudaStream_t st) {
+  launch_k(k_embed, (dim + 255) / 256, 256, 0, st, fmt, table, scales, rows, dim, token_dev, x, err);
   return cudaGetLastError();
 }
 

@@ -77,9 +77,10 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st);
 // post-processing folded into the scores kernel where it tiles the keys.
 cudaError_t launch_attention_post(const QkvPostArgs &qp, const AttnArgs &a, cudaStream_t st);
 
-// Embed (model.go:660-664): x = dequantized row *token_dev of a table.
-cudaError_t launch_embed(int fmt, const void *table, const float *scales, int dim, const int *token_dev, float *x,
-                         cudaStream_t st);
+// Embed (model.go:660-664): x = dequantized row *token_dev of a table of
+// `rows` rows; a token outside [0, rows) sets DEV_ERR_RANGE in *err instead.
+cudaError_t launch_embed(int fmt, const void *table, const float *scales, int rows, int dim, const int *token_dev,
+                         float *x, int *err, cudaStream_t st);
 
 // argmax (sample.go:45-53): the first index of the strict maximum.
 cudaError_t launch_argmax(const float *v, int n, int *out, cudaStream_t st);

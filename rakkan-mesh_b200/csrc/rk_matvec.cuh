@@ -17,7 +17,9 @@ enum Epi : int {
 };
 
 // Device error codes written to the device's error word.
-enum DevErr : int { DEV_OK = 0, DEV_ERR_TIMEOUT = 1 };
+// Device error word values: a bounded wait gave up; a kernel refused an
+// out-of-range index (and skipped the access).
+enum DevErr : int { DEV_OK = 0, DEV_ERR_TIMEOUT = 1, DEV_ERR_RANGE = 2 };
 
 // Row sharding's all-gather, fused into the kernels (one process per GPU,
 // peers' memory mapped through CUDA IPC), in the manner of a low-latency
