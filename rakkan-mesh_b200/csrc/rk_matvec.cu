@@ -268,7 +268,11 @@ __host__ __device__ constexpr int stage_bytes(int cols, bool norm) {
 }
 
 constexpr int kSegBytes = 4096;  // weight bytes per segment
-constexpr int kPrefetchSegs = 4;  // segments per warp prefetched into L2 before the predecessor ends
+// Segments per warp prefetched into L2 before the predecessor ends. One is
+// best (measured over 0, 1, 2, 4: 288, 290.5, 289, 282 tok/s on the 8B
+// step): the SM's copy engine works through bulk prefetches in order, so
+// more of them delay the weight ring's own copies after the wait.
+constexpr int kPrefetchSegs = 1;
 
 template <int FMT>
 struct QTraits;
