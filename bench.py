@@ -21,9 +21,11 @@ cpu_baseline: the CPU oracle (a C restatement of the reference's Go CPU
 --impl reference runs only that CPU implementation (no GPU).
 With --gpus N (under torchrun) the default --mode rows shards every layer's
 weight rows over the N GPUs (whole kv heads per GPU) and reassembles each
-product's output with an NCCL all-gather inside the step's CUDA graph: one
-sequence decoded by all N GPUs (strong scaling; value = its tokens/s).
---mode replicas runs N independent copies instead (weak scaling).
+product's output inside the kernels (tagged words stored over NVLink; NCCL
+all-gathers where that is not possible): one sequence decoded by all N GPUs
+(strong scaling; value = its tokens/s). --mode replicas runs N independent
+copies instead (weak scaling); --mode pipeline splits the layers into N
+stages (rk_plan_stages) that pass the activation on (roofline not measured).
 """
 import argparse
 import json
@@ -53,7 +55,7 @@ def parse():
     p.add_argument("--dtype", default="q8_0")
     p.add_argument("--ctx", type=int, default=CTX)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--mode", default="rows", choices=["rows", "replicas"],
+    p.add_argument("--mode", default="rows", choices=["rows", "replicas", "pipeline"],
                    help="N>1: shard every layer's rows over the N GPUs (NCCL all-gather; one sequence), "
                         "or run N independent replicas")
     p.add_argument("--layers", type=int, default=0,
@@ -269,6 +271,8 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
     import rkcuda as rk
+    if world > 1 and args.mode == "pipeline":
+        return run_pipeline(args, world, rank, local, dist, torch)
     import synth
 
     dev = rk.Device(local)
@@ -368,6 +372,70 @@ def main():
     dev.close()
     if dist:
         dist.destroy_process_group()
+
+
+def run_pipeline(args, world, rank, local, dist, torch):
+    """--mode pipeline: the layers split over the N GPUs by rk_plan_stages
+    (planStages with equal speeds), the activation passed rank to rank;
+    one sequence, so the stages run one after another (config 5's layer
+    pipeline; no batch-1 speed-up is expected, as in the reference)."""
+    import numpy as np
+    import rkcuda as rk
+    import synth
+    dev = rk.Device(local)
+    over = {"layers": args.layers} if args.layers > 0 else {}
+    c = synth.config(args.model, args.dtype, seq_len=args.ctx + 64, **over)
+    gid = [rk.group_id() if rank == 0 else None]
+    dist.broadcast_object_list(gid, src=0)
+    group = rk.Group(dev, world, rank, gid[0])
+    per = sum(synth.matrix_bytes(synth.mat_fmt(c, k), int(np.prod(synth.mat_shape(c, k)))) for k in synth.MATS)
+    spans = rk.plan_stages([per] * c.layers, [per] * c.layers, [1.0] * world, [per * c.layers] * world, world)
+    node, first, end = spans[rank]
+    pr = synth.PipelineRank(dev, c, SEED, group, first, end, ctx=args.ctx + 64)
+    pr.stage.fill_cache(args.ctx, SEED)
+    pos, tok = args.ctx, 1
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize(local)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    pr.pipeline.bench(pos, max(3, args.warmup))
+    barrier()
+    with Clocks(local) as clk:
+        ms = pr.pipeline.bench(pos, args.steps)
+        barrier()
+    clocks = clk.summary()
+    ms = max_over_ranks(ms)
+    for _ in range(max(3, args.warmup)):
+        pr.pipeline.step(tok, pos)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        pr.pipeline.step(tok, pos)
+    barrier()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / args.steps)
+    if rank == 0:
+        cfg = workload(args)
+        cfg["parallelism"] = f"pipeline{world}"
+        cfg["stages"] = [[a, b] for _, a, b in spans]
+        line = {
+            "metric": METRIC, "value": 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8xint8->int32, f32 combine", "data": "synthetic", "config": cfg,
+            "e2e": {"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+            "roofline": None, "cpu_baseline": None, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    pr.free()
+    barrier()
+    group.free()
+    dev.close()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

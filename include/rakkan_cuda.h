@@ -73,6 +73,7 @@ typedef struct rk_stage rk_stage;
 typedef struct rk_head rk_head;
 typedef struct rk_model rk_model;
 typedef struct rk_group rk_group;
+typedef struct rk_pipeline rk_pipeline;
 
 /* gpu.Info (device.go:21-47). */
 typedef struct {
@@ -240,8 +241,9 @@ int rk_model_generate(rk_model *m, const int *prompt, int n_prompt, int n_new, i
  * [r·kvHeads/G, …) of Wq/Wk/Wv (rows of whole heads, so RoPE, the KV cache
  * and attention stay local), rows [r·dim/G, …) of Wo and W2, rows
  * [r·hidden/G, …) of W1 and W3, and rows [r·vocab/G, …) of the classifier;
- * after attention, Wo, W1/W3 and W2 the outputs are reassembled with an
- * NCCL all-gather over NVLink, captured in the step's CUDA graph. kvHeads,
+ * after attention, Wo, W1/W3 and W2 the outputs are reassembled: each value
+ * stored into every rank's buffer over NVLink inside the producing kernel,
+ * or by an NCCL all-gather captured in the step's CUDA graph. kvHeads,
  * dim, hidden and vocab must be multiples of G. NCCL (libnccl.so.2) is
  * loaded at run time by the first group call. */
 #define RK_GROUP_ID_BYTES 128
@@ -265,14 +267,47 @@ int rk_layer_from_device_shard(rk_device *d, const rk_config *c, int nshards, in
  * model built on it, run collectively on every rank. */
 int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *g,
                        rk_stage **out);
-/* 1 when the stage's gathers are fused into its kernels (NVLink stores into
- * the peers' buffers through CUDA IPC, a flag per gather point); 0 when they
- * are NCCL all-gathers (peers not reachable by P2P, RK_GATHER=nccl, or an
- * unsharded stage). */
+/* 1 when the stage's gathers are fused into its kernels (each value stored
+ * into every rank's buffer over NVLink through CUDA IPC, as an 8-byte word
+ * with a step tag that the reader waits for); 0 when they are NCCL
+ * all-gathers (peers not reachable by P2P, RK_GATHER=nccl, or an unsharded
+ * stage). */
 int rk_stage_fused_gathers(const rk_stage *s);
 /* A head whose classifier holds the rank's vocab/G rows; logits are whole. */
 int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *g,
                       rk_head **out);
+
+/* ---- Layer pipeline (config 5): planStages (internal/llm/plan.go:122-207)
+ *      and the stage-to-stage hand-off of llm's pipelined generation
+ *      (generate.go:522-585 over the stages a plan assigns). ---- */
+/* The plan: layer l reads cost[l] bytes per token and needs mem[l] bytes of
+ * memory; node n streams speed[n] GB/s, holds capacity[n] bytes (a node
+ * fits layers [from, to) when their mem sums to at most that) and has
+ * free_mem[n] (ties; may be NULL). stages <= 0: the fastest nodes take as
+ * many layers as they hold; stages > 0: that many of the fastest nodes (no
+ * more than nodes or layers), a layer each at least, the slowest stage as
+ * quick as can be. Nodes rank by speed, then free memory, then index (the
+ * reference breaks the last tie by peer id). On entry *nspans is the room in
+ * span_*; on return, the number of spans: span s is layers
+ * [span_from[s], span_to[s]) on node span_node[s], in order. Host only. */
+int rk_plan_stages(const int64_t *cost, const int64_t *mem, int layers, const double *speed, const int64_t *capacity,
+                   const int64_t *free_mem, int nodes, int stages, int *nspans, int *span_node, int *span_from,
+                   int *span_to);
+/* One rank's part of a pipeline over group g (one GPU per rank): stage holds
+ * this rank's contiguous layers (an unsharded stage), the first rank also
+ * passes the embedding table and the last the head (the others NULL).
+ * Collective. */
+int rk_pipeline_new(rk_group *g, rk_matrix *embed, rk_stage *stage, rk_head *head, rk_pipeline **out);
+void rk_pipeline_free(rk_pipeline *p);
+/* One token through all stages (collective: every rank calls it with the
+ * same token and position): the first rank embeds it, x (dim floats) passes
+ * rank to rank by NCCL send/receive, the last rank computes the logits and
+ * their argmax, which every rank gets in *next. logits (vocab floats) are
+ * written on the last rank only; may be NULL. */
+int rk_pipeline_step(rk_pipeline *p, int token, int pos, float *logits, int *next);
+/* iters pipeline steps at position pos as graph replays, device-timed
+ * (each rank times its own stream; collective). */
+int rk_bench_pipeline(rk_pipeline *p, int pos, int iters, float *ms_per_step);
 
 /* ---- rakkan_tensor_v1 matmul / matmul_t (tensor.go:286-339) ----
  * C[m×n] = A[m×k]·B with B [k×n] (transposed 0, "matmul") or [n×k]

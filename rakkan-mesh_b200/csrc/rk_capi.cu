@@ -13,6 +13,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <condition_variable>
 #include <cstdarg>
 #include <cstdlib>
@@ -232,6 +233,9 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*broadcast)(const void *, void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   const char *(*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -246,8 +250,12 @@ static const NcclApi &nccl() {
     a.comm_init_rank = (decltype(a.comm_init_rank))dlsym(h, "ncclCommInitRank");
     a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
     a.all_gather = (decltype(a.all_gather))dlsym(h, "ncclAllGather");
+    a.send = (decltype(a.send))dlsym(h, "ncclSend");
+    a.recv = (decltype(a.recv))dlsym(h, "ncclRecv");
+    a.broadcast = (decltype(a.broadcast))dlsym(h, "ncclBroadcast");
     a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
-    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather && a.error_string;
+    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather && a.send && a.recv &&
+           a.broadcast && a.error_string;
     return a;
   }();
   return api;
@@ -2370,6 +2378,264 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
       CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, s->vals[l], d->st));
   }
   return sync_dev(d);
+}
+
+// ---------------------------------------------------------------------------
+// Layer pipeline: the stage plan (planStages, internal/llm/plan.go:122-207)
+// and one rank's part of a pipelined step.
+// ---------------------------------------------------------------------------
+extern "C" int rk_plan_stages(const int64_t *cost, const int64_t *mem, int layers, const double *speed,
+                              const int64_t *capacity, const int64_t *free_mem, int nodes, int stages, int *nspans,
+                              int *span_node, int *span_from, int *span_to) {
+  if (!cost || !mem || layers <= 0 || !speed || !capacity || nodes < 0 || !nspans || !span_node || !span_from ||
+      !span_to)
+    return fail(RK_ERR_ARGS, "bad argument");
+  // fits(n, from, to): the node holds layers [from, to) (the reference's
+  // nodeFit over memory, here the layers' bytes against the node's).
+  std::vector<int64_t> msum(layers + 1, 0), sum(layers + 1, 0);
+  for (int i = 0; i < layers; i++) {
+    msum[i + 1] = msum[i] + mem[i];
+    sum[i + 1] = sum[i] + cost[i];
+  }
+  auto fits = [&](int n, int from, int to) { return msum[to] - msum[from] <= capacity[n]; };
+  // Nodes that hold at least one layer, fastest first (then more free
+  // memory, then lower index: sortNodes, plan.go:103-113).
+  std::vector<int> order;
+  for (int n = 0; n < nodes; n++)
+    for (int i = 0; i < layers; i++)
+      if (fits(n, i, i + 1)) {
+        order.push_back(n);
+        break;
+      }
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    if (speed[a] != speed[b]) return speed[a] > speed[b];
+    const int64_t fa = free_mem ? free_mem[a] : 0, fb = free_mem ? free_mem[b] : 0;
+    if (fa != fb) return fa > fb;
+    return a < b;
+  });
+  struct Span {
+    int from, to, node;
+  };
+  std::vector<Span> out;
+  if (stages <= 0) {
+    // The fastest nodes take as many layers as they hold (plan.go:141-156).
+    int at = 0;
+    for (int n : order) {
+      if (at == layers) break;
+      int k = 0;
+      while (k < layers - at && fits(n, at, at + k + 1)) k++;
+      if (k > 0) {
+        out.push_back({at, at + k, n});
+        at += k;
+      }
+    }
+    if (at < layers || out.empty()) return fail(RK_ERR_ARGS, "the model's %d layers do not fit the nodes", layers);
+  } else {
+    const int use = std::min(std::min(stages, (int)order.size()), layers);
+    order.resize(use);
+    if (order.empty()) return fail(RK_ERR_ARGS, "no node holds a layer");
+    // Cut the layers, in node order, into stages within `bound` (seconds
+    // per token: bytes over speed), each later node keeping a layer.
+    auto cut = [&](double bound, std::vector<Span> *res) {
+      int at = 0;
+      for (int j = 0; j < use; j++) {
+        const int n = order[j], left = use - j - 1;
+        int k = 0;
+        while (at + k < layers - left && fits(n, at, at + k + 1) &&
+               (double)(sum[at + k + 1] - sum[at]) / std::max(speed[n], 1e-9) <= bound)
+          k++;
+        if (k == 0) return false;
+        if (res) res->push_back({at, at + k, n});
+        at += k;
+      }
+      return at >= layers;
+    };
+    std::vector<double> bounds;
+    for (int n : order)
+      for (int i = 0; i < layers; i++)
+        for (int j = i + 1; j <= layers; j++) bounds.push_back((double)(sum[j] - sum[i]) / std::max(speed[n], 1e-9));
+    std::sort(bounds.begin(), bounds.end());
+    bounds.erase(std::unique(bounds.begin(), bounds.end()), bounds.end());
+    // Go's lower-bound search over "cut succeeds" (slices.BinarySearchFunc),
+    // as the reference does. Where capacities make cutting non-monotone in
+    // the bound, its answer is still the reference's.
+    size_t lo = 0, hi = bounds.size();
+    while (lo < hi) {
+      const size_t mid = (lo + hi) / 2;
+      if (cut(bounds[mid], nullptr)) hi = mid;
+      else lo = mid + 1;
+    }
+    if (lo == bounds.size())
+      return fail(RK_ERR_ARGS, "the model's %d layers do not fit the %d fastest nodes", layers, use);
+    cut(bounds[lo], &out);
+  }
+  const int cap = *nspans;
+  if ((int)out.size() > cap) {
+    *nspans = (int)out.size();
+    return fail(RK_ERR_ARGS, "%d spans do not fit the %d given", (int)out.size(), cap);
+  }
+  *nspans = (int)out.size();
+  for (size_t i = 0; i < out.size(); i++) {
+    span_node[i] = out[i].node;
+    span_from[i] = out[i].from;
+    span_to[i] = out[i].to;
+  }
+  return RK_OK;
+}
+
+struct rk_pipeline {
+  rk_device *d = nullptr;
+  rk_group *grp = nullptr;
+  rk_matrix *embed = nullptr;  // first rank
+  rk_stage *stage = nullptr;
+  rk_head *head = nullptr;  // last rank
+  int *token_dev = nullptr, *next_dev = nullptr;
+  unsigned long long *key_dev = nullptr;
+  int *pin_tok = nullptr;
+  float *pin_logits = nullptr;
+  cudaGraphExec_t graph = nullptr;
+};
+
+static void pipeline_release(rk_pipeline *p) {
+  if (!p) return;
+  cudaSetDevice(p->d->ordinal);
+  cudaStreamSynchronize(p->d->st);
+  if (p->graph) cudaGraphExecDestroy(p->graph);
+  cudaFree(p->token_dev);
+  cudaFree(p->next_dev);
+  cudaFree(p->key_dev);
+  cudaFreeHost(p->pin_tok);
+  cudaFreeHost(p->pin_logits);
+  delete p;
+}
+
+// One rank's step: x from the previous rank (or the embedding of *token_dev
+// on the first), this rank's layers, x on to the next rank (or the head and
+// argmax on the last), then the next token from the last rank to all.
+static int record_pipeline(rk_pipeline *p, cudaStream_t st) {
+  rk_stage *s = p->stage;
+  rk_group *g = p->grp;
+  const int D = s->c.dim, last = g->n - 1;
+  ncclResult_t r;
+  if (g->rank == 0) {
+    CK(launch_embed(p->embed->fmt, p->embed->w, p->embed->s, p->embed->rows, D, p->token_dev, s->x, p->d->err_dev, st));
+  } else if ((r = nccl().recv(s->x, D, ncclFloat32, g->rank - 1, g->comm, st)) != ncclSuccess) {
+    return nccl_fail(r, "pipeline receive");
+  }
+  int rc = record_layers(s, st);
+  if (rc) return rc;
+  if (g->rank < last) {
+    if ((r = nccl().send(s->x, D, ncclFloat32, g->rank + 1, g->comm, st)) != ncclSuccess)
+      return nccl_fail(r, "pipeline send");
+  } else {
+    if ((rc = record_head(p->head, s->x, st))) return rc;
+    CK(launch_argmax_multi(p->head->logits, s->c.vocab, p->key_dev, p->next_dev, nullptr, st));
+  }
+  if ((r = nccl().broadcast(p->next_dev, p->next_dev, 1, ncclInt32, last, g->comm, st)) != ncclSuccess)
+    return nccl_fail(r, "pipeline token broadcast");
+  CK(cudaGetLastError());
+  return RK_OK;
+}
+
+extern "C" int rk_pipeline_new(rk_group *g, rk_matrix *embed, rk_stage *stage, rk_head *head, rk_pipeline **out) {
+  if (!g || !stage || !out) return fail(RK_ERR_ARGS, "null argument");
+  if (g->n < 2) return fail(RK_ERR_ARGS, "a pipeline needs at least two ranks");
+  if (stage->d != g->d || stage->G != 1) return fail(RK_ERR_ARGS, "the stage must be a whole (unsharded) stage on the group's device");
+  const bool first = g->rank == 0, last = g->rank == g->n - 1;
+  if (first != (embed != nullptr)) return fail(RK_ERR_ARGS, "the first rank, and only it, passes the embedding table");
+  if (last != (head != nullptr)) return fail(RK_ERR_ARGS, "the last rank, and only it, passes the head");
+  if (embed && (embed->d != g->d || embed->rows != stage->c.vocab || embed->cols != stage->c.dim))
+    return fail(RK_ERR_ARGS, "embedding table of the wrong shape or device");
+  if (head && (head->d != g->d || head->grp)) return fail(RK_ERR_ARGS, "the head must be a whole head on the group's device");
+  rk_device *d = g->d;
+  Guard gd(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  auto *p = new rk_pipeline();
+  p->d = d;
+  p->grp = g;
+  p->embed = embed;
+  p->stage = stage;
+  p->head = head;
+  cudaError_t e = cudaMalloc(&p->token_dev, 16);
+  if (e == cudaSuccess) e = cudaMemset(p->token_dev, 0, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&p->next_dev, 16);
+  if (e == cudaSuccess) e = cudaMemset(p->next_dev, 0, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&p->key_dev, 16);
+  if (e == cudaSuccess) e = cudaMemset(p->key_dev, 0, 16);
+  if (e == cudaSuccess) e = cudaMallocHost(&p->pin_tok, 64);
+  if (e == cudaSuccess && last) e = cudaMallocHost(&p->pin_logits, 4 * (size_t)stage->c.vocab);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  if (e != cudaSuccess) {
+    pipeline_release(p);
+    return cuda_fail(e, "pipeline allocation");
+  }
+  if ((rc = capture(d, [p](cudaStream_t st) { return record_pipeline(p, st); }, &p->graph))) {
+    pipeline_release(p);
+    return rc;
+  }
+  *out = p;
+  return RK_OK;
+}
+
+extern "C" void rk_pipeline_free(rk_pipeline *p) {
+  if (!p) return;
+  rk_device *d = p->d;
+  Guard g(d);
+  pipeline_release(p);
+}
+
+extern "C" int rk_pipeline_step(rk_pipeline *p, int token, int pos, float *logits, int *next) {
+  if (!p) return fail(RK_ERR_ARGS, "null pipeline");
+  rk_stage *s = p->stage;
+  if (pos < 0 || pos >= s->ctx) return fail(RK_ERR_ARGS, "position %d outside the stage's %d", pos, s->ctx);
+  if (token < 0 || token >= s->c.vocab) return fail(RK_ERR_ARGS, "token %d outside the vocabulary", token);
+  rk_device *d = p->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  p->pin_tok[0] = token;
+  p->pin_tok[1] = pos;
+  CK(cudaMemcpyAsync(p->token_dev, &p->pin_tok[0], 4, cudaMemcpyHostToDevice, d->st));
+  CK(cudaMemcpyAsync(s->pos_dev, &p->pin_tok[1], 4, cudaMemcpyHostToDevice, d->st));
+  CK(cudaGraphLaunch(p->graph, d->st));
+  const bool last = p->grp->rank == p->grp->n - 1;
+  if (logits && last)
+    CK(cudaMemcpyAsync(p->pin_logits, p->head->logits, 4 * (size_t)s->c.vocab, cudaMemcpyDeviceToHost, d->st));
+  CK(cudaMemcpyAsync(&p->pin_tok[2], p->next_dev, 4, cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  if (logits && last) memcpy(logits, p->pin_logits, 4 * (size_t)s->c.vocab);
+  if (next) *next = p->pin_tok[2];
+  return RK_OK;
+}
+
+extern "C" int rk_bench_pipeline(rk_pipeline *p, int pos, int iters, float *ms_per_step) {
+  if (!p || iters <= 0 || !ms_per_step) return fail(RK_ERR_ARGS, "bad argument");
+  rk_device *d = p->d;
+  if (pos < 0 || pos >= p->stage->ctx) return fail(RK_ERR_ARGS, "position out of range");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  p->pin_tok[4] = pos;
+  p->pin_tok[5] = 0;
+  CK(cudaMemcpyAsync(p->token_dev, &p->pin_tok[5], 4, cudaMemcpyHostToDevice, d->st));
+  CK(cudaEventRecord(e0, d->st));
+  for (int i = 0; i < iters; i++) {
+    CK(cudaMemcpyAsync(p->stage->pos_dev, &p->pin_tok[4], 4, cudaMemcpyHostToDevice, d->st));
+    CK(cudaGraphLaunch(p->graph, d->st));
+  }
+  CK(cudaEventRecord(e1, d->st));
+  CK(cudaEventSynchronize(e1));
+  float ms = 0.0f;
+  CK(cudaEventElapsedTime(&ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if ((rc = check_dev_err(d))) return rc;
+  *ms_per_step = ms / iters;
+  return RK_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -36,6 +36,7 @@ EXPORTS = [
     "rk_bench_matvec", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
     "rk_group_size", "rk_group_all_gather", "rk_layer_upload_shard", "rk_layer_from_device_shard",
     "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
+    "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
 ]
 
 
@@ -128,6 +129,9 @@ def lib():
             "rk_matrix_generate_rows": (i, [vp, i, i, i, i, i, u64, u64, f, vp]),
             "rk_model_kernel_count": (i, [vp, vp]), "rk_model_profile": (i, [vp, i, i, vp]),
             "rk_stage_fill_cache": (i, [vp, i, u64]),
+            "rk_plan_stages": (i, [vp, vp, i, vp, vp, vp, i, i, vp, vp, vp, vp]),
+            "rk_pipeline_new": (i, [vp, vp, vp, vp, vp]), "rk_pipeline_free": (None, [vp]),
+            "rk_pipeline_step": (i, [vp, i, i, vp, vp]), "rk_bench_pipeline": (i, [vp, i, i, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -497,6 +501,50 @@ class Model:
     def free(self):
         if self.h:
             lib().rk_model_free(self.h)
+            self.h = C.c_void_p()
+
+
+def plan_stages(cost, mem, speed, capacity, stages, free_mem=None):
+    """planStages (plan.go:122-207) through rk_plan_stages: a list of
+    (node, first layer, end layer) spans."""
+    cost = np.ascontiguousarray(cost, dtype=np.int64)
+    mem = np.ascontiguousarray(mem, dtype=np.int64)
+    speed = np.ascontiguousarray(speed, dtype=np.float64)
+    capacity = np.ascontiguousarray(capacity, dtype=np.int64)
+    free = None if free_mem is None else np.ascontiguousarray(free_mem, dtype=np.int64)
+    room = max(1, len(speed))
+    node, first, end = (np.zeros(room, np.int32) for _ in range(3))
+    n = C.c_int(room)
+    _check(lib().rk_plan_stages(_ptr(cost), _ptr(mem), cost.size, _ptr(speed), _ptr(capacity), _ptr(free), speed.size,
+                                stages, C.byref(n), _ptr(node), _ptr(first), _ptr(end)))
+    return [(int(node[i]), int(first[i]), int(end[i])) for i in range(n.value)]
+
+
+class Pipeline:
+    """One rank's part of a layer pipeline over a Group: the first rank
+    passes the embedding table, the last the head (rk_pipeline_*)."""
+
+    def __init__(self, group, embed_table, stage, head, vocab):
+        self.vocab = vocab
+        self.last = group.rank == group.nranks - 1
+        self.h = C.c_void_p()
+        _check(lib().rk_pipeline_new(group.h, embed_table.h if embed_table else None, stage.h,
+                                     head.h if head else None, C.byref(self.h)))
+
+    def step(self, token, pos, want_logits=True):
+        logits = np.empty(self.vocab, dtype=np.float32) if want_logits and self.last else None
+        nxt = C.c_int()
+        _check(lib().rk_pipeline_step(self.h, token, pos, _ptr(logits), C.byref(nxt)))
+        return nxt.value, logits
+
+    def bench(self, pos, iters):
+        ms = C.c_float()
+        _check(lib().rk_bench_pipeline(self.h, pos, iters, C.byref(ms)))
+        return ms.value
+
+    def free(self):
+        if self.h:
+            lib().rk_pipeline_free(self.h)
             self.h = C.c_void_p()
 
 

@@ -197,3 +197,55 @@ class DeviceModel:
 def matrix_bytes(fmt, n):
     """matBytes (model.go:269-279)."""
     return {rk.FMT_BF16: 2 * n, rk.FMT_Q8_0: n + (n // 32) * 4, rk.FMT_Q4_0: n // 2 + (n // 32) * 4}.get(fmt, 4 * n)
+
+
+class PipelineRank:
+    """Rank `group.rank`'s part of a layer pipeline of a synthetic model:
+    layers [first, end) (their weights those of the whole model's layers
+    first..end-1, so the oracle's single model matches), the embedding table
+    on the first rank and the head on the last (rk.Pipeline)."""
+
+    def __init__(self, dev, c, seed, group, first, end, ctx=None):
+        self.c, self.dev = c, dev
+        self.ctx = ctx or c.seq_len
+        self.layers = []
+        for l in range(first, end):
+            mats = [generate_matrix(dev, *mat_shape(c, k), mat_fmt(c, k), seed, tid(l, k)) for k in MATS]
+            self.layers.append(rk.Layer(dev, c, mats=mats, vectors=host_layer_vectors(c)))
+        self.stage = rk.Stage(dev, c, self.layers, self.ctx)
+        ef = embed_fmt(c)
+        first_rank, last_rank = group.rank == 0, group.rank == group.nranks - 1
+        self.embed = generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_EMBED) if first_rank else None
+        self.wcls, self.head = None, None
+        if last_rank:
+            if c.shared_classifier:
+                self.wcls = self.embed if first_rank else generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_EMBED)
+            else:
+                self.wcls = generate_matrix(dev, c.vocab, c.dim, ef, seed, TID_CLS)
+            self.head = rk.Head(dev, c, np.ones(c.dim, np.float32), self.wcls)
+        self.pipeline = rk.Pipeline(group, self.embed, self.stage, self.head, c.vocab)
+
+    def generate(self, prompt, n_new):
+        """The greedy loop (generate.go:522-585) over the pipeline: tokens,
+        and on the last rank every step's logits."""
+        toks, logits = [], []
+        steps = len(prompt) + n_new - 1
+        nxt = 0
+        for i in range(steps):
+            tok = int(prompt[i]) if i < len(prompt) else nxt
+            nxt, lg = self.pipeline.step(tok, i)
+            if lg is not None:
+                logits.append(lg)
+            if i >= len(prompt) - 1:
+                toks.append(nxt)
+        return np.array(toks[:n_new], np.int32), (np.stack(logits) if logits else None)
+
+    def free(self):
+        self.pipeline.free()
+        if self.head:
+            self.head.free()
+        self.stage.free()
+        for l in self.layers:
+            l.free()
+        for m in {id(x): x for x in (self.embed, self.wcls) if x is not None}.values():
+            m.free()
