@@ -319,6 +319,27 @@ int rk_tensor_matmul(rk_device *d, int dtype, int transposed, int m, int k, int 
 /* The same on device buffers, enqueued on the device's stream (no sync). */
 int rk_tensor_matmul_device(rk_device *d, int dtype, int transposed, int m, int k, int n, const void *a_dev,
                             const void *b_dev, void *c_dev);
+/* The element and row operations of rakkan_tensor_v1 (tensor.go:341-486) on
+ * row-major host buffers, as the reference computes each element; dtype
+ * checks return RK_ERR_ARGS as the reference returns tenErrArgs.
+ * add (341-363): c = Canonical(a + b) (f32) or a + b wrapping (i32); b has
+ *   `rows` rows or one row (broadcast). int8 is refused.
+ * scale (365-383): c (f32) = Canonical(float32(a)·k), a f32 or i32.
+ * relu (385-406): a > 0 ? a : 0, a NaN (f32) becoming the canonical NaN.
+ * softmax (408-433, f32, per row): mx = row[0] then every later value
+ *   greater than it; Exp32(v - mx); their sum in order; Canonical(e / sum)
+ *   with IEEE division.
+ * quantize (435-450, f32 -> int8): clamp(RoundToEven(v / k), ±127) with
+ *   IEEE division; k must be > 0; a NaN quotient gives 0 (Go's int8 of NaN
+ *   on amd64).
+ * argmax (452-476, f32 or i32, per row): the first index of the strict
+ *   maximum scanning from index 0 (a NaN never wins; at index 0 it stays). */
+int rk_tensor_add(rk_device *d, int dtype, int rows, int cols, const void *a, const void *b, int b_rows, void *c);
+int rk_tensor_scale(rk_device *d, int dtype, int rows, int cols, const void *a, float k, float *c);
+int rk_tensor_relu(rk_device *d, int dtype, int rows, int cols, const void *a, void *c);
+int rk_tensor_softmax(rk_device *d, int dtype, int rows, int cols, const float *a, float *c);
+int rk_tensor_quantize(rk_device *d, int dtype, int rows, int cols, const float *a, float k, int8_t *c);
+int rk_tensor_argmax(rk_device *d, int dtype, int rows, int cols, const void *a, int32_t *out);
 
 /* ---- Device-side weight import (num.QuantizeQ8 / QuantizeQ4,
  *      quant.go:25-68) and the seeded synthetic generator used by tests

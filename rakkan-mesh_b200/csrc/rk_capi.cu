@@ -2080,6 +2080,95 @@ extern "C" int rk_tensor_matmul(rk_device *d, int dtype, int transposed, int m, 
   return check_dev_err(d);
 }
 
+// rakkan_tensor_v1's element and row operations (tensor.go:341-486): host
+// buffers in and out through device copies, the reference's argument checks
+// (tenErrArgs) as RK_ERR_ARGS.
+static int tensor_elemwise(rk_device *d, size_t in_a, const void *a, size_t in_b, const void *b, size_t out_bytes,
+                           void *c, const char *what,
+                           const std::function<cudaError_t(const void *, const void *, void *, cudaStream_t)> &run) {
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  void *da = nullptr, *db = nullptr, *dc = nullptr;
+  cudaError_t e = cudaMalloc(&da, std::max<size_t>(in_a, 16));
+  if (e == cudaSuccess && b) e = cudaMalloc(&db, std::max<size_t>(in_b, 16));
+  if (e == cudaSuccess) e = cudaMalloc(&dc, std::max<size_t>(out_bytes, 16));
+  if (e == cudaSuccess && in_a) e = cudaMemcpyAsync(da, a, in_a, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess && b && in_b) e = cudaMemcpyAsync(db, b, in_b, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess) e = run(da, db, dc, d->st);
+  if (e == cudaSuccess && out_bytes) e = cudaMemcpyAsync(c, dc, out_bytes, cudaMemcpyDeviceToHost, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  cudaFree(da);
+  cudaFree(db);
+  cudaFree(dc);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return check_dev_err(d);
+}
+
+static bool ten_shape_ok(int rows, int cols) { return rows > 0 && cols > 0 && (long long)rows * cols <= (1LL << 31); }
+
+extern "C" int rk_tensor_add(rk_device *d, int dtype, int rows, int cols, const void *a, const void *b, int b_rows,
+                             void *c) {
+  if (!d || !a || !b || !c || !ten_shape_ok(rows, cols)) return fail(RK_ERR_ARGS, "bad argument");
+  if (dtype == RK_TENSOR_I8 || (dtype != RK_TENSOR_F32 && dtype != RK_TENSOR_I32) || (b_rows != rows && b_rows != 1))
+    return fail(RK_ERR_ARGS, "add: dtype or shape mismatch");
+  const size_t n = (size_t)rows * cols;
+  return tensor_elemwise(d, 4 * n, a, 4 * (size_t)b_rows * cols, b, 4 * n, c, "tensor add",
+                         [&](const void *da, const void *db, void *dc, cudaStream_t st) {
+                           return launch_tensor_add(dtype == RK_TENSOR_F32 ? 0 : 1, rows, cols, da, db, b_rows, dc, st);
+                         });
+}
+
+extern "C" int rk_tensor_scale(rk_device *d, int dtype, int rows, int cols, const void *a, float k, float *c) {
+  if (!d || !a || !c || !ten_shape_ok(rows, cols)) return fail(RK_ERR_ARGS, "bad argument");
+  if (dtype != RK_TENSOR_F32 && dtype != RK_TENSOR_I32) return fail(RK_ERR_ARGS, "scale: int8 input");
+  const size_t n = (size_t)rows * cols;
+  return tensor_elemwise(d, 4 * n, a, 0, nullptr, 4 * n, c, "tensor scale",
+                         [&](const void *da, const void *, void *dc, cudaStream_t st) {
+                           return launch_tensor_scale(dtype == RK_TENSOR_F32 ? 0 : 1, (long long)n, da, k, (float *)dc, st);
+                         });
+}
+
+extern "C" int rk_tensor_relu(rk_device *d, int dtype, int rows, int cols, const void *a, void *c) {
+  if (!d || !a || !c || !ten_shape_ok(rows, cols)) return fail(RK_ERR_ARGS, "bad argument");
+  if (dtype != RK_TENSOR_F32 && dtype != RK_TENSOR_I32) return fail(RK_ERR_ARGS, "relu: int8 input");
+  const size_t n = (size_t)rows * cols;
+  return tensor_elemwise(d, 4 * n, a, 0, nullptr, 4 * n, c, "tensor relu",
+                         [&](const void *da, const void *, void *dc, cudaStream_t st) {
+                           return launch_tensor_relu(dtype == RK_TENSOR_F32 ? 0 : 1, (long long)n, da, dc, st);
+                         });
+}
+
+extern "C" int rk_tensor_softmax(rk_device *d, int dtype, int rows, int cols, const float *a, float *c) {
+  if (!d || !a || !c || !ten_shape_ok(rows, cols)) return fail(RK_ERR_ARGS, "bad argument");
+  if (dtype != RK_TENSOR_F32) return fail(RK_ERR_ARGS, "softmax: not f32");
+  const size_t n = (size_t)rows * cols;
+  return tensor_elemwise(d, 4 * n, a, 0, nullptr, 4 * n, c, "tensor softmax",
+                         [&](const void *da, const void *, void *dc, cudaStream_t st) {
+                           return launch_tensor_softmax(rows, cols, (const float *)da, (float *)dc, st);
+                         });
+}
+
+extern "C" int rk_tensor_quantize(rk_device *d, int dtype, int rows, int cols, const float *a, float k, int8_t *c) {
+  if (!d || !a || !c || !ten_shape_ok(rows, cols)) return fail(RK_ERR_ARGS, "bad argument");
+  if (dtype != RK_TENSOR_F32 || !(k > 0.0f)) return fail(RK_ERR_ARGS, "quantize: not f32, or scale not positive");
+  const size_t n = (size_t)rows * cols;
+  return tensor_elemwise(d, 4 * n, a, 0, nullptr, n, c, "tensor quantize",
+                         [&](const void *da, const void *, void *dc, cudaStream_t st) {
+                           return launch_tensor_quantize((long long)n, (const float *)da, k, (int8_t *)dc, st);
+                         });
+}
+
+extern "C" int rk_tensor_argmax(rk_device *d, int dtype, int rows, int cols, const void *a, int32_t *out) {
+  if (!d || !a || !out || !ten_shape_ok(rows, cols)) return fail(RK_ERR_ARGS, "bad argument");
+  if (dtype != RK_TENSOR_F32 && dtype != RK_TENSOR_I32) return fail(RK_ERR_ARGS, "argmax: int8 input");
+  const size_t n = (size_t)rows * cols;
+  return tensor_elemwise(d, 4 * n, a, 0, nullptr, 4 * (size_t)rows, out, "tensor argmax",
+                         [&](const void *da, const void *, void *dc, cudaStream_t st) {
+                           return launch_tensor_argmax(dtype == RK_TENSOR_F32 ? 0 : 1, rows, cols, da, (int *)dc, st);
+                         });
+}
+
 // ---------------------------------------------------------------------------
 // Device-side import and the seeded generator
 // ---------------------------------------------------------------------------

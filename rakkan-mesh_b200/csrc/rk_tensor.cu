@@ -417,4 +417,137 @@ cudaError_t launch_tensor_matmul(int dtype, int transposed, int m, int k, int n,
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// rakkan_tensor_v1's element and row operations (sandbox/tensor.go:341-486),
+// each element as the reference computes it.
+// ---------------------------------------------------------------------------
+__global__ void k_ten_add_f32(const float *a, const float *b, float *c, long long n, int cols, int bcast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    c[i] = canonical(__fadd_rn(a[i], b[bcast ? i % cols : i]));
+}
+__global__ void k_ten_add_i32(const int *a, const int *b, int *c, long long n, int cols, int bcast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    c[i] = (int)((unsigned)a[i] + (unsigned)b[bcast ? i % cols : i]);  // Go's int32 addition wraps
+}
+__global__ void k_ten_scale(const void *a, int is_i32, float k, float *c, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = is_i32 ? __int2float_rn(reinterpret_cast<const int *>(a)[i]) : reinterpret_cast<const float *>(a)[i];
+    c[i] = canonical(__fmul_rn(v, k));
+  }
+}
+__global__ void k_ten_relu(const void *a, int is_i32, void *c, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    if (is_i32) {
+      const int v = reinterpret_cast<const int *>(a)[i];
+      reinterpret_cast<int *>(c)[i] = v > 0 ? v : 0;
+    } else {
+      const float v = reinterpret_cast<const float *>(a)[i];
+      reinterpret_cast<float *>(c)[i] = v > 0.0f ? v : (v != v ? u2f(kCanonNaN) : 0.0f);
+    }
+  }
+}
+// q = clamp(float32(RoundToEven(float64(v / k))), ±127) as int8; Go's int8 of
+// a NaN is 0 on amd64 (the conversion's integer-indefinite value truncated).
+__global__ void k_ten_quantize(const float *a, float k, int8_t *c, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float q = rintf(__fdiv_rn(a[i], k));
+    c[i] = q != q ? (int8_t)0 : (int8_t)(int)fminf(127.0f, fmaxf(-127.0f, q));
+  }
+}
+// Softmax per row, a warp per row: mx by the reference's scan (row[0], then
+// each later value greater than it), exps in parallel, their sum in order
+// by lane 0, then IEEE division.
+__global__ void k_ten_softmax(const float *a, float *c, int rows, int cols) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float *row = a + (long long)r * cols;
+  float *out = c + (long long)r * cols;
+  float mx = row[0];
+  if (lane == 0)
+    for (int i = 1; i < cols; i++)
+      if (row[i] > mx) mx = row[i];
+  mx = __shfl_sync(0xffffffffu, mx, 0);
+  for (int i = lane; i < cols; i += 32) out[i] = exp32(__fsub_rn(row[i], mx));
+  __syncwarp();
+  float sum = 0.0f;
+  if (lane == 0)
+    for (int i = 0; i < cols; i++) sum = __fadd_rn(sum, out[i]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  __syncwarp();
+  for (int i = lane; i < cols; i += 32) out[i] = canonical(__fdiv_rn(out[i], sum));
+}
+// argmax per row, a warp per row: the first index j with a[j] greater than
+// every earlier candidate (strict >, so NaN never wins and a NaN at index 0
+// keeps it). Each lane scans its strided indices the same way; lanes then
+// combine by value, ties (including -0 against +0) to the lower index.
+template <typename T>
+__global__ void k_ten_argmax(const T *a, int rows, int cols, int *out) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const T *row = a + (long long)r * cols;
+  int best = -1;
+  T bv = T(0);
+  for (int j = lane; j < cols; j += 32) {
+    const T v = row[j];
+    if (best < 0 ? v == v : v > bv) {
+      best = j;
+      bv = v;
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const int ob = __shfl_xor_sync(0xffffffffu, best, off);
+    const T ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    if (ob >= 0 && (best < 0 || ov > bv || (!(bv > ov) && ob < best))) {
+      best = ob;
+      bv = ov;
+    }
+  }
+  if (lane == 0) {
+    const T v0 = row[0];
+    out[r] = (v0 != v0 || best < 0) ? 0 : best;
+  }
+}
+
+static int ten_grid(long long n) { return (int)std::min<long long>((n + 255) / 256, 148LL * 16); }
+
+cudaError_t launch_tensor_add(int dtype, int rows, int cols, const void *a, const void *b, int b_rows, void *c,
+                              cudaStream_t st) {
+  const long long n = (long long)rows * cols;
+  if (n <= 0) return cudaSuccess;
+  const int bc = b_rows == 1 && rows != 1;
+  if (dtype == 0)
+    k_ten_add_f32<<<ten_grid(n), 256, 0, st>>>((const float *)a, (const float *)b, (float *)c, n, cols, bc);
+  else
+    k_ten_add_i32<<<ten_grid(n), 256, 0, st>>>((const int *)a, (const int *)b, (int *)c, n, cols, bc);
+  return cudaGetLastError();
+}
+cudaError_t launch_tensor_scale(int dtype, long long n, const void *a, float k, float *c, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_ten_scale<<<ten_grid(n), 256, 0, st>>>(a, dtype != 0, k, c, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_tensor_relu(int dtype, long long n, const void *a, void *c, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_ten_relu<<<ten_grid(n), 256, 0, st>>>(a, dtype != 0, c, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_tensor_quantize(long long n, const float *a, float k, int8_t *c, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_ten_quantize<<<ten_grid(n), 256, 0, st>>>(a, k, c, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_tensor_softmax(int rows, int cols, const float *a, float *c, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  k_ten_softmax<<<(rows + 7) / 8, 256, 0, st>>>(a, c, rows, cols);
+  return cudaGetLastError();
+}
+cudaError_t launch_tensor_argmax(int dtype, int rows, int cols, const void *a, int *out, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  if (dtype == 0) k_ten_argmax<float><<<(rows + 7) / 8, 256, 0, st>>>((const float *)a, rows, cols, out);
+  else k_ten_argmax<int><<<(rows + 7) / 8, 256, 0, st>>>((const int *)a, rows, cols, out);
+  return cudaGetLastError();
+}
+
 }  // namespace rk

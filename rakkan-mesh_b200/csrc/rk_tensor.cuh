@@ -17,6 +17,16 @@ enum TensorDType : int { DT_F32 = 0, DT_I8 = 1, DT_I32 = 2 };
 cudaError_t launch_tensor_matmul(int dtype, int transposed, int m, int k, int n, const void *a, const void *b, void *c,
                                  int num_sms, int *err, cudaStream_t st);
 
+// rakkan_tensor_v1's element and row operations (sandbox/tensor.go:341-486);
+// dtype 0 = f32, otherwise i32, device buffers.
+cudaError_t launch_tensor_add(int dtype, int rows, int cols, const void *a, const void *b, int b_rows, void *c,
+                              cudaStream_t st);
+cudaError_t launch_tensor_scale(int dtype, long long n, const void *a, float k, float *c, cudaStream_t st);
+cudaError_t launch_tensor_relu(int dtype, long long n, const void *a, void *c, cudaStream_t st);
+cudaError_t launch_tensor_quantize(long long n, const float *a, float k, int8_t *c, cudaStream_t st);
+cudaError_t launch_tensor_softmax(int rows, int cols, const float *a, float *c, cudaStream_t st);
+cudaError_t launch_tensor_argmax(int dtype, int rows, int cols, const void *a, int *out, cudaStream_t st);
+
 // Whether an int8 product of this shape and these operand addresses can use
 // the tensor-core kernel (16-byte aligned operands and rows, k < 2^17).
 bool tensor_i8_tc_ok(int transposed, int m, int k, int n, const void *a, const void *b);

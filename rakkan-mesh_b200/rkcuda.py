@@ -37,6 +37,7 @@ EXPORTS = [
     "rk_group_size", "rk_group_all_gather", "rk_layer_upload_shard", "rk_layer_from_device_shard",
     "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
     "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
+    "rk_tensor_add", "rk_tensor_scale", "rk_tensor_relu", "rk_tensor_softmax", "rk_tensor_quantize", "rk_tensor_argmax",
 ]
 
 
@@ -132,6 +133,9 @@ def lib():
             "rk_plan_stages": (i, [vp, vp, i, vp, vp, vp, i, i, vp, vp, vp, vp]),
             "rk_pipeline_new": (i, [vp, vp, vp, vp, vp]), "rk_pipeline_free": (None, [vp]),
             "rk_pipeline_step": (i, [vp, i, i, vp, vp]), "rk_bench_pipeline": (i, [vp, i, i, vp]),
+            "rk_tensor_add": (i, [vp, i, i, i, vp, vp, i, vp]), "rk_tensor_scale": (i, [vp, i, i, i, vp, f, vp]),
+            "rk_tensor_relu": (i, [vp, i, i, i, vp, vp]), "rk_tensor_softmax": (i, [vp, i, i, i, vp, vp]),
+            "rk_tensor_quantize": (i, [vp, i, i, i, vp, f, vp]), "rk_tensor_argmax": (i, [vp, i, i, i, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -546,6 +550,53 @@ class Pipeline:
         if self.h:
             lib().rk_pipeline_free(self.h)
             self.h = C.c_void_p()
+
+
+def _tdtype(a):
+    return {np.dtype(np.float32): TENSOR_F32, np.dtype(np.int8): TENSOR_I8, np.dtype(np.int32): TENSOR_I32}[a.dtype]
+
+
+def tensor_add(dev, a, b):
+    """rakkan_tensor_v1 add: a [rows, cols] + b [rows or 1, cols]."""
+    a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    c = np.empty_like(a)
+    _check(lib().rk_tensor_add(dev.h, _tdtype(a), a.shape[0], a.shape[1], _ptr(a), _ptr(b), b.shape[0], _ptr(c)))
+    return c
+
+
+def tensor_scale(dev, a, k):
+    a = np.ascontiguousarray(a)
+    c = np.empty(a.shape, np.float32)
+    _check(lib().rk_tensor_scale(dev.h, _tdtype(a), a.shape[0], a.shape[1], _ptr(a), k, _ptr(c)))
+    return c
+
+
+def tensor_relu(dev, a):
+    a = np.ascontiguousarray(a)
+    c = np.empty_like(a)
+    _check(lib().rk_tensor_relu(dev.h, _tdtype(a), a.shape[0], a.shape[1], _ptr(a), _ptr(c)))
+    return c
+
+
+def tensor_softmax(dev, a):
+    a = np.ascontiguousarray(a)
+    c = np.empty(a.shape, np.float32)
+    _check(lib().rk_tensor_softmax(dev.h, _tdtype(a), a.shape[0], a.shape[1], _ptr(a), _ptr(c)))
+    return c
+
+
+def tensor_quantize(dev, a, k):
+    a = np.ascontiguousarray(a)
+    c = np.empty(a.shape, np.int8)
+    _check(lib().rk_tensor_quantize(dev.h, _tdtype(a), a.shape[0], a.shape[1], _ptr(a), k, _ptr(c)))
+    return c
+
+
+def tensor_argmax(dev, a):
+    a = np.ascontiguousarray(a)
+    out = np.empty(a.shape[0], np.int32)
+    _check(lib().rk_tensor_argmax(dev.h, _tdtype(a), a.shape[0], a.shape[1], _ptr(a), _ptr(out)))
+    return out
 
 
 def tensor_matmul(dev, a, b, transposed):
