@@ -277,6 +277,22 @@ int rk_stage_fused_gathers(const rk_stage *s);
 int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *g,
                       rk_head **out);
 
+/* ---- The reference's model part formats (internal/llm/shard.go:165-300):
+ *      a part's tensors in order, little-endian, each matrix in its own type
+ *      (float32; bfloat16; or, quantized, the float32 scales then the
+ *      values). A part of the wrong size is refused (RK_ERR_ARGS). ---- */
+/* LoadLayer (shard.go:258-269) then Layer.toDevice: RmsAtt, Wq, Wk, Wv, Wo,
+ * RmsFfn, W1, W2, W3, then Bq, Bk, Bv (qkv_bias) and QNorm, KNorm (qk_norm),
+ * each matrix in Config.matType (model.go:105-113). */
+int rk_layer_load_part(rk_device *d, const rk_config *c, const void *part, int64_t bytes, rk_layer **out);
+/* LoadEmbed (shard.go:282-287): the vocab × dim table in Config.embedType. */
+int rk_embed_load_part(rk_device *d, const rk_config *c, const void *part, int64_t bytes, rk_matrix **out);
+/* LoadHead (shard.go:292-300): RmsFinal, then the classifier unless it is
+ * shared (then embed is the classifier). *wcls_out receives the uploaded
+ * classifier (the caller frees it after the head), or NULL when shared. */
+int rk_head_load_part(rk_device *d, const rk_config *c, const void *part, int64_t bytes, rk_matrix *embed,
+                      rk_matrix **wcls_out, rk_head **out);
+
 /* ---- Layer pipeline (config 5): planStages (internal/llm/plan.go:122-207)
  *      and the stage-to-stage hand-off of llm's pipelined generation
  *      (generate.go:522-585 over the stages a plan assigns). ---- */

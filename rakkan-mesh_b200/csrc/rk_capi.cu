@@ -2470,6 +2470,119 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
 }
 
 // ---------------------------------------------------------------------------
+// The reference's model part formats (internal/llm/shard.go:165-300): a
+// part's tensors in order, little-endian; a matrix in its own type (float32,
+// bfloat16, or the scales then the values when quantized). Decoded into host
+// views, then uploaded as Layer.toDevice / Matrix.toDevice do.
+// ---------------------------------------------------------------------------
+struct PartDecoder {  // shard.go:187-240
+  const uint8_t *p;
+  int64_t left;
+  bool bad = false;
+  std::vector<std::vector<float>> floats;  // aligned copies of the part's float arrays
+  const uint8_t *take(int64_t n) {
+    if (bad || n < 0 || n > left) {
+      bad = true;
+      return nullptr;
+    }
+    const uint8_t *r = p;
+    p += n;
+    left -= n;
+    return r;
+  }
+  const float *vec(int64_t n) {
+    const uint8_t *b = take(4 * n);
+    if (!b) return nullptr;
+    floats.emplace_back((size_t)n);
+    memcpy(floats.back().data(), b, 4 * (size_t)n);
+    return floats.back().data();
+  }
+  rk_host_matrix mat(int64_t n, int fmt) {
+    rk_host_matrix m{};
+    m.fmt = fmt;
+    switch (fmt) {
+      case RK_FMT_Q8_0: m.scales = vec(n / 32); m.w = take(n); break;
+      case RK_FMT_Q4_0: m.scales = vec(n / 32); m.w = take(n / 2); break;
+      case RK_FMT_BF16: m.w = take(2 * n); break;
+      default: m.w = take(4 * n); break;
+    }
+    return m;
+  }
+  bool done() const { return !bad && left == 0; }
+};
+
+// Config.embedType (model.go:96-101): the embedding table and a separate
+// classifier stay q8_0 in quantized models.
+static int embed_fmt(const rk_config *c) {
+  return c->dtype == RK_DTYPE_F32 ? RK_FMT_F32 : c->dtype == RK_DTYPE_BF16 ? RK_FMT_BF16 : RK_FMT_Q8_0;
+}
+
+extern "C" int rk_layer_load_part(rk_device *d, const rk_config *c, const void *part, int64_t bytes, rk_layer **out) {
+  if (!d || !c || !part || bytes < 0 || !out) return fail(RK_ERR_ARGS, "null argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  const int64_t D = c->dim, hs = head_size(c), q = (int64_t)c->heads * hs, kv = (int64_t)c->kv_heads * hs, H = c->hidden;
+  const int m = mat_fmt(c, false), sens = mat_fmt(c, true);
+  PartDecoder dec{(const uint8_t *)part, bytes};
+  rk_host_layer h{};  // Layer.tensors order, model.go:328-343
+  h.rms_att = dec.vec(D);
+  h.wq = dec.mat(q * D, m);
+  h.wk = dec.mat(kv * D, m);
+  h.wv = dec.mat(kv * D, sens);
+  h.wo = dec.mat(D * q, m);
+  h.rms_ffn = dec.vec(D);
+  h.w1 = dec.mat(H * D, m);
+  h.w2 = dec.mat(D * H, sens);
+  h.w3 = dec.mat(H * D, m);
+  if (c->qkv_bias) {
+    h.bq = dec.vec(q);
+    h.bk = dec.vec(kv);
+    h.bv = dec.vec(kv);
+  }
+  if (c->qk_norm) {
+    h.q_norm = dec.vec(hs);
+    h.k_norm = dec.vec(hs);
+  }
+  if (!dec.done()) return fail(RK_ERR_ARGS, "model part has the wrong size");
+  return rk_layer_upload(d, c, &h, out);
+}
+
+extern "C" int rk_embed_load_part(rk_device *d, const rk_config *c, const void *part, int64_t bytes, rk_matrix **out) {
+  if (!d || !c || !part || bytes < 0 || !out) return fail(RK_ERR_ARGS, "null argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  PartDecoder dec{(const uint8_t *)part, bytes};
+  const rk_host_matrix e = dec.mat((int64_t)c->vocab * c->dim, embed_fmt(c));  // LoadEmbed, shard.go:282-287
+  if (!dec.done()) return fail(RK_ERR_ARGS, "model part has the wrong size");
+  return rk_matrix_upload(d, c->vocab, c->dim, e.fmt, e.w, e.scales, out);
+}
+
+extern "C" int rk_head_load_part(rk_device *d, const rk_config *c, const void *part, int64_t bytes, rk_matrix *embed,
+                                 rk_matrix **wcls_out, rk_head **out) {
+  if (!d || !c || !part || bytes < 0 || !out || !wcls_out) return fail(RK_ERR_ARGS, "null argument");
+  int rc = rk_config_validate(c);
+  if (rc) return rc;
+  *wcls_out = nullptr;
+  PartDecoder dec{(const uint8_t *)part, bytes};  // LoadHead, shard.go:292-300
+  const float *rms = dec.vec(c->dim);
+  rk_host_matrix w{};
+  if (!c->shared_classifier) w = dec.mat((int64_t)c->vocab * c->dim, embed_fmt(c));
+  if (!dec.done()) return fail(RK_ERR_ARGS, "model part has the wrong size");
+  rk_matrix *wcls = embed;
+  if (!c->shared_classifier) {
+    if ((rc = rk_matrix_upload(d, c->vocab, c->dim, w.fmt, w.w, w.scales, &wcls))) return rc;
+  } else if (!embed) {
+    return fail(RK_ERR_ARGS, "a shared classifier needs the embedding table");
+  }
+  if ((rc = rk_head_new(d, c, rms, wcls, out))) {
+    if (wcls != embed) rk_matrix_free(wcls);
+    return rc;
+  }
+  if (wcls != embed) *wcls_out = wcls;
+  return RK_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Layer pipeline: the stage plan (planStages, internal/llm/plan.go:122-207)
 // and one rank's part of a pipelined step.
 // ---------------------------------------------------------------------------

@@ -38,6 +38,7 @@ EXPORTS = [
     "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
     "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
     "rk_tensor_add", "rk_tensor_scale", "rk_tensor_relu", "rk_tensor_softmax", "rk_tensor_quantize", "rk_tensor_argmax",
+    "rk_layer_load_part", "rk_embed_load_part", "rk_head_load_part",
 ]
 
 
@@ -136,6 +137,8 @@ def lib():
             "rk_tensor_add": (i, [vp, i, i, i, vp, vp, i, vp]), "rk_tensor_scale": (i, [vp, i, i, i, vp, f, vp]),
             "rk_tensor_relu": (i, [vp, i, i, i, vp, vp]), "rk_tensor_softmax": (i, [vp, i, i, i, vp, vp]),
             "rk_tensor_quantize": (i, [vp, i, i, i, vp, f, vp]), "rk_tensor_argmax": (i, [vp, i, i, i, vp, vp]),
+            "rk_layer_load_part": (i, [vp, vp, vp, i64, vp]), "rk_embed_load_part": (i, [vp, vp, vp, i64, vp]),
+            "rk_head_load_part": (i, [vp, vp, vp, i64, vp, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -506,6 +509,38 @@ class Model:
         if self.h:
             lib().rk_model_free(self.h)
             self.h = C.c_void_p()
+
+
+def _part_buf(part):
+    part = bytes(part)
+    return C.create_string_buffer(part, len(part)), len(part)
+
+
+def layer_load_part(dev, cfg, part):
+    """LoadLayer (shard.go:258-269) + Layer.toDevice: a Layer from a part's bytes."""
+    buf, n = _part_buf(part)
+    layer = Layer.__new__(Layer)
+    layer.h = C.c_void_p()
+    _check(lib().rk_layer_load_part(dev.h, C.byref(cfg), buf, n, C.byref(layer.h)))
+    return layer
+
+
+def embed_load_part(dev, cfg, part, fmt):
+    """LoadEmbed (shard.go:282-287): the embedding table as a Matrix."""
+    buf, n = _part_buf(part)
+    h = C.c_void_p()
+    _check(lib().rk_embed_load_part(dev.h, C.byref(cfg), buf, n, C.byref(h)))
+    return Matrix(dev, cfg.vocab, cfg.dim, fmt, handle=h)
+
+
+def head_load_part(dev, cfg, part, embed, fmt):
+    """LoadHead (shard.go:292-300): (Head, its own classifier Matrix or None)."""
+    buf, n = _part_buf(part)
+    h, w = C.c_void_p(), C.c_void_p()
+    _check(lib().rk_head_load_part(dev.h, C.byref(cfg), buf, n, embed.h if embed else None, C.byref(w), C.byref(h)))
+    head = Head.__new__(Head)
+    head.vocab, head.h = cfg.vocab, h
+    return head, (Matrix(dev, cfg.vocab, cfg.dim, fmt, handle=w) if w.value else None)
 
 
 def plan_stages(cost, mem, speed, capacity, stages, free_mem=None):
