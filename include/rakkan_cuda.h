@@ -277,6 +277,15 @@ int rk_stage_fused_gathers(const rk_stage *s);
 int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *g,
                       rk_head **out);
 
+/* MatMulBF16 (num/matvec.go:124-147): out[i·m + j] = DotBF16(row j of w,
+ * row i of x) for the n rows of x (w->cols floats each) and the m = w->rows
+ * rows of a bfloat16 matrix; host buffers. */
+int rk_matmul_bf16(rk_matrix *w, int n, const float *x, float *out);
+/* MeasureSpeed (llm/speed.go:16-47) on device d: GB of weights per second
+ * of 4096×4096 bfloat16 products (the reference's LCG matrix), the median
+ * of seven whole MulVec calls after one warm-up; the planner's speed. */
+int rk_measure_speed(rk_device *d, double *gbps);
+
 /* ---- The reference's model part formats (internal/llm/shard.go:165-300):
  *      a part's tensors in order, little-endian, each matrix in its own type
  *      (float32; bfloat16; or, quantized, the float32 scales then the

@@ -14,6 +14,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <condition_variable>
 #include <cstdarg>
 #include <cstdlib>
@@ -2467,6 +2468,77 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
       CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, s->vals[l], d->st));
   }
   return sync_dev(d);
+}
+
+// MatMulBF16 (num/matvec.go:124-147): out[i·m + j] = DotBF16(row j of w,
+// row i of x), what MatVecBF16 gives each row of x, so each row of x is one
+// bf16 matvec launch (the kernel's lane order and tree are DotBF16's).
+extern "C" int rk_matmul_bf16(rk_matrix *w, int n, const float *x, float *out) {
+  if (!w || n < 0 || (n > 0 && (!x || !out))) return fail(RK_ERR_ARGS, "bad argument");
+  if (w->fmt != RK_FMT_BF16) return fail(RK_ERR_ARGS, "MatMulBF16 needs a bfloat16 matrix");
+  if (n == 0) return RK_OK;
+  rk_device *d = w->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  const size_t k = (size_t)w->cols, m = (size_t)w->rows;
+  float *dx = nullptr, *dout = nullptr;
+  cudaError_t e = cudaMalloc(&dx, 4 * k * n);
+  if (e == cudaSuccess) e = cudaMalloc(&dout, 4 * m * n);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, 4 * k * n, cudaMemcpyHostToDevice, d->st);
+  for (int i = 0; i < n && e == cudaSuccess; i++) {
+    float *o = dout + m * i;
+    rc = enqueue_matvecs(d, 1, &w, &o, dx + k * i, nullptr, nullptr, nullptr, EPI_STORE);
+    if (rc) break;
+  }
+  if (e == cudaSuccess && !rc) e = cudaMemcpyAsync(out, dout, 4 * m * n, cudaMemcpyDeviceToHost, d->st);
+  if (e == cudaSuccess && !rc) e = cudaStreamSynchronize(d->st);
+  cudaFree(dx);
+  cudaFree(dout);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "bf16 matmul");
+  return check_dev_err(d);
+}
+
+// num.ToBF16 (matvec.go:23-29): round to nearest even, a NaN kept NaN.
+static uint16_t host_to_bf16(float f) {
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  if (f != f) return (uint16_t)((b >> 16) | 0x40);
+  return (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+}
+
+// MeasureSpeed (llm/speed.go:16-47) on a device: a 4096×4096 bfloat16
+// matrix of the reference's LCG values, x[i] = (i mod 17)/17; one warm-up
+// product, then the median of seven timed ones (each a whole MulVec call,
+// host to host, as the reference times it); GB of weights per second.
+extern "C" int rk_measure_speed(rk_device *d, double *gbps) {
+  if (!d || !gbps) return fail(RK_ERR_ARGS, "null argument");
+  constexpr int rows = 4096, cols = 4096;
+  std::vector<uint16_t> w((size_t)rows * cols);
+  uint32_t seed = 1;
+  for (auto &v : w) {
+    seed = seed * 1664525u + 1013904223u;
+    const float f = (float)((int32_t)(seed >> 8) - (1 << 23)) / (float)(1 << 30);
+    v = host_to_bf16(f);
+  }
+  std::vector<float> x(cols), out(rows);
+  for (int i = 0; i < cols; i++) x[i] = (float)(i % 17) / 17.0f;
+  rk_matrix *m = nullptr;
+  int rc = rk_matrix_upload(d, rows, cols, RK_FMT_BF16, w.data(), nullptr, &m);
+  if (rc) return rc;
+  std::vector<double> times;
+  for (int it = 0; it < 8 && !rc; it++) {
+    const auto t0 = std::chrono::steady_clock::now();
+    rc = rk_matrix_mulvec(m, out.data(), x.data());
+    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (it > 0) times.push_back(dt);
+  }
+  rk_matrix_free(m);
+  if (rc) return rc;
+  std::sort(times.begin(), times.end());
+  *gbps = 2.0 * rows * cols / times[times.size() / 2] / 1e9;
+  return RK_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -38,7 +38,7 @@ EXPORTS = [
     "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
     "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
     "rk_tensor_add", "rk_tensor_scale", "rk_tensor_relu", "rk_tensor_softmax", "rk_tensor_quantize", "rk_tensor_argmax",
-    "rk_layer_load_part", "rk_embed_load_part", "rk_head_load_part",
+    "rk_layer_load_part", "rk_embed_load_part", "rk_head_load_part", "rk_matmul_bf16", "rk_measure_speed",
 ]
 
 
@@ -139,6 +139,7 @@ def lib():
             "rk_tensor_quantize": (i, [vp, i, i, i, vp, f, vp]), "rk_tensor_argmax": (i, [vp, i, i, i, vp, vp]),
             "rk_layer_load_part": (i, [vp, vp, vp, i64, vp]), "rk_embed_load_part": (i, [vp, vp, vp, i64, vp]),
             "rk_head_load_part": (i, [vp, vp, vp, i64, vp, vp, vp]),
+            "rk_matmul_bf16": (i, [vp, i, vp, vp]), "rk_measure_speed": (i, [vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -509,6 +510,21 @@ class Model:
         if self.h:
             lib().rk_model_free(self.h)
             self.h = C.c_void_p()
+
+
+def matmul_bf16(w, x):
+    """MatMulBF16 (matvec.go:124-147) with a bfloat16 Matrix w: [n, w.rows]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty((x.shape[0], w.rows), np.float32)
+    _check(lib().rk_matmul_bf16(w.h, x.shape[0], _ptr(x), _ptr(out)))
+    return out
+
+
+def measure_speed(dev):
+    """MeasureSpeed (speed.go:16-47): GB/s of bfloat16 weights."""
+    v = C.c_double()
+    _check(lib().rk_measure_speed(dev.h, C.byref(v)))
+    return v.value
 
 
 def _part_buf(part):
