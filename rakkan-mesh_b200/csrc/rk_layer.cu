@@ -198,7 +198,13 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  griddep_wait();
+  // With POST (the stage's graphs) the key rows below the new position were
+  // written by earlier graph launches and the new row comes from this kernel,
+  // so the key copies start before the predecessor (the QKV product) ends;
+  // the position count is the host's (or the previous launch's advance).
+  // Without POST (the Batch API appends keys with a kernel of the same
+  // submission) everything waits.
+  if (!POST) griddep_wait();
   const int P = attn_positions(a);
   const int t0 = blockIdx.x * kTileT;
   if (t0 >= P) return;
@@ -214,8 +220,10 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
     if (lane < nt)
       umma::bulk_g2s(umma::smem_u32(sk + lane * KP), a.keys + (long long)(t0 + lane) * a.kv_dim + kvh * HS, HS * 4u,
                      bar);
-    if (lane == 0) umma::bulk_g2s(umma::smem_u32(sq), a.q + (kvh * kvMul + g0) * HS, (uint32_t)ng * HS * 4u, bar);
   }
+  if (POST) griddep_wait();
+  if (warp == 0 && lane == 0)
+    umma::bulk_g2s(umma::smem_u32(sq), a.q + (kvh * kvMul + g0) * HS, (uint32_t)ng * HS * 4u, bar);
   if (POST) {
     const int pos = P - 1;
     const bool has_new = pos < t0 + nt;
