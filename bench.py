@@ -64,8 +64,9 @@ def parse():
                    help="--kernel tensor: one MxKxN shape instead of config 2's sweep")
     p.add_argument("--tensor-dtype", default="both", choices=["both", "i8", "f32"])
     p.add_argument("--tensor-op", default="both", choices=["both", "matmul", "matmul_t"])
-    p.add_argument("--kernel", default=None, choices=["matvec", "tensor"],
-                   help="time one kernel alone instead of the decode step (profiling aid)")
+    p.add_argument("--kernel", default=None, choices=["matvec", "tensor", "prefill"],
+                   help="time one kernel alone instead of the decode step, or a prefill (profiling aids)")
+    p.add_argument("--prefill", type=int, default=512, help="--kernel prefill: prompt tokens")
     p.add_argument("--shape", default="28672x4096", help="rows x cols for --kernel matvec")
     p.add_argument("--prologue", default="fused", choices=["fused", "given"],
                    help="--kernel matvec: quantize the input inside the kernel (as the decode step does) "
@@ -121,6 +122,35 @@ def run_tensor(args):
                                   "m": m, "k": k, "n": n, "ms": ms, "tops": 2 * m * n * k / (ms * 1e-3) / 1e12,
                                   "gbs": nbytes / (ms * 1e-3) / 1e9, "hbm_peak_gbs": peaks.get("hbm_gbs")}),
                       flush=True)
+    dev.close()
+
+
+def run_prefill(args):
+    """Stage.ForwardMany over a seeded prompt of --prefill activations from
+    position 0, through the public stage API (activations in from host
+    memory and back), timed on the host around the synchronous call. An
+    all-Q8_0 stage runs each projection once per 64 tokens on the tensor
+    cores; the attention goes token by token."""
+    import numpy as np
+    import rkcuda as rk
+    import synth
+    dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
+    n = args.prefill
+    c = synth.config(args.model, args.dtype, seq_len=n + 64)
+    dm = synth.DeviceModel(dev, c, SEED, ctx=n + 64)
+    xs = np.random.default_rng(SEED).standard_normal((n, c.dim)).astype(np.float32)
+    for _ in range(max(1, args.warmup)):
+        dm.stage.forward(xs, 0)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        dm.stage.forward(xs, 0)
+        times.append(time.perf_counter() - t0)
+    ms = 1000.0 * statistics.median(times)
+    print(json.dumps({"kernel": "prefill", "model": args.model, "dtype": args.dtype, "tokens": n,
+                      "batched": dm.stage.batched(), "ms": ms, "tok_s": n * 1000.0 / ms,
+                      "steps": args.steps}), flush=True)
+    dm.free()
     dev.close()
 
 
@@ -256,6 +286,8 @@ def main():
         return run_reference(args, rank)
     if args.kernel == "tensor":
         return run_tensor(args)
+    if args.kernel == "prefill":
+        return run_prefill(args)
     if args.kernel:
         return run_kernel(args)
 

@@ -110,6 +110,12 @@ int64_t rk_matrix_bytes(const rk_matrix *m);
 int rk_same_device(const rk_matrix *a, const rk_matrix *b);
 /* out[rows] = m·x[cols] (Matrix.MulVec, device.go:762-764). */
 int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x);
+/* out[t][rows] = m·x[t][cols] for t < n: the products of ForwardMany's
+ * token-by-token Forward (model.go:504-518), each bit for bit one
+ * Matrix.MulVec (device.go:762-764). A Q8_0 matrix whose width is a
+ * multiple of 128 takes one pass over its weights on the tensor cores;
+ * other matrices run one product per vector. */
+int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const float *x);
 /* outs[i] = ms[i]·x for matrices on one device, in one submission
  * (MulVecs, device.go:769-793). */
 int rk_mulvecs(int n, rk_matrix *const *ms, float *const *outs, const float *x);
@@ -203,8 +209,13 @@ int rk_stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int 
 void rk_stage_free(rk_stage *s);                                                        /* Stage.Close, model.go:495-500 */
 int rk_stage_positions(const rk_stage *s);                                              /* Stage.Positions, model.go:487 */
 /* Stage.ForwardMany (model.go:504-518): tokens activations of dim floats,
- * at positions pos, pos+1, ..., run through the stage in place. */
+ * at positions pos, pos+1, ..., run through the stage in place. Up to 64
+ * tokens at a time; when every matrix of an unsharded stage is Q8_0 with
+ * widths that are multiples of 128, each projection runs once per 64
+ * tokens on the tensor cores (bits as the token-by-token Forward). */
 int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens);
+/* 1 when rk_stage_forward runs this stage's products batched, else 0. */
+int rk_stage_batched(const rk_stage *s);
 /* Head (model.go:413-417) from an uploaded classifier (not owned). */
 int rk_head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_head **out);
 void rk_head_free(rk_head *h);

@@ -14,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "librakkan_cuda.so")
-SOURCES = ["rk_matvec.cu", "rk_layer.cu", "rk_tensor.cu", "rk_gen.cu", "rk_capi.cu", "rk_noalloc.cu"]
+SOURCES = ["rk_matvec.cu", "rk_layer.cu", "rk_tensor.cu", "rk_gen.cu", "rk_capi.cu", "rk_noalloc.cu", "rk_mvmany.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 FLAGS = [

@@ -189,6 +189,7 @@ extern "C" int rk_device_open(int index, rk_device **out) {
   cudaError_t e = init_matvec_attributes();
   if (e == cudaSuccess) e = init_layer_attributes();
   if (e == cudaSuccess) e = init_tensor_attributes();
+  if (e == cudaSuccess) e = init_mvmany_attributes();
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&d->err_dev, 2 * sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, 2 * sizeof(int));
@@ -568,6 +569,49 @@ extern "C" int rk_mulvecs(int n, rk_matrix *const *ms, float *const *outs, const
 extern "C" int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x) {
   if (!m) return fail(RK_ERR_ARGS, "null matrix");
   return rk_mulvecs(1, &m, &out, x);
+}
+
+extern "C" int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const float *x) {
+  if (!m || n < 0 || (n > 0 && (!x || !out))) return fail(RK_ERR_ARGS, "bad argument");
+  if (n == 0) return RK_OK;
+  if (m->fmt != RK_FMT_Q8_0 || !mv_many_ok(m->rows, m->cols, m->w, m->s)) {
+    // Formats and widths the batched kernel does not take: one product per
+    // vector, as ForwardMany's per-token Forward does.
+    for (int t = 0; t < n; t++) {
+      int rc = rk_matrix_mulvec(m, out + (size_t)t * m->rows, x + (size_t)t * m->cols);
+      if (rc) return rc;
+    }
+    return RK_OK;
+  }
+  rk_device *d = m->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  const size_t cols = (size_t)m->cols, rows = (size_t)m->rows;
+  float *dx = nullptr, *dxs = nullptr, *dout = nullptr;
+  int8_t *dqx = nullptr;
+  cudaError_t e = cudaMalloc(&dx, 4 * n * cols);
+  if (e == cudaSuccess) e = cudaMalloc(&dqx, n * cols);
+  if (e == cudaSuccess) e = cudaMalloc(&dxs, 4 * n * (cols / 32));
+  if (e == cudaSuccess) e = cudaMalloc(&dout, 4 * n * rows);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, 4 * n * cols, cudaMemcpyHostToDevice, d->st);
+  if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, d->st);
+  if (e == cudaSuccess) {
+    MmArgs a{};
+    a.rows = m->rows;
+    a.cols = m->cols;
+    a.ntok = n;
+    a.out = dout;
+    a.out_stride = (long long)rows;
+    a.epi = EPI_STORE;
+    a.err = d->err_dev;
+    e = launch_mv_many(a, m->w, m->s, dqx, dxs, d->sms, d->st);
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, 4 * n * rows, cudaMemcpyDeviceToHost, d->st);
+  rc = e == cudaSuccess ? sync_dev(d) : cuda_fail(e, "batched matvec");
+  cudaStreamSynchronize(d->st);
+  for (void *p : {(void *)dx, (void *)dqx, (void *)dxs, (void *)dout}) cudaFree(p);
+  return rc;
 }
 
 extern "C" int rk_matrix_download(rk_matrix *m, void *w, float *scales) {
@@ -1186,6 +1230,14 @@ struct rk_stage {
   int64_t bytes = 0;
   cudaGraphExec_t graph = nullptr;
   int io_tokens = 64;  // gpuBatch, gpustage.go:17
+  // ForwardMany's batched layers (stage_forward_many), when every product
+  // takes the batched kernel: per-token rows of q, k, v, attOut, hb, hb2
+  // (io_tokens each), the tokens' Q8_0 inputs, and their positions.
+  bool many = false;
+  float *m_q = nullptr, *m_k = nullptr, *m_v = nullptr, *m_att = nullptr, *m_hb = nullptr, *m_hb2 = nullptr,
+        *m_xs = nullptr;
+  int8_t *m_qx = nullptr;
+  int *m_pos = nullptr, *pin_pos = nullptr;
   // Row sharding (layer_dims): this process's rank of G; null/1 unsharded.
   rk_group *grp = nullptr;
   int G = 1, rank = 0;
@@ -1217,6 +1269,7 @@ static void stage_release(rk_stage *s) {
     if (s->peer_base[g] && s->peer_base[g] != s->xbase) cudaIpcCloseMemHandle(s->peer_base[g]);
   for (void *p : s->allocs) cudaFree(p);
   cudaFreeHost(s->pin_io);
+  cudaFreeHost(s->pin_pos);
   s->d->used -= s->bytes;
   delete s;
 }
@@ -1258,14 +1311,70 @@ __global__ void k_epoch(unsigned *epoch) {
 // Records one position's pass through the stage's layers (gpustage.go:119-152
 // in the order of Stage.Forward, model.go:537-611), reading the position
 // from s->pos_dev. x is s->x.
+// The arguments of layer li's post-processing (bias, QK-norm, RoPE, cache
+// append; model.go:542-568) and attention (model.go:571-587) for one token
+// whose q/k/v are given, at position *pos_dev, writing out (this rank's
+// heads of attOut).
+static void attention_args(const rk_stage *s, size_t li, float *q, float *k, float *v, float *out,
+                           const int *pos_dev, QkvPostArgs *qp_out, AttnArgs *at_out) {
+  const rk_config *c = &s->c;
+  const rk_layer *l = s->layers[li];
+  const float *vec = l->vecs->v;
+  const int hs = head_size(c), G = s->G, heads_l = c->heads / G, kvh_l = c->kv_heads / G;
+  const int h0 = s->rank * heads_l, kv0 = s->rank * kvh_l;
+  QkvPostArgs qp{};
+  qp.q = q;
+  qp.k = k;
+  qp.v = v;
+  if (c->qkv_bias) {
+    qp.bq = vec + l->o_bq + h0 * hs;
+    qp.bk = vec + l->o_bk + kv0 * hs;
+    qp.bv = vec + l->o_bv + kv0 * hs;
+  }
+  if (c->qk_norm) {
+    qp.q_norm = vec + l->o_qn;
+    qp.k_norm = vec + l->o_kn;
+  }
+  qp.cos_ = s->cos_;
+  qp.sin_ = s->sin_;
+  qp.key_cache = s->keys[li];
+  qp.val_cache = s->vals[li];
+  qp.v_pitch = s->v_pitch;
+  qp.pos_dev = pos_dev;
+  qp.heads = heads_l;
+  qp.kv_heads = kvh_l;
+  qp.hs = hs;
+  qp.eps = cfg_eps(c);
+  qp.recip_hs = host_recip32((float)hs);
+  AttnArgs at{};
+  at.q = q;
+  at.keys = s->keys[li];
+  at.vals = s->vals[li];
+  at.v_pitch = s->v_pitch;
+  at.att = s->att;
+  at.out = out;
+  at.positions_dev = pos_dev;
+  at.positions_add = 1;
+  at.max_positions = s->ctx;
+  at.heads = heads_l;
+  at.kv_heads = kvh_l;
+  at.hs = hs;
+  at.kv_dim = kvh_l * hs;
+  at.att_stride = s->att_stride;
+  at.inv_sqrt = (float)(1 / sqrt((double)hs));
+  at.err = s->d->err_dev;
+  *qp_out = qp;
+  *at_out = at;
+}
+
 static int record_layers(rk_stage *s, cudaStream_t st) {
   rk_device *d = s->d;
   const rk_config *c = &s->c;
   const int hs = head_size(c), qd = c->heads * hs, D = c->dim, H = c->hidden;
-  // This rank's part (everything when unsharded): query heads h0.., kv
-  // heads kv0.., rows r0.. of Wo/W2 (of D) and rH0.. of W1/W3 (of H).
-  const int G = s->G, heads_l = c->heads / G, kvh_l = c->kv_heads / G;
-  const int h0 = s->rank * heads_l, kv0 = s->rank * kvh_l, r0 = s->rank * (D / G), rH0 = s->rank * (H / G);
+  // This rank's part (everything when unsharded): query heads h0.., rows
+  // r0.. of Wo/W2 (of D) and rH0.. of W1/W3 (of H).
+  const int G = s->G, heads_l = c->heads / G;
+  const int h0 = s->rank * heads_l, r0 = s->rank * (D / G), rH0 = s->rank * (H / G);
   auto gather = [&](float *buf, int total) -> int { return G > 1 ? group_gather(s->grp, buf, total / G, st) : RK_OK; };
   // Fused gathers (p2p): gather point slot = layer·4 + {0: attOut, 1: x
   // after Wo, 2: hb, 3: x after W2}. A point is fused when its producer
@@ -1301,8 +1410,7 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   };
   if (s->p2p) CK(launch_k(k_epoch, 1, 32, 0, st, epoch));
   const float eps = cfg_eps(c);
-  const float recipD = host_recip32((float)D), recipHS = host_recip32((float)hs);
-  const float invSqrt = (float)(1 / sqrt((double)hs));
+  const float recipD = host_recip32((float)D);
   // ms·(rmsNorm(x, norm_w) or x). A quantized product's CTAs quantize their
   // input themselves when it fits their shared memory; otherwise one
   // quantize launch fills the stage's scratch first. Float matrices get the
@@ -1351,50 +1459,11 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     const GatherWait w_prev = f_prev ? wait_for(sl - 1, s->off_xll) : GatherWait{};
     int rc = products(3, qkv, qkv_out, s->x, vec + l->o_rms_att, D, EPI_STORE, nullptr, &w_prev);
     if (rc) return rc;
-    // Bias, QK-norm, RoPE, cache append (model.go:542-568).
-    QkvPostArgs qp{};
-    qp.q = s->q;
-    qp.k = s->k;
-    qp.v = s->v;
-    if (c->qkv_bias) {
-      qp.bq = vec + l->o_bq + h0 * hs;
-      qp.bk = vec + l->o_bk + kv0 * hs;
-      qp.bv = vec + l->o_bv + kv0 * hs;
-    }
-    if (c->qk_norm) {
-      qp.q_norm = vec + l->o_qn;
-      qp.k_norm = vec + l->o_kn;
-    }
-    qp.cos_ = s->cos_;
-    qp.sin_ = s->sin_;
-    qp.key_cache = s->keys[li];
-    qp.val_cache = s->vals[li];
-    qp.v_pitch = s->v_pitch;
-    qp.pos_dev = s->pos_dev;
-    qp.heads = heads_l;
-    qp.kv_heads = kvh_l;
-    qp.hs = hs;
-    qp.eps = eps;
-    qp.recip_hs = recipHS;
-    // Attention over positions 0..pos (model.go:571-587), after the
-    // post-processing above.
-    AttnArgs at{};
-    at.q = s->q;
-    at.keys = s->keys[li];
-    at.vals = s->vals[li];
-    at.v_pitch = s->v_pitch;
-    at.att = s->att;
-    at.out = s->att_out + h0 * hs;
-    at.positions_dev = s->pos_dev;
-    at.positions_add = 1;
-    at.max_positions = s->ctx;
-    at.heads = heads_l;
-    at.kv_heads = kvh_l;
-    at.hs = hs;
-    at.kv_dim = kvh_l * hs;
-    at.att_stride = s->att_stride;
-    at.inv_sqrt = invSqrt;
-    at.err = s->d->err_dev;
+    // Bias, QK-norm, RoPE, cache append (model.go:542-568), then attention
+    // over positions 0..pos (model.go:571-587).
+    QkvPostArgs qp;
+    AttnArgs at;
+    attention_args(s, li, s->q, s->k, s->v, s->att_out + h0 * hs, s->pos_dev, &qp, &at);
     if (f_att) at.put = put_for(sl, s->off_attll, (size_t)h0 * hs);
     CK(launch_attention_post(qp, at, st));
     if (!f_att && (rc = gather(s->att_out, qd))) return rc;
@@ -1569,6 +1638,73 @@ static int stage_p2p_setup(rk_stage *s) {
   return RK_OK;
 }
 
+// Whether ForwardMany can run the stage's layers with batched products:
+// unsharded, every matrix Q8_0 and taken by the batched kernel.
+static bool stage_many_ok(const rk_stage *s) {
+  if (s->G != 1 || s->layers.empty()) return false;
+  for (const rk_layer *l : s->layers)
+    for (const rk_matrix *m : {l->wq, l->wk, l->wv, l->wo, l->w1, l->w3, l->w2})
+      if (m->fmt != RK_FMT_Q8_0 || !mv_many_ok(m->rows, m->cols, m->w, m->s)) return false;
+  return true;
+}
+
+// Stage.ForwardMany (model.go:504-518) for the nt tokens in s->io at
+// positions pos.., layer by layer. Each projection runs once for all nt
+// tokens on the tensor cores (launch_mv_many); the bias / QK-norm / RoPE /
+// cache append and the attention run token after token in position order,
+// so token t's attention reads the cache rows appended before it, as the
+// reference's token-by-token Forward does. Every element is computed by the
+// same operations in the same order as in Forward.
+static int stage_forward_many(rk_stage *s, int pos, int nt) {
+  rk_device *d = s->d;
+  const rk_config *c = &s->c;
+  cudaStream_t st = d->st;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
+  const float eps = cfg_eps(c), recipD = host_recip32((float)D);
+  for (int t = 0; t < nt; t++) s->pin_pos[t] = pos + t;
+  CK(cudaMemcpyAsync(s->m_pos, s->pin_pos, sizeof(int) * nt, cudaMemcpyHostToDevice, st));
+  const auto product = [&](const rk_matrix *m, float *out, long long stride, int epi) {
+    MmArgs a{};
+    a.rows = m->rows;
+    a.cols = m->cols;
+    a.ntok = nt;
+    a.out = out;
+    a.out_stride = stride;
+    a.epi = epi;
+    a.err = d->err_dev;
+    return launch_mv_many(a, m->w, m->s, s->m_qx, s->m_xs, d->sms, st);
+  };
+  float *X = s->io;
+  for (size_t li = 0; li < s->layers.size(); li++) {
+    const rk_layer *l = s->layers[li];
+    const float *vec = l->vecs->v;
+    // q, k, v = Wq·xb, Wk·xb, Wv·xb with xb = rmsNorm(x, RmsAtt) (model.go:538-539).
+    CK(launch_quantize_many(X, nt, D, vec + l->o_rms_att, recipD, eps, s->m_qx, s->m_xs, st));
+    CK(product(l->wq, s->m_q, qd, EPI_STORE));
+    CK(product(l->wk, s->m_k, kvd, EPI_STORE));
+    CK(product(l->wv, s->m_v, kvd, EPI_STORE));
+    for (int t = 0; t < nt; t++) {
+      QkvPostArgs qp;
+      AttnArgs at;
+      attention_args(s, li, s->m_q + (size_t)t * qd, s->m_k + (size_t)t * kvd, s->m_v + (size_t)t * kvd,
+                     s->m_att + (size_t)t * qd, s->m_pos + t, &qp, &at);
+      CK(launch_attention_post(qp, at, st));
+    }
+    // x += Wo·attOut (model.go:588-594).
+    CK(launch_quantize_many(s->m_att, nt, qd, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, st));
+    CK(product(l->wo, X, D, EPI_ADD));
+    // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603).
+    CK(launch_quantize_many(X, nt, D, vec + l->o_rms_ffn, recipD, eps, s->m_qx, s->m_xs, st));
+    CK(product(l->w1, s->m_hb, H, EPI_STORE));
+    CK(product(l->w3, s->m_hb2, H, EPI_STORE));
+    CK(launch_silu_mul_many(s->m_hb, s->m_hb2, (long long)nt * H, d->sms, st));
+    // x = Canonical(x + W2·hb) (model.go:604-610).
+    CK(launch_quantize_many(s->m_hb, nt, H, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, st));
+    CK(product(l->w2, X, D, EPI_ADD_CANON));
+  }
+  return RK_OK;
+}
+
 static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *grp,
                      rk_stage **out) {
   if (!d || !c || !out || n < 0 || (n > 0 && !layers) || ctx <= 0) return fail(RK_ERR_ARGS, "bad argument");
@@ -1644,6 +1780,24 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     if ((rc = A(4 * (size_t)(s->v_pitch > 0 ? s->v_pitch : ctx) * kvd, &p))) goto fail_;
     s->vals.push_back((float *)p);
   }
+  s->many = stage_many_ok(s);
+  if (s->many) {
+    const size_t T = (size_t)s->io_tokens;
+    ALLOC(m_q, 4 * T * qd);
+    ALLOC(m_k, 4 * T * kvd);
+    ALLOC(m_v, 4 * T * kvd);
+    ALLOC(m_att, 4 * T * qd);
+    ALLOC(m_hb, 4 * T * H);
+    ALLOC(m_hb2, 4 * T * H);
+    ALLOC(m_qx, T * widest);
+    ALLOC(m_xs, 4 * T * (widest / 32));
+    ALLOC(m_pos, 4 * T);
+    cudaError_t e = cudaMallocHost(&s->pin_pos, 4 * T);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "stage staging");
+      goto fail_;
+    }
+  }
 #undef ALLOC
   {
     cudaError_t e = cudaMallocHost(&s->pin_io, 4 * (size_t)s->io_tokens * D);
@@ -1706,6 +1860,8 @@ extern "C" void rk_stage_free(rk_stage *s) {
 
 extern "C" int rk_stage_positions(const rk_stage *s) { return s ? s->ctx : 0; }
 
+extern "C" int rk_stage_batched(const rk_stage *s) { return s && s->many ? 1 : 0; }
+
 extern "C" int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens) {
   if (!s || (tokens > 0 && !xs) || tokens < 0) return fail(RK_ERR_ARGS, "bad argument");
   if (pos < 0 || pos + tokens > s->ctx) return fail(RK_ERR_ARGS, "positions [%d, %d) outside the stage's %d", pos, pos + tokens, s->ctx);
@@ -1718,10 +1874,14 @@ extern "C" int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens) {
     const int nt = std::min(s->io_tokens, tokens - start);
     memcpy(s->pin_io, xs + (size_t)start * D, sizeof(float) * (size_t)nt * D);
     CK(cudaMemcpyAsync(s->io, s->pin_io, sizeof(float) * (size_t)nt * D, cudaMemcpyHostToDevice, d->st));
-    const int hdr[2] = {0, pos + start};
-    CK(cudaMemcpyAsync(s->tok_dev, &hdr[0], sizeof(int), cudaMemcpyHostToDevice, d->st));
-    CK(cudaMemcpyAsync(s->pos_dev, &hdr[1], sizeof(int), cudaMemcpyHostToDevice, d->st));
-    for (int t = 0; t < nt; t++) CK(cudaGraphLaunch(s->graph, d->st));
+    if (s->many && nt > 1) {
+      if ((rc = stage_forward_many(s, pos + start, nt))) return rc;
+    } else {
+      const int hdr[2] = {0, pos + start};
+      CK(cudaMemcpyAsync(s->tok_dev, &hdr[0], sizeof(int), cudaMemcpyHostToDevice, d->st));
+      CK(cudaMemcpyAsync(s->pos_dev, &hdr[1], sizeof(int), cudaMemcpyHostToDevice, d->st));
+      for (int t = 0; t < nt; t++) CK(cudaGraphLaunch(s->graph, d->st));
+    }
     CK(cudaMemcpyAsync(s->pin_io, s->io, sizeof(float) * (size_t)nt * D, cudaMemcpyDeviceToHost, d->st));
     if ((rc = sync_dev(d))) return rc;
     memcpy(xs + (size_t)start * D, s->pin_io, sizeof(float) * (size_t)nt * D);

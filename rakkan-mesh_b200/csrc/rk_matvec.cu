@@ -205,6 +205,32 @@ cudaError_t launch_quantize_act(const float *x, int n, const float *w, float rec
   return launch_k(k_quantize_act<false>, 1, threads, 0, st, x, n, w, recipN, eps, qx, xs, xsum);
 }
 
+// quantize8 (after rmsNorm when w is given) of each of n rows of x
+// ([n][cols]), a CTA per row: ForwardMany's token-by-token prologue of a
+// batched product. qx is [n][cols], xs [n][cols/32].
+template <bool NORM>
+__global__ void __launch_bounds__(512) k_quantize_many(const float *__restrict__ x, int cols,
+                                                       const float *__restrict__ w, float recipN, float eps,
+                                                       int8_t *__restrict__ qx, float *__restrict__ xs) {
+  __shared__ float s_inv;
+  __shared__ __align__(16) float stage[kQuantStage];
+  __shared__ __align__(16) float wstage[NORM ? kQuantStage : 4];
+  griddep_trigger();
+  griddep_wait();
+  const size_t t = blockIdx.x;
+  quantize_warps<NORM>(x + t * cols, cols, w, recipN, eps, qx + t * cols, xs + t * (cols / 32), nullptr, &s_inv,
+                       stage, wstage, kQuantStage, false);
+}
+
+cudaError_t launch_quantize_many(const float *x, int n, int cols, const float *w, float recipN, float eps,
+                                 int8_t *qx, float *xs, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (cols <= 0 || cols % 32) return cudaErrorInvalidValue;
+  const int threads = cols >= 16 * 32 ? 512 : (cols / 32) * 32;
+  if (w) return launch_k(k_quantize_many<true>, n, threads, 0, st, x, cols, w, recipN, eps, qx, xs);
+  return launch_k(k_quantize_many<false>, n, threads, 0, st, x, cols, w, recipN, eps, qx, xs);
+}
+
 // ---------------------------------------------------------------------------
 // PTX helpers: mbarrier + 1-D bulk copy global -> shared (no multicast).
 // ---------------------------------------------------------------------------

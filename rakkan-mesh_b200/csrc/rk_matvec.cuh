@@ -105,4 +105,35 @@ bool matvec_fused_ok(int fmt, int cols, bool norm);
 // any launch or graph capture.
 cudaError_t init_matvec_attributes();
 
+// ---- Products of one Q8_0 matrix with many input vectors (ForwardMany's
+// projections, model.go:504-518: each token's product is one MatVecQ8) on
+// the tcgen05 tensor cores; bits identical to the single-vector kernel. ----
+struct MmArgs {
+  int rows, cols, ntok;
+  float *out;             // token t's row r at out[t·out_stride + r]
+  long long out_stride;
+  int epi;                // EPI_STORE, EPI_ADD or EPI_ADD_CANON
+  int *err;               // device error word (a bounded wait gave up)
+};
+
+// Whether a matrix can take the batched kernel: Q8_0 rows of a multiple of
+// 128 columns, weights and scales 16-byte aligned, TMA available.
+bool mv_many_ok(int rows, int cols, const void *w, const float *ws);
+
+// out = W·x_t for the ntok tokens whose Q8_0 inputs are qx [ntok][cols]
+// and xs [ntok][cols/32] (16-byte aligned device buffers).
+cudaError_t launch_mv_many(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx, const float *xs,
+                           int num_sms, cudaStream_t st);
+
+// quantize8 of each of n rows of x [n][cols] (after rmsNorm with w when w
+// is given): qx [n][cols], xs [n][cols/32].
+cudaError_t launch_quantize_many(const float *x, int n, int cols, const float *w, float recipN, float eps,
+                                 int8_t *qx, float *xs, cudaStream_t st);
+
+// hb[i] = silu(hb[i])·hb2[i] (model.go:601-603) for i < n.
+cudaError_t launch_silu_mul_many(float *hb, const float *hb2, long long n, int num_sms, cudaStream_t st);
+
+// Raises the batched kernel's shared-memory limit; once per device.
+cudaError_t init_mvmany_attributes();
+
 }  // namespace rk

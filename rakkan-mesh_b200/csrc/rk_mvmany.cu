@@ -1,0 +1,301 @@
+// rk_mvmany.cu — Q8_0 products of one matrix with many input vectors on the
+// tcgen05 tensor cores: the projections of Stage.ForwardMany
+// (internal/llm/model.go:504-518), which runs Forward once per token, so
+// every token's product is one MatVecQ8 (internal/num/quant.go:167-181).
+//
+// Reference arithmetic, per row and token (quant.go:157-164, 198-207): the
+// token's Q8_0 input (quantize8, quant.go:34-53); block b's exact int32 sum
+// of w·qx; s[b mod 8] += float32(float32(sum_b)·float32(ws_b·xs_b)) in
+// increasing b from +0; out = ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)).
+//
+// B200 mapping. A CTA owns 128 rows × NT tokens. TMA brings, per stage of
+// 128 input columns (four quant blocks), the weight tile (128 rows × 128
+// bytes, 128-byte swizzle), the tokens' Q8 tile (NT × 128 bytes, same
+// swizzle) and the two scale tiles (128 × 4 and NT × 4 floats) into a ring
+// of shared-memory stages. One thread issues one tcgen05.mma kind::i8 with
+// K = 32 per quant block, without accumulation, into its own TMEM column
+// group: after it, TMEM holds that block's exact int32 sums for all 128 × NT
+// (row, token) pairs. Epilogue warps read the blocks back in increasing b
+// (a thread per row and eight tokens) and run the eight f32 chains per
+// (row, token) in registers. The integer products cost the tensor pipe a
+// few cycles per block; the ordered float work on the CUDA cores and the
+// weight stream bound the kernel. Consecutive CTAs take the token tiles of
+// one row tile, so a weight tile comes from HBM once and from L2 after.
+#include <algorithm>
+#include <cuda.h>
+#include <type_traits>
+
+#include "rk_common.cuh"
+#include "rk_matvec.cuh"
+#include "rk_tensor.cuh"
+#include "rk_umma.cuh"
+
+namespace rk {
+
+constexpr int kMmStages = 6;  // shared-memory stages (128 input columns each)
+constexpr int kMmGroups = 4;  // TMEM column groups (one stage's four blocks each)
+
+template <int NT>
+struct MmCfg {
+  static constexpr int kEpiWarps = NT / 2;  // NT/8 warpgroups: a row and 8 tokens per thread
+  static constexpr int kThreads = 32 * (kEpiWarps + 2);
+  static constexpr int kW = 128 * 128;    // weight tile bytes
+  static constexpr int kX = NT * 128;     // token tile bytes
+  static constexpr int kWs = 128 * 16;    // weight scales: 128 rows × 4 blocks
+  static constexpr int kXs = NT * 16;     // token scales: NT tokens × 4 blocks
+  static constexpr int kTx = kW + kX + kWs + kXs;
+  static constexpr int kStage = (kTx + 1023) / 1024 * 1024;
+  static constexpr int kSmem = kMmStages * kStage + 1024;  // + slack to align the ring to 1024 bytes
+  static constexpr int kCols = kMmGroups * 4 * NT;         // 256 or 512 TMEM columns
+};
+
+// Blocks K0..K0+NK-1 of a stage for this thread's row and eight tokens,
+// into chains 4·HALF + kk (a stage starts at block 4i, so even stages feed
+// chains 0-3 and odd stages chains 4-7). v[kk][j]: the block sums of token
+// j; ws: the row's four weight scales; xs: the eight tokens' four input
+// scales each, in shared memory.
+template <int HALF, int K0, int NK>
+RK_DEV void mm_terms(float (&acc)[8][8], const int32_t (&v)[NK][8], float4 ws, const float4 *xs) {
+  const float w4[4] = {ws.x, ws.y, ws.z, ws.w};
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const float4 x4 = xs[j];
+    const float xj[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+    for (int kk = 0; kk < NK; kk++) {
+      const float term = __fmul_rn(__int2float_rn(v[kk][j]), __fmul_rn(w4[K0 + kk], xj[K0 + kk]));
+      acc[j][4 * HALF + K0 + kk] = __fadd_rn(acc[j][4 * HALF + K0 + kk], term);
+    }
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
+    k_mv_many_q8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                 const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs, MmArgs a) {
+  using C = MmCfg<NT>;
+  constexpr int S = kMmStages, G = kMmGroups, E = C::kEpiWarps;
+  extern __shared__ uint8_t dsmem[];
+  __shared__ __align__(8) uint64_t bars[2 * S + 2 * G + 1];
+  __shared__ uint32_t tmem_slot;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ring = (umma::smem_u32(dsmem) + 1023u) & ~1023u;
+  uint8_t *const ring_p = dsmem + (ring - umma::smem_u32(dsmem));
+  const uint32_t bar0 = umma::smem_u32(bars);
+  const auto full = [&](int s) { return bar0 + 8u * s; };
+  const auto empty = [&](int s) { return bar0 + 8u * (S + s); };
+  const auto accf = [&](int g) { return bar0 + 8u * (2 * S + g); };
+  const auto acce = [&](int g) { return bar0 + 8u * (2 * S + G + g); };
+  const uint32_t done = bar0 + 8u * (2 * S + 2 * G);
+  const int t0 = blockIdx.x * NT, r0 = blockIdx.y * 128;
+  const int nkb = a.cols / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      umma::mbar_init(full(s), 1);
+      umma::mbar_init(empty(s), 1 + E);  // the MMAs' commit and every epilogue warp
+    }
+    for (int g = 0; g < G; g++) {
+      umma::mbar_init(accf(g), 1);
+      umma::mbar_init(acce(g), E);
+    }
+    umma::mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    umma::prefetch_tmap(&tmW);
+    umma::prefetch_tmap(&tmX);
+    umma::prefetch_tmap(&tmWs);
+    umma::prefetch_tmap(&tmXs);
+  }
+  __syncwarp();
+  if (warp == E + 1) umma::tmem_alloc(umma::smem_u32(&tmem_slot), C::kCols);
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+  griddep_wait();  // the tokens' Q8 input and the output come from earlier kernels
+
+  if (warp == E) {
+    if (lane == 0) {  // TMA producer
+      int issued = 0;
+      for (int i = 0; i < nkb; i++) {
+        const int s = i % S;
+        if (i >= S && !umma::mbar_wait(empty(s), ((i / S) & 1) ^ 1)) {
+          atomicExch(a.err, DEV_ERR_TIMEOUT);
+          break;
+        }
+        const uint32_t st = ring + s * C::kStage;
+        umma::mbar_expect_tx(full(s), C::kTx);
+        umma::tma_load_2d(st, &tmW, i * 128, r0, full(s));
+        umma::tma_load_2d(st + C::kW, &tmX, i * 128, t0, full(s));
+        umma::tma_load_2d(st + C::kW + C::kX, &tmWs, i * 4, r0, full(s));
+        umma::tma_load_2d(st + C::kW + C::kX + C::kWs, &tmXs, i * 4, t0, full(s));
+        issued = i + 1;
+      }
+      // Copies still in flight land before the CTA exits (bounded).
+      for (int i = max(0, issued - S); i < issued; i++) umma::mbar_wait(full(i % S), (i / S) & 1);
+    }
+    __syncwarp();
+  } else if (warp == E + 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = umma::idesc_i8(128, NT, 0);
+      for (int i = 0; i < nkb; i++) {
+        const int s = i % S, g = i % G;
+        if (!umma::mbar_wait(full(s), (i / S) & 1) || (i >= G && !umma::mbar_wait(acce(g), ((i / G) & 1) ^ 1))) {
+          atomicExch(a.err, DEV_ERR_TIMEOUT);
+          break;
+        }
+        umma::fence_after_sync();
+        const uint32_t sw = ring + s * C::kStage, sx = sw + C::kW;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          umma::mma_i8(tmem + (uint32_t)(g * 4 * NT + kk * NT), umma::desc_sw128(sw + kk * 32),
+                       umma::desc_sw128(sx + kk * 32), idesc, 0u);
+        umma::mma_commit(empty(s));  // this stage's operands are read
+        umma::mma_commit(accf(g));   // group g holds blocks 4i..4i+3
+      }
+      umma::mma_commit(done);
+    }
+    __syncwarp();
+  } else {  // epilogue: warp w reads TMEM lanes 32·(w mod 4).., tokens 8·(w / 4)..
+    const int q = warp & 3, tk0 = 8 * (warp >> 2);
+    const int row = r0 + 32 * q + lane;
+    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)tk0;
+    float acc[8][8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int c = 0; c < 8; c++) acc[j][c] = 0.0f;
+    bool ok = true;
+    // Stage i: waits for its sums, reads them out of TMEM and releases the
+    // TMEM group, adds the terms, then releases the shared-memory stage
+    // (its scales were read in place).
+    const auto stage = [&](int i, auto half) -> bool {
+      const int s = i % S, g = i % G;
+      if (!umma::mbar_wait(accf(g), (i / G) & 1) || !umma::mbar_wait(full(s), (i / S) & 1)) return false;
+      umma::fence_after_sync();
+      const uint8_t *sp = ring_p + s * C::kStage;
+      const float4 ws = *reinterpret_cast<const float4 *>(sp + C::kW + C::kX + 16 * (32 * q + lane));
+      const float4 *xs = reinterpret_cast<const float4 *>(sp + C::kW + C::kX + C::kWs) + tk0;
+      constexpr int H = decltype(half)::value;
+      const uint32_t tg = tl + (uint32_t)(g * 4 * NT);
+      if constexpr (NT <= 16) {  // all four blocks' sums at once
+        int32_t v[4][8];
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) umma::tmem_ld8(tg + (uint32_t)(kk * NT), v[kk]);
+        umma::tmem_ld_wait();
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) umma::mbar_arrive(acce(g));
+        mm_terms<H, 0, 4>(acc, v, ws, xs);
+      } else {  // two blocks at a time (the wider CTA has fewer registers per thread)
+        int32_t v[2][8];
+        umma::tmem_ld8(tg, v[0]);
+        umma::tmem_ld8(tg + (uint32_t)NT, v[1]);
+        umma::tmem_ld_wait();
+        mm_terms<H, 0, 2>(acc, v, ws, xs);
+        umma::tmem_ld8(tg + (uint32_t)(2 * NT), v[0]);
+        umma::tmem_ld8(tg + (uint32_t)(3 * NT), v[1]);
+        umma::tmem_ld_wait();
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) umma::mbar_arrive(acce(g));
+        mm_terms<H, 2, 2>(acc, v, ws, xs);
+      }
+      __syncwarp();
+      if (lane == 0) umma::mbar_arrive(empty(s));
+      return true;
+    };
+    for (int i = 0; i < nkb; i += 2) {
+      if (!(ok = stage(i, std::integral_constant<int, 0>()))) break;
+      if (i + 1 < nkb && !(ok = stage(i + 1, std::integral_constant<int, 1>()))) break;
+    }
+    if (!ok) {
+      atomicExch(a.err, DEV_ERR_TIMEOUT);
+    } else if (row < a.rows) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int t = t0 + tk0 + j;
+        if (t >= a.ntok) break;
+        const float r = __fadd_rn(__fadd_rn(__fadd_rn(acc[j][0], acc[j][1]), __fadd_rn(acc[j][2], acc[j][3])),
+                                  __fadd_rn(__fadd_rn(acc[j][4], acc[j][5]), __fadd_rn(acc[j][6], acc[j][7])));
+        float *p = a.out + (size_t)t * a.out_stride + row;
+        if (a.epi == EPI_ADD)
+          *p = __fadd_rn(*p, r);
+        else if (a.epi == EPI_ADD_CANON)
+          *p = canonical(__fadd_rn(*p, r));
+        else
+          *p = r;
+      }
+    }
+  }
+  // TMEM is freed only after every MMA this CTA issued has completed.
+  if (!umma::mbar_wait(done, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
+  umma::fence_before_sync();
+  __syncthreads();
+  griddep_trigger();
+  if (warp == E + 1) umma::tmem_dealloc(tmem, C::kCols);
+}
+
+// hb[i] = silu(hb[i]) · hb2[i] (model.go:601-603) over n elements.
+__global__ void k_silu_mul_many(float *__restrict__ hb, const float *__restrict__ hb2, long long n) {
+  griddep_trigger();
+  griddep_wait();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    hb[i] = __fmul_rn(silu(hb[i]), hb2[i]);
+}
+
+template <int NT>
+static cudaError_t set_mm_attr() {
+  return cudaFuncSetAttribute(k_mv_many_q8<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmCfg<NT>::kSmem);
+}
+
+cudaError_t init_mvmany_attributes() {
+  cudaError_t e = set_mm_attr<16>();
+  const cudaError_t e2 = set_mm_attr<32>();
+  return e != cudaSuccess ? e : e2;
+}
+
+bool mv_many_ok(int rows, int cols, const void *w, const float *ws) {
+  const auto aligned = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+  // The scale rows (cols/32 floats) must be whole 16-byte strides for TMA,
+  // and a stage is 128 columns.
+  return rows > 0 && cols > 0 && cols % 128 == 0 && cols < (1 << 17) && aligned(w) && aligned(ws) &&
+         tmap_available();
+}
+
+template <int NT>
+static cudaError_t launch_mm_nt(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx,
+                                const float *xs, cudaStream_t st) {
+  CUtensorMap tmW, tmX, tmWs, tmXs;
+  const int nb = a.cols / 32;
+  if (!tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)a.cols, (uint64_t)a.rows, (uint64_t)a.cols, 128,
+               128, true) ||
+      !tmap_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, (uint64_t)a.cols, (uint64_t)a.ntok, (uint64_t)a.cols, 128,
+               NT, true) ||
+      !tmap_2d(&tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, (uint64_t)nb, (uint64_t)a.rows, 4ull * nb, 4, 128,
+               false) ||
+      !tmap_2d(&tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)nb, (uint64_t)a.ntok, 4ull * nb, 4, NT, false))
+    return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)((a.ntok + NT - 1) / NT), (unsigned)((a.rows + 127) / 128));
+  return launch_k(k_mv_many_q8<NT>, grid, MmCfg<NT>::kThreads, MmCfg<NT>::kSmem, st, tmW, tmX, tmWs, tmXs, a);
+}
+
+cudaError_t launch_mv_many(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx, const float *xs,
+                           int num_sms, cudaStream_t st) {
+  if (a.ntok <= 0) return cudaSuccess;
+  if (!mv_many_ok(a.rows, a.cols, w, ws) || ((uintptr_t)qx & 15) || ((uintptr_t)xs & 15))
+    return cudaErrorInvalidValue;
+  const long long row_tiles = (a.rows + 127) / 128;
+  // 32 tokens per CTA halve the weight tiles' re-reads from L2 once the
+  // grid fills the SMs anyway; otherwise 16 give twice the CTAs.
+  if (a.ntok > 16 && row_tiles * ((a.ntok + 31) / 32) >= num_sms) return launch_mm_nt<32>(a, w, ws, qx, xs, st);
+  return launch_mm_nt<16>(a, w, ws, qx, xs, st);
+}
+
+cudaError_t launch_silu_mul_many(float *hb, const float *hb2, long long n, int num_sms, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const long long blocks = std::min<long long>((n + 255) / 256, 4LL * num_sms);
+  return launch_k(k_silu_mul_many, (unsigned)blocks, 256, 0, st, hb, hb2, n);
+}
+
+}  // namespace rk

@@ -2,6 +2,7 @@
 // (rakkan-mesh internal/sandbox/tensor.go:286-339).
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace rk {
@@ -34,6 +35,14 @@ bool tensor_i8_tc_ok(int transposed, int m, int k, int n, const void *a, const v
 // Fills n elements of an int8 (dtype DT_I8) or float matrix with hashed
 // values of (seed, index): int8 in [-127, 127], floats in [-1, 1).
 cudaError_t launch_fill_hash(int dtype, void *p, long long n, uint32_t seed, cudaStream_t st);
+
+// A 2-D tensor map of a row-major matrix [outer][inner] (row_bytes apart)
+// seen in box_inner × box_outer tiles, with the 128-byte swizzle or none;
+// out-of-range elements read as zero. False when the driver entry point is
+// missing or the encoding is refused.
+bool tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *ptr, uint64_t inner, uint64_t outer,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+bool tmap_available();
 
 // Raises the tensor-core kernels' shared-memory limit; once per device.
 cudaError_t init_tensor_attributes();

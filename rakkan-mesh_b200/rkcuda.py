@@ -25,12 +25,12 @@ NOALLOC_MAX_COLS = 32768
 EXPORTS = [
     "rk_last_error", "rk_version", "rk_device_count", "rk_device_get_info", "rk_device_best", "rk_device_open",
     "rk_device_close", "rk_device_used", "rk_matrix_upload", "rk_matrix_free", "rk_matrix_bytes", "rk_same_device",
-    "rk_matrix_mulvec", "rk_mulvecs", "rk_matrix_mulvec_noalloc", "rk_vectors_upload", "rk_vectors_free", "rk_arena_new",
+    "rk_matrix_mulvec", "rk_matrix_mulvec_many", "rk_mulvecs", "rk_matrix_mulvec_noalloc", "rk_vectors_upload", "rk_vectors_free", "rk_arena_new",
     "rk_arena_set_quant_scratch", "rk_arena_bytes", "rk_arena_free", "rk_batch_begin", "rk_batch_write",
     "rk_batch_read", "rk_batch_matvecs", "rk_batch_quantize", "rk_batch_rmsnorm", "rk_batch_addvec", "rk_batch_rope",
     "rk_batch_copy", "rk_batch_attention", "rk_batch_residual", "rk_batch_silumul", "rk_batch_submit",
     "rk_config_validate", "rk_layer_upload", "rk_layer_from_device", "rk_layer_free", "rk_stage_new", "rk_stage_free",
-    "rk_stage_positions", "rk_stage_forward", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
+    "rk_stage_positions", "rk_stage_forward", "rk_stage_batched", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
     "rk_model_new", "rk_model_free", "rk_model_step", "rk_model_generate", "rk_tensor_matmul",
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
     "rk_bench_matvec", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
@@ -93,7 +93,7 @@ def lib():
             "rk_device_open": (i, [i, vp]), "rk_device_close": (None, [vp]), "rk_device_used": (i64, [vp]),
             "rk_matrix_upload": (i, [vp, i, i, i, vp, vp, vp]), "rk_matrix_free": (None, [vp]),
             "rk_matrix_bytes": (i64, [vp]), "rk_same_device": (i, [vp, vp]),
-            "rk_matrix_mulvec": (i, [vp, vp, vp]), "rk_mulvecs": (i, [i, vp, vp, vp]),
+            "rk_matrix_mulvec": (i, [vp, vp, vp]), "rk_matrix_mulvec_many": (i, [vp, i, vp, vp]), "rk_mulvecs": (i, [i, vp, vp, vp]),
             "rk_matrix_mulvec_noalloc": (i, [vp, vp, vp, vp]),
             "rk_vectors_upload": (i, [vp, vp, i64, vp]), "rk_vectors_free": (None, [vp]),
             "rk_arena_new": (i, [vp, i64, i64, vp]), "rk_arena_set_quant_scratch": (None, [vp, i64, i64]),
@@ -110,7 +110,7 @@ def lib():
             "rk_layer_upload": (i, [vp, vp, vp, vp]),
             "rk_layer_from_device": (i, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
             "rk_layer_free": (None, [vp]), "rk_stage_new": (i, [vp, vp, vp, i, i, vp]),
-            "rk_stage_free": (None, [vp]), "rk_stage_positions": (i, [vp]), "rk_stage_forward": (i, [vp, vp, i, i]),
+            "rk_stage_free": (None, [vp]), "rk_stage_positions": (i, [vp]), "rk_stage_forward": (i, [vp, vp, i, i]), "rk_stage_batched": (i, [vp]),
             "rk_head_new": (i, [vp, vp, vp, vp, vp]), "rk_head_free": (None, [vp]),
             "rk_head_logits": (i, [vp, vp, vp]), "rk_embed": (i, [vp, i, vp]),
             "rk_sample_argmax": (i, [vp, vp, i, vp]),
@@ -239,6 +239,14 @@ class Matrix:
         x = np.ascontiguousarray(x, dtype=np.float32)
         out = np.empty(self.rows, dtype=np.float32)
         _check(lib().rk_matrix_mulvec(self.h, _ptr(out), _ptr(x)))
+        return out
+
+    def mulvec_many(self, xs):
+        """W·x for every row x of xs [n][cols] (one MatVecQ8 each), in one
+        pass over the weights when the batched kernel takes the matrix."""
+        xs = np.ascontiguousarray(xs, dtype=np.float32).reshape(-1, self.cols)
+        out = np.empty((xs.shape[0], self.rows), dtype=np.float32)
+        _check(lib().rk_matrix_mulvec_many(self.h, xs.shape[0], _ptr(out), _ptr(xs)))
         return out
 
     def bench(self, iters=20, flush=True, fused=False):
@@ -417,6 +425,12 @@ class Stage:
         """1 when a sharded stage exchanges activations by NVLink stores and
         flags inside its kernels, 0 for NCCL all-gathers (or unsharded)."""
         return lib().rk_stage_fused_gathers(self.h)
+
+    def batched(self):
+        """1 when forward() of several tokens runs the products batched on
+        the tensor cores (an unsharded, all-Q8_0 stage of 128-multiple
+        widths), else 0."""
+        return lib().rk_stage_batched(self.h)
 
     def fill_cache(self, positions, seed):
         _check(lib().rk_stage_fill_cache(self.h, positions, seed))
