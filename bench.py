@@ -64,7 +64,7 @@ def parse():
                    help="--kernel tensor: one MxKxN shape instead of config 2's sweep")
     p.add_argument("--tensor-dtype", default="both", choices=["both", "i8", "f32"])
     p.add_argument("--tensor-op", default="both", choices=["both", "matmul", "matmul_t"])
-    p.add_argument("--kernel", default=None, choices=["matvec", "tensor", "prefill"],
+    p.add_argument("--kernel", default=None, choices=["matvec", "matvec_many", "tensor", "prefill"],
                    help="time one kernel alone instead of the decode step, or a prefill (profiling aids)")
     p.add_argument("--prefill", type=int, default=512, help="--kernel prefill: prompt tokens")
     p.add_argument("--shape", default="28672x4096", help="rows x cols for --kernel matvec")
@@ -90,6 +90,29 @@ def run_kernel(args):
     print(json.dumps({"kernel": f"k_matvec_q<{args.dtype}>", "shape": args.shape, "prologue": args.prologue, "ms": ms,
                       "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
                       "frac": nbytes / (ms * 1e-3) / 1e9 / peak}), flush=True)
+    m.free()
+    dev.close()
+
+
+def run_kernel_many(args):
+    """One batched Q8_0 product of --shape with --prefill input vectors (at
+    most 64, a ForwardMany submission), L2 flushed before each launch. The
+    weights are read once per launch; every (row, vector, block) costs the
+    epilogue four f32 operations."""
+    import rkcuda as rk
+    rows, cols = map(int, args.shape.split("x"))
+    n = args.prefill
+    dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
+    m = rk.Matrix.generate(dev, rows, cols, rk.FMT_Q8_0, SEED, 1, 0.02)
+    m.bench_many(n, max(1, args.warmup))
+    ms = m.bench_many(n, args.steps)
+    nbytes = rows * cols + rows * cols // 32 * 4
+    peak, kind = measured_peak()
+    print(json.dumps({"kernel": "k_mv_many_q8", "shape": args.shape, "vectors": n, "ms": ms,
+                      "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
+                      "frac": nbytes / (ms * 1e-3) / 1e9 / peak,
+                      "int8_tops": 2.0 * rows * cols * n / (ms * 1e-3) / 1e12,
+                      "epilogue_gflops": 4.0 * rows * (cols // 32) * n / (ms * 1e-3) / 1e9}), flush=True)
     m.free()
     dev.close()
 
@@ -288,6 +311,8 @@ def main():
         return run_tensor(args)
     if args.kernel == "prefill":
         return run_prefill(args)
+    if args.kernel == "matvec_many":
+        return run_kernel_many(args)
     if args.kernel:
         return run_kernel(args)
 

@@ -403,6 +403,10 @@ int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, void *q, float
 #define RK_BENCH_FLUSH 1
 #define RK_BENCH_FUSED 2
 int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per_launch);
+/* Mean device time (CUDA events) of one batched product of a Q8_0 matrix
+ * with n seeded input vectors (rk_matrix_mulvec_many's kernel, inputs
+ * already quantized on the device), after one warm-up launch. */
+int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, float *ms_per_launch);
 /* Times `iters` tensor matmuls (rk_tensor_matmul_device) of the given dtype,
  * layout and shape on device buffers this call allocates and fills with
  * hashed values (int8 in [-127, 127], floats in [-1, 1)); returns the mean

@@ -1236,6 +1236,7 @@ struct rk_stage {
   bool many = false;
   float *m_q = nullptr, *m_k = nullptr, *m_v = nullptr, *m_att = nullptr, *m_hb = nullptr, *m_hb2 = nullptr,
         *m_xs = nullptr;
+  float *m_scores = nullptr;  // per-token score rows [io_tokens][heads][att_stride]
   int8_t *m_qx = nullptr;
   int *m_pos = nullptr, *pin_pos = nullptr;
   // Row sharding (layer_dims): this process's rank of G; null/1 unsharded.
@@ -1675,6 +1676,29 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
     return launch_mv_many(a, m->w, m->s, s->m_qx, s->m_xs, d->sms, st);
   };
   float *X = s->io;
+  // When the attention runs batched, every kernel of the submission reads
+  // its predecessor's results only after griddepcontrol.wait, so they are
+  // launched with programmatic dependent launch, as a captured decode step
+  // is: each starts while its predecessor finishes. The token-by-token
+  // attention is launched without it: its fused scores kernel copies key
+  // rows before that wait, which is safe only after the previous token's
+  // kernels have completed.
+  bool batched_attention = false;
+  {
+    QkvPostArgs qp;
+    AttnArgs at;
+    attention_args(s, 0, s->m_q, s->m_k, s->m_v, s->m_att, s->m_pos, &qp, &at);
+    at.att = s->m_scores;
+    at.tok_q = at.tok_out = qd;
+    at.tok_att = (long long)c->heads * s->att_stride;
+    at.max_positions = pos + nt;
+    batched_attention = attention_many_ok(at);
+  }
+  struct PdlScope {
+    bool old;
+    explicit PdlScope(bool on) : old(g_pdl) { g_pdl = on; }
+    ~PdlScope() { g_pdl = old; }
+  } pdl_scope(batched_attention);
   for (size_t li = 0; li < s->layers.size(); li++) {
     const rk_layer *l = s->layers[li];
     const float *vec = l->vecs->v;
@@ -1683,12 +1707,25 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
     CK(product(l->wq, s->m_q, qd, EPI_STORE));
     CK(product(l->wk, s->m_k, kvd, EPI_STORE));
     CK(product(l->wv, s->m_v, kvd, EPI_STORE));
-    for (int t = 0; t < nt; t++) {
-      QkvPostArgs qp;
-      AttnArgs at;
-      attention_args(s, li, s->m_q + (size_t)t * qd, s->m_k + (size_t)t * kvd, s->m_v + (size_t)t * kvd,
-                     s->m_att + (size_t)t * qd, s->m_pos + t, &qp, &at);
-      CK(launch_attention_post(qp, at, st));
+    // Bias, QK-norm, RoPE, cache append and attention (model.go:542-587):
+    // all tokens' appends, then all tokens' attention, in three launches;
+    // shapes the batched kernels do not take go token by token.
+    QkvPostArgs qp;
+    AttnArgs at;
+    attention_args(s, li, s->m_q, s->m_k, s->m_v, s->m_att, s->m_pos, &qp, &at);
+    qp.tok_q = at.tok_q = at.tok_out = qd;
+    qp.tok_kv = kvd;
+    at.att = s->m_scores;
+    at.tok_att = (long long)c->heads * s->att_stride;
+    at.max_positions = pos + nt;
+    if (batched_attention) {
+      CK(launch_attention_many(qp, at, nt, st));
+    } else {
+      for (int t = 0; t < nt; t++) {
+        attention_args(s, li, s->m_q + (size_t)t * qd, s->m_k + (size_t)t * kvd, s->m_v + (size_t)t * kvd,
+                       s->m_att + (size_t)t * qd, s->m_pos + t, &qp, &at);
+        CK(launch_attention_post(qp, at, st));
+      }
     }
     // x += Wo·attOut (model.go:588-594).
     CK(launch_quantize_many(s->m_att, nt, qd, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, st));
@@ -1792,6 +1829,7 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     ALLOC(m_qx, T * widest);
     ALLOC(m_xs, 4 * T * (widest / 32));
     ALLOC(m_pos, 4 * T);
+    ALLOC(m_scores, 4 * T * c->heads * s->att_stride);
     cudaError_t e = cudaMallocHost(&s->pin_pos, 4 * T);
     if (e != cudaSuccess) {
       rc = cuda_fail(e, "stage staging");
@@ -2488,6 +2526,59 @@ extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   if ((rc = check_dev_err(d))) return rc;
+  *ms_per_launch = total / iters;
+  return RK_OK;
+}
+
+extern "C" int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, float *ms_per_launch) {
+  if (!m || n <= 0 || iters <= 0 || !ms_per_launch) return fail(RK_ERR_ARGS, "bad argument");
+  if (m->fmt != RK_FMT_Q8_0 || !mv_many_ok(m->rows, m->cols, m->w, m->s))
+    return fail(RK_ERR_ARGS, "the batched kernel takes Q8_0 matrices of a multiple of 128 columns");
+  rk_device *d = m->d;
+  const int flush = flags & RK_BENCH_FLUSH;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  if (flush && (rc = ensure_flush(d))) return rc;
+  const size_t cols = (size_t)m->cols, rows = (size_t)m->rows;
+  float *dx = nullptr, *dxs = nullptr, *dout = nullptr;
+  int8_t *dqx = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float total = 0.0f;
+  // Seeded inputs, quantized once; then each timed launch is the batched
+  // product alone (L2 flushed first when asked).
+  cudaError_t e = cudaMalloc(&dx, 4 * n * cols);
+  if (e == cudaSuccess) e = cudaMalloc(&dqx, n * cols);
+  if (e == cudaSuccess) e = cudaMalloc(&dxs, 4 * n * (cols / 32));
+  if (e == cudaSuccess) e = cudaMalloc(&dout, 4 * n * rows);
+  if (e == cudaSuccess) e = launch_fill_hash(DT_F32, dx, (long long)(n * cols), 7u, d->st);
+  if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, d->st);
+  if (e == cudaSuccess) e = cudaEventCreate(&e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&e1);
+  MmArgs a{};
+  a.rows = m->rows;
+  a.cols = m->cols;
+  a.ntok = n;
+  a.out = dout;
+  a.out_stride = (long long)rows;
+  a.epi = EPI_STORE;
+  a.err = d->err_dev;
+  for (int i = 0; e == cudaSuccess && i < iters + 1; i++) {
+    if (flush) k_flush_read<<<d->sms * 4, 512, 0, d->st>>>((const int4 *)d->flush, (long long)(d->flush_bytes / 16), d->err_dev + 1);
+    e = cudaEventRecord(e0, d->st);
+    if (e == cudaSuccess) e = launch_mv_many(a, m->w, m->s, dqx, dxs, d->sms, d->st);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, d->st);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (i > 0) total += ms;  // the first launch is a warm-up
+  }
+  rc = e == cudaSuccess ? check_dev_err(d) : cuda_fail(e, "batched matvec bench");
+  cudaStreamSynchronize(d->st);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  for (void *p : {(void *)dx, (void *)dqx, (void *)dxs, (void *)dout}) cudaFree(p);
+  if (rc) return rc;
   *ms_per_launch = total / iters;
   return RK_OK;
 }

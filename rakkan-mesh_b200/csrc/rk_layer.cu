@@ -181,8 +181,14 @@ RK_DEV void head_post(float *v, int hs, const float *bias, const float *nw, cons
 // tile holds the new position (pos = P - 1) post-process the kv head's raw k
 // for that row of the tile; the first group's CTA also appends k and v to
 // the caches (the next kernel reads the value row).
-template <int HS, bool POST>
+//
+// BATCH (launch_attention_many, never with POST): grid.z covers the head
+// groups of every token, token tz = blockIdx.z / groups; its q and scores
+// lie tz·tok_q and tz·tok_att further and its position count is
+// positions_dev[tz] + positions_add.
+template <int HS, bool POST, bool BATCH = false>
 __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int gpb, const QkvPostArgs qp) {
+  static_assert(!(POST && BATCH), "a batched launch post-processes every token first");
   // Key rows HS+4 floats apart: lane p's 16-byte loads of row p then cover
   // all banks in each group of eight lanes.
   constexpr int KP = HS + 4;
@@ -205,11 +211,15 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
   // Without POST (the Batch API appends keys with a kernel of the same
   // submission) everything waits.
   if (!POST) griddep_wait();
-  const int P = attn_positions(a);
+  const int kvh = blockIdx.y, kvMul = a.heads / a.kv_heads;
+  const int zg = BATCH ? (kvMul + gpb - 1) / gpb : 1;
+  const int tz = BATCH ? (int)blockIdx.z / zg : 0, zi = BATCH ? (int)blockIdx.z % zg : (int)blockIdx.z;
+  const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
+  const float *const qbase = BATCH ? a.q + tz * a.tok_q : a.q;
+  float *const att = BATCH ? a.att + tz * a.tok_att : a.att;
   const int t0 = blockIdx.x * kTileT;
   if (t0 >= P) return;
-  const int kvh = blockIdx.y, kvMul = a.heads / a.kv_heads;
-  const int g0 = blockIdx.z * gpb, ng = min(gpb, kvMul - g0);
+  const int g0 = zi * gpb, ng = min(gpb, kvMul - g0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nt = min(kTileT, P - t0);
   // The tile's key rows (contiguous 4·HS-byte runs of the cache) and the
@@ -223,7 +233,7 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
   }
   if (POST) griddep_wait();
   if (warp == 0 && lane == 0)
-    umma::bulk_g2s(umma::smem_u32(sq), a.q + (kvh * kvMul + g0) * HS, (uint32_t)ng * HS * 4u, bar);
+    umma::bulk_g2s(umma::smem_u32(sq), qbase + (kvh * kvMul + g0) * HS, (uint32_t)ng * HS * 4u, bar);
   if (POST) {
     const int pos = P - 1;
     const bool has_new = pos < t0 + nt;
@@ -237,7 +247,7 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
         sco[i] = qp.cos_[(long long)pos * (HS / 2) + i];
         ssi[i] = qp.sin_[(long long)pos * (HS / 2) + i];
       }
-      if (has_new && blockIdx.z == 0)
+      if (has_new && zi == 0)
 #pragma unroll
         for (int u = 0; u < HS / 32; u++) {
           vv[u] = qp.v[kvh * HS + lane + 32 * u];
@@ -255,7 +265,7 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
     if (has_new && post_warp) {
       head_post(snew, HS, qp.bk ? qp.bk + kvh * HS : nullptr, qp.k_norm, sco, ssi, qp.recip_hs, qp.eps);
       for (int i = lane; i < HS; i += 32) sk[(pos - t0) * KP + i] = snew[i];
-      if (blockIdx.z == 0) {
+      if (zi == 0) {
         // The cache append (model.go:567-568).
         const int kvDim = qp.kv_heads * HS;
 #pragma unroll
@@ -302,7 +312,7 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
   }
   const float dot = __fadd_rn(__fadd_rn(__fadd_rn(e8[0], e8[1]), __fadd_rn(e8[2], e8[3])),
                               __fadd_rn(__fadd_rn(e8[4], e8[5]), __fadd_rn(e8[6], e8[7])));
-  if (lane < nt) a.att[(long long)(kvh * kvMul + g0 + warp) * a.att_stride + t0 + lane] = __fmul_rn(dot, a.inv_sqrt);
+  if (lane < nt) att[(long long)(kvh * kvMul + g0 + warp) * a.att_stride + t0 + lane] = __fmul_rn(dot, a.inv_sqrt);
 }
 
 // softmax (model.go:640-654): the maximum in any order (Go's max is order
@@ -562,6 +572,10 @@ static int fs_wph(int gpb) {
 RK_HD int fs_ppad(int maxP) { return ((maxP + 31) & ~31) + 40; }
 RK_HD int fs_vpad(int maxP) { return ((maxP + 31) & ~31) + 4; }
 
+// BATCH (launch_attention_many): grid.z is the token tz, whose scores and
+// output lie tz·tok_att and tz·tok_out further and whose position count is
+// positions_dev[tz] + positions_add.
+template <bool BATCH>
 __global__ void __launch_bounds__(kFsMaxThreads)
     k_attn_softmax_wsum(const AttnArgs a, int gpb, int wph) {
   griddep_trigger();
@@ -587,7 +601,10 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   __syncwarp();
   cluster_arrive_relaxed();
   griddep_wait();
-  const int P = attn_positions(a);
+  const int tz = BATCH ? (int)blockIdx.z : 0;
+  const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
+  const float *const att = BATCH ? a.att + tz * a.tok_att : a.att;
+  float *const out = BATCH ? a.out + tz * a.tok_out : a.out;
   const int P4 = P & ~3;
   // This CTA's chunk [lo, hi) of the positions: whole float4s [lo, hi4),
   // then (last chunk only) the fewer than 4 positions from P4 on.
@@ -600,12 +617,12 @@ __global__ void __launch_bounds__(kFsMaxThreads)
     if (bytes)
       for (int g = 0; g < gpb; g++)
         umma::bulk_g2s(umma::smem_u32(sE + (size_t)g * ppad + lo),
-                       a.att + (long long)(hbase + g) * a.att_stride + lo, bytes, bar);
+                       att + (long long)(hbase + g) * a.att_stride + lo, bytes, bar);
   }
 
   const int g = warp % gpb, sub = warp / gpb;
   float *e = sE + (size_t)g * ppad;
-  const float *x = a.att + (long long)(hbase + g) * a.att_stride;
+  const float *x = att + (long long)(hbase + g) * a.att_stride;
   const bool tail_lane = sub == 0 && hi4 + lane < hi;
   const float tail = tail_lane ? x[hi4 + lane] : 0.0f;
   if (!umma::mbar_wait(bar, 0) && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
@@ -766,7 +783,7 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   }
   for (int t = P32; t < P; t++) acc = __fadd_rn(acc, __fmul_rn(w[t], v[t]));
   const int o = (hbase + h) * a.hs + slice * kFsSlice + d;
-  a.out[o] = acc;
+  out[o] = acc;
   if (a.put.nll > 0) {
     const unsigned tag = gather_tag(*a.put.epoch, a.put.slot, a.put.nslots);
     for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + o, acc, tag);
@@ -850,7 +867,7 @@ static cudaError_t launch_attention_impl(const AttnArgs &a, const QkvPostArgs *q
     if (fused) {
       dim3 g(a.kv_heads, a.hs / kFsSlice);
       const int c = fs_cluster(g);
-      launch_kc(k_attn_softmax_wsum, g, gpb * wph * 32, dim3(1, c, 1), smem, st, a, gpb, wph);
+      launch_kc(k_attn_softmax_wsum<false>, g, gpb * wph * 32, dim3(1, c, 1), smem, st, a, gpb, wph);
       return cudaGetLastError();
     }
   }
@@ -880,7 +897,9 @@ cudaError_t init_layer_attributes() {
   const int smem = sizeof(float) * (kWsStages * kWsT * 32 + kWsStages * kWsMaxGroup * kWsT);
   cudaError_t e = cudaFuncSetAttribute(k_attn_wsum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_attn_softmax_wsum, cudaFuncAttributeMaxDynamicSharedMemorySize, kFsSmemLimit);
+    e = cudaFuncSetAttribute(k_attn_softmax_wsum<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFsSmemLimit);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attn_softmax_wsum<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFsSmemLimit);
   int dev = 0;
   if (e == cudaSuccess) e = cudaGetDevice(&dev);
   if (e == cudaSuccess && dev >= 0 && dev < 64)
@@ -897,7 +916,7 @@ cudaError_t init_layer_attributes() {
       cfg.attrs = &at;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, k_attn_softmax_wsum, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, k_attn_softmax_wsum<false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -915,17 +934,21 @@ __global__ void k_qkv_post(const QkvPostArgs a) {
   griddep_wait();
   const int lane = threadIdx.x;
   const int hs = a.hs, half = hs / 2;
-  const int pos = *a.pos_dev;
+  // grid.y: the token of a batched launch (its rows lie tz·tok_q and
+  // tz·tok_kv further, its position is pos_dev[tz]); 0 otherwise.
+  const int tz = blockIdx.y;
+  const int pos = a.pos_dev[tz];
+  float *const vrow = a.v + tz * a.tok_kv;
   const int kvDim = a.kv_heads * hs;
   const bool isq = blockIdx.x < a.heads;
   const int head = isq ? blockIdx.x : blockIdx.x - a.heads;
-  float *v = (isq ? a.q : a.k) + head * hs;
+  float *v = (isq ? a.q + tz * a.tok_q : a.k + tz * a.tok_kv) + head * hs;
   const float *bias = isq ? a.bq : a.bk;
   // 1. bias (addTo, model.go:543-545).
   if (bias)
     for (int i = lane; i < hs; i += 32) v[i] = __fadd_rn(v[i], bias[head * hs + i]);
   if (!isq && a.bv)
-    for (int i = lane; i < hs; i += 32) a.v[head * hs + i] = __fadd_rn(a.v[head * hs + i], a.bv[head * hs + i]);
+    for (int i = lane; i < hs; i += 32) vrow[head * hs + i] = __fadd_rn(vrow[head * hs + i], a.bv[head * hs + i]);
   __syncwarp();
   // 2. QK-norm (rmsNorm of the head, model.go:547-554).
   const float *nw = isq ? a.q_norm : a.k_norm;
@@ -947,14 +970,47 @@ __global__ void k_qkv_post(const QkvPostArgs a) {
     float *kc = a.key_cache + (long long)pos * kvDim + head * hs;
     for (int i = lane; i < hs; i += 32) {
       kc[i] = v[i];
-      if (a.v_pitch > 0) a.val_cache[(long long)(head * hs + i) * a.v_pitch + pos] = a.v[head * hs + i];
-      else a.val_cache[(long long)pos * kvDim + head * hs + i] = a.v[head * hs + i];
+      if (a.v_pitch > 0) a.val_cache[(long long)(head * hs + i) * a.v_pitch + pos] = vrow[head * hs + i];
+      else a.val_cache[(long long)pos * kvDim + head * hs + i] = vrow[head * hs + i];
     }
   }
 }
 
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st) {
   launch_k(k_qkv_post, a.heads + a.kv_heads, 32, 0, st, a);
+  return cudaGetLastError();
+}
+
+bool attention_many_ok(const AttnArgs &a) {
+  const int kvMul = a.heads / a.kv_heads;
+  const auto a16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  // The tiled scores kernel and the single softmax + value kernel, with
+  // every token's q and score rows 16-byte aligned.
+  return a.positions_dev && scores_tile_ok(a) && kvMul <= 8 && a.hs % kFsSlice == 0 && a.kv_dim % 4 == 0 &&
+         a.att_stride % 4 == 0 && a.err && a.v_pitch > 0 && a.v_pitch % 4 == 0 && a16(a.vals) && a16(a.att) &&
+         a.tok_q % 4 == 0 && a.tok_att % 4 == 0 && fs_smem_bytes(kvMul, fs_wph(kvMul), a.max_positions) > 0;
+}
+
+cudaError_t launch_attention_many(const QkvPostArgs &qp, const AttnArgs &a, int nt, cudaStream_t st) {
+  if (nt <= 0) return cudaSuccess;
+  if (!attention_many_ok(a) || nt > 65535 / 8) return cudaErrorInvalidValue;
+  // 1. Every token's bias, QK-norm, RoPE and cache append: the scores of
+  // token t read the key rows of tokens before it.
+  launch_k(k_qkv_post, dim3(qp.heads + qp.kv_heads, nt), 32, 0, st, qp);
+  // 2. Every token's scores (the tiles past a token's positions exit).
+  const int maxP = a.max_positions, kvMul = a.heads / a.kv_heads;
+  const int gpb = kvMul < 8 ? kvMul : 8, zg = (kvMul + gpb - 1) / gpb;
+  const dim3 g1((maxP + kTileT - 1) / kTileT, a.kv_heads, zg * nt);
+  const int threads = gpb * 32 < 64 ? 64 : gpb * 32;
+  const QkvPostArgs none{};
+  if (a.hs == 64) launch_k(k_attn_scores_tile<64, false, true>, g1, threads, 0, st, a, gpb, none);
+  else launch_k(k_attn_scores_tile<128, false, true>, g1, threads, 0, st, a, gpb, none);
+  // 3. Every token's softmax and weighted values.
+  const int wph = fs_wph(kvMul);
+  const dim3 g(a.kv_heads, a.hs / kFsSlice, nt);
+  const int c = fs_cluster(dim3(g.x * g.z, g.y));  // clusters run along y; every CTA of the grid counts
+  launch_kc(k_attn_softmax_wsum<true>, g, kvMul * wph * 32, dim3(1, c, 1), fs_smem_bytes(kvMul, wph, maxP), st, a,
+            kvMul, wph);
   return cudaGetLastError();
 }
 

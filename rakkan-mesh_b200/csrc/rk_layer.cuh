@@ -45,6 +45,10 @@ struct AttnArgs {
   int heads, kv_heads, hs, kv_dim, att_stride;
   float inv_sqrt;
   int *err;  // device error word for a pipeline wait that timed out
+  // launch_attention_many: token t's q, scores and output lie t·tok_q,
+  // t·tok_att and t·tok_out floats further, and its position count is
+  // positions_dev[t] + positions_add. Unused otherwise.
+  long long tok_q, tok_att, tok_out;
   // Row sharding: the output values also go to every rank's tagged copy
   // (at out's offset), one 8-byte value|tag word each.
   GatherPut put;
@@ -70,12 +74,25 @@ struct QkvPostArgs {
   const int *pos_dev;
   int heads, kv_heads, hs;
   float eps, recip_hs;
+  // launch_attention_many: token t's q and k/v lie t·tok_q and t·tok_kv
+  // floats further and its position is pos_dev[t]. 0 otherwise.
+  long long tok_q, tok_kv;
 };
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st);
 
 // launch_qkv_post then launch_attention for the same position, with the
 // post-processing folded into the scores kernel where it tiles the keys.
 cudaError_t launch_attention_post(const QkvPostArgs &qp, const AttnArgs &a, cudaStream_t st);
+
+// The post-processing and attention of nt consecutive tokens of one
+// sequence (a batched ForwardMany chunk), qp and a describing token 0 with
+// the tok_* strides set: every token's bias / QK-norm / RoPE and cache
+// append first, then every token's scores, then every token's softmax and
+// weighted values, three launches in all. Each token's arithmetic is the
+// single-token kernels'. a.max_positions bounds the largest position count.
+// attention_many_ok tells whether the shapes suit these kernels.
+bool attention_many_ok(const AttnArgs &a);
+cudaError_t launch_attention_many(const QkvPostArgs &qp, const AttnArgs &a, int nt, cudaStream_t st);
 
 // Embed (model.go:660-664): x = dequantized row *token_dev of a table of
 // `rows` rows; a token outside [0, rows) sets DEV_ERR_RANGE in *err instead.

@@ -33,7 +33,7 @@ EXPORTS = [
     "rk_stage_positions", "rk_stage_forward", "rk_stage_batched", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
     "rk_model_new", "rk_model_free", "rk_model_step", "rk_model_generate", "rk_tensor_matmul",
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
-    "rk_bench_matvec", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
+    "rk_bench_matvec", "rk_bench_matvec_many", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
     "rk_group_size", "rk_group_all_gather", "rk_layer_upload_shard", "rk_layer_from_device_shard",
     "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
     "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
@@ -120,7 +120,7 @@ def lib():
             "rk_tensor_matmul_device": (i, [vp, i, i, i, i, i, vp, vp, vp]),
             "rk_matrix_generate": (i, [vp, i, i, i, u64, u64, f, vp]), "rk_matrix_download": (i, [vp, vp, vp]),
             "rk_generate_normal": (i, [vp, u64, u64, i64, i64, f, vp]), "rk_quantize": (i, [vp, i, vp, i64, vp, vp]),
-            "rk_bench_matvec": (i, [vp, i, i, vp]), "rk_bench_model": (i, [vp, i, i, vp]),
+            "rk_bench_matvec": (i, [vp, i, i, vp]), "rk_bench_matvec_many": (i, [vp, i, i, i, vp]), "rk_bench_model": (i, [vp, i, i, vp]),
             "rk_bench_tensor": (i, [vp, i, i, i, i, i, i, i, vp]),
             "rk_group_id": (i, [vp]), "rk_group_new": (i, [vp, i, i, vp, vp]), "rk_group_free": (None, [vp]),
             "rk_group_size": (i, [vp, vp, vp]), "rk_group_all_gather": (i, [vp, vp, i64]),
@@ -255,6 +255,12 @@ class Matrix:
         ms = C.c_float()
         flags = (RK_BENCH_FLUSH if flush else 0) | (RK_BENCH_FUSED if fused else 0)
         _check(lib().rk_bench_matvec(self.h, iters, flags, C.byref(ms)))
+        return ms.value
+
+    def bench_many(self, n, iters=20, flush=True):
+        """Mean kernel time (ms) of one batched product with n vectors."""
+        ms = C.c_float()
+        _check(lib().rk_bench_matvec_many(self.h, n, iters, RK_BENCH_FLUSH if flush else 0, C.byref(ms)))
         return ms.value
 
     def free(self):

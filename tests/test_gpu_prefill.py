@@ -76,6 +76,8 @@ VARIANTS = {
     "mha": dict(kv_heads=4),
     "qwen2": dict(qkv_bias=1, rope_theta=1e6, norm_eps=1e-6),
     "qwen3_hs128": dict(head_dim=128, qk_norm=1, rope_theta=1e6, norm_eps=1e-6),
+    # Head width 32: batched products, attention token by token.
+    "hs32": dict(heads=8, kv_heads=2, head_dim=32),
 }
 
 
@@ -104,6 +106,30 @@ def test_batched_prefill_matches_cpu(dev, variant):
         for t in range(85):
             same_bits(got[t], om.forward(xs[t], t))
         for t in range(85, 90):
+            same_bits(st.forward(xs[t], t), om.forward(xs[t], t))
+    finally:
+        st.free()
+        for l in layers:
+            l.free()
+        om.free()
+    assert dev.used() == 0
+
+
+def test_long_batched_prefill_matches_cpu(dev):
+    """330 tokens in one call (six submissions, the last 10 tokens long):
+    later submissions' attention spans hundreds of cached positions, in the
+    batched attention's clusters, with 7 query heads per kv head."""
+    c = prefill_config(heads=14, kv_heads=2, head_dim=64, dim=256, layers=2, seq_len=400)
+    om = ro.OracleModel(c, seed=23)
+    layers = upload_layers(dev, c, oracle_weights(om, c))
+    st = rk.Stage(dev, c, layers, c.seq_len)
+    try:
+        assert st.batched() == 1
+        xs = np.random.default_rng(29).standard_normal((332, c.dim)).astype(np.float32)
+        got = st.forward(xs[:330].ravel(), 0).reshape(330, c.dim)
+        for t in range(330):
+            same_bits(got[t], om.forward(xs[t], t))
+        for t in range(330, 332):
             same_bits(st.forward(xs[t], t), om.forward(xs[t], t))
     finally:
         st.free()
