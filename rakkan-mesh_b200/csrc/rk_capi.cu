@@ -588,19 +588,21 @@ extern "C" int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const floa
   int rc = set_device(d);
   if (rc) return rc;
   const size_t cols = (size_t)m->cols, rows = (size_t)m->rows;
+  const int xs_pitch = (n + 3) & ~3;  // the batched kernel's block-major input scales
   float *dx = nullptr, *dxs = nullptr, *dout = nullptr;
   int8_t *dqx = nullptr;
   cudaError_t e = cudaMalloc(&dx, 4 * n * cols);
   if (e == cudaSuccess) e = cudaMalloc(&dqx, n * cols);
-  if (e == cudaSuccess) e = cudaMalloc(&dxs, 4 * n * (cols / 32));
+  if (e == cudaSuccess) e = cudaMalloc(&dxs, 4 * (size_t)xs_pitch * (cols / 32));
   if (e == cudaSuccess) e = cudaMalloc(&dout, 4 * n * rows);
   if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, 4 * n * cols, cudaMemcpyHostToDevice, d->st);
-  if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, d->st);
+  if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, xs_pitch, d->st);
   if (e == cudaSuccess) {
     MmArgs a{};
     a.rows = m->rows;
     a.cols = m->cols;
     a.ntok = n;
+    a.xs_pitch = xs_pitch;
     a.out = dout;
     a.out_stride = (long long)rows;
     a.epi = EPI_STORE;
@@ -1669,6 +1671,7 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
     a.rows = m->rows;
     a.cols = m->cols;
     a.ntok = nt;
+    a.xs_pitch = s->io_tokens;
     a.out = out;
     a.out_stride = stride;
     a.epi = epi;
@@ -1703,7 +1706,7 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
     const rk_layer *l = s->layers[li];
     const float *vec = l->vecs->v;
     // q, k, v = Wq·xb, Wk·xb, Wv·xb with xb = rmsNorm(x, RmsAtt) (model.go:538-539).
-    CK(launch_quantize_many(X, nt, D, vec + l->o_rms_att, recipD, eps, s->m_qx, s->m_xs, st));
+    CK(launch_quantize_many(X, nt, D, vec + l->o_rms_att, recipD, eps, s->m_qx, s->m_xs, s->io_tokens, st));
     CK(product(l->wq, s->m_q, qd, EPI_STORE));
     CK(product(l->wk, s->m_k, kvd, EPI_STORE));
     CK(product(l->wv, s->m_v, kvd, EPI_STORE));
@@ -1728,15 +1731,15 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
       }
     }
     // x += Wo·attOut (model.go:588-594).
-    CK(launch_quantize_many(s->m_att, nt, qd, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, st));
+    CK(launch_quantize_many(s->m_att, nt, qd, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, s->io_tokens, st));
     CK(product(l->wo, X, D, EPI_ADD));
     // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603).
-    CK(launch_quantize_many(X, nt, D, vec + l->o_rms_ffn, recipD, eps, s->m_qx, s->m_xs, st));
+    CK(launch_quantize_many(X, nt, D, vec + l->o_rms_ffn, recipD, eps, s->m_qx, s->m_xs, s->io_tokens, st));
     CK(product(l->w1, s->m_hb, H, EPI_STORE));
     CK(product(l->w3, s->m_hb2, H, EPI_STORE));
     CK(launch_silu_mul_many(s->m_hb, s->m_hb2, (long long)nt * H, d->sms, st));
     // x = Canonical(x + W2·hb) (model.go:604-610).
-    CK(launch_quantize_many(s->m_hb, nt, H, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, st));
+    CK(launch_quantize_many(s->m_hb, nt, H, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, s->io_tokens, st));
     CK(product(l->w2, X, D, EPI_ADD_CANON));
   }
   return RK_OK;
@@ -2541,6 +2544,7 @@ extern "C" int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, f
   if (rc) return rc;
   if (flush && (rc = ensure_flush(d))) return rc;
   const size_t cols = (size_t)m->cols, rows = (size_t)m->rows;
+  const int xs_pitch = (n + 3) & ~3;  // the batched kernel's block-major input scales
   float *dx = nullptr, *dxs = nullptr, *dout = nullptr;
   int8_t *dqx = nullptr;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
@@ -2549,16 +2553,17 @@ extern "C" int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, f
   // product alone (L2 flushed first when asked).
   cudaError_t e = cudaMalloc(&dx, 4 * n * cols);
   if (e == cudaSuccess) e = cudaMalloc(&dqx, n * cols);
-  if (e == cudaSuccess) e = cudaMalloc(&dxs, 4 * n * (cols / 32));
+  if (e == cudaSuccess) e = cudaMalloc(&dxs, 4 * (size_t)xs_pitch * (cols / 32));
   if (e == cudaSuccess) e = cudaMalloc(&dout, 4 * n * rows);
   if (e == cudaSuccess) e = launch_fill_hash(DT_F32, dx, (long long)(n * cols), 7u, d->st);
-  if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, d->st);
+  if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, xs_pitch, d->st);
   if (e == cudaSuccess) e = cudaEventCreate(&e0);
   if (e == cudaSuccess) e = cudaEventCreate(&e1);
   MmArgs a{};
   a.rows = m->rows;
   a.cols = m->cols;
   a.ntok = n;
+  a.xs_pitch = xs_pitch;
   a.out = dout;
   a.out_stride = (long long)rows;
   a.epi = EPI_STORE;

@@ -70,10 +70,12 @@ RK_DEV void stage_load(const float *__restrict__ x, const float *__restrict__ w,
 // publishes the chunk).
 RK_DEV void stage_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <bool NORM>
+// PITCHED: block b's scale goes to xs[b·xs_pitch] (a block-major scale
+// array shared by many vectors) instead of xs[b].
+template <bool NORM, bool PITCHED = false>
 RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__restrict__ w, float recipN, float eps,
                            int8_t *qx, float *xs, int *xsum, float *s_inv, float *stage, float *wstage,
-                           int stage_floats, bool preloaded) {
+                           int stage_floats, bool preloaded, int xs_pitch = 1) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool single = n <= stage_floats;
   float inv = 0.0f;
@@ -175,7 +177,7 @@ RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__re
       sum += __shfl_xor_sync(qmask, sum, 1);
       sum += __shfl_xor_sync(qmask, sum, 2);
       if (sub == 0) {
-        xs[b] = d;
+        xs[PITCHED ? (size_t)b * xs_pitch : (size_t)b] = d;
         if (xsum) xsum[b] = sum;
       }
     }
@@ -207,28 +209,30 @@ cudaError_t launch_quantize_act(const float *x, int n, const float *w, float rec
 
 // quantize8 (after rmsNorm when w is given) of each of n rows of x
 // ([n][cols]), a CTA per row: ForwardMany's token-by-token prologue of a
-// batched product. qx is [n][cols], xs [n][cols/32].
+// batched product. qx is [n][cols]; the scales are block-major, row t's
+// block b at xs[b·xs_pitch + t].
 template <bool NORM>
 __global__ void __launch_bounds__(512) k_quantize_many(const float *__restrict__ x, int cols,
                                                        const float *__restrict__ w, float recipN, float eps,
-                                                       int8_t *__restrict__ qx, float *__restrict__ xs) {
+                                                       int8_t *__restrict__ qx, float *__restrict__ xs,
+                                                       int xs_pitch) {
   __shared__ float s_inv;
   __shared__ __align__(16) float stage[kQuantStage];
   __shared__ __align__(16) float wstage[NORM ? kQuantStage : 4];
   griddep_trigger();
   griddep_wait();
   const size_t t = blockIdx.x;
-  quantize_warps<NORM>(x + t * cols, cols, w, recipN, eps, qx + t * cols, xs + t * (cols / 32), nullptr, &s_inv,
-                       stage, wstage, kQuantStage, false);
+  quantize_warps<NORM, true>(x + t * cols, cols, w, recipN, eps, qx + t * cols, xs + t, nullptr, &s_inv, stage,
+                             wstage, kQuantStage, false, xs_pitch);
 }
 
 cudaError_t launch_quantize_many(const float *x, int n, int cols, const float *w, float recipN, float eps,
-                                 int8_t *qx, float *xs, cudaStream_t st) {
+                                 int8_t *qx, float *xs, int xs_pitch, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  if (cols <= 0 || cols % 32) return cudaErrorInvalidValue;
+  if (cols <= 0 || cols % 32 || xs_pitch < n) return cudaErrorInvalidValue;
   const int threads = cols >= 16 * 32 ? 512 : (cols / 32) * 32;
-  if (w) return launch_k(k_quantize_many<true>, n, threads, 0, st, x, cols, w, recipN, eps, qx, xs);
-  return launch_k(k_quantize_many<false>, n, threads, 0, st, x, cols, w, recipN, eps, qx, xs);
+  if (w) return launch_k(k_quantize_many<true>, n, threads, 0, st, x, cols, w, recipN, eps, qx, xs, xs_pitch);
+  return launch_k(k_quantize_many<false>, n, threads, 0, st, x, cols, w, recipN, eps, qx, xs, xs_pitch);
 }
 
 // ---------------------------------------------------------------------------

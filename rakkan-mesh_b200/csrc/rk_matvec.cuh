@@ -110,6 +110,7 @@ cudaError_t init_matvec_attributes();
 // the tcgen05 tensor cores; bits identical to the single-vector kernel. ----
 struct MmArgs {
   int rows, cols, ntok;
+  int xs_pitch;           // the input scales are block-major: token t's block b at xs[b·xs_pitch + t]
   float *out;             // token t's row r at out[t·out_stride + r]
   long long out_stride;
   int epi;                // EPI_STORE, EPI_ADD or EPI_ADD_CANON
@@ -121,14 +122,16 @@ struct MmArgs {
 bool mv_many_ok(int rows, int cols, const void *w, const float *ws);
 
 // out = W·x_t for the ntok tokens whose Q8_0 inputs are qx [ntok][cols]
-// and xs [ntok][cols/32] (16-byte aligned device buffers).
+// and xs [cols/32][xs_pitch] (16-byte aligned device buffers; xs_pitch a
+// multiple of 4, at least ntok).
 cudaError_t launch_mv_many(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx, const float *xs,
                            int num_sms, cudaStream_t st);
 
 // quantize8 of each of n rows of x [n][cols] (after rmsNorm with w when w
-// is given): qx [n][cols], xs [n][cols/32].
+// is given): qx [n][cols], and the scales block-major, xs [cols/32][xs_pitch]
+// with xs_pitch >= n.
 cudaError_t launch_quantize_many(const float *x, int n, int cols, const float *w, float recipN, float eps,
-                                 int8_t *qx, float *xs, cudaStream_t st);
+                                 int8_t *qx, float *xs, int xs_pitch, cudaStream_t st);
 
 // hb[i] = silu(hb[i])·hb2[i] (model.go:601-603) for i < n.
 cudaError_t launch_silu_mul_many(float *hb, const float *hb2, long long n, int num_sms, cudaStream_t st);

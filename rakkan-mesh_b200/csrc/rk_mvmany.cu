@@ -42,7 +42,7 @@ struct MmCfg {
   static constexpr int kW = 128 * 128;    // weight tile bytes
   static constexpr int kX = NT * 128;     // token tile bytes
   static constexpr int kWs = 128 * 16;    // weight scales: 128 rows × 4 blocks
-  static constexpr int kXs = NT * 16;     // token scales: NT tokens × 4 blocks
+  static constexpr int kXs = NT * 16;     // token scales: 4 blocks × NT tokens (block-major)
   static constexpr int kTx = kW + kX + kWs + kXs;
   static constexpr int kStage = (kTx + 1023) / 1024 * 1024;
   static constexpr int kSmem = kMmStages * kStage + 1024;  // + slack to align the ring to 1024 bytes
@@ -50,21 +50,27 @@ struct MmCfg {
 };
 
 // Blocks K0..K0+NK-1 of a stage for this thread's row and eight tokens,
-// into chains 4·HALF + kk (a stage starts at block 4i, so even stages feed
-// chains 0-3 and odd stages chains 4-7). v[kk][j]: the block sums of token
-// j; ws: the row's four weight scales; xs: the eight tokens' four input
-// scales each, in shared memory.
-template <int HALF, int K0, int NK>
-RK_DEV void mm_terms(float (&acc)[8][8], const int32_t (&v)[NK][8], float4 ws, const float4 *xs) {
+// into chains 4·HALF + block (a stage starts at block 4i, so even stages
+// feed chains 0-3 and odd stages chains 4-7). v[kk][j]: the block sums of
+// token j; ws: the row's four weight scales; xs: the stage's input scales
+// in shared memory, block-major ([4][NT]), at this thread's first token.
+// Per (row, token, block): term = float32(sum)·(ws·xs), chain += term, as
+// qrow. (sm_100's packed f32x2 multiply and add were tried here: they did
+// not reproduce these scalar operations' bits on every input, so the
+// epilogue stays scalar.)
+template <int NT, int HALF, int K0, int NK>
+RK_DEV void mm_terms(float (&acc)[8][8], const int32_t (&v)[NK][8], float4 ws, const float *xs) {
   const float w4[4] = {ws.x, ws.y, ws.z, ws.w};
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const float4 x4 = xs[j];
-    const float xj[4] = {x4.x, x4.y, x4.z, x4.w};
+  for (int kk = 0; kk < NK; kk++) {
+    const int b = K0 + kk;
+    const float4 xa = *reinterpret_cast<const float4 *>(xs + b * NT);
+    const float4 xb = *reinterpret_cast<const float4 *>(xs + b * NT + 4);
+    const float x8[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-    for (int kk = 0; kk < NK; kk++) {
-      const float term = __fmul_rn(__int2float_rn(v[kk][j]), __fmul_rn(w4[K0 + kk], xj[K0 + kk]));
-      acc[j][4 * HALF + K0 + kk] = __fadd_rn(acc[j][4 * HALF + K0 + kk], term);
+    for (int j = 0; j < 8; j++) {
+      const float term = __fmul_rn(__int2float_rn(v[kk][j]), __fmul_rn(w4[b], x8[j]));
+      acc[j][4 * HALF + b] = __fadd_rn(acc[j][4 * HALF + b], term);
     }
   }
 }
@@ -128,7 +134,7 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
         umma::tma_load_2d(st, &tmW, i * 128, r0, full(s));
         umma::tma_load_2d(st + C::kW, &tmX, i * 128, t0, full(s));
         umma::tma_load_2d(st + C::kW + C::kX, &tmWs, i * 4, r0, full(s));
-        umma::tma_load_2d(st + C::kW + C::kX + C::kWs, &tmXs, i * 4, t0, full(s));
+        umma::tma_load_2d(st + C::kW + C::kX + C::kWs, &tmXs, t0, i * 4, full(s));
         issued = i + 1;
       }
       // Copies still in flight land before the CTA exits (bounded).
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
     const int q = warp & 3, tk0 = 8 * (warp >> 2);
     const int row = r0 + 32 * q + lane;
     const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)tk0;
-    float acc[8][8];
+    float acc[8][8];  // [token][chain], from +0
 #pragma unroll
     for (int j = 0; j < 8; j++)
 #pragma unroll
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
       umma::fence_after_sync();
       const uint8_t *sp = ring_p + s * C::kStage;
       const float4 ws = *reinterpret_cast<const float4 *>(sp + C::kW + C::kX + 16 * (32 * q + lane));
-      const float4 *xs = reinterpret_cast<const float4 *>(sp + C::kW + C::kX + C::kWs) + tk0;
+      const float *xs = reinterpret_cast<const float *>(sp + C::kW + C::kX + C::kWs) + tk0;
       constexpr int H = decltype(half)::value;
       const uint32_t tg = tl + (uint32_t)(g * 4 * NT);
       if constexpr (NT <= 16) {  // all four blocks' sums at once
@@ -186,20 +192,20 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
         umma::fence_before_sync();
         __syncwarp();
         if (lane == 0) umma::mbar_arrive(acce(g));
-        mm_terms<H, 0, 4>(acc, v, ws, xs);
+        mm_terms<NT, H, 0, 4>(acc, v, ws, xs);
       } else {  // two blocks at a time (the wider CTA has fewer registers per thread)
         int32_t v[2][8];
         umma::tmem_ld8(tg, v[0]);
         umma::tmem_ld8(tg + (uint32_t)NT, v[1]);
         umma::tmem_ld_wait();
-        mm_terms<H, 0, 2>(acc, v, ws, xs);
+        mm_terms<NT, H, 0, 2>(acc, v, ws, xs);
         umma::tmem_ld8(tg + (uint32_t)(2 * NT), v[0]);
         umma::tmem_ld8(tg + (uint32_t)(3 * NT), v[1]);
         umma::tmem_ld_wait();
         umma::fence_before_sync();
         __syncwarp();
         if (lane == 0) umma::mbar_arrive(acce(g));
-        mm_terms<H, 2, 2>(acc, v, ws, xs);
+        mm_terms<NT, H, 2, 2>(acc, v, ws, xs);
       }
       __syncwarp();
       if (lane == 0) umma::mbar_arrive(empty(s));
@@ -218,13 +224,13 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
         if (t >= a.ntok) break;
         const float r = __fadd_rn(__fadd_rn(__fadd_rn(acc[j][0], acc[j][1]), __fadd_rn(acc[j][2], acc[j][3])),
                                   __fadd_rn(__fadd_rn(acc[j][4], acc[j][5]), __fadd_rn(acc[j][6], acc[j][7])));
-        float *p = a.out + (size_t)t * a.out_stride + row;
+        float *o = a.out + (size_t)t * a.out_stride + row;
         if (a.epi == EPI_ADD)
-          *p = __fadd_rn(*p, r);
+          *o = __fadd_rn(*o, r);
         else if (a.epi == EPI_ADD_CANON)
-          *p = canonical(__fadd_rn(*p, r));
+          *o = canonical(__fadd_rn(*o, r));
         else
-          *p = r;
+          *o = r;
       }
     }
   }
@@ -274,7 +280,8 @@ static cudaError_t launch_mm_nt(const MmArgs &a, const uint8_t *w, const float *
                NT, true) ||
       !tmap_2d(&tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, (uint64_t)nb, (uint64_t)a.rows, 4ull * nb, 4, 128,
                false) ||
-      !tmap_2d(&tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)nb, (uint64_t)a.ntok, 4ull * nb, 4, NT, false))
+      !tmap_2d(&tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)a.xs_pitch, (uint64_t)nb, 4ull * a.xs_pitch, NT,
+               4, false))
     return cudaErrorInvalidValue;
   const dim3 grid((unsigned)((a.ntok + NT - 1) / NT), (unsigned)((a.rows + 127) / 128));
   return launch_k(k_mv_many_q8<NT>, grid, MmCfg<NT>::kThreads, MmCfg<NT>::kSmem, st, tmW, tmX, tmWs, tmXs, a);
@@ -283,7 +290,8 @@ static cudaError_t launch_mm_nt(const MmArgs &a, const uint8_t *w, const float *
 cudaError_t launch_mv_many(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx, const float *xs,
                            int num_sms, cudaStream_t st) {
   if (a.ntok <= 0) return cudaSuccess;
-  if (!mv_many_ok(a.rows, a.cols, w, ws) || ((uintptr_t)qx & 15) || ((uintptr_t)xs & 15))
+  if (!mv_many_ok(a.rows, a.cols, w, ws) || ((uintptr_t)qx & 15) || ((uintptr_t)xs & 15) || a.xs_pitch % 4 ||
+      a.xs_pitch < a.ntok)
     return cudaErrorInvalidValue;
   const long long row_tiles = (a.rows + 127) / 128;
   // 32 tokens per CTA halve the weight tiles' re-reads from L2 once the
