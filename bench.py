@@ -64,7 +64,8 @@ def parse():
                    help="--kernel tensor: one MxKxN shape instead of config 2's sweep")
     p.add_argument("--tensor-dtype", default="both", choices=["both", "i8", "f32"])
     p.add_argument("--tensor-op", default="both", choices=["both", "matmul", "matmul_t"])
-    p.add_argument("--kernel", default=None, choices=["matvec", "matvec_many", "tensor", "prefill"],
+    p.add_argument("--batch", type=int, default=32, help="--kernel decode_batch: sequences decoded together")
+    p.add_argument("--kernel", default=None, choices=["matvec", "matvec_many", "tensor", "prefill", "decode_batch"],
                    help="time one kernel alone instead of the decode step, or a prefill (profiling aids)")
     p.add_argument("--prefill", type=int, default=512, help="--kernel prefill: prompt tokens")
     p.add_argument("--shape", default="28672x4096", help="rows x cols for --kernel matvec")
@@ -91,6 +92,38 @@ def run_kernel(args):
                       "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
                       "frac": nbytes / (ms * 1e-3) / 1e9 / peak}), flush=True)
     m.free()
+    dev.close()
+
+
+def run_decode_batch(args):
+    """Config 4's batch-32 decode: --batch sequences, each with a --ctx-token
+    cache (seeded values, as the headline's), one decode step of all of them
+    per call through the public stage API (activations in from host memory
+    and back, timed on the host). The stage's layers only: no embedding
+    lookup or classifier."""
+    import numpy as np
+    import rkcuda as rk
+    import synth
+    dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
+    n = args.batch
+    c = synth.config(args.model, args.dtype, seq_len=args.ctx + 64)
+    dm = synth.DeviceModel(dev, c, SEED, ctx=args.ctx + 64, nseq=n)
+    dm.stage.fill_cache(args.ctx, SEED)
+    xs = np.random.default_rng(SEED).standard_normal((n, c.dim)).astype(np.float32)
+    pos = [args.ctx] * n
+    for _ in range(max(3, args.warmup)):
+        dm.stage.forward_batch(xs, pos)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        dm.stage.forward_batch(xs, pos)
+        times.append(time.perf_counter() - t0)
+    ms = 1000.0 * statistics.median(times)
+    print(json.dumps({"kernel": "decode_batch", "model": args.model, "dtype": args.dtype, "batch": n,
+                      "context": args.ctx, "ms_per_step": ms, "tok_s": n * 1000.0 / ms, "steps": args.steps,
+                      "scope": "the stage's layers (no embedding or classifier), host buffers in and out"}),
+          flush=True)
+    dm.free()
     dev.close()
 
 
@@ -313,6 +346,8 @@ def main():
         return run_prefill(args)
     if args.kernel == "matvec_many":
         return run_kernel_many(args)
+    if args.kernel == "decode_batch":
+        return run_decode_batch(args)
     if args.kernel:
         return run_kernel(args)
 

@@ -216,6 +216,20 @@ int rk_stage_positions(const rk_stage *s);                                      
 int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens);
 /* 1 when rk_stage_forward runs this stage's products batched, else 0. */
 int rk_stage_batched(const rk_stage *s);
+/* Batched decode: a stage holding the caches of nseq (at most 64)
+ * independent sequences, each as NewStage's (model.go:466-484) would. The
+ * reference's Stage holds one sequence and has no batched step; each
+ * sequence's results here are what its own Stage.Forward (model.go:522-613)
+ * computes, bit for bit. Needs what the batched prefill needs (unsharded,
+ * every matrix Q8_0, widths multiples of 128) and head width 64 or 128.
+ * rk_stage_forward, rk_stage_fill_cache and the decode graph act on
+ * sequence 0 (rk_stage_fill_cache fills every sequence's caches alike). */
+int rk_stage_new_batch(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, int nseq,
+                       rk_stage **out);
+/* One decode step of sequences 0..nseq-1: xs[nseq][dim] in place, sequence
+ * q's token at positions[q]. The products run once for all of them on the
+ * tensor cores; each sequence attends over its own cache. */
+int rk_stage_forward_batch(rk_stage *s, float *xs, const int *positions, int nseq);
 /* Head (model.go:413-417) from an uploaded classifier (not owned). */
 int rk_head_new(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_head **out);
 void rk_head_free(rk_head *h);

@@ -1236,6 +1236,11 @@ struct rk_stage {
   // takes the batched kernel: per-token rows of q, k, v, attOut, hb, hb2
   // (io_tokens each), the tokens' Q8_0 inputs, and their positions.
   bool many = false;
+  // Independent sequences whose caches the stage holds (a batched decode
+  // step, rk_stage_forward_batch): layer l's keys of sequence q start at
+  // keys[l] + q·ctx·kvd, its values at vals[l] + q·kvd·v_pitch. Everything
+  // else (rk_stage_forward, the decode graph, the Batch API) uses sequence 0.
+  int nseq = 1;
   float *m_q = nullptr, *m_k = nullptr, *m_v = nullptr, *m_att = nullptr, *m_hb = nullptr, *m_hb2 = nullptr,
         *m_xs = nullptr;
   float *m_scores = nullptr;  // per-token score rows [io_tokens][heads][att_stride]
@@ -1651,6 +1656,25 @@ static bool stage_many_ok(const rk_stage *s) {
   return true;
 }
 
+// The batched attention's arguments for layer li, token 0 of a submission
+// (per-token strides set). per_seq: token t belongs to sequence t (its own
+// caches), else all tokens are one sequence's consecutive positions.
+static void attention_many_args(const rk_stage *s, size_t li, bool per_seq, int max_positions, QkvPostArgs *qp,
+                                AttnArgs *at) {
+  const rk_config *c = &s->c;
+  const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs;
+  attention_args(s, li, s->m_q, s->m_k, s->m_v, s->m_att, s->m_pos, qp, at);
+  qp->tok_q = at->tok_q = at->tok_out = qd;
+  qp->tok_kv = kvd;
+  at->att = s->m_scores;
+  at->tok_att = (long long)c->heads * s->att_stride;
+  at->max_positions = max_positions;
+  if (per_seq) {
+    qp->tok_keys = at->tok_keys = (long long)s->ctx * kvd;
+    qp->tok_vals = at->tok_vals = (long long)kvd * (s->v_pitch > 0 ? s->v_pitch : s->ctx);
+  }
+}
+
 // Stage.ForwardMany (model.go:504-518) for the nt tokens in s->io at
 // positions pos.., layer by layer. Each projection runs once for all nt
 // tokens on the tensor cores (launch_mv_many); the bias / QK-norm / RoPE /
@@ -1658,13 +1682,22 @@ static bool stage_many_ok(const rk_stage *s) {
 // so token t's attention reads the cache rows appended before it, as the
 // reference's token-by-token Forward does. Every element is computed by the
 // same operations in the same order as in Forward.
-static int stage_forward_many(rk_stage *s, int pos, int nt) {
+//
+// per_seq (a batched decode step, rk_stage_forward_batch): token t is the
+// next token of sequence t, at position positions[t], with its own caches;
+// every token's arithmetic is still the reference's Forward for that
+// sequence.
+static int stage_forward_many(rk_stage *s, const int *positions, int nt, bool per_seq) {
   rk_device *d = s->d;
   const rk_config *c = &s->c;
   cudaStream_t st = d->st;
   const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
   const float eps = cfg_eps(c), recipD = host_recip32((float)D);
-  for (int t = 0; t < nt; t++) s->pin_pos[t] = pos + t;
+  int max_pos = 0;
+  for (int t = 0; t < nt; t++) {
+    s->pin_pos[t] = positions[t];
+    max_pos = std::max(max_pos, positions[t] + 1);
+  }
   CK(cudaMemcpyAsync(s->m_pos, s->pin_pos, sizeof(int) * nt, cudaMemcpyHostToDevice, st));
   const auto product = [&](const rk_matrix *m, float *out, long long stride, int epi) {
     MmArgs a{};
@@ -1690,13 +1723,10 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
   {
     QkvPostArgs qp;
     AttnArgs at;
-    attention_args(s, 0, s->m_q, s->m_k, s->m_v, s->m_att, s->m_pos, &qp, &at);
-    at.att = s->m_scores;
-    at.tok_q = at.tok_out = qd;
-    at.tok_att = (long long)c->heads * s->att_stride;
-    at.max_positions = pos + nt;
+    attention_many_args(s, 0, per_seq, max_pos, &qp, &at);
     batched_attention = attention_many_ok(at);
   }
+  if (per_seq && !batched_attention) return fail(RK_ERR_ARGS, "batched decode needs the batched attention kernels");
   struct PdlScope {
     bool old;
     explicit PdlScope(bool on) : old(g_pdl) { g_pdl = on; }
@@ -1715,12 +1745,7 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
     // shapes the batched kernels do not take go token by token.
     QkvPostArgs qp;
     AttnArgs at;
-    attention_args(s, li, s->m_q, s->m_k, s->m_v, s->m_att, s->m_pos, &qp, &at);
-    qp.tok_q = at.tok_q = at.tok_out = qd;
-    qp.tok_kv = kvd;
-    at.att = s->m_scores;
-    at.tok_att = (long long)c->heads * s->att_stride;
-    at.max_positions = pos + nt;
+    attention_many_args(s, li, per_seq, max_pos, &qp, &at);
     if (batched_attention) {
       CK(launch_attention_many(qp, at, nt, st));
     } else {
@@ -1746,7 +1771,7 @@ static int stage_forward_many(rk_stage *s, int pos, int nt) {
 }
 
 static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, rk_group *grp,
-                     rk_stage **out) {
+                     rk_stage **out, int nseq = 1) {
   if (!d || !c || !out || n < 0 || (n > 0 && !layers) || ctx <= 0) return fail(RK_ERR_ARGS, "bad argument");
   int rc = rk_config_validate(c);
   if (rc) return rc;
@@ -1771,6 +1796,7 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
   s->grp = grp;
   s->G = G;
   s->rank = rank;
+  s->nseq = nseq;
   const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs / G, D = c->dim, H = c->hidden;
   const int widest = std::max(D, std::max(qd, H));
   void *p;
@@ -1815,9 +1841,9 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
   ALLOC(pos_dev, 4);
   ALLOC(tok_dev, 4);
   for (int i = 0; i < n; i++) {
-    if ((rc = A(4 * (size_t)ctx * kvd, &p))) goto fail_;
+    if ((rc = A(4 * (size_t)nseq * ctx * kvd, &p))) goto fail_;
     s->keys.push_back((float *)p);
-    if ((rc = A(4 * (size_t)(s->v_pitch > 0 ? s->v_pitch : ctx) * kvd, &p))) goto fail_;
+    if ((rc = A(4 * (size_t)nseq * (s->v_pitch > 0 ? s->v_pitch : ctx) * kvd, &p))) goto fail_;
     s->vals.push_back((float *)p);
   }
   s->many = stage_many_ok(s);
@@ -1836,6 +1862,17 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     cudaError_t e = cudaMallocHost(&s->pin_pos, 4 * T);
     if (e != cudaSuccess) {
       rc = cuda_fail(e, "stage staging");
+      goto fail_;
+    }
+  }
+  if (nseq > 1) {
+    QkvPostArgs qp;
+    AttnArgs at;
+    if (nseq > s->io_tokens || !s->many || (attention_many_args(s, 0, true, ctx, &qp, &at), !attention_many_ok(at))) {
+      rc = fail(RK_ERR_ARGS,
+                "a stage of %d sequences needs at most %d of them, an unsharded all-Q8_0 stage whose widths are "
+                "multiples of 128, and head width 64 or 128",
+                nseq, s->io_tokens);
       goto fail_;
     }
   }
@@ -1903,6 +1940,34 @@ extern "C" int rk_stage_positions(const rk_stage *s) { return s ? s->ctx : 0; }
 
 extern "C" int rk_stage_batched(const rk_stage *s) { return s && s->many ? 1 : 0; }
 
+extern "C" int rk_stage_new_batch(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, int nseq,
+                                  rk_stage **out) {
+  if (nseq < 1) return fail(RK_ERR_ARGS, "bad sequence count %d", nseq);
+  return stage_new(d, c, layers, n, ctx, nullptr, out, nseq);
+}
+
+extern "C" int rk_stage_forward_batch(rk_stage *s, float *xs, const int *positions, int nseq) {
+  if (!s || nseq < 0 || (nseq > 0 && (!xs || !positions))) return fail(RK_ERR_ARGS, "bad argument");
+  if (nseq > s->nseq) return fail(RK_ERR_ARGS, "%d sequences on a stage of %d", nseq, s->nseq);
+  if (nseq == 0) return RK_OK;
+  for (int q = 0; q < nseq; q++)
+    if (positions[q] < 0 || positions[q] >= s->ctx)
+      return fail(RK_ERR_ARGS, "position %d of sequence %d outside the stage's %d", positions[q], q, s->ctx);
+  if (s->nseq == 1) return rk_stage_forward(s, xs, positions[0], 1);
+  rk_device *d = s->d;
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  const size_t bytes = sizeof(float) * (size_t)nseq * s->c.dim;
+  memcpy(s->pin_io, xs, bytes);
+  CK(cudaMemcpyAsync(s->io, s->pin_io, bytes, cudaMemcpyHostToDevice, d->st));
+  if ((rc = stage_forward_many(s, positions, nseq, true))) return rc;
+  CK(cudaMemcpyAsync(s->pin_io, s->io, bytes, cudaMemcpyDeviceToHost, d->st));
+  if ((rc = sync_dev(d))) return rc;
+  memcpy(xs, s->pin_io, bytes);
+  return RK_OK;
+}
+
 extern "C" int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens) {
   if (!s || (tokens > 0 && !xs) || tokens < 0) return fail(RK_ERR_ARGS, "bad argument");
   if (pos < 0 || pos + tokens > s->ctx) return fail(RK_ERR_ARGS, "positions [%d, %d) outside the stage's %d", pos, pos + tokens, s->ctx);
@@ -1916,7 +1981,9 @@ extern "C" int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens) {
     memcpy(s->pin_io, xs + (size_t)start * D, sizeof(float) * (size_t)nt * D);
     CK(cudaMemcpyAsync(s->io, s->pin_io, sizeof(float) * (size_t)nt * D, cudaMemcpyHostToDevice, d->st));
     if (s->many && nt > 1) {
-      if ((rc = stage_forward_many(s, pos + start, nt))) return rc;
+      int positions[64];
+      for (int t = 0; t < nt; t++) positions[t] = pos + start + t;
+      if ((rc = stage_forward_many(s, positions, nt, false))) return rc;
     } else {
       const int hdr[2] = {0, pos + start};
       CK(cudaMemcpyAsync(s->tok_dev, &hdr[0], sizeof(int), cudaMemcpyHostToDevice, d->st));
@@ -2715,14 +2782,18 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
   // Position t's cache row is elements [t·kvd, …) of the layer's stream;
   // this rank holds columns [c0, c0 + kvd_l) (its kv heads).
   const int kvd = s->c.kv_heads * head_size(&s->c), kvd_l = kvd / s->G, c0 = s->rank * kvd_l;
-  for (size_t l = 0; l < s->layers.size(); l++) {
-    CK(launch_gen_normal_2d(seed, 0xA0000ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, s->keys[l], d->st));
-    if (s->v_pitch > 0)
-      CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, 1, s->v_pitch, 1.0f, s->vals[l],
-                              d->st));
-    else
-      CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, s->vals[l], d->st));
-  }
+  // A stage of several sequences gets the same rows in every sequence's caches.
+  const size_t kstride = (size_t)s->ctx * kvd_l, vstride = (size_t)kvd_l * (s->v_pitch > 0 ? s->v_pitch : s->ctx);
+  for (int q = 0; q < s->nseq; q++)
+    for (size_t l = 0; l < s->layers.size(); l++) {
+      float *keys = s->keys[l] + q * kstride, *vals = s->vals[l] + q * vstride;
+      CK(launch_gen_normal_2d(seed, 0xA0000ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, keys, d->st));
+      if (s->v_pitch > 0)
+        CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, 1, s->v_pitch, 1.0f, vals,
+                                d->st));
+      else
+        CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, vals, d->st));
+    }
   return sync_dev(d);
 }
 

@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
   const int tz = BATCH ? (int)blockIdx.z / zg : 0, zi = BATCH ? (int)blockIdx.z % zg : (int)blockIdx.z;
   const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
   const float *const qbase = BATCH ? a.q + tz * a.tok_q : a.q;
+  const float *const keys = BATCH ? a.keys + tz * a.tok_keys : a.keys;
   float *const att = BATCH ? a.att + tz * a.tok_att : a.att;
   const int t0 = blockIdx.x * kTileT;
   if (t0 >= P) return;
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
     if (lane == 0) umma::mbar_expect_tx(bar, (uint32_t)(nt + ng) * HS * 4u);
     __syncwarp();
     if (lane < nt)
-      umma::bulk_g2s(umma::smem_u32(sk + lane * KP), a.keys + (long long)(t0 + lane) * a.kv_dim + kvh * HS, HS * 4u,
+      umma::bulk_g2s(umma::smem_u32(sk + lane * KP), keys + (long long)(t0 + lane) * a.kv_dim + kvh * HS, HS * 4u,
                      bar);
   }
   if (POST) griddep_wait();
@@ -605,6 +606,7 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
   const float *const att = BATCH ? a.att + tz * a.tok_att : a.att;
   float *const out = BATCH ? a.out + tz * a.tok_out : a.out;
+  const float *const vals = BATCH ? a.vals + tz * a.tok_vals : a.vals;
   const int P4 = P & ~3;
   // This CTA's chunk [lo, hi) of the positions: whole float4s [lo, hi4),
   // then (last chunk only) the fewer than 4 positions from P4 on.
@@ -688,14 +690,14 @@ __global__ void __launch_bounds__(kFsMaxThreads)
       umma::mbar_expect_tx(vbar, bytes * kFsSlice);
       for (int dd = 0; dd < kFsSlice; dd++)
         umma::bulk_g2s(umma::smem_u32(sV + (size_t)dd * vpad),
-                       a.vals + (long long)(kvh * a.hs + slice * kFsSlice + dd) * a.v_pitch, bytes, vbar);
+                       vals + (long long)(kvh * a.hs + slice * kFsSlice + dd) * a.v_pitch, bytes, vbar);
     }
   } else {
     // Row cache: copied asynchronously and transposed, element d of row t
     // to sV[d][t], 4 bytes per copy (a warp writes 32 consecutive positions
     // of one element; a thread's 8 copies of a row share one 32-byte
     // sector). They land while the softmax runs.
-    const float *vb = a.vals + kvh * a.hs + slice * kFsSlice;
+    const float *vb = vals + kvh * a.hs + slice * kFsSlice;
     for (int t = threadIdx.x; t < P; t += blockDim.x) {
       const float *src = vb + (long long)t * a.kv_dim;
 #pragma unroll
@@ -939,6 +941,7 @@ __global__ void k_qkv_post(const QkvPostArgs a) {
   const int tz = blockIdx.y;
   const int pos = a.pos_dev[tz];
   float *const vrow = a.v + tz * a.tok_kv;
+  float *const key_cache = a.key_cache + tz * a.tok_keys, *const val_cache = a.val_cache + tz * a.tok_vals;
   const int kvDim = a.kv_heads * hs;
   const bool isq = blockIdx.x < a.heads;
   const int head = isq ? blockIdx.x : blockIdx.x - a.heads;
@@ -967,11 +970,11 @@ __global__ void k_qkv_post(const QkvPostArgs a) {
   __syncwarp();
   // 4. The key/value cache append (model.go:567-568).
   if (!isq) {
-    float *kc = a.key_cache + (long long)pos * kvDim + head * hs;
+    float *kc = key_cache + (long long)pos * kvDim + head * hs;
     for (int i = lane; i < hs; i += 32) {
       kc[i] = v[i];
-      if (a.v_pitch > 0) a.val_cache[(long long)(head * hs + i) * a.v_pitch + pos] = vrow[head * hs + i];
-      else a.val_cache[(long long)pos * kvDim + head * hs + i] = vrow[head * hs + i];
+      if (a.v_pitch > 0) val_cache[(long long)(head * hs + i) * a.v_pitch + pos] = vrow[head * hs + i];
+      else val_cache[(long long)pos * kvDim + head * hs + i] = vrow[head * hs + i];
     }
   }
 }
@@ -988,7 +991,8 @@ bool attention_many_ok(const AttnArgs &a) {
   // every token's q and score rows 16-byte aligned.
   return a.positions_dev && scores_tile_ok(a) && kvMul <= 8 && a.hs % kFsSlice == 0 && a.kv_dim % 4 == 0 &&
          a.att_stride % 4 == 0 && a.err && a.v_pitch > 0 && a.v_pitch % 4 == 0 && a16(a.vals) && a16(a.att) &&
-         a.tok_q % 4 == 0 && a.tok_att % 4 == 0 && fs_smem_bytes(kvMul, fs_wph(kvMul), a.max_positions) > 0;
+         a.tok_q % 4 == 0 && a.tok_att % 4 == 0 && a.tok_keys % 4 == 0 && a.tok_vals % 4 == 0 &&
+         fs_smem_bytes(kvMul, fs_wph(kvMul), a.max_positions) > 0;
 }
 
 cudaError_t launch_attention_many(const QkvPostArgs &qp, const AttnArgs &a, int nt, cudaStream_t st) {

@@ -47,8 +47,10 @@ struct AttnArgs {
   int *err;  // device error word for a pipeline wait that timed out
   // launch_attention_many: token t's q, scores and output lie t·tok_q,
   // t·tok_att and t·tok_out floats further, and its position count is
-  // positions_dev[t] + positions_add. Unused otherwise.
-  long long tok_q, tok_att, tok_out;
+  // positions_dev[t] + positions_add. With several sequences (a batched
+  // decode step), token t's keys and values lie t·tok_keys and t·tok_vals
+  // floats further (0: one sequence). Unused otherwise.
+  long long tok_q, tok_att, tok_out, tok_keys, tok_vals;
   // Row sharding: the output values also go to every rank's tagged copy
   // (at out's offset), one 8-byte value|tag word each.
   GatherPut put;
@@ -75,8 +77,9 @@ struct QkvPostArgs {
   int heads, kv_heads, hs;
   float eps, recip_hs;
   // launch_attention_many: token t's q and k/v lie t·tok_q and t·tok_kv
-  // floats further and its position is pos_dev[t]. 0 otherwise.
-  long long tok_q, tok_kv;
+  // floats further and its position is pos_dev[t]; its cache rows lie
+  // t·tok_keys and t·tok_vals floats further (several sequences). 0 otherwise.
+  long long tok_q, tok_kv, tok_keys, tok_vals;
 };
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st);
 

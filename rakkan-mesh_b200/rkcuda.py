@@ -30,7 +30,7 @@ EXPORTS = [
     "rk_batch_read", "rk_batch_matvecs", "rk_batch_quantize", "rk_batch_rmsnorm", "rk_batch_addvec", "rk_batch_rope",
     "rk_batch_copy", "rk_batch_attention", "rk_batch_residual", "rk_batch_silumul", "rk_batch_submit",
     "rk_config_validate", "rk_layer_upload", "rk_layer_from_device", "rk_layer_free", "rk_stage_new", "rk_stage_free",
-    "rk_stage_positions", "rk_stage_forward", "rk_stage_batched", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
+    "rk_stage_positions", "rk_stage_forward", "rk_stage_batched", "rk_stage_new_batch", "rk_stage_forward_batch", "rk_head_new", "rk_head_free", "rk_head_logits", "rk_embed", "rk_sample_argmax",
     "rk_model_new", "rk_model_free", "rk_model_step", "rk_model_generate", "rk_tensor_matmul",
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
     "rk_bench_matvec", "rk_bench_matvec_many", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
@@ -110,7 +110,7 @@ def lib():
             "rk_layer_upload": (i, [vp, vp, vp, vp]),
             "rk_layer_from_device": (i, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
             "rk_layer_free": (None, [vp]), "rk_stage_new": (i, [vp, vp, vp, i, i, vp]),
-            "rk_stage_free": (None, [vp]), "rk_stage_positions": (i, [vp]), "rk_stage_forward": (i, [vp, vp, i, i]), "rk_stage_batched": (i, [vp]),
+            "rk_stage_free": (None, [vp]), "rk_stage_positions": (i, [vp]), "rk_stage_forward": (i, [vp, vp, i, i]), "rk_stage_batched": (i, [vp]), "rk_stage_new_batch": (i, [vp, vp, vp, i, i, i, vp]), "rk_stage_forward_batch": (i, [vp, vp, vp, i]),
             "rk_head_new": (i, [vp, vp, vp, vp, vp]), "rk_head_free": (None, [vp]),
             "rk_head_logits": (i, [vp, vp, vp]), "rk_embed": (i, [vp, i, vp]),
             "rk_sample_argmax": (i, [vp, vp, i, vp]),
@@ -415,11 +415,13 @@ class Layer:
 class Stage:
     """llm.Stage on a device (model.go:446-613)."""
 
-    def __init__(self, dev, cfg, layers, ctx, group=None):
+    def __init__(self, dev, cfg, layers, ctx, group=None, nseq=1):
         hs = (C.c_void_p * max(1, len(layers)))(*[l.h for l in layers])
         self.h = C.c_void_p()
         self.dim = cfg.dim
-        if group is None:
+        if nseq > 1:
+            _check(lib().rk_stage_new_batch(dev.h, C.byref(cfg), hs, len(layers), ctx, nseq, C.byref(self.h)))
+        elif group is None:
             _check(lib().rk_stage_new(dev.h, C.byref(cfg), hs, len(layers), ctx, C.byref(self.h)))
         else:
             _check(lib().rk_stage_new_group(dev.h, C.byref(cfg), hs, len(layers), ctx, group.h, C.byref(self.h)))
@@ -431,6 +433,15 @@ class Stage:
         """1 when a sharded stage exchanges activations by NVLink stores and
         flags inside its kernels, 0 for NCCL all-gathers (or unsharded)."""
         return lib().rk_stage_fused_gathers(self.h)
+
+    def forward_batch(self, xs, positions):
+        """One decode step of several sequences: row q of xs is sequence q's
+        activation at positions[q] (a stage made with nseq > 1)."""
+        xs = np.ascontiguousarray(xs, dtype=np.float32).reshape(-1, self.dim).copy()
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        assert pos.size == xs.shape[0]
+        _check(lib().rk_stage_forward_batch(self.h, _ptr(xs), _ptr(pos), xs.shape[0]))
+        return xs
 
     def batched(self):
         """1 when forward() of several tokens runs the products batched on

@@ -140,7 +140,7 @@ class DeviceModel:
     """A whole synthetic model on one device: embed, stage of all layers,
     head and the greedy decode loop (rk_model)."""
 
-    def __init__(self, dev, c, seed, ctx=None, keep_host=False, group=None):
+    def __init__(self, dev, c, seed, ctx=None, keep_host=False, group=None, nseq=1):
         """keep_host: also download every matrix (host_weights, keyed like
         the oracle's OracleModel(weights=...)) before the layers own them.
         group: an rk.Group; this process then holds its row shard of every
@@ -168,7 +168,7 @@ class DeviceModel:
         if keep_host:
             self.host_weights["embed"] = self.embed.download()
             self.host_weights["cls"] = self.wcls.download()
-        self.stage = rk.Stage(dev, c, self.layers, self.ctx, group=group)
+        self.stage = rk.Stage(dev, c, self.layers, self.ctx, group=group, nseq=nseq)
         self.head = rk.Head(dev, c, np.ones(c.dim, np.float32), self.wcls, group=group)
         self.model = rk.Model(dev, self.embed, self.stage, self.head, c.vocab)
 

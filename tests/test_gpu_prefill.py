@@ -153,3 +153,42 @@ def test_unbatched_stages_report_it(dev):
         for l in layers:
             l.free()
         om.free()
+
+
+def test_batched_decode_matches_cpu(dev):
+    """Several independent sequences decoded together (rk_stage_forward_batch):
+    each sequence's cache is filled to its own length, then three steps run
+    for all of them at once, each at its own position. Every sequence's
+    activations equal its own oracle Stage's Forward, bit for bit; a prefill
+    through rk_stage_forward then uses sequence 0's cache as a one-sequence
+    stage would."""
+    c = prefill_config(heads=8, kv_heads=2, head_dim=64, dim=256, layers=2, seq_len=200, qkv_bias=1)
+    nseq, seed = 5, 41
+    fills = [0, 7, 64, 130, 33]
+    # One oracle Stage per sequence (the same seeded weights in each).
+    oms = [ro.OracleModel(c, seed=31, vec_seed=5) for _ in range(nseq)]
+    layers = upload_layers(dev, c, oracle_weights(oms[0], c), 5)
+    st = rk.Stage(dev, c, layers, c.seq_len, nseq=nseq)
+    try:
+        st.fill_cache(max(fills), seed)
+        for o, f in zip(oms, fills):
+            o.fill_cache(f, seed)
+        rng = np.random.default_rng(43)
+        for step in range(3):
+            xs = rng.standard_normal((nseq, c.dim)).astype(np.float32)
+            pos = [f + step for f in fills]
+            got = st.forward_batch(xs, pos)
+            for q in range(nseq):
+                same_bits(got[q], oms[q].forward(xs[q], pos[q]))
+        # Fewer sequences than the stage holds: the first three only.
+        xs = rng.standard_normal((3, c.dim)).astype(np.float32)
+        got = st.forward_batch(xs, [f + 3 for f in fills[:3]])
+        for q in range(3):
+            same_bits(got[q], oms[q].forward(xs[q], fills[q] + 3))
+    finally:
+        st.free()
+        for l in layers:
+            l.free()
+        for o in oms:
+            o.free()
+    assert dev.used() == 0
