@@ -321,14 +321,19 @@ __global__ void __launch_bounds__(288) k_attn_scores_tile(const AttnArgs a, int 
 // thread, then multiplication by Recip32 of the sum. One CTA per head.
 constexpr int kSoftmaxThreads = 256;
 constexpr int kSoftmaxSmem = 12224;  // floats kept in shared memory (static limit 48 KB)
+// BATCH (a batched decode step): grid.y is the token tz, whose scores lie
+// tz·tok_att further and whose position count is positions_dev[tz] +
+// positions_add.
+template <bool BATCH = false>
 __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs a) {
   griddep_trigger();
   griddep_wait();
   __shared__ __align__(16) float sv[kSoftmaxSmem];
   __shared__ float red[kSoftmaxThreads / 32];
   __shared__ float s_val;
-  const int P = attn_positions(a);
-  float *x = a.att + (long long)blockIdx.x * a.att_stride;
+  const int tz = BATCH ? (int)blockIdx.y : 0;
+  const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
+  float *x = (BATCH ? a.att + tz * a.tok_att : a.att) + (long long)blockIdx.x * a.att_stride;
   const bool in_smem = P <= kSoftmaxSmem;
   float *v = in_smem ? sv : x;
   float m = x[0];
@@ -374,6 +379,65 @@ __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs
   __syncthreads();
   const float inv = s_val;
   for (int i = threadIdx.x; i < P; i += blockDim.x) x[i] = __fmul_rn(v[i], inv);
+}
+
+// Weighted values of a batched decode step over transposed value caches
+// (element i of position t at vals[i·v_pitch + t]): out[h·hs+i] = the sum
+// over t in order from +0 of float32(w_h[t]·v_t[i]) (model.go:582-587),
+// with w the softmax weights k_attn_softmax<true> left in att. Grid: (kv
+// head, token); a thread per value element, running the chains of the kv
+// head's G query heads side by side (each value is loaded once for them).
+// A thread's value row is contiguous, so it streams through registers four
+// positions per 16-byte load, the next 8 loads in flight while the current
+// 8 are added; the weights are the same for every thread of the CTA. Small
+// CTAs without shared memory keep many of them on each SM, which is what a
+// step of many sequences needs.
+template <int G>
+__global__ void __launch_bounds__(128) k_attn_wsum_seq(const AttnArgs a) {
+  griddep_trigger();
+  griddep_wait();
+  const int tz = blockIdx.y, kvh = blockIdx.x, i = threadIdx.x;
+  const int P = a.positions_dev[tz] + a.positions_add;
+  const float *vrow = a.vals + tz * a.tok_vals + (long long)(kvh * a.hs + i) * a.v_pitch;
+  const float *wb = a.att + tz * a.tok_att + (long long)(kvh * G) * a.att_stride;
+  float acc[G];
+#pragma unroll
+  for (int g = 0; g < G; g++) acc[g] = 0.0f;
+  constexpr int U = 8;
+  const int n4 = P >> 2;
+  const float4 *v4 = reinterpret_cast<const float4 *>(vrow);
+  const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float4 cur[U], nxt[U];
+#pragma unroll
+  for (int u = 0; u < U; u++) cur[u] = u < n4 ? v4[u] : zero;
+  for (int b = 0; b < n4; b += U) {
+#pragma unroll
+    for (int u = 0; u < U; u++) nxt[u] = b + U + u < n4 ? v4[b + U + u] : zero;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      if (b + u < n4) {
+        const int t = 4 * (b + u);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          const float4 w = *reinterpret_cast<const float4 *>(wb + (long long)g * a.att_stride + t);
+          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.x, cur[u].x));
+          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.y, cur[u].y));
+          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.z, cur[u].z));
+          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.w, cur[u].w));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) cur[u] = nxt[u];
+  }
+  for (int t = 4 * n4; t < P; t++) {
+    const float v = vrow[t];
+#pragma unroll
+    for (int g = 0; g < G; g++) acc[g] = __fadd_rn(acc[g], __fmul_rn(wb[(long long)g * a.att_stride + t], v));
+  }
+  float *out = a.out + tz * a.tok_out;
+#pragma unroll
+  for (int g = 0; g < G; g++) out[(kvh * G + g) * a.hs + i] = acc[g];
 }
 
 // Weighted values: out[h·hs+i] = sum over t in order from +0 of
@@ -873,7 +937,7 @@ static cudaError_t launch_attention_impl(const AttnArgs &a, const QkvPostArgs *q
       return cudaGetLastError();
     }
   }
-  launch_k(k_attn_softmax, a.heads, kSoftmaxThreads, 0, st, a);
+  launch_k(k_attn_softmax<false>, a.heads, kSoftmaxThreads, 0, st, a);
   // The staged kernel copies 16-byte pieces: it needs whole 32-float slices
   // and 16-byte-aligned rows of values and scores.
   const bool staged = a.hs % 32 == 0 && a.kv_dim % 4 == 0 && a.att_stride % 4 == 0 &&
@@ -1009,7 +1073,24 @@ cudaError_t launch_attention_many(const QkvPostArgs &qp, const AttnArgs &a, int 
   const QkvPostArgs none{};
   if (a.hs == 64) launch_k(k_attn_scores_tile<64, false, true>, g1, threads, 0, st, a, gpb, none);
   else launch_k(k_attn_scores_tile<128, false, true>, g1, threads, 0, st, a, gpb, none);
-  // 3. Every token's softmax and weighted values.
+  // 3. Every token's softmax and weighted values. Tokens of different
+  // sequences (a batched decode step) take the streaming pair of kernels;
+  // a prompt's tokens take the single fused kernel.
+  if (a.tok_keys != 0) {
+    launch_k(k_attn_softmax<true>, dim3(a.heads, nt), kSoftmaxThreads, 0, st, a);
+    const dim3 gw(a.kv_heads, nt);
+    switch (kvMul) {
+      case 1: launch_k(k_attn_wsum_seq<1>, gw, a.hs, 0, st, a); break;
+      case 2: launch_k(k_attn_wsum_seq<2>, gw, a.hs, 0, st, a); break;
+      case 3: launch_k(k_attn_wsum_seq<3>, gw, a.hs, 0, st, a); break;
+      case 4: launch_k(k_attn_wsum_seq<4>, gw, a.hs, 0, st, a); break;
+      case 5: launch_k(k_attn_wsum_seq<5>, gw, a.hs, 0, st, a); break;
+      case 6: launch_k(k_attn_wsum_seq<6>, gw, a.hs, 0, st, a); break;
+      case 7: launch_k(k_attn_wsum_seq<7>, gw, a.hs, 0, st, a); break;
+      default: launch_k(k_attn_wsum_seq<8>, gw, a.hs, 0, st, a); break;
+    }
+    return cudaGetLastError();
+  }
   const int wph = fs_wph(kvMul);
   const dim3 g(a.kv_heads, a.hs / kFsSlice, nt);
   const int c = fs_cluster(dim3(g.x * g.z, g.y));  // clusters run along y; every CTA of the grid counts

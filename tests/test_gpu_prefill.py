@@ -155,16 +155,18 @@ def test_unbatched_stages_report_it(dev):
         om.free()
 
 
-def test_batched_decode_matches_cpu(dev):
+@pytest.mark.parametrize("heads,kv_heads,fills,seq_len", [(8, 2, [0, 7, 64, 130, 33], 200),
+                                                           (4, 4, [1500, 3, 777], 1600),
+                                                           (14, 2, [250, 1, 99, 5], 300)],
+                         ids=["gqa4", "mha_long", "gqa7"])
+def test_batched_decode_matches_cpu(dev, heads, kv_heads, fills, seq_len):
     """Several independent sequences decoded together (rk_stage_forward_batch):
-    each sequence's cache is filled to its own length, then three steps run
-    for all of them at once, each at its own position. Every sequence's
-    activations equal its own oracle Stage's Forward, bit for bit; a prefill
-    through rk_stage_forward then uses sequence 0's cache as a one-sequence
-    stage would."""
-    c = prefill_config(heads=8, kv_heads=2, head_dim=64, dim=256, layers=2, seq_len=200, qkv_bias=1)
-    nseq, seed = 5, 41
-    fills = [0, 7, 64, 130, 33]
+    each sequence's cache is filled to its own length (up to 1500 positions),
+    then three steps run for all of them at once, each at its own position,
+    with 4, 1 and 7 query heads per kv head. Every sequence's activations
+    equal its own oracle Stage's Forward, bit for bit."""
+    c = prefill_config(heads=heads, kv_heads=kv_heads, head_dim=64, dim=256, layers=2, seq_len=seq_len, qkv_bias=1)
+    nseq, seed = len(fills), 41
     # One oracle Stage per sequence (the same seeded weights in each).
     oms = [ro.OracleModel(c, seed=31, vec_seed=5) for _ in range(nseq)]
     layers = upload_layers(dev, c, oracle_weights(oms[0], c), 5)
@@ -180,10 +182,10 @@ def test_batched_decode_matches_cpu(dev):
             got = st.forward_batch(xs, pos)
             for q in range(nseq):
                 same_bits(got[q], oms[q].forward(xs[q], pos[q]))
-        # Fewer sequences than the stage holds: the first three only.
-        xs = rng.standard_normal((3, c.dim)).astype(np.float32)
-        got = st.forward_batch(xs, [f + 3 for f in fills[:3]])
-        for q in range(3):
+        # Fewer sequences than the stage holds: the first two only.
+        xs = rng.standard_normal((2, c.dim)).astype(np.float32)
+        got = st.forward_batch(xs, [f + 3 for f in fills[:2]])
+        for q in range(2):
             same_bits(got[q], oms[q].forward(xs[q], fills[q] + 3))
     finally:
         st.free()
