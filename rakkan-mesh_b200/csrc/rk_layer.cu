@@ -385,59 +385,75 @@ __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs
 // (element i of position t at vals[i·v_pitch + t]): out[h·hs+i] = the sum
 // over t in order from +0 of float32(w_h[t]·v_t[i]) (model.go:582-587),
 // with w the softmax weights k_attn_softmax<true> left in att. Grid: (kv
-// head, token); a thread per value element, running the chains of the kv
-// head's G query heads side by side (each value is loaded once for them).
-// A thread's value row is contiguous, so it streams through registers four
-// positions per 16-byte load, the next 8 loads in flight while the current
-// 8 are added; the weights are the same for every thread of the CTA. Small
-// CTAs without shared memory keep many of them on each SM, which is what a
-// step of many sequences needs.
+// head × 32-element group, token); one warp per CTA, a lane per value
+// element, running the chains of the kv head's G query heads side by side.
+// The warp copies its 32 rows in tiles of 64 positions into shared memory
+// with 16-byte cp.async (half a warp per 256-byte row segment, so every
+// load is whole sectors), the next tile in flight while the lanes add the
+// current one from shared memory (rows 68 floats apart: conflict-free).
 template <int G>
-__global__ void __launch_bounds__(128) k_attn_wsum_seq(const AttnArgs a) {
+__global__ void __launch_bounds__(32) k_attn_wsum_seq(const AttnArgs a) {
+  constexpr int TP = 64, PITCH = TP + 4;
+  __shared__ __align__(16) float sv[2][32 * PITCH];
   griddep_trigger();
   griddep_wait();
-  const int tz = blockIdx.y, kvh = blockIdx.x, i = threadIdx.x;
+  const int lane = threadIdx.x, tz = blockIdx.y;
+  const int ngr = a.hs / 32, kvh = blockIdx.x / ngr, e0 = (blockIdx.x % ngr) * 32;
   const int P = a.positions_dev[tz] + a.positions_add;
-  const float *vrow = a.vals + tz * a.tok_vals + (long long)(kvh * a.hs + i) * a.v_pitch;
+  const float *vb = a.vals + tz * a.tok_vals + (long long)(kvh * a.hs + e0) * a.v_pitch;
   const float *wb = a.att + tz * a.tok_att + (long long)(kvh * G) * a.att_stride;
+  const int ntile = (P + TP - 1) / TP;
+  // Tile k into buffer buf: 32 rows × 16 float4, flat index f = lane + 32j
+  // (row f / 16, float4 f % 16); positions at or past P are not read.
+  const auto load_tile = [&](int k, int buf) {
+    const int t0 = k * TP;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const int f = lane + 32 * j, r = f >> 4, c = f & 15, t = t0 + 4 * c;
+      if (t < P)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(&sv[buf][r * PITCH + 4 * c])),
+                     "l"(vb + (long long)r * a.v_pitch + t)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   float acc[G];
 #pragma unroll
   for (int g = 0; g < G; g++) acc[g] = 0.0f;
-  constexpr int U = 8;
-  const int n4 = P >> 2;
-  const float4 *v4 = reinterpret_cast<const float4 *>(vrow);
-  const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  float4 cur[U], nxt[U];
+  if (ntile > 0) load_tile(0, 0);
+  for (int k = 0; k < ntile; k++) {
+    if (k + 1 < ntile) {
+      load_tile(k + 1, (k + 1) & 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+    const float *row = sv[k & 1] + lane * PITCH;
+    const int t0 = k * TP, n = min(TP, P - t0), n4 = n >> 2;
+    for (int c = 0; c < n4; c++) {
+      const float4 v = *reinterpret_cast<const float4 *>(row + 4 * c);
 #pragma unroll
-  for (int u = 0; u < U; u++) cur[u] = u < n4 ? v4[u] : zero;
-  for (int b = 0; b < n4; b += U) {
-#pragma unroll
-    for (int u = 0; u < U; u++) nxt[u] = b + U + u < n4 ? v4[b + U + u] : zero;
-#pragma unroll
-    for (int u = 0; u < U; u++) {
-      if (b + u < n4) {
-        const int t = 4 * (b + u);
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-          const float4 w = *reinterpret_cast<const float4 *>(wb + (long long)g * a.att_stride + t);
-          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.x, cur[u].x));
-          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.y, cur[u].y));
-          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.z, cur[u].z));
-          acc[g] = __fadd_rn(acc[g], __fmul_rn(w.w, cur[u].w));
-        }
+      for (int g = 0; g < G; g++) {
+        const float4 w = *reinterpret_cast<const float4 *>(wb + (long long)g * a.att_stride + t0 + 4 * c);
+        acc[g] = __fadd_rn(acc[g], __fmul_rn(w.x, v.x));
+        acc[g] = __fadd_rn(acc[g], __fmul_rn(w.y, v.y));
+        acc[g] = __fadd_rn(acc[g], __fmul_rn(w.z, v.z));
+        acc[g] = __fadd_rn(acc[g], __fmul_rn(w.w, v.w));
       }
     }
+    for (int t = 4 * n4; t < n; t++) {
+      const float v = row[t];
 #pragma unroll
-    for (int u = 0; u < U; u++) cur[u] = nxt[u];
-  }
-  for (int t = 4 * n4; t < P; t++) {
-    const float v = vrow[t];
-#pragma unroll
-    for (int g = 0; g < G; g++) acc[g] = __fadd_rn(acc[g], __fmul_rn(wb[(long long)g * a.att_stride + t], v));
+      for (int g = 0; g < G; g++)
+        acc[g] = __fadd_rn(acc[g], __fmul_rn(wb[(long long)g * a.att_stride + t0 + t], v));
+    }
+    __syncwarp();  // every lane is done with this buffer before it is refilled
   }
   float *out = a.out + tz * a.tok_out;
 #pragma unroll
-  for (int g = 0; g < G; g++) out[(kvh * G + g) * a.hs + i] = acc[g];
+  for (int g = 0; g < G; g++) out[(kvh * G + g) * a.hs + e0 + lane] = acc[g];
 }
 
 // Weighted values: out[h·hs+i] = sum over t in order from +0 of
@@ -1078,16 +1094,16 @@ cudaError_t launch_attention_many(const QkvPostArgs &qp, const AttnArgs &a, int 
   // a prompt's tokens take the single fused kernel.
   if (a.tok_keys != 0) {
     launch_k(k_attn_softmax<true>, dim3(a.heads, nt), kSoftmaxThreads, 0, st, a);
-    const dim3 gw(a.kv_heads, nt);
+    const dim3 gw(a.kv_heads * (a.hs / 32), nt);
     switch (kvMul) {
-      case 1: launch_k(k_attn_wsum_seq<1>, gw, a.hs, 0, st, a); break;
-      case 2: launch_k(k_attn_wsum_seq<2>, gw, a.hs, 0, st, a); break;
-      case 3: launch_k(k_attn_wsum_seq<3>, gw, a.hs, 0, st, a); break;
-      case 4: launch_k(k_attn_wsum_seq<4>, gw, a.hs, 0, st, a); break;
-      case 5: launch_k(k_attn_wsum_seq<5>, gw, a.hs, 0, st, a); break;
-      case 6: launch_k(k_attn_wsum_seq<6>, gw, a.hs, 0, st, a); break;
-      case 7: launch_k(k_attn_wsum_seq<7>, gw, a.hs, 0, st, a); break;
-      default: launch_k(k_attn_wsum_seq<8>, gw, a.hs, 0, st, a); break;
+      case 1: launch_k(k_attn_wsum_seq<1>, gw, 32, 0, st, a); break;
+      case 2: launch_k(k_attn_wsum_seq<2>, gw, 32, 0, st, a); break;
+      case 3: launch_k(k_attn_wsum_seq<3>, gw, 32, 0, st, a); break;
+      case 4: launch_k(k_attn_wsum_seq<4>, gw, 32, 0, st, a); break;
+      case 5: launch_k(k_attn_wsum_seq<5>, gw, 32, 0, st, a); break;
+      case 6: launch_k(k_attn_wsum_seq<6>, gw, 32, 0, st, a); break;
+      case 7: launch_k(k_attn_wsum_seq<7>, gw, 32, 0, st, a); break;
+      default: launch_k(k_attn_wsum_seq<8>, gw, 32, 0, st, a); break;
     }
     return cudaGetLastError();
   }
