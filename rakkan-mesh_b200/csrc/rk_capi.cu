@@ -14,6 +14,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <initializer_list>
 #include <chrono>
 #include <condition_variable>
 #include <cstdarg>
@@ -598,16 +599,8 @@ extern "C" int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const floa
   if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, 4 * n * cols, cudaMemcpyHostToDevice, d->st);
   if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, xs_pitch, d->st);
   if (e == cudaSuccess) {
-    MmArgs a{};
-    a.rows = m->rows;
-    a.cols = m->cols;
-    a.ntok = n;
-    a.xs_pitch = xs_pitch;
-    a.out = dout;
-    a.out_stride = (long long)rows;
-    a.epi = EPI_STORE;
-    a.err = d->err_dev;
-    e = launch_mv_many(a, m->w, m->s, dqx, dxs, d->sms, d->st);
+    const MmMat mat{m->w, m->s, m->rows, dout, (long long)rows, EPI_STORE};
+    e = launch_mv_many(1, &mat, m->cols, n, dqx, dxs, xs_pitch, d->err_dev, d->sms, d->st);
   }
   if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, 4 * n * rows, cudaMemcpyDeviceToHost, d->st);
   rc = e == cudaSuccess ? sync_dev(d) : cuda_fail(e, "batched matvec");
@@ -1699,17 +1692,13 @@ static int stage_forward_many(rk_stage *s, const int *positions, int nt, bool pe
     max_pos = std::max(max_pos, positions[t] + 1);
   }
   CK(cudaMemcpyAsync(s->m_pos, s->pin_pos, sizeof(int) * nt, cudaMemcpyHostToDevice, st));
-  const auto product = [&](const rk_matrix *m, float *out, long long stride, int epi) {
-    MmArgs a{};
-    a.rows = m->rows;
-    a.cols = m->cols;
-    a.ntok = nt;
-    a.xs_pitch = s->io_tokens;
-    a.out = out;
-    a.out_stride = stride;
-    a.epi = epi;
-    a.err = d->err_dev;
-    return launch_mv_many(a, m->w, m->s, s->m_qx, s->m_xs, d->sms, st);
+  // Up to three matrices that share the quantized input, in one launch.
+  const auto products = [&](int cols, std::initializer_list<MmMat> mats) {
+    return launch_mv_many((int)mats.size(), mats.begin(), cols, nt, s->m_qx, s->m_xs, s->io_tokens, d->err_dev,
+                          d->sms, st);
+  };
+  const auto mat = [](const rk_matrix *m, float *out, long long stride, int epi) {
+    return MmMat{m->w, m->s, m->rows, out, stride, epi};
   };
   float *X = s->io;
   // When the attention runs batched, every kernel of the submission reads
@@ -1737,9 +1726,8 @@ static int stage_forward_many(rk_stage *s, const int *positions, int nt, bool pe
     const float *vec = l->vecs->v;
     // q, k, v = Wq·xb, Wk·xb, Wv·xb with xb = rmsNorm(x, RmsAtt) (model.go:538-539).
     CK(launch_quantize_many(X, nt, D, vec + l->o_rms_att, recipD, eps, s->m_qx, s->m_xs, s->io_tokens, st));
-    CK(product(l->wq, s->m_q, qd, EPI_STORE));
-    CK(product(l->wk, s->m_k, kvd, EPI_STORE));
-    CK(product(l->wv, s->m_v, kvd, EPI_STORE));
+    CK(products(D, {mat(l->wq, s->m_q, qd, EPI_STORE), mat(l->wk, s->m_k, kvd, EPI_STORE),
+                    mat(l->wv, s->m_v, kvd, EPI_STORE)}));
     // Bias, QK-norm, RoPE, cache append and attention (model.go:542-587):
     // all tokens' appends, then all tokens' attention, in three launches;
     // shapes the batched kernels do not take go token by token.
@@ -1757,15 +1745,14 @@ static int stage_forward_many(rk_stage *s, const int *positions, int nt, bool pe
     }
     // x += Wo·attOut (model.go:588-594).
     CK(launch_quantize_many(s->m_att, nt, qd, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, s->io_tokens, st));
-    CK(product(l->wo, X, D, EPI_ADD));
+    CK(products(qd, {mat(l->wo, X, D, EPI_ADD)}));
     // hb = silu(W1·xb)·(W3·xb) with xb = rmsNorm(x, RmsFfn) (model.go:597-603).
     CK(launch_quantize_many(X, nt, D, vec + l->o_rms_ffn, recipD, eps, s->m_qx, s->m_xs, s->io_tokens, st));
-    CK(product(l->w1, s->m_hb, H, EPI_STORE));
-    CK(product(l->w3, s->m_hb2, H, EPI_STORE));
+    CK(products(D, {mat(l->w1, s->m_hb, H, EPI_STORE), mat(l->w3, s->m_hb2, H, EPI_STORE)}));
     CK(launch_silu_mul_many(s->m_hb, s->m_hb2, (long long)nt * H, d->sms, st));
     // x = Canonical(x + W2·hb) (model.go:604-610).
     CK(launch_quantize_many(s->m_hb, nt, H, nullptr, 0.0f, 0.0f, s->m_qx, s->m_xs, s->io_tokens, st));
-    CK(product(l->w2, X, D, EPI_ADD_CANON));
+    CK(products(H, {mat(l->w2, X, D, EPI_ADD_CANON)}));
   }
   return RK_OK;
 }
@@ -2626,19 +2613,11 @@ extern "C" int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, f
   if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, xs_pitch, d->st);
   if (e == cudaSuccess) e = cudaEventCreate(&e0);
   if (e == cudaSuccess) e = cudaEventCreate(&e1);
-  MmArgs a{};
-  a.rows = m->rows;
-  a.cols = m->cols;
-  a.ntok = n;
-  a.xs_pitch = xs_pitch;
-  a.out = dout;
-  a.out_stride = (long long)rows;
-  a.epi = EPI_STORE;
-  a.err = d->err_dev;
+  const MmMat mat{m->w, m->s, m->rows, dout, (long long)rows, EPI_STORE};
   for (int i = 0; e == cudaSuccess && i < iters + 1; i++) {
     if (flush) k_flush_read<<<d->sms * 4, 512, 0, d->st>>>((const int4 *)d->flush, (long long)(d->flush_bytes / 16), d->err_dev + 1);
     e = cudaEventRecord(e0, d->st);
-    if (e == cudaSuccess) e = launch_mv_many(a, m->w, m->s, dqx, dxs, d->sms, d->st);
+    if (e == cudaSuccess) e = launch_mv_many(1, &mat, m->cols, n, dqx, dxs, xs_pitch, d->err_dev, d->sms, d->st);
     if (e == cudaSuccess) e = cudaEventRecord(e1, d->st);
     if (e == cudaSuccess) e = cudaEventSynchronize(e1);
     float ms = 0.0f;

@@ -108,24 +108,29 @@ cudaError_t init_matvec_attributes();
 // ---- Products of one Q8_0 matrix with many input vectors (ForwardMany's
 // projections, model.go:504-518: each token's product is one MatVecQ8) on
 // the tcgen05 tensor cores; bits identical to the single-vector kernel. ----
-struct MmArgs {
-  int rows, cols, ntok;
-  int xs_pitch;           // the input scales are block-major: token t's block b at xs[b·xs_pitch + t]
-  float *out;             // token t's row r at out[t·out_stride + r]
+// One matrix of a batched launch: Q8_0 weights and scales, its output
+// (token t's row r at out[t·out_stride + r]) and what is done with it.
+struct MmMat {
+  const uint8_t *w;
+  const float *ws;
+  int rows;
+  float *out;
   long long out_stride;
-  int epi;                // EPI_STORE, EPI_ADD or EPI_ADD_CANON
-  int *err;               // device error word (a bounded wait gave up)
+  int epi;  // EPI_STORE, EPI_ADD or EPI_ADD_CANON
 };
+constexpr int kMmMaxMats = 3;
 
 // Whether a matrix can take the batched kernel: Q8_0 rows of a multiple of
 // 128 columns, weights and scales 16-byte aligned, TMA available.
 bool mv_many_ok(int rows, int cols, const void *w, const float *ws);
 
-// out = W·x_t for the ntok tokens whose Q8_0 inputs are qx [ntok][cols]
-// and xs [cols/32][xs_pitch] (16-byte aligned device buffers; xs_pitch a
-// multiple of 4, at least ntok).
-cudaError_t launch_mv_many(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx, const float *xs,
-                           int num_sms, cudaStream_t st);
+// out_m = W_m·x_t for up to kMmMaxMats matrices of cols columns sharing the
+// input (one launch; their row tiles share the grid) and the ntok tokens
+// whose Q8_0 inputs are qx [ntok][cols] and xs [cols/32][xs_pitch]
+// (16-byte aligned device buffers; xs_pitch a multiple of 4, at least
+// ntok). err: the device error word a timed-out wait sets.
+cudaError_t launch_mv_many(int nmats, const MmMat *mats, int cols, int ntok, const int8_t *qx, const float *xs,
+                           int xs_pitch, int *err, int num_sms, cudaStream_t st);
 
 // quantize8 of each of n rows of x [n][cols] (after rmsNorm with w when w
 // is given): qx [n][cols], and the scales block-major, xs [cols/32][xs_pitch]

@@ -32,6 +32,22 @@
 
 namespace rk {
 
+// The launch's matrices: CTA row tile y belongs to matrix m when tile0[m]
+// <= y < tile0[m+1]; its rows start at (y - tile0[m])·128.
+struct MmArgs {
+  int cols, ntok, nmats;
+  int tile0[kMmMaxMats + 1];
+  int rows[kMmMaxMats];
+  float *out[kMmMaxMats];
+  long long out_stride[kMmMaxMats];
+  int epi[kMmMaxMats];
+  int *err;
+};
+// Tensor maps of every matrix's weights and scales (kernel parameters).
+struct MmMaps {
+  CUtensorMap w[kMmMaxMats], ws[kMmMaxMats];
+};
+
 constexpr int kMmStages = 6;  // shared-memory stages (128 input columns each)
 constexpr int kMmGroups = 4;  // TMEM column groups (one stage's four blocks each)
 
@@ -77,8 +93,8 @@ RK_DEV void mm_terms(float (&acc)[8][8], const int32_t (&v)[NK][8], float4 ws, c
 
 template <int NT>
 __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
-    k_mv_many_q8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                 const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs, MmArgs a) {
+    k_mv_many_q8(const __grid_constant__ MmMaps maps, const __grid_constant__ CUtensorMap tmX,
+                 const __grid_constant__ CUtensorMap tmXs, const MmArgs a) {
   using C = MmCfg<NT>;
   constexpr int S = kMmStages, G = kMmGroups, E = C::kEpiWarps;
   extern __shared__ uint8_t dsmem[];
@@ -93,7 +109,10 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
   const auto accf = [&](int g) { return bar0 + 8u * (2 * S + g); };
   const auto acce = [&](int g) { return bar0 + 8u * (2 * S + G + g); };
   const uint32_t done = bar0 + 8u * (2 * S + 2 * G);
-  const int t0 = blockIdx.x * NT, r0 = blockIdx.y * 128;
+  const int y = blockIdx.y;
+  const int m = a.nmats > 1 && y >= a.tile0[1] ? (a.nmats > 2 && y >= a.tile0[2] ? 2 : 1) : 0;
+  const CUtensorMap *const tmW = &maps.w[m], *const tmWs = &maps.ws[m];
+  const int t0 = blockIdx.x * NT, r0 = (y - a.tile0[m]) * 128;
   const int nkb = a.cols / 128;
 
   if (threadIdx.x == 0) {
@@ -107,9 +126,9 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
     }
     umma::mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    umma::prefetch_tmap(&tmW);
+    umma::prefetch_tmap(tmW);
     umma::prefetch_tmap(&tmX);
-    umma::prefetch_tmap(&tmWs);
+    umma::prefetch_tmap(tmWs);
     umma::prefetch_tmap(&tmXs);
   }
   __syncwarp();
@@ -131,9 +150,9 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
         }
         const uint32_t st = ring + s * C::kStage;
         umma::mbar_expect_tx(full(s), C::kTx);
-        umma::tma_load_2d(st, &tmW, i * 128, r0, full(s));
+        umma::tma_load_2d(st, tmW, i * 128, r0, full(s));
         umma::tma_load_2d(st + C::kW, &tmX, i * 128, t0, full(s));
-        umma::tma_load_2d(st + C::kW + C::kX, &tmWs, i * 4, r0, full(s));
+        umma::tma_load_2d(st + C::kW + C::kX, tmWs, i * 4, r0, full(s));
         umma::tma_load_2d(st + C::kW + C::kX + C::kWs, &tmXs, t0, i * 4, full(s));
         issued = i + 1;
       }
@@ -217,17 +236,17 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
     }
     if (!ok) {
       atomicExch(a.err, DEV_ERR_TIMEOUT);
-    } else if (row < a.rows) {
+    } else if (row < a.rows[m]) {
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const int t = t0 + tk0 + j;
         if (t >= a.ntok) break;
         const float r = __fadd_rn(__fadd_rn(__fadd_rn(acc[j][0], acc[j][1]), __fadd_rn(acc[j][2], acc[j][3])),
                                   __fadd_rn(__fadd_rn(acc[j][4], acc[j][5]), __fadd_rn(acc[j][6], acc[j][7])));
-        float *o = a.out + (size_t)t * a.out_stride + row;
-        if (a.epi == EPI_ADD)
+        float *o = a.out[m] + (size_t)t * a.out_stride[m] + row;
+        if (a.epi[m] == EPI_ADD)
           *o = __fadd_rn(*o, r);
-        else if (a.epi == EPI_ADD_CANON)
+        else if (a.epi[m] == EPI_ADD_CANON)
           *o = canonical(__fadd_rn(*o, r));
         else
           *o = r;
@@ -270,34 +289,56 @@ bool mv_many_ok(int rows, int cols, const void *w, const float *ws) {
 }
 
 template <int NT>
-static cudaError_t launch_mm_nt(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx,
-                                const float *xs, cudaStream_t st) {
-  CUtensorMap tmW, tmX, tmWs, tmXs;
+static cudaError_t launch_mm_nt(const MmArgs &a, const MmMat *mats, const int8_t *qx, const float *xs, int xs_pitch,
+                                cudaStream_t st) {
+  MmMaps maps;
+  CUtensorMap tmX, tmXs;
   const int nb = a.cols / 32;
-  if (!tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)a.cols, (uint64_t)a.rows, (uint64_t)a.cols, 128,
-               128, true) ||
-      !tmap_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, (uint64_t)a.cols, (uint64_t)a.ntok, (uint64_t)a.cols, 128,
+  for (int m = 0; m < a.nmats; m++)
+    if (!tmap_2d(&maps.w[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, mats[m].w, (uint64_t)a.cols, (uint64_t)mats[m].rows,
+                 (uint64_t)a.cols, 128, 128, true) ||
+        !tmap_2d(&maps.ws[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, mats[m].ws, (uint64_t)nb, (uint64_t)mats[m].rows,
+                 4ull * nb, 4, 128, false))
+      return cudaErrorInvalidValue;
+  for (int m = a.nmats; m < kMmMaxMats; m++) {
+    maps.w[m] = maps.w[0];
+    maps.ws[m] = maps.ws[0];
+  }
+  if (!tmap_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, qx, (uint64_t)a.cols, (uint64_t)a.ntok, (uint64_t)a.cols, 128,
                NT, true) ||
-      !tmap_2d(&tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, (uint64_t)nb, (uint64_t)a.rows, 4ull * nb, 4, 128,
-               false) ||
-      !tmap_2d(&tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)a.xs_pitch, (uint64_t)nb, 4ull * a.xs_pitch, NT,
-               4, false))
+      !tmap_2d(&tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)xs_pitch, (uint64_t)nb, 4ull * xs_pitch, NT, 4,
+               false))
     return cudaErrorInvalidValue;
-  const dim3 grid((unsigned)((a.ntok + NT - 1) / NT), (unsigned)((a.rows + 127) / 128));
-  return launch_k(k_mv_many_q8<NT>, grid, MmCfg<NT>::kThreads, MmCfg<NT>::kSmem, st, tmW, tmX, tmWs, tmXs, a);
+  const dim3 grid((unsigned)((a.ntok + NT - 1) / NT), (unsigned)a.tile0[a.nmats]);
+  return launch_k(k_mv_many_q8<NT>, grid, MmCfg<NT>::kThreads, MmCfg<NT>::kSmem, st, maps, tmX, tmXs, a);
 }
 
-cudaError_t launch_mv_many(const MmArgs &a, const uint8_t *w, const float *ws, const int8_t *qx, const float *xs,
-                           int num_sms, cudaStream_t st) {
-  if (a.ntok <= 0) return cudaSuccess;
-  if (!mv_many_ok(a.rows, a.cols, w, ws) || ((uintptr_t)qx & 15) || ((uintptr_t)xs & 15) || a.xs_pitch % 4 ||
-      a.xs_pitch < a.ntok)
+cudaError_t launch_mv_many(int nmats, const MmMat *mats, int cols, int ntok, const int8_t *qx, const float *xs,
+                           int xs_pitch, int *err, int num_sms, cudaStream_t st) {
+  if (ntok <= 0) return cudaSuccess;
+  if (nmats < 1 || nmats > kMmMaxMats || ((uintptr_t)qx & 15) || ((uintptr_t)xs & 15) || xs_pitch % 4 ||
+      xs_pitch < ntok)
     return cudaErrorInvalidValue;
-  const long long row_tiles = (a.rows + 127) / 128;
+  MmArgs a{};
+  a.cols = cols;
+  a.ntok = ntok;
+  a.nmats = nmats;
+  a.err = err;
+  for (int m = 0; m < nmats; m++) {
+    if (!mv_many_ok(mats[m].rows, cols, mats[m].w, mats[m].ws)) return cudaErrorInvalidValue;
+    a.rows[m] = mats[m].rows;
+    a.out[m] = mats[m].out;
+    a.out_stride[m] = mats[m].out_stride;
+    a.epi[m] = mats[m].epi;
+    a.tile0[m + 1] = a.tile0[m] + (mats[m].rows + 127) / 128;
+  }
+  for (int m = nmats + 1; m <= kMmMaxMats; m++) a.tile0[m] = a.tile0[nmats];
+  const long long row_tiles = a.tile0[nmats];
+  if (row_tiles > 65535) return cudaErrorInvalidValue;
   // 32 tokens per CTA halve the weight tiles' re-reads from L2 once the
   // grid fills the SMs anyway; otherwise 16 give twice the CTAs.
-  if (a.ntok > 16 && row_tiles * ((a.ntok + 31) / 32) >= num_sms) return launch_mm_nt<32>(a, w, ws, qx, xs, st);
-  return launch_mm_nt<16>(a, w, ws, qx, xs, st);
+  if (ntok > 16 && row_tiles * ((ntok + 31) / 32) >= num_sms) return launch_mm_nt<32>(a, mats, qx, xs, xs_pitch, st);
+  return launch_mm_nt<16>(a, mats, qx, xs, xs_pitch, st);
 }
 
 cudaError_t launch_silu_mul_many(float *hb, const float *hb2, long long n, int num_sms, cudaStream_t st) {
