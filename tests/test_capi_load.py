@@ -40,3 +40,17 @@ def test_device_count_without_gpu_is_zero_or_more():
     n = C.c_int(-1)
     assert rk.lib().rk_device_count(C.byref(n)) == rk.RK_OK
     assert n.value >= 0
+
+
+def test_batched_entry_points_check_arguments_without_gpu():
+    """The batched prefill / batched decode entry points refuse bad
+    arguments before they touch a device."""
+    L = rk.lib()
+    assert L.rk_matrix_mulvec_many(None, 4, None, None) == rk.RK_ERR_ARGS
+    assert L.rk_bench_matvec_many(None, 4, 1, 0, None) == rk.RK_ERR_ARGS
+    assert L.rk_stage_batched(None) == 0
+    out = C.c_void_p()
+    assert L.rk_stage_new_batch(None, None, None, 0, 16, 0, C.byref(out)) == rk.RK_ERR_ARGS
+    assert L.rk_stage_new_batch(None, None, None, 0, 16, 4, C.byref(out)) == rk.RK_ERR_ARGS
+    assert L.rk_stage_forward_batch(None, None, None, 2) == rk.RK_ERR_ARGS
+    assert b"argument" in L.rk_last_error() or b"sequence" in L.rk_last_error()
