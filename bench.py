@@ -26,6 +26,13 @@ all-gathers where that is not possible): one sequence decoded by all N GPUs
 (strong scaling; value = its tokens/s). --mode replicas runs N independent
 copies instead (weak scaling); --mode pipeline splits the layers into N
 stages (rk_plan_stages) that pass the activation on (roofline not measured).
+
+Other measurements (one JSON line each, not the headline):
+  --kernel matvec        one decode matvec of --shape (L2 flushed)
+  --kernel matvec_many   one batched Q8_0 product of --shape with --prefill vectors
+  --kernel tensor        rakkan_tensor_v1 matmul / matmul_t, config 2's sweep
+  --kernel prefill       ForwardMany over --prefill tokens of --model (config 3's 512-token prefill)
+  --kernel decode_batch  one decode step of --batch sequences with --ctx-token caches (config 4's batch 32)
 """
 import argparse
 import json
