@@ -328,14 +328,38 @@ def cpu_sample(args, steps=1, sample_layers=2, threads=None):
 
 
 def run_reference(args, rank):
+    """The reference arm: the CPU implementation of the path (the oracle, a C
+    restatement of the reference's Go CPU path; the Go toolchain is absent
+    on this box) on the same workload as the CUDA arm: the whole model
+    (every layer and the classifier) at position ctx over a ctx-token cache,
+    W untimed warm-up steps, then exactly K timed steps, each one whole
+    decode step (forward, logits, argmax), on all the host threads it can
+    use. Under torchrun only rank 0 runs it."""
     if rank != 0:
         return
-    value, cores, sample = cpu_sample(args, steps=max(1, args.steps // 10))
+    import rk_oracle as ro
+    import synth
+    c = synth.config(args.model, args.dtype, seq_len=args.ctx + 1)
+    om = ro.OracleModel(c, SEED, ctx=args.ctx + 1)
+    try:
+        om.fill_cache(args.ctx, SEED)
+        for _ in range(args.warmup):
+            om.step(1, args.ctx)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            om.step(1, args.ctx)
+        ms = (time.perf_counter() - t0) * 1000.0 / max(1, args.steps)
+    finally:
+        om.free()
+    value = 1000.0 / ms
+    sample = (f"the whole decode step ({c.layers} layers at position {args.ctx}, classifier, argmax), "
+              f"{args.steps} timed steps after {args.warmup} warm-ups")
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8xint8->int32, f32 combine", "data": "synthetic",
             "impl": "reference", "config": workload(args),
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": ro.THREADS, "kind": "port",
+                             "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -402,9 +426,15 @@ def main():
         return float(t.item())
 
     # Warm-up, then K device-timed steps (graph replays at position ctx).
+    # Starting the clock sampler takes a while and not the same on every
+    # rank, so inside its context one more untimed replay (whose gathers
+    # align the ranks) and a barrier come directly before the timed ones.
     dm.model.bench(pos, max(3, args.warmup))
     barrier()
     with Clocks(local) as clk:
+        barrier()
+        dm.model.bench(pos, 1)
+        barrier()
         ms = dm.model.bench(pos, args.steps)
         barrier()
     clocks = clk.summary()
@@ -440,11 +470,15 @@ def main():
     traffic = ratio * prof.matvec_bytes / prof.matvec_launches if ratio and prof.matvec_launches else None
     # Sequences decoded at once: one sharded over all GPUs, or one per replica.
     seqs = 1 if sharded else world
+    parity = None
+    if world > 1:
+        _, lg = dm.model.step(tok, pos)
+        parity = parity_vs_1gpu(args, dev, c, lg, rank, local, dist, torch)
     if rank == 0:
         cfg = workload(args)
-        cfg["parallelism"] = f"rows{world}" if sharded else (f"replicas{world}" if world > 1 else "none")
+        par = {"mode": f"rows{world}" if sharded else (f"replicas{world}" if world > 1 else "none")}
         if sharded:
-            cfg["gathers"] = "fused (tagged words stored over NVLink)" if dm.stage.fused_gathers() else "NCCL all-gather"
+            par["gathers"] = "fused (tagged words stored over NVLink)" if dm.stage.fused_gathers() else "NCCL all-gather"
         line = {
             "metric": METRIC, "value": seqs * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -462,7 +496,10 @@ def main():
             "cpu_baseline": baseline,
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
+            "parallel": par,
         }
+        if parity is not None:
+            line["parity_vs_1gpu"] = parity
         print(json.dumps(line), flush=True)
     dm.free()
     if group:
@@ -471,6 +508,38 @@ def main():
     dev.close()
     if dist:
         dist.destroy_process_group()
+    if parity is False:
+        sys.exit(3)
+
+
+def parity_vs_1gpu(args, dev, c, logits, rank, local, dist, torch):
+    """After the timed region: the logits of one step at the bench position
+    on every rank (None on a rank that has none) against the same step of an
+    unsharded model built on rank 0's GPU (the one-GPU model is the one the
+    parity tests check against the oracle). Every rank returns the verdict:
+    True if all ranks' logits equal it bit for bit."""
+    import numpy as np
+    import synth
+    got = [None] * dist.get_world_size()
+    dist.all_gather_object(got, None if logits is None else np.asarray(logits, np.float32))
+    ok = [True]
+    if rank == 0:
+        ref = synth.DeviceModel(dev, c, SEED, ctx=args.ctx + 64)
+        try:
+            ref.stage.fill_cache(args.ctx, SEED)
+            _, want = ref.model.step(1, args.ctx)
+        finally:
+            ref.free()
+        want = np.asarray(want, np.float32).view(np.uint32)
+        have = [g for g in got if g is not None]
+        ok[0] = bool(have) and all(np.array_equal(g.view(np.uint32), want) for g in have)
+        if not ok[0]:
+            print(json.dumps({"parity_vs_1gpu": False,
+                              "ranks_differing": [i for i, g in enumerate(got) if g is not None
+                                                  and not np.array_equal(g.view(np.uint32), want)]}),
+                  file=sys.stderr, flush=True)
+    dist.broadcast_object_list(ok, src=0)
+    return bool(ok[0])
 
 
 def run_pipeline(args, world, rank, local, dist, torch):
@@ -506,6 +575,9 @@ def run_pipeline(args, world, rank, local, dist, torch):
     pr.pipeline.bench(pos, max(3, args.warmup))
     barrier()
     with Clocks(local) as clk:
+        barrier()
+        pr.pipeline.bench(pos, 1)
+        barrier()
         ms = pr.pipeline.bench(pos, args.steps)
         barrier()
     clocks = clk.summary()
@@ -518,16 +590,18 @@ def run_pipeline(args, world, rank, local, dist, torch):
         pr.pipeline.step(tok, pos)
     barrier()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / args.steps)
+    _, lg = pr.pipeline.step(tok, pos)
+    parity = parity_vs_1gpu(args, dev, c, lg, rank, local, dist, torch)
     if rank == 0:
         cfg = workload(args)
-        cfg["parallelism"] = f"pipeline{world}"
-        cfg["stages"] = [[a, b] for _, a, b in spans]
+        par = {"mode": f"pipeline{world}", "stages": [[a, b] for _, a, b in spans]}
         line = {
             "metric": METRIC, "value": 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8xint8->int32, f32 combine", "data": "synthetic", "config": cfg,
             "e2e": {"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
-            "roofline": None, "cpu_baseline": None, "clocks": clocks,
+            "roofline": None, "cpu_baseline": None, "clocks": clocks, "parallel": par,
+            "parity_vs_1gpu": parity,
         }
         print(json.dumps(line), flush=True)
     pr.free()
@@ -535,6 +609,8 @@ def run_pipeline(args, world, rank, local, dist, torch):
     group.free()
     dev.close()
     dist.destroy_process_group()
+    if not parity:
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -122,7 +122,10 @@ int rk_mulvecs(int n, rk_matrix *const *ms, float *const *outs, const float *x);
 
 /* out_dev[rows] = m·x_dev[cols] for a Q8_0 or Q4_0 matrix, with x_dev and
  * out_dev device buffers the caller owns, enqueued on `stream` (a
- * cudaStream_t; NULL: the device's own stream) and waited for. No
+ * cudaStream_t; NULL: the device's own stream). The call is synchronous:
+ * it waits for the product on that stream, then reads the device's error
+ * word, before it returns; it holds the device's mutex throughout, like
+ * every other entry point. No
  * counterpart in the reference: it exists for callers that cannot let the
  * library allocate device memory during the call — a node that reserves its
  * whole GPU memory up front for weights, caches and buffers, a worker

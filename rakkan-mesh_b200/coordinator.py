@@ -77,15 +77,26 @@ def run_stage(st, xs, pos, place, others=()):
         return np.ascontiguousarray(out, dtype=np.float32).reshape(xs.shape)
 
 
-def generate(stages, embed, logits_of, prompt, max_tokens, place, stop=()):
+def generate(stages, embed, logits_of, prompt, max_tokens, place, stop=(), seq_len=None):
     """Service.Generate's loop without a draft (generate.go:511-586):
     embed(tokens) -> rows, logits_of(row) -> logits; the prompt through
     every stage in one pass, then one token per pass, the next token the
     first strict maximum of the logits (Sampler.Sample at temperature 0,
-    sample.go:45-53). Returns (new tokens, stats)."""
+    sample.go:45-53). Returns (new tokens, stats).
+
+    seq_len is the stages' context (positions their caches hold). As in
+    generate.go:442-450, a prompt that fills it is refused, and max_tokens
+    is clamped to the positions left (max_tokens <= 0: all of them), so a
+    run ends at the context instead of passing a position the stages
+    cannot hold (which would read as a node failure)."""
     tokens = list(prompt)
     if not tokens:
         raise ValueError("empty prompt")
+    if seq_len is not None:
+        if len(tokens) >= seq_len:
+            raise ValueError(f"prompt of {len(tokens)} tokens fills the context of {seq_len}")
+        left = seq_len - len(tokens)
+        max_tokens = min(max_tokens, left) if max_tokens > 0 else left
     stats = {"passes": 0, "tokens": 0, "failovers": 0}
     pos, out = 0, []
     xs = embed(tokens)

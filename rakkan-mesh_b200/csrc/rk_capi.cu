@@ -3238,6 +3238,15 @@ int internal_matrix_view(const rk_matrix *m, int *device, int *rows, int *cols, 
   *sms = m->d->sms;
   return RK_OK;
 }
+
+// The matrix's device mutex, held by rk_matrix_mulvec_noalloc for its whole
+// call as every other entry point holds it.
+void internal_device_lock(const rk_matrix *m) { m->d->mu.lock(); }
+void internal_device_unlock(const rk_matrix *m) { m->d->mu.unlock(); }
+
+// Reads and clears the device error word, with check_dev_err's mapping of
+// the word to a status (call with the device mutex held, after a sync).
+int internal_check_dev_err(const rk_matrix *m) { return check_dev_err(m->d); }
 }  // namespace rk
 
 extern "C" int rk_sample_argmax(rk_device *d, const float *logits, int n, int *index) {

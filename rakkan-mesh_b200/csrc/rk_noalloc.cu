@@ -44,7 +44,21 @@ namespace rk {
 int internal_fail(int code, const char *msg);
 int internal_matrix_view(const rk_matrix *m, int *device, int *rows, int *cols, int *fmt, const void **w,
                          const float **scales, void **stream, int **err_word, int *sms);
+void internal_device_lock(const rk_matrix *m);
+void internal_device_unlock(const rk_matrix *m);
+int internal_check_dev_err(const rk_matrix *m);
 }  // namespace rk
+
+namespace {
+// Holds the matrix's device mutex for the whole call: the call shares the
+// device's stream (when given none) and its error word with every other
+// entry point on that device.
+struct DeviceLock {
+  const rk_matrix *m;
+  explicit DeviceLock(const rk_matrix *mm) : m(mm) { rk::internal_device_lock(m); }
+  ~DeviceLock() { rk::internal_device_unlock(m); }
+};
+}  // namespace
 
 // Looks up the scratch array's address on the current device (once).
 static int scratch_address(int device, void **out) {
@@ -80,6 +94,7 @@ extern "C" int rk_matrix_mulvec_noalloc(rk_matrix *m, const float *x_dev, float 
     snprintf(msg, sizeof msg, "noalloc: %d columns exceed the fixed scratch of %d (RK_NOALLOC_MAX_COLS)", cols, kMaxCols);
     return rk::internal_fail(RK_ERR_TOO_BIG, msg);
   }
+  DeviceLock lock(m);
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return rk::internal_fail(RK_ERR_CUDA, "noalloc: cudaSetDevice failed");
   void *base = nullptr;
@@ -115,12 +130,7 @@ extern "C" int rk_matrix_mulvec_noalloc(rk_matrix *m, const float *x_dev, float 
     snprintf(msg, sizeof msg, "noalloc: %s", cudaGetErrorString(e));
     return rk::internal_fail(RK_ERR_CUDA, msg);
   }
-  int word = 0;
-  e = cudaMemcpy(&word, err_word, sizeof word, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return rk::internal_fail(RK_ERR_CUDA, "noalloc: reading the device error word failed");
-  if (word != 0) {
-    cudaMemset(err_word, 0, sizeof(int));
-    return rk::internal_fail(RK_ERR_TIMEOUT, "noalloc: a kernel's bounded wait expired");
-  }
-  return RK_OK;
+  // The device error word, classified as every other entry point does
+  // (an expired bounded wait, or an index a kernel refused).
+  return rk::internal_check_dev_err(m);
 }

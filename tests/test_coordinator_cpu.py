@@ -120,3 +120,31 @@ def test_first_max_is_the_samplers_rule():
     assert co.first_max([np.nan, 5.0, 6.0]) == 0
     assert co.first_max([1.0, np.nan, 0.5]) == 0
     assert co.first_max([-np.inf, 2.0, np.nan, 2.0]) == 1
+
+
+def test_generation_stops_at_the_context():
+    """generate.go:442-450: a prompt that fills the context is refused, and
+    max_tokens is clamped to the positions the stages hold, so the run ends
+    cleanly instead of passing the context (which a stage refuses and the
+    loop would take for a node failure)."""
+    embed, logits = model()
+    stages, place, calls = pipeline()
+    with pytest.raises(ValueError, match="fills the context"):
+        co.generate(stages, embed, logits, [1, 7, 2, 9], 5, place, seq_len=4)
+
+    class Bounded(FakeStage):
+        def forward(self, xs, pos):
+            if pos + len(np.asarray(xs).reshape(-1, DIM)) > 10:
+                raise RuntimeError("position past the context")
+            return super().forward(xs, pos)
+
+    calls = [0]
+    stages = [co.PlannedStage(3 * i, 3 * i + 3, i, Bounded(i, calls)) for i in range(3)]
+    got, stats = co.generate(stages, embed, logits, [1, 7, 2, 9], 100, place, seq_len=10)
+    want, _ = run(n=6)
+    assert len(got) == 6 and got == want and stats["failovers"] == 0
+    # max_tokens <= 0 means every position left.
+    calls = [0]
+    stages = [co.PlannedStage(3 * i, 3 * i + 3, i, Bounded(i, calls)) for i in range(3)]
+    got, _ = co.generate(stages, embed, logits, [1, 7, 2, 9], 0, place, seq_len=10)
+    assert got == want
