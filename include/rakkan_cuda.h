@@ -98,6 +98,17 @@ int rk_device_best(int *index);                      /* gpu.Best, device.go:182-
 int rk_device_open(int index, rk_device **out);      /* gpu.Open, device.go:238-279 */
 void rk_device_close(rk_device *d);                  /* Device.Close, device.go:345 */
 int64_t rk_device_used(rk_device *d);                /* Device.Used, device.go:338-342 */
+/* Failure-path self-test (no reference counterpart: the reference's GPU
+ * waits are Vulkan fences, device.go:491-503). Every device-side wait in
+ * this library is bounded: on expiry the kernel sets the device's error
+ * word and ends, and the call that ran it returns RK_ERR_TIMEOUT. This runs
+ * both kinds of wait where nothing will complete them — the chained
+ * product waiting for tagged input words no producer writes (a peer that
+ * stopped mid-step), and an mbarrier waiting for copy bytes that never come
+ * — each limited to limit_ns (1 ns .. 10 s). Returns RK_ERR_TIMEOUT when
+ * both expired and reported as designed (RK_ERR_STATE if one did not); the
+ * device stays usable. */
+int rk_device_wait_selftest(rk_device *d, int64_t limit_ns);
 
 /* ---- Matrices: Device.Upload, Matrix.{MulVec, Free, Bytes}, MulVecs,
  *      SameDevice (device.go:585-793) ---- */

@@ -225,6 +225,65 @@ extern "C" void rk_device_close(rk_device *d) {
 
 extern "C" int64_t rk_device_used(rk_device *d) { return d ? d->used : 0; }
 
+// Runs each kind of bounded device wait where nothing completes it, with a
+// limit of limit_ns: the chained product kernel waiting for tagged input
+// words that no producer writes (what a rank sees when a peer stops
+// mid-step), and an mbarrier waiting for copy bytes that never come. Each
+// must give up, set the device's error word and end its kernel; the call
+// then reports that as any expired wait is reported (RK_ERR_TIMEOUT, the
+// word cleared), and the device stays usable.
+extern "C" int rk_device_wait_selftest(rk_device *d, int64_t limit_ns) {
+  if (!d || limit_ns <= 0 || limit_ns > 10000000000LL) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(d);
+  int rc = set_device(d);
+  if (rc) return rc;
+  // A product of sms rows × 32 columns of zero Q8_0 weights whose input is
+  // 32 tagged words that stay at tag 0, while the wait expects epoch 1's.
+  const int rows = d->sms, cols = 32;
+  const size_t wbytes = (size_t)rows * cols, sbytes = 4 * (size_t)rows, lbytes = 8 * (size_t)cols;
+  const size_t off_s = (wbytes + 255) & ~size_t(255), off_ll = off_s + ((sbytes + 255) & ~size_t(255));
+  const size_t off_epoch = off_ll + lbytes, off_out = off_epoch + 16, total = off_out + 4 * (size_t)rows;
+  char *buf = nullptr;
+  CK(cudaMalloc(&buf, total));
+  cudaError_t e = cudaMemsetAsync(buf, 0, total, d->st);
+  const unsigned one = 1;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(buf + off_epoch, &one, 4, cudaMemcpyHostToDevice, d->st);
+  ChainArgs ca{};
+  MvArgs &a = ca.step[0];
+  a.fmt = FMT_Q8_0;
+  a.cols = cols;
+  a.epi = EPI_STORE;
+  a.err = d->err_dev;
+  a.part[0].w = (const uint8_t *)buf;
+  a.part[0].s = (const float *)(buf + off_s);
+  a.part[0].out = (float *)(buf + off_out);
+  a.part[0].rows = rows;
+  a.nparts = 1;
+  a.pro = PRO_QUANT;
+  a.wait.ll = (const unsigned long long *)(buf + off_ll);
+  a.wait.epoch = (const unsigned *)(buf + off_epoch);
+  a.wait.slot = 0;
+  a.wait.nslots = 1;
+  ca.nsteps = 1;
+  ca.wait_ns = (unsigned long long)limit_ns;
+  if (e == cudaSuccess) e = launch_matvec_chain(ca, d->sms, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  int gather_word = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&gather_word, d->err_dev, sizeof gather_word, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, sizeof(int));
+  if (e == cudaSuccess) e = launch_mbar_wait_selftest(d->err_dev, (unsigned long long)limit_ns, d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  int mbar_word = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&mbar_word, d->err_dev, sizeof mbar_word, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemset(d->err_dev, 0, sizeof(int));
+  cudaFree(buf);
+  if (e != cudaSuccess) return cuda_fail(e, "wait self-test");
+  if (gather_word != DEV_ERR_TIMEOUT || mbar_word != DEV_ERR_TIMEOUT)
+    return fail(RK_ERR_STATE, "wait self-test: a wait did not report its expiry (gather word %d, mbarrier word %d)",
+                gather_word, mbar_word);
+  return fail(RK_ERR_TIMEOUT, "wait self-test: both bounded waits expired and reported (as designed)");
+}
+
 // ---------------------------------------------------------------------------
 // Groups: one NCCL communicator per process (one process per GPU), for the
 // row-sharded stage and head. NCCL is loaded when the first group is made,
@@ -470,6 +529,19 @@ static cudaError_t launch_mv(rk_device *d, const MvArgs &a, cudaStream_t st) {
   if (e == cudaSuccess) e = cudaEventCreate(&pl.e1);
   if (e == cudaSuccess) e = cudaEventRecord(pl.e0, st);
   if (e == cudaSuccess) e = launch_matvec(a, d->sms, st);
+  if (e == cudaSuccess) e = cudaEventRecord(pl.e1, st);
+  g_prof->push_back(pl);
+  return e;
+}
+
+static cudaError_t launch_chain(rk_device *d, const ChainArgs &ca, cudaStream_t st) {
+  if (!g_prof) return launch_matvec_chain(ca, d->sms, st);
+  ProfLaunch pl{};
+  for (int k = 0; k < ca.nsteps; k++) pl.bytes += algorithmic_bytes(ca.step[k]);
+  cudaError_t e = cudaEventCreate(&pl.e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&pl.e1);
+  if (e == cudaSuccess) e = cudaEventRecord(pl.e0, st);
+  if (e == cudaSuccess) e = launch_matvec_chain(ca, d->sms, st);
   if (e == cudaSuccess) e = cudaEventRecord(pl.e1, st);
   g_prof->push_back(pl);
   return e;
@@ -1246,6 +1318,11 @@ struct rk_stage {
   // words: value and tag) and the step epoch live in one allocation
   // `xbase`, mapped by every peer through CUDA IPC.
   int p2p = 0;
+  // Chained products (k_matvec_chain): each layer's Wo, W1·W3, W2 and the
+  // next layer's Q/K/V in one launch, handing their outputs on through the
+  // tagged copies in `xbase` (on one GPU too, where the only peer is this
+  // GPU). Decided when the step graph is recorded.
+  int chain = 0;
   char *xbase = nullptr;
   size_t off_xll = 0, off_attll = 0, off_hbll = 0, off_epoch = 0;
   char *peer_base[kMaxPeers] = {};  // by rank; this rank's entry is xbase
@@ -1383,7 +1460,8 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   // their own input, the single-kernel attention); the last layer's x
   // stays an NCCL all-gather, so whatever reads the stage's output reads
   // plain floats.
-  unsigned *epoch = s->p2p ? (unsigned *)(s->xbase + s->off_epoch) : nullptr;
+  auto epoch_of = [](rk_stage *st_) { return (unsigned *)(st_->xbase + st_->off_epoch); };
+  unsigned *epoch = epoch_of(s);
   const int nslots = 4 * (int)s->layers.size();
   // The tagged copy of a vector (off_ll: its offset in the block) from
   // element `elem` on, in every rank's memory.
@@ -1440,6 +1518,134 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
     }
     return enqueue_matvecs(d, n, ms, outs, in, nullptr, nullptr, nullptr, epi, st);
   };
+  // ---- Chained products: per layer the attention, then one launch of Wo,
+  // W1·W3, W2 and the next layer's Q/K/V (layer 0's Q/K/V alone first).
+  // Each step's output reaches the next through the tagged copies in the
+  // stage's block (every rank's, when sharded). ----
+  const int L = (int)s->layers.size();
+  auto qkv_step = [&](int li, const GatherWait *w) {
+    rk_layer *l = s->layers[li];
+    MvArgs a{};
+    a.fmt = l->wq->fmt;
+    a.cols = D;
+    a.epi = EPI_STORE;
+    a.err = d->err_dev;
+    a.part[0] = part_of(l->wq, s->q);
+    a.part[1] = part_of(l->wk, s->k);
+    a.part[2] = part_of(l->wv, s->v);
+    a.nparts = 3;
+    a.pro = PRO_NORM_QUANT;
+    a.x = s->x;
+    a.norm_w = l->vecs->v + l->o_rms_att;
+    a.recipN = recipD;
+    a.eps = eps;
+    if (w) a.wait = *w;
+    return a;
+  };
+  // The chain after layer li's attention; ok=false when some product
+  // cannot take part.
+  auto layer_chain = [&](int li, bool *ok) {
+    rk_layer *l = s->layers[li];
+    const float *vec = l->vecs->v;
+    const int sl = 4 * li;
+    const bool f_att = G > 1;
+    ChainArgs ca{};
+    MvArgs &wo = ca.step[0];
+    wo.fmt = l->wo->fmt;
+    wo.cols = qd;
+    wo.epi = EPI_ADD;
+    wo.err = d->err_dev;
+    wo.part[0] = part_of(l->wo, s->x + r0);
+    wo.nparts = 1;
+    wo.pro = PRO_QUANT;
+    wo.x = s->att_out;
+    if (f_att) wo.wait = wait_for(sl, s->off_attll);
+    wo.put = put_for(sl + 1, s->off_xll, r0);
+    MvArgs &ff = ca.step[1];
+    ff.fmt = l->w1->fmt;
+    ff.cols = D;
+    ff.epi = EPI_SILU;
+    ff.err = d->err_dev;
+    ff.part[0] = part_of(l->w1, s->hb + rH0);
+    ff.part[1] = part_of(l->w3, s->hb2 + rH0);
+    ff.nparts = 2;
+    ff.pro = PRO_NORM_QUANT;
+    ff.x = s->x;
+    ff.norm_w = vec + l->o_rms_ffn;
+    ff.recipN = recipD;
+    ff.eps = eps;
+    ff.wait = wait_for(sl + 1, s->off_xll);
+    ff.put = put_for(sl + 2, s->off_hbll, rH0);
+    MvArgs &w2 = ca.step[2];
+    w2.fmt = l->w2->fmt;
+    w2.cols = H;
+    w2.epi = EPI_ADD_CANON;
+    w2.err = d->err_dev;
+    w2.part[0] = part_of(l->w2, s->x + r0);
+    w2.nparts = 1;
+    w2.pro = PRO_QUANT;
+    w2.x = s->hb;
+    w2.wait = wait_for(sl + 2, s->off_hbll);
+    ca.nsteps = 3;
+    if (li + 1 < L) {
+      w2.put = put_for(sl + 3, s->off_xll, r0);
+      const GatherWait wx = wait_for(sl + 3, s->off_xll);
+      ca.step[3] = qkv_step(li + 1, &wx);
+      ca.nsteps = 4;
+    }
+    // One format throughout; the W3 rows pair with W1's.
+    *ok = l->w3->fmt == l->w1->fmt && matvec_chain_ok(ca, d->sms);
+    for (int k = 0; k < ca.nsteps && *ok; k++)
+      for (int p = 1; p < ca.step[k].nparts; p++) *ok = *ok && ca.step[k].part[p].rows > 0;
+    if (li + 1 < L) {
+      rk_layer *n = s->layers[li + 1];
+      *ok = *ok && n->wk->fmt == n->wq->fmt && n->wv->fmt == n->wq->fmt;
+    }
+    return ca;
+  };
+  // Chains need the tagged copies on every rank: always on one GPU, and
+  // with the fused gathers (peer memory mapped) when sharded; the
+  // attention output of a sharded stage arrives as tagged words too.
+  const char *chain_env = getenv("RK_CHAIN");
+  bool chain = L > 0 && (G == 1 || (s->p2p && s->v_pitch > 0)) && chain_env && strcmp(chain_env, "1") == 0;
+  if (chain) {
+    ChainArgs first{};
+    first.step[0] = qkv_step(0, nullptr);
+    first.nsteps = 1;
+    rk_layer *l0 = s->layers[0];
+    chain = matvec_chain_ok(first, d->sms) && l0->wk->fmt == l0->wq->fmt && l0->wv->fmt == l0->wq->fmt;
+    for (int li = 0; li < L && chain; li++) {
+      bool ok = false;
+      layer_chain(li, &ok);
+      chain = ok;
+    }
+    if (chain && G > 1) {
+      // The sharded attention must store its output as tagged words.
+      for (int li = 0; li < L && chain; li++) chain = fusable(s->layers[li]->wo, s->layers[li]->wo, qd, false);
+    }
+  }
+  s->chain = chain ? 1 : 0;
+  if (chain) {
+    if (!s->p2p) CK(launch_k(k_epoch, 1, 32, 0, st, epoch_of(s)));
+    ChainArgs first{};
+    first.step[0] = qkv_step(0, nullptr);
+    first.nsteps = 1;
+    CK(launch_chain(d, first, st));
+    for (int li = 0; li < L; li++) {
+      QkvPostArgs qp;
+      AttnArgs at;
+      attention_args(s, li, s->q, s->k, s->v, s->att_out + h0 * hs, s->pos_dev, &qp, &at);
+      if (G > 1) at.put = put_for(4 * li, s->off_attll, (size_t)h0 * hs);
+      CK(launch_attention_post(qp, at, st));
+      bool ok = false;
+      const ChainArgs ca = layer_chain(li, &ok);
+      CK(launch_chain(d, ca, st));
+    }
+    // A sharded stage's output x: every rank's rows, for whatever reads it.
+    if (G > 1) return gather(s->x, D);
+    return RK_OK;
+  }
+
   for (size_t li = 0; li < s->layers.size(); li++) {
     rk_layer *l = s->layers[li];
     const float *vec = l->vecs->v;
@@ -1793,8 +1999,9 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     if ((rc = A((bytes), &p))) goto fail_;    \
     s->field = (decltype(s->field))p;         \
   } while (0)
-  if (G > 1) {
-    // The gathered activations, their tagged copies and the epoch in one block.
+  {
+    // The gathered (or chained) activations, their tagged copies and the
+    // epoch in one block.
     auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
     const size_t ox = 0, oatt = ox + a16(4 * (size_t)D), ohb = oatt + a16(4 * (size_t)qd);
     s->off_xll = ohb + a16(4 * (size_t)H);
@@ -1806,10 +2013,9 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     s->x = (float *)(s->xbase + ox);
     s->att_out = (float *)(s->xbase + oatt);
     s->hb = (float *)(s->xbase + ohb);
-  } else {
-    ALLOC(x, 4 * (size_t)D);
-    ALLOC(att_out, 4 * (size_t)qd);
-    ALLOC(hb, 4 * (size_t)H);
+    // (stage_alloc zeroes it: tags of epoch 0, which no step uses, since
+    // the step graph advances the epoch first.)
+    s->peer_base[s->rank] = s->xbase;
   }
   ALLOC(xb, 4 * (size_t)D);
   ALLOC(q, 4 * (size_t)(qd / G));

@@ -221,13 +221,18 @@ RK_DEV unsigned long long ll_load(const unsigned long long *p) {
   return w;
 }
 
+// How long a device-side wait spins before it gives up and reports
+// DEV_ERR_TIMEOUT (nanoseconds of %globaltimer). A kernel that takes a limit
+// as an argument uses that instead; 0 there means this default.
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+
 // Copies n gathered floats into shared memory `dst`, each once its word
 // carries `tag` (all threads; then a CTA barrier). false when a word has
-// not arrived after about a second.
-RK_DEV bool ll_gather_load(const unsigned long long *ll, int n, unsigned tag, float *dst) {
-  __shared__ int s_bad;
-  if (threadIdx.x == 0) s_bad = 0;
-  __syncthreads();
+// not arrived within limit_ns (0: kWaitLimitNs). The verdict is combined by
+// the barrier itself, so the function may be called again at once.
+RK_DEV bool ll_gather_load(const unsigned long long *ll, int n, unsigned tag, float *dst,
+                           unsigned long long limit_ns = 0) {
+  if (limit_ns == 0) limit_ns = kWaitLimitNs;
   const uint64_t t0 = globaltimer_ns();
   bool ok = true;
   // Eight words in flight per thread; a word that has not arrived is
@@ -244,15 +249,13 @@ RK_DEV bool ll_gather_load(const unsigned long long *ll, int n, unsigned tag, fl
       const int i = i0 + u * blockDim.x;
       if (i >= n) continue;
       while ((unsigned)(w[u] >> 32) != tag && ok) {
-        if (globaltimer_ns() - t0 > 1000000000ull) ok = false;
+        if (globaltimer_ns() - t0 > limit_ns) ok = false;
         else w[u] = ll_load(ll + i);
       }
       dst[i] = u2f((uint32_t)w[u]);
     }
   }
-  if (!ok) s_bad = 1;
-  __syncthreads();
-  return s_bad == 0;
+  return __syncthreads_or(!ok) == 0;
 }
 
 // Whether launches on this host thread use programmatic dependent launch

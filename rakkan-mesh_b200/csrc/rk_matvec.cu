@@ -17,6 +17,7 @@
 // is exactly qrow's lane order, and at the end of the row combine8 gives
 // the reference's bits. The integer part is order-free, so only those 8
 // serial f32 chains per row are ordered.
+#include <algorithm>
 #include <cstdlib>
 
 #include "rk_common.cuh"
@@ -72,12 +73,29 @@ RK_DEV void stage_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // PITCHED: block b's scale goes to xs[b·xs_pitch] (a block-major scale
 // array shared by many vectors) instead of xs[b].
+//
+// With `ll`, x's values come from tagged words instead (a gathered input:
+// ll_gather_load of each chunk, waiting up to limit_ns for `tag`; a word
+// that does not arrive sets *err to DEV_ERR_TIMEOUT and the stale value is
+// used, so the kernel still ends).
 template <bool NORM, bool PITCHED = false>
 RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__restrict__ w, float recipN, float eps,
                            int8_t *qx, float *xs, int *xsum, float *s_inv, float *stage, float *wstage,
-                           int stage_floats, bool preloaded, int xs_pitch = 1) {
+                           int stage_floats, bool preloaded, int xs_pitch = 1,
+                           const unsigned long long *ll = nullptr, unsigned tag = 0, int *err = nullptr,
+                           unsigned long long limit_ns = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool single = n <= stage_floats;
+  // One chunk of x (and of w) into the staging areas.
+  auto stage_load = [&](const float *xx, const float *ww, int c0, int m, float *st, float *wst) {
+    if (ll) {
+      rk::stage_load(nullptr, ww, c0, m, st, wst);
+      if (!ll_gather_load(ll + c0, m, tag, st, limit_ns) && threadIdx.x == 0 && err)
+        atomicExch(err, DEV_ERR_TIMEOUT);
+    } else {
+      rk::stage_load(xx, ww, c0, m, st, wst);
+    }
+  };
   float inv = 0.0f;
   if (NORM) {
     float s = 0.0f;
@@ -260,13 +278,14 @@ RK_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the barrier's phase `parity` to complete, for at most ~1 s.
-RK_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Waits for the barrier's phase `parity` to complete, for at most limit_ns
+// (kWaitLimitNs, about a second, by default).
+RK_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > 1000000000ull) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -636,6 +655,281 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_matvec_q(const MvArgs a, int 
 }
 
 // ---------------------------------------------------------------------------
+// A chain of products in one launch (the products of a layer between two
+// attentions: Wo, W1·W3, W2 and the next layer's Q/K/V).
+//
+// Every product of a decode step needs the whole output of the one before,
+// so as separate launches each pays a launch, a prologue (input staged,
+// normalised and quantized) and a tail in which the SMs' weight streams run
+// dry, four times per layer. Here one persistent CTA per SM runs the steps
+// in order, and the weight rings run on across step boundaries: a warp's
+// producer lane issues the next step's segments as soon as it has issued
+// its last one of the current step, since weights depend on no step's
+// output. A step's output reaches the next step as tagged 8-byte words
+// (value and tag, the row-sharded gathers' protocol; on one GPU the only
+// "peer" is the GPU itself), so the next step's prologue waits for the
+// words it reads, not for a kernel boundary. The rows of every step are
+// split over the warps exactly as k_matvec_q splits them, so each output
+// element's arithmetic is k_matvec_q's (bits equal to num.MatVecQ8/Q4).
+//
+// A step's EPI_ADD / EPI_ADD_CANON reads its own output rows before it
+// writes them; when an earlier step of the chain wrote those rows (W2 after
+// Wo, both adding into x), the two steps have the same row count, so row r
+// is computed by the same thread in both and the read sees the write.
+// ---------------------------------------------------------------------------
+__host__ __device__ inline long long step_units(const MvArgs &a) {
+  if (a.epi == EPI_SILU) return a.part[0].rows;
+  long long u = 0;
+  for (int p = 0; p < a.nparts; p++) u += a.part[p].rows;
+  return u;
+}
+
+// This warp's units [u0, u1) of a step, and its segments per unit.
+struct StepSpan {
+  long long u0, u1;
+  int nsub, nseg;
+  RK_DEV long long segments() const { return (u1 - u0) * nsub * nseg; }
+};
+
+template <int FMT>
+RK_DEV StepSpan step_span(const MvArgs &a, long long gw, long long G) {
+  using T = QTraits<FMT>;
+  StepSpan sp;
+  const long long units = step_units(a);
+  sp.u0 = units * gw / G;
+  sp.u1 = units * (gw + 1) / G;
+  sp.nsub = a.epi == EPI_SILU ? 2 : 1;
+  sp.nseg = ((a.cols >> 5) + T::kSegBlocks - 1) / T::kSegBlocks;
+  return sp;
+}
+
+// Shared-memory layout of a chain CTA (host and device agree on it).
+struct ChainSmem {
+  int in_off, xs_off, xsum_off, stage_off, wstage_off, ring_off, total;
+};
+template <int FMT, int WARPS, int SLOTS>
+__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf) {
+  ChainSmem m;
+  const int nb = max_cols / 32;
+  m.in_off = WARPS * SLOTS * 8;
+  m.xs_off = m.in_off + ((max_cols + 15) & ~15);
+  m.xsum_off = m.xs_off + ((nb * 4 + 15) & ~15);
+  m.stage_off = m.xsum_off + ((nb * 4 + 15) & ~15);
+  m.wstage_off = m.stage_off + 4 * sf;
+  m.ring_off = m.wstage_off + 4 * wsf;
+  m.total = m.ring_off + WARPS * SLOTS * slot_bytes<FMT>();
+  return m;
+}
+
+template <int FMT, int WARPS, int SLOTS>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf) {
+  using T = QTraits<FMT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ns = ca.nsteps;
+  const ChainSmem L = chain_smem<FMT, WARPS, SLOTS>(max_cols, sf, wsf);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+  int8_t *sqx = reinterpret_cast<int8_t *>(smem + L.in_off);
+  float *sxs = reinterpret_cast<float *>(smem + L.xs_off);
+  int *sxsum = reinterpret_cast<int *>(smem + L.xsum_off);
+  float *stage = reinterpret_cast<float *>(smem + L.stage_off);
+  float *wstage = reinterpret_cast<float *>(smem + L.wstage_off);
+  uint8_t *ring = smem + L.ring_off + warp * SLOTS * slot_bytes<FMT>();
+  const long long gw = (long long)blockIdx.x * WARPS + warp, G = (long long)gridDim.x * WARPS;
+  const long long cw0 = (long long)blockIdx.x * WARPS, cw1 = cw0 + WARPS;  // this CTA's warps
+  const uint32_t bar0 = smem_addr(bars + warp * SLOTS);
+  const unsigned long long limit = ca.wait_ns ? ca.wait_ns : kWaitLimitNs;
+  int *err = ca.step[0].err;
+
+  // The producer (lane 0): step pk, its cursor, segments left in it.
+  uint64_t pol = 0;
+  int pk = 0, pslot = 0;
+  long long pleft = 0;
+  StepSpan psp{};
+  Cursor pc{};
+  auto seek = [&]() {  // from step pk on, the first step with segments for this warp
+    for (; pk < ns; pk++) {
+      psp = step_span<FMT>(ca.step[pk], gw, G);
+      pleft = psp.segments();
+      if (pleft > 0) {
+        cursor_init(pc, ca.step[pk], psp.nsub, psp.u0);
+        return;
+      }
+    }
+  };
+  if (lane == 0) {
+    for (int k = 0; k < SLOTS; k++) mbar_init(bar0 + 8 * k, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    pol = evict_first_policy();
+    seek();
+  }
+  __syncwarp();
+  auto issue = [&]() {
+    if (pk >= ns) return;
+    const MvArgs &a = ca.step[pk];
+    const SegInfo sg = seg_info<FMT>(a, a.cols >> 5, pc);
+    uint8_t *dst = ring + pslot * slot_bytes<FMT>();
+    const uint32_t bar = bar0 + 8 * pslot;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
+    bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
+    bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
+    pslot = pslot + 1 == SLOTS ? 0 : pslot + 1;
+    if (--pleft > 0) {
+      cursor_next(pc, a, psp.nsub, psp.nseg);
+    } else {
+      pk++;
+      seek();
+    }
+  };
+
+  // Weights are read by no step's predecessor as output: the first slots
+  // are filled before the predecessor kernel has finished, together with
+  // the first step's norm weights.
+  griddep_trigger();
+  if (lane == 0)
+    for (int k = 0; k < SLOTS; k++) issue();
+  {
+    const MvArgs &a = ca.step[0];
+    if (a.pro == PRO_NORM_QUANT && a.cols <= sf && !a.wait.ll) stage_load(nullptr, a.norm_w, 0, a.cols, stage, wstage);
+  }
+  griddep_wait();
+
+  int slot = 0;
+  uint32_t parity = 0;
+  bool dead = false;  // a segment's copy never landed: this warp stops
+  for (int k = 0; k < ns; k++) {
+    const MvArgs &a = ca.step[k];
+    const int cols = a.cols, nb = cols >> 5;
+    const long long units = step_units(a);
+    // ---- prologue: the step's input into shared memory as Q8_0 ----
+    __syncthreads();  // every warp is done with the previous step's input
+    const bool cta_has = units * cw0 / G < units * cw1 / G;
+    if (cta_has) {
+      const bool norm = a.pro == PRO_NORM_QUANT;
+      const unsigned wtag = a.wait.ll ? gather_tag(*a.wait.epoch, a.wait.slot, a.wait.nslots) : 0u;
+      const bool single = cols <= sf;
+      bool pre = false;
+      if (k == 0 && !a.wait.ll) {
+        // Plain input from the predecessor kernel (the first step only).
+        stage_load(a.x, nullptr, 0, min(cols, sf), stage, wstage);
+        pre = true;
+      } else if (single) {
+        if (norm) stage_load(nullptr, a.norm_w, 0, cols, stage, wstage);
+        if (!ll_gather_load(a.wait.ll, cols, wtag, stage, limit) && threadIdx.x == 0) atomicExch(err, DEV_ERR_TIMEOUT);
+        pre = true;
+      }
+      __shared__ float s_inv;
+      if (norm)
+        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage, sf, pre, 1,
+                             a.wait.ll, wtag, err, limit);
+      else
+        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sf, pre, 1,
+                              a.wait.ll, wtag, err, limit);
+      __syncthreads();
+    }
+    // ---- this warp's rows of the step ----
+    const StepSpan sp = step_span<FMT>(a, gw, G);
+    const long long total = sp.segments();
+    if (total == 0) continue;
+    const unsigned put_tag = a.put.nll > 0 ? gather_tag(*a.put.epoch, a.put.slot, a.put.nslots) : 0u;
+    Cursor cc;
+    cursor_init(cc, a, sp.nsub, sp.u0);
+    float acc = 0.0f, r0 = 0.0f;
+    for (long long j = 0; j < total; j++) {
+      if (!dead && !mbar_wait_bounded(bar0 + 8 * slot, parity, limit)) {
+        if (lane == 0) atomicExch(err, DEV_ERR_TIMEOUT);
+        // Give the other copies already issued a bounded chance to land.
+        int js = slot;
+        uint32_t jp = parity;
+        for (int q = 1; q < SLOTS; q++) {
+          js = js + 1 == SLOTS ? 0 : js + 1;
+          if (js == 0) jp ^= 1;
+          mbar_wait_bounded(bar0 + 8 * js, jp, limit);
+        }
+        dead = true;
+      }
+      if (!dead) {
+        const SegInfo sg = seg_info<FMT>(a, nb, cc);
+        const uint8_t *W = ring + slot * slot_bytes<FMT>();
+        const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
+        if (cc.sg == 0) acc = 0.0f;
+        const int nfull = sg.nblk >> 5;
+#pragma unroll 2
+        for (int c = 0; c < nfull; c++) {
+          const int bb = c * 32 + lane;
+          const float term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
+#pragma unroll
+          for (int q = 0; q < 4; q++) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q));
+        }
+        if (sg.nblk & 31) {
+          const int bb = nfull * 32 + lane;
+          float term = 0.0f;
+          if (bb < sg.nblk) term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float t = __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q);
+            if (nfull * 32 + (lane & 7) + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
+          }
+        }
+        if (cc.sg == sp.nseg - 1) {
+          const float r = combine8(acc);
+          if (lane == 0) {
+            float *out = a.part[cc.part].out;
+            float v = r;
+            bool put = true;
+            switch (a.epi) {
+              case EPI_STORE: break;
+              case EPI_ADD: v = __fadd_rn(out[cc.row], r); break;
+              case EPI_ADD_CANON: v = canonical(__fadd_rn(out[cc.row], r)); break;
+              case EPI_SILU:
+                if (cc.sub == 0) {
+                  r0 = r;
+                  put = false;
+                } else {
+                  v = __fmul_rn(silu(r0), r);
+                  out = a.part[0].out;
+                }
+                break;
+            }
+            if (put) {
+              out[cc.row] = v;
+              if (cc.part == 0 || a.epi == EPI_SILU)
+                for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + cc.row, v, put_tag);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && !dead) issue();
+      cursor_next(cc, a, sp.nsub, sp.nseg);
+      slot = slot + 1 == SLOTS ? 0 : slot + 1;
+      if (slot == 0) parity ^= 1;
+    }
+  }
+}
+
+// An mbarrier wait that nothing completes: the barrier expects 16 bytes of
+// asynchronous copies and none is issued. The wait gives up after limit_ns
+// and sets *err to DEV_ERR_TIMEOUT, as the product kernels' ring waits do
+// when a copy never lands; nothing is left in flight.
+__global__ void k_mbar_wait_selftest(int *err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_addr(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(b, 16);
+    if (!mbar_wait_bounded(b, 0, limit_ns)) atomicExch(err, DEV_ERR_TIMEOUT);
+  }
+}
+
+cudaError_t launch_mbar_wait_selftest(int *err, unsigned long long limit_ns, cudaStream_t st) {
+  return launch_k(k_mbar_wait_selftest, 1, 32, 0, st, err, limit_ns);
+}
+
+// ---------------------------------------------------------------------------
 // float32 / bfloat16 matvec (num.MatVec32 / MatVecBF16, matvec.go:106-123):
 // warp per row, lane j sums elements j, j+32, ... in order, then Dot32's
 // combination tree.
@@ -726,7 +1020,70 @@ cudaError_t init_matvec_attributes() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemLimit);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemLimit);
   return e;
+}
+
+// Staging of a chain: x in chunks of sf floats (the largest of 8192, 4096,
+// 2048 whose layout fits), the norm weights beside them for the steps that
+// normalise.
+static int chain_total(int fmt, int mc, int sf, int wsf) {
+  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0, kWarps, kSlots>(mc, sf, wsf).total
+                         : chain_smem<FMT_Q4_0, kWarps, kSlots>(mc, sf, wsf).total;
+}
+
+static void chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *wsf) {
+  int mc = 0;
+  for (int k = 0; k < ca.nsteps; k++) mc = std::max(mc, ca.step[k].cols);
+  int f = 0, wf = 0;
+  for (int cand : {8192, 4096, 2048}) {
+    f = std::min(mc, cand);
+    wf = 0;
+    for (int k = 0; k < ca.nsteps; k++)
+      if (ca.step[k].pro == PRO_NORM_QUANT) wf = std::max(wf, std::min(ca.step[k].cols, f));
+    if (ca.nsteps < 1 || chain_total(ca.step[0].fmt, mc, f, wf) <= kSmemLimit) break;
+  }
+  *max_cols = mc;
+  *sf = f;
+  *wsf = wf;
+}
+
+int matvec_chain_smem(const ChainArgs &ca) {
+  int mc, sf, wsf;
+  chain_dims(ca, &mc, &sf, &wsf);
+  if (ca.nsteps < 1) return 0;
+  return chain_total(ca.step[0].fmt, mc, sf, wsf);
+}
+
+bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
+  if (ca.nsteps < 1 || ca.nsteps > kChainMax) return false;
+  const int fmt = ca.step[0].fmt;
+  if (fmt != FMT_Q8_0 && fmt != FMT_Q4_0) return false;
+  for (int k = 0; k < ca.nsteps; k++) {
+    const MvArgs &a = ca.step[k];
+    if (a.fmt != fmt || a.cols <= 0 || a.cols % 32 || a.cols > kSmemColsMax) return false;
+    if (a.pro != PRO_QUANT && a.pro != PRO_NORM_QUANT) return false;
+    if (k > 0 && !a.wait.ll) return false;
+    // Every CTA that reads a step's input writes some of its output, which
+    // is what lets tagged buffers be reused without a barrier.
+    if (step_units(a) < num_sms) return false;
+  }
+  return matvec_chain_smem(ca) <= kSmemLimit;
+}
+
+cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t st) {
+  if (!matvec_chain_ok(ca, num_sms)) return cudaErrorInvalidValue;
+  int mc, sf, wsf;
+  chain_dims(ca, &mc, &sf, &wsf);
+  const int smem = matvec_chain_smem(ca);
+  if (ca.step[0].fmt == FMT_Q8_0)
+    return launch_k(k_matvec_chain<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem, st, ca, mc, sf, wsf);
+  return launch_k(k_matvec_chain<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem, st, ca, mc, sf, wsf);
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {

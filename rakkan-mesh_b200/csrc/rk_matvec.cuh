@@ -82,6 +82,19 @@ struct MvArgs {
 
 enum Prologue : int { PRO_GIVEN = 0, PRO_QUANT = 1, PRO_NORM_QUANT = 2 };
 
+// A chain of quantized products of one format in one launch
+// (k_matvec_chain): step k+1 reads step k's output through tagged words
+// (its `wait`, which step k's `put` fills); step 0 reads plain x after the
+// predecessor kernel, or tagged words. Every step quantizes its own input
+// (PRO_QUANT or PRO_NORM_QUANT). wait_ns bounds every wait (0: about a
+// second).
+constexpr int kChainMax = 4;
+struct ChainArgs {
+  MvArgs step[kChainMax];
+  int nsteps;
+  unsigned long long wait_ns;
+};
+
 // Widest input whose Q8_0 form a matvec CTA stages in shared memory.
 constexpr int kSmemColsMax = 32768;
 
@@ -95,6 +108,17 @@ cudaError_t launch_quantize_act(const float *x, int n, const float *w, float rec
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st);
 
 int matvec_smem_bytes(int fmt, int cols);
+
+// Whether launch_matvec_chain takes the chain (one format, fused
+// prologues, tagged inputs after the first step, at least num_sms units per
+// step, shared memory within the limit), and the chain's launch.
+bool matvec_chain_ok(const ChainArgs &ca, int num_sms);
+int matvec_chain_smem(const ChainArgs &ca);
+cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t st);
+
+// One mbarrier wait that nothing completes, bounded by limit_ns: sets *err
+// to DEV_ERR_TIMEOUT (the failure path's self-test).
+cudaError_t launch_mbar_wait_selftest(int *err, unsigned long long limit_ns, cudaStream_t st);
 
 // Whether a matvec of this format and width can quantize its input in its
 // own prologue (PRO_NORM_QUANT when norm, else PRO_QUANT): the input and its

@@ -24,7 +24,7 @@ NOALLOC_MAX_COLS = 32768
 # Every symbol include/rakkan_cuda.h declares.
 EXPORTS = [
     "rk_last_error", "rk_version", "rk_device_count", "rk_device_get_info", "rk_device_best", "rk_device_open",
-    "rk_device_close", "rk_device_used", "rk_matrix_upload", "rk_matrix_free", "rk_matrix_bytes", "rk_same_device",
+    "rk_device_close", "rk_device_used", "rk_device_wait_selftest", "rk_matrix_upload", "rk_matrix_free", "rk_matrix_bytes", "rk_same_device",
     "rk_matrix_mulvec", "rk_matrix_mulvec_many", "rk_mulvecs", "rk_matrix_mulvec_noalloc", "rk_vectors_upload", "rk_vectors_free", "rk_arena_new",
     "rk_arena_set_quant_scratch", "rk_arena_bytes", "rk_arena_free", "rk_batch_begin", "rk_batch_write",
     "rk_batch_read", "rk_batch_matvecs", "rk_batch_quantize", "rk_batch_rmsnorm", "rk_batch_addvec", "rk_batch_rope",
@@ -90,7 +90,7 @@ def lib():
         sig = {
             "rk_last_error": (C.c_char_p, []), "rk_version": (C.c_char_p, []),
             "rk_device_count": (i, [vp]), "rk_device_get_info": (i, [i, vp]), "rk_device_best": (i, [vp]),
-            "rk_device_open": (i, [i, vp]), "rk_device_close": (None, [vp]), "rk_device_used": (i64, [vp]),
+            "rk_device_open": (i, [i, vp]), "rk_device_close": (None, [vp]), "rk_device_used": (i64, [vp]), "rk_device_wait_selftest": (i, [vp, i64]),
             "rk_matrix_upload": (i, [vp, i, i, i, vp, vp, vp]), "rk_matrix_free": (None, [vp]),
             "rk_matrix_bytes": (i64, [vp]), "rk_same_device": (i, [vp, vp]),
             "rk_matrix_mulvec": (i, [vp, vp, vp]), "rk_matrix_mulvec_many": (i, [vp, i, vp, vp]), "rk_mulvecs": (i, [i, vp, vp, vp]),
