@@ -221,6 +221,34 @@ RK_DEV unsigned long long ll_load(const unsigned long long *p) {
   return w;
 }
 
+// The threads that take part in a CTA-wide phase, and its barrier: every
+// thread of the CTA (__syncthreads), or threads 0..N-1 only (named barrier
+// 1), for kernels whose other warps run on independently (a producer warp
+// that keeps copying while the others stage an input).
+struct CtaGroup {
+  RK_DEV static int size() { return blockDim.x; }
+  RK_DEV static void sync() { __syncthreads(); }
+  RK_DEV static bool sync_or(bool v) { return __syncthreads_or(v) != 0; }
+};
+template <int N>
+struct ThreadGroup {
+  static_assert(N % 32 == 0, "whole warps");
+  RK_DEV static int size() { return N; }
+  RK_DEV static void sync() { asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory"); }
+  RK_DEV static bool sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(N)
+        : "memory");
+    return r != 0;
+  }
+};
+
 // How long a device-side wait spins before it gives up and reports
 // DEV_ERR_TIMEOUT (nanoseconds of %globaltimer). A kernel that takes a limit
 // as an argument uses that instead; 0 there means this default.
@@ -230,32 +258,48 @@ constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 // carries `tag` (all threads; then a CTA barrier). false when a word has
 // not arrived within limit_ns (0: kWaitLimitNs). The verdict is combined by
 // the barrier itself, so the function may be called again at once.
+template <class Grp = CtaGroup>
 RK_DEV bool ll_gather_load(const unsigned long long *ll, int n, unsigned tag, float *dst,
                            unsigned long long limit_ns = 0) {
   if (limit_ns == 0) limit_ns = kWaitLimitNs;
+  const int nt = Grp::size();
   const uint64_t t0 = globaltimer_ns();
   bool ok = true;
-  // Eight words in flight per thread; a word that has not arrived is
-  // re-read on its own.
-  for (int i0 = threadIdx.x; i0 < n && ok; i0 += 8 * blockDim.x) {
+  // Eight words in flight per thread. Words that have not arrived are
+  // re-read together, so each further pass costs one round trip however
+  // many of the eight are missing.
+  for (int i0 = threadIdx.x; i0 < n && ok; i0 += 8 * nt) {
     unsigned long long w[8];
 #pragma unroll
     for (int u = 0; u < 8; u++) {
-      const int i = i0 + u * blockDim.x;
+      const int i = i0 + u * nt;
       w[u] = i < n ? ll_load(ll + i) : 0ull;
+    }
+    for (;;) {
+      bool all = true;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + u * nt;
+        if (i < n && (unsigned)(w[u] >> 32) != tag) all = false;
+      }
+      if (all) break;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + u * nt;
+        if (i < n && (unsigned)(w[u] >> 32) != tag) w[u] = ll_load(ll + i);
+      }
     }
 #pragma unroll
     for (int u = 0; u < 8; u++) {
-      const int i = i0 + u * blockDim.x;
-      if (i >= n) continue;
-      while ((unsigned)(w[u] >> 32) != tag && ok) {
-        if (globaltimer_ns() - t0 > limit_ns) ok = false;
-        else w[u] = ll_load(ll + i);
-      }
-      dst[i] = u2f((uint32_t)w[u]);
+      const int i = i0 + u * nt;
+      if (i < n) dst[i] = u2f((uint32_t)w[u]);
     }
   }
-  return __syncthreads_or(!ok) == 0;
+  return !Grp::sync_or(!ok);
 }
 
 // Whether launches on this host thread use programmatic dependent launch

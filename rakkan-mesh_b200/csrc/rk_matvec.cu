@@ -39,14 +39,16 @@ namespace rk {
 // broadcasts Rsqrt32 through *s_inv; when x spans several chunks it is
 // loaded twice (norm, then quantization). With `preloaded` the caller has
 // already issued stage_load for the first chunk.
+template <class Grp = CtaGroup>
 RK_DEV void stage_load(const float *__restrict__ x, const float *__restrict__ w, int c0, int m, float *stage,
                        float *wstage) {
   const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  const int nt = Grp::size();
   if (vec) {
     // Asynchronous 16-byte copies: every load of the chunk is in flight at
     // once; the caller's barrier is preceded by stage_wait(). x may be null
     // (its values come another way).
-    for (int i = threadIdx.x; i < m / 4; i += blockDim.x) {
+    for (int i = threadIdx.x; i < m / 4; i += nt) {
       if (x)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
                          (uint32_t)__cvta_generic_to_shared(stage + 4 * i)),
@@ -60,7 +62,7 @@ RK_DEV void stage_load(const float *__restrict__ x, const float *__restrict__ w,
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   } else {
-    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    for (int i = threadIdx.x; i < m; i += nt) {
       if (x) stage[i] = x[c0 + i];
       if (w) wstage[i] = w[c0 + i];
     }
@@ -78,22 +80,25 @@ RK_DEV void stage_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // ll_gather_load of each chunk, waiting up to limit_ns for `tag`; a word
 // that does not arrive sets *err to DEV_ERR_TIMEOUT and the stale value is
 // used, so the kernel still ends).
-template <bool NORM, bool PITCHED = false>
+//
+// Grp: the threads taking part (all of the CTA, or a named-barrier group).
+template <bool NORM, bool PITCHED = false, class Grp = CtaGroup>
 RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__restrict__ w, float recipN, float eps,
                            int8_t *qx, float *xs, int *xsum, float *s_inv, float *stage, float *wstage,
                            int stage_floats, bool preloaded, int xs_pitch = 1,
                            const unsigned long long *ll = nullptr, unsigned tag = 0, int *err = nullptr,
                            unsigned long long limit_ns = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nt = Grp::size();
   const bool single = n <= stage_floats;
   // One chunk of x (and of w) into the staging areas.
   auto stage_load = [&](const float *xx, const float *ww, int c0, int m, float *st, float *wst) {
     if (ll) {
-      rk::stage_load(nullptr, ww, c0, m, st, wst);
-      if (!ll_gather_load(ll + c0, m, tag, st, limit_ns) && threadIdx.x == 0 && err)
+      rk::stage_load<Grp>(nullptr, ww, c0, m, st, wst);
+      if (!ll_gather_load<Grp>(ll + c0, m, tag, st, limit_ns) && threadIdx.x == 0 && err)
         atomicExch(err, DEV_ERR_TIMEOUT);
     } else {
-      rk::stage_load(xx, ww, c0, m, st, wst);
+      rk::stage_load<Grp>(xx, ww, c0, m, st, wst);
     }
   };
   float inv = 0.0f;
@@ -102,11 +107,11 @@ RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__re
     for (int c0 = 0; c0 < n; c0 += stage_floats) {
       const int m = min(stage_floats, n - c0);
       if (!(preloaded && c0 == 0)) {
-        __syncthreads();
+        Grp::sync();
         stage_load(x, single ? w : nullptr, c0, m, stage, wstage);
       }
       stage_wait();
-      __syncthreads();
+      Grp::sync();
       if (warp == 0) {
         // Lane j's chain over elements j, j+32, ... (Dot32's order), its
         // operands in eight rotating registers refilled eight steps ahead
@@ -139,25 +144,25 @@ RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__re
       const float dot = combine32(s);
       if (lane == 0) *s_inv = rsqrt32(__fadd_rn(__fmul_rn(dot, recipN), eps));
     }
-    __syncthreads();
+    Grp::sync();
     inv = *s_inv;
   }
   for (int c0 = 0; c0 < n; c0 += stage_floats) {
     const int m = min(stage_floats, n - c0);
     if (!(NORM && single)) {
       if (!(preloaded && c0 == 0 && !NORM)) {
-        __syncthreads();
+        Grp::sync();
         stage_load(x, NORM ? w : nullptr, c0, m, stage, wstage);
       }
       stage_wait();
-      __syncthreads();
+      Grp::sync();
     }
     // Four threads (a lane quad) quantize block t of the chunk, eight
     // values each: amax and the integer sum are quad reductions (both order
     // free). A thread reads its eight values in an order rotated by t, so
     // the 32 lanes of a warp hit 32 different banks.
     const int ntask = (m / 32) * 4;
-    for (int task = threadIdx.x; task < ntask; task += blockDim.x) {
+    for (int task = threadIdx.x; task < ntask; task += nt) {
       const int t = task >> 2, sub = task & 3;
       const unsigned qmask = 0xfu << (lane & ~3);
       const int b = c0 / 32 + t;
@@ -684,228 +689,274 @@ __host__ __device__ inline long long step_units(const MvArgs &a) {
   return u;
 }
 
-// This warp's units [u0, u1) of a step, and its segments per unit.
-struct StepSpan {
+// A CTA's part of a step: units [u0, u1) (the same split for steps of the
+// same unit count), segments per unit and sub-row, and where the step's
+// segments start in the CTA's stream of segments.
+struct StepPart {
   long long u0, u1;
   int nsub, nseg;
-  RK_DEV long long segments() const { return (u1 - u0) * nsub * nseg; }
+  int base;  // a CTA's segments per launch number far fewer than 2^31
+  RK_DEV int segments() const { return int(u1 - u0) * nsub * nseg; }
 };
 
 template <int FMT>
-RK_DEV StepSpan step_span(const MvArgs &a, long long gw, long long G) {
+RK_DEV StepPart step_part(const MvArgs &a, long long cta, long long ncta, int base) {
   using T = QTraits<FMT>;
-  StepSpan sp;
+  StepPart sp;
   const long long units = step_units(a);
-  sp.u0 = units * gw / G;
-  sp.u1 = units * (gw + 1) / G;
+  sp.u0 = units * cta / ncta;
+  sp.u1 = units * (cta + 1) / ncta;
   sp.nsub = a.epi == EPI_SILU ? 2 : 1;
   sp.nseg = ((a.cols >> 5) + T::kSegBlocks - 1) / T::kSegBlocks;
+  sp.base = base;
   return sp;
+}
+
+// The matrix part and row of unit u's sub-row `sub`.
+RK_DEV void unit_loc(const MvArgs &a, int nsub, long long u, int sub, int &part, int &row) {
+  if (nsub == 2) {
+    part = sub;
+    row = int(u);
+    return;
+  }
+  part = 0;
+  while (part < a.nparts - 1 && u >= a.part[part].rows) {
+    u -= a.part[part].rows;
+    part++;
+  }
+  row = int(u);
 }
 
 // Shared-memory layout of a chain CTA (host and device agree on it).
 struct ChainSmem {
-  int in_off, xs_off, xsum_off, stage_off, wstage_off, ring_off, total;
+  int nslot, in_off, xs_off, xsum_off, stage_off, wstage_off, ring_off, total;
 };
-template <int FMT, int WARPS, int SLOTS>
-__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf) {
+template <int FMT>
+__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf, int nslot) {
   ChainSmem m;
   const int nb = max_cols / 32;
-  m.in_off = WARPS * SLOTS * 8;
+  m.nslot = nslot;
+  m.in_off = nslot * 16;  // a full and an empty mbarrier per slot
   m.xs_off = m.in_off + ((max_cols + 15) & ~15);
   m.xsum_off = m.xs_off + ((nb * 4 + 15) & ~15);
   m.stage_off = m.xsum_off + ((nb * 4 + 15) & ~15);
   m.wstage_off = m.stage_off + 4 * sf;
-  m.ring_off = m.wstage_off + 4 * wsf;
-  m.total = m.ring_off + WARPS * SLOTS * slot_bytes<FMT>();
+  m.ring_off = (m.wstage_off + 4 * wsf + 127) & ~127;
+  m.total = m.ring_off + nslot * slot_bytes<FMT>();
   return m;
 }
 
-template <int FMT, int WARPS, int SLOTS>
-__global__ void __launch_bounds__(WARPS * 32, 1)
-    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf) {
+// Waits for the barrier's phase `parity`, for at most limit_ns, and gives up
+// at once when the CTA has been told to stop (*abort).
+RK_DEV bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, unsigned long long limit_ns, const volatile int *abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort || globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+RK_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+constexpr int kChainWarps = 16;  // consumer warps of a chain CTA (plus one producer warp)
+
+// Warp-specialised: WARPS consumer warps (threads 0..32·WARPS-1, named
+// barrier 1 for their CTA-wide phases) and one producer warp. The producer
+// walks the CTA's segments of every step in order and copies each into the
+// next slot of a CTA-wide ring (1-D bulk copies, completion on the slot's
+// full mbarrier; never multicast), waiting on the slot's empty mbarrier
+// before reusing it. It reads only weights, which no kernel writes, so it
+// waits for no step's input: while the consumers stage one step's input the
+// ring fills with that step's weights, and at a step's end the ring keeps
+// the SM's copies in flight however few warps still have rows. Consumer
+// warp w takes the CTA's units w, w+WARPS, ... of each step; a segment's
+// slot and phase follow from its position in the CTA's stream.
+template <int FMT, int WARPS>
+__global__ void __launch_bounds__((WARPS + 1) * 32, 1)
+    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf, int nslot) {
   using T = QTraits<FMT>;
+  using Grp = ThreadGroup<WARPS * 32>;
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ volatile int s_abort;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ns = ca.nsteps;
-  const ChainSmem L = chain_smem<FMT, WARPS, SLOTS>(max_cols, sf, wsf);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+  const ChainSmem L = chain_smem<FMT>(max_cols, sf, wsf, nslot);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // full[nslot], empty[nslot]
   int8_t *sqx = reinterpret_cast<int8_t *>(smem + L.in_off);
   float *sxs = reinterpret_cast<float *>(smem + L.xs_off);
   int *sxsum = reinterpret_cast<int *>(smem + L.xsum_off);
   float *stage = reinterpret_cast<float *>(smem + L.stage_off);
   float *wstage = reinterpret_cast<float *>(smem + L.wstage_off);
-  uint8_t *ring = smem + L.ring_off + warp * SLOTS * slot_bytes<FMT>();
-  const long long gw = (long long)blockIdx.x * WARPS + warp, G = (long long)gridDim.x * WARPS;
-  const long long cw0 = (long long)blockIdx.x * WARPS, cw1 = cw0 + WARPS;  // this CTA's warps
-  const uint32_t bar0 = smem_addr(bars + warp * SLOTS);
+  uint8_t *ring = smem + L.ring_off;
+  const uint32_t full0 = smem_addr(bars), empty0 = smem_addr(bars + nslot);
+  const long long cta = blockIdx.x, ncta = gridDim.x;
   const unsigned long long limit = ca.wait_ns ? ca.wait_ns : kWaitLimitNs;
   int *err = ca.step[0].err;
 
-  // The producer (lane 0): step pk, its cursor, segments left in it.
-  uint64_t pol = 0;
-  int pk = 0, pslot = 0;
-  long long pleft = 0;
-  StepSpan psp{};
-  Cursor pc{};
-  auto seek = [&]() {  // from step pk on, the first step with segments for this warp
-    for (; pk < ns; pk++) {
-      psp = step_span<FMT>(ca.step[pk], gw, G);
-      pleft = psp.segments();
-      if (pleft > 0) {
-        cursor_init(pc, ca.step[pk], psp.nsub, psp.u0);
-        return;
-      }
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int k = 0; k < nslot; k++) {
+      mbar_init(full0 + 8 * k, 1);
+      mbar_init(empty0 + 8 * k, 1);
     }
-  };
-  if (lane == 0) {
-    for (int k = 0; k < SLOTS; k++) mbar_init(bar0 + 8 * k, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    pol = evict_first_policy();
-    seek();
   }
-  __syncwarp();
-  auto issue = [&]() {
-    if (pk >= ns) return;
-    const MvArgs &a = ca.step[pk];
-    const SegInfo sg = seg_info<FMT>(a, a.cols >> 5, pc);
-    uint8_t *dst = ring + pslot * slot_bytes<FMT>();
-    const uint32_t bar = bar0 + 8 * pslot;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
-    bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
-    bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
-    pslot = pslot + 1 == SLOTS ? 0 : pslot + 1;
-    if (--pleft > 0) {
-      cursor_next(pc, a, psp.nsub, psp.nseg);
-    } else {
-      pk++;
-      seek();
-    }
-  };
-
-  // Weights are read by no step's predecessor as output: the first slots
-  // are filled before the predecessor kernel has finished, together with
-  // the first step's norm weights.
+  __syncthreads();
   griddep_trigger();
-  if (lane == 0)
-    for (int k = 0; k < SLOTS; k++) issue();
-  {
-    const MvArgs &a = ca.step[0];
-    if (a.pro == PRO_NORM_QUANT && a.cols <= sf && !a.wait.ll) stage_load(nullptr, a.norm_w, 0, a.cols, stage, wstage);
-  }
-  griddep_wait();
 
-  int slot = 0;
-  uint32_t parity = 0;
-  bool dead = false;  // a segment's copy never landed: this warp stops
+  if (warp == WARPS) {
+    // ---- producer ----
+    if (lane != 0) return;
+    const uint64_t pol = evict_first_policy();
+    int pos = 0, base = 0;
+    bool stop = false;
+    for (int k = 0; k < ns && !stop; k++) {
+      const MvArgs &a = ca.step[k];
+      const StepPart sp = step_part<FMT>(a, cta, ncta, base);
+      base += sp.segments();
+      const int nb = a.cols >> 5;
+      for (long long u = sp.u0; u < sp.u1 && !stop; u++)
+        for (int sub = 0; sub < sp.nsub && !stop; sub++) {
+          Cursor c{};
+          unit_loc(a, sp.nsub, u, sub, c.part, c.row);
+          for (c.sg = 0; c.sg < sp.nseg; c.sg++, pos++) {
+            const int slot = pos % nslot;
+            if (pos >= nslot &&
+                !mbar_wait_or_abort(empty0 + 8 * slot, uint32_t((pos / nslot - 1) & 1), limit, &s_abort)) {
+              if (!s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
+              s_abort = 1;
+              stop = true;
+              break;
+            }
+            const SegInfo sg = seg_info<FMT>(a, nb, c);
+            uint8_t *dst = ring + slot * slot_bytes<FMT>();
+            const uint32_t bar = full0 + 8 * slot;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
+            bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
+            bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
+          }
+        }
+    }
+    // No copy may still be in flight when the CTA ends: wait for the last
+    // slots' fills (done at once unless the consumers stopped early).
+    for (int p = pos > nslot ? pos - nslot : 0; p < pos; p++)
+      mbar_wait_bounded(full0 + 8 * (p % nslot), uint32_t((p / nslot) & 1), limit);
+    return;
+  }
+
+  // ---- consumers ----
+  const bool norm0 = ca.step[0].pro == PRO_NORM_QUANT && ca.step[0].cols <= sf && !ca.step[0].wait.ll;
+  if (norm0) stage_load<Grp>(nullptr, ca.step[0].norm_w, 0, ca.step[0].cols, stage, wstage);
+  griddep_wait();
+  int base = 0;
   for (int k = 0; k < ns; k++) {
     const MvArgs &a = ca.step[k];
     const int cols = a.cols, nb = cols >> 5;
-    const long long units = step_units(a);
+    const StepPart sp = step_part<FMT>(a, cta, ncta, base);
+    base += sp.segments();
     // ---- prologue: the step's input into shared memory as Q8_0 ----
-    __syncthreads();  // every warp is done with the previous step's input
-    const bool cta_has = units * cw0 / G < units * cw1 / G;
-    if (cta_has) {
+    Grp::sync();  // every consumer is done with the previous step's input
+    if (sp.u1 > sp.u0) {
       const bool norm = a.pro == PRO_NORM_QUANT;
       const unsigned wtag = a.wait.ll ? gather_tag(*a.wait.epoch, a.wait.slot, a.wait.nslots) : 0u;
       const bool single = cols <= sf;
       bool pre = false;
       if (k == 0 && !a.wait.ll) {
         // Plain input from the predecessor kernel (the first step only).
-        stage_load(a.x, nullptr, 0, min(cols, sf), stage, wstage);
+        stage_load<Grp>(a.x, nullptr, 0, min(cols, sf), stage, wstage);
         pre = true;
       } else if (single) {
-        if (norm) stage_load(nullptr, a.norm_w, 0, cols, stage, wstage);
-        if (!ll_gather_load(a.wait.ll, cols, wtag, stage, limit) && threadIdx.x == 0) atomicExch(err, DEV_ERR_TIMEOUT);
+        if (norm) stage_load<Grp>(nullptr, a.norm_w, 0, cols, stage, wstage);
+        if (!ll_gather_load<Grp>(a.wait.ll, cols, wtag, stage, limit) && threadIdx.x == 0)
+          atomicExch(err, DEV_ERR_TIMEOUT);
         pre = true;
       }
       __shared__ float s_inv;
       if (norm)
-        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage, sf, pre, 1,
-                             a.wait.ll, wtag, err, limit);
+        quantize_warps<true, false, Grp>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage,
+                                         sf, pre, 1, a.wait.ll, wtag, err, limit);
       else
-        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sf, pre, 1,
-                              a.wait.ll, wtag, err, limit);
-      __syncthreads();
+        quantize_warps<false, false, Grp>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sf,
+                                          pre, 1, a.wait.ll, wtag, err, limit);
+      Grp::sync();
     }
-    // ---- this warp's rows of the step ----
-    const StepSpan sp = step_span<FMT>(a, gw, G);
-    const long long total = sp.segments();
-    if (total == 0) continue;
+    // ---- this warp's units of the step ----
     const unsigned put_tag = a.put.nll > 0 ? gather_tag(*a.put.epoch, a.put.slot, a.put.nslots) : 0u;
-    Cursor cc;
-    cursor_init(cc, a, sp.nsub, sp.u0);
-    float acc = 0.0f, r0 = 0.0f;
-    for (long long j = 0; j < total; j++) {
-      if (!dead && !mbar_wait_bounded(bar0 + 8 * slot, parity, limit)) {
-        if (lane == 0) atomicExch(err, DEV_ERR_TIMEOUT);
-        // Give the other copies already issued a bounded chance to land.
-        int js = slot;
-        uint32_t jp = parity;
-        for (int q = 1; q < SLOTS; q++) {
-          js = js + 1 == SLOTS ? 0 : js + 1;
-          if (js == 0) jp ^= 1;
-          mbar_wait_bounded(bar0 + 8 * js, jp, limit);
-        }
-        dead = true;
-      }
-      if (!dead) {
-        const SegInfo sg = seg_info<FMT>(a, nb, cc);
-        const uint8_t *W = ring + slot * slot_bytes<FMT>();
-        const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
-        if (cc.sg == 0) acc = 0.0f;
-        const int nfull = sg.nblk >> 5;
+    const int per_unit = sp.nsub * sp.nseg;
+    for (long long u = sp.u0 + warp; u < sp.u1; u += WARPS) {
+      float r0 = 0.0f;
+      for (int sub = 0; sub < sp.nsub; sub++) {
+        Cursor c{};
+        unit_loc(a, sp.nsub, u, sub, c.part, c.row);
+        float acc = 0.0f;
+        for (c.sg = 0; c.sg < sp.nseg; c.sg++) {
+          const int pos = sp.base + int(u - sp.u0) * per_unit + sub * sp.nseg + c.sg;
+          const int slot = pos % nslot;
+          bool ok = !s_abort;
+          if (ok && !mbar_wait_or_abort(full0 + 8 * slot, uint32_t((pos / nslot) & 1), limit, &s_abort)) {
+            if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
+            if (lane == 0) s_abort = 1;
+            ok = false;
+          }
+          if (ok) {
+            const SegInfo sg = seg_info<FMT>(a, nb, c);
+            const uint8_t *W = ring + slot * slot_bytes<FMT>();
+            const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
+            // Full 32-block chunks: lane t takes block t; lanes 0..7 then
+            // add the terms of blocks t, t+8, t+16, t+24 in order.
+            const int nfull = sg.nblk >> 5;
 #pragma unroll 2
-        for (int c = 0; c < nfull; c++) {
-          const int bb = c * 32 + lane;
-          const float term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
+            for (int ch = 0; ch < nfull; ch++) {
+              const int bb = ch * 32 + lane;
+              const float term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
 #pragma unroll
-          for (int q = 0; q < 4; q++) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q));
-        }
-        if (sg.nblk & 31) {
-          const int bb = nfull * 32 + lane;
-          float term = 0.0f;
-          if (bb < sg.nblk) term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
+              for (int q = 0; q < 4; q++) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q));
+            }
+            if (sg.nblk & 31) {
+              // A partial chunk: blocks past the row are skipped, not added.
+              const int bb = nfull * 32 + lane;
+              float term = 0.0f;
+              if (bb < sg.nblk) term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
-            const float t = __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q);
-            if (nfull * 32 + (lane & 7) + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
+              for (int q = 0; q < 4; q++) {
+                const float t = __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q);
+                if (nfull * 32 + (lane & 7) + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
+              }
+            }
           }
+          __syncwarp();
+          if (lane == 0 && ok) mbar_arrive(empty0 + 8 * slot);
         }
-        if (cc.sg == sp.nseg - 1) {
-          const float r = combine8(acc);
-          if (lane == 0) {
-            float *out = a.part[cc.part].out;
-            float v = r;
-            bool put = true;
-            switch (a.epi) {
-              case EPI_STORE: break;
-              case EPI_ADD: v = __fadd_rn(out[cc.row], r); break;
-              case EPI_ADD_CANON: v = canonical(__fadd_rn(out[cc.row], r)); break;
-              case EPI_SILU:
-                if (cc.sub == 0) {
-                  r0 = r;
-                  put = false;
-                } else {
-                  v = __fmul_rn(silu(r0), r);
-                  out = a.part[0].out;
-                }
-                break;
-            }
-            if (put) {
-              out[cc.row] = v;
-              if (cc.part == 0 || a.epi == EPI_SILU)
-                for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + cc.row, v, put_tag);
-            }
+        const float r = combine8(acc);
+        if (lane == 0 && !s_abort) {
+          float *out = a.part[c.part].out;
+          float v = r;
+          bool put = true;
+          switch (a.epi) {
+            case EPI_STORE: break;
+            case EPI_ADD: v = __fadd_rn(out[c.row], r); break;
+            case EPI_ADD_CANON: v = canonical(__fadd_rn(out[c.row], r)); break;
+            case EPI_SILU:
+              if (sub == 0) {
+                r0 = r;
+                put = false;
+              } else {
+                v = __fmul_rn(silu(r0), r);
+                out = a.part[0].out;
+              }
+              break;
+          }
+          if (put) {
+            out[c.row] = v;
+            if (c.part == 0 || a.epi == EPI_SILU)
+              for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + c.row, v, put_tag);
           }
         }
       }
-      __syncwarp();
-      if (lane == 0 && !dead) issue();
-      cursor_next(cc, a, sp.nsub, sp.nseg);
-      slot = slot + 1 == SLOTS ? 0 : slot + 1;
-      if (slot == 0) parity ^= 1;
     }
   }
 }
@@ -1021,43 +1072,44 @@ cudaError_t init_matvec_attributes() {
     e = cudaFuncSetAttribute(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kChainWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kChainWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   return e;
 }
 
 // Staging of a chain: x in chunks of sf floats (the largest of 8192, 4096,
-// 2048 whose layout fits), the norm weights beside them for the steps that
-// normalise.
-static int chain_total(int fmt, int mc, int sf, int wsf) {
-  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0, kWarps, kSlots>(mc, sf, wsf).total
-                         : chain_smem<FMT_Q4_0, kWarps, kSlots>(mc, sf, wsf).total;
+// 2048 that leaves a ring of kChainMinSlots), the norm weights beside them
+// for the steps that normalise; the rest of the CTA's shared memory is ring.
+constexpr int kChainMinSlots = 24, kChainMaxSlots = 64;
+
+static ChainSmem chain_layout(int fmt, int mc, int sf, int wsf, int nslot) {
+  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, wsf, nslot) : chain_smem<FMT_Q4_0>(mc, sf, wsf, nslot);
 }
 
-static void chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *wsf) {
+static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *wsf) {
   int mc = 0;
   for (int k = 0; k < ca.nsteps; k++) mc = std::max(mc, ca.step[k].cols);
-  int f = 0, wf = 0;
+  const int fmt = ca.nsteps > 0 ? ca.step[0].fmt : FMT_Q8_0;
+  const int sb = fmt == FMT_Q8_0 ? slot_bytes<FMT_Q8_0>() : slot_bytes<FMT_Q4_0>();
+  ChainSmem best{};
   for (int cand : {8192, 4096, 2048}) {
-    f = std::min(mc, cand);
-    wf = 0;
+    const int f = std::min(mc, cand);
+    int wf = 0;
     for (int k = 0; k < ca.nsteps; k++)
       if (ca.step[k].pro == PRO_NORM_QUANT) wf = std::max(wf, std::min(ca.step[k].cols, f));
-    if (ca.nsteps < 1 || chain_total(ca.step[0].fmt, mc, f, wf) <= kSmemLimit) break;
+    const ChainSmem zero = chain_layout(fmt, mc, f, wf, 0);
+    int n = std::min((kSmemLimit - zero.total) / (sb + 16), kChainMaxSlots);
+    while (n > 0 && chain_layout(fmt, mc, f, wf, n).total > kSmemLimit) n--;
+    *max_cols = mc;
+    *sf = f;
+    *wsf = wf;
+    best = chain_layout(fmt, mc, f, wf, std::max(n, 0));
+    if (n >= kChainMinSlots) break;
   }
-  *max_cols = mc;
-  *sf = f;
-  *wsf = wf;
-}
-
-int matvec_chain_smem(const ChainArgs &ca) {
-  int mc, sf, wsf;
-  chain_dims(ca, &mc, &sf, &wsf);
-  if (ca.nsteps < 1) return 0;
-  return chain_total(ca.step[0].fmt, mc, sf, wsf);
+  return best;
 }
 
 bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
@@ -1073,17 +1125,24 @@ bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
     // is what lets tagged buffers be reused without a barrier.
     if (step_units(a) < num_sms) return false;
   }
-  return matvec_chain_smem(ca) <= kSmemLimit;
+  int mc, sf, wsf;
+  const ChainSmem L = chain_dims(ca, &mc, &sf, &wsf);
+  return L.nslot >= kChainMinSlots && L.total <= kSmemLimit;
+}
+
+int matvec_chain_smem(const ChainArgs &ca) {
+  int mc, sf, wsf;
+  return chain_dims(ca, &mc, &sf, &wsf).total;
 }
 
 cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t st) {
   if (!matvec_chain_ok(ca, num_sms)) return cudaErrorInvalidValue;
   int mc, sf, wsf;
-  chain_dims(ca, &mc, &sf, &wsf);
-  const int smem = matvec_chain_smem(ca);
+  const ChainSmem L = chain_dims(ca, &mc, &sf, &wsf);
+  const int threads = (kChainWarps + 1) * 32;
   if (ca.step[0].fmt == FMT_Q8_0)
-    return launch_k(k_matvec_chain<FMT_Q8_0, kWarps, kSlots>, num_sms, kWarps * 32, smem, st, ca, mc, sf, wsf);
-  return launch_k(k_matvec_chain<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem, st, ca, mc, sf, wsf);
+    return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps>, num_sms, threads, L.total, st, ca, mc, sf, wsf, L.nslot);
+  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps>, num_sms, threads, L.total, st, ca, mc, sf, wsf, L.nslot);
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
