@@ -33,6 +33,7 @@ extern "C" {
 #define RK_OK 0
 #define RK_ERR_ARGS (-1)     /* bad handle, argument, shape or type (tenErrArgs, tensor.go:57) */
 #define RK_ERR_TOO_BIG (-3)  /* over a size limit (tenErrTooBig, tensor.go:58) */
+#define RK_ERR_BLOB (-5)     /* blob too short for the requested tensor (tenErrBlob, tensor.go:59) */
 #define RK_ERR_CUDA (-10)    /* a CUDA call failed */
 #define RK_ERR_NOMEM (-11)   /* device allocation failed */
 #define RK_ERR_TIMEOUT (-12) /* a bounded device-side wait expired */
@@ -74,6 +75,7 @@ typedef struct rk_head rk_head;
 typedef struct rk_model rk_model;
 typedef struct rk_group rk_group;
 typedef struct rk_pipeline rk_pipeline;
+typedef struct rk_tensors rk_tensors;
 
 /* gpu.Info (device.go:21-47). */
 typedef struct {
@@ -404,6 +406,42 @@ int rk_tensor_relu(rk_device *d, int dtype, int rows, int cols, const void *a, v
 int rk_tensor_softmax(rk_device *d, int dtype, int rows, int cols, const float *a, float *c);
 int rk_tensor_quantize(rk_device *d, int dtype, int rows, int cols, const float *a, float k, int8_t *c);
 int rk_tensor_argmax(rk_device *d, int dtype, int rows, int cols, const void *a, int32_t *out);
+
+/* ---- rakkan_tensor_v1's tensor table, device-resident (tensor.go:92-158,
+ *      186-275, 286-505). A task's tensors live in device memory by handle,
+ *      so a chain of operations (matmul, add, relu, ...) never leaves the GPU;
+ *      only from_memory / from_blob upload and to_memory / argmax download.
+ *      Every operation makes a new tensor, as the reference's do, counted
+ *      against the table's byte budget (the task's memory budget,
+ *      image.go:85-88). Calls return a positive handle (or a count) or a
+ *      negative RK_ERR_*: RK_ERR_ARGS for tenErrArgs, RK_ERR_TOO_BIG for
+ *      tenErrTooBig, RK_ERR_BLOB for tenErrBlob. Gas is the caller's to
+ *      charge (runner.go:248-263). ---- */
+int rk_tensors_new(rk_device *d, int64_t budget_bytes, rk_tensors **out);
+void rk_tensors_free(rk_tensors *t);                                      /* the task's end */
+int64_t rk_tensors_used(const rk_tensors *t);                             /* hostBytes, image.go:88 */
+/* from_memory (tenFromMemory, tensor.go:204-218): little-endian bytes of a
+ * rows×cols tensor; float32 NaNs canonicalised on load (decodeInto,
+ * tensor.go:187-202). */
+int rk_tensors_from_memory(rk_tensors *t, const void *src, int dtype, int rows, int cols);
+/* from_blob (tenFromBlob, tensor.go:220-242): the tensor's bytes at
+ * `offset` of an attached blob the caller has mapped (blob, blob_size). */
+int rk_tensors_from_blob(rk_tensors *t, const void *blob, int64_t blob_size, int64_t offset, int dtype, int rows,
+                         int cols);
+/* to_memory (tenToMemory, tensor.go:244-275): bytes written. */
+int64_t rk_tensors_to_memory(rk_tensors *t, int h, void *dst, int64_t n);
+/* rows / cols / dtype (tenDim, tensor.go:277-284): which = 0, 1, 2. */
+int rk_tensors_dim(rk_tensors *t, int h, int which);
+int rk_tensors_release(rk_tensors *t, int h);                            /* free, tensor.go:492-501 */
+int rk_tensors_matmul(rk_tensors *t, int ha, int hb, int transposed);   /* matmul / matmul_t, tensor.go:286-339 */
+int rk_tensors_add(rk_tensors *t, int ha, int hb);                       /* tensor.go:341-364 */
+int rk_tensors_scale(rk_tensors *t, int h, float k);                     /* tensor.go:366-387 */
+int rk_tensors_relu(rk_tensors *t, int h);                               /* tensor.go:389-412 */
+int rk_tensors_softmax(rk_tensors *t, int h);                            /* tensor.go:414-443 */
+int rk_tensors_quantize(rk_tensors *t, int h, float k);                  /* tensor.go:445-461 */
+/* argmax (tenArgmax, tensor.go:463-486): each row's first maximum as
+ * int32s into dst (n bytes); returns the row count. */
+int rk_tensors_argmax(rk_tensors *t, int h, int32_t *dst, int64_t n);
 
 /* ---- Device-side weight import (num.QuantizeQ8 / QuantizeQ4,
  *      quant.go:25-68) and the seeded synthetic generator used by tests

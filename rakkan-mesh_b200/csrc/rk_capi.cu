@@ -22,6 +22,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -2629,6 +2630,293 @@ extern "C" int rk_tensor_argmax(rk_device *d, int dtype, int rows, int cols, con
                          [&](const void *da, const void *, void *dc, cudaStream_t st) {
                            return launch_tensor_argmax(dtype == RK_TENSOR_F32 ? 0 : 1, rows, cols, da, (int *)dc, st);
                          });
+}
+
+
+// ---------------------------------------------------------------------------
+// rakkan_tensor_v1's tensor table on the device (tensor.go:92-158, 186-275,
+// 286-505): tensors live in device memory by handle, so a guest's chain of
+// operations (matmul -> add -> relu ...) stays on the GPU; only from_memory /
+// from_blob upload and to_memory / argmax download. Each operation makes a
+// new tensor, as the reference's do, within the table's byte budget.
+// ---------------------------------------------------------------------------
+namespace {
+struct DevTensor {
+  int dtype = 0, rows = 0, cols = 0;
+  void *p = nullptr;
+  int64_t bytes = 0;
+};
+int64_t ten_elem_size(int dtype) { return dtype == RK_TENSOR_F32 || dtype == RK_TENSOR_I32 ? 4 : dtype == RK_TENSOR_I8 ? 1 : 0; }
+constexpr int kMaxTensorDim = 1 << 24;  // maxTensorDim, tensor.go:60
+}  // namespace
+
+struct rk_tensors {
+  rk_device *d = nullptr;
+  int64_t budget = 0, used = 0;
+  std::map<int, DevTensor> table;
+  int next = 0;
+};
+
+extern "C" int rk_tensors_new(rk_device *d, int64_t budget_bytes, rk_tensors **out) {
+  if (!d || !out || budget_bytes < 0) return fail(RK_ERR_ARGS, "bad argument");
+  auto *t = new rk_tensors();
+  t->d = d;
+  t->budget = budget_bytes;
+  *out = t;
+  return RK_OK;
+}
+
+extern "C" void rk_tensors_free(rk_tensors *t) {
+  if (!t) return;
+  Guard g(t->d);
+  cudaSetDevice(t->d->ordinal);
+  cudaStreamSynchronize(t->d->st);
+  for (auto &kv : t->table) cudaFree(kv.second.p);
+  t->d->used -= t->used;
+  delete t;
+}
+
+extern "C" int64_t rk_tensors_used(const rk_tensors *t) { return t ? t->used : 0; }
+
+// newTensor (tensor.go:119-141): a zeroed tensor within the budget, or 0
+// (bad type or shape: *why = RK_ERR_ARGS; over the budget: RK_ERR_TOO_BIG).
+static DevTensor *tt_new(rk_tensors *t, int dtype, int rows, int cols, DevTensor *out, int *why) {
+  const int64_t es = ten_elem_size(dtype);
+  if (es == 0 || rows <= 0 || cols <= 0 || rows > kMaxTensorDim || cols > kMaxTensorDim) {
+    *why = RK_ERR_ARGS;
+    return nullptr;
+  }
+  const int64_t n = (int64_t)rows * cols * es;
+  if (t->used + n > t->budget) {
+    *why = RK_ERR_TOO_BIG;
+    return nullptr;
+  }
+  out->dtype = dtype;
+  out->rows = rows;
+  out->cols = cols;
+  out->bytes = n;
+  cudaError_t e = cudaMalloc(&out->p, std::max<int64_t>(n, 16));
+  if (e == cudaSuccess) e = cudaMemsetAsync(out->p, 0, n, t->d->st);
+  if (e != cudaSuccess) {
+    cudaFree(out->p);
+    cudaGetLastError();
+    *why = RK_ERR_NOMEM;
+    return nullptr;
+  }
+  t->used += n;
+  t->d->used += n;
+  return out;
+}
+
+static void tt_drop(rk_tensors *t, DevTensor &x) {
+  cudaFree(x.p);
+  t->used -= x.bytes;
+  t->d->used -= x.bytes;
+  x.p = nullptr;
+}
+
+static int tt_add(rk_tensors *t, const DevTensor &x) {
+  t->table[++t->next] = x;
+  return t->next;
+}
+
+static DevTensor *tt_get(rk_tensors *t, int h) {
+  auto it = t->table.find(h);
+  return it == t->table.end() ? nullptr : &it->second;
+}
+
+// Runs a kernel sequence into a fresh result tensor; returns its handle, or
+// the error (the result is dropped).
+static int tt_result(rk_tensors *t, DevTensor &c, cudaError_t e, const char *what) {
+  rk_device *d = t->d;
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);
+  if (e != cudaSuccess) {
+    tt_drop(t, c);
+    return cuda_fail(e, what);
+  }
+  int rc = check_dev_err(d);
+  if (rc) {
+    tt_drop(t, c);
+    return rc;
+  }
+  return tt_add(t, c);
+}
+
+// Uploads raw little-endian bytes into a new tensor (decodeInto: float32
+// NaNs canonicalised on the device).
+static int tt_upload(rk_tensors *t, const void *raw, int dtype, int rows, int cols, int too_big_code) {
+  DevTensor c;
+  int why = 0;
+  if (!tt_new(t, dtype, rows, cols, &c, &why)) {
+    if (why == RK_ERR_TOO_BIG) return fail(too_big_code, "tensor of %d×%d over the budget", rows, cols);
+    if (why == RK_ERR_NOMEM) return fail(RK_ERR_NOMEM, "device allocation failed");
+    return fail(RK_ERR_ARGS, "bad tensor type or shape");
+  }
+  cudaError_t e = cudaMemcpyAsync(c.p, raw, c.bytes, cudaMemcpyHostToDevice, t->d->st);
+  if (e == cudaSuccess && dtype == RK_TENSOR_F32) e = launch_tensor_canon(c.bytes / 4, (float *)c.p, t->d->st);
+  return tt_result(t, c, e, "tensor upload");
+}
+
+extern "C" int rk_tensors_from_memory(rk_tensors *t, const void *src, int dtype, int rows, int cols) {
+  if (!t || !src) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  // tenFromMemory reports a tensor it cannot make as tenErrArgs (tensor.go:206-209).
+  return tt_upload(t, src, dtype, rows, cols, RK_ERR_ARGS);
+}
+
+extern "C" int rk_tensors_from_blob(rk_tensors *t, const void *blob, int64_t blob_size, int64_t offset, int dtype,
+                                    int rows, int cols) {
+  if (!t || (!blob && blob_size > 0) || blob_size < 0 || offset < 0) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  // tenFromBlob (tensor.go:220-242): the tensor is made first (tenErrTooBig),
+  // then the blob must hold it from `offset` on (tenErrBlob).
+  const int64_t es = ten_elem_size(dtype);
+  if (es == 0 || rows <= 0 || cols <= 0 || rows > kMaxTensorDim || cols > kMaxTensorDim)
+    return fail(RK_ERR_TOO_BIG, "bad tensor type or shape");
+  const int64_t n = (int64_t)rows * cols * es;
+  if (t->used + n > t->budget) return fail(RK_ERR_TOO_BIG, "tensor of %d×%d over the budget", rows, cols);
+  if (offset + n > blob_size) return fail(RK_ERR_BLOB, "blob of %lld bytes too short for %lld bytes at %lld",
+                                          (long long)blob_size, (long long)n, (long long)offset);
+  return tt_upload(t, static_cast<const char *>(blob) + offset, dtype, rows, cols, RK_ERR_TOO_BIG);
+}
+
+extern "C" int64_t rk_tensors_to_memory(rk_tensors *t, int h, void *dst, int64_t n) {
+  if (!t) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *x = tt_get(t, h);
+  if (!x || !dst || n < x->bytes) return fail(RK_ERR_ARGS, "to_memory: bad handle or buffer too small");
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  CK(cudaMemcpy(dst, x->p, x->bytes, cudaMemcpyDeviceToHost));
+  return x->bytes;
+}
+
+extern "C" int rk_tensors_dim(rk_tensors *t, int h, int which) {
+  if (!t || which < 0 || which > 2) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *x = tt_get(t, h);
+  if (!x) return fail(RK_ERR_ARGS, "bad handle");
+  return which == 0 ? x->rows : which == 1 ? x->cols : x->dtype;
+}
+
+extern "C" int rk_tensors_release(rk_tensors *t, int h) {
+  if (!t) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *x = tt_get(t, h);
+  if (!x) return fail(RK_ERR_ARGS, "bad handle");
+  cudaSetDevice(t->d->ordinal);
+  cudaStreamSynchronize(t->d->st);
+  tt_drop(t, *x);
+  t->table.erase(h);
+  return RK_OK;
+}
+
+extern "C" int rk_tensors_matmul(rk_tensors *t, int ha, int hb, int transposed) {
+  if (!t) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *a = tt_get(t, ha), *b = tt_get(t, hb);
+  if (!a || !b || a->dtype != b->dtype || a->dtype == RK_TENSOR_I32) return fail(RK_ERR_ARGS, "matmul: bad operands");
+  const int m = a->rows, k = a->cols, n = transposed ? b->rows : b->cols;
+  if ((transposed ? b->cols : b->rows) != k) return fail(RK_ERR_ARGS, "matmul: inner dimensions differ");
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  DevTensor c;
+  int why = 0;
+  if (!tt_new(t, a->dtype == RK_TENSOR_I8 ? RK_TENSOR_I32 : RK_TENSOR_F32, m, n, &c, &why))
+    return fail(why == RK_ERR_NOMEM ? RK_ERR_NOMEM : RK_ERR_TOO_BIG, "matmul: result over the budget");
+  const cudaError_t e = launch_tensor_matmul(a->dtype, transposed ? 1 : 0, m, k, n, a->p, b->p, c.p, t->d->sms,
+                                             t->d->err_dev, t->d->st);
+  return tt_result(t, c, e, "tensor matmul");
+}
+
+extern "C" int rk_tensors_add(rk_tensors *t, int ha, int hb) {
+  if (!t) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *a = tt_get(t, ha), *b = tt_get(t, hb);
+  if (!a || !b || a->dtype != b->dtype || a->dtype == RK_TENSOR_I8 || a->cols != b->cols ||
+      (b->rows != a->rows && b->rows != 1))
+    return fail(RK_ERR_ARGS, "add: bad operands");
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  DevTensor c;
+  int why = 0;
+  if (!tt_new(t, a->dtype, a->rows, a->cols, &c, &why)) return fail(RK_ERR_TOO_BIG, "add: result over the budget");
+  const cudaError_t e =
+      launch_tensor_add(a->dtype == RK_TENSOR_F32 ? 0 : 1, a->rows, a->cols, a->p, b->p, b->rows, c.p, t->d->st);
+  return tt_result(t, c, e, "tensor add");
+}
+
+// scale, relu, softmax and quantize: one input tensor, one result.
+static int tt_unary(rk_tensors *t, int h, bool ok_i8, bool ok_i32, bool f32_only, int out_dtype_f32, int out_dtype_i32,
+                    const char *what, const std::function<cudaError_t(const DevTensor &, DevTensor &)> &run) {
+  if (!t) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *a = tt_get(t, h);
+  if (!a || (a->dtype == RK_TENSOR_I8 && !ok_i8) || (a->dtype == RK_TENSOR_I32 && !ok_i32) ||
+      (f32_only && a->dtype != RK_TENSOR_F32))
+    return fail(RK_ERR_ARGS, "%s: bad operand", what);
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  DevTensor c;
+  int why = 0;
+  const int od = a->dtype == RK_TENSOR_F32 ? out_dtype_f32 : out_dtype_i32;
+  if (!tt_new(t, od, a->rows, a->cols, &c, &why)) return fail(RK_ERR_TOO_BIG, "%s: result over the budget", what);
+  return tt_result(t, c, run(*a, c), what);
+}
+
+extern "C" int rk_tensors_scale(rk_tensors *t, int h, float k) {
+  return tt_unary(t, h, false, true, false, RK_TENSOR_F32, RK_TENSOR_F32, "scale",
+                  [&](const DevTensor &a, DevTensor &c) {
+                    return launch_tensor_scale(a.dtype == RK_TENSOR_F32 ? 0 : 1, (long long)a.rows * a.cols, a.p, k,
+                                               (float *)c.p, t->d->st);
+                  });
+}
+
+extern "C" int rk_tensors_relu(rk_tensors *t, int h) {
+  return tt_unary(t, h, false, true, false, RK_TENSOR_F32, RK_TENSOR_I32, "relu",
+                  [&](const DevTensor &a, DevTensor &c) {
+                    return launch_tensor_relu(a.dtype == RK_TENSOR_F32 ? 0 : 1, (long long)a.rows * a.cols, a.p, c.p,
+                                              t->d->st);
+                  });
+}
+
+extern "C" int rk_tensors_softmax(rk_tensors *t, int h) {
+  return tt_unary(t, h, false, false, true, RK_TENSOR_F32, RK_TENSOR_F32, "softmax",
+                  [&](const DevTensor &a, DevTensor &c) {
+                    return launch_tensor_softmax(a.rows, a.cols, (const float *)a.p, (float *)c.p, t->d->st);
+                  });
+}
+
+extern "C" int rk_tensors_quantize(rk_tensors *t, int h, float k) {
+  if (!(k > 0.0f)) return fail(RK_ERR_ARGS, "quantize: scale not positive");
+  return tt_unary(t, h, false, false, true, RK_TENSOR_I8, RK_TENSOR_I8, "quantize",
+                  [&](const DevTensor &a, DevTensor &c) {
+                    return launch_tensor_quantize((long long)a.rows * a.cols, (const float *)a.p, k, (int8_t *)c.p,
+                                                  t->d->st);
+                  });
+}
+
+extern "C" int rk_tensors_argmax(rk_tensors *t, int h, int32_t *dst, int64_t n) {
+  if (!t) return fail(RK_ERR_ARGS, "bad argument");
+  Guard g(t->d);
+  DevTensor *a = tt_get(t, h);
+  if (!a || a->dtype == RK_TENSOR_I8 || !dst || n < (int64_t)a->rows * 4)
+    return fail(RK_ERR_ARGS, "argmax: bad operand or buffer too small");
+  int rc = set_device(t->d);
+  if (rc) return rc;
+  int *out = nullptr;
+  cudaError_t e = cudaMalloc(&out, 4 * (size_t)a->rows);
+  if (e == cudaSuccess)
+    e = launch_tensor_argmax(a->dtype == RK_TENSOR_F32 ? 0 : 1, a->rows, a->cols, a->p, out, t->d->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dst, out, 4 * (size_t)a->rows, cudaMemcpyDeviceToHost, t->d->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(t->d->st);
+  cudaFree(out);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor argmax");
+  return a->rows;
 }
 
 // ---------------------------------------------------------------------------

@@ -729,8 +729,23 @@ RK_DEV void unit_loc(const MvArgs &a, int nsub, long long u, int sub, int &part,
 
 // Shared-memory layout of a chain CTA (host and device agree on it).
 struct ChainSmem {
-  int nslot, in_off, xs_off, xsum_off, stage_off, wstage_off, ring_off, total;
+  int nslot, in_off, xs_off, xsum_off, stage_off, wstage_off, carry_off, ring_off, total;
 };
+
+// A row's running state handed from the warp of one segment to the warp of
+// the next: qrow's eight sums, the finished W1 row of an EPI_SILU pair, and
+// the position it is for (the entry's reader waits until seq names it).
+struct Carry {
+  float acc[8];
+  float r0;
+  volatile int seq;
+  int pad[2];
+};
+// Entries, indexed by the reader's position. More than the ring's slots:
+// a position is processed only while every position more than nslot before
+// it has released its slot, and a reader takes its carry before releasing,
+// so an entry is never rewritten before its reader has it.
+constexpr int kCarries = 128;
 template <int FMT>
 __host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf, int nslot) {
   ChainSmem m;
@@ -741,7 +756,8 @@ __host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf, i
   m.xsum_off = m.xs_off + ((nb * 4 + 15) & ~15);
   m.stage_off = m.xsum_off + ((nb * 4 + 15) & ~15);
   m.wstage_off = m.stage_off + 4 * sf;
-  m.ring_off = (m.wstage_off + 4 * wsf + 127) & ~127;
+  m.carry_off = (m.wstage_off + 4 * wsf + 15) & ~15;
+  m.ring_off = (m.carry_off + kCarries * (int)sizeof(Carry) + 127) & ~127;
   m.total = m.ring_off + nslot * slot_bytes<FMT>();
   return m;
 }
@@ -762,6 +778,8 @@ RK_DEV void mbar_arrive(uint32_t bar) {
 }
 
 constexpr int kChainWarps = 16;  // consumer warps of a chain CTA (plus one producer warp)
+constexpr int kChainIssuers = 8;  // lanes of the producer warp that issue copies
+constexpr int kChainSlotsMax = 64;
 
 // Warp-specialised: WARPS consumer warps (threads 0..32·WARPS-1, named
 // barrier 1 for their CTA-wide phases) and one producer warp. The producer
@@ -772,8 +790,24 @@ constexpr int kChainWarps = 16;  // consumer warps of a chain CTA (plus one prod
 // waits for no step's input: while the consumers stage one step's input the
 // ring fills with that step's weights, and at a step's end the ring keeps
 // the SM's copies in flight however few warps still have rows. Consumer
-// warp w takes the CTA's units w, w+WARPS, ... of each step; a segment's
-// slot and phase follow from its position in the CTA's stream.
+// warp w takes the CTA's segments w, w+WARPS, ... of each step, so the
+// positions being worked on span about WARPS slots and the rest of the ring
+// is in flight; a segment's slot and phase follow from its position. A row
+// of several segments, and the two rows of an EPI_SILU pair, pass their
+// running state to the next segment's warp through a Carry entry: every
+// segment's block terms are computed at once, and only qrow's eight sums
+// run in block order from warp to warp.
+//
+// Producer lane j (of kChainIssuers) issues positions j, j+kChainIssuers,
+// ...; a copy's issue is a handful of instructions, but one thread issuing
+// every copy of an SM could not keep HBM busy.
+//
+// Warps run ahead of one another, so a consumer may reach position p while
+// the slot's previous fill (p - nslot) has not landed; a parity wait would
+// then see that older phase's parity as complete. A consumer therefore
+// first waits until the slot's fill count (s_fill) shows p's fill issued:
+// a lane issues p only after the consumer of p - nslot released the slot,
+// so the slot's phase is then the one p fills.
 template <int FMT, int WARPS>
 __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
     k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf, int nslot) {
@@ -781,6 +815,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
   using Grp = ThreadGroup<WARPS * 32>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ volatile int s_abort;
+  __shared__ volatile int s_fill[kChainSlotsMax];  // fills issued into each slot
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ns = ca.nsteps;
   const ChainSmem L = chain_smem<FMT>(max_cols, sf, wsf, nslot);
@@ -791,6 +826,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
   float *stage = reinterpret_cast<float *>(smem + L.stage_off);
   float *wstage = reinterpret_cast<float *>(smem + L.wstage_off);
   uint8_t *ring = smem + L.ring_off;
+  Carry *carry = reinterpret_cast<Carry *>(smem + L.carry_off);
   const uint32_t full0 = smem_addr(bars), empty0 = smem_addr(bars + nslot);
   const long long cta = blockIdx.x, ncta = gridDim.x;
   const unsigned long long limit = ca.wait_ns ? ca.wait_ns : kWaitLimitNs;
@@ -799,6 +835,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int k = 0; k < nslot; k++) {
+      s_fill[k] = 0;
       mbar_init(full0 + 8 * k, 1);
       mbar_init(empty0 + 8 * k, 1);
     }
@@ -809,7 +846,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
 
   if (warp == WARPS) {
     // ---- producer ----
-    if (lane != 0) return;
+    if (lane >= kChainIssuers) return;
     const uint64_t pol = evict_first_policy();
     int pos = 0, base = 0;
     bool stop = false;
@@ -823,32 +860,38 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
           Cursor c{};
           unit_loc(a, sp.nsub, u, sub, c.part, c.row);
           for (c.sg = 0; c.sg < sp.nseg; c.sg++, pos++) {
-            const int slot = pos % nslot;
-            if (pos >= nslot &&
-                !mbar_wait_or_abort(empty0 + 8 * slot, uint32_t((pos / nslot - 1) & 1), limit, &s_abort)) {
+            if (pos % kChainIssuers != lane) continue;
+            const int fill = pos / nslot, slot = pos - fill * nslot;
+            if (fill > 0 &&
+                !mbar_wait_or_abort(empty0 + 8 * slot, uint32_t((fill - 1) & 1), limit, &s_abort)) {
               if (!s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
               s_abort = 1;
               stop = true;
               break;
             }
+            // The slot's last reader released it through the empty
+            // mbarrier, which orders its reads before this copy's writes.
             const SegInfo sg = seg_info<FMT>(a, nb, c);
             uint8_t *dst = ring + slot * slot_bytes<FMT>();
             const uint32_t bar = full0 + 8 * slot;
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
             bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
             bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
+            __threadfence_block();
+            s_fill[slot] = fill + 1;
           }
         }
     }
-    // No copy may still be in flight when the CTA ends: wait for the last
-    // slots' fills (done at once unless the consumers stopped early).
+    // No copy may still be in flight when the CTA ends: wait for this lane's
+    // fills among the last nslot positions (done at once unless the
+    // consumers stopped early).
     for (int p = pos > nslot ? pos - nslot : 0; p < pos; p++)
-      mbar_wait_bounded(full0 + 8 * (p % nslot), uint32_t((p / nslot) & 1), limit);
+      if (p % kChainIssuers == lane) mbar_wait_bounded(full0 + 8 * (p % nslot), uint32_t((p / nslot) & 1), limit);
     return;
   }
 
   // ---- consumers ----
+  for (int e = threadIdx.x; e < kCarries; e += WARPS * 32) carry[e].seq = -1;
   const bool norm0 = ca.step[0].pro == PRO_NORM_QUANT && ca.step[0].cols <= sf && !ca.step[0].wait.ll;
   if (norm0) stage_load<Grp>(nullptr, ca.step[0].norm_w, 0, ca.step[0].cols, stage, wstage);
   griddep_wait();
@@ -859,7 +902,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
     const StepPart sp = step_part<FMT>(a, cta, ncta, base);
     base += sp.segments();
     // ---- prologue: the step's input into shared memory as Q8_0 ----
-    Grp::sync();  // every consumer is done with the previous step's input
+    Grp::sync();  // every consumer is done with the previous step
     if (sp.u1 > sp.u0) {
       const bool norm = a.pro == PRO_NORM_QUANT;
       const unsigned wtag = a.wait.ll ? gather_tag(*a.wait.epoch, a.wait.slot, a.wait.nslots) : 0u;
@@ -884,78 +927,107 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
                                           pre, 1, a.wait.ll, wtag, err, limit);
       Grp::sync();
     }
-    // ---- this warp's units of the step ----
+    // ---- this warp's segments of the step ----
     const unsigned put_tag = a.put.nll > 0 ? gather_tag(*a.put.epoch, a.put.slot, a.put.nslots) : 0u;
-    const int per_unit = sp.nsub * sp.nseg;
-    for (long long u = sp.u0 + warp; u < sp.u1; u += WARPS) {
-      float r0 = 0.0f;
-      for (int sub = 0; sub < sp.nsub; sub++) {
-        Cursor c{};
-        unit_loc(a, sp.nsub, u, sub, c.part, c.row);
-        float acc = 0.0f;
-        for (c.sg = 0; c.sg < sp.nseg; c.sg++) {
-          const int pos = sp.base + int(u - sp.u0) * per_unit + sub * sp.nseg + c.sg;
-          const int slot = pos % nslot;
-          bool ok = !s_abort;
-          if (ok && !mbar_wait_or_abort(full0 + 8 * slot, uint32_t((pos / nslot) & 1), limit, &s_abort)) {
-            if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
-            if (lane == 0) s_abort = 1;
-            ok = false;
-          }
-          if (ok) {
-            const SegInfo sg = seg_info<FMT>(a, nb, c);
-            const uint8_t *W = ring + slot * slot_bytes<FMT>();
-            const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
-            // Full 32-block chunks: lane t takes block t; lanes 0..7 then
-            // add the terms of blocks t, t+8, t+16, t+24 in order.
-            const int nfull = sg.nblk >> 5;
-#pragma unroll 2
-            for (int ch = 0; ch < nfull; ch++) {
-              const int bb = ch * 32 + lane;
-              const float term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
-#pragma unroll
-              for (int q = 0; q < 4; q++) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q));
-            }
-            if (sg.nblk & 31) {
-              // A partial chunk: blocks past the row are skipped, not added.
-              const int bb = nfull * 32 + lane;
-              float term = 0.0f;
-              if (bb < sg.nblk) term = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
-#pragma unroll
-              for (int q = 0; q < 4; q++) {
-                const float t = __shfl_sync(0xffffffffu, term, (lane & 7) + 8 * q);
-                if (nfull * 32 + (lane & 7) + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
-              }
-            }
-          }
-          __syncwarp();
-          if (lane == 0 && ok) mbar_arrive(empty0 + 8 * slot);
+    const int per_unit = sp.nsub * sp.nseg, nsegs = sp.segments();
+    for (int i = warp; i < nsegs; i += WARPS) {
+      const int pos = sp.base + i;
+      const int ui = i / per_unit, rem = i - ui * per_unit;
+      const int sub = rem / sp.nseg, sgi = rem - sub * sp.nseg;
+      Cursor c{};
+      unit_loc(a, sp.nsub, sp.u0 + ui, sub, c.part, c.row);
+      c.sg = sgi;
+      const int fill = pos / nslot, slot = pos - fill * nslot;
+      bool ok = !s_abort;
+      if (ok && s_fill[slot] <= fill) {
+        const uint64_t t0 = globaltimer_ns();
+        while (s_fill[slot] <= fill && !s_abort && globaltimer_ns() - t0 <= limit) {
         }
+      }
+      __threadfence_block();
+      if (ok && (s_fill[slot] <= fill ||
+                 !mbar_wait_or_abort(full0 + 8 * slot, uint32_t(fill & 1), limit, &s_abort))) {
+        if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
+        if (lane == 0) s_abort = 1;
+        ok = false;
+      }
+      // The segment's block terms: lane t holds blocks t, t+32, t+64, ...
+      const SegInfo sg = seg_info<FMT>(a, nb, c);
+      float term[T::kSegBlocks / 32];
+#pragma unroll
+      for (int ch = 0; ch < T::kSegBlocks / 32; ch++) term[ch] = 0.0f;
+      if (ok) {
+        const uint8_t *W = ring + slot * slot_bytes<FMT>();
+        const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
+#pragma unroll
+        for (int ch = 0; ch < T::kSegBlocks / 32; ch++) {
+          const int bb = ch * 32 + lane;
+          if (bb < sg.nblk) term[ch] = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
+        }
+      }
+      // The running sums so far (a segment after the first of its unit),
+      // taken before the slot is released.
+      float acc = 0.0f, r0 = 0.0f;
+      if (rem > 0 && ok) {
+        Carry &cr = carry[pos % kCarries];
+        if (cr.seq != pos) {
+          const uint64_t t0 = globaltimer_ns();
+          while (cr.seq != pos && !s_abort && globaltimer_ns() - t0 <= limit) {
+          }
+        }
+        if (cr.seq != pos) {
+          if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
+          if (lane == 0) s_abort = 1;
+          ok = false;
+        } else {
+          __threadfence_block();
+          acc = cr.acc[lane & 7];
+          r0 = cr.r0;
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(empty0 + 8 * slot);
+      if (!ok) continue;
+      // qrow's eight chains: lanes 0..7 add the terms of blocks t, t+8,
+      // t+16, t+24 of each 32-block chunk in order; blocks past the row are
+      // skipped, not added.
+#pragma unroll
+      for (int ch = 0; ch < T::kSegBlocks / 32; ch++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float t = __shfl_sync(0xffffffffu, term[ch], (lane & 7) + 8 * q);
+          if (ch * 32 + (lane & 7) + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
+        }
+      }
+      if (sgi == sp.nseg - 1) {
         const float r = combine8(acc);
-        if (lane == 0 && !s_abort) {
+        if (sp.nsub == 2 && sub == 0) {
+          r0 = r;  // W1's row; W3's sums start from zero
+          acc = 0.0f;
+        } else if (lane == 0) {
           float *out = a.part[c.part].out;
           float v = r;
-          bool put = true;
           switch (a.epi) {
             case EPI_STORE: break;
             case EPI_ADD: v = __fadd_rn(out[c.row], r); break;
             case EPI_ADD_CANON: v = canonical(__fadd_rn(out[c.row], r)); break;
             case EPI_SILU:
-              if (sub == 0) {
-                r0 = r;
-                put = false;
-              } else {
-                v = __fmul_rn(silu(r0), r);
-                out = a.part[0].out;
-              }
+              v = __fmul_rn(silu(r0), r);
+              out = a.part[0].out;
               break;
           }
-          if (put) {
-            out[c.row] = v;
-            if (c.part == 0 || a.epi == EPI_SILU)
-              for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + c.row, v, put_tag);
-          }
+          out[c.row] = v;
+          if (c.part == 0 || a.epi == EPI_SILU)
+            for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + c.row, v, put_tag);
         }
+      }
+      if (rem < per_unit - 1) {
+        Carry &cw = carry[(pos + 1) % kCarries];
+        if (lane < 8) cw.acc[lane] = acc;
+        if (lane == 0) cw.r0 = r0;
+        __syncwarp();
+        __threadfence_block();
+        if (lane == 0) cw.seq = pos + 1;
       }
     }
   }
@@ -1083,7 +1155,7 @@ cudaError_t init_matvec_attributes() {
 // Staging of a chain: x in chunks of sf floats (the largest of 8192, 4096,
 // 2048 that leaves a ring of kChainMinSlots), the norm weights beside them
 // for the steps that normalise; the rest of the CTA's shared memory is ring.
-constexpr int kChainMinSlots = 24, kChainMaxSlots = 64;
+constexpr int kChainMinSlots = 24, kChainMaxSlots = kChainSlotsMax;
 
 static ChainSmem chain_layout(int fmt, int mc, int sf, int wsf, int nslot) {
   return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, wsf, nslot) : chain_smem<FMT_Q4_0>(mc, sf, wsf, nslot);

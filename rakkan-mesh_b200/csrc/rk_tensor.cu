@@ -512,6 +512,18 @@ __global__ void k_ten_argmax(const T *a, int rows, int cols, int *out) {
 
 static int ten_grid(long long n) { return (int)std::min<long long>((n + 255) / 256, 148LL * 16); }
 
+// decodeInto's float32 load (tensor.go:186-192): every NaN becomes the
+// canonical NaN, in place.
+__global__ void k_ten_canon(float *p, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    p[i] = canonical(p[i]);
+}
+cudaError_t launch_tensor_canon(long long n, float *p, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_ten_canon<<<ten_grid(n), 256, 0, st>>>(p, n);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_tensor_add(int dtype, int rows, int cols, const void *a, const void *b, int b_rows, void *c,
                               cudaStream_t st) {
   const long long n = (long long)rows * cols;

@@ -27,6 +27,8 @@ cudaError_t launch_tensor_relu(int dtype, long long n, const void *a, void *c, c
 cudaError_t launch_tensor_quantize(long long n, const float *a, float k, int8_t *c, cudaStream_t st);
 cudaError_t launch_tensor_softmax(int rows, int cols, const float *a, float *c, cudaStream_t st);
 cudaError_t launch_tensor_argmax(int dtype, int rows, int cols, const void *a, int *out, cudaStream_t st);
+// decodeInto's canonicalisation of loaded float32 values, in place.
+cudaError_t launch_tensor_canon(long long n, float *p, cudaStream_t st);
 
 // Whether an int8 product of this shape and these operand addresses can use
 // the tensor-core kernel (16-byte aligned operands and rows, k < 2^17).

@@ -39,6 +39,9 @@ EXPORTS = [
     "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
     "rk_tensor_add", "rk_tensor_scale", "rk_tensor_relu", "rk_tensor_softmax", "rk_tensor_quantize", "rk_tensor_argmax",
     "rk_layer_load_part", "rk_embed_load_part", "rk_head_load_part", "rk_matmul_bf16", "rk_measure_speed",
+    "rk_tensors_new", "rk_tensors_free", "rk_tensors_used", "rk_tensors_from_memory", "rk_tensors_from_blob",
+    "rk_tensors_to_memory", "rk_tensors_dim", "rk_tensors_release", "rk_tensors_matmul", "rk_tensors_add",
+    "rk_tensors_scale", "rk_tensors_relu", "rk_tensors_softmax", "rk_tensors_quantize", "rk_tensors_argmax",
 ]
 
 
@@ -137,6 +140,12 @@ def lib():
             "rk_tensor_add": (i, [vp, i, i, i, vp, vp, i, vp]), "rk_tensor_scale": (i, [vp, i, i, i, vp, f, vp]),
             "rk_tensor_relu": (i, [vp, i, i, i, vp, vp]), "rk_tensor_softmax": (i, [vp, i, i, i, vp, vp]),
             "rk_tensor_quantize": (i, [vp, i, i, i, vp, f, vp]), "rk_tensor_argmax": (i, [vp, i, i, i, vp, vp]),
+            "rk_tensors_new": (i, [vp, i64, vp]), "rk_tensors_free": (None, [vp]), "rk_tensors_used": (i64, [vp]),
+            "rk_tensors_from_memory": (i, [vp, vp, i, i, i]), "rk_tensors_from_blob": (i, [vp, vp, i64, i64, i, i, i]),
+            "rk_tensors_to_memory": (i64, [vp, i, vp, i64]), "rk_tensors_dim": (i, [vp, i, i]),
+            "rk_tensors_release": (i, [vp, i]), "rk_tensors_matmul": (i, [vp, i, i, i]), "rk_tensors_add": (i, [vp, i, i]),
+            "rk_tensors_scale": (i, [vp, i, f]), "rk_tensors_relu": (i, [vp, i]), "rk_tensors_softmax": (i, [vp, i]),
+            "rk_tensors_quantize": (i, [vp, i, f]), "rk_tensors_argmax": (i, [vp, i, vp, i64]),
             "rk_layer_load_part": (i, [vp, vp, vp, i64, vp]), "rk_embed_load_part": (i, [vp, vp, vp, i64, vp]),
             "rk_head_load_part": (i, [vp, vp, vp, i64, vp, vp, vp]),
             "rk_matmul_bf16": (i, [vp, i, vp, vp]), "rk_measure_speed": (i, [vp, vp]),
@@ -723,3 +732,78 @@ def quantize(dev, fmt, w):
     s = np.empty(w.size // 32, dtype=np.float32)
     _check(lib().rk_quantize(dev.h, fmt, _ptr(w), w.size, _ptr(q), _ptr(s)))
     return q, s
+
+
+class Tensors:
+    """rakkan_tensor_v1's tensor table on a device (rk_tensors_*): handles of
+    device-resident tensors; the calls return a handle, or raise RkError
+    with the reference's error code (RK_ERR_ARGS / TOO_BIG / BLOB)."""
+
+    DTYPES = {np.dtype(np.float32): TENSOR_F32, np.dtype(np.int8): TENSOR_I8, np.dtype(np.int32): TENSOR_I32}
+    NP = {TENSOR_F32: np.float32, TENSOR_I8: np.int8, TENSOR_I32: np.int32}
+
+    def __init__(self, dev, budget):
+        self.dev = dev
+        self.h = C.c_void_p()
+        _check(lib().rk_tensors_new(dev.h, budget, C.byref(self.h)))
+
+    @staticmethod
+    def _h(rc):
+        if rc < 0:
+            raise RkError(rc, lib().rk_last_error().decode())
+        return rc
+
+    def from_memory(self, a):
+        a = np.ascontiguousarray(a)
+        rows, cols = a.shape if a.ndim == 2 else (1, a.size)
+        return self._h(lib().rk_tensors_from_memory(self.h, _ptr(a), self.DTYPES[a.dtype], rows, cols))
+
+    def from_blob(self, blob, offset, dtype, rows, cols):
+        blob = np.frombuffer(bytes(blob), np.uint8) if not isinstance(blob, np.ndarray) else blob
+        return self._h(lib().rk_tensors_from_blob(self.h, _ptr(blob), blob.nbytes, offset, dtype, rows, cols))
+
+    def dims(self, t):
+        return tuple(self._h(lib().rk_tensors_dim(self.h, t, w)) for w in range(3))
+
+    def to_numpy(self, t):
+        rows, cols, dt = self.dims(t)
+        out = np.empty((rows, cols), self.NP[dt])
+        got = lib().rk_tensors_to_memory(self.h, t, _ptr(out), out.nbytes)
+        self._h(got)
+        assert got == out.nbytes
+        return out
+
+    def matmul(self, a, b, transposed=False):
+        return self._h(lib().rk_tensors_matmul(self.h, a, b, 1 if transposed else 0))
+
+    def add(self, a, b):
+        return self._h(lib().rk_tensors_add(self.h, a, b))
+
+    def scale(self, a, k):
+        return self._h(lib().rk_tensors_scale(self.h, a, k))
+
+    def relu(self, a):
+        return self._h(lib().rk_tensors_relu(self.h, a))
+
+    def softmax(self, a):
+        return self._h(lib().rk_tensors_softmax(self.h, a))
+
+    def quantize(self, a, k):
+        return self._h(lib().rk_tensors_quantize(self.h, a, k))
+
+    def argmax(self, a):
+        rows = self.dims(a)[0]
+        out = np.empty(rows, np.int32)
+        self._h(lib().rk_tensors_argmax(self.h, a, _ptr(out), out.nbytes))
+        return out
+
+    def release(self, t):
+        self._h(lib().rk_tensors_release(self.h, t))
+
+    def used(self):
+        return lib().rk_tensors_used(self.h)
+
+    def free(self):
+        if self.h:
+            lib().rk_tensors_free(self.h)
+            self.h = C.c_void_p()
