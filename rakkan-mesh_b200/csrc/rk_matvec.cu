@@ -773,18 +773,29 @@ RK_DEV bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, unsigned long long
   }
 }
 
+// A slot's fill count, published with release semantics after the fill's
+// mbarrier arrive, and read with acquire semantics before a consumer's wait.
+RK_DEV void st_release_shared(const volatile int *p, int v) {
+  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_addr((const void *)p)), "r"(v) : "memory");
+}
+RK_DEV int ld_acquire_shared(const volatile int *p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr((const void *)p)) : "memory");
+  return v;
+}
+
 RK_DEV void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-constexpr int kChainWarps = 16;  // consumer warps of a chain CTA (plus one producer warp)
-constexpr int kChainIssuers = 8;  // lanes of the producer warp that issue copies
+constexpr int kChainWarps = 12;     // consumer warps of a chain CTA
+constexpr int kChainProducers = 8;  // producer warps (lane 0 of each issues copies)
 constexpr int kChainSlotsMax = 64;
 
 // Warp-specialised: WARPS consumer warps (threads 0..32·WARPS-1, named
-// barrier 1 for their CTA-wide phases) and one producer warp. The producer
-// walks the CTA's segments of every step in order and copies each into the
-// next slot of a CTA-wide ring (1-D bulk copies, completion on the slot's
+// barrier 1 for their CTA-wide phases) and PRODUCERS producer warps. The
+// producers walk the CTA's segments of every step in order and copy each
+// into the next slot of a CTA-wide ring (1-D bulk copies, completion on the slot's
 // full mbarrier; never multicast), waiting on the slot's empty mbarrier
 // before reusing it. It reads only weights, which no kernel writes, so it
 // waits for no step's input: while the consumers stage one step's input the
@@ -798,9 +809,10 @@ constexpr int kChainSlotsMax = 64;
 // segment's block terms are computed at once, and only qrow's eight sums
 // run in block order from warp to warp.
 //
-// Producer lane j (of kChainIssuers) issues positions j, j+kChainIssuers,
-// ...; a copy's issue is a handful of instructions, but one thread issuing
-// every copy of an SM could not keep HBM busy.
+// Producer warp j (of PRODUCERS) issues positions j, j+PRODUCERS, ... from
+// its lane 0: a warp's bulk-copy issues go one after another, and one warp
+// issuing every copy of an SM does not keep HBM busy (measured: about
+// 1.5 TB/s over the GPU), so the issuing is spread over warps.
 //
 // Warps run ahead of one another, so a consumer may reach position p while
 // the slot's previous fill (p - nslot) has not landed; a parity wait would
@@ -808,8 +820,8 @@ constexpr int kChainSlotsMax = 64;
 // first waits until the slot's fill count (s_fill) shows p's fill issued:
 // a lane issues p only after the consumer of p - nslot released the slot,
 // so the slot's phase is then the one p fills.
-template <int FMT, int WARPS>
-__global__ void __launch_bounds__((WARPS + 1) * 32, 1)
+template <int FMT, int WARPS, int PRODUCERS>
+__global__ void __launch_bounds__((WARPS + PRODUCERS) * 32, 1)
     k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf, int nslot) {
   using T = QTraits<FMT>;
   using Grp = ThreadGroup<WARPS * 32>;
@@ -844,9 +856,10 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
   __syncthreads();
   griddep_trigger();
 
-  if (warp == WARPS) {
-    // ---- producer ----
-    if (lane >= kChainIssuers) return;
+  if (warp >= WARPS) {
+    // ---- producers ----
+    const int pw = warp - WARPS;
+    if (lane != 0) return;
     const uint64_t pol = evict_first_policy();
     int pos = 0, base = 0;
     bool stop = false;
@@ -860,7 +873,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
           Cursor c{};
           unit_loc(a, sp.nsub, u, sub, c.part, c.row);
           for (c.sg = 0; c.sg < sp.nseg; c.sg++, pos++) {
-            if (pos % kChainIssuers != lane) continue;
+            if (pos % PRODUCERS != pw) continue;
             const int fill = pos / nslot, slot = pos - fill * nslot;
             if (fill > 0 &&
                 !mbar_wait_or_abort(empty0 + 8 * slot, uint32_t((fill - 1) & 1), limit, &s_abort)) {
@@ -877,16 +890,15 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
             mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
             bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
             bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
-            __threadfence_block();
-            s_fill[slot] = fill + 1;
+            st_release_shared(&s_fill[slot], fill + 1);
           }
         }
     }
-    // No copy may still be in flight when the CTA ends: wait for this lane's
+    // No copy may still be in flight when the CTA ends: wait for this warp's
     // fills among the last nslot positions (done at once unless the
     // consumers stopped early).
     for (int p = pos > nslot ? pos - nslot : 0; p < pos; p++)
-      if (p % kChainIssuers == lane) mbar_wait_bounded(full0 + 8 * (p % nslot), uint32_t((p / nslot) & 1), limit);
+      if (p % PRODUCERS == pw) mbar_wait_bounded(full0 + 8 * (p % nslot), uint32_t((p / nslot) & 1), limit);
     return;
   }
 
@@ -939,13 +951,12 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, 1)
       c.sg = sgi;
       const int fill = pos / nslot, slot = pos - fill * nslot;
       bool ok = !s_abort;
-      if (ok && s_fill[slot] <= fill) {
+      if (ok && ld_acquire_shared(&s_fill[slot]) <= fill) {
         const uint64_t t0 = globaltimer_ns();
-        while (s_fill[slot] <= fill && !s_abort && globaltimer_ns() - t0 <= limit) {
+        while (ld_acquire_shared(&s_fill[slot]) <= fill && !s_abort && globaltimer_ns() - t0 <= limit) {
         }
       }
-      __threadfence_block();
-      if (ok && (s_fill[slot] <= fill ||
+      if (ok && (ld_acquire_shared(&s_fill[slot]) <= fill ||
                  !mbar_wait_or_abort(full0 + 8 * slot, uint32_t(fill & 1), limit, &s_abort))) {
         if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
         if (lane == 0) s_abort = 1;
@@ -1144,10 +1155,10 @@ cudaError_t init_matvec_attributes() {
     e = cudaFuncSetAttribute(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kChainWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainProducers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kChainWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainProducers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   return e;
 }
@@ -1211,10 +1222,12 @@ cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t s
   if (!matvec_chain_ok(ca, num_sms)) return cudaErrorInvalidValue;
   int mc, sf, wsf;
   const ChainSmem L = chain_dims(ca, &mc, &sf, &wsf);
-  const int threads = (kChainWarps + 1) * 32;
+  const int threads = (kChainWarps + kChainProducers) * 32;
   if (ca.step[0].fmt == FMT_Q8_0)
-    return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps>, num_sms, threads, L.total, st, ca, mc, sf, wsf, L.nslot);
-  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps>, num_sms, threads, L.total, st, ca, mc, sf, wsf, L.nslot);
+    return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainProducers>, num_sms, threads, L.total, st, ca, mc, sf,
+                    wsf, L.nslot);
+  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainProducers>, num_sms, threads, L.total, st, ca, mc, sf,
+                  wsf, L.nslot);
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "librakkan_cuda.so")
 
 RK_OK, RK_ERR_ARGS, RK_ERR_TOO_BIG = 0, -1, -3
 RK_ERR_CUDA, RK_ERR_NOMEM, RK_ERR_TIMEOUT, RK_ERR_STATE = -10, -11, -12, -13
+RK_ERR_BLOB = -5
 FMT_F32, FMT_BF16, FMT_Q8_0, FMT_Q4_0 = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16, DTYPE_Q8_0, DTYPE_Q4_0, DTYPE_Q4_M = 0, 1, 2, 3, 4
 TENSOR_F32, TENSOR_I8, TENSOR_I32 = 0, 1, 2

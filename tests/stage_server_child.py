@@ -2,7 +2,8 @@
 seeded synthetic model of the given config on GPU 0, serves its layers
 through stage_server.StageServer, prints its port, and serves until
 killed. With --fail-after N it drops a stage's connection on its N-th
-forward (a simulated crash)."""
+forward (a simulated crash); --fail-from L limits that to the shard
+starting at layer L."""
 import argparse
 import json
 import os
@@ -19,6 +20,7 @@ p = argparse.ArgumentParser()
 p.add_argument("--config", required=True)
 p.add_argument("--seed", type=int, required=True)
 p.add_argument("--fail-after", type=int, default=0)
+p.add_argument("--fail-from", type=int, default=-1, help="only the shard starting at this layer fails")
 args = p.parse_args()
 over = json.loads(args.config)
 c = synth.config("", over.pop("dtype", "q8_0"), **over)
@@ -29,6 +31,8 @@ count = {}
 
 def fail_next(shard):
     count[shard] = count.get(shard, 0) + 1
+    if args.fail_from >= 0 and shard[1] != args.fail_from:
+        return False
     return args.fail_after > 0 and count[shard] == args.fail_after
 
 

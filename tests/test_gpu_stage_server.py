@@ -29,9 +29,10 @@ CFG = dict(dim=256, hidden=384, layers=4, heads=4, kv_heads=2, vocab=64, seq_len
 SEED = 17
 
 
-def start_server(fail_after=0):
+def start_server(fail_after=0, fail_from=-1):
     p = subprocess.Popen([sys.executable, os.path.join(HERE, "stage_server_child.py"), "--config",
-                          json.dumps(dict(CFG, dtype="q8_0")), "--seed", str(SEED), "--fail-after", str(fail_after)],
+                          json.dumps(dict(CFG, dtype="q8_0")), "--seed", str(SEED), "--fail-after", str(fail_after),
+                          "--fail-from", str(fail_from)],
                          stdout=subprocess.PIPE, text=True)
     line = p.stdout.readline()
     if not line:
@@ -44,7 +45,7 @@ def test_pipeline_over_stage_servers_with_failover(dev):
     c = synth.config("", "q8_0", **CFG)
     dm = synth.DeviceModel(dev, c, SEED, keep_host=True)
     om = ro.OracleModel(c, SEED, weights=dm.host_weights)
-    pa, a = start_server(fail_after=4)
+    pa, a = start_server(fail_after=4, fail_from=2)
     pb, b = start_server()
     servers = {0: a, 1: b}
     opened = []
