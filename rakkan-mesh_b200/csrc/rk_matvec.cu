@@ -690,17 +690,15 @@ __host__ __device__ inline long long step_units(const MvArgs &a) {
 }
 
 // A CTA's part of a step: units [u0, u1) (the same split for steps of the
-// same unit count), segments per unit and sub-row, and where the step's
-// segments start in the CTA's stream of segments.
+// same unit count), segments per unit and sub-row.
 struct StepPart {
   long long u0, u1;
   int nsub, nseg;
-  int base;  // a CTA's segments per launch number far fewer than 2^31
   RK_DEV int segments() const { return int(u1 - u0) * nsub * nseg; }
 };
 
 template <int FMT>
-RK_DEV StepPart step_part(const MvArgs &a, long long cta, long long ncta, int base) {
+RK_DEV StepPart step_part(const MvArgs &a, long long cta, long long ncta) {
   using T = QTraits<FMT>;
   StepPart sp;
   const long long units = step_units(a);
@@ -708,7 +706,6 @@ RK_DEV StepPart step_part(const MvArgs &a, long long cta, long long ncta, int ba
   sp.u1 = units * (cta + 1) / ncta;
   sp.nsub = a.epi == EPI_SILU ? 2 : 1;
   sp.nseg = ((a.cols >> 5) + T::kSegBlocks - 1) / T::kSegBlocks;
-  sp.base = base;
   return sp;
 }
 
@@ -727,33 +724,49 @@ RK_DEV void unit_loc(const MvArgs &a, int nsub, long long u, int sub, int &part,
   row = int(u);
 }
 
-// Shared-memory layout of a chain CTA (host and device agree on it).
-struct ChainSmem {
-  int nslot, in_off, xs_off, xsum_off, stage_off, wstage_off, carry_off, ring_off, total;
+// A segment of a step's CTA part, from its index i: the unit, its sub-row,
+// and the segment of that row.
+struct SegRef {
+  int ui, rem, sub, sgi;
 };
+RK_DEV SegRef seg_ref(const StepPart &sp, int i) {
+  SegRef r;
+  const int per_unit = sp.nsub * sp.nseg;
+  r.ui = i / per_unit;
+  r.rem = i - r.ui * per_unit;
+  r.sub = r.rem / sp.nseg;
+  r.sgi = r.rem - r.sub * sp.nseg;
+  return r;
+}
 
 // A row's running state handed from the warp of one segment to the warp of
 // the next: qrow's eight sums, the finished W1 row of an EPI_SILU pair, and
-// the position it is for (the entry's reader waits until seq names it).
+// the position it is for. seq = -1: free; a reader frees the entry once it
+// has the state, and a writer waits for a free entry, so warps that run
+// ahead of one another never overwrite an unread entry.
 struct Carry {
   float acc[8];
   float r0;
   volatile int seq;
   int pad[2];
 };
-// Entries, indexed by the reader's position. More than the ring's slots:
-// a position is processed only while every position more than nslot before
-// it has released its slot, and a reader takes its carry before releasing,
-// so an entry is never rewritten before its reader has it.
 constexpr int kCarries = 128;
+
+// Shared-memory layout of a chain CTA (host and device agree on it).
+struct ChainSmem {
+  int nslot, in_off, xs_off, xsum_off, stage_off, wstage_off, carry_off, ring_off, total;
+};
 template <int FMT>
 __host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf, int nslot) {
   ChainSmem m;
   const int nb = max_cols / 32;
   m.nslot = nslot;
-  m.in_off = nslot * 16;  // a full and an empty mbarrier per slot
-  m.xs_off = m.in_off + ((max_cols + 15) & ~15);
-  m.xsum_off = m.xs_off + ((nb * 4 + 15) & ~15);
+  m.in_off = (nslot * 8 + 15) & ~15;  // a full mbarrier per slot
+  // qx is read 16 bytes past a partial chunk's last block at most 31
+  // blocks beyond the row (those terms are not added): keep a block of
+  // slack after it.
+  m.xs_off = m.in_off + ((max_cols + 32 * 32 + 15) & ~15);
+  m.xsum_off = m.xs_off + ((nb * 4 + 32 * 4 + 15) & ~15);
   m.stage_off = m.xsum_off + ((nb * 4 + 15) & ~15);
   m.wstage_off = m.stage_off + 4 * sf;
   m.carry_off = (m.wstage_off + 4 * wsf + 15) & ~15;
@@ -762,159 +775,158 @@ __host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf, i
   return m;
 }
 
-// Waits for the barrier's phase `parity`, for at most limit_ns, and gives up
-// at once when the CTA has been told to stop (*abort).
-RK_DEV bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, unsigned long long limit_ns, const volatile int *abort) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Waits on a volatile shared word with a bound (nanoseconds).
+RK_DEV bool spin_until_eq(const volatile int *w, int v, unsigned long long limit) {
+  if (*w == v) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort || globaltimer_ns() - t0 > limit_ns) return false;
+  while (*w != v)
+    if (globaltimer_ns() - t0 > limit) return false;
+  return true;
+}
+
+// Q8_0 block terms of 32-block chunk c of a segment, two lanes per block:
+// lane l takes half (l & 1) of block 32c + l/2 (ta) and of block
+// 32c + 16 + l/2 (tb), 16 consecutive bytes each, so the weight and input
+// loads of a warp are conflict-free; the pair's partial sums are added,
+// then term = float32(sum)·float32(ws·xs) as qrow forms it (quant.go:157-164).
+// qa / qb and xa / xb are the input's halves and scales for those blocks.
+RK_DEV void q8_pair_terms(const uint8_t *W, const float *S, int c, int nblk, int4 qa, int4 qb, float xa, float xb,
+                          float &ta, float &tb) {
+  const int lane = threadIdx.x & 31;
+  const int ba = 32 * c + (lane >> 1), bb = ba + 16;
+  int sa = 0, sb = 0;
+  if (ba < nblk) {
+    const int4 w = *reinterpret_cast<const int4 *>(W + 1024 * c + 16 * lane);
+    sa = __dp4a(w.x, qa.x, 0);
+    sa = __dp4a(w.y, qa.y, sa);
+    sa = __dp4a(w.z, qa.z, sa);
+    sa = __dp4a(w.w, qa.w, sa);
   }
+  if (bb < nblk) {
+    const int4 w = *reinterpret_cast<const int4 *>(W + 1024 * c + 512 + 16 * lane);
+    sb = __dp4a(w.x, qb.x, 0);
+    sb = __dp4a(w.y, qb.y, sb);
+    sb = __dp4a(w.z, qb.z, sb);
+    sb = __dp4a(w.w, qb.w, sb);
+  }
+  sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+  sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+  ta = __fmul_rn(__int2float_rn(sa), __fmul_rn(S[ba], xa));
+  tb = __fmul_rn(__int2float_rn(sb), __fmul_rn(S[bb], xb));
 }
 
-// A slot's fill count, published with release semantics after the fill's
-// mbarrier arrive, and read with acquire semantics before a consumer's wait.
-RK_DEV void st_release_shared(const volatile int *p, int v) {
-  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_addr((const void *)p)), "r"(v) : "memory");
-}
-RK_DEV int ld_acquire_shared(const volatile int *p) {
-  int v;
-  asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr((const void *)p)) : "memory");
-  return v;
-}
+constexpr int kChainWarps = 12;  // warps of a chain CTA
+constexpr int kChainDepth = 3;   // ring slots per warp
 
-RK_DEV void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-constexpr int kChainWarps = 12;     // consumer warps of a chain CTA
-constexpr int kChainProducers = 8;  // producer warps (lane 0 of each issues copies)
-constexpr int kChainSlotsMax = 64;
-
-// Warp-specialised: WARPS consumer warps (threads 0..32·WARPS-1, named
-// barrier 1 for their CTA-wide phases) and PRODUCERS producer warps. The
-// producers walk the CTA's segments of every step in order and copy each
-// into the next slot of a CTA-wide ring (1-D bulk copies, completion on the slot's
-// full mbarrier; never multicast), waiting on the slot's empty mbarrier
-// before reusing it. It reads only weights, which no kernel writes, so it
-// waits for no step's input: while the consumers stage one step's input the
-// ring fills with that step's weights, and at a step's end the ring keeps
-// the SM's copies in flight however few warps still have rows. Consumer
-// warp w takes the CTA's segments w, w+WARPS, ... of each step, so the
-// positions being worked on span about WARPS slots and the rest of the ring
-// is in flight; a segment's slot and phase follow from its position. A row
-// of several segments, and the two rows of an EPI_SILU pair, pass their
-// running state to the next segment's warp through a Carry entry: every
-// segment's block terms are computed at once, and only qrow's eight sums
-// run in block order from warp to warp.
+// The chain kernel. One CTA per SM; warp w owns ring slots
+// [w·DEPTH, (w+1)·DEPTH) and takes segments w, w+WARPS, ... of the CTA's
+// part of each step (so the warps' shares of a step differ by one segment
+// at most). Lane 0 keeps DEPTH of the warp's segments in flight (1-D bulk
+// copies, completion on the slot's mbarrier; never multicast), running on
+// into the next step's segments, since weights depend on no step's output:
+// while the warps stage one step's input, their rings fill with that
+// step's weights. A row of several segments, and the two rows of an
+// EPI_SILU pair, hand their running sums to the next segment's warp through
+// a Carry entry: every segment's block terms are formed at once, and only
+// qrow's eight sums run in block order from warp to warp.
 //
-// Producer warp j (of PRODUCERS) issues positions j, j+PRODUCERS, ... from
-// its lane 0: a warp's bulk-copy issues go one after another, and one warp
-// issuing every copy of an SM does not keep HBM busy (measured: about
-// 1.5 TB/s over the GPU), so the issuing is spread over warps.
-//
-// Warps run ahead of one another, so a consumer may reach position p while
-// the slot's previous fill (p - nslot) has not landed; a parity wait would
-// then see that older phase's parity as complete. A consumer therefore
-// first waits until the slot's fill count (s_fill) shows p's fill issued:
-// a lane issues p only after the consumer of p - nslot released the slot,
-// so the slot's phase is then the one p fills.
-template <int FMT, int WARPS, int PRODUCERS>
-__global__ void __launch_bounds__((WARPS + PRODUCERS) * 32, 1)
-    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf, int nslot) {
+// When every unit of a step has a number of segments dividing WARPS, each
+// warp always meets the same segment of its rows, and keeps that
+// segment's Q8_0 input in registers for the whole step: the segment's
+// shared-memory reads are then its weights and scales only.
+template <int FMT, int WARPS, int DEPTH>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf) {
   using T = QTraits<FMT>;
-  using Grp = ThreadGroup<WARPS * 32>;
+  using Grp = CtaGroup;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ volatile int s_abort;
-  __shared__ volatile int s_fill[kChainSlotsMax];  // fills issued into each slot
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ns = ca.nsteps;
-  const ChainSmem L = chain_smem<FMT>(max_cols, sf, wsf, nslot);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // full[nslot], empty[nslot]
+  const ChainSmem L = chain_smem<FMT>(max_cols, sf, wsf, WARPS * DEPTH);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
   int8_t *sqx = reinterpret_cast<int8_t *>(smem + L.in_off);
   float *sxs = reinterpret_cast<float *>(smem + L.xs_off);
   int *sxsum = reinterpret_cast<int *>(smem + L.xsum_off);
   float *stage = reinterpret_cast<float *>(smem + L.stage_off);
   float *wstage = reinterpret_cast<float *>(smem + L.wstage_off);
-  uint8_t *ring = smem + L.ring_off;
   Carry *carry = reinterpret_cast<Carry *>(smem + L.carry_off);
-  const uint32_t full0 = smem_addr(bars), empty0 = smem_addr(bars + nslot);
+  uint8_t *ring = smem + L.ring_off + warp * DEPTH * slot_bytes<FMT>();
+  const uint32_t bar0 = smem_addr(bars + warp * DEPTH);
   const long long cta = blockIdx.x, ncta = gridDim.x;
   const unsigned long long limit = ca.wait_ns ? ca.wait_ns : kWaitLimitNs;
   int *err = ca.step[0].err;
 
-  if (threadIdx.x == 0) {
-    s_abort = 0;
-    for (int k = 0; k < nslot; k++) {
-      s_fill[k] = 0;
-      mbar_init(full0 + 8 * k, 1);
-      mbar_init(empty0 + 8 * k, 1);
+  // ---- the warp's copies: lane 0 walks its segments (k, i) ----
+  uint64_t pol = 0;
+  int pk = 0, pi = warp, pslot = 0;
+  int issued = 0;  // lane 0: copies issued; every lane: segments consumed
+  int consumed = 0;
+  auto pseek = [&]() {  // to the first (step, index) at or after (pk, pi) with a segment
+    while (pk < ns) {
+      const StepPart sp = step_part<FMT>(ca.step[pk], cta, ncta);
+      if (pi < sp.segments()) return;
+      pk++;
+      pi = warp;
     }
+  };
+  auto issue = [&]() {
+    if (pk >= ns) return;
+    const MvArgs &a = ca.step[pk];
+    const StepPart sp = step_part<FMT>(a, cta, ncta);
+    const SegRef r = seg_ref(sp, pi);
+    Cursor c{};
+    unit_loc(a, sp.nsub, sp.u0 + r.ui, r.sub, c.part, c.row);
+    c.sg = r.sgi;
+    const SegInfo sg = seg_info<FMT>(a, a.cols >> 5, c);
+    uint8_t *dst = ring + pslot * slot_bytes<FMT>();
+    const uint32_t bar = bar0 + 8 * pslot;
+    // The slot's previous segment was read by this warp before this copy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
+    bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
+    bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
+    pslot = pslot + 1 == DEPTH ? 0 : pslot + 1;
+    issued++;
+    pi += WARPS;
+    pseek();
+  };
+  // Stops the warp after an expired wait: its copies still in flight (from
+  // segment `from` on) get a bounded chance to land, so none writes into the
+  // CTA's shared memory after the CTA ends.
+  bool dead = false;
+  auto die = [&](int from) {
+    if (lane == 0) {
+      atomicExch(err, DEV_ERR_TIMEOUT);
+      for (int q = from; q < issued; q++) mbar_wait_bounded(bar0 + 8 * (q % DEPTH), uint32_t((q / DEPTH) & 1), limit);
+    }
+    __syncwarp();
+    dead = true;
+  };
+  if (lane == 0) {
+    for (int k = 0; k < DEPTH; k++) mbar_init(bar0 + 8 * k, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    pol = evict_first_policy();
+    pseek();
   }
-  __syncthreads();
+  for (int e = threadIdx.x; e < kCarries; e += blockDim.x) carry[e].seq = -1;
+  __syncwarp();
+  // Weights are no kernel's output: the ring fills before the predecessor
+  // kernel ends, together with the first step's norm weights.
   griddep_trigger();
-
-  if (warp >= WARPS) {
-    // ---- producers ----
-    const int pw = warp - WARPS;
-    if (lane != 0) return;
-    const uint64_t pol = evict_first_policy();
-    int pos = 0, base = 0;
-    bool stop = false;
-    for (int k = 0; k < ns && !stop; k++) {
-      const MvArgs &a = ca.step[k];
-      const StepPart sp = step_part<FMT>(a, cta, ncta, base);
-      base += sp.segments();
-      const int nb = a.cols >> 5;
-      for (long long u = sp.u0; u < sp.u1 && !stop; u++)
-        for (int sub = 0; sub < sp.nsub && !stop; sub++) {
-          Cursor c{};
-          unit_loc(a, sp.nsub, u, sub, c.part, c.row);
-          for (c.sg = 0; c.sg < sp.nseg; c.sg++, pos++) {
-            if (pos % PRODUCERS != pw) continue;
-            const int fill = pos / nslot, slot = pos - fill * nslot;
-            if (fill > 0 &&
-                !mbar_wait_or_abort(empty0 + 8 * slot, uint32_t((fill - 1) & 1), limit, &s_abort)) {
-              if (!s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
-              s_abort = 1;
-              stop = true;
-              break;
-            }
-            // The slot's last reader released it through the empty
-            // mbarrier, which orders its reads before this copy's writes.
-            const SegInfo sg = seg_info<FMT>(a, nb, c);
-            uint8_t *dst = ring + slot * slot_bytes<FMT>();
-            const uint32_t bar = full0 + 8 * slot;
-            mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
-            bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
-            bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
-            st_release_shared(&s_fill[slot], fill + 1);
-          }
-        }
-    }
-    // No copy may still be in flight when the CTA ends: wait for this warp's
-    // fills among the last nslot positions (done at once unless the
-    // consumers stopped early).
-    for (int p = pos > nslot ? pos - nslot : 0; p < pos; p++)
-      if (p % PRODUCERS == pw) mbar_wait_bounded(full0 + 8 * (p % nslot), uint32_t((p / nslot) & 1), limit);
-    return;
-  }
-
-  // ---- consumers ----
-  for (int e = threadIdx.x; e < kCarries; e += WARPS * 32) carry[e].seq = -1;
+  if (lane == 0)
+    for (int k = 0; k < DEPTH; k++) issue();
   const bool norm0 = ca.step[0].pro == PRO_NORM_QUANT && ca.step[0].cols <= sf && !ca.step[0].wait.ll;
-  if (norm0) stage_load<Grp>(nullptr, ca.step[0].norm_w, 0, ca.step[0].cols, stage, wstage);
+  if (norm0) stage_load(nullptr, ca.step[0].norm_w, 0, ca.step[0].cols, stage, wstage);
   griddep_wait();
-  int base = 0;
+
+  int slot = 0;
+  uint32_t parity = 0;
   for (int k = 0; k < ns; k++) {
     const MvArgs &a = ca.step[k];
     const int cols = a.cols, nb = cols >> 5;
-    const StepPart sp = step_part<FMT>(a, cta, ncta, base);
-    base += sp.segments();
+    const StepPart sp = step_part<FMT>(a, cta, ncta);
     // ---- prologue: the step's input into shared memory as Q8_0 ----
-    Grp::sync();  // every consumer is done with the previous step
+    __syncthreads();  // every warp is done with the previous step
     if (sp.u1 > sp.u0) {
       const bool norm = a.pro == PRO_NORM_QUANT;
       const unsigned wtag = a.wait.ll ? gather_tag(*a.wait.epoch, a.wait.slot, a.wait.nslots) : 0u;
@@ -922,108 +934,138 @@ __global__ void __launch_bounds__((WARPS + PRODUCERS) * 32, 1)
       bool pre = false;
       if (k == 0 && !a.wait.ll) {
         // Plain input from the predecessor kernel (the first step only).
-        stage_load<Grp>(a.x, nullptr, 0, min(cols, sf), stage, wstage);
+        stage_load(a.x, nullptr, 0, min(cols, sf), stage, wstage);
         pre = true;
       } else if (single) {
-        if (norm) stage_load<Grp>(nullptr, a.norm_w, 0, cols, stage, wstage);
-        if (!ll_gather_load<Grp>(a.wait.ll, cols, wtag, stage, limit) && threadIdx.x == 0)
-          atomicExch(err, DEV_ERR_TIMEOUT);
+        if (norm) stage_load(nullptr, a.norm_w, 0, cols, stage, wstage);
+        if (!ll_gather_load(a.wait.ll, cols, wtag, stage, limit) && threadIdx.x == 0) atomicExch(err, DEV_ERR_TIMEOUT);
         pre = true;
       }
       __shared__ float s_inv;
       if (norm)
-        quantize_warps<true, false, Grp>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage,
-                                         sf, pre, 1, a.wait.ll, wtag, err, limit);
+        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage, sf, pre, 1,
+                             a.wait.ll, wtag, err, limit);
       else
-        quantize_warps<false, false, Grp>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sf,
-                                          pre, 1, a.wait.ll, wtag, err, limit);
-      Grp::sync();
+        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sf, pre, 1,
+                              a.wait.ll, wtag, err, limit);
+      __syncthreads();
     }
-    // ---- this warp's segments of the step ----
+    const int nsegs = sp.segments();
+    if (warp >= nsegs) continue;
     const unsigned put_tag = a.put.nll > 0 ? gather_tag(*a.put.epoch, a.put.slot, a.put.nslots) : 0u;
-    const int per_unit = sp.nsub * sp.nseg, nsegs = sp.segments();
+    const int per_unit = sp.nsub * sp.nseg;
+    // The Q8_0 input of this warp's segment, cached for the step when it is
+    // always the same segment.
+    constexpr int kChunks = T::kSegBlocks / 32;
+    const bool cached = FMT == FMT_Q8_0 && WARPS % per_unit == 0;
+    int4 qa[kChunks], qb[kChunks];
+    float xa[kChunks], xb[kChunks];
+    auto load_input = [&](int blk0) {
+#pragma unroll
+      for (int c = 0; c < kChunks; c++) {
+        const int ba = blk0 + 32 * c + (lane >> 1);
+        qa[c] = *reinterpret_cast<const int4 *>(sqx + 32 * ba + 16 * (lane & 1));
+        qb[c] = *reinterpret_cast<const int4 *>(sqx + 32 * (ba + 16) + 16 * (lane & 1));
+        xa[c] = sxs[ba];
+        xb[c] = sxs[ba + 16];
+      }
+    };
+    if (cached) {
+      const SegRef r = seg_ref(sp, warp);
+      load_input(r.sgi * T::kSegBlocks);
+    }
     for (int i = warp; i < nsegs; i += WARPS) {
-      const int pos = sp.base + i;
-      const int ui = i / per_unit, rem = i - ui * per_unit;
-      const int sub = rem / sp.nseg, sgi = rem - sub * sp.nseg;
+      const SegRef r = seg_ref(sp, i);
+      const int pos = i;  // within the step
       Cursor c{};
-      unit_loc(a, sp.nsub, sp.u0 + ui, sub, c.part, c.row);
-      c.sg = sgi;
-      const int fill = pos / nslot, slot = pos - fill * nslot;
-      bool ok = !s_abort;
-      if (ok && ld_acquire_shared(&s_fill[slot]) <= fill) {
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_shared(&s_fill[slot]) <= fill && !s_abort && globaltimer_ns() - t0 <= limit) {
-        }
-      }
-      if (ok && (ld_acquire_shared(&s_fill[slot]) <= fill ||
-                 !mbar_wait_or_abort(full0 + 8 * slot, uint32_t(fill & 1), limit, &s_abort))) {
-        if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
-        if (lane == 0) s_abort = 1;
-        ok = false;
-      }
-      // The segment's block terms: lane t holds blocks t, t+32, t+64, ...
+      unit_loc(a, sp.nsub, sp.u0 + r.ui, r.sub, c.part, c.row);
+      c.sg = r.sgi;
+      const bool last = r.sgi == sp.nseg - 1, final_row = last && !(sp.nsub == 2 && r.sub == 0);
+      // The residual's old value, fetched early (EPI_ADD, EPI_ADD_CANON).
+      float old = 0.0f;
+      if (final_row && lane == 0 && (a.epi == EPI_ADD || a.epi == EPI_ADD_CANON)) old = a.part[c.part].out[c.row];
+      if (!dead && !__all_sync(0xffffffffu, mbar_wait_bounded(bar0 + 8 * slot, parity, limit))) die(consumed + 1);
       const SegInfo sg = seg_info<FMT>(a, nb, c);
-      float term[T::kSegBlocks / 32];
+      const uint8_t *W = ring + slot * slot_bytes<FMT>();
+      const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
+      float term[kChunks], term2[kChunks];
 #pragma unroll
-      for (int ch = 0; ch < T::kSegBlocks / 32; ch++) term[ch] = 0.0f;
-      if (ok) {
-        const uint8_t *W = ring + slot * slot_bytes<FMT>();
-        const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
+      for (int ch = 0; ch < kChunks; ch++) term[ch] = term2[ch] = 0.0f;
+      if (!dead) {
+        if (FMT == FMT_Q8_0) {
+          if (!cached) load_input(sg.blk0);
 #pragma unroll
-        for (int ch = 0; ch < T::kSegBlocks / 32; ch++) {
-          const int bb = ch * 32 + lane;
-          if (bb < sg.nblk) term[ch] = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
-        }
-      }
-      // The running sums so far (a segment after the first of its unit),
-      // taken before the slot is released.
-      float acc = 0.0f, r0 = 0.0f;
-      if (rem > 0 && ok) {
-        Carry &cr = carry[pos % kCarries];
-        if (cr.seq != pos) {
-          const uint64_t t0 = globaltimer_ns();
-          while (cr.seq != pos && !s_abort && globaltimer_ns() - t0 <= limit) {
+          for (int ch = 0; ch < kChunks; ch++)
+            if (32 * ch < sg.nblk) q8_pair_terms(W, S, ch, sg.nblk, qa[ch], qb[ch], xa[ch], xb[ch], term[ch], term2[ch]);
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < kChunks; ch++) {
+            const int bb = ch * 32 + lane;
+            if (bb < sg.nblk) term[ch] = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
           }
         }
-        if (cr.seq != pos) {
-          if (lane == 0 && !s_abort) atomicExch(err, DEV_ERR_TIMEOUT);
-          if (lane == 0) s_abort = 1;
-          ok = false;
+      }
+      __syncwarp();
+      // The slot is read: its next segment's copy goes out now.
+      if (lane == 0 && !dead) issue();
+      slot = slot + 1 == DEPTH ? 0 : slot + 1;
+      if (slot == 0) parity ^= 1;
+      consumed++;
+      // The running sums so far (a segment after the first of its unit).
+      float acc = 0.0f, r0 = 0.0f;
+      if (r.rem > 0 && !dead) {
+        Carry &cr = carry[(k * 7919 + pos) % kCarries];
+        if (!__all_sync(0xffffffffu, spin_until_eq(&cr.seq, pos, limit))) {
+          die(consumed);
         } else {
           __threadfence_block();
           acc = cr.acc[lane & 7];
           r0 = cr.r0;
+          __syncwarp();
+          if (lane == 0) cr.seq = -1;
         }
       }
-      __syncwarp();
-      if (lane == 0 && ok) mbar_arrive(empty0 + 8 * slot);
-      if (!ok) continue;
-      // qrow's eight chains: lanes 0..7 add the terms of blocks t, t+8,
-      // t+16, t+24 of each 32-block chunk in order; blocks past the row are
+      if (dead) continue;
+      // qrow's eight chains: lane j < 8 adds the terms of blocks j, j+8,
+      // j+16, j+24 of each chunk in order; blocks past the row are
       // skipped, not added.
+      const int j = lane & 7;
 #pragma unroll
-      for (int ch = 0; ch < T::kSegBlocks / 32; ch++) {
+      for (int ch = 0; ch < kChunks; ch++) {
+        if (FMT == FMT_Q8_0) {
+          // Block 32ch + b lies in lane 2b's first term (b < 16) or lane
+          // 2(b - 16)'s second.
+          const float t0 = __shfl_sync(0xffffffffu, term[ch], 2 * j);
+          const float t1 = __shfl_sync(0xffffffffu, term[ch], 2 * j + 16);
+          const float t2 = __shfl_sync(0xffffffffu, term2[ch], 2 * j);
+          const float t3 = __shfl_sync(0xffffffffu, term2[ch], 2 * j + 16);
+          const int b0 = 32 * ch + j;
+          if (b0 < sg.nblk) acc = __fadd_rn(acc, t0);
+          if (b0 + 8 < sg.nblk) acc = __fadd_rn(acc, t1);
+          if (b0 + 16 < sg.nblk) acc = __fadd_rn(acc, t2);
+          if (b0 + 24 < sg.nblk) acc = __fadd_rn(acc, t3);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          const float t = __shfl_sync(0xffffffffu, term[ch], (lane & 7) + 8 * q);
-          if (ch * 32 + (lane & 7) + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
+          for (int q = 0; q < 4; q++) {
+            const float t = __shfl_sync(0xffffffffu, term[ch], j + 8 * q);
+            if (ch * 32 + j + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
+          }
         }
       }
-      if (sgi == sp.nseg - 1) {
-        const float r = combine8(acc);
-        if (sp.nsub == 2 && sub == 0) {
-          r0 = r;  // W1's row; W3's sums start from zero
+      if (last) {
+        const float rr = combine8(acc);
+        if (!final_row) {
+          r0 = rr;  // W1's row; W3's sums start from zero
           acc = 0.0f;
         } else if (lane == 0) {
           float *out = a.part[c.part].out;
-          float v = r;
+          float v = rr;
           switch (a.epi) {
             case EPI_STORE: break;
-            case EPI_ADD: v = __fadd_rn(out[c.row], r); break;
-            case EPI_ADD_CANON: v = canonical(__fadd_rn(out[c.row], r)); break;
+            case EPI_ADD: v = __fadd_rn(old, rr); break;
+            case EPI_ADD_CANON: v = canonical(__fadd_rn(old, rr)); break;
             case EPI_SILU:
-              v = __fmul_rn(silu(r0), r);
+              v = __fmul_rn(silu(r0), rr);
               out = a.part[0].out;
               break;
           }
@@ -1032,8 +1074,12 @@ __global__ void __launch_bounds__((WARPS + PRODUCERS) * 32, 1)
             for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + c.row, v, put_tag);
         }
       }
-      if (rem < per_unit - 1) {
-        Carry &cw = carry[(pos + 1) % kCarries];
+      if (r.rem < per_unit - 1) {
+        Carry &cw = carry[(k * 7919 + pos + 1) % kCarries];
+        if (!__all_sync(0xffffffffu, spin_until_eq(&cw.seq, -1, limit))) {
+          die(consumed);
+          continue;
+        }
         if (lane < 8) cw.acc[lane] = acc;
         if (lane == 0) cw.r0 = r0;
         __syncwarp();
@@ -1155,20 +1201,19 @@ cudaError_t init_matvec_attributes() {
     e = cudaFuncSetAttribute(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainProducers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainDepth>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainProducers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainDepth>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   return e;
 }
 
 // Staging of a chain: x in chunks of sf floats (the largest of 8192, 4096,
-// 2048 that leaves a ring of kChainMinSlots), the norm weights beside them
-// for the steps that normalise; the rest of the CTA's shared memory is ring.
-constexpr int kChainMinSlots = 24, kChainMaxSlots = kChainSlotsMax;
-
-static ChainSmem chain_layout(int fmt, int mc, int sf, int wsf, int nslot) {
+// 2048 that fits beside the rings), the norm weights beside them for the
+// steps that normalise.
+static ChainSmem chain_layout(int fmt, int mc, int sf, int wsf) {
+  const int nslot = kChainWarps * kChainDepth;
   return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, wsf, nslot) : chain_smem<FMT_Q4_0>(mc, sf, wsf, nslot);
 }
 
@@ -1176,23 +1221,19 @@ static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *ws
   int mc = 0;
   for (int k = 0; k < ca.nsteps; k++) mc = std::max(mc, ca.step[k].cols);
   const int fmt = ca.nsteps > 0 ? ca.step[0].fmt : FMT_Q8_0;
-  const int sb = fmt == FMT_Q8_0 ? slot_bytes<FMT_Q8_0>() : slot_bytes<FMT_Q4_0>();
-  ChainSmem best{};
+  ChainSmem L{};
   for (int cand : {8192, 4096, 2048}) {
     const int f = std::min(mc, cand);
     int wf = 0;
     for (int k = 0; k < ca.nsteps; k++)
       if (ca.step[k].pro == PRO_NORM_QUANT) wf = std::max(wf, std::min(ca.step[k].cols, f));
-    const ChainSmem zero = chain_layout(fmt, mc, f, wf, 0);
-    int n = std::min((kSmemLimit - zero.total) / (sb + 16), kChainMaxSlots);
-    while (n > 0 && chain_layout(fmt, mc, f, wf, n).total > kSmemLimit) n--;
     *max_cols = mc;
     *sf = f;
     *wsf = wf;
-    best = chain_layout(fmt, mc, f, wf, std::max(n, 0));
-    if (n >= kChainMinSlots) break;
+    L = chain_layout(fmt, mc, f, wf);
+    if (L.total <= kSmemLimit) break;
   }
-  return best;
+  return L;
 }
 
 bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
@@ -1209,8 +1250,7 @@ bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
     if (step_units(a) < num_sms) return false;
   }
   int mc, sf, wsf;
-  const ChainSmem L = chain_dims(ca, &mc, &sf, &wsf);
-  return L.nslot >= kChainMinSlots && L.total <= kSmemLimit;
+  return chain_dims(ca, &mc, &sf, &wsf).total <= kSmemLimit;
 }
 
 int matvec_chain_smem(const ChainArgs &ca) {
@@ -1222,12 +1262,11 @@ cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t s
   if (!matvec_chain_ok(ca, num_sms)) return cudaErrorInvalidValue;
   int mc, sf, wsf;
   const ChainSmem L = chain_dims(ca, &mc, &sf, &wsf);
-  const int threads = (kChainWarps + kChainProducers) * 32;
+  const int threads = kChainWarps * 32;
   if (ca.step[0].fmt == FMT_Q8_0)
-    return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainProducers>, num_sms, threads, L.total, st, ca, mc, sf,
-                    wsf, L.nslot);
-  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainProducers>, num_sms, threads, L.total, st, ca, mc, sf,
-                  wsf, L.nslot);
+    return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf,
+                    wsf);
+  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf, wsf);
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
