@@ -724,53 +724,108 @@ RK_DEV void unit_loc(const MvArgs &a, int nsub, long long u, int sub, int &part,
   row = int(u);
 }
 
-// A segment of a step's CTA part, from its index i: the unit, its sub-row,
-// and the segment of that row.
-struct SegRef {
-  int ui, rem, sub, sgi;
+// A segment's place in a step's CTA part: unit, sub-row, segment of the
+// row. next() steps to the following segment without dividing.
+struct SegPos {
+  int ui, sub, sgi;
+  RK_DEV void next(const StepPart &sp) {
+    if (++sgi < sp.nseg) return;
+    sgi = 0;
+    if (++sub < sp.nsub) return;
+    sub = 0;
+    ui++;
+  }
+  RK_DEV int rem(const StepPart &sp) const { return sub * sp.nseg + sgi; }
 };
-RK_DEV SegRef seg_ref(const StepPart &sp, int i) {
-  SegRef r;
+RK_DEV SegPos seg_pos(const StepPart &sp, int i) {
+  SegPos p;
   const int per_unit = sp.nsub * sp.nseg;
-  r.ui = i / per_unit;
-  r.rem = i - r.ui * per_unit;
-  r.sub = r.rem / sp.nseg;
-  r.sgi = r.rem - r.sub * sp.nseg;
-  return r;
+  p.ui = i / per_unit;
+  const int rem = i - p.ui * per_unit;
+  p.sub = rem / sp.nseg;
+  p.sgi = rem - p.sub * sp.nseg;
+  return p;
 }
 
-// A row's running state handed from the warp of one segment to the warp of
-// the next: qrow's eight sums, the finished W1 row of an EPI_SILU pair, and
-// the position it is for. seq = -1: free; a reader frees the entry once it
-// has the state, and a writer waits for a free entry, so warps that run
-// ahead of one another never overwrite an unread entry.
+// A warp's walk over its contiguous range of a step's segments, with the
+// current segment's matrix part and row and the parts' base pointers kept
+// in registers, so that each step to the next segment is a few additions
+// (no division, and no look-up of the parts). Rows of a part are
+// contiguous, so a warp's segments within a part follow one another in
+// memory; an EPI_SILU pair alternates W1's and W3's rows.
+template <int FMT>
+struct SegStream {
+  SegPos p;
+  int part, row, nb;
+  const uint8_t *w0, *w1;  // weights of parts (nsub == 2: W1, W3; else w0, the current part)
+  const float *s0, *s1;
+  int rows;             // nsub == 1: rows of the current part
+  RK_DEV void load_part(const MvArgs &a, int k) {
+    w0 = a.part[k].w;
+    s0 = a.part[k].s;
+    rows = a.part[k].rows;
+  }
+  RK_DEV void init(const MvArgs &a, const StepPart &sp, int i) {
+    p = seg_pos(sp, i);
+    nb = a.cols >> 5;
+    unit_loc(a, sp.nsub, sp.u0 + p.ui, p.sub, part, row);
+    if (sp.nsub == 2) {
+      w0 = a.part[0].w;
+      s0 = a.part[0].s;
+      w1 = a.part[1].w;
+      s1 = a.part[1].s;
+    } else {
+      load_part(a, part);
+    }
+  }
+  RK_DEV void next(const MvArgs &a, const StepPart &sp) {
+    const int ui0 = p.ui;
+    p.next(sp);
+    if (sp.nsub == 2) {
+      part = p.sub;
+      row += p.ui - ui0;
+    } else if (p.ui != ui0 && ++row == rows) {
+      row = 0;
+      load_part(a, ++part);
+    }
+  }
+  // The segment: its first block and block count, and where its weights
+  // and scales are.
+  RK_DEV int blk0() const { return p.sgi * QTraits<FMT>::kSegBlocks; }
+  RK_DEV int nblk() const { return min(QTraits<FMT>::kSegBlocks, nb - blk0()); }
+  RK_DEV long long first_block() const { return (long long)row * nb + blk0(); }
+  RK_DEV const uint8_t *wsrc(int nsub) const {
+    return (nsub == 2 && part == 1 ? w1 : w0) + first_block() * QTraits<FMT>::kBlkBytes;
+  }
+  RK_DEV const float *scales(int nsub) const { return (nsub == 2 && part == 1 ? s1 : s0) + first_block(); }
+};
+
+// A unit's running state handed across a warp boundary: qrow's eight sums,
+// silu(W1's row) of an EPI_SILU pair, and the step it belongs to.
 struct Carry {
   float acc[8];
   float r0;
   volatile int seq;
   int pad[2];
 };
-constexpr int kCarries = 128;
 
 // Shared-memory layout of a chain CTA (host and device agree on it).
 struct ChainSmem {
-  int nslot, in_off, xs_off, xsum_off, stage_off, wstage_off, carry_off, ring_off, total;
+  int nslot, in_off, xs_off, xsum_off, stage_off, carry_off, ring_off, total;
 };
 template <int FMT>
-__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int wsf, int nslot) {
+__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int nslot, int warps) {
   ChainSmem m;
   const int nb = max_cols / 32;
   m.nslot = nslot;
   m.in_off = (nslot * 8 + 15) & ~15;  // a full mbarrier per slot
-  // qx is read 16 bytes past a partial chunk's last block at most 31
-  // blocks beyond the row (those terms are not added): keep a block of
-  // slack after it.
+  // A partial chunk's loads reach up to 31 blocks past the row (those terms
+  // are not added): keep that much slack after qx and xs.
   m.xs_off = m.in_off + ((max_cols + 32 * 32 + 15) & ~15);
   m.xsum_off = m.xs_off + ((nb * 4 + 32 * 4 + 15) & ~15);
-  m.stage_off = m.xsum_off + ((nb * 4 + 15) & ~15);
-  m.wstage_off = m.stage_off + 4 * sf;
-  m.carry_off = (m.wstage_off + 4 * wsf + 15) & ~15;
-  m.ring_off = (m.carry_off + kCarries * (int)sizeof(Carry) + 127) & ~127;
+  m.stage_off = m.xsum_off + (FMT == FMT_Q4_0 ? ((nb * 4 + 32 * 4 + 15) & ~15) : 0);  // xsum: Q4_0 only
+  m.carry_off = (m.stage_off + 4 * sf + 15) & ~15;
+  m.ring_off = (m.carry_off + (warps + 1) * (int)sizeof(Carry) + 127) & ~127;
   m.total = m.ring_off + nslot * slot_bytes<FMT>();
   return m;
 }
@@ -786,113 +841,119 @@ RK_DEV bool spin_until_eq(const volatile int *w, int v, unsigned long long limit
 
 // Q8_0 block terms of 32-block chunk c of a segment, two lanes per block:
 // lane l takes half (l & 1) of block 32c + l/2 (ta) and of block
-// 32c + 16 + l/2 (tb), 16 consecutive bytes each, so the weight and input
-// loads of a warp are conflict-free; the pair's partial sums are added,
-// then term = float32(sum)·float32(ws·xs) as qrow forms it (quant.go:157-164).
-// qa / qb and xa / xb are the input's halves and scales for those blocks.
-RK_DEV void q8_pair_terms(const uint8_t *W, const float *S, int c, int nblk, int4 qa, int4 qb, float xa, float xb,
+// 32c + 16 + l/2 (tb), 16 consecutive bytes each, so a warp's weight and
+// input loads are conflict-free; the pair's partial sums are added, then
+// term = float32(sum)·float32(ws·xs) as qrow forms it (quant.go:157-164).
+// X: the input's Q8_0 bytes at the segment's first block, XS its scales.
+RK_DEV void q8_pair_terms(const uint8_t *W, const float *S, const int8_t *X, const float *XS, int c, int nblk,
                           float &ta, float &tb) {
   const int lane = threadIdx.x & 31;
   const int ba = 32 * c + (lane >> 1), bb = ba + 16;
   int sa = 0, sb = 0;
   if (ba < nblk) {
     const int4 w = *reinterpret_cast<const int4 *>(W + 1024 * c + 16 * lane);
-    sa = __dp4a(w.x, qa.x, 0);
-    sa = __dp4a(w.y, qa.y, sa);
-    sa = __dp4a(w.z, qa.z, sa);
-    sa = __dp4a(w.w, qa.w, sa);
+    const int4 q = *reinterpret_cast<const int4 *>(X + 1024 * c + 16 * lane);
+    sa = __dp4a(w.x, q.x, 0);
+    sa = __dp4a(w.y, q.y, sa);
+    sa = __dp4a(w.z, q.z, sa);
+    sa = __dp4a(w.w, q.w, sa);
   }
   if (bb < nblk) {
     const int4 w = *reinterpret_cast<const int4 *>(W + 1024 * c + 512 + 16 * lane);
-    sb = __dp4a(w.x, qb.x, 0);
-    sb = __dp4a(w.y, qb.y, sb);
-    sb = __dp4a(w.z, qb.z, sb);
-    sb = __dp4a(w.w, qb.w, sb);
+    const int4 q = *reinterpret_cast<const int4 *>(X + 1024 * c + 512 + 16 * lane);
+    sb = __dp4a(w.x, q.x, 0);
+    sb = __dp4a(w.y, q.y, sb);
+    sb = __dp4a(w.z, q.z, sb);
+    sb = __dp4a(w.w, q.w, sb);
   }
   sa += __shfl_xor_sync(0xffffffffu, sa, 1);
   sb += __shfl_xor_sync(0xffffffffu, sb, 1);
-  ta = __fmul_rn(__int2float_rn(sa), __fmul_rn(S[ba], xa));
-  tb = __fmul_rn(__int2float_rn(sb), __fmul_rn(S[bb], xb));
+  ta = __fmul_rn(__int2float_rn(sa), __fmul_rn(S[ba], XS[ba]));
+  tb = __fmul_rn(__int2float_rn(sb), __fmul_rn(S[bb], XS[bb]));
 }
 
-constexpr int kChainWarps = 12;  // warps of a chain CTA
-constexpr int kChainDepth = 3;   // ring slots per warp
+constexpr int kChainWarps = 16;  // warps of a chain CTA
+constexpr int kChainDepth = 2;   // ring slots per warp
 
-// The chain kernel. One CTA per SM; warp w owns ring slots
-// [w·DEPTH, (w+1)·DEPTH) and takes segments w, w+WARPS, ... of the CTA's
-// part of each step (so the warps' shares of a step differ by one segment
-// at most). Lane 0 keeps DEPTH of the warp's segments in flight (1-D bulk
-// copies, completion on the slot's mbarrier; never multicast), running on
-// into the next step's segments, since weights depend on no step's output:
-// while the warps stage one step's input, their rings fill with that
-// step's weights. A row of several segments, and the two rows of an
-// EPI_SILU pair, hand their running sums to the next segment's warp through
-// a Carry entry: every segment's block terms are formed at once, and only
-// qrow's eight sums run in block order from warp to warp.
+// The chain kernel. One CTA per SM. Each step's units are split over the
+// CTAs (as for every product), and a CTA's segments of the step over its
+// warps in contiguous ranges that differ by one segment at most, so a
+// row's segments, and the two rows of an EPI_SILU pair, are mostly one
+// warp's: qrow's eight running sums stay in registers from segment to
+// segment. Warp w owns ring slots [w·DEPTH, (w+1)·DEPTH); lane 0 keeps
+// DEPTH of the warp's segments in flight (1-D bulk copies, completion on
+// the slot's mbarrier; never multicast), running on into the warp's next
+// step's segments, since weights depend on no step's output: while the
+// warps stage one step's input, their rings fill with that step's weights.
 //
-// When every unit of a step has a number of segments dividing WARPS, each
-// warp always meets the same segment of its rows, and keeps that
-// segment's Q8_0 input in registers for the whole step: the segment's
-// shared-memory reads are then its weights and scales only.
+// A unit that straddles a warp boundary: the earlier warp hands its
+// running state (sums, and silu(W1's row) of a pair) to the next through a
+// Carry entry at the end of its range; the next warp keeps the terms of its
+// segments of that unit in a term buffer (its part of the staging area,
+// idle once the step's input is staged) and finishes the unit last, once
+// the carry is there. No warp waits for another in the middle of its range.
 template <int FMT, int WARPS, int DEPTH>
 __global__ void __launch_bounds__(WARPS * 32, 1)
-    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int wsf) {
+    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int tbw) {
   using T = QTraits<FMT>;
-  using Grp = CtaGroup;
+  constexpr int kChunks = T::kSegBlocks / 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ns = ca.nsteps;
-  const ChainSmem L = chain_smem<FMT>(max_cols, sf, wsf, WARPS * DEPTH);
+  const ChainSmem L = chain_smem<FMT>(max_cols, sf, WARPS * DEPTH, WARPS);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
   int8_t *sqx = reinterpret_cast<int8_t *>(smem + L.in_off);
   float *sxs = reinterpret_cast<float *>(smem + L.xs_off);
   int *sxsum = reinterpret_cast<int *>(smem + L.xsum_off);
   float *stage = reinterpret_cast<float *>(smem + L.stage_off);
-  float *wstage = reinterpret_cast<float *>(smem + L.wstage_off);
   Carry *carry = reinterpret_cast<Carry *>(smem + L.carry_off);
   uint8_t *ring = smem + L.ring_off + warp * DEPTH * slot_bytes<FMT>();
+  float *const wtb = stage + warp * tbw;  // this warp's term buffer
   const uint32_t bar0 = smem_addr(bars + warp * DEPTH);
   const long long cta = blockIdx.x, ncta = gridDim.x;
   const unsigned long long limit = ca.wait_ns ? ca.wait_ns : kWaitLimitNs;
   int *err = ca.step[0].err;
 
-  // ---- the warp's copies: lane 0 walks its segments (k, i) ----
+  // ---- the warp's copies: lane 0 walks its ranges of segments ----
   uint64_t pol = 0;
-  int pk = 0, pi = warp, pslot = 0;
+  int pk = 0, pi = 0, pend = 0, pslot = 0;
+  StepPart psp{};
+  SegStream<FMT> ps{};
   int issued = 0;  // lane 0: copies issued; every lane: segments consumed
   int consumed = 0;
-  auto pseek = [&]() {  // to the first (step, index) at or after (pk, pi) with a segment
-    while (pk < ns) {
-      const StepPart sp = step_part<FMT>(ca.step[pk], cta, ncta);
-      if (pi < sp.segments()) return;
-      pk++;
-      pi = warp;
-    }
+  auto prange = [&](int k) {  // the warp's range [pi, pend) of step k
+    psp = step_part<FMT>(ca.step[k], cta, ncta);
+    const int S = psp.segments();
+    pi = S * warp / WARPS;
+    pend = S * (warp + 1) / WARPS;
+    if (pi < pend) ps.init(ca.step[k], psp, pi);
+  };
+  auto pseek = [&]() {
+    while (pk < ns && pi >= pend)
+      if (++pk < ns) prange(pk);
   };
   auto issue = [&]() {
     if (pk >= ns) return;
-    const MvArgs &a = ca.step[pk];
-    const StepPart sp = step_part<FMT>(a, cta, ncta);
-    const SegRef r = seg_ref(sp, pi);
-    Cursor c{};
-    unit_loc(a, sp.nsub, sp.u0 + r.ui, r.sub, c.part, c.row);
-    c.sg = r.sgi;
-    const SegInfo sg = seg_info<FMT>(a, a.cols >> 5, c);
+    const int nblk = ps.nblk();
+    const uint32_t wbytes = uint32_t(nblk * T::kBlkBytes);
+    // The scales' copy: a 16-byte-aligned superset of the segment's run.
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(ps.scales(psp.nsub));
+    const uintptr_t s0 = sa & ~uintptr_t(15), s1 = (sa + uintptr_t(nblk) * 4 + 15) & ~uintptr_t(15);
     uint8_t *dst = ring + pslot * slot_bytes<FMT>();
     const uint32_t bar = bar0 + 8 * pslot;
-    // The slot's previous segment was read by this warp before this copy.
+    // (The slot's previous segment was read by this warp before this copy.)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, sg.wbytes + sg.sbytes);
-    bulk_g2s(smem_addr(dst), sg.wsrc, sg.wbytes, bar, pol);
-    bulk_g2s(smem_addr(dst + kSegBytes), sg.ssrc, sg.sbytes, bar, pol);
+    mbar_expect_tx(bar, wbytes + uint32_t(s1 - s0));
+    bulk_g2s(smem_addr(dst), ps.wsrc(psp.nsub), wbytes, bar, pol);
+    bulk_g2s(smem_addr(dst + kSegBytes), reinterpret_cast<const void *>(s0), uint32_t(s1 - s0), bar, pol);
     pslot = pslot + 1 == DEPTH ? 0 : pslot + 1;
     issued++;
-    pi += WARPS;
+    if (++pi < pend) ps.next(ca.step[pk], psp);
     pseek();
   };
   // Stops the warp after an expired wait: its copies still in flight (from
-  // segment `from` on) get a bounded chance to land, so none writes into the
-  // CTA's shared memory after the CTA ends.
+  // segment `from` on) get a bounded chance to land, so none writes into
+  // the CTA's shared memory after the CTA ends.
   bool dead = false;
   auto die = [&](int from) {
     if (lane == 0) {
@@ -906,16 +967,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     for (int k = 0; k < DEPTH; k++) mbar_init(bar0 + 8 * k, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     pol = evict_first_policy();
+    prange(0);
     pseek();
   }
-  for (int e = threadIdx.x; e < kCarries; e += blockDim.x) carry[e].seq = -1;
   __syncwarp();
   // Weights are no kernel's output: the ring fills before the predecessor
   // kernel ends, together with the first step's norm weights.
   griddep_trigger();
   if (lane == 0)
     for (int k = 0; k < DEPTH; k++) issue();
-  const bool norm0 = ca.step[0].pro == PRO_NORM_QUANT && ca.step[0].cols <= sf && !ca.step[0].wait.ll;
+  const int sfn = sf / 2;  // a normalising step stages x and its weights in halves
+  float *wstage = stage + sfn;
+  const bool norm0 = ca.step[0].pro == PRO_NORM_QUANT && ca.step[0].cols <= sfn && !ca.step[0].wait.ll;
   if (norm0) stage_load(nullptr, ca.step[0].norm_w, 0, ca.step[0].cols, stage, wstage);
   griddep_wait();
 
@@ -927,14 +990,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const StepPart sp = step_part<FMT>(a, cta, ncta);
     // ---- prologue: the step's input into shared memory as Q8_0 ----
     __syncthreads();  // every warp is done with the previous step
+    if (threadIdx.x <= WARPS) carry[threadIdx.x].seq = -1;
     if (sp.u1 > sp.u0) {
       const bool norm = a.pro == PRO_NORM_QUANT;
       const unsigned wtag = a.wait.ll ? gather_tag(*a.wait.epoch, a.wait.slot, a.wait.nslots) : 0u;
-      const bool single = cols <= sf;
+      const int sfk = norm ? sfn : sf;  // floats of x per staged chunk
+      const bool single = cols <= sfk;
       bool pre = false;
       if (k == 0 && !a.wait.ll) {
         // Plain input from the predecessor kernel (the first step only).
-        stage_load(a.x, nullptr, 0, min(cols, sf), stage, wstage);
+        stage_load(a.x, nullptr, 0, min(cols, sfk), stage, wstage);
         pre = true;
       } else if (single) {
         if (norm) stage_load(nullptr, a.norm_w, 0, cols, stage, wstage);
@@ -943,65 +1008,109 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
       __shared__ float s_inv;
       if (norm)
-        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage, sf, pre, 1,
+        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage, sfk, pre, 1,
                              a.wait.ll, wtag, err, limit);
       else
-        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sf, pre, 1,
+        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sfk, pre, 1,
                               a.wait.ll, wtag, err, limit);
-      __syncthreads();
     }
-    const int nsegs = sp.segments();
-    if (warp >= nsegs) continue;
+    __syncthreads();  // the input is staged; the staging area is term buffers now
+    const int S = sp.segments();
+    const int g0 = S * warp / WARPS, g1 = S * (warp + 1) / WARPS;
+    const SegPos first = seg_pos(sp, g0);
+    const SegPos after = seg_pos(sp, g1);
+    // Whether the warp's first unit began in the previous warp's range, and
+    // whether its last one goes on into the next warp's.
+    const bool starts_mid = first.rem(sp) != 0, ends_mid = after.rem(sp) != 0;
     const unsigned put_tag = a.put.nll > 0 ? gather_tag(*a.put.epoch, a.put.slot, a.put.nslots) : 0u;
-    const int per_unit = sp.nsub * sp.nseg;
-    // The Q8_0 input of this warp's segment, cached for the step when it is
-    // always the same segment.
-    constexpr int kChunks = T::kSegBlocks / 32;
-    const bool cached = FMT == FMT_Q8_0 && WARPS % per_unit == 0;
-    int4 qa[kChunks], qb[kChunks];
-    float xa[kChunks], xb[kChunks];
-    auto load_input = [&](int blk0) {
+
+    // The chains and epilogue of one segment of unit ui: lane j < 8 adds
+    // the terms of blocks j, j+8, j+16, j+24 of each chunk in block order
+    // (term(b) gives block b's term); at a sub-row's end the eight sums
+    // combine (quant.go:163) and the row goes out, or, for W1's row of a
+    // pair, silu of it is kept for W3's row.
+    float acc = 0.0f, r0 = 0.0f;
+    auto finish = [&](const SegPos &p, int nblk, float old, int part, int row, auto &&term) {
+      const int j = lane & 7;
 #pragma unroll
-      for (int c = 0; c < kChunks; c++) {
-        const int ba = blk0 + 32 * c + (lane >> 1);
-        qa[c] = *reinterpret_cast<const int4 *>(sqx + 32 * ba + 16 * (lane & 1));
-        qb[c] = *reinterpret_cast<const int4 *>(sqx + 32 * (ba + 16) + 16 * (lane & 1));
-        xa[c] = sxs[ba];
-        xb[c] = sxs[ba + 16];
+      for (int ch = 0; ch < kChunks; ch++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const int b = 32 * ch + j + 8 * q;
+          const float t = term(ch, q);
+          if (b < nblk) acc = __fadd_rn(acc, t);
+        }
       }
+      if (p.sgi != sp.nseg - 1) return;
+      const float rr = combine8(acc);
+      acc = 0.0f;
+      if (sp.nsub == 2 && p.sub == 0) {
+        r0 = silu(rr);  // W1's row through SiLU, for W3's (model.go:601-603)
+        return;
+      }
+      if (lane == 0) {
+        float *out = a.part[part].out;
+        float v = rr;
+        switch (a.epi) {
+          case EPI_STORE: break;
+          case EPI_ADD: v = __fadd_rn(old, rr); break;                  // model.go:592-594
+          case EPI_ADD_CANON: v = canonical(__fadd_rn(old, rr)); break;  // model.go:608-610
+          case EPI_SILU:
+            v = __fmul_rn(r0, rr);
+            out = a.part[0].out;
+            break;
+        }
+        out[row] = v;
+        if (part == 0 || a.epi == EPI_SILU)
+          for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + row, v, put_tag);
+      }
+      r0 = 0.0f;
     };
-    if (cached) {
-      const SegRef r = seg_ref(sp, warp);
-      load_input(r.sgi * T::kSegBlocks);
-    }
-    for (int i = warp; i < nsegs; i += WARPS) {
-      const SegRef r = seg_ref(sp, i);
-      const int pos = i;  // within the step
-      Cursor c{};
-      unit_loc(a, sp.nsub, sp.u0 + r.ui, r.sub, c.part, c.row);
-      c.sg = r.sgi;
-      const bool last = r.sgi == sp.nseg - 1, final_row = last && !(sp.nsub == 2 && r.sub == 0);
-      // The residual's old value, fetched early (EPI_ADD, EPI_ADD_CANON).
-      float old = 0.0f;
-      if (final_row && lane == 0 && (a.epi == EPI_ADD || a.epi == EPI_ADD_CANON)) old = a.part[c.part].out[c.row];
+    // The residual's old value (EPI_ADD, EPI_ADD_CANON) of the row the
+    // segment ends, read early.
+    auto old_of = [&](const SegPos &p, int part, int row) {
+      float v = 0.0f;
+      if (lane == 0 && p.sgi == sp.nseg - 1 && (a.epi == EPI_ADD || a.epi == EPI_ADD_CANON)) v = a.part[part].out[row];
+      return v;
+    };
+
+    SegStream<FMT> cs{};
+    if (g0 < g1) cs.init(a, sp, g0);
+    int deferred = 0;  // segments of the first unit kept in the term buffer
+    for (int i = g0; i < g1; i++) {
+      const SegPos p = cs.p;
+      const int prow = cs.row, ppart = cs.part;
+      const bool defer = starts_mid && p.ui == first.ui;
+      const float old = defer ? 0.0f : old_of(p, ppart, prow);
       if (!dead && !__all_sync(0xffffffffu, mbar_wait_bounded(bar0 + 8 * slot, parity, limit))) die(consumed + 1);
-      const SegInfo sg = seg_info<FMT>(a, nb, c);
+      SegInfo sg;
+      sg.blk0 = cs.blk0();
+      sg.nblk = cs.nblk();
+      const int soff = int((reinterpret_cast<uintptr_t>(cs.scales(sp.nsub)) & 15) >> 2);
+      if (i + 1 < g1) cs.next(a, sp);
       const uint8_t *W = ring + slot * slot_bytes<FMT>();
-      const float *S = reinterpret_cast<const float *>(W + kSegBytes) + sg.soff;
+      const float *Sc = reinterpret_cast<const float *>(W + kSegBytes) + soff;
       float term[kChunks], term2[kChunks];
 #pragma unroll
       for (int ch = 0; ch < kChunks; ch++) term[ch] = term2[ch] = 0.0f;
       if (!dead) {
         if (FMT == FMT_Q8_0) {
-          if (!cached) load_input(sg.blk0);
+          const int8_t *X = sqx + 32 * sg.blk0;
+          const float *XS = sxs + sg.blk0;
+          if (sg.nblk == T::kSegBlocks) {
+            // A whole segment: no guards, so the chunks' loads overlap.
 #pragma unroll
-          for (int ch = 0; ch < kChunks; ch++)
-            if (32 * ch < sg.nblk) q8_pair_terms(W, S, ch, sg.nblk, qa[ch], qb[ch], xa[ch], xb[ch], term[ch], term2[ch]);
+            for (int ch = 0; ch < kChunks; ch++) q8_pair_terms(W, Sc, X, XS, ch, T::kSegBlocks, term[ch], term2[ch]);
+          } else {
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ch++)
+              if (32 * ch < sg.nblk) q8_pair_terms(W, Sc, X, XS, ch, sg.nblk, term[ch], term2[ch]);
+          }
         } else {
 #pragma unroll
           for (int ch = 0; ch < kChunks; ch++) {
             const int bb = ch * 32 + lane;
-            if (bb < sg.nblk) term[ch] = block_term<FMT>(W, S, bb, sg.blk0 + bb, sqx, sxs, sxsum);
+            if (bb < sg.nblk) term[ch] = block_term<FMT>(W, Sc, bb, sg.blk0 + bb, sqx, sxs, sxsum);
           }
         }
       }
@@ -1011,81 +1120,74 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       slot = slot + 1 == DEPTH ? 0 : slot + 1;
       if (slot == 0) parity ^= 1;
       consumed++;
-      // The running sums so far (a segment after the first of its unit).
-      float acc = 0.0f, r0 = 0.0f;
-      if (r.rem > 0 && !dead) {
-        Carry &cr = carry[(k * 7919 + pos) % kCarries];
-        if (!__all_sync(0xffffffffu, spin_until_eq(&cr.seq, pos, limit))) {
-          die(consumed);
-        } else {
-          __threadfence_block();
-          acc = cr.acc[lane & 7];
-          r0 = cr.r0;
-          __syncwarp();
-          if (lane == 0) cr.seq = -1;
-        }
-      }
       if (dead) continue;
-      // qrow's eight chains: lane j < 8 adds the terms of blocks j, j+8,
-      // j+16, j+24 of each chunk in order; blocks past the row are
-      // skipped, not added.
+      if (defer) {
+        // Kept, in block order, for when the carry has come.
+        float *dst = wtb + deferred * T::kSegBlocks;
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ch++) {
+          if (FMT == FMT_Q8_0) {
+            if ((lane & 1) == 0) {
+              dst[32 * ch + (lane >> 1)] = term[ch];
+              dst[32 * ch + 16 + (lane >> 1)] = term2[ch];
+            }
+          } else {
+            dst[32 * ch + lane] = term[ch];
+          }
+        }
+        deferred++;
+        continue;
+      }
+      // Block 32ch + b lies in lane 2b's first term (b < 16) or lane
+      // 2(b - 16)'s second (Q8_0 lane pairs), or in lane b (Q4_0).
       const int j = lane & 7;
-#pragma unroll
-      for (int ch = 0; ch < kChunks; ch++) {
+      finish(p, sg.nblk, old, ppart, prow, [&](int ch, int q) {
         if (FMT == FMT_Q8_0) {
-          // Block 32ch + b lies in lane 2b's first term (b < 16) or lane
-          // 2(b - 16)'s second.
-          const float t0 = __shfl_sync(0xffffffffu, term[ch], 2 * j);
-          const float t1 = __shfl_sync(0xffffffffu, term[ch], 2 * j + 16);
-          const float t2 = __shfl_sync(0xffffffffu, term2[ch], 2 * j);
-          const float t3 = __shfl_sync(0xffffffffu, term2[ch], 2 * j + 16);
-          const int b0 = 32 * ch + j;
-          if (b0 < sg.nblk) acc = __fadd_rn(acc, t0);
-          if (b0 + 8 < sg.nblk) acc = __fadd_rn(acc, t1);
-          if (b0 + 16 < sg.nblk) acc = __fadd_rn(acc, t2);
-          if (b0 + 24 < sg.nblk) acc = __fadd_rn(acc, t3);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            const float t = __shfl_sync(0xffffffffu, term[ch], j + 8 * q);
-            if (ch * 32 + j + 8 * q < sg.nblk) acc = __fadd_rn(acc, t);
-          }
+          const float t = __shfl_sync(0xffffffffu, q < 2 ? term[ch] : term2[ch], 2 * j + 16 * (q & 1));
+          return t;
         }
+        return __shfl_sync(0xffffffffu, term[ch], j + 8 * q);
+      });
+    }
+    __syncwarp();
+    if (dead) continue;
+    // The last unit goes on in the next warp: its state, unless it is the
+    // first unit too (finished below).
+    const bool last_is_first = starts_mid && (g1 == g0 || seg_pos(sp, g1 - 1).ui == first.ui);
+    auto send = [&]() {
+      Carry &cw = carry[warp + 1];
+      if (lane < 8) cw.acc[lane] = acc;
+      if (lane == 0) cw.r0 = r0;
+      __syncwarp();
+      __threadfence_block();
+      if (lane == 0) cw.seq = k;
+    };
+    if (ends_mid && !last_is_first) send();
+    if (starts_mid) {
+      // The first unit: the previous warp's state, then this warp's kept
+      // segments of it, in order.
+      float acc_main = acc, r0_main = r0;
+      Carry &cr = carry[warp];
+      if (!__all_sync(0xffffffffu, spin_until_eq(&cr.seq, k, limit))) {
+        die(consumed);
+        continue;
       }
-      if (last) {
-        const float rr = combine8(acc);
-        if (!final_row) {
-          r0 = rr;  // W1's row; W3's sums start from zero
-          acc = 0.0f;
-        } else if (lane == 0) {
-          float *out = a.part[c.part].out;
-          float v = rr;
-          switch (a.epi) {
-            case EPI_STORE: break;
-            case EPI_ADD: v = __fadd_rn(old, rr); break;
-            case EPI_ADD_CANON: v = canonical(__fadd_rn(old, rr)); break;
-            case EPI_SILU:
-              v = __fmul_rn(silu(r0), rr);
-              out = a.part[0].out;
-              break;
-          }
-          out[c.row] = v;
-          if (c.part == 0 || a.epi == EPI_SILU)
-            for (int g = 0; g < a.put.nll; g++) ll_store(a.put.ll[g] + c.row, v, put_tag);
-        }
+      __threadfence_block();
+      acc = cr.acc[lane & 7];
+      r0 = cr.r0;
+      SegPos q = first;
+      for (int d = 0; d < deferred; d++, q.next(sp)) {
+        Cursor c{};
+        unit_loc(a, sp.nsub, sp.u0 + q.ui, q.sub, c.part, c.row);
+        c.sg = q.sgi;
+        const SegInfo sg = seg_info<FMT>(a, nb, c);
+        const float *src = wtb + d * T::kSegBlocks;
+        finish(q, sg.nblk, old_of(q, c.part, c.row), c.part, c.row,
+               [&](int ch, int qq) { return src[32 * ch + (lane & 7) + 8 * qq]; });
       }
-      if (r.rem < per_unit - 1) {
-        Carry &cw = carry[(k * 7919 + pos + 1) % kCarries];
-        if (!__all_sync(0xffffffffu, spin_until_eq(&cw.seq, -1, limit))) {
-          die(consumed);
-          continue;
-        }
-        if (lane < 8) cw.acc[lane] = acc;
-        if (lane == 0) cw.r0 = r0;
-        __syncwarp();
-        __threadfence_block();
-        if (lane == 0) cw.seq = pos + 1;
-      }
+      if (ends_mid && last_is_first) send();
+      acc = acc_main;
+      r0 = r0_main;
     }
   }
 }
@@ -1210,27 +1312,34 @@ cudaError_t init_matvec_attributes() {
 }
 
 // Staging of a chain: x in chunks of sf floats (the largest of 8192, 4096,
-// 2048 that fits beside the rings), the norm weights beside them for the
-// steps that normalise.
-static ChainSmem chain_layout(int fmt, int mc, int sf, int wsf) {
+// 2048, or the widest input if less, that fits beside the rings; a
+// normalising step stages x and its weights in the halves). Once a step's
+// input is staged, the area holds the warps' term buffers: tbw floats each,
+// room for all but one segment of the widest unit.
+static ChainSmem chain_layout(int fmt, int mc, int sf) {
   const int nslot = kChainWarps * kChainDepth;
-  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, wsf, nslot) : chain_smem<FMT_Q4_0>(mc, sf, wsf, nslot);
+  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, nslot, kChainWarps)
+                         : chain_smem<FMT_Q4_0>(mc, sf, nslot, kChainWarps);
 }
 
-static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *wsf) {
-  int mc = 0;
-  for (int k = 0; k < ca.nsteps; k++) mc = std::max(mc, ca.step[k].cols);
+static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *tbw) {
+  int mc = 0, need = 0, per_unit = 1;
   const int fmt = ca.nsteps > 0 ? ca.step[0].fmt : FMT_Q8_0;
+  const int seg_blocks = fmt == FMT_Q8_0 ? QTraits<FMT_Q8_0>::kSegBlocks : QTraits<FMT_Q4_0>::kSegBlocks;
+  for (int k = 0; k < ca.nsteps; k++) {
+    const MvArgs &a = ca.step[k];
+    mc = std::max(mc, a.cols);
+    need = std::max(need, a.pro == PRO_NORM_QUANT ? 2 * a.cols : a.cols);
+    const int nseg = (a.cols / 32 + seg_blocks - 1) / seg_blocks;
+    per_unit = std::max(per_unit, (a.epi == EPI_SILU ? 2 : 1) * nseg);
+  }
+  *tbw = (per_unit - 1) * seg_blocks;
   ChainSmem L{};
   for (int cand : {8192, 4096, 2048}) {
-    const int f = std::min(mc, cand);
-    int wf = 0;
-    for (int k = 0; k < ca.nsteps; k++)
-      if (ca.step[k].pro == PRO_NORM_QUANT) wf = std::max(wf, std::min(ca.step[k].cols, f));
+    const int f = (std::max(std::min(need, cand), kChainWarps * *tbw) + 63) & ~63;
     *max_cols = mc;
     *sf = f;
-    *wsf = wf;
-    L = chain_layout(fmt, mc, f, wf);
+    L = chain_layout(fmt, mc, f);
     if (L.total <= kSmemLimit) break;
   }
   return L;
@@ -1249,24 +1358,24 @@ bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
     // is what lets tagged buffers be reused without a barrier.
     if (step_units(a) < num_sms) return false;
   }
-  int mc, sf, wsf;
-  return chain_dims(ca, &mc, &sf, &wsf).total <= kSmemLimit;
+  int mc, sf, tbw;
+  return chain_dims(ca, &mc, &sf, &tbw).total <= kSmemLimit;
 }
 
 int matvec_chain_smem(const ChainArgs &ca) {
-  int mc, sf, wsf;
-  return chain_dims(ca, &mc, &sf, &wsf).total;
+  int mc, sf, tbw;
+  return chain_dims(ca, &mc, &sf, &tbw).total;
 }
 
 cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t st) {
   if (!matvec_chain_ok(ca, num_sms)) return cudaErrorInvalidValue;
-  int mc, sf, wsf;
-  const ChainSmem L = chain_dims(ca, &mc, &sf, &wsf);
+  int mc, sf, tbw;
+  const ChainSmem L = chain_dims(ca, &mc, &sf, &tbw);
   const int threads = kChainWarps * 32;
   if (ca.step[0].fmt == FMT_Q8_0)
     return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf,
-                    wsf);
-  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf, wsf);
+                    tbw);
+  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf, tbw);
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
