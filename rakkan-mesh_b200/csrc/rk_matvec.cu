@@ -814,7 +814,7 @@ struct ChainSmem {
   int nslot, in_off, xs_off, xsum_off, stage_off, carry_off, ring_off, total;
 };
 template <int FMT>
-__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int nslot, int warps) {
+__host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int sfw, int nslot, int warps) {
   ChainSmem m;
   const int nb = max_cols / 32;
   m.nslot = nslot;
@@ -824,7 +824,7 @@ __host__ __device__ inline ChainSmem chain_smem(int max_cols, int sf, int nslot,
   m.xs_off = m.in_off + ((max_cols + 32 * 32 + 15) & ~15);
   m.xsum_off = m.xs_off + ((nb * 4 + 32 * 4 + 15) & ~15);
   m.stage_off = m.xsum_off + (FMT == FMT_Q4_0 ? ((nb * 4 + 32 * 4 + 15) & ~15) : 0);  // xsum: Q4_0 only
-  m.carry_off = (m.stage_off + 4 * sf + 15) & ~15;
+  m.carry_off = (m.stage_off + 4 * (sf + sfw) + 15) & ~15;
   m.ring_off = (m.carry_off + (warps + 1) * (int)sizeof(Carry) + 127) & ~127;
   m.total = m.ring_off + nslot * slot_bytes<FMT>();
   return m;
@@ -894,13 +894,13 @@ constexpr int kChainDepth = 2;   // ring slots per warp
 // the carry is there. No warp waits for another in the middle of its range.
 template <int FMT, int WARPS, int DEPTH>
 __global__ void __launch_bounds__(WARPS * 32, 1)
-    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int tbw) {
+    k_matvec_chain(const __grid_constant__ ChainArgs ca, int max_cols, int sf, int sfw, int tbw) {
   using T = QTraits<FMT>;
   constexpr int kChunks = T::kSegBlocks / 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ns = ca.nsteps;
-  const ChainSmem L = chain_smem<FMT>(max_cols, sf, WARPS * DEPTH, WARPS);
+  const ChainSmem L = chain_smem<FMT>(max_cols, sf, sfw, WARPS * DEPTH, WARPS);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
   int8_t *sqx = reinterpret_cast<int8_t *>(smem + L.in_off);
   float *sxs = reinterpret_cast<float *>(smem + L.xs_off);
@@ -976,10 +976,32 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   griddep_trigger();
   if (lane == 0)
     for (int k = 0; k < DEPTH; k++) issue();
-  const int sfn = sf / 2;  // a normalising step stages x and its weights in halves
-  float *wstage = stage + sfn;
-  const bool norm0 = ca.step[0].pro == PRO_NORM_QUANT && ca.step[0].cols <= sfn && !ca.step[0].wait.ll;
-  if (norm0) stage_load(nullptr, ca.step[0].norm_w, 0, ca.step[0].cols, stage, wstage);
+  // The staging area: x in its first sf floats (term buffers there once a
+  // step's input is staged), a normalising step's weights in the sfw after,
+  // which no step's consumption touches: a step's norm weights are copied
+  // there by every warp as it finishes the step before (by all before the
+  // predecessor kernel ends, for the first step), so they are there when the
+  // step's input arrives.
+  float *wstage = stage + sf;
+  const int sfn = min(sf, sfw);  // x floats per chunk of a normalising step
+  unsigned nwmask = 0;  // the steps whose norm weights are prefetched
+  for (int k = 0; k < ns; ++k)
+    if (ca.step[k].pro == PRO_NORM_QUANT && ca.step[k].cols <= sfn && (k > 0 || !ca.step[0].wait.ll)) nwmask |= 1u << k;
+  auto norm_w_ready = [nwmask](int k) { return (nwmask >> k) & 1u; };
+  auto prefetch_norm_w = [&](int k, int part, int nparts) {  // this group's share of step k's norm weights
+    const int cols = ca.step[k].cols, n4 = cols / 4;
+    const int i0 = n4 * part / nparts, i1 = n4 * (part + 1) / nparts;
+    const float *w = ca.step[k].norm_w;
+    if ((reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+      for (int i = i0 + lane; i < i1; i += 32)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(wstage + 4 * i)), "l"(w + 4 * i)
+                     : "memory");
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+      for (int i = 4 * i0 + lane; i < 4 * i1; i += 32) wstage[i] = w[i];
+    }
+  };
+  if (norm_w_ready(0)) prefetch_norm_w(0, warp, WARPS);
   griddep_wait();
 
   int slot = 0;
@@ -997,21 +1019,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       const int sfk = norm ? sfn : sf;  // floats of x per staged chunk
       const bool single = cols <= sfk;
       bool pre = false;
+      // (A normalising step's weights are staged already when norm_w_ready.)
       if (k == 0 && !a.wait.ll) {
         // Plain input from the predecessor kernel (the first step only).
         stage_load(a.x, nullptr, 0, min(cols, sfk), stage, wstage);
         pre = true;
       } else if (single) {
-        if (norm) stage_load(nullptr, a.norm_w, 0, cols, stage, wstage);
         if (!ll_gather_load(a.wait.ll, cols, wtag, stage, limit) && threadIdx.x == 0) atomicExch(err, DEV_ERR_TIMEOUT);
         pre = true;
       }
       __shared__ float s_inv;
+      // The blocks' input sums are Q4_0's alone; a Q8_0 CTA has no room for
+      // them (that region would be the staging area being read).
+      int *const qsum = FMT == FMT_Q4_0 ? sxsum : nullptr;
       if (norm)
-        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, sxsum, &s_inv, stage, wstage, sfk, pre, 1,
+        quantize_warps<true>(a.x, cols, a.norm_w, a.recipN, a.eps, sqx, sxs, qsum, &s_inv, stage, wstage, sfk, pre, 1,
                              a.wait.ll, wtag, err, limit);
       else
-        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, sxsum, &s_inv, stage, nullptr, sfk, pre, 1,
+        quantize_warps<false>(a.x, cols, nullptr, 0.0f, 0.0f, sqx, sxs, qsum, &s_inv, stage, nullptr, sfk, pre, 1,
                               a.wait.ll, wtag, err, limit);
     }
     __syncthreads();  // the input is staged; the staging area is term buffers now
@@ -1150,6 +1175,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       });
     }
     __syncwarp();
+    // The next step's norm weights: this warp's share, now that it is done
+    // with the step's weights (the area is not this step's).
+    if (norm_w_ready(k + 1)) prefetch_norm_w(k + 1, warp, WARPS);
     if (dead) continue;
     // The last unit goes on in the next warp: its state, unless it is the
     // first unit too (finished below).
@@ -1316,20 +1344,21 @@ cudaError_t init_matvec_attributes() {
 // normalising step stages x and its weights in the halves). Once a step's
 // input is staged, the area holds the warps' term buffers: tbw floats each,
 // room for all but one segment of the widest unit.
-static ChainSmem chain_layout(int fmt, int mc, int sf) {
+static ChainSmem chain_layout(int fmt, int mc, int sf, int sfw) {
   const int nslot = kChainWarps * kChainDepth;
-  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, nslot, kChainWarps)
-                         : chain_smem<FMT_Q4_0>(mc, sf, nslot, kChainWarps);
+  return fmt == FMT_Q8_0 ? chain_smem<FMT_Q8_0>(mc, sf, sfw, nslot, kChainWarps)
+                         : chain_smem<FMT_Q4_0>(mc, sf, sfw, nslot, kChainWarps);
 }
 
-static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *tbw) {
-  int mc = 0, need = 0, per_unit = 1;
+static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *sfw, int *tbw) {
+  int mc = 0, need = 0, per_unit = 1, wneed = 0;
   const int fmt = ca.nsteps > 0 ? ca.step[0].fmt : FMT_Q8_0;
   const int seg_blocks = fmt == FMT_Q8_0 ? QTraits<FMT_Q8_0>::kSegBlocks : QTraits<FMT_Q4_0>::kSegBlocks;
   for (int k = 0; k < ca.nsteps; k++) {
     const MvArgs &a = ca.step[k];
     mc = std::max(mc, a.cols);
-    need = std::max(need, a.pro == PRO_NORM_QUANT ? 2 * a.cols : a.cols);
+    need = std::max(need, a.cols);
+    if (a.pro == PRO_NORM_QUANT) wneed = std::max(wneed, a.cols);
     const int nseg = (a.cols / 32 + seg_blocks - 1) / seg_blocks;
     per_unit = std::max(per_unit, (a.epi == EPI_SILU ? 2 : 1) * nseg);
   }
@@ -1337,9 +1366,11 @@ static ChainSmem chain_dims(const ChainArgs &ca, int *max_cols, int *sf, int *tb
   ChainSmem L{};
   for (int cand : {8192, 4096, 2048}) {
     const int f = (std::max(std::min(need, cand), kChainWarps * *tbw) + 63) & ~63;
+    const int fw = (std::min(wneed, f) + 63) & ~63;
     *max_cols = mc;
     *sf = f;
-    L = chain_layout(fmt, mc, f);
+    *sfw = fw;
+    L = chain_layout(fmt, mc, f, fw);
     if (L.total <= kSmemLimit) break;
   }
   return L;
@@ -1358,24 +1389,25 @@ bool matvec_chain_ok(const ChainArgs &ca, int num_sms) {
     // is what lets tagged buffers be reused without a barrier.
     if (step_units(a) < num_sms) return false;
   }
-  int mc, sf, tbw;
-  return chain_dims(ca, &mc, &sf, &tbw).total <= kSmemLimit;
+  int mc, sf, sfw, tbw;
+  return chain_dims(ca, &mc, &sf, &sfw, &tbw).total <= kSmemLimit;
 }
 
 int matvec_chain_smem(const ChainArgs &ca) {
-  int mc, sf, tbw;
-  return chain_dims(ca, &mc, &sf, &tbw).total;
+  int mc, sf, sfw, tbw;
+  return chain_dims(ca, &mc, &sf, &sfw, &tbw).total;
 }
 
 cudaError_t launch_matvec_chain(const ChainArgs &ca, int num_sms, cudaStream_t st) {
   if (!matvec_chain_ok(ca, num_sms)) return cudaErrorInvalidValue;
-  int mc, sf, tbw;
-  const ChainSmem L = chain_dims(ca, &mc, &sf, &tbw);
+  int mc, sf, sfw, tbw;
+  const ChainSmem L = chain_dims(ca, &mc, &sf, &sfw, &tbw);
   const int threads = kChainWarps * 32;
   if (ca.step[0].fmt == FMT_Q8_0)
     return launch_k(k_matvec_chain<FMT_Q8_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf,
-                    tbw);
-  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf, tbw);
+                    sfw, tbw);
+  return launch_k(k_matvec_chain<FMT_Q4_0, kChainWarps, kChainDepth>, num_sms, threads, L.total, st, ca, mc, sf, sfw,
+                  tbw);
 }
 
 cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
