@@ -459,7 +459,8 @@ def main():
     launches = dm.model.kernel_count()
 
     baseline = None
-    if rank == 0 and not args.no_cpu_baseline:
+    # Rank 0 at N=1 only: a sharded peer would wait on its gathers meanwhile.
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_sample(args)
         baseline = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
 
@@ -472,6 +473,7 @@ def main():
     seqs = 1 if sharded else world
     parity = None
     if world > 1:
+        barrier()
         _, lg = dm.model.step(tok, pos)
         parity = parity_vs_1gpu(args, dev, c, lg, rank, local, dist, torch)
     if rank == 0:
@@ -489,7 +491,8 @@ def main():
                     "d2h_bytes_per_step": 4 * c.vocab + 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
-                         "traffic": traffic, "kernel": "k_matvec_q<Q8_0>",
+                         "traffic": traffic,
+                         "kernel": "k_matvec_chain<Q8_0>" if dm.stage.chained() else "k_matvec_q<Q8_0>",
                          "bytes_per_step": prof.matvec_bytes, "matvec_ms_per_step": prof.matvec_ms,
                          "matvec_launches_per_step": prof.matvec_launches,
                          "eager_step_ms": prof.step_ms},

@@ -314,6 +314,13 @@ int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers
  * all-gathers (peers not reachable by P2P, RK_GATHER=nccl, or an unsharded
  * stage). */
 int rk_stage_fused_gathers(const rk_stage *s);
+/* 1 when the stage's decode step runs its products as chains (one launch of
+ * Wo, W1·W3, W2 and the next layer's Q/K/V after each layer's attention,
+ * the products handing their outputs on as tagged words); 0 when each
+ * product is its own launch. Known once the stage has recorded its step
+ * (after its first decode step); 0 before. No reference counterpart: a
+ * diagnostic of how the stage runs, like rk_stage_fused_gathers. */
+int rk_stage_chained(const rk_stage *s);
 /* A head whose classifier holds the rank's vocab/G rows; logits are whole. */
 int rk_head_new_group(rk_device *d, const rk_config *c, const float *rms_final, rk_matrix *wcls, rk_group *g,
                       rk_head **out);
