@@ -283,10 +283,12 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def traffic_ratio():
+def traffic_ratio(chained=False):
     """DRAM bytes per algorithmic byte of a Q8_0 matvec launch, from the
-    committed ncu summary (one launch of the 28672x4096 W1/W3 shape)."""
-    path = os.path.join(ROOT, "profiles", "matvec_q8_28672x4096.txt")
+    committed ncu summary (one launch of the 28672x4096 W1/W3 shape, or of
+    one layer's chain when the step runs chains)."""
+    name = "matvec_chain_q8_llama3-8b_layer.txt" if chained else "matvec_q8_28672x4096.txt"
+    path = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_algorithmic_byte:"):
@@ -467,7 +469,7 @@ def main():
     # DRAM bytes of the average matvec launch of a step: the captured
     # launch's traffic per algorithmic byte times the step's average
     # algorithmic bytes per launch (traffic scales with the rows read).
-    ratio = traffic_ratio()
+    ratio = traffic_ratio(dm.stage.chained())
     traffic = ratio * prof.matvec_bytes / prof.matvec_launches if ratio and prof.matvec_launches else None
     # Sequences decoded at once: one sharded over all GPUs, or one per replica.
     seqs = 1 if sharded else world
@@ -496,6 +498,14 @@ def main():
                          "bytes_per_step": prof.matvec_bytes, "matvec_ms_per_step": prof.matvec_ms,
                          "matvec_launches_per_step": prof.matvec_launches,
                          "eager_step_ms": prof.step_ms},
+            # Where a step's time goes, from the eagerly launched steps of
+            # the roofline pass (each launch timed with CUDA events): the
+            # products (with their gathers when sharded) and the rest
+            # (attention, glue, the gaps between launches); graph_step is
+            # the timed graph replay's time.
+            "breakdown_ms": {"graph_step": ms, "eager_step": prof.step_ms, "products": prof.matvec_ms,
+                             "attention_and_rest": prof.step_ms - prof.matvec_ms,
+                             "product_launches": prof.matvec_launches, "launches": prof.launches},
             "cpu_baseline": baseline,
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
