@@ -135,20 +135,22 @@ def run_decode_batch(args):
 
 
 def run_kernel_many(args):
-    """One batched Q8_0 product of --shape with --prefill input vectors (at
-    most 64, a ForwardMany submission), L2 flushed before each launch. The
-    weights are read once per launch; every (row, vector, block) costs the
-    epilogue four f32 operations."""
+    """One batched Q8_0 (or, with --dtype q4_0, Q4_0) product of --shape
+    with --prefill input vectors (at most 64, a ForwardMany submission), L2
+    flushed before each launch. The weights are read once per launch; every
+    (row, vector, block) costs the epilogue four f32 operations."""
     import rkcuda as rk
     rows, cols = map(int, args.shape.split("x"))
     n = args.prefill
+    q4 = args.dtype == "q4_0"
     dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
-    m = rk.Matrix.generate(dev, rows, cols, rk.FMT_Q8_0, SEED, 1, 0.02)
+    m = rk.Matrix.generate(dev, rows, cols, rk.FMT_Q4_0 if q4 else rk.FMT_Q8_0, SEED, 1, 0.02)
     m.bench_many(n, max(1, args.warmup))
     ms = m.bench_many(n, args.steps)
-    nbytes = rows * cols + rows * cols // 32 * 4
+    nbytes = rows * cols // (2 if q4 else 1) + rows * cols // 32 * 4
     peak, kind = measured_peak()
-    print(json.dumps({"kernel": "k_mv_many_q8", "shape": args.shape, "vectors": n, "ms": ms,
+    print(json.dumps({"kernel": "k_mv_many", "fmt": "q4_0" if q4 else "q8_0", "shape": args.shape, "vectors": n,
+                      "ms": ms,
                       "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
                       "frac": nbytes / (ms * 1e-3) / 1e9 / peak,
                       "int8_tops": 2.0 * rows * cols * n / (ms * 1e-3) / 1e12,

@@ -125,8 +125,8 @@ int rk_same_device(const rk_matrix *a, const rk_matrix *b);
 int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x);
 /* out[t][rows] = m·x[t][cols] for t < n: the products of ForwardMany's
  * token-by-token Forward (model.go:504-518), each bit for bit one
- * Matrix.MulVec (device.go:762-764). A Q8_0 matrix whose width is a
- * multiple of 128 takes one pass over its weights on the tensor cores;
+ * Matrix.MulVec (device.go:762-764). A Q8_0 or Q4_0 matrix whose width is
+ * a multiple of 128 takes one pass over its weights on the tensor cores;
  * other matrices run one product per vector. */
 int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const float *x);
 /* outs[i] = ms[i]·x for matrices on one device, in one submission
@@ -226,9 +226,9 @@ void rk_stage_free(rk_stage *s);                                                
 int rk_stage_positions(const rk_stage *s);                                              /* Stage.Positions, model.go:487 */
 /* Stage.ForwardMany (model.go:504-518): tokens activations of dim floats,
  * at positions pos, pos+1, ..., run through the stage in place. Up to 64
- * tokens at a time; when every matrix of an unsharded stage is Q8_0 with
- * widths that are multiples of 128, each projection runs once per 64
- * tokens on the tensor cores (bits as the token-by-token Forward). */
+ * tokens at a time; when every matrix of an unsharded stage is Q8_0 or
+ * Q4_0 with widths that are multiples of 128, each projection runs once per
+ * 64 tokens on the tensor cores (bits as the token-by-token Forward). */
 int rk_stage_forward(rk_stage *s, float *xs, int pos, int tokens);
 /* 1 when rk_stage_forward runs this stage's products batched, else 0. */
 int rk_stage_batched(const rk_stage *s);
@@ -237,7 +237,8 @@ int rk_stage_batched(const rk_stage *s);
  * reference's Stage holds one sequence and has no batched step; each
  * sequence's results here are what its own Stage.Forward (model.go:522-613)
  * computes, bit for bit. Needs what the batched prefill needs (unsharded,
- * every matrix Q8_0, widths multiples of 128) and head width 64 or 128.
+ * every matrix Q8_0 or Q4_0, widths multiples of 128) and head width 64 or
+ * 128.
  * rk_stage_forward, rk_stage_fill_cache and the decode graph act on
  * sequence 0 (rk_stage_fill_cache fills every sequence's caches alike). */
 int rk_stage_new_batch(rk_device *d, const rk_config *c, rk_layer *const *layers, int n, int ctx, int nseq,
@@ -476,7 +477,7 @@ int rk_quantize(rk_device *d, int fmt, const float *w, int64_t n, void *q, float
 #define RK_BENCH_FLUSH 1
 #define RK_BENCH_FUSED 2
 int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per_launch);
-/* Mean device time (CUDA events) of one batched product of a Q8_0 matrix
+/* Mean device time (CUDA events) of one batched product of a Q8_0 or Q4_0 matrix
  * with n seeded input vectors (rk_matrix_mulvec_many's kernel, inputs
  * already quantized on the device), after one warm-up launch. */
 int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, float *ms_per_launch);

@@ -648,7 +648,7 @@ extern "C" int rk_matrix_mulvec(rk_matrix *m, float *out, const float *x) {
 extern "C" int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const float *x) {
   if (!m || n < 0 || (n > 0 && (!x || !out))) return fail(RK_ERR_ARGS, "bad argument");
   if (n == 0) return RK_OK;
-  if (m->fmt != RK_FMT_Q8_0 || !mv_many_ok(m->rows, m->cols, m->w, m->s)) {
+  if (!mv_many_ok(m->fmt, m->rows, m->cols, m->w, m->s)) {
     // Formats and widths the batched kernel does not take: one product per
     // vector, as ForwardMany's per-token Forward does.
     for (int t = 0; t < n; t++) {
@@ -672,7 +672,7 @@ extern "C" int rk_matrix_mulvec_many(rk_matrix *m, int n, float *out, const floa
   if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, 4 * n * cols, cudaMemcpyHostToDevice, d->st);
   if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, xs_pitch, d->st);
   if (e == cudaSuccess) {
-    const MmMat mat{m->w, m->s, m->rows, dout, (long long)rows, EPI_STORE};
+    const MmMat mat{m->w, m->s, m->rows, dout, (long long)rows, EPI_STORE, m->fmt};
     e = launch_mv_many(1, &mat, m->cols, n, dqx, dxs, xs_pitch, d->err_dev, d->sms, d->st);
   }
   if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, 4 * n * rows, cudaMemcpyDeviceToHost, d->st);
@@ -1852,12 +1852,12 @@ static int stage_p2p_setup(rk_stage *s) {
 }
 
 // Whether ForwardMany can run the stage's layers with batched products:
-// unsharded, every matrix Q8_0 and taken by the batched kernel.
+// unsharded, every matrix Q8_0 or Q4_0 and taken by the batched kernel.
 static bool stage_many_ok(const rk_stage *s) {
   if (s->G != 1 || s->layers.empty()) return false;
   for (const rk_layer *l : s->layers)
     for (const rk_matrix *m : {l->wq, l->wk, l->wv, l->wo, l->w1, l->w3, l->w2})
-      if (m->fmt != RK_FMT_Q8_0 || !mv_many_ok(m->rows, m->cols, m->w, m->s)) return false;
+      if (!mv_many_ok(m->fmt, m->rows, m->cols, m->w, m->s)) return false;
   return true;
 }
 
@@ -1904,13 +1904,22 @@ static int stage_forward_many(rk_stage *s, const int *positions, int nt, bool pe
     max_pos = std::max(max_pos, positions[t] + 1);
   }
   CK(cudaMemcpyAsync(s->m_pos, s->pin_pos, sizeof(int) * nt, cudaMemcpyHostToDevice, st));
-  // Up to three matrices that share the quantized input, in one launch.
+  // Up to three matrices that share the quantized input, in one launch
+  // per format (a mixed-format model's Q4_0 and Q8_0 matrices apart).
   const auto products = [&](int cols, std::initializer_list<MmMat> mats) {
-    return launch_mv_many((int)mats.size(), mats.begin(), cols, nt, s->m_qx, s->m_xs, s->io_tokens, d->err_dev,
-                          d->sms, st);
+    for (const int fmt : {FMT_Q8_0, FMT_Q4_0}) {
+      MmMat same[kMmMaxMats];
+      int n = 0;
+      for (const MmMat &m : mats)
+        if (m.fmt == fmt) same[n++] = m;
+      if (n == 0) continue;
+      const cudaError_t e = launch_mv_many(n, same, cols, nt, s->m_qx, s->m_xs, s->io_tokens, d->err_dev, d->sms, st);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
   };
   const auto mat = [](const rk_matrix *m, float *out, long long stride, int epi) {
-    return MmMat{m->w, m->s, m->rows, out, stride, epi};
+    return MmMat{m->w, m->s, m->rows, out, stride, epi, m->fmt};
   };
   float *X = s->io;
   // When the attention runs batched, every kernel of the submission reads
@@ -3089,8 +3098,8 @@ extern "C" int rk_bench_matvec(rk_matrix *m, int iters, int flags, float *ms_per
 
 extern "C" int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, float *ms_per_launch) {
   if (!m || n <= 0 || iters <= 0 || !ms_per_launch) return fail(RK_ERR_ARGS, "bad argument");
-  if (m->fmt != RK_FMT_Q8_0 || !mv_many_ok(m->rows, m->cols, m->w, m->s))
-    return fail(RK_ERR_ARGS, "the batched kernel takes Q8_0 matrices of a multiple of 128 columns");
+  if (!mv_many_ok(m->fmt, m->rows, m->cols, m->w, m->s))
+    return fail(RK_ERR_ARGS, "the batched kernel takes Q8_0 and Q4_0 matrices of a multiple of 128 columns");
   rk_device *d = m->d;
   const int flush = flags & RK_BENCH_FLUSH;
   Guard g(d);
@@ -3113,7 +3122,7 @@ extern "C" int rk_bench_matvec_many(rk_matrix *m, int n, int iters, int flags, f
   if (e == cudaSuccess) e = launch_quantize_many(dx, n, m->cols, nullptr, 0.0f, 0.0f, dqx, dxs, xs_pitch, d->st);
   if (e == cudaSuccess) e = cudaEventCreate(&e0);
   if (e == cudaSuccess) e = cudaEventCreate(&e1);
-  const MmMat mat{m->w, m->s, m->rows, dout, (long long)rows, EPI_STORE};
+  const MmMat mat{m->w, m->s, m->rows, dout, (long long)rows, EPI_STORE, m->fmt};
   for (int i = 0; e == cudaSuccess && i < iters + 1; i++) {
     if (flush) k_flush_read<<<d->sms * 4, 512, 0, d->st>>>((const int4 *)d->flush, (long long)(d->flush_bytes / 16), d->err_dev + 1);
     e = cudaEventRecord(e0, d->st);

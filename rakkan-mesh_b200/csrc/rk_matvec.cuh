@@ -129,11 +129,12 @@ bool matvec_fused_ok(int fmt, int cols, bool norm);
 // any launch or graph capture.
 cudaError_t init_matvec_attributes();
 
-// ---- Products of one Q8_0 matrix with many input vectors (ForwardMany's
-// projections, model.go:504-518: each token's product is one MatVecQ8) on
-// the tcgen05 tensor cores; bits identical to the single-vector kernel. ----
-// One matrix of a batched launch: Q8_0 weights and scales, its output
-// (token t's row r at out[t·out_stride + r]) and what is done with it.
+// ---- Products of one Q8_0 or Q4_0 matrix with many input vectors
+// (ForwardMany's projections, model.go:504-518: each token's product is one
+// MatVecQ8/Q4) on the tcgen05 tensor cores; bits identical to the
+// single-vector kernel. ----
+// One matrix of a batched launch: its format, weights and scales, its
+// output (token t's row r at out[t·out_stride + r]) and what is done with it.
 struct MmMat {
   const uint8_t *w;
   const float *ws;
@@ -141,12 +142,13 @@ struct MmMat {
   float *out;
   long long out_stride;
   int epi;  // EPI_STORE, EPI_ADD or EPI_ADD_CANON
+  int fmt;  // FMT_Q8_0 or FMT_Q4_0, the same for every matrix of a launch
 };
 constexpr int kMmMaxMats = 3;
 
-// Whether a matrix can take the batched kernel: Q8_0 rows of a multiple of
-// 128 columns, weights and scales 16-byte aligned, TMA available.
-bool mv_many_ok(int rows, int cols, const void *w, const float *ws);
+// Whether a matrix can take the batched kernel: Q8_0 or Q4_0 rows of a
+// multiple of 128 columns, weights and scales 16-byte aligned, TMA available.
+bool mv_many_ok(int fmt, int rows, int cols, const void *w, const float *ws);
 
 // out_m = W_m·x_t for up to kMmMaxMats matrices of cols columns sharing the
 // input (one launch; their row tiles share the grid) and the ntok tokens

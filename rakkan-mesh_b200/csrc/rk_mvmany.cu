@@ -1,7 +1,7 @@
-// rk_mvmany.cu — Q8_0 products of one matrix with many input vectors on the
-// tcgen05 tensor cores: the projections of Stage.ForwardMany
+// rk_mvmany.cu — Q8_0 and Q4_0 products of one matrix with many input
+// vectors on the tcgen05 tensor cores: the projections of Stage.ForwardMany
 // (internal/llm/model.go:504-518), which runs Forward once per token, so
-// every token's product is one MatVecQ8 (internal/num/quant.go:167-181).
+// every token's product is one MatVecQ8/Q4 (internal/num/quant.go:167-196).
 //
 // Reference arithmetic, per row and token (quant.go:157-164, 198-207): the
 // token's Q8_0 input (quantize8, quant.go:34-53); block b's exact int32 sum
@@ -21,6 +21,14 @@
 // few cycles per block; the ordered float work on the CUDA cores and the
 // weight stream bound the kernel. Consecutive CTAs take the token tiles of
 // one row tile, so a weight tile comes from HBM once and from L2 after.
+//
+// Q4_0 (blockSumsQ4, quant.go:209-218: byte j of a block's 16 holds
+// element j in its low nibble and element j+16 in its high one, each
+// nibble - 8): the MMA has no 4-bit integer kind, so TMA brings the packed
+// tile (128 rows × 64 bytes a stage) and four converter warps write each
+// element's nibble - 8 as an int8 into the same swizzled 128 × 128 tile a
+// Q8_0 stage loads directly; the MMAs then give the same exact block sums
+// Σ (nibble - 8)·qx as the reference.
 #include <algorithm>
 #include <cuda.h>
 #include <type_traits>
@@ -51,16 +59,20 @@ struct MmMaps {
 constexpr int kMmStages = 6;  // shared-memory stages (128 input columns each)
 constexpr int kMmGroups = 4;  // TMEM column groups (one stage's four blocks each)
 
-template <int NT>
+template <int NT, int FMT>
 struct MmCfg {
+  static constexpr bool kQ4 = FMT == FMT_Q4_0;
   static constexpr int kEpiWarps = NT / 2;  // NT/8 warpgroups: a row and 8 tokens per thread
-  static constexpr int kThreads = 32 * (kEpiWarps + 2);
-  static constexpr int kW = 128 * 128;    // weight tile bytes
+  static constexpr int kConvWarps = kQ4 ? 4 : 0;  // Q4_0: the weight tile's expansion
+  static constexpr int kThreads = 32 * (kEpiWarps + 2 + kConvWarps);
+  static constexpr int kW = 128 * 128;    // int8 weight tile bytes
   static constexpr int kX = NT * 128;     // token tile bytes
   static constexpr int kWs = 128 * 16;    // weight scales: 128 rows × 4 blocks
   static constexpr int kXs = NT * 16;     // token scales: 4 blocks × NT tokens (block-major)
-  static constexpr int kTx = kW + kX + kWs + kXs;
-  static constexpr int kStage = (kTx + 1023) / 1024 * 1024;
+  static constexpr int kPk = kQ4 ? 128 * 64 : 0;  // the packed Q4_0 tile, after the scales
+  static constexpr int kPkOff = kW + kX + kWs + kXs;
+  static constexpr int kTx = (kQ4 ? kPk : kW) + kX + kWs + kXs;  // bytes TMA brings a stage
+  static constexpr int kStage = (kPkOff + kPk + 1023) / 1024 * 1024;
   static constexpr int kSmem = kMmStages * kStage + 1024;  // + slack to align the ring to 1024 bytes
   static constexpr int kCols = kMmGroups * 4 * NT;         // 256 or 512 TMEM columns
 };
@@ -91,14 +103,14 @@ RK_DEV void mm_terms(float (&acc)[8][8], const int32_t (&v)[NK][8], float4 ws, c
   }
 }
 
-template <int NT>
-__global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
-    k_mv_many_q8(const __grid_constant__ MmMaps maps, const __grid_constant__ CUtensorMap tmX,
-                 const __grid_constant__ CUtensorMap tmXs, const MmArgs a) {
-  using C = MmCfg<NT>;
+template <int NT, int FMT>
+__global__ void __launch_bounds__(MmCfg<NT, FMT>::kThreads, 1)
+    k_mv_many(const __grid_constant__ MmMaps maps, const __grid_constant__ CUtensorMap tmX,
+              const __grid_constant__ CUtensorMap tmXs, const MmArgs a) {
+  using C = MmCfg<NT, FMT>;
   constexpr int S = kMmStages, G = kMmGroups, E = C::kEpiWarps;
   extern __shared__ uint8_t dsmem[];
-  __shared__ __align__(8) uint64_t bars[2 * S + 2 * G + 1];
+  __shared__ __align__(8) uint64_t bars[3 * S + 2 * G + 1];
   __shared__ uint32_t tmem_slot;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ring = (umma::smem_u32(dsmem) + 1023u) & ~1023u;
@@ -109,6 +121,7 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
   const auto accf = [&](int g) { return bar0 + 8u * (2 * S + g); };
   const auto acce = [&](int g) { return bar0 + 8u * (2 * S + G + g); };
   const uint32_t done = bar0 + 8u * (2 * S + 2 * G);
+  const auto conv = [&](int s) { return bar0 + 8u * (2 * S + 2 * G + 1 + s); };  // Q4_0: stage s expanded
   const int y = blockIdx.y;
   const int m = a.nmats > 1 && y >= a.tile0[1] ? (a.nmats > 2 && y >= a.tile0[2] ? 2 : 1) : 0;
   const CUtensorMap *const tmW = &maps.w[m], *const tmWs = &maps.ws[m];
@@ -125,6 +138,8 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
       umma::mbar_init(acce(g), E);
     }
     umma::mbar_init(done, 1);
+    if (C::kQ4)
+      for (int s = 0; s < S; s++) umma::mbar_init(conv(s), C::kConvWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     umma::prefetch_tmap(tmW);
     umma::prefetch_tmap(&tmX);
@@ -150,7 +165,8 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
         }
         const uint32_t st = ring + s * C::kStage;
         umma::mbar_expect_tx(full(s), C::kTx);
-        umma::tma_load_2d(st, tmW, i * 128, r0, full(s));
+        if (C::kQ4) umma::tma_load_2d(st + C::kPkOff, tmW, i * 64, r0, full(s));
+        else umma::tma_load_2d(st, tmW, i * 128, r0, full(s));
         umma::tma_load_2d(st + C::kW, &tmX, i * 128, t0, full(s));
         umma::tma_load_2d(st + C::kW + C::kX, tmWs, i * 4, r0, full(s));
         umma::tma_load_2d(st + C::kW + C::kX + C::kWs, &tmXs, t0, i * 4, full(s));
@@ -165,7 +181,8 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
       constexpr uint32_t idesc = umma::idesc_i8(128, NT, 0);
       for (int i = 0; i < nkb; i++) {
         const int s = i % S, g = i % G;
-        if (!umma::mbar_wait(full(s), (i / S) & 1) || (i >= G && !umma::mbar_wait(acce(g), ((i / G) & 1) ^ 1))) {
+        if (!umma::mbar_wait(C::kQ4 ? conv(s) : full(s), (i / S) & 1) ||
+            (i >= G && !umma::mbar_wait(acce(g), ((i / G) & 1) ^ 1))) {
           atomicExch(a.err, DEV_ERR_TIMEOUT);
           break;
         }
@@ -179,6 +196,39 @@ __global__ void __launch_bounds__(MmCfg<NT>::kThreads, 1)
         umma::mma_commit(accf(g));   // group g holds blocks 4i..4i+3
       }
       umma::mma_commit(done);
+    }
+    __syncwarp();
+  } else if (warp >= E + 2) {
+    // Q4_0 converters: thread ct expands packed blocks ct, ct+128, ... of
+    // the stage (row r = n/4, block b = n%4): element j (low nibble of
+    // byte j) to int8 column 32b + j, element j+16 (high nibble) to column
+    // 32b + 16 + j, as nibble - 8, at the 128-byte swizzle's place (16-byte
+    // chunk c of row r at chunk c ^ (r mod 8)), which is where TMA puts a
+    // Q8_0 tile. The MMA reads the stage once every converter warp has
+    // fenced its stores for the async proxy and arrived.
+    const int ct = (warp - (E + 2)) * 32 + lane;
+    for (int i = 0; i < nkb; i++) {
+      const int s = i % S;
+      if (!umma::mbar_wait(full(s), (i / S) & 1)) {
+        if (lane == 0) atomicExch(a.err, DEV_ERR_TIMEOUT);
+        break;
+      }
+      uint8_t *const wx = ring_p + s * C::kStage;
+      const uint8_t *const pk = wx + C::kPkOff;
+#pragma unroll
+      for (int n = ct; n < 512; n += 128) {
+        const int r = n >> 2, b = n & 3;
+        const uint4 v = *reinterpret_cast<const uint4 *>(pk + r * 64 + b * 16);
+        const auto lo = [](uint32_t x) { return __vsub4(x & 0x0f0f0f0fu, 0x08080808u); };
+        const auto hi = [](uint32_t x) { return __vsub4((x >> 4) & 0x0f0f0f0fu, 0x08080808u); };
+        const uint4 l = make_uint4(lo(v.x), lo(v.y), lo(v.z), lo(v.w));
+        const uint4 h = make_uint4(hi(v.x), hi(v.y), hi(v.z), hi(v.w));
+        *reinterpret_cast<uint4 *>(wx + r * 128 + (((2 * b) ^ (r & 7)) << 4)) = l;
+        *reinterpret_cast<uint4 *>(wx + r * 128 + (((2 * b + 1) ^ (r & 7)) << 4)) = h;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) umma::mbar_arrive(conv(s));
     }
     __syncwarp();
   } else {  // epilogue: warp w reads TMEM lanes 32·(w mod 4).., tokens 8·(w / 4)..
@@ -269,34 +319,39 @@ __global__ void k_silu_mul_many(float *__restrict__ hb, const float *__restrict_
     hb[i] = __fmul_rn(silu(hb[i]), hb2[i]);
 }
 
-template <int NT>
+template <int NT, int FMT>
 static cudaError_t set_mm_attr() {
-  return cudaFuncSetAttribute(k_mv_many_q8<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmCfg<NT>::kSmem);
+  return cudaFuncSetAttribute(k_mv_many<NT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              MmCfg<NT, FMT>::kSmem);
 }
 
 cudaError_t init_mvmany_attributes() {
-  cudaError_t e = set_mm_attr<16>();
-  const cudaError_t e2 = set_mm_attr<32>();
-  return e != cudaSuccess ? e : e2;
+  for (const cudaError_t e : {set_mm_attr<16, FMT_Q8_0>(), set_mm_attr<32, FMT_Q8_0>(), set_mm_attr<16, FMT_Q4_0>()})
+    if (e != cudaSuccess) return e;
+  return cudaSuccess;
 }
 
-bool mv_many_ok(int rows, int cols, const void *w, const float *ws) {
+bool mv_many_ok(int fmt, int rows, int cols, const void *w, const float *ws) {
   const auto aligned = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
   // The scale rows (cols/32 floats) must be whole 16-byte strides for TMA,
-  // and a stage is 128 columns.
-  return rows > 0 && cols > 0 && cols % 128 == 0 && cols < (1 << 17) && aligned(w) && aligned(ws) &&
-         tmap_available();
+  // and a stage is 128 columns (64 packed bytes of a Q4_0 row).
+  return (fmt == FMT_Q8_0 || fmt == FMT_Q4_0) && rows > 0 && cols > 0 && cols % 128 == 0 && cols < (1 << 17) &&
+         aligned(w) && aligned(ws) && tmap_available();
 }
 
-template <int NT>
+template <int NT, int FMT>
 static cudaError_t launch_mm_nt(const MmArgs &a, const MmMat *mats, const int8_t *qx, const float *xs, int xs_pitch,
                                 cudaStream_t st) {
   MmMaps maps;
   CUtensorMap tmX, tmXs;
   const int nb = a.cols / 32;
+  // Q8_0 weight tiles land swizzled for the MMA; Q4_0 packed tiles land as
+  // they are, for the converters.
+  const bool q4 = FMT == FMT_Q4_0;
+  const uint64_t wrow = q4 ? (uint64_t)a.cols / 2 : (uint64_t)a.cols;
   for (int m = 0; m < a.nmats; m++)
-    if (!tmap_2d(&maps.w[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, mats[m].w, (uint64_t)a.cols, (uint64_t)mats[m].rows,
-                 (uint64_t)a.cols, 128, 128, true) ||
+    if (!tmap_2d(&maps.w[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, mats[m].w, wrow, (uint64_t)mats[m].rows, wrow,
+                 q4 ? 64 : 128, 128, !q4) ||
         !tmap_2d(&maps.ws[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, mats[m].ws, (uint64_t)nb, (uint64_t)mats[m].rows,
                  4ull * nb, 4, 128, false))
       return cudaErrorInvalidValue;
@@ -310,7 +365,8 @@ static cudaError_t launch_mm_nt(const MmArgs &a, const MmMat *mats, const int8_t
                false))
     return cudaErrorInvalidValue;
   const dim3 grid((unsigned)((a.ntok + NT - 1) / NT), (unsigned)a.tile0[a.nmats]);
-  return launch_k(k_mv_many_q8<NT>, grid, MmCfg<NT>::kThreads, MmCfg<NT>::kSmem, st, maps, tmX, tmXs, a);
+  return launch_k(k_mv_many<NT, FMT>, grid, MmCfg<NT, FMT>::kThreads, MmCfg<NT, FMT>::kSmem, st, maps, tmX, tmXs,
+                  a);
 }
 
 cudaError_t launch_mv_many(int nmats, const MmMat *mats, int cols, int ntok, const int8_t *qx, const float *xs,
@@ -319,13 +375,15 @@ cudaError_t launch_mv_many(int nmats, const MmMat *mats, int cols, int ntok, con
   if (nmats < 1 || nmats > kMmMaxMats || ((uintptr_t)qx & 15) || ((uintptr_t)xs & 15) || xs_pitch % 4 ||
       xs_pitch < ntok)
     return cudaErrorInvalidValue;
+  const int fmt = mats[0].fmt;  // one format per launch
   MmArgs a{};
   a.cols = cols;
   a.ntok = ntok;
   a.nmats = nmats;
   a.err = err;
   for (int m = 0; m < nmats; m++) {
-    if (!mv_many_ok(mats[m].rows, cols, mats[m].w, mats[m].ws)) return cudaErrorInvalidValue;
+    if (mats[m].fmt != fmt || !mv_many_ok(fmt, mats[m].rows, cols, mats[m].w, mats[m].ws))
+      return cudaErrorInvalidValue;
     a.rows[m] = mats[m].rows;
     a.out[m] = mats[m].out;
     a.out_stride[m] = mats[m].out_stride;
@@ -336,9 +394,12 @@ cudaError_t launch_mv_many(int nmats, const MmMat *mats, int cols, int ntok, con
   const long long row_tiles = a.tile0[nmats];
   if (row_tiles > 65535) return cudaErrorInvalidValue;
   // 32 tokens per CTA halve the weight tiles' re-reads from L2 once the
-  // grid fills the SMs anyway; otherwise 16 give twice the CTAs.
-  if (ntok > 16 && row_tiles * ((ntok + 31) / 32) >= num_sms) return launch_mm_nt<32>(a, mats, qx, xs, xs_pitch, st);
-  return launch_mm_nt<16>(a, mats, qx, xs, xs_pitch, st);
+  // grid fills the SMs anyway; otherwise 16 give twice the CTAs. (Q4_0
+  // takes 16: its converter warps leave the wider CTA too few registers.)
+  if (fmt == FMT_Q4_0) return launch_mm_nt<16, FMT_Q4_0>(a, mats, qx, xs, xs_pitch, st);
+  if (ntok > 16 && row_tiles * ((ntok + 31) / 32) >= num_sms)
+    return launch_mm_nt<32, FMT_Q8_0>(a, mats, qx, xs, xs_pitch, st);
+  return launch_mm_nt<16, FMT_Q8_0>(a, mats, qx, xs, xs_pitch, st);
 }
 
 cudaError_t launch_silu_mul_many(float *hb, const float *hb2, long long n, int num_sms, cudaStream_t st) {

@@ -1,6 +1,6 @@
-"""Batched products of one Q8_0 matrix with many input vectors (the tensor
-core kernel behind ForwardMany) and whole batched prefills, against the
-CPU oracle bit for bit.
+"""Batched products of one Q8_0 or Q4_0 matrix with many input vectors (the
+tensor core kernel behind ForwardMany) and whole batched prefills, against
+the CPU oracle bit for bit.
 
 The reference's ForwardMany (internal/llm/model.go:504-518) runs Forward
 token by token, so every token's product is one MatVecQ8 (quant.go:167-181)
@@ -11,7 +11,8 @@ multiple of 128, token counts that are not a multiple of a CTA's 16 or 32
 tokens, both CTA widths, and the reference's awkward inputs (denormals,
 -0, 1e-30; internal/gpu/gpu_test.go:35-48). The prefills cover two 64-token
 submissions, a start position above 0, GQA, MHA, Qwen2's bias and Qwen3's
-QK-norm with head width 128.
+QK-norm with head width 128, in Q8_0, Q4_0 (expanded to int8 in shared
+memory for the MMAs) and the mixed Q4_M model format (a launch per format).
 """
 import numpy as np
 import pytest
@@ -30,8 +31,9 @@ SHAPES = [(300, 896, 37), (128, 896, 16), (1000, 4864, 5), (4864, 896, 160), (7,
           (384, 1024, 33)]
 
 
+@pytest.mark.parametrize("fmt", [rk.FMT_Q8_0, rk.FMT_Q4_0], ids=["q8_0", "q4_0"])
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_mulvec_many_matches_cpu(dev, shape):
+def test_mulvec_many_matches_cpu(dev, shape, fmt):
     rows, cols, n = shape
     rng = np.random.default_rng(rows * 7 + cols + n)
     w = awkward(rng, rows * cols, 0.02)
@@ -42,22 +44,23 @@ def test_mulvec_many_matches_cpu(dev, shape):
     if n > 2:
         xs[1] = 0.0  # an input whose every block quantizes to zero
         xs[2, :32] = 0.0
-    q, s = ro.quantize(rk.FMT_Q8_0, w)
-    m = rk.Matrix(dev, rows, cols, rk.FMT_Q8_0, q, s)
+    q, s = ro.quantize(fmt, w)
+    m = rk.Matrix(dev, rows, cols, fmt, q, s)
     try:
         got = m.mulvec_many(xs)
         for t in range(n):
-            same_bits(got[t], ro.matvec(rk.FMT_Q8_0, q, s, xs[t], rows, cols))
+            same_bits(got[t], ro.matvec(fmt, q, s, xs[t], rows, cols))
     finally:
         m.free()
     assert dev.used() == 0
 
 
 def test_mulvec_many_other_formats(dev):
-    """Matrices the batched kernel does not take (Q4_0, widths that are not
-    multiples of 128) give the same bits through one product per vector."""
+    """Matrices the batched kernel does not take (widths that are not
+    multiples of 128, float formats) give the same bits through one product
+    per vector."""
     rng = np.random.default_rng(3)
-    for fmt, rows, cols in [(rk.FMT_Q4_0, 200, 256), (rk.FMT_Q8_0, 96, 96), (rk.FMT_F32, 40, 64)]:
+    for fmt, rows, cols in [(rk.FMT_Q4_0, 200, 160), (rk.FMT_Q8_0, 96, 96), (rk.FMT_F32, 40, 64)]:
         w = awkward(rng, rows * cols, 0.02)
         q, s = (w, None) if fmt == rk.FMT_F32 else ro.quantize(fmt, w)
         xs = np.stack([awkward(rng, cols, 1.0) for _ in range(5)])
@@ -81,16 +84,17 @@ VARIANTS = {
 }
 
 
-def prefill_config(**over):
+def prefill_config(dtype="q8_0", **over):
     base = dict(dim=256, hidden=384, layers=3, heads=4, kv_heads=2, vocab=50, seq_len=160, shared_classifier=1,
                 head_dim=0, rope_theta=0.0, norm_eps=0.0, qkv_bias=0, qk_norm=0)
     base.update(over)
-    return synth.config("", "q8_0", **base)
+    return synth.config("", dtype, **base)
 
 
+@pytest.mark.parametrize("dtype", ["q8_0", "q4_0", "q4_m"])
 @pytest.mark.parametrize("variant", sorted(VARIANTS))
-def test_batched_prefill_matches_cpu(dev, variant):
-    c = prefill_config(**VARIANTS[variant])
+def test_batched_prefill_matches_cpu(dev, variant, dtype):
+    c = prefill_config(dtype, **VARIANTS[variant])
     vs = 303
     om = ro.OracleModel(c, seed=17, vec_seed=vs)
     layers = upload_layers(dev, c, oracle_weights(om, c), vs)
@@ -155,17 +159,20 @@ def test_unbatched_stages_report_it(dev):
         om.free()
 
 
-@pytest.mark.parametrize("heads,kv_heads,fills,seq_len", [(8, 2, [0, 7, 64, 130, 33], 200),
-                                                           (4, 4, [1500, 3, 777], 1600),
-                                                           (14, 2, [250, 1, 99, 5], 300)],
-                         ids=["gqa4", "mha_long", "gqa7"])
-def test_batched_decode_matches_cpu(dev, heads, kv_heads, fills, seq_len):
+@pytest.mark.parametrize("heads,kv_heads,fills,seq_len,dtype", [(8, 2, [0, 7, 64, 130, 33], 200, "q8_0"),
+                                                                 (4, 4, [1500, 3, 777], 1600, "q8_0"),
+                                                                 (14, 2, [250, 1, 99, 5], 300, "q8_0"),
+                                                                 (8, 2, [0, 7, 64, 130, 33], 200, "q4_0"),
+                                                                 (4, 4, [900, 3, 77], 1000, "q4_m")],
+                         ids=["gqa4", "mha_long", "gqa7", "gqa4_q4_0", "mha_q4_m"])
+def test_batched_decode_matches_cpu(dev, heads, kv_heads, fills, seq_len, dtype):
     """Several independent sequences decoded together (rk_stage_forward_batch):
     each sequence's cache is filled to its own length (up to 1500 positions),
     then three steps run for all of them at once, each at its own position,
     with 4, 1 and 7 query heads per kv head. Every sequence's activations
     equal its own oracle Stage's Forward, bit for bit."""
-    c = prefill_config(heads=heads, kv_heads=kv_heads, head_dim=64, dim=256, layers=2, seq_len=seq_len, qkv_bias=1)
+    c = prefill_config(dtype, heads=heads, kv_heads=kv_heads, head_dim=64, dim=256, layers=2, seq_len=seq_len,
+                       qkv_bias=1)
     nseq, seed = len(fills), 41
     # One oracle Stage per sequence (the same seeded weights in each).
     oms = [ro.OracleModel(c, seed=31, vec_seed=5) for _ in range(nseq)]
