@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--dtype", default="q8_0")
     p.add_argument("--ctx", type=int, default=CTX)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-workloads", action="store_true",
+                   help="skip the other configurations' workloads (measured after the headline at N=1)")
     p.add_argument("--mode", default="rows", choices=["rows", "replicas", "pipeline"],
                    help="N>1: shard every layer's rows over the N GPUs (NCCL all-gather; one sequence), "
                         "or run N independent replicas")
@@ -217,6 +219,95 @@ def run_prefill(args):
                       "steps": args.steps}), flush=True)
     dm.free()
     dev.close()
+
+
+def secondary_workloads(dev):
+    """The other configurations' workloads, measured through the public API
+    after the headline (one GPU, synthetic seeded weights and inputs, each
+    timed after a warm-up): config 1's 8-token prompt + 128 greedy tokens;
+    config 2's tensor matmul_t sweep (device time, L2 flushed); config 3's
+    512-token prefill + 256 greedy tokens; config 4's Q4_0 batch-1 decode at
+    a 4096-token context (graph replays, device time) and batch-32 decode in
+    Q8_0 and Q4_0 (one step of 32 sequences per call, host time); config
+    5's 2048-token prefill + 512 greedy tokens. Generation goes through
+    rk_model_generate (the prompt in ForwardMany submissions of 64 tokens,
+    then one step graph per token, each token read back); prefill figures
+    are its time for the prompt and one token. A workload that fails
+    reports its error instead of a number."""
+    import numpy as np
+    import rkcuda as rk
+    import synth
+    out = {}
+
+    def timed(fn, reps=1):
+        fn()  # warm-up
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) * 1000.0 / reps
+
+    def generation(key, name, dtype, n_prompt, n_new):
+        c = synth.config(name, dtype, seq_len=n_prompt + n_new + 8)
+        dm = synth.DeviceModel(dev, c, SEED, ctx=n_prompt + n_new + 8)
+        try:
+            p = np.random.default_rng(SEED).integers(0, c.vocab, n_prompt).astype(np.int32)
+            pre = timed(lambda: dm.model.generate(p, 1))
+            total = timed(lambda: dm.model.generate(p, n_new))
+            out[key] = {"prompt": n_prompt, "new_tokens": n_new, "batched_prompt": dm.stage.batched(),
+                        "total_ms": total, "prefill_ms": pre, "prefill_tok_s": n_prompt * 1000.0 / pre,
+                        "decode_tok_s": (n_new - 1) * 1000.0 / max(total - pre, 1e-9),
+                        "workload_tok_s": (n_prompt + n_new) * 1000.0 / total}
+        finally:
+            dm.free()
+
+    def decode_bs1(key, name, dtype, ctx=4096, iters=20):
+        c = synth.config(name, dtype, seq_len=ctx + 64)
+        dm = synth.DeviceModel(dev, c, SEED, ctx=ctx + 64)
+        try:
+            dm.stage.fill_cache(ctx, SEED)
+            dm.model.bench(ctx, 3)
+            ms = dm.model.bench(ctx, iters)
+            out[key] = {"context": ctx, "ms_per_step": ms, "tok_s": 1000.0 / ms, "timing": "device, graph replays"}
+        finally:
+            dm.free()
+
+    def decode_batch(key, name, dtype, n=32, ctx=4096, steps=5):
+        c = synth.config(name, dtype, seq_len=ctx + 64)
+        dm = synth.DeviceModel(dev, c, SEED, ctx=ctx + 64, nseq=n)
+        try:
+            dm.stage.fill_cache(ctx, SEED)
+            xs = np.random.default_rng(SEED).standard_normal((n, c.dim)).astype(np.float32)
+            ms = timed(lambda: dm.stage.forward_batch(xs, [ctx] * n), steps)
+            out[key] = {"batch": n, "context": ctx, "ms_per_step": ms, "tok_s": n * 1000.0 / ms,
+                        "scope": "the stage's layers, host buffers in and out"}
+        finally:
+            dm.free()
+
+    def tensor_sweep(key):
+        rows = []
+        for dtype, name in ((rk.TENSOR_I8, "i8"), (rk.TENSOR_F32, "f32")):
+            for m in (1, 16, 128, 512):
+                rk.bench_tensor(dev, dtype, True, m, 4096, 4096, 2)
+                ms = rk.bench_tensor(dev, dtype, True, m, 4096, 4096, 10)
+                rows.append({"dtype": name, "op": "matmul_t", "m": m, "n": 4096, "k": 4096, "ms": ms,
+                             "tops": 2 * m * 4096 * 4096 / (ms * 1e-3) / 1e12})
+        out[key] = rows
+
+    jobs = [
+        ("config1_stories15m_q8_0", lambda k: generation(k, "stories15M", "q8_0", 8, 128)),
+        ("config2_tensor_matmul_t", tensor_sweep),
+        ("config3_qwen2.5-0.5b_q8_0", lambda k: generation(k, "qwen2.5-0.5b", "q8_0", 512, 256)),
+        ("config4_llama3-8b_q4_0_bs1", lambda k: decode_bs1(k, "llama3-8b", "q4_0")),
+        ("config4_llama3-8b_q8_0_bs32", lambda k: decode_batch(k, "llama3-8b", "q8_0")),
+        ("config4_llama3-8b_q4_0_bs32", lambda k: decode_batch(k, "llama3-8b", "q4_0")),
+        ("config5_qwen3-32b_q8_0", lambda k: generation(k, "qwen3-32b", "q8_0", 2048, 512)),
+    ]
+    for key, job in jobs:
+        try:
+            job(key)
+        except Exception as e:  # noqa: BLE001 (reported, not fatal to the headline)
+            out[key] = {"error": f"{type(e).__name__}: {e}"}
+    return out
 
 
 def workload(args):
@@ -515,8 +606,14 @@ def main():
         }
         if parity is not None:
             line["parity_vs_1gpu"] = parity
+        if world == 1 and args.layers == 0 and not args.no_workloads:
+            # The other configurations, once the headline model is freed.
+            dm.free()
+            dm = None
+            line["workloads"] = secondary_workloads(dev)
         print(json.dumps(line), flush=True)
-    dm.free()
+    if dm is not None:
+        dm.free()
     if group:
         barrier()
         group.free()

@@ -270,7 +270,10 @@ int rk_model_step(rk_model *m, int token, int pos, float *logits, int *next);
 /* Greedy decode: prompt[0..n_prompt) at positions 0.., then n_new tokens
  * fed back on the device. out_tokens receives the n_new generated tokens;
  * out_logits, if not NULL, the logits of every step after the first
- * prompt token ((n_prompt - 1 + n_new) × vocab floats). */
+ * prompt token ((n_prompt - 1 + n_new) × vocab floats). Without out_logits,
+ * a stage that runs ForwardMany batched (rk_stage_batched) takes the
+ * prompt's tokens but the last in submissions of up to 64 (the same bits
+ * as token by token). */
 int rk_model_generate(rk_model *m, const int *prompt, int n_prompt, int n_new, int *out_tokens, float *out_logits);
 
 /* ---- Row sharding over the GPUs of one box (one process per GPU) ----

@@ -1312,6 +1312,7 @@ struct rk_stage {
   float *m_scores = nullptr;  // per-token score rows [io_tokens][heads][att_stride]
   int8_t *m_qx = nullptr;
   int *m_pos = nullptr, *pin_pos = nullptr;
+  cudaEvent_t pos_copied = nullptr;  // the last copy out of pin_pos (recorded after it)
   // Row sharding (layer_dims): this process's rank of G; null/1 unsharded.
   rk_group *grp = nullptr;
   int G = 1, rank = 0;
@@ -1349,6 +1350,7 @@ static void stage_release(rk_stage *s) {
   for (void *p : s->allocs) cudaFree(p);
   cudaFreeHost(s->pin_io);
   cudaFreeHost(s->pin_pos);
+  if (s->pos_copied) cudaEventDestroy(s->pos_copied);
   s->d->used -= s->bytes;
   delete s;
 }
@@ -1899,11 +1901,16 @@ static int stage_forward_many(rk_stage *s, const int *positions, int nt, bool pe
   const int hs = head_size(c), qd = c->heads * hs, kvd = c->kv_heads * hs, D = c->dim, H = c->hidden;
   const float eps = cfg_eps(c), recipD = host_recip32((float)D);
   int max_pos = 0;
+  // Submissions may be queued back to back (rk_model_generate's prompt):
+  // the previous one's copy out of pin_pos must have run before the host
+  // rewrites it, or that submission would see these positions.
+  CK(cudaEventSynchronize(s->pos_copied));
   for (int t = 0; t < nt; t++) {
     s->pin_pos[t] = positions[t];
     max_pos = std::max(max_pos, positions[t] + 1);
   }
   CK(cudaMemcpyAsync(s->m_pos, s->pin_pos, sizeof(int) * nt, cudaMemcpyHostToDevice, st));
+  CK(cudaEventRecord(s->pos_copied, st));
   // Up to three matrices that share the quantized input, in one launch
   // per format (a mixed-format model's Q4_0 and Q8_0 matrices apart).
   const auto products = [&](int cols, std::initializer_list<MmMat> mats) {
@@ -2068,6 +2075,7 @@ static int stage_new(rk_device *d, const rk_config *c, rk_layer *const *layers, 
     ALLOC(m_pos, 4 * T);
     ALLOC(m_scores, 4 * T * c->heads * s->att_stride);
     cudaError_t e = cudaMallocHost(&s->pin_pos, 4 * T);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->pos_copied, cudaEventDisableTiming);
     if (e != cudaSuccess) {
       rc = cuda_fail(e, "stage staging");
       goto fail_;
@@ -2362,6 +2370,7 @@ struct rk_model {
   rk_stage *stage = nullptr;
   rk_head *head = nullptr;
   int *token_dev = nullptr, *next_dev = nullptr;
+  int *prompt_dev = nullptr;  // a batched prompt chunk's tokens (64)
   unsigned long long *key_dev = nullptr;  // argmax key (0 between steps)
   int *pin_tok = nullptr;
   float *pin_logits = nullptr;
@@ -2394,6 +2403,7 @@ static void model_release(rk_model *m) {
   cudaStreamSynchronize(m->d->st);
   if (m->graph) cudaGraphExecDestroy(m->graph);
   cudaFree(m->token_dev);
+  cudaFree(m->prompt_dev);
   cudaFree(m->next_dev);
   cudaFree(m->key_dev);
   cudaFreeHost(m->pin_tok);
@@ -2421,6 +2431,7 @@ extern "C" int rk_model_new(rk_device *d, rk_matrix *embed, rk_stage *stage, rk_
   if (e == cudaSuccess) e = cudaMemset(m->key_dev, 0, 16);
   if (e == cudaSuccess) e = cudaMalloc(&m->next_dev, 16);
   if (e == cudaSuccess) e = cudaMemset(m->next_dev, 0, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&m->prompt_dev, sizeof(int) * 64);
   if (e == cudaSuccess) e = cudaMallocHost(&m->pin_tok, 64);
   if (e == cudaSuccess) e = cudaMallocHost(&m->pin_logits, 4 * (size_t)stage->c.vocab);
   if (e != cudaSuccess) {
@@ -2485,13 +2496,36 @@ extern "C" int rk_model_generate(rk_model *m, const int *prompt, int n_prompt, i
   Guard g(d);
   int rc = set_device(d);
   if (rc) return rc;
+  // Without per-position logits, the prompt's tokens but the last run
+  // through the stage's ForwardMany (batched products when the stage takes
+  // them; bits as Forward token by token), in chunks of the stage's
+  // io_tokens with at least two tokens each; the step graph then takes the
+  // last prompt token and the generated ones.
+  int first = 0;
+  if (!out_logits && s->many && n_prompt > 2) {
+    first = n_prompt - 1;
+    if (first % s->io_tokens == 1) first--;
+  }
+  const int D = s->c.dim;
   int *pin = nullptr;
   CK(cudaMallocHost(&pin, sizeof(int) * (size_t)(n_prompt + n_new + 2)));
   memcpy(pin, prompt, sizeof(int) * n_prompt);
-  pin[n_prompt + n_new] = 0;
+  pin[n_prompt + n_new] = first;
   auto run = [&]() -> int {
+    for (int start = 0; start < first; start += s->io_tokens) {
+      const int nt = std::min(s->io_tokens, first - start);
+      int positions[64];
+      CK(cudaMemcpyAsync(m->prompt_dev, &pin[start], sizeof(int) * nt, cudaMemcpyHostToDevice, d->st));
+      for (int t = 0; t < nt; t++) {
+        positions[t] = start + t;
+        CK(launch_embed(m->embed->fmt, m->embed->w, m->embed->s, m->embed->rows, D, m->prompt_dev + t,
+                        s->io + (size_t)t * D, d->err_dev, d->st));
+      }
+      int r = stage_forward_many(s, positions, nt, false);
+      if (r) return r;
+    }
     CK(cudaMemcpyAsync(s->pos_dev, &pin[n_prompt + n_new], 4, cudaMemcpyHostToDevice, d->st));
-    for (int i = 0; i < steps; i++) {
+    for (int i = first; i < steps; i++) {
       // Prompt tokens are fed from the host; generated ones are already in
       // token_dev (k_feed_token).
       if (i < n_prompt) CK(cudaMemcpyAsync(m->token_dev, &pin[i], 4, cudaMemcpyHostToDevice, d->st));

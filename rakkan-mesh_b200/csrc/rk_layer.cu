@@ -120,6 +120,17 @@ RK_DEV int attn_positions(const AttnArgs &a) {
   return a.positions_dev ? *a.positions_dev + a.positions_add : a.positions;
 }
 
+// A position count read from the device (a graph replay, a batched
+// submission) above what the launch was sized for (max_positions) is
+// refused: the error word gets DEV_ERR_RANGE and the launch does nothing,
+// rather than reach past its shared memory or the caches.
+RK_DEV bool attn_positions_fit(const AttnArgs &a, int P) {
+  const int maxP = a.positions_dev ? a.max_positions : a.positions;
+  if (P >= 0 && P <= maxP) return true;
+  if (a.err && threadIdx.x == 0) atomicExch(a.err, DEV_ERR_RANGE);
+  return false;
+}
+
 // Scores: att[h][t] = float32(Dot32(q_h, k_t)·invSqrt). A warp per position
 // t, for every query head of one key/value head (grid.y): k_t is read once
 // for the group.
@@ -333,6 +344,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs
   __shared__ float s_val;
   const int tz = BATCH ? (int)blockIdx.y : 0;
   const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
+  if (!attn_positions_fit(a, P)) return;
   float *x = (BATCH ? a.att + tz * a.tok_att : a.att) + (long long)blockIdx.x * a.att_stride;
   const bool in_smem = P <= kSoftmaxSmem;
   float *v = in_smem ? sv : x;
@@ -400,6 +412,7 @@ __global__ void __launch_bounds__(32) k_attn_wsum_seq(const AttnArgs a) {
   const int lane = threadIdx.x, tz = blockIdx.y;
   const int ngr = a.hs / 32, kvh = blockIdx.x / ngr, e0 = (blockIdx.x % ngr) * 32;
   const int P = a.positions_dev[tz] + a.positions_add;
+  if (!attn_positions_fit(a, P)) return;
   const float *vb = a.vals + tz * a.tok_vals + (long long)(kvh * a.hs + e0) * a.v_pitch;
   const float *wb = a.att + tz * a.tok_att + (long long)(kvh * G) * a.att_stride;
   const int ntile = (P + TP - 1) / TP;
@@ -684,6 +697,10 @@ __global__ void __launch_bounds__(kFsMaxThreads)
   griddep_wait();
   const int tz = BATCH ? (int)blockIdx.z : 0;
   const int P = BATCH ? a.positions_dev[tz] + a.positions_add : attn_positions(a);
+  if (!attn_positions_fit(a, P)) {
+    cluster_wait();  // (every member sees the same count and leaves here)
+    return;
+  }
   const float *const att = BATCH ? a.att + tz * a.tok_att : a.att;
   float *const out = BATCH ? a.out + tz * a.tok_out : a.out;
   const float *const vals = BATCH ? a.vals + tz * a.tok_vals : a.vals;
