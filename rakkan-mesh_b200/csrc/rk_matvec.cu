@@ -158,45 +158,48 @@ RK_DEV void quantize_warps(const float *__restrict__ x, int n, const float *__re
       Grp::sync();
     }
     // Four threads (a lane quad) quantize block t of the chunk, eight
-    // values each: amax and the integer sum are quad reductions (both order
-    // free). A thread reads its eight values in an order rotated by t, so
-    // the 32 lanes of a warp hit 32 different banks.
+    // values each: two 16-byte loads of x (and of the norm weights), one
+    // 8-byte store of the eight int8s (every staging area, qx and its
+    // blocks start on 16-byte boundaries). amax and the integer sum are
+    // quad reductions (both order free).
     const int ntask = (m / 32) * 4;
     for (int task = threadIdx.x; task < ntask; task += nt) {
       const int t = task >> 2, sub = task & 3;
       const unsigned qmask = 0xfu << (lane & ~3);
       const int b = c0 / 32 + t;
-      const float *src = stage + t * 32 + sub * 8;
-      float v[8];
+      const int o = t * 32 + sub * 8;
+      const float4 xa = *reinterpret_cast<const float4 *>(stage + o);
+      const float4 xb = *reinterpret_cast<const float4 *>(stage + o + 4);
+      float v[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      if (NORM) {
+        const float4 wa = *reinterpret_cast<const float4 *>(wstage + o);
+        const float4 wb = *reinterpret_cast<const float4 *>(wstage + o + 4);
+        const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = __fmul_rn(w8[j], __fmul_rn(inv, v[j]));
+      }
       uint32_t kmax = 0;
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const int jj = (j + t) & 7;
-        float vv = src[jj];
-        if (NORM) vv = __fmul_rn(wstage[t * 32 + sub * 8 + jj], __fmul_rn(inv, vv));
-        v[j] = vv;
-        kmax = max(kmax, f2u(fabsf(vv)));
-      }
+      for (int j = 0; j < 8; j++) kmax = max(kmax, f2u(fabsf(v[j])));
       kmax = max(kmax, __shfl_xor_sync(qmask, kmax, 1));
       kmax = max(kmax, __shfl_xor_sync(qmask, kmax, 2));
       // amax as Go's max: an unsigned max of the |v| bit patterns (bit order
       // is value order for non-negative floats; a NaN lands above +Inf).
       const float amax = kmax > 0x7f800000u ? u2f(kCanonNaN) : u2f(kmax);
       const float d = __fmul_rn(amax, u2f(K_1_127));
-      int8_t *q = qx + b * 32 + sub * 8;
       int sum = 0;
-      if (d == 0.0f || d != d) {
-#pragma unroll
-        for (int j = 0; j < 8; j++) q[(j + t) & 7] = 0;
-      } else {
+      uint32_t lo = 0, hi = 0;  // the eight int8s, element j in byte j
+      if (!(d == 0.0f || d != d)) {
         const float id = recip32(d);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
           const int qq = quant_q8(__fmul_rn(v[j], id));
-          q[(j + t) & 7] = (int8_t)qq;
           sum += qq;
+          if (j < 4) lo |= (uint32_t)(qq & 0xff) << (8 * j);
+          else hi |= (uint32_t)(qq & 0xff) << (8 * (j - 4));
         }
       }
+      *reinterpret_cast<uint2 *>(qx + b * 32 + sub * 8) = make_uint2(lo, hi);
       sum += __shfl_xor_sync(qmask, sum, 1);
       sum += __shfl_xor_sync(qmask, sum, 2);
       if (sub == 0) {
