@@ -401,12 +401,14 @@ __global__ void __launch_bounds__(kSoftmaxThreads) k_attn_softmax(const AttnArgs
 // element, running the chains of the kv head's G query heads side by side.
 // The warp copies its 32 rows in tiles of 64 positions into shared memory
 // with 16-byte cp.async (half a warp per 256-byte row segment, so every
-// load is whole sectors), the next tile in flight while the lanes add the
-// current one from shared memory (rows 68 floats apart: conflict-free).
+// load is whole sectors), the next two tiles in flight while the lanes add
+// the current one from shared memory (rows 68 floats apart: conflict-free).
+// (With one tile in flight the 32-sequence step read values at a third of
+// HBM's bandwidth: a warp's 8 KB did not cover the latency.)
 template <int G>
 __global__ void __launch_bounds__(32) k_attn_wsum_seq(const AttnArgs a) {
-  constexpr int TP = 64, PITCH = TP + 4;
-  __shared__ __align__(16) float sv[2][32 * PITCH];
+  constexpr int TP = 64, PITCH = TP + 4, NS = 3;
+  __shared__ __align__(16) float sv[NS][32 * PITCH];
   griddep_trigger();
   griddep_wait();
   const int lane = threadIdx.x, tz = blockIdx.y;
@@ -417,11 +419,14 @@ __global__ void __launch_bounds__(32) k_attn_wsum_seq(const AttnArgs a) {
   const float *wb = a.att + tz * a.tok_att + (long long)(kvh * G) * a.att_stride;
   const int ntile = (P + TP - 1) / TP;
   // Tile k into buffer buf: 32 rows × 16 float4, flat index f = lane + 32j
-  // (row f / 16, float4 f % 16); positions at or past P are not read.
+  // (row f / 16, float4 f % 16); positions at or past P are not read. A
+  // tile past the last is an empty copy group, so the group count per
+  // iteration stays the same.
   const auto load_tile = [&](int k, int buf) {
     const int t0 = k * TP;
 #pragma unroll
     for (int j = 0; j < 16; j++) {
+      if (k >= ntile) break;
       const int f = lane + 32 * j, r = f >> 4, c = f & 15, t = t0 + 4 * c;
       if (t < P)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
@@ -434,16 +439,13 @@ __global__ void __launch_bounds__(32) k_attn_wsum_seq(const AttnArgs a) {
   float acc[G];
 #pragma unroll
   for (int g = 0; g < G; g++) acc[g] = 0.0f;
-  if (ntile > 0) load_tile(0, 0);
+#pragma unroll
+  for (int k = 0; k < NS - 1; k++) load_tile(k, k);
   for (int k = 0; k < ntile; k++) {
-    if (k + 1 < ntile) {
-      load_tile(k + 1, (k + 1) & 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
+    load_tile(k + NS - 1, (k + NS - 1) % NS);  // the buffer tile k - 1 used
+    asm volatile("cp.async.wait_group %0;" ::"n"(NS - 1) : "memory");  // tile k has landed
     __syncwarp();
-    const float *row = sv[k & 1] + lane * PITCH;
+    const float *row = sv[k % NS] + lane * PITCH;
     const int t0 = k * TP, n = min(TP, P - t0), n4 = n >> 2;
     for (int c = 0; c < n4; c++) {
       const float4 v = *reinterpret_cast<const float4 *>(row + 4 * c);
