@@ -85,19 +85,24 @@ def parse():
 
 
 def run_kernel(args):
-    """One Q8_0/Q4_0 matvec of --shape, L2 flushed before each launch."""
+    """One matvec of --shape in --dtype (q8_0, q4_0, f32, bf16), L2 flushed
+    before each launch."""
     import rkcuda as rk
     rows, cols = map(int, args.shape.split("x"))
-    fmt = {"q8_0": rk.FMT_Q8_0, "q4_0": rk.FMT_Q4_0}[args.dtype]
+    fmt = {"q8_0": rk.FMT_Q8_0, "q4_0": rk.FMT_Q4_0, "f32": rk.FMT_F32, "bf16": rk.FMT_BF16}[args.dtype]
     dev = rk.Device(int(os.environ.get("LOCAL_RANK", "0")))
     m = rk.Matrix.generate(dev, rows, cols, fmt, SEED, 1, 0.02)
-    fused = args.prologue == "fused"
+    quantized = fmt in (rk.FMT_Q8_0, rk.FMT_Q4_0)
+    fused = args.prologue == "fused" and quantized
     m.bench(max(1, args.warmup), flush=True, fused=fused)
     ms = m.bench(args.steps, flush=True, fused=fused)
     n = rows * cols
-    nbytes = n + n // 32 * 4 if fmt == rk.FMT_Q8_0 else n // 2 + n // 32 * 4
+    nbytes = {rk.FMT_Q8_0: n + n // 32 * 4, rk.FMT_Q4_0: n // 2 + n // 32 * 4, rk.FMT_F32: 4 * n,
+              rk.FMT_BF16: 2 * n}[fmt]
     peak, kind = measured_peak()
-    print(json.dumps({"kernel": f"k_matvec_q<{args.dtype}>", "shape": args.shape, "prologue": args.prologue, "ms": ms,
+    kname = f"k_matvec_q<{args.dtype}>" if quantized else f"k_matvec_f<{args.dtype}>"
+    print(json.dumps({"kernel": kname, "shape": args.shape, "prologue": args.prologue if quantized else "none",
+                      "ms": ms,
                       "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_source": kind,
                       "frac": nbytes / (ms * 1e-3) / 1e9 / peak}), flush=True)
     m.free()

@@ -3013,7 +3013,8 @@ static int matrix_generate(rk_device *d, long long first, int rows, int cols, in
         // would need the previous slice's last block (not for finite weights).
         e = launch_quantize_q4_w(tmp, cnt, m->w + off / 2, m->s + off / 32, stale, d->st);
         break;
-      default: e = cudaErrorInvalidValue;  // bf16 generation: convert on the host
+      case RK_FMT_BF16: e = launch_to_bf16(tmp, cnt, reinterpret_cast<uint16_t *>(m->w) + off, d->st); break;
+      default: e = cudaErrorInvalidValue;
     }
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(d->st);

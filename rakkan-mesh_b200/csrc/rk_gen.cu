@@ -83,6 +83,22 @@ __global__ void k_quantize_q8_w(const float *w, long long nblocks, int8_t *q, fl
   }
 }
 
+__global__ void k_to_bf16(const float *__restrict__ w, long long n, uint16_t *__restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float f = w[i];
+    const uint32_t b = __float_as_uint(f);
+    out[i] = f != f ? (uint16_t)((b >> 16) | 0x40u) : (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+  }
+}
+
+cudaError_t launch_to_bf16(const float *w, long long n, uint16_t *out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_to_bf16<<<int(blocks), 256, 0, st>>>(w, n, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_quantize_q8_w(const float *w, long long n, int8_t *q, float *scales, cudaStream_t st) {
   const long long nb = n / 32;
   if (nb <= 0) return cudaSuccess;

@@ -1270,17 +1270,118 @@ __global__ void __launch_bounds__(256) k_matvec_f(const MvArgs a) {
           row -= a.part[part].rows;
           part++;
         }
+      // Lane j's chain over elements j, j+32, ... (Dot32's order). Each
+      // round loads the lane's next kU weights and inputs before the chain
+      // adds them in order, so kU loads per lane are in flight rather than
+      // one; elements past the row are not added (adding +0 could turn a
+      // -0 sum into +0).
+      constexpr int kU = 16;
       float s = 0.0f;
-      if (FMT == FMT_F32) {
-        const float *w = reinterpret_cast<const float *>(a.part[part].w) + row * cols;
-        for (int e = lane; e < cols; e += 32) s = __fadd_rn(s, __fmul_rn(__ldg(w + e), a.x[e]));
-      } else {
-        const uint16_t *w = reinterpret_cast<const uint16_t *>(a.part[part].w) + row * cols;
-        for (int e = lane; e < cols; e += 32)
-          s = __fadd_rn(s, __fmul_rn(__uint_as_float(uint32_t(__ldg(w + e)) << 16), a.x[e]));
+      const char *wrow = reinterpret_cast<const char *>(a.part[part].w) + row * cols * (FMT == FMT_F32 ? 4 : 2);
+      for (int e0 = lane; e0 < cols; e0 += 32 * kU) {
+        float wv[kU], xv[kU];
+#pragma unroll
+        for (int k = 0; k < kU; k++) {
+          const int e = e0 + 32 * k;
+          if (e < cols) {
+            wv[k] = FMT == FMT_F32 ? __ldg(reinterpret_cast<const float *>(wrow) + e)
+                                   : __uint_as_float(uint32_t(__ldg(reinterpret_cast<const uint16_t *>(wrow) + e)) << 16);
+            xv[k] = __ldg(a.x + e);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kU; k++)
+          if (e0 + 32 * k < cols) s = __fadd_rn(s, __fmul_rn(wv[k], xv[k]));
       }
       const float r = combine32(s);
       if (lane == 0) {
+        float *out = a.part[part].out;
+        switch (a.epi) {
+          case EPI_STORE: out[row] = r; break;
+          case EPI_ADD: out[row] = __fadd_rn(out[row], r); break;
+          case EPI_ADD_CANON: out[row] = canonical(__fadd_rn(out[row], r)); break;
+          case EPI_SILU:
+            if (sub == 0) r0 = r;
+            else a.part[0].out[row] = __fmul_rn(silu(r0), r);
+            break;
+        }
+      }
+    }
+  }
+}
+
+// bfloat16 matvec with 16-byte loads (DotBF16, matvec.go:47-58). Dot32's 32
+// chains are independent, so lane q of a row's four lanes runs chains
+// 8q..8q+7: at step i it adds elements 32i + 8q .. 32i + 8q + 7, eight
+// adjacent weights that one 16-byte load brings. A warp serves eight rows
+// (lanes 4r..4r+3 row r), kMvbU steps of loads in flight per lane; x is
+// staged in shared memory once per CTA. combine32's tree (matvec.go:60-66)
+// is then two lane exchanges (chains j and j+8, then j+16: lanes q^1, q^2)
+// and three pairings inside the lane (chains j, j^1, j^2, j^4), the same
+// additions. Widths must be multiples of 8 (16-byte rows).
+constexpr int kMvbU = 8, kMvbMaxCols = 12288;
+__global__ void __launch_bounds__(256) k_matvec_bf16v(const MvArgs a) {
+  extern __shared__ __align__(16) float mvb_x[];
+  griddep_trigger();
+  griddep_wait();
+  const int cols = a.cols;
+  for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
+    reinterpret_cast<float4 *>(mvb_x)[i] = reinterpret_cast<const float4 *>(a.x)[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, q = lane & 3, rg = lane >> 2;
+  const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long G = (long long)gridDim.x * (blockDim.x >> 5);
+  const int nsub = a.epi == EPI_SILU ? 2 : 1;
+  long long units = 0;
+  if (nsub == 2) units = a.part[0].rows;
+  else
+    for (int p = 0; p < a.nparts; p++) units += a.part[p].rows;
+  const int nsteps = (cols + 31) / 32;
+  for (long long grp = gw; grp < (units + 7) / 8; grp += G) {
+    const long long u = grp * 8 + rg;
+    const bool live = u < units;
+    float r0 = 0.0f;
+    for (int sub = 0; sub < nsub; sub++) {
+      int part = nsub == 2 ? sub : 0;
+      long long row = live ? u : 0;
+      if (nsub == 1)
+        while (part < a.nparts - 1 && row >= a.part[part].rows) {
+          row -= a.part[part].rows;
+          part++;
+        }
+      const uint16_t *w = reinterpret_cast<const uint16_t *>(a.part[part].w) + row * cols + 8 * q;
+      float acc[8];
+#pragma unroll
+      for (int c = 0; c < 8; c++) acc[c] = 0.0f;
+      for (int i0 = 0; i0 < nsteps; i0 += kMvbU) {
+        uint4 wv[kMvbU];
+#pragma unroll
+        for (int k = 0; k < kMvbU; k++)
+          if (live && 32 * (i0 + k) + 8 * q < cols) wv[k] = __ldg(reinterpret_cast<const uint4 *>(w + 32 * (i0 + k)));
+#pragma unroll
+        for (int k = 0; k < kMvbU; k++) {
+          const int e = 32 * (i0 + k) + 8 * q;
+          if (!live || e >= cols) continue;
+          const float4 xa = *reinterpret_cast<const float4 *>(mvb_x + e);
+          const float4 xb = *reinterpret_cast<const float4 *>(mvb_x + e + 4);
+          const float x8[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+          const uint32_t h[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            const float wf = __uint_as_float((c & 1) ? (h[c >> 1] & 0xffff0000u) : (h[c >> 1] << 16));
+            acc[c] = __fadd_rn(acc[c], __fmul_rn(wf, x8[c]));
+          }
+        }
+      }
+      // combine32: e_j = (s_j + s_{j+8}) + (s_{j+16} + s_{j+24}), then
+      // ((e0+e1)+(e2+e3))+((e4+e5)+(e6+e7)); chain 8q+c is acc[c] of lane q.
+#pragma unroll
+      for (int c = 0; c < 8; c++) acc[c] = __fadd_rn(acc[c], __shfl_xor_sync(0xffffffffu, acc[c], 1));
+#pragma unroll
+      for (int c = 0; c < 8; c++) acc[c] = __fadd_rn(acc[c], __shfl_xor_sync(0xffffffffu, acc[c], 2));
+      const float r = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                                __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+      if (live && q == 0) {
         float *out = a.part[part].out;
         switch (a.epi) {
           case EPI_STORE: out[row] = r; break;
@@ -1425,6 +1526,10 @@ cudaError_t launch_matvec(const MvArgs &a, int num_sms, cudaStream_t st) {
     return launch_k(k_matvec_q<FMT_Q4_0, kWarps, kSlots>, num_sms, kWarps * 32, smem_for<FMT_Q4_0>(a.cols, fused, norm), st, a,
                     in_smem);
   if (a.fmt == FMT_F32) return launch_k(k_matvec_f<FMT_F32>, num_sms * 4, 256, 0, st, a);
+  // 16-byte rows and input: the eight-chains-a-lane kernel.
+  bool vec = a.cols % 8 == 0 && a.cols <= kMvbMaxCols && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  for (int p = 0; p < a.nparts; p++) vec = vec && (reinterpret_cast<uintptr_t>(a.part[p].w) & 15) == 0;
+  if (vec) return launch_k(k_matvec_bf16v, num_sms * 4, 256, 4 * a.cols, st, a);
   return launch_k(k_matvec_f<FMT_BF16>, num_sms * 4, 256, 0, st, a);
 }
 

@@ -116,16 +116,24 @@ def test_generator_matches_host(dev):
         same_bits(rk.generate_normal(dev, seed, tid, off, n, 0.02), ro.gen_normal(seed, tid, n, 0.02, offset=off))
 
 
-@pytest.mark.parametrize("fmt", [rk.FMT_Q8_0, rk.FMT_Q4_0], ids=["q8_0", "q4_0"])
+@pytest.mark.parametrize("fmt", [rk.FMT_Q8_0, rk.FMT_Q4_0, rk.FMT_F32, rk.FMT_BF16], ids=["q8_0", "q4_0", "f32", "bf16"])
 def test_generated_matrix_matches_host_import(dev, fmt):
-    """rk_matrix_generate = QuantizeQ8/Q4 of the host generator's floats."""
+    """rk_matrix_generate = QuantizeQ8/Q4 (or ToBF16, or the floats) of the
+    host generator's floats."""
     rows, cols = 300, 896
     m = rk.Matrix.generate(dev, rows, cols, fmt, 42, 17, 0.02)
     try:
         q, s = m.download()
-        hq, hs = ro.quantize(fmt, ro.gen_normal(42, 17, rows * cols, 0.02))
-        assert (q.view(np.uint8) == hq.view(np.uint8)).all()
-        same_bits(s, hs)
+        w = ro.gen_normal(42, 17, rows * cols, 0.02)
+        if fmt == rk.FMT_F32:
+            same_bits(q, w)
+        elif fmt == rk.FMT_BF16:
+            hq = np.array([ro.lib().rko_to_bf16(float(v)) for v in w], dtype=np.uint16)
+            assert (q.view(np.uint16) == hq).all()
+        else:
+            hq, hs = ro.quantize(fmt, w)
+            assert (q.view(np.uint8) == hq.view(np.uint8)).all()
+            same_bits(s, hs)
     finally:
         m.free()
 
