@@ -320,8 +320,9 @@ int rk_stage_new_group(rk_device *d, const rk_config *c, rk_layer *const *layers
 int rk_stage_fused_gathers(const rk_stage *s);
 /* 1 when the stage's decode step runs its products as chains (one launch of
  * Wo, W1·W3, W2 and the next layer's Q/K/V after each layer's attention,
- * the products handing their outputs on as tagged words); 0 when each
- * product is its own launch. Known once the stage has recorded its step
+ * the products handing their outputs on as tagged words; RK_CHAIN=1 in the
+ * environment when the stage is built); 0 when each product is its own
+ * launch (the default). Known once the stage has recorded its step
  * (after its first decode step); 0 before. No reference counterpart: a
  * diagnostic of how the stage runs, like rk_stage_fused_gathers. */
 int rk_stage_chained(const rk_stage *s);

@@ -1609,12 +1609,13 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
   // Chains need the tagged copies on every rank: always on one GPU, and
   // with the fused gathers (peer memory mapped) when sharded; the
   // attention output of a sharded stage arrives as tagged words too.
-  // They are the default for sharded stages, where each product boundary
-  // is also a gather (Llama-3-8B Q8_0 on two B200s: 354 tok/s against 331
-  // for the per-product graph); on one GPU the per-product graph is as
-  // fast (295 against 291). RK_CHAIN=1 or 0 chooses either way.
+  // They are opt-in (RK_CHAIN=1): measured on the same boxes, the
+  // per-product graph, whose launches overlap through programmatic
+  // dependent launch, is as fast or faster (Llama-3-8B Q8_0: 295 against
+  // 292 tok/s on one B200, 359.6 against 354.6 on two, 429.6 against 407.9
+  // on four).
   const char *chain_env = getenv("RK_CHAIN");
-  const bool want_chain = chain_env && *chain_env ? strcmp(chain_env, "1") == 0 : G > 1;
+  const bool want_chain = chain_env && strcmp(chain_env, "1") == 0;
   bool chain = L > 0 && (G == 1 || (s->p2p && s->v_pitch > 0)) && want_chain;
   if (chain) {
     ChainArgs first{};
