@@ -63,7 +63,9 @@ template <int NT, int FMT>
 struct MmCfg {
   static constexpr bool kQ4 = FMT == FMT_Q4_0;
   static constexpr int kEpiWarps = NT / 2;  // NT/8 warpgroups: a row and 8 tokens per thread
-  static constexpr int kConvWarps = kQ4 ? 4 : 0;  // Q4_0: the weight tile's expansion
+  // Q4_0: the weight tile's expansion (two warps beside the 32-token CTA's
+  // sixteen epilogue warps, whose registers the 16-token CTA does not need).
+  static constexpr int kConvWarps = kQ4 ? (NT == 32 ? 2 : 4) : 0;
   static constexpr int kThreads = 32 * (kEpiWarps + 2 + kConvWarps);
   static constexpr int kW = 128 * 128;    // int8 weight tile bytes
   static constexpr int kX = NT * 128;     // token tile bytes
@@ -199,14 +201,14 @@ __global__ void __launch_bounds__(MmCfg<NT, FMT>::kThreads, 1)
     }
     __syncwarp();
   } else if (warp >= E + 2) {
-    // Q4_0 converters: thread ct expands packed blocks ct, ct+128, ... of
+    // Q4_0 converters: thread ct expands packed blocks ct, ct+nct, ... of
     // the stage (row r = n/4, block b = n%4): element j (low nibble of
     // byte j) to int8 column 32b + j, element j+16 (high nibble) to column
     // 32b + 16 + j, as nibble - 8, at the 128-byte swizzle's place (16-byte
     // chunk c of row r at chunk c ^ (r mod 8)), which is where TMA puts a
     // Q8_0 tile. The MMA reads the stage once every converter warp has
     // fenced its stores for the async proxy and arrived.
-    const int ct = (warp - (E + 2)) * 32 + lane;
+    const int ct = (warp - (E + 2)) * 32 + lane, nct = 32 * C::kConvWarps;
     for (int i = 0; i < nkb; i++) {
       const int s = i % S;
       if (!umma::mbar_wait(full(s), (i / S) & 1)) {
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(MmCfg<NT, FMT>::kThreads, 1)
       uint8_t *const wx = ring_p + s * C::kStage;
       const uint8_t *const pk = wx + C::kPkOff;
 #pragma unroll
-      for (int n = ct; n < 512; n += 128) {
+      for (int n = ct; n < 512; n += nct) {
         const int r = n >> 2, b = n & 3;
         const uint4 v = *reinterpret_cast<const uint4 *>(pk + r * 64 + b * 16);
         const auto lo = [](uint32_t x) { return __vsub4(x & 0x0f0f0f0fu, 0x08080808u); };
@@ -326,7 +328,8 @@ static cudaError_t set_mm_attr() {
 }
 
 cudaError_t init_mvmany_attributes() {
-  for (const cudaError_t e : {set_mm_attr<16, FMT_Q8_0>(), set_mm_attr<32, FMT_Q8_0>(), set_mm_attr<16, FMT_Q4_0>()})
+  for (const cudaError_t e : {set_mm_attr<16, FMT_Q8_0>(), set_mm_attr<32, FMT_Q8_0>(), set_mm_attr<16, FMT_Q4_0>(),
+                              set_mm_attr<32, FMT_Q4_0>()})
     if (e != cudaSuccess) return e;
   return cudaSuccess;
 }
@@ -394,12 +397,14 @@ cudaError_t launch_mv_many(int nmats, const MmMat *mats, int cols, int ntok, con
   const long long row_tiles = a.tile0[nmats];
   if (row_tiles > 65535) return cudaErrorInvalidValue;
   // 32 tokens per CTA halve the weight tiles' re-reads from L2 once the
-  // grid fills the SMs anyway; otherwise 16 give twice the CTAs. (Q4_0
-  // takes 16: its converter warps leave the wider CTA too few registers.)
-  if (fmt == FMT_Q4_0) return launch_mm_nt<16, FMT_Q4_0>(a, mats, qx, xs, xs_pitch, st);
-  if (ntok > 16 && row_tiles * ((ntok + 31) / 32) >= num_sms)
-    return launch_mm_nt<32, FMT_Q8_0>(a, mats, qx, xs, xs_pitch, st);
-  return launch_mm_nt<16, FMT_Q8_0>(a, mats, qx, xs, xs_pitch, st);
+  // grid fills the SMs anyway; otherwise 16 give twice the CTAs. For Q4_0
+  // the 32-token tile also halves the expansions of each weight.
+  const bool wide = ntok > 16 && row_tiles * ((ntok + 31) / 32) >= num_sms;
+  if (fmt == FMT_Q4_0)
+    return wide ? launch_mm_nt<32, FMT_Q4_0>(a, mats, qx, xs, xs_pitch, st)
+                : launch_mm_nt<16, FMT_Q4_0>(a, mats, qx, xs, xs_pitch, st);
+  return wide ? launch_mm_nt<32, FMT_Q8_0>(a, mats, qx, xs, xs_pitch, st)
+              : launch_mm_nt<16, FMT_Q8_0>(a, mats, qx, xs, xs_pitch, st);
 }
 
 cudaError_t launch_silu_mul_many(float *hb, const float *hb2, long long n, int num_sms, cudaStream_t st) {
