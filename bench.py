@@ -677,7 +677,7 @@ def run_pipeline(args, world, rank, local, dist, torch):
     spans = rk.plan_stages([per] * c.layers, [per] * c.layers, [1.0] * world, [per * c.layers] * world, world)
     node, first, end = spans[rank]
     pr = synth.PipelineRank(dev, c, SEED, group, first, end, ctx=args.ctx + 64)
-    pr.stage.fill_cache(args.ctx, SEED)
+    pr.stage.fill_cache(args.ctx, SEED, first_layer=first)
     pos, tok = args.ctx, 1
 
     def barrier():

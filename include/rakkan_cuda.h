@@ -511,6 +511,9 @@ int rk_model_profile(rk_model *m, int pos, int iters, rk_profile *out);
  * seeded generator's N(0,1) values (tensor ids 0xA0000 + 2·layer for keys,
  * + 1 for values): a synthetic context of that length. */
 int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed);
+/* The same for a stage whose layer i is layer first_layer + i of the whole
+ * model (a layer pipeline's rank), so its caches match the whole model's. */
+int rk_stage_fill_cache_from(rk_stage *s, int positions, uint64_t seed, int first_layer);
 
 #ifdef __cplusplus
 }

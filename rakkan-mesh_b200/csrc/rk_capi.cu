@@ -1511,8 +1511,14 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
         if (wait) p.wait = *wait;
         return enqueue_matvecs(d, n, ms, outs, x, nullptr, nullptr, nullptr, epi, st, p);
       }
+      // A gathered input needs the fused prologue (the gather points are
+      // chosen so); the outputs still go to the peers when the point after
+      // this product is fused, whatever the prologue.
+      if (wait && wait->ll) return fail(RK_ERR_ARGS, "a gathered input for a product without the fused prologue");
       CK(launch_quantize_act(x, cols, norm_w, recip, eps, nullptr, s->qx, s->xs, s->xsum, st));
-      return enqueue_matvecs(d, n, ms, outs, x, s->qx, s->xs, s->xsum, epi, st);
+      Pro p;
+      if (put) p.put = *put;
+      return enqueue_matvecs(d, n, ms, outs, x, s->qx, s->xs, s->xsum, epi, st, p);
     }
     const float *in = x;
     if (norm_w) {
@@ -1712,10 +1718,12 @@ static int record_layers(rk_stage *s, cudaStream_t st) {
         if (f_x1) a.wait = wait_for(sl + 1, s->off_xll);
         if (f_hb) a.put = put_for(sl + 2, s->off_hbll, rH0);
       } else if (quantized_fmt(a.fmt)) {
+        if (f_x1) return fail(RK_ERR_ARGS, "a gathered input for a product without the fused prologue");
         CK(launch_quantize_act(s->x, D, norm_w, recipD, eps, nullptr, s->qx, s->xs, s->xsum, st));
         a.qx = s->qx;
         a.xs = s->xs;
         a.xsum = s->xsum;
+        if (f_hb) a.put = put_for(sl + 2, s->off_hbll, rH0);  // (the epilogue stores them either way)
       } else {
         CK(launch_rmsnorm(s->x, s->xb, norm_w, D, 1, 0, recipD, eps, st));
         a.x = s->xb;
@@ -3298,7 +3306,11 @@ extern "C" int rk_model_profile(rk_model *m, int pos, int iters, rk_profile *out
 }
 
 extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
-  if (!s || positions < 0 || positions > s->ctx) return fail(RK_ERR_ARGS, "bad argument");
+  return rk_stage_fill_cache_from(s, positions, seed, 0);
+}
+
+extern "C" int rk_stage_fill_cache_from(rk_stage *s, int positions, uint64_t seed, int first_layer) {
+  if (!s || positions < 0 || positions > s->ctx || first_layer < 0) return fail(RK_ERR_ARGS, "bad argument");
   rk_device *d = s->d;
   Guard g(d);
   int rc = set_device(d);
@@ -3311,12 +3323,13 @@ extern "C" int rk_stage_fill_cache(rk_stage *s, int positions, uint64_t seed) {
   for (int q = 0; q < s->nseq; q++)
     for (size_t l = 0; l < s->layers.size(); l++) {
       float *keys = s->keys[l] + q * kstride, *vals = s->vals[l] + q * vstride;
-      CK(launch_gen_normal_2d(seed, 0xA0000ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, keys, d->st));
+      const unsigned long long gl = (unsigned long long)first_layer + l;  // the whole model's layer index
+      CK(launch_gen_normal_2d(seed, 0xA0000ull + 2 * gl, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, keys, d->st));
       if (s->v_pitch > 0)
-        CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, 1, s->v_pitch, 1.0f, vals,
+        CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * gl, positions, kvd, c0, kvd_l, 1, s->v_pitch, 1.0f, vals,
                                 d->st));
       else
-        CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * l, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, vals, d->st));
+        CK(launch_gen_normal_2d(seed, 0xA0001ull + 2 * gl, positions, kvd, c0, kvd_l, kvd_l, 1, 1.0f, vals, d->st));
     }
   return sync_dev(d);
 }

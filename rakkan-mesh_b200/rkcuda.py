@@ -36,7 +36,7 @@ EXPORTS = [
     "rk_tensor_matmul_device", "rk_matrix_generate", "rk_matrix_download", "rk_generate_normal", "rk_quantize",
     "rk_bench_matvec", "rk_bench_matvec_many", "rk_bench_tensor", "rk_bench_model", "rk_group_id", "rk_group_new", "rk_group_free",
     "rk_group_size", "rk_group_all_gather", "rk_layer_upload_shard", "rk_layer_from_device_shard",
-    "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_stage_chained", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache",
+    "rk_stage_new_group", "rk_head_new_group", "rk_matrix_generate_rows", "rk_stage_fused_gathers", "rk_stage_chained", "rk_model_kernel_count", "rk_model_profile", "rk_stage_fill_cache", "rk_stage_fill_cache_from",
     "rk_plan_stages", "rk_pipeline_new", "rk_pipeline_free", "rk_pipeline_step", "rk_bench_pipeline",
     "rk_tensor_add", "rk_tensor_scale", "rk_tensor_relu", "rk_tensor_softmax", "rk_tensor_quantize", "rk_tensor_argmax",
     "rk_layer_load_part", "rk_embed_load_part", "rk_head_load_part", "rk_matmul_bf16", "rk_measure_speed",
@@ -134,7 +134,7 @@ def lib():
             "rk_head_new_group": (i, [vp, vp, vp, vp, vp, vp]), "rk_stage_fused_gathers": (i, [vp]), "rk_stage_chained": (i, [vp]),
             "rk_matrix_generate_rows": (i, [vp, i, i, i, i, i, u64, u64, f, vp]),
             "rk_model_kernel_count": (i, [vp, vp]), "rk_model_profile": (i, [vp, i, i, vp]),
-            "rk_stage_fill_cache": (i, [vp, i, u64]),
+            "rk_stage_fill_cache": (i, [vp, i, u64]), "rk_stage_fill_cache_from": (i, [vp, i, u64, i]),
             "rk_plan_stages": (i, [vp, vp, i, vp, vp, vp, i, i, vp, vp, vp, vp]),
             "rk_pipeline_new": (i, [vp, vp, vp, vp, vp]), "rk_pipeline_free": (None, [vp]),
             "rk_pipeline_step": (i, [vp, i, i, vp, vp]), "rk_bench_pipeline": (i, [vp, i, i, vp]),
@@ -464,8 +464,11 @@ class Stage:
         widths), else 0."""
         return lib().rk_stage_batched(self.h)
 
-    def fill_cache(self, positions, seed):
-        _check(lib().rk_stage_fill_cache(self.h, positions, seed))
+    def fill_cache(self, positions, seed, first_layer=0):
+        """A seeded synthetic context in every layer's caches (positions
+        rows); first_layer: the whole model's index of the stage's first
+        layer (a pipeline rank's stage), so its caches match that model's."""
+        _check(lib().rk_stage_fill_cache_from(self.h, positions, seed, first_layer))
 
     def forward(self, xs, pos):
         xs = np.ascontiguousarray(xs, dtype=np.float32).copy()

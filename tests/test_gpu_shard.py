@@ -26,6 +26,12 @@ def _small(dtype, variant):
     over = dict(layers=2, dim=1024, hidden=2816, heads=16, kv_heads=8, vocab=8192, seq_len=CTX)
     if variant == "qwen3":
         over.update(head_dim=128, qk_norm=1, rope_theta=1e6, norm_eps=1e-6, heads=16, kv_heads=8)
+    if variant == "wide_hidden":
+        # Hidden wider than a product's own quantizing prologue takes (as
+        # Qwen3-32B's 25600): W2 quantizes its input in a separate launch
+        # while the next layer's Q/K/V still gathers x as tagged words, which
+        # W2's epilogue must store.
+        over.update(hidden=16896)
     return synth.config("llama3-8b", dtype, **over)
 
 
@@ -47,7 +53,7 @@ def _rank(rank, world, gid, dtype, variant, out):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("variant", ["llama", "qwen3"])
+@pytest.mark.parametrize("variant", ["llama", "qwen3", "wide_hidden"])
 @pytest.mark.parametrize("dtype", ["q8_0", "q4_0"])
 def test_row_sharded_decode_matches_oracle(dtype, variant, world):
     if rk.device_count() < world:
