@@ -2837,8 +2837,11 @@ extern "C" int rk_tensors_from_blob(rk_tensors *t, const void *blob, int64_t blo
     return fail(RK_ERR_TOO_BIG, "bad tensor type or shape");
   const int64_t n = (int64_t)rows * cols * es;
   if (t->used + n > t->budget) return fail(RK_ERR_TOO_BIG, "tensor of %d×%d over the budget", rows, cols);
-  if (offset + n > blob_size) return fail(RK_ERR_BLOB, "blob of %lld bytes too short for %lld bytes at %lld",
-                                          (long long)blob_size, (long long)n, (long long)offset);
+  // (offset is the guest's: compared without forming offset + n, which a
+  // huge offset would overflow)
+  if (offset > blob_size || n > blob_size - offset)
+    return fail(RK_ERR_BLOB, "blob of %lld bytes too short for %lld bytes at %lld", (long long)blob_size,
+                (long long)n, (long long)offset);
   return tt_upload(t, static_cast<const char *>(blob) + offset, dtype, rows, cols, RK_ERR_TOO_BIG);
 }
 

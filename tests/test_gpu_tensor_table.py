@@ -90,6 +90,10 @@ def test_load_canonicalises_nan_and_checks(dev):
         with pytest.raises(rk.RkError) as e:
             tt.from_blob(np.zeros(100, np.uint8), 90, rk.TENSOR_I8, 1, 16)
         assert e.value.code == rk.RK_ERR_BLOB
+        for off in (101, 2**62, 2**63 - 8):  # past the blob, and offsets whose sum with the size would overflow
+            with pytest.raises(rk.RkError) as e:
+                tt.from_blob(np.zeros(100, np.uint8), off, rk.TENSOR_I8, 1, 16)
+            assert e.value.code == rk.RK_ERR_BLOB
         with pytest.raises(rk.RkError) as e:
             tt.matmul(h, h)  # 1x4 · 1x4: inner dimensions differ
         assert e.value.code == rk.RK_ERR_ARGS
